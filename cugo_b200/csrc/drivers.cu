@@ -1,0 +1,322 @@
+// Seeded random-legal drivers of the benchmark configurations, on the GPU.
+//
+// The reference has no such driver (its rollouts use canonical actions or a
+// host LCG, tests/torch50_test.cpp:196-200); these kernels play the rule
+// defined once for every implementation:
+//   game i: seed = seed_base + i, first player = i & 1
+//   decision d of game i picks the floor(r0 * n / 2^32)-th of its n legal
+//   actions, r0 = Philox4x32-10({i lo, i hi, d, stream}, {seed lo, seed hi})[0]
+//   event hash: FNV-1a 64 over the start record and every committed event.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "engine/driver.cuh"
+#include "engine/env.cuh"
+#include "../../include/cugo_b200.h"
+
+using namespace cb;
+
+namespace {
+
+constexpr int kBlock = 128;
+constexpr u64 kFnvOffset = 0xcbf29ce484222325ull;
+constexpr u64 kFnvPrime = 0x100000001b3ull;
+
+__device__ __forceinline__ u64 fnv_words(u64 h, const i64* words, int n) {
+  for (int w = 0; w < n; ++w) {
+    const u64 v = static_cast<u64>(words[w]);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      h ^= (v >> (8 * b)) & 0xffu;
+      h *= kFnvPrime;
+    }
+  }
+  return h;
+}
+
+// Whole games: thread k plays game game0 + k to the end (or max_decisions).
+__global__ void __launch_bounds__(kBlock) rollout_kernel(
+    i64 game0, i64 n, i64 seed_base, int max_decisions, u32 stream, u64* __restrict__ final_rows,
+    i64* __restrict__ reward0_out, int32_t* __restrict__ decisions_out,
+    int32_t* __restrict__ events_out, u64* __restrict__ hash_out, int16_t* __restrict__ status_out) {
+  const i64 k = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const u64 game = static_cast<u64>(game0 + k);
+  const u64 seed = static_cast<u64>(seed_base) + game;
+  Game g;
+  create_game(g, seed, static_cast<u32>(game & 1u));
+  i64 words[kEventWords];
+  start_words(g, words);
+  u64 h = fnv_words(kFnvOffset, words, kStartWords);
+  int d = 0, ev = 0;
+  i32 st = 0;
+  i64 rew = 0;
+  while (!g.done() && d < max_decisions) {
+    const LegalInfo li = torch_legal(g);
+    const u32 r0 = game_draw(game, static_cast<u32>(d), stream, seed).v[0];
+    const u32 a = pick_set_bit(li.legal.w0, li.legal.w1, li.legal.w2, r0);
+    if (a == 0xffffu) {
+      st = -2;
+      break;
+    }
+    const EventBase before = event_base(g);
+    const StepOut r = step_game(g, a);
+    ++d;
+    st = static_cast<i32>(r.status);
+    rew = r.reward0;
+    if (r.status != kOk) break;
+    if (r.committed) {
+      event_words(before, g, words);
+      h = fnv_words(h, words, kEventWords);
+      ++ev;
+    }
+  }
+  zero_padding(g);
+  u64* out = final_rows + k * kRowWords;
+#pragma unroll
+  for (int w = 0; w < kRowWords; ++w) out[w] = g.w[w];
+  reward0_out[k] = rew;
+  decisions_out[k] = d;
+  events_out[k] = ev;
+  hash_out[k] = h;
+  status_out[k] = static_cast<int16_t>(st);
+}
+
+// One decision of every slot: a finished game is replaced by the slot's next
+// game (index + n_slots), then observe -> random legal pick -> step.  Features
+// and masks of the decision are written like observe() writes them.
+struct SlotTile {
+  union {
+    u64 rows[32][kRowWords];
+    struct {
+      u32 bits[32][kBitWords + 1];
+      float scal[32][kScalarColumns];
+    } pk;
+  };
+  u64 legal[32][3];
+};
+
+__global__ void __launch_bounds__(kBlock) selfplay_step_kernel(
+    u64* __restrict__ states, i64 n_slots, i64 seed_base, i64* __restrict__ slot_game,
+    int32_t* __restrict__ slot_decision, int32_t* __restrict__ slot_completed,
+    int64_t* __restrict__ slot_steps, float* __restrict__ features, bool* __restrict__ legal_out) {
+  __shared__ SlotTile tiles[kBlock / 32];
+  SlotTile& t = tiles[threadIdx.x >> 5];
+  const int lane = threadIdx.x & 31;
+  const i64 slot = (i64)blockIdx.x * kBlock + threadIdx.x;
+  const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
+  const i64 my_src = slot < n_slots ? slot : -1;
+  // Gather the 32 rows.
+#pragma unroll 8
+  for (int r = 0; r < 32; ++r) {
+    const i64 id = __shfl_sync(0xffffffffu, my_src, r);
+    if (lane < kRowWords) t.rows[r][lane] = id >= 0 ? __ldg(states + id * kRowWords + lane) : 0ull;
+  }
+  __syncwarp();
+  Game g;
+#pragma unroll
+  for (int w = 0; w < kRowWords; ++w) g.w[w] = t.rows[lane][w];
+  __syncwarp();
+  ObsPacket pk;
+  ObsMeta meta;
+  u32 action = 0xffffu;
+  i64 game = 0;
+  u32 decision = 0;
+  if (slot < n_slots) {
+    game = slot_game[slot];
+    decision = static_cast<u32>(slot_decision[slot]);
+    if (g.done()) {
+      slot_completed[slot] += 1;
+      game += n_slots;
+      decision = 0;
+      create_game(g, static_cast<u64>(seed_base + game), static_cast<u32>(game & 1));
+    }
+    observe_game(g, pk, meta);
+    const u32 r0 = game_draw(static_cast<u64>(game), decision, 0u, static_cast<u64>(seed_base + game)).v[0];
+    action = pick_set_bit(meta.legal.w0, meta.legal.w1, meta.legal.w2, r0);
+  } else {
+    for (u32 k = 0; k < kBitWords; ++k) pk.bits[k] = 0;
+    for (u32 k = 0; k < kScalarColumns; ++k) pk.scal[k] = 0.0f;
+    meta.legal = Legal{};
+  }
+  // Packets to shared memory, then the cooperative feature/mask writes.
+#pragma unroll
+  for (int k = 0; k < (int)kBitWords; ++k) t.pk.bits[lane][k] = pk.bits[k];
+#pragma unroll
+  for (int k = 0; k < (int)kScalarColumns; ++k) t.pk.scal[lane][k] = pk.scal[k];
+  t.legal[lane][0] = meta.legal.w0;
+  t.legal[lane][1] = meta.legal.w1;
+  t.legal[lane][2] = meta.legal.w2;
+  __syncwarp();
+  const i64 left = n_slots - tile_base;
+  const int rows_here = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
+  for (int r = 0; r < rows_here; ++r) {
+    float4* row = reinterpret_cast<float4*>(features + (tile_base + r) * (i64)kFeatures);
+#pragma unroll
+    for (int k = 0; k < 6; ++k) {
+      const int q = lane + 32 * k;
+      if (q < (int)(kFeatures / 4)) {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const u32 c = 4u * q + j;
+          const int s = scalar_slot(c);
+          v[j] = s >= 0 ? t.pk.scal[r][s] : ((t.pk.bits[r][c >> 5] >> (c & 31u)) & 1u ? 1.0f : 0.0f);
+        }
+        __stcs(row + q, make_float4(v[0], v[1], v[2], v[3]));
+      }
+    }
+  }
+  {
+    uint8_t* block = reinterpret_cast<uint8_t*>(legal_out) + tile_base * (i64)kActions;
+    const int bytes = rows_here * (int)kActions;
+    const int words = bytes >> 2;
+    for (int wi = lane; wi < words; wi += 32) {
+      u32 v = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int b = 4 * wi + j;
+        const int r = b / (int)kActions, a = b - r * (int)kActions;
+        v |= static_cast<u32>((t.legal[r][a >> 6] >> (a & 63)) & 1ull) << (8 * j);
+      }
+      reinterpret_cast<u32*>(block)[wi] = v;
+    }
+    for (int b = 4 * words + lane; b < bytes; b += 32) {
+      const int r = b / (int)kActions, a = b - r * (int)kActions;
+      block[b] = static_cast<uint8_t>((t.legal[r][a >> 6] >> (a & 63)) & 1ull);
+    }
+  }
+  __syncwarp();
+  if (slot < n_slots) {
+    if (action != 0xffffu) {
+      step_game(g, action);
+      ++decision;
+      slot_steps[slot] += 1;
+    }
+    slot_game[slot] = game;
+    slot_decision[slot] = static_cast<int32_t>(decision);
+  }
+  zero_padding(g);
+#pragma unroll
+  for (int w = 0; w < kRowWords; ++w) t.rows[lane][w] = g.w[w];
+  __syncwarp();
+#pragma unroll 8
+  for (int r = 0; r < 32; ++r) {
+    const i64 id = __shfl_sync(0xffffffffu, my_src, r);
+    if (id >= 0 && lane < kRowWords) states[id * kRowWords + lane] = t.rows[r][lane];
+  }
+}
+
+// Branching roots: game r advanced by k_r < 21 random-legal decisions, stopping
+// before a decision that would finish the game.
+__global__ void __launch_bounds__(kBlock) branch_roots_kernel(i64 n_roots, i64 seed_base,
+                                                              u64* __restrict__ roots) {
+  const i64 r = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n_roots) return;
+  const u64 seed = static_cast<u64>(seed_base + r);
+  Game g;
+  create_game(g, seed, static_cast<u32>(r & 1));
+  const u32 k = static_cast<u32>((static_cast<u64>(game_draw(r, 0xffffu, 2u, seed).v[0]) * 21u) >> 32);
+  for (u32 d = 0; d < k && !g.done(); ++d) {
+    const LegalInfo li = torch_legal(g);
+    const u32 a = pick_set_bit(li.legal.w0, li.legal.w1, li.legal.w2,
+                               game_draw(r, d, 0u, seed).v[0]);
+    if (a == 0xffffu) break;
+    Game next = g;
+    step_game(next, a);
+    if (next.done()) break;
+    g = next;
+  }
+  zero_padding(g);
+  u64* out = roots + r * kRowWords;
+#pragma unroll
+  for (int w = 0; w < kRowWords; ++w) out[w] = g.w[w];
+}
+
+// Branch i of root r = i / per_root: (env id, a random legal action of the root
+// drawn from stream 1 with counter {r, b}).
+__global__ void __launch_bounds__(kBlock) branch_actions_kernel(const u64* __restrict__ roots,
+                                                                i64 n_roots, i64 per_root,
+                                                                i64 seed_base, i64* __restrict__ ids,
+                                                                i64* __restrict__ actions) {
+  const i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_roots * per_root) return;
+  const i64 r = i / per_root, b = i - r * per_root;
+  Game g;
+  const u64* row = roots + r * kRowWords;
+#pragma unroll
+  for (int w = 0; w < kRowWords; ++w) g.w[w] = __ldg(row + w);
+  const LegalInfo li = torch_legal(g);
+  const u64 ctr = static_cast<u64>(r) | (static_cast<u64>(b) << 32);
+  const u32 a = pick_set_bit(li.legal.w0, li.legal.w1, li.legal.w2,
+                             game_draw(ctr, 0u, 1u, static_cast<u64>(seed_base + r)).v[0]);
+  ids[i] = r;
+  actions[i] = a == 0xffffu ? -1 : static_cast<i64>(a);
+}
+
+inline int launch_status() {
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+inline unsigned blocks_for(i64 n) { return static_cast<unsigned>((n + kBlock - 1) / kBlock); }
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_rollout_random(int64_t game0, int64_t n, int64_t seed_base, int32_t max_decisions,
+                             uint32_t stream_id, uint8_t* final_rows, int64_t* reward0,
+                             int32_t* decisions, int32_t* events, uint64_t* hashes,
+                             int16_t* last_status, cudaStream_t stream) {
+  if (n < 0 || max_decisions < 0) return CUGO_B200_ERR_ARG;
+  if (n > 0 && (!final_rows || !reward0 || !decisions || !events || !hashes || !last_status))
+    return CUGO_B200_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(final_rows) & 7u) return CUGO_B200_ERR_ALIGN;
+  if (n == 0) return CUGO_B200_OK;
+  rollout_kernel<<<blocks_for(n), kBlock, 0, stream>>>(
+      game0, n, seed_base, max_decisions, stream_id, reinterpret_cast<u64*>(final_rows), reward0,
+      decisions, events, hashes, last_status);
+  return launch_status();
+}
+
+int cugo_b200_selfplay_random_step(uint8_t* states, int64_t n_slots, int64_t seed_base,
+                                   int64_t* slot_game, int32_t* slot_decision,
+                                   int32_t* slot_completed, int64_t* slot_steps, float* features,
+                                   bool* legal, cudaStream_t stream) {
+  if (n_slots < 0) return CUGO_B200_ERR_ARG;
+  if (n_slots > 0 && (!states || !slot_game || !slot_decision || !slot_completed || !slot_steps ||
+                      !features || !legal))
+    return CUGO_B200_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(states) & 7u) || (reinterpret_cast<uintptr_t>(features) & 15u) ||
+      (reinterpret_cast<uintptr_t>(legal) & 3u))
+    return CUGO_B200_ERR_ALIGN;
+  if (n_slots == 0) return CUGO_B200_OK;
+  selfplay_step_kernel<<<blocks_for(n_slots), kBlock, 0, stream>>>(
+      reinterpret_cast<u64*>(states), n_slots, seed_base, slot_game, slot_decision, slot_completed,
+      slot_steps, features, legal);
+  return launch_status();
+}
+
+int cugo_b200_branch_roots(int64_t n_roots, int64_t seed_base, uint8_t* roots, cudaStream_t stream) {
+  if (n_roots < 0 || (n_roots > 0 && !roots)) return CUGO_B200_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(roots) & 7u) return CUGO_B200_ERR_ALIGN;
+  if (n_roots == 0) return CUGO_B200_OK;
+  branch_roots_kernel<<<blocks_for(n_roots), kBlock, 0, stream>>>(n_roots, seed_base,
+                                                                 reinterpret_cast<u64*>(roots));
+  return launch_status();
+}
+
+int cugo_b200_branch_actions(const uint8_t* roots, int64_t n_roots, int64_t per_root,
+                             int64_t seed_base, int64_t* env_ids, int64_t* actions,
+                             cudaStream_t stream) {
+  if (n_roots < 0 || per_root < 0) return CUGO_B200_ERR_ARG;
+  const i64 n = n_roots * per_root;
+  if (n > 0 && (!roots || !env_ids || !actions)) return CUGO_B200_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(roots) & 7u) return CUGO_B200_ERR_ALIGN;
+  if (n == 0) return CUGO_B200_OK;
+  branch_actions_kernel<<<blocks_for(n), kBlock, 0, stream>>>(
+      reinterpret_cast<const u64*>(roots), n_roots, per_root, seed_base, env_ids, actions);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -19,6 +19,12 @@
 #endif
 
 #if defined(__CUDACC__)
+#define CB_HDC __host__ __device__ constexpr
+#else
+#define CB_HDC constexpr
+#endif
+
+#if defined(__CUDACC__)
 #define CB_UNROLL _Pragma("unroll")
 #define CB_NO_UNROLL _Pragma("unroll 1")
 #else
@@ -43,7 +49,7 @@ constexpr Mask kStandardDeck = (Mask{1} << 48) - 1;
 constexpr Mask kBonusCards = Mask{3} << 48;
 constexpr Mask kFullDeck = (Mask{1} << 50) - 1;
 
-constexpr Mask cards_of(u32 a, u32 b, u32 c = 64, u32 d = 64, u32 e = 64) {
+CB_HDC Mask cards_of(u32 a, u32 b, u32 c = 64, u32 d = 64, u32 e = 64) {
   return (Mask{1} << a) | (Mask{1} << b) | (c < 64 ? Mask{1} << c : 0) |
          (d < 64 ? Mask{1} << d : 0) | (e < 64 ? Mask{1} << e : 0);
 }

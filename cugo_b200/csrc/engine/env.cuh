@@ -525,40 +525,62 @@ struct ObsMeta {
   i32 status;
 };
 
+// Legal actions of the floor choice: 127 + card for each selectable card.
+CB_HD Legal choice_legal(Mask choices) {
+  Legal m;
+  choices &= kFullDeck;
+  m.w1 = (choices & 1u) ? (u64{1} << 63) : 0;  // card 0 is action 127
+  m.w2 = choices >> 1;                         // cards 1..49 are actions 128..176
+  return m;
+}
+
+// The legal mask and packet status of make_torch_packet50 without the features.
+struct LegalInfo {
+  Legal legal;
+  u32 status = kOk;
+  u32 kind = kDecNone;  // decision kind written to the observation (0 when done)
+  Peek peek;            // the pending probe, when a floor choice is pending
+};
+
+CB_HD LegalInfo torch_legal(const Game& g) {
+  LegalInfo r;
+  if (g.pend_active()) {
+    r.peek = peek_pending(g);
+    r.status = r.peek.status;
+    if (r.status == kOk) {
+      r.legal = choice_legal(r.peek.choices);
+      r.kind = r.peek.decision;
+    }
+    return r;
+  }
+  if (g.done()) return r;
+  r.kind = decision_kind(g);
+  if (r.kind == kDecGukjin) r.legal.w2 = (u64{1} << (177 - 128)) | (u64{1} << (178 - 128));
+  else r.legal = primary_legal(g);
+  return r;
+}
+
 // make_torch_packet50 + encode: the observation of one row.
 CB_HD void observe_game(const Game& g, ObsPacket& pk, ObsMeta& meta) {
   meta.done = g.done() ? 1u : 0u;
+  const LegalInfo li = torch_legal(g);
+  meta.legal = li.legal;
+  meta.status = static_cast<i32>(li.status);
   if (g.pend_active()) {
-    const Peek p = peek_pending(g);
     meta.player = g.pend_actor();
-    if (p.status != kOk) {
-      meta.legal = Legal{};
-      meta.status = static_cast<i32>(p.status);
-      pack_failed_probe(g.pend_primary(), p.revealed, pk);
+    if (li.status != kOk) {
+      pack_failed_probe(g.pend_primary(), li.peek.revealed, pk);
       return;
     }
-    Legal choice;
-    choice.w2 = (p.choices & kFullDeck) >> 1;  // actions 127 + card: bit 63 of w1 is card 0
-    choice.w1 = (p.choices & 1u) ? (u64{1} << 63) : 0;
-    meta.legal = choice;
-    meta.status = kOk;
     Game v = g;
-    if (p.decision != kDecNone) stage_pending_view(v, p);
+    if (li.peek.decision != kDecNone) stage_pending_view(v, li.peek);
     v.set_actor(g.pend_actor());
-    PacketInputs in{p.decision, g.pend_primary(), p.revealed, p.choices, true};
+    PacketInputs in{li.peek.decision, g.pend_primary(), li.peek.revealed, li.peek.choices, true};
     pack_observation(v, in, pk);
     return;
   }
-  const u32 kind = decision_kind(g);
-  Legal legal;
-  if (!g.done()) {
-    if (kind == kDecGukjin) legal.w2 = (u64{1} << (177 - 128)) | (u64{1} << (178 - 128));
-    else legal = primary_legal(g);
-  }
-  meta.legal = legal;
   meta.player = observer_seat(g);
-  meta.status = kOk;
-  PacketInputs in{g.done() ? 0u : kind, kNoAction, kNoCard, 0, false};
+  PacketInputs in{li.kind, kNoAction, kNoCard, 0, false};
   pack_observation(g, in, pk);
 }
 
@@ -770,29 +792,16 @@ CB_HD StepOut step_game(Game& g, u32 action) {
     return StepOut{kFinished, reward0(g), g.done(), g.nagari(), 0};
   }
   const bool choosing = g.pend_active() != 0;
-  Peek p;
-  Legal legal;
-  u32 kind = kDecNone;
-  if (choosing) {
-    p = peek_pending(g);
-    if (p.status != kOk) {
-      g.set_status(p.status);
-      return StepOut{p.status, 0, g.done(), g.nagari(), 0};
-    }
-    if (action >= kChoiceBegin && action < kChoiceBegin + 50u)
-      legal.set((p.choices >> (action - kChoiceBegin)) & 1u ? action : kNoAction);
-  } else {
-    kind = decision_kind(g);
-    if (kind == kDecGukjin) {
-      legal.w2 = (u64{1} << (177 - 128)) | (u64{1} << (178 - 128));
-    } else {
-      legal = primary_legal(g);
-    }
+  const LegalInfo li = torch_legal(g);
+  if (li.status != kOk) {
+    g.set_status(li.status);
+    return StepOut{li.status, 0, g.done(), g.nagari(), 0};
   }
-  if (!legal.has(action)) {
+  if (!li.legal.has(action)) {
     g.set_status(kNotLegal);
     return StepOut{kNotLegal, 0, g.done(), g.nagari(), 0};
   }
+  const Peek& p = li.peek;
   if (choosing) {
     if (p.decision == kDecPiCard) g.set_n_pi(g.n_pi() + 1u);
     else g.set_n_resolve(g.n_resolve() + 1u);

@@ -1,0 +1,462 @@
+// Batch-environment kernels for sm_100a and their C ABI (include/cugo_b200.h).
+//
+// Layout in HBM: game rows are the reference's 248-byte TorchEnv50 images,
+// [N, 248] uint8 (31 little-endian u64 words each); features are fp32 [M, 720],
+// legal masks bool [M, 179].
+//
+// Kernel shape: 128-thread blocks, one game per thread, one 32-game tile per
+// warp.  A warp moves its 32 rows between HBM and shared memory cooperatively
+// (each row is one 248-byte coalesced access of 31 lanes, gathered through the
+// id list for indexed ops), each thread runs the rule code on its row held in
+// registers, and the warp writes the 32 feature rows (2,880 B each) and the
+// 5,728-byte block of legal masks with 16-byte and 4-byte vector stores.
+// Nothing is allocated; every launch goes to the caller's stream, so all
+// entry points can be captured in a CUDA graph.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "engine/env.cuh"
+#include "engine/driver.cuh"
+#include "../../include/cugo_b200.h"
+
+using namespace cb;
+
+namespace {
+
+constexpr int kWarpsPerBlock = 4;
+constexpr int kBlock = 32 * kWarpsPerBlock;
+constexpr unsigned kFull = 0xffffffffu;
+
+// Per-warp shared staging: the 32 row images, reused for the 32 packets.
+struct WarpTile {
+  union {
+    u64 rows[32][kRowWords];
+    struct {
+      u32 bits[32][kBitWords + 1];  // odd stride: conflict-free per-lane stores
+      float scal[32][kScalarColumns];
+    } pk;
+  };
+  u64 legal[32][3];
+};
+static_assert(sizeof(WarpTile) <= 9 * 1024, "tile fits the shared budget");
+
+__device__ __forceinline__ WarpTile& my_tile() {
+  __shared__ WarpTile tiles[kWarpsPerBlock];
+  return tiles[threadIdx.x >> 5];
+}
+
+// Row id this lane's game reads: ids[row] for indexed ops, row itself otherwise;
+// -1 past the end of the batch or for an id outside [0, n_states).
+__device__ __forceinline__ i64 lane_source(const i64* ids, i64 row, i64 m, i64 n_states) {
+  if (row >= m) return -1;
+  const i64 id = ids ? __ldg(ids + row) : row;
+  return (id >= 0 && id < n_states) ? id : -1;
+}
+
+// Gathers the warp's 32 source rows into the tile (zero rows for missing ids).
+__device__ __forceinline__ void gather_rows(WarpTile& t, const u64* __restrict__ src, i64 my_src) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll 8
+  for (int r = 0; r < 32; ++r) {
+    const i64 id = __shfl_sync(kFull, my_src, r);
+    if (lane < kRowWords) t.rows[r][lane] = id >= 0 ? __ldg(src + id * kRowWords + lane) : 0ull;
+  }
+  __syncwarp();
+}
+
+// Writes tile rows back to dst[dst_row] for every lane whose dst_row >= 0.
+__device__ __forceinline__ void scatter_rows(const WarpTile& t, u64* __restrict__ dst, i64 my_dst) {
+  __syncwarp();
+  const int lane = threadIdx.x & 31;
+#pragma unroll 8
+  for (int r = 0; r < 32; ++r) {
+    const i64 id = __shfl_sync(kFull, my_dst, r);
+    if (id >= 0 && lane < kRowWords) dst[id * kRowWords + lane] = t.rows[r][lane];
+  }
+}
+
+__device__ __forceinline__ void load_game(const WarpTile& t, Game& g) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < kRowWords; ++k) g.w[k] = t.rows[lane][k];
+}
+
+__device__ __forceinline__ void store_game(WarpTile& t, Game g) {
+  zero_padding(g);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < kRowWords; ++k) t.rows[lane][k] = g.w[k];
+}
+
+__device__ __forceinline__ void store_packet(WarpTile& t, const ObsPacket& pk, const Legal& legal) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < (int)kBitWords; ++k) t.pk.bits[lane][k] = pk.bits[k];
+#pragma unroll
+  for (int k = 0; k < (int)kScalarColumns; ++k) t.pk.scal[lane][k] = pk.scal[k];
+  t.legal[lane][0] = legal.w0;
+  t.legal[lane][1] = legal.w1;
+  t.legal[lane][2] = legal.w2;
+}
+
+// Cooperative write of the tile's feature rows: row `base + r` for r < rows.
+// Lane l owns float4 columns 4l, 4l+128, ... of every row.
+__device__ __forceinline__ void emit_features(const WarpTile& t, float* __restrict__ out, i64 base,
+                                              int rows) {
+  __syncwarp();
+  const int lane = threadIdx.x & 31;
+  // Per lane: for each of its 24 columns, the scalar slot or (word, bit).
+  int slot[6][4];
+  u32 word[6][4], bitpos[6][4];
+#pragma unroll
+  for (int k = 0; k < 6; ++k)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const u32 c = 4u * (lane + 32u * k) + j;
+      slot[k][j] = c < kFeatures ? scalar_slot(c) : -1;
+      word[k][j] = c >> 5;
+      bitpos[k][j] = c & 31u;
+    }
+  for (int r = 0; r < rows; ++r) {
+    float4* row = reinterpret_cast<float4*>(out + (base + r) * (i64)kFeatures);
+#pragma unroll
+    for (int k = 0; k < 6; ++k) {
+      const int q = lane + 32 * k;
+      if (q < (int)(kFeatures / 4)) {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          v[j] = slot[k][j] >= 0 ? t.pk.scal[r][slot[k][j]]
+                                 : ((t.pk.bits[r][word[k][j]] >> bitpos[k][j]) & 1u ? 1.0f : 0.0f);
+        __stcs(row + q, make_float4(v[0], v[1], v[2], v[3]));
+      }
+    }
+  }
+}
+
+// Cooperative write of the tile's legal masks (bool [rows, 179], contiguous
+// from row `base`); whole 4-byte words, then the tail bytes.
+__device__ __forceinline__ void emit_legal(const WarpTile& t, bool* __restrict__ out, i64 base,
+                                           int rows) {
+  const int lane = threadIdx.x & 31;
+  uint8_t* block = reinterpret_cast<uint8_t*>(out) + base * (i64)kActions;
+  const int bytes = rows * (int)kActions;
+  const int words = bytes >> 2;
+  for (int wi = lane; wi < words; wi += 32) {
+    u32 v = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = 4 * wi + j;
+      const int r = b / (int)kActions, a = b - r * (int)kActions;
+      const u64 w = t.legal[r][a >> 6];
+      v |= static_cast<u32>((w >> (a & 63)) & 1ull) << (8 * j);
+    }
+    reinterpret_cast<u32*>(block)[wi] = v;
+  }
+  for (int b = 4 * words + lane; b < bytes; b += 32) {
+    const int r = b / (int)kActions, a = b - r * (int)kActions;
+    block[b] = static_cast<uint8_t>((t.legal[r][a >> 6] >> (a & 63)) & 1ull);
+  }
+}
+
+__device__ __forceinline__ u32 torch_action(i64 raw) {
+  return raw >= 0 && raw < (i64)kActions ? static_cast<u32>(raw) : kNoAction;
+}
+
+// ---- kernels -------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kBlock) create_kernel(const i64* __restrict__ seeds,
+                                                        const i64* __restrict__ first, i64 n,
+                                                        u64* __restrict__ rows) {
+  WarpTile& t = my_tile();
+  const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
+  Game g;
+  if (row < n) create_game(g, static_cast<u64>(__ldg(seeds + row)), static_cast<u32>(__ldg(first + row) & 1));
+  else for (int k = 0; k < kRowWords; ++k) g.w[k] = 0;
+  store_game(t, g);
+  scatter_rows(t, rows, row < n ? row : -1);
+}
+
+// observe / observe_indexed: ids == nullptr reads row i for output i.
+__global__ void __launch_bounds__(kBlock) observe_kernel(
+    const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids, i64 m,
+    float* __restrict__ features, bool* __restrict__ legal, uint8_t* __restrict__ players,
+    bool* __restrict__ done, int16_t* __restrict__ status) {
+  WarpTile& t = my_tile();
+  const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
+  const i64 src = lane_source(ids, row, m, n_states);
+  gather_rows(t, states, src);
+  Game g;
+  load_game(t, g);
+  __syncwarp();
+  ObsPacket pk;
+  ObsMeta meta;
+  if (src >= 0) {
+    observe_game(g, pk, meta);
+  } else {
+    for (u32 k = 0; k < kBitWords; ++k) pk.bits[k] = 0;
+    for (u32 k = 0; k < kScalarColumns; ++k) pk.scal[k] = 0.0f;
+    meta.legal = Legal{};
+    meta.player = 0;
+    meta.done = 1;
+    meta.status = -1;
+  }
+  store_packet(t, pk, meta.legal);
+  const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
+  const i64 left = m - tile_base;
+  const int rows_here = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
+  emit_features(t, features, tile_base, rows_here);
+  emit_legal(t, legal, tile_base, rows_here);
+  if (row < m) {
+    players[row] = static_cast<uint8_t>(meta.player);
+    done[row] = meta.done != 0;
+    status[row] = static_cast<int16_t>(meta.status);
+  }
+}
+
+// step / step_indexed / step_events_indexed / branch_indexed.
+//   ids == nullptr: row i steps state i in place.
+//   children != nullptr: the stepped copy goes to children[i] (branch); the
+//   parent row is not written; a bad id gives a zero child.
+__global__ void __launch_bounds__(kBlock) step_kernel(
+    u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids,
+    const i64* __restrict__ actions, i64 m, u64* __restrict__ children,
+    float* __restrict__ reward, bool* __restrict__ done, bool* __restrict__ nagari,
+    int16_t* __restrict__ status, bool* __restrict__ committed, i64* __restrict__ events) {
+  WarpTile& t = my_tile();
+  const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
+  const i64 src = lane_source(ids, row, m, n_states);
+  gather_rows(t, states, src);
+  Game g;
+  load_game(t, g);
+  __syncwarp();
+  StepOut out{static_cast<u32>(-1), 0, 1, 0, 0};
+  i64 ev[kEventWords];
+#pragma unroll
+  for (int k = 0; k < (int)kEventWords; ++k) ev[k] = 0;
+  if (src >= 0) {
+    const EventBase before = event_base(g);
+    out = step_game(g, torch_action(__ldg(actions + row)));
+    if (events && out.committed) event_words(before, g, ev);
+  } else if (children) {
+    for (int k = 0; k < kRowWords; ++k) g.w[k] = 0;
+  }
+  store_game(t, g);
+  if (children) scatter_rows(t, children, row < m ? row : -1);
+  else scatter_rows(t, states, src);
+  if (row < m) {
+    reward[row] = static_cast<float>(out.reward0);
+    done[row] = out.done != 0;
+    nagari[row] = out.nagari != 0;
+    status[row] = static_cast<int16_t>(static_cast<i32>(out.status));
+    committed[row] = out.committed != 0;
+    if (events) {
+#pragma unroll
+      for (int k = 0; k < (int)kEventWords; ++k) events[row * kEventWords + k] = ev[k];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kBlock) clone_kernel(const u64* __restrict__ states, i64 n_states,
+                                                       const i64* __restrict__ ids, i64 m,
+                                                       u64* __restrict__ children) {
+  WarpTile& t = my_tile();
+  const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
+  gather_rows(t, states, lane_source(ids, row, m, n_states));
+  scatter_rows(t, children, row < m ? row : -1);
+}
+
+__global__ void hands_kernel(const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids,
+                             i64 m, i64* __restrict__ hands) {
+  const i64 row = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= m) return;
+  const i64 id = lane_source(ids, row, m, n_states);
+  const u64 h0 = id >= 0 ? __ldg(states + id * kRowWords + 0) : 0;
+  const u64 h1 = id >= 0 ? __ldg(states + id * kRowWords + 1) : 0;
+  reinterpret_cast<longlong2*>(hands)[row] = make_longlong2((long long)h0, (long long)h1);
+}
+
+__global__ void stock_kernel(const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids,
+                             i64 m, i64* __restrict__ out) {
+  const i64 row = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= m) return;
+  const i64 id = lane_source(ids, row, m, n_states);
+  u64 packed = ~0ull;
+  if (id >= 0) {
+    Game g;
+    g.w[3] = __ldg(states + id * kRowWords + 3);
+    g.w[6] = __ldg(states + id * kRowWords + 6);
+    packed = stock_preview(g);
+  }
+  out[row] = static_cast<i64>(packed);
+}
+
+__global__ void start_kernel(const u64* __restrict__ states, i64 n, i64* __restrict__ out) {
+  const i64 row = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= n) return;
+  Game g;
+  const u64* s = states + row * kRowWords;
+  g.w[0] = __ldg(s + 0);
+  g.w[1] = __ldg(s + 1);
+  g.w[2] = __ldg(s + 2);
+  g.w[4] = __ldg(s + 4);
+  g.w[5] = __ldg(s + 5);
+  g.w[9] = __ldg(s + 9);
+  g.w[10] = __ldg(s + 10);
+  g.w[11] = __ldg(s + 11);
+  g.w[18] = __ldg(s + 18);
+  g.w[19] = __ldg(s + 19);
+  start_words(g, out + row * kStartWords);
+}
+
+// ---- launch helpers ------------------------------------------------------------
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+inline int launch_status() {
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+inline unsigned blocks_for(i64 n, int per_block) { return static_cast<unsigned>((n + per_block - 1) / per_block); }
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_abi_version(void) { return CUGO_B200_ABI_VERSION; }
+int64_t cugo_b200_state_bytes(void) { return kRowBytes; }
+int64_t cugo_b200_feature_count(void) { return kFeatures; }
+int64_t cugo_b200_action_count(void) { return kActions; }
+int64_t cugo_b200_primary_action_count(void) { return kPrimaryActions; }
+int64_t cugo_b200_choice_action_begin(void) { return kChoiceBegin; }
+int64_t cugo_b200_event_words(void) { return kEventWords; }
+int64_t cugo_b200_start_words(void) { return kStartWords; }
+int64_t cugo_b200_status_ok(void) { return kOk; }
+
+int cugo_b200_create(const int64_t* seeds, const int64_t* first_players, int64_t n,
+                     uint8_t* states, cudaStream_t stream) {
+  if (n < 0 || (n > 0 && (!seeds || !first_players || !states))) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8)) return CUGO_B200_ERR_ALIGN;
+  if (n == 0) return CUGO_B200_OK;
+  create_kernel<<<blocks_for(n, kBlock), kBlock, 0, stream>>>(seeds, first_players, n,
+                                                             reinterpret_cast<u64*>(states));
+  return launch_status();
+}
+
+static int observe_common(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                          int64_t m, float* features, bool* legal, uint8_t* players, bool* done,
+                          int16_t* status, cudaStream_t stream) {
+  if (n_states < 0 || m < 0) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (!features || !legal || !players || !done || !status)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(features, 16) || !aligned(legal, 4)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  observe_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<const u64*>(states), n_states, env_ids, m, features, legal, players, done,
+      status);
+  return launch_status();
+}
+
+int cugo_b200_observe(const uint8_t* states, int64_t n, float* features, bool* legal,
+                      uint8_t* players, bool* done, int16_t* status, cudaStream_t stream) {
+  return observe_common(states, n, nullptr, n, features, legal, players, done, status, stream);
+}
+
+int cugo_b200_observe_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                              int64_t m, float* features, bool* legal, uint8_t* players,
+                              bool* done, int16_t* status, cudaStream_t stream) {
+  if (m > 0 && !env_ids) return CUGO_B200_ERR_ARG;
+  return observe_common(states, n_states, env_ids, m, features, legal, players, done, status,
+                        stream);
+}
+
+static int step_common(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                       const int64_t* actions, int64_t m, uint8_t* children, float* reward,
+                       bool* done, bool* nagari, int16_t* status, bool* committed,
+                       int64_t* events, cudaStream_t stream) {
+  if (n_states < 0 || m < 0) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (!actions || !reward || !done || !nagari || !status || !committed))
+    return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(children, 8) || !aligned(events, 8)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  step_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<u64*>(states), n_states, env_ids, actions, m,
+      reinterpret_cast<u64*>(children), reward, done, nagari, status, committed, events);
+  return launch_status();
+}
+
+int cugo_b200_step(uint8_t* states, int64_t n, const int64_t* actions, float* reward, bool* done,
+                   bool* nagari, int16_t* status, bool* committed, cudaStream_t stream) {
+  return step_common(states, n, nullptr, actions, n, nullptr, reward, done, nagari, status,
+                     committed, nullptr, stream);
+}
+
+int cugo_b200_step_indexed(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                           const int64_t* actions, int64_t m, float* reward, bool* done,
+                           bool* nagari, int16_t* status, bool* committed, cudaStream_t stream) {
+  if (m > 0 && !env_ids) return CUGO_B200_ERR_ARG;
+  return step_common(states, n_states, env_ids, actions, m, nullptr, reward, done, nagari, status,
+                     committed, nullptr, stream);
+}
+
+int cugo_b200_step_events_indexed(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                                  const int64_t* actions, int64_t m, float* reward, bool* done,
+                                  bool* nagari, int16_t* status, bool* committed, int64_t* events,
+                                  cudaStream_t stream) {
+  if (m > 0 && (!env_ids || !events)) return CUGO_B200_ERR_ARG;
+  return step_common(states, n_states, env_ids, actions, m, nullptr, reward, done, nagari, status,
+                     committed, events, stream);
+}
+
+int cugo_b200_branch_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                             const int64_t* actions, int64_t m, uint8_t* children, float* reward,
+                             bool* done, bool* nagari, int16_t* status, bool* committed,
+                             cudaStream_t stream) {
+  if (m > 0 && (!env_ids || !children)) return CUGO_B200_ERR_ARG;
+  return step_common(const_cast<uint8_t*>(states), n_states, env_ids, actions, m, children, reward,
+                     done, nagari, status, committed, nullptr, stream);
+}
+
+int cugo_b200_clone_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                            int64_t m, uint8_t* children, cudaStream_t stream) {
+  if (n_states < 0 || m < 0 || (m > 0 && (!env_ids || !children))) return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(children, 8)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  clone_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<const u64*>(states), n_states, env_ids, m, reinterpret_cast<u64*>(children));
+  return launch_status();
+}
+
+int cugo_b200_hands_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                            int64_t m, int64_t* hands, cudaStream_t stream) {
+  if (n_states < 0 || m < 0 || (m > 0 && (!env_ids || !hands))) return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(hands, 16)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  hands_kernel<<<blocks_for(m, 256), 256, 0, stream>>>(reinterpret_cast<const u64*>(states), n_states,
+                                                       env_ids, m, hands);
+  return launch_status();
+}
+
+int cugo_b200_stock_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                            int64_t m, int64_t* stock, cudaStream_t stream) {
+  if (n_states < 0 || m < 0 || (m > 0 && (!env_ids || !stock))) return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  stock_kernel<<<blocks_for(m, 256), 256, 0, stream>>>(reinterpret_cast<const u64*>(states), n_states,
+                                                       env_ids, m, stock);
+  return launch_status();
+}
+
+int cugo_b200_start(const uint8_t* states, int64_t n, int64_t* out, cudaStream_t stream) {
+  if (n < 0 || (n > 0 && (!states || !out))) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8)) return CUGO_B200_ERR_ALIGN;
+  if (n == 0) return CUGO_B200_OK;
+  start_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(reinterpret_cast<const u64*>(states), n, out);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,350 @@
+"""Drop-in for the reference's extension loader (python/cugo_torch50_ext.py:141-193).
+
+``load_extension()`` returns an object with the reference module's 11 ops and 8
+constants (python/csrc/torch50_ext.cpp:36-72): same names, argument order, output
+shapes, dtypes, list return values and RuntimeError messages.  Each op checks its
+tensors on the host, allocates its outputs with ``torch.empty`` on the states'
+device and enqueues one kernel of libcugo_b200.so on the current CUDA stream — no
+host synchronisation, so the ops can be captured in CUDA graphs.
+
+There is no CPU path: without CUDA or without the native library the loader raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+from typing import Any
+
+import torch
+
+from . import build as _build
+
+_VP, _I64, _I32, _U32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32
+
+# name -> argument types after the leading pointers (all return int status)
+_SIGNATURES: dict[str, list] = {
+    "cugo_b200_create": [_VP, _VP, _I64, _VP, _VP],
+    "cugo_b200_observe": [_VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_observe_indexed": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_step": [_VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_step_indexed": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_step_events_indexed": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_branch_indexed": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_clone_indexed": [_VP, _I64, _VP, _I64, _VP, _VP],
+    "cugo_b200_hands_indexed": [_VP, _I64, _VP, _I64, _VP, _VP],
+    "cugo_b200_stock_indexed": [_VP, _I64, _VP, _I64, _VP, _VP],
+    "cugo_b200_start": [_VP, _I64, _VP, _VP],
+    "cugo_b200_rollout_random": [_I64, _I64, _I64, _I32, _U32, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_selfplay_random_step": [_VP, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_branch_roots": [_I64, _I64, _VP, _VP],
+    "cugo_b200_branch_actions": [_VP, _I64, _I64, _I64, _VP, _VP, _VP],
+}
+_CONSTANTS = {
+    "FEATURE_COUNT": "cugo_b200_feature_count",
+    "ACTION_COUNT": "cugo_b200_action_count",
+    "PRIMARY_ACTION_COUNT": "cugo_b200_primary_action_count",
+    "CHOICE_ACTION_BEGIN": "cugo_b200_choice_action_begin",
+    "EVENT_WORDS": "cugo_b200_event_words",
+    "START_WORDS": "cugo_b200_start_words",
+    "STATE_BYTES": "cugo_b200_state_bytes",
+    "STATUS_OK": "cugo_b200_status_ok",
+}
+_ERRORS = {-1: "invalid argument", -2: "misaligned pointer", -3: "kernel launch failed"}
+
+_LIB: ctypes.CDLL | None = None
+
+
+def library_path() -> Path:
+    return _build.LIB
+
+
+def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
+    """dlopen libcugo_b200.so (building it first when it is missing)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = _build.LIB
+    if not path.exists():
+        if not build_if_missing:
+            raise RuntimeError(f"cugo_b200 native library missing: {path}")
+        _build.build()
+    lib = ctypes.CDLL(str(path))
+    for name, argtypes in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = ctypes.c_int
+    for fn_name in _CONSTANTS.values():
+        getattr(lib, fn_name).restype = ctypes.c_int64
+        getattr(lib, fn_name).argtypes = []
+    lib.cugo_b200_abi_version.restype = ctypes.c_int
+    _LIB = lib
+    return lib
+
+
+def _check(rc: int, op: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"cugo_b200 {op}: {_ERRORS.get(rc, f'error {rc}')}")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _check_cuda_1d(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if t.dim() != 1:
+        raise RuntimeError(f"{name} must be one-dimensional")
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} has the wrong dtype")
+
+
+def _check_states(states: torch.Tensor, state_bytes: int) -> None:
+    if not states.is_cuda:
+        raise RuntimeError("states must be a CUDA tensor")
+    if not states.is_contiguous():
+        raise RuntimeError("states must be contiguous")
+    if states.dtype != torch.uint8:
+        raise RuntimeError("states must have dtype torch.uint8")
+    if states.dim() != 2:
+        raise RuntimeError("states must have shape [N, STATE_BYTES]")
+    if states.size(1) != state_bytes:
+        raise RuntimeError("states second dimension must equal STATE_BYTES")
+
+
+def _same_device(a: torch.Tensor, b: torch.Tensor, an: str, bn: str) -> None:
+    if a.device != b.device:
+        raise RuntimeError(f"{an} and {bn} must be on the same CUDA device")
+
+
+class CugoB200Extension:
+    """The reference extension's op surface over libcugo_b200.so."""
+
+    def __init__(self, lib: ctypes.CDLL) -> None:
+        self._lib = lib
+        for attr, fn_name in _CONSTANTS.items():
+            setattr(self, attr, int(getattr(lib, fn_name)()))
+
+    # -- helpers ----------------------------------------------------------------
+    @staticmethod
+    def _stream(device: torch.device) -> int:
+        return torch.cuda.current_stream(device).cuda_stream
+
+    def _obs_outputs(self, m: int, device: torch.device) -> list[torch.Tensor]:
+        return [
+            torch.empty((m, self.FEATURE_COUNT), dtype=torch.float32, device=device),
+            torch.empty((m, self.ACTION_COUNT), dtype=torch.bool, device=device),
+            torch.empty((m,), dtype=torch.uint8, device=device),
+            torch.empty((m,), dtype=torch.bool, device=device),
+            torch.empty((m,), dtype=torch.int16, device=device),
+        ]
+
+    @staticmethod
+    def _step_outputs(m: int, device: torch.device) -> list[torch.Tensor]:
+        return [
+            torch.empty((m,), dtype=torch.float32, device=device),
+            torch.empty((m,), dtype=torch.bool, device=device),
+            torch.empty((m,), dtype=torch.bool, device=device),
+            torch.empty((m,), dtype=torch.int16, device=device),
+            torch.empty((m,), dtype=torch.bool, device=device),
+        ]
+
+    def _states(self, states: torch.Tensor) -> None:
+        _check_states(states, self.STATE_BYTES)
+
+    # -- ops (python/csrc/torch50_ext.cpp:38-59) --------------------------------
+    def create(self, seeds: torch.Tensor, first_players: torch.Tensor) -> torch.Tensor:
+        _check_cuda_1d(seeds, torch.int64, "seeds")
+        _check_cuda_1d(first_players, torch.int64, "first_players")
+        if seeds.numel() != first_players.numel():
+            raise RuntimeError("seeds and first_players must have the same length")
+        _same_device(seeds, first_players, "seeds", "first_players")
+        n = seeds.numel()
+        with torch.cuda.device(seeds.device):
+            states = torch.empty((n, self.STATE_BYTES), dtype=torch.uint8, device=seeds.device)
+            _check(self._lib.cugo_b200_create(_ptr(seeds), _ptr(first_players), n, _ptr(states),
+                                              self._stream(seeds.device)), "create")
+        return states
+
+    def observe(self, states: torch.Tensor) -> list[torch.Tensor]:
+        self._states(states)
+        n = states.size(0)
+        with torch.cuda.device(states.device):
+            out = self._obs_outputs(n, states.device)
+            _check(self._lib.cugo_b200_observe(_ptr(states), n, *map(_ptr, out),
+                                               self._stream(states.device)), "observe")
+        return out
+
+    def observe_indexed(self, states: torch.Tensor, env_ids: torch.Tensor) -> list[torch.Tensor]:
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _same_device(states, env_ids, "states", "env_ids")
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            out = self._obs_outputs(m, states.device)
+            _check(self._lib.cugo_b200_observe_indexed(
+                _ptr(states), states.size(0), _ptr(env_ids), m, *map(_ptr, out),
+                self._stream(states.device)), "observe_indexed")
+        return out
+
+    def step(self, states: torch.Tensor, actions: torch.Tensor) -> list[torch.Tensor]:
+        self._states(states)
+        _check_cuda_1d(actions, torch.int64, "actions")
+        if states.size(0) != actions.numel():
+            raise RuntimeError("states and actions must have the same batch size")
+        _same_device(states, actions, "states", "actions")
+        n = states.size(0)
+        with torch.cuda.device(states.device):
+            out = self._step_outputs(n, states.device)
+            _check(self._lib.cugo_b200_step(_ptr(states), n, _ptr(actions), *map(_ptr, out),
+                                            self._stream(states.device)), "step")
+        return out
+
+    def _indexed_args(self, states, env_ids, actions) -> None:
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _check_cuda_1d(actions, torch.int64, "actions")
+        if env_ids.numel() != actions.numel():
+            raise RuntimeError("env_ids and actions must have the same length")
+        _same_device(states, env_ids, "states", "env_ids")
+        _same_device(states, actions, "states", "actions")
+
+    def step_indexed(self, states, env_ids, actions) -> list[torch.Tensor]:
+        self._indexed_args(states, env_ids, actions)
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            out = self._step_outputs(m, states.device)
+            _check(self._lib.cugo_b200_step_indexed(
+                _ptr(states), states.size(0), _ptr(env_ids), _ptr(actions), m, *map(_ptr, out),
+                self._stream(states.device)), "step_indexed")
+        return out
+
+    def step_events_indexed(self, states, env_ids, actions) -> list[torch.Tensor]:
+        self._indexed_args(states, env_ids, actions)
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            out = self._step_outputs(m, states.device)
+            events = torch.empty((m, self.EVENT_WORDS), dtype=torch.int64, device=states.device)
+            _check(self._lib.cugo_b200_step_events_indexed(
+                _ptr(states), states.size(0), _ptr(env_ids), _ptr(actions), m, *map(_ptr, out),
+                _ptr(events), self._stream(states.device)), "step_events_indexed")
+        return out + [events]
+
+    def clone_indexed(self, states, env_ids) -> torch.Tensor:
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _same_device(states, env_ids, "states", "env_ids")
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            children = torch.empty((m, self.STATE_BYTES), dtype=torch.uint8, device=states.device)
+            _check(self._lib.cugo_b200_clone_indexed(
+                _ptr(states), states.size(0), _ptr(env_ids), m, _ptr(children),
+                self._stream(states.device)), "clone_indexed")
+        return children
+
+    def branch_indexed(self, states, env_ids, actions) -> list[torch.Tensor]:
+        self._indexed_args(states, env_ids, actions)
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            children = torch.empty((m, self.STATE_BYTES), dtype=torch.uint8, device=states.device)
+            out = self._step_outputs(m, states.device)
+            _check(self._lib.cugo_b200_branch_indexed(
+                _ptr(states), states.size(0), _ptr(env_ids), _ptr(actions), m, _ptr(children),
+                *map(_ptr, out), self._stream(states.device)), "branch_indexed")
+        return [children] + out
+
+    def hands_indexed(self, states, env_ids) -> torch.Tensor:
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _same_device(states, env_ids, "states", "env_ids")
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            hands = torch.empty((m, 2), dtype=torch.int64, device=states.device)
+            _check(self._lib.cugo_b200_hands_indexed(
+                _ptr(states), states.size(0), _ptr(env_ids), m, _ptr(hands),
+                self._stream(states.device)), "hands_indexed")
+        return hands
+
+    def stock_indexed(self, states, env_ids) -> torch.Tensor:
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _same_device(states, env_ids, "states", "env_ids")
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            stock = torch.empty((m,), dtype=torch.int64, device=states.device)
+            _check(self._lib.cugo_b200_stock_indexed(
+                _ptr(states), states.size(0), _ptr(env_ids), m, _ptr(stock),
+                self._stream(states.device)), "stock_indexed")
+        return stock
+
+    def start(self, states) -> torch.Tensor:
+        self._states(states)
+        n = states.size(0)
+        with torch.cuda.device(states.device):
+            out = torch.empty((n, self.START_WORDS), dtype=torch.int64, device=states.device)
+            _check(self._lib.cugo_b200_start(_ptr(states), n, _ptr(out),
+                                             self._stream(states.device)), "start")
+        return out
+
+    # -- benchmark drivers (no counterpart in the reference extension) ----------
+    def rollout_random(self, game0: int, n: int, seed_base: int = 12345, max_decisions: int = 256,
+                       stream_id: int = 0, device: torch.device | str = "cuda") -> dict[str, Any]:
+        device = torch.device(device)
+        with torch.cuda.device(device):
+            out = dict(
+                final_rows=torch.empty((n, self.STATE_BYTES), dtype=torch.uint8, device=device),
+                reward0=torch.empty((n,), dtype=torch.int64, device=device),
+                decisions=torch.empty((n,), dtype=torch.int32, device=device),
+                events=torch.empty((n,), dtype=torch.int32, device=device),
+                hashes=torch.empty((n,), dtype=torch.int64, device=device),
+                last_status=torch.empty((n,), dtype=torch.int16, device=device),
+            )
+            _check(self._lib.cugo_b200_rollout_random(
+                game0, n, seed_base, max_decisions, stream_id, _ptr(out["final_rows"]),
+                _ptr(out["reward0"]), _ptr(out["decisions"]), _ptr(out["events"]),
+                _ptr(out["hashes"]), _ptr(out["last_status"]), self._stream(device)),
+                "rollout_random")
+        return out
+
+    def selfplay_random_step(self, states, slot_game, slot_decision, slot_completed, slot_steps,
+                             features, legal, seed_base: int = 12345) -> None:
+        n = states.size(0)
+        with torch.cuda.device(states.device):
+            _check(self._lib.cugo_b200_selfplay_random_step(
+                _ptr(states), n, seed_base, _ptr(slot_game), _ptr(slot_decision),
+                _ptr(slot_completed), _ptr(slot_steps), _ptr(features), _ptr(legal),
+                self._stream(states.device)), "selfplay_random_step")
+
+    def branch_roots(self, n_roots: int, seed_base: int = 12345,
+                     device: torch.device | str = "cuda") -> torch.Tensor:
+        device = torch.device(device)
+        with torch.cuda.device(device):
+            roots = torch.empty((n_roots, self.STATE_BYTES), dtype=torch.uint8, device=device)
+            _check(self._lib.cugo_b200_branch_roots(n_roots, seed_base, _ptr(roots),
+                                                    self._stream(device)), "branch_roots")
+        return roots
+
+    def branch_actions(self, roots: torch.Tensor, per_root: int, seed_base: int = 12345):
+        n = roots.size(0) * per_root
+        with torch.cuda.device(roots.device):
+            ids = torch.empty((n,), dtype=torch.int64, device=roots.device)
+            actions = torch.empty((n,), dtype=torch.int64, device=roots.device)
+            _check(self._lib.cugo_b200_branch_actions(
+                _ptr(roots), roots.size(0), per_root, seed_base, _ptr(ids), _ptr(actions),
+                self._stream(roots.device)), "branch_actions")
+        return ids, actions
+
+
+_EXT: CugoB200Extension | None = None
+
+
+def load_extension(*, verbose: bool = False) -> CugoB200Extension:
+    """Same contract as the reference's load_extension(): CUDA is required."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("PyTorch CUDA is not available")
+    global _EXT
+    if _EXT is None:
+        _EXT = CugoB200Extension(load_library())
+    return _EXT

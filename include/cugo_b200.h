@@ -1,0 +1,164 @@
+/* cugo_b200 — C ABI of the B200 batch environment for Hangame Shin Matgo.
+ *
+ * Each entry point replaces one op of the reference's pybind extension
+ * (python/csrc/torch50_ext.cpp:36-59, host wrappers python/csrc/torch50_ext.cu:478-686)
+ * with the same arguments, output shapes and semantics, but as plain device
+ * pointers and sizes:
+ *
+ *   states    uint8 [n_states, 248]  game rows, byte-compatible with the
+ *                                    reference's TorchEnv50 (8-byte aligned)
+ *   env_ids   int64 [m]              rows to read; an id outside [0, n_states)
+ *                                    gives the documented "invalid id" outputs
+ *   actions   int64 [m]              unified actions 0..178; other values are
+ *                                    "not legal" (status 3), state unchanged
+ *   features  float [m, 720]         16-byte aligned
+ *   legal     bool  [m, 179]         4-byte aligned
+ *
+ * All pointers are device pointers of the current device.  Every call only
+ * enqueues work on `stream` (no host synchronisation, no allocation), so calls
+ * can be captured in CUDA graphs.  Return value: CUGO_B200_OK or a negative
+ * CUGO_B200_ERR_* for a bad argument, a misaligned pointer or a launch
+ * failure; per-row game errors are reported in the status outputs, never as
+ * device faults.  Indexed ops that step (step_indexed, step_events_indexed)
+ * must not list the same env id twice in one call.
+ */
+#ifndef CUGO_B200_H
+#define CUGO_B200_H
+
+#include <stdbool.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* cudaStream_t;
+
+#if defined(__GNUC__)
+#define CUGO_B200_API __attribute__((visibility("default")))
+#else
+#define CUGO_B200_API
+#endif
+
+#define CUGO_B200_ABI_VERSION 1
+#define CUGO_B200_OK 0
+#define CUGO_B200_ERR_ARG (-1)
+#define CUGO_B200_ERR_ALIGN (-2)
+#define CUGO_B200_ERR_LAUNCH (-3)
+
+CUGO_B200_API int cugo_b200_abi_version(void);
+
+/* Contract constants (python/csrc/torch50_ext.cpp:61-71). */
+CUGO_B200_API int64_t cugo_b200_state_bytes(void);          /* STATE_BYTES = 248 */
+CUGO_B200_API int64_t cugo_b200_feature_count(void);        /* FEATURE_COUNT = 720 */
+CUGO_B200_API int64_t cugo_b200_action_count(void);         /* ACTION_COUNT = 179 */
+CUGO_B200_API int64_t cugo_b200_primary_action_count(void); /* PRIMARY_ACTION_COUNT = 127 */
+CUGO_B200_API int64_t cugo_b200_choice_action_begin(void);  /* CHOICE_ACTION_BEGIN = 127 */
+CUGO_B200_API int64_t cugo_b200_event_words(void);          /* EVENT_WORDS = 9 */
+CUGO_B200_API int64_t cugo_b200_start_words(void);          /* START_WORDS = 8 */
+CUGO_B200_API int64_t cugo_b200_status_ok(void);            /* STATUS_OK = 0 */
+
+/* create (torch50_ext.cu:478-499): fresh games from (seed, first_player & 1). */
+CUGO_B200_API int cugo_b200_create(const int64_t* seeds, const int64_t* first_players, int64_t n,
+                     uint8_t* states, cudaStream_t stream);
+
+/* observe (torch50_ext.cu:501-518): features, legal mask, deciding player,
+ * done flag and packet status of every row; read only. */
+CUGO_B200_API int cugo_b200_observe(const uint8_t* states, int64_t n, float* features, bool* legal,
+                      uint8_t* players, bool* done, int16_t* status, cudaStream_t stream);
+
+/* observe_indexed (torch50_ext.cu:520-544): the same for rows env_ids; an invalid
+ * id gives zero features, no legal action, player 0, done 1, status -1. */
+CUGO_B200_API int cugo_b200_observe_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                              int64_t m, float* features, bool* legal, uint8_t* players,
+                              bool* done, int16_t* status, cudaStream_t stream);
+
+/* step (torch50_ext.cu:546-569): applies actions[i] to row i in place; outputs
+ * player 0's reward (final once done), done, nagari, status and whether a
+ * primary action was committed. */
+CUGO_B200_API int cugo_b200_step(uint8_t* states, int64_t n, const int64_t* actions, float* reward, bool* done,
+                   bool* nagari, int16_t* status, bool* committed, cudaStream_t stream);
+
+/* step_indexed (torch50_ext.cu:571-600): rows env_ids in place; an invalid id
+ * gives reward 0, done 1, nagari 0, status -1, committed 0. */
+CUGO_B200_API int cugo_b200_step_indexed(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                           const int64_t* actions, int64_t m, float* reward, bool* done,
+                           bool* nagari, int16_t* status, bool* committed, cudaStream_t stream);
+
+/* step_events_indexed (torch50_ext.cu:626-660): step_indexed plus the committed
+ * action's event record, int64 [m, 9] (zero when nothing was committed). */
+CUGO_B200_API int cugo_b200_step_events_indexed(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                                  const int64_t* actions, int64_t m, float* reward, bool* done,
+                                  bool* nagari, int16_t* status, bool* committed, int64_t* events,
+                                  cudaStream_t stream);
+
+/* branch_indexed (torch50_ext.cu:703-734): children[i] = row env_ids[i] stepped
+ * with actions[i]; parents are not written; an invalid id gives a zero child
+ * and the invalid-id step outputs. */
+CUGO_B200_API int cugo_b200_branch_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                             const int64_t* actions, int64_t m, uint8_t* children, float* reward,
+                             bool* done, bool* nagari, int16_t* status, bool* committed,
+                             cudaStream_t stream);
+
+/* clone_indexed (torch50_ext.cu:679-701): children[i] = row env_ids[i], zero row
+ * for an invalid id. */
+CUGO_B200_API int cugo_b200_clone_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                            int64_t m, uint8_t* children, cudaStream_t stream);
+
+/* hands_indexed (torch50_ext.cu:736-758): int64 [m, 2] hand masks, 0 when invalid. */
+CUGO_B200_API int cugo_b200_hands_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                            int64_t m, int64_t* hands, cudaStream_t stream);
+
+/* stock_indexed (torch50_ext.cu:602-624): int64 [m], the next 8 stock draws one
+ * card id per byte (0xFF past the end); -1 when invalid. */
+CUGO_B200_API int cugo_b200_stock_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                            int64_t m, int64_t* stock, cudaStream_t stream);
+
+/* start (torch50_ext.cu:662-677): int64 [n, 8] opening records. */
+CUGO_B200_API int cugo_b200_start(const uint8_t* states, int64_t n, int64_t* out, cudaStream_t stream);
+
+/* ---- Benchmark drivers ------------------------------------------------------
+ * These have no counterpart in the reference's extension: they run the seeded
+ * random-legal rule of the benchmark configurations on the GPU.  Game i uses
+ * seed seed_base + i and first player i & 1; decision d of game i takes the
+ * floor(r0 * n / 2^32)-th of its n legal actions, with r0 the first word of
+ * Philox4x32-10(counter {i lo, i hi, d, stream}, key {seed lo, seed hi}).
+ */
+
+/* Plays games game0 .. game0+n-1 to the end (at most max_decisions steps each):
+ * final rows [n, 248], player 0's reward, decisions taken, events committed,
+ * FNV-1a 64 hash of the start record and every event record, last step status
+ * (-2 when a game had no legal action). */
+CUGO_B200_API int cugo_b200_rollout_random(int64_t game0, int64_t n, int64_t seed_base,
+                                           int32_t max_decisions, uint32_t stream_id,
+                                           uint8_t* final_rows, int64_t* reward0,
+                                           int32_t* decisions, int32_t* events, uint64_t* hashes,
+                                           int16_t* last_status, cudaStream_t stream);
+
+/* One decision of every slot: a finished game is replaced by game index +
+ * n_slots (counted in slot_completed), then the slot's observation is written to
+ * features/legal exactly as observe() writes it, a random legal action is drawn
+ * and stepped (counted in slot_steps). */
+CUGO_B200_API int cugo_b200_selfplay_random_step(uint8_t* states, int64_t n_slots,
+                                                 int64_t seed_base, int64_t* slot_game,
+                                                 int32_t* slot_decision, int32_t* slot_completed,
+                                                 int64_t* slot_steps, float* features, bool* legal,
+                                                 cudaStream_t stream);
+
+/* Branching roots: game r advanced by k_r random-legal decisions, k_r uniform in
+ * 0..20 (stream 2, decision 0xFFFF), stopping before a decision that would end
+ * the game. */
+CUGO_B200_API int cugo_b200_branch_roots(int64_t n_roots, int64_t seed_base, uint8_t* roots,
+                                         cudaStream_t stream);
+
+/* Branch i = r * per_root + b: env_ids[i] = r and a random legal action of root
+ * r drawn from stream 1 with counter {r, b} (-1 when the root has none). */
+CUGO_B200_API int cugo_b200_branch_actions(const uint8_t* roots, int64_t n_roots,
+                                           int64_t per_root, int64_t seed_base, int64_t* env_ids,
+                                           int64_t* actions, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -138,3 +138,27 @@ def rollout_random(game0: int, n: int, seed_base: int = 12345, max_decisions: in
         ctypes.c_int(threads or default_threads()))
     return dict(final_rows=final_rows, reward0=reward0, decisions=decisions, events=events,
                 hashes=hashes, last_status=last_status)
+
+
+def branch_roots(n_roots: int, seed_base: int = 12345, threads: int | None = None) -> np.ndarray:
+    rows = np.zeros((n_roots, STATE_BYTES), dtype=np.uint8)
+    lib().cugo_ref_branch_roots(ctypes.c_int64(n_roots), ctypes.c_int64(seed_base), _p(rows),
+                                ctypes.c_int(threads or default_threads()))
+    return rows
+
+
+def branch_actions(roots: np.ndarray, per_root: int, seed_base: int = 12345):
+    roots = np.ascontiguousarray(roots, dtype=np.uint8)
+    n = roots.shape[0] * per_root
+    ids = np.zeros(n, dtype=np.int64)
+    actions = np.zeros(n, dtype=np.int64)
+    lib().cugo_ref_branch_actions(_p(roots), ctypes.c_int64(roots.shape[0]), ctypes.c_int64(per_root),
+                                  ctypes.c_int64(seed_base), _p(ids), _p(actions))
+    return ids, actions
+
+
+def philox_word(game: int, decision: int, stream: int, seed: int) -> int:
+    fn = lib().cugo_ref_philox_word
+    fn.restype = ctypes.c_uint32
+    fn.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64]
+    return int(fn(game & (2**64 - 1), decision, stream, seed & (2**64 - 1)))

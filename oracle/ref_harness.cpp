@@ -262,4 +262,57 @@ void cugo_ref_rollout_random(int64_t game0, int64_t n, int64_t seed_base, int ma
   });
 }
 
+// Branching roots (config 2): game r advanced by k_r random-legal decisions,
+// k_r = floor(r0 * 21 / 2^32) with r0 from (game r, decision 0xFFFF, stream 2),
+// stopping before a decision that would end the game.
+void cugo_ref_branch_roots(int64_t n_roots, int64_t seed_base, uint8_t* rows, int threads) {
+  parallel_rows(n_roots, threads, [&](int64_t lo, int64_t hi) {
+    for (int64_t r = lo; r < hi; ++r) {
+      const uint64_t seed = static_cast<uint64_t>(seed_base + r);
+      TorchEnv50 env = make_torch_env50(seed, static_cast<uint8_t>(r & 1));
+      const uint32_t k = static_cast<uint32_t>(
+          (static_cast<uint64_t>(oracle_driver_word(static_cast<uint64_t>(r), 0xffffu, 2u, seed)) * 21u) >> 32);
+      for (uint32_t d = 0; d < k && env.done == 0; ++d) {
+        const TorchPacket50 packet = make_torch_packet50(env);
+        uint8_t legal[kTorch50ActionCount];
+        for (uint16_t a = 0; a < kTorch50ActionCount; ++a)
+          legal[a] = has_torch_action50(packet.legal_actions, a) ? 1 : 0;
+        const int pick = oracle_pick_legal(legal, kTorch50ActionCount,
+                                           oracle_driver_word(static_cast<uint64_t>(r), d, 0u, seed));
+        if (pick < 0) break;
+        TorchEnv50 next = env;
+        torch_step50(next, static_cast<uint16_t>(pick));
+        if (next.done != 0) break;
+        env = next;
+      }
+      canonical_row(env, rows + r * 248);
+    }
+  });
+}
+
+// Branch i = r * per_root + b of config 2: env id r and the legal action of root r
+// drawn with counter {r, b, 0, 1} (-1 when the root has none).
+void cugo_ref_branch_actions(const uint8_t* roots, int64_t n_roots, int64_t per_root,
+                             int64_t seed_base, int64_t* ids, int64_t* actions) {
+  for (int64_t r = 0; r < n_roots; ++r) {
+    const TorchEnv50 env = load_row(roots + r * 248);
+    const TorchPacket50 packet = make_torch_packet50(env);
+    uint8_t legal[kTorch50ActionCount];
+    for (uint16_t a = 0; a < kTorch50ActionCount; ++a)
+      legal[a] = has_torch_action50(packet.legal_actions, a) ? 1 : 0;
+    const uint64_t seed = static_cast<uint64_t>(seed_base + r);
+    for (int64_t b = 0; b < per_root; ++b) {
+      const uint64_t ctr = static_cast<uint64_t>(r) | (static_cast<uint64_t>(b) << 32);
+      const int pick = oracle_pick_legal(legal, kTorch50ActionCount,
+                                         oracle_driver_word(ctr, 0u, 1u, seed));
+      ids[r * per_root + b] = r;
+      actions[r * per_root + b] = pick;
+    }
+  }
+}
+
+uint32_t cugo_ref_philox_word(uint64_t game, uint32_t decision, uint32_t stream, uint64_t seed) {
+  return oracle_driver_word(game, decision, stream, seed);
+}
+
 }  // extern "C"

@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstring>
 
+#include "../../cugo_b200/csrc/engine/driver.cuh"
 #include "../../cugo_b200/csrc/engine/env.cuh"
 
 using namespace cb;
@@ -76,6 +77,15 @@ void cugo_host_start(const uint8_t* rows, int64_t n, int64_t* out) {
 
 void cugo_host_stock(const uint8_t* rows, int64_t n, int64_t* out) {
   for (int64_t i = 0; i < n; ++i) out[i] = static_cast<int64_t>(stock_preview(load(rows + i * kRowBytes)));
+}
+
+uint32_t cugo_host_philox_word(uint64_t game, uint32_t decision, uint32_t stream, uint64_t seed) {
+  return game_draw(game, decision, stream, seed).v[0];
+}
+
+void cugo_host_philox(const uint32_t* ctr, const uint32_t* key, uint32_t* out) {
+  const Philox4 p = philox4x32_10(ctr[0], ctr[1], ctr[2], ctr[3], key[0], key[1]);
+  for (int i = 0; i < 4; ++i) out[i] = p.v[i];
 }
 
 }  // extern "C"

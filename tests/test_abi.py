@@ -1,0 +1,74 @@
+"""The C ABI library loads, exports every declared entry point and validates its
+arguments on the host (CPU only: no call here reaches a kernel launch)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from cugo_b200 import ext as ext_mod
+from cugo_b200 import load_library
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "cugo_b200.h"
+
+
+def declared_symbols() -> list[str]:
+    return re.findall(r"CUGO_B200_API\s+\w+\s+(cugo_b200_\w+)\s*\(", HEADER.read_text())
+
+
+def test_library_exports_every_declared_symbol():
+    lib = load_library()
+    names = declared_symbols()
+    assert len(names) >= 24
+    for name in names:
+        assert hasattr(lib, name), name
+
+
+def test_contract_constants():
+    e = ext_mod.CugoB200Extension(load_library())
+    assert (e.FEATURE_COUNT, e.ACTION_COUNT, e.PRIMARY_ACTION_COUNT, e.CHOICE_ACTION_BEGIN,
+            e.EVENT_WORDS, e.START_WORDS, e.STATE_BYTES, e.STATUS_OK) == (720, 179, 127, 127, 9, 8,
+                                                                           248, 0)
+    assert load_library().cugo_b200_abi_version() == 1
+
+
+def test_argument_errors_without_launch():
+    lib = load_library()
+    # Negative sizes and missing pointers are rejected before any launch.
+    assert lib.cugo_b200_create(None, None, -1, None, None) == -1
+    assert lib.cugo_b200_create(None, None, 4, None, None) == -1
+    assert lib.cugo_b200_observe(None, -2, None, None, None, None, None, None) == -1
+    assert lib.cugo_b200_step_indexed(None, 4, None, None, 2, None, None, None, None, None,
+                                      None) == -1
+    # Misaligned states pointer.
+    assert lib.cugo_b200_create(8, 8, 1, 0x1003, None) == -2
+    # Empty batches are a no-op success.
+    assert lib.cugo_b200_create(None, None, 0, None, None) == 0
+    assert lib.cugo_b200_clone_indexed(None, 0, None, 0, None, None) == 0
+    assert lib.cugo_b200_start(None, 0, None, None) == 0
+
+
+@pytest.fixture()
+def cpu_ext():
+    return ext_mod.CugoB200Extension(load_library())
+
+
+def test_shim_messages_match_reference(cpu_ext):
+    e = cpu_ext
+    ids = torch.zeros(2, dtype=torch.int64)
+    with pytest.raises(RuntimeError, match="seeds must be a CUDA tensor"):
+        e.create(ids, ids)
+    with pytest.raises(RuntimeError, match="states must be a CUDA tensor"):
+        e.observe(torch.zeros((2, 248), dtype=torch.uint8))
+    with pytest.raises(RuntimeError, match="states must be a CUDA tensor"):
+        e.step_indexed(torch.zeros((2, 248), dtype=torch.uint8), ids, ids)
+
+
+def test_loader_requires_cuda(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    monkeypatch.setattr(ext_mod, "_EXT", None)
+    with pytest.raises(RuntimeError, match="PyTorch CUDA is not available"):
+        ext_mod.load_extension()
