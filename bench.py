@@ -1,0 +1,391 @@
+#!/usr/bin/env python
+"""Benchmark of the self-play hot path (prints ONE JSON line on rank 0).
+
+Headline (BASELINE metric): complete games/s of config 3 — PPO self-play with the
+3x512 residual MLP policy, 262,144 seeded games per GPU played to settlement
+(weak scaling: every rank plays its own disjoint block of deal seeds).  One step
+is one such batch: create -> {observe -> policy -> Gumbel-max sample -> step ->
+compact} until every game has ended.
+
+Also measured in the same run (inputs resident in HBM, CUDA events):
+  engine_only  config 1: 1,048,576 slots x 64 decisions of the fused
+               observe -> random-legal pick -> step kernel (auto-reset)
+  branching    config 2: 65,536 roots x 256 branches through branch_indexed
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cugo|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "complete games/s per box (3x512 MLP self-play)"
+SEED_BASE = 12345
+ARCHS = {"512x3": (512, 3), "2048x4": (2048, 4)}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["cugo", "reference"], default="cugo")
+    ap.add_argument("--games", type=int, default=262_144, help="games per GPU per step")
+    ap.add_argument("--arch", choices=sorted(ARCHS), default="512x3")
+    ap.add_argument("--no-extras", action="store_true", help="skip configs 1 and 2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---- distributed plumbing ------------------------------------------------------------
+
+def dist_init(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "cugo":
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif args.impl == "cugo":
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def all_reduce(values, world, op="sum"):
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+# ---- clocks ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+        target = str(device_index)
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            target = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:  # noqa: BLE001 - fall back to the index
+            pass
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", target], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        rows = [r.split(", ") for r in self.path.read_text().splitlines() if r.count(",") >= 8]
+        self.path.unlink(missing_ok=True)
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ---- config 3: policy self-play --------------------------------------------------------
+
+def selfplay_bench(args, world, rank, ext, policy):
+    from cugo_b200.selfplay import RoundTimer, play_batch
+
+    g = args.games
+    dev = torch.device("cuda")
+    total_steps = args.warmup + args.steps
+    # Game blocks for every step, resident in HBM before timing: rank r, step s
+    # plays games (s * world + r) * g .. + g.
+    blocks = [torch.arange(g, dtype=torch.int64, device=dev) + (s * world + rank) * g
+              for s in range(total_steps)]
+    for s in range(args.warmup):
+        play_batch(ext, policy, blocks[s])
+    barrier(world)
+    timer = RoundTimer(enabled=True)
+    launches: list[int] = []
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    results = []
+    clocks = ClockSampler(torch.cuda.current_device())
+    start.record()
+    for s in range(args.warmup, total_steps):
+        results.append(play_batch(ext, policy, blocks[s], timer=timer, launches=launches))
+    stop.record()
+    barrier(world)
+    clk = clocks.stop()
+    elapsed = start.elapsed_time(stop) / 1e3
+    games = sum(r.games for r in results)
+    decisions = sum(r.decisions for r in results)
+    bad = sum(r.bad_status for r in results)
+    tot_games, tot_dec, tot_bad = all_reduce([games, decisions, bad], world)
+    (max_elapsed,) = all_reduce([elapsed], world, op="max")
+    mlp_ms, mlp_launches, mlp_rows = timer.total_ms()
+
+    # End to end through the public API: game indices from pinned host memory,
+    # rewards read back every step.
+    host_blocks = [b.cpu().pin_memory() for b in blocks[args.warmup:]]
+    reward_host = torch.empty(g, dtype=torch.float32).pin_memory()
+    barrier(world)
+    t0 = time.perf_counter()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for hb in host_blocks:
+        idx = hb.to(dev, non_blocking=True)
+        r = play_batch(ext, policy, idx)
+        reward_host.copy_(r.reward0, non_blocking=True)
+    e_stop.record()
+    barrier(world)
+    e_elapsed = e_start.elapsed_time(e_stop) / 1e3
+    (e_max,) = all_reduce([e_elapsed], world, op="max")
+    _wall = time.perf_counter() - t0
+    return dict(games=tot_games, decisions=tot_dec, bad=tot_bad, elapsed=max_elapsed,
+                mlp_ms=mlp_ms, mlp_launches=mlp_launches, mlp_rows=mlp_rows,
+                launches=sum(launches), clocks=clk, e2e_elapsed=e_max,
+                e2e_games=tot_games, h2d=g * 8, d2h=g * 4)
+
+
+# ---- config 1 and 2: engine only -----------------------------------------------------
+
+def engine_only_bench(ext, slots=1 << 20, decisions=64, warm=3):
+    dev = torch.device("cuda")
+    idx = torch.arange(slots, dtype=torch.int64, device=dev)
+    states = ext.create(idx + SEED_BASE, idx & 1)
+    slot_game = idx.clone()
+    slot_dec = torch.zeros(slots, dtype=torch.int32, device=dev)
+    completed = torch.zeros(slots, dtype=torch.int32, device=dev)
+    steps = torch.zeros(slots, dtype=torch.int64, device=dev)
+    feats = torch.empty((slots, 720), dtype=torch.float32, device=dev)
+    legal = torch.empty((slots, 179), dtype=torch.bool, device=dev)
+    for _ in range(warm):
+        ext.selfplay_random_step(states, slot_game, slot_dec, completed, steps, feats, legal)
+    completed.zero_()
+    steps.zero_()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(decisions):
+        ext.selfplay_random_step(states, slot_game, slot_dec, completed, steps, feats, legal)
+    b.record()
+    torch.cuda.synchronize()
+    sec = a.elapsed_time(b) / 1e3
+    dec = int(steps.sum())
+    games = int(completed.sum())
+    return dict(slots=slots, decisions_per_slot=decisions, seconds=sec,
+                steps_per_s=dec / sec, games_per_s=games / sec, launches=decisions,
+                launch_ms=sec * 1e3 / decisions, decisions_per_launch=dec / decisions)
+
+
+def branching_bench(ext, roots_n=65_536, per_root=256, reps=3):
+    roots = ext.branch_roots(roots_n, seed_base=SEED_BASE)
+    ids, actions = ext.branch_actions(roots, per_root, seed_base=SEED_BASE)
+    out = ext.branch_indexed(roots, ids, actions)  # warm-up
+    del out
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        out = ext.branch_indexed(roots, ids, actions)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) / 1e3)
+        del out
+    sec = min(times)
+    n = roots_n * per_root
+    return dict(roots=roots_n, branches=n, seconds=sec, branches_per_s=n / sec)
+
+
+# ---- CPU: the reference engine (oracle/_ref) + a PyTorch-CPU policy --------------------
+
+def cpu_selfplay(games: int, arch: str, threads: int, policy_cpu=None) -> dict:
+    """Plays `games` seeded games with the reference's own engine compiled from its
+    sources (oracle/_ref) and the same residual MLP on PyTorch-CPU (fp32)."""
+    from oracle import ref
+
+    torch.set_num_threads(threads)
+    hidden, blocks = ARCHS[arch]
+    if policy_cpu is None:
+        from cugo_b200.policy import ResidualMlpPolicy
+        policy_cpu = ResidualMlpPolicy(hidden, blocks, "relu", device="cpu")
+        policy_cpu.weights = [w.float() for w in policy_cpu.weights]
+        policy_cpu.biases = [b.float() for b in policy_cpu.biases]
+    idx = np.arange(games, dtype=np.int64)
+    rows = ref.create(idx + SEED_BASE, idx & 1, threads=threads)
+    rng = np.random.default_rng(0)
+    t0 = time.perf_counter()
+    live = np.ones(games, dtype=bool)
+    decisions = 0
+    for _ in range(128):
+        f, legal, _, done, _ = ref.observe(rows, threads=threads)
+        live &= ~done
+        if not live.any():
+            break
+        sel = np.nonzero(live)[0]
+        with torch.no_grad():
+            x = torch.from_numpy(f[sel])
+            w, bb = policy_cpu.weights, policy_cpu.biases
+            h = torch.nn.functional.linear(x, w[0], bb[0])
+            for i in range(blocks):
+                h = h + torch.nn.functional.linear(
+                    torch.relu(torch.nn.functional.linear(h, w[1 + 2 * i], bb[1 + 2 * i])),
+                    w[2 + 2 * i], bb[2 + 2 * i])
+            logits = torch.nn.functional.linear(torch.relu(h), w[-1], bb[-1]).numpy()[:, :179]
+        gumbel = -np.log(-np.log(rng.random(logits.shape)))
+        score = np.where(legal[sel], logits + gumbel, -np.inf)
+        acts = np.zeros(games, dtype=np.int64)
+        acts[sel] = score.argmax(1)
+        stepped = ref.step(rows, acts, threads=threads)[0]
+        rows[sel] = stepped[sel]
+        decisions += sel.size
+    sec = time.perf_counter() - t0
+    return dict(games=games, decisions=decisions, seconds=sec, games_per_s=games / sec)
+
+
+def host_threads() -> int:
+    return max(1, len(os.sched_getaffinity(0)))
+
+
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    threads = host_threads()
+    sample = 2048
+    for _ in range(args.warmup):
+        cpu_selfplay(256, args.arch, threads)
+    runs = [cpu_selfplay(sample, args.arch, threads) for _ in range(args.steps)]
+    games = sum(r["games"] for r in runs)
+    sec = sum(r["seconds"] for r in runs)
+    value = games / sec
+    desc = (f"{sample} seeded games per step played to settlement on {threads} host threads: "
+            f"the reference's own engine (include/cugo/**, compiled by oracle/Makefile) + "
+            f"the {args.arch} ReLU residual MLP on PyTorch-CPU fp32 + Gumbel-max sampling")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "games/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded deals 12345 + i)",
+        "config": {"workload": f"config3-ppo-selfplay-{args.arch}", "games_per_step": sample,
+                   "host_threads": threads},
+        "cpu_baseline": {"value": value, "unit": "games/s", "cores": threads, "kind": "reference",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "games/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+# ---- main -------------------------------------------------------------------------------
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_init(args)
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        return
+    from cugo_b200 import load_extension
+    from cugo_b200.policy import ResidualMlpPolicy
+
+    ext = load_extension()
+    hidden, blocks = ARCHS[args.arch]
+    policy = ResidualMlpPolicy(hidden, blocks, "relu", device="cuda", seed=0)
+    sp = selfplay_bench(args, world, rank, ext, policy)
+    extras = {}
+    if not args.no_extras:
+        extras["engine_only"] = engine_only_bench(ext)
+        extras["branching"] = branching_bench(ext)
+    peaks = measured_peaks()
+    if "engine_only" in extras:
+        e = extras["engine_only"]
+        # Algorithmic bytes of one decision: observe_indexed 3,319 + mask read 179 +
+        # action 8 + step_indexed 521 (ids, action, state read + write, outputs).
+        gbs = e["steps_per_s"] * 4027 / 1e9
+        e["roofline"] = {"bound": "hbm", "bytes_per_decision": 4027, "achieved": gbs,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"]}
+    if "branching" in extras:
+        b = extras["branching"]
+        gbs = b["branches_per_s"] * 274 / 1e9
+        b["roofline"] = {"bound": "hbm", "bytes_per_branch": 274, "achieved": gbs,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"]}
+    value = sp["games"] / sp["elapsed"]
+    mlp_flops = policy.flops_per_row() * sp["mlp_rows"]
+    mlp_tflops = mlp_flops / (sp["mlp_ms"] / 1e3) / 1e12 if sp["mlp_ms"] > 0 else 0.0
+    out = {
+        "metric": METRIC, "value": value, "unit": "games/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sp["elapsed"] * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded deals (seed 12345 + game), Kaiming-normal bf16 weights (seed 0)",
+        "config": {"workload": f"config3-ppo-selfplay-{args.arch}", "games_per_gpu": args.games,
+                   "policy": f"{args.arch} residual MLP, ReLU, 179 logits + value",
+                   "parallelism": f"dp{world} (disjoint seed blocks)",
+                   "l2": "inputs exceed L2 (fp32 features of 262,144 games = 755 MB per round)"},
+        "decisions_per_s": sp["decisions"] / sp["elapsed"],
+        "bad_status": sp["bad"],
+        "e2e": {"value": sp["e2e_games"] / sp["e2e_elapsed"], "unit": "games/s",
+                "h2d_bytes_per_step": sp["h2d"], "d2h_bytes_per_step": sp["d2h"]},
+        "roofline": {"kernel": "policy MLP forward (bf16 GEMM chain)", "bound": "tensor",
+                     "achieved": mlp_tflops, "peak": peaks["bf16_tflops_sustained"],
+                     "unit": "TFLOP/s", "frac": mlp_tflops / peaks["bf16_tflops_sustained"],
+                     "traffic": None, "peak_source": peaks["source"] + " (sustained)"},
+        "clocks": sp["clocks"],
+        "gpu_launches": sp["launches"],
+        "extras": extras,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_selfplay(2048, args.arch, host_threads())
+        out["cpu_baseline"] = {
+            "value": cpu["games_per_s"], "unit": "games/s", "cores": host_threads(),
+            "kind": "reference",
+            "sample": "2048 seeded games to settlement: reference engine (oracle/_ref) + "
+                      f"{args.arch} MLP on PyTorch-CPU fp32"}
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

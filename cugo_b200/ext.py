@@ -38,6 +38,7 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_selfplay_random_step": [_VP, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_branch_roots": [_I64, _I64, _VP, _VP],
     "cugo_b200_branch_actions": [_VP, _I64, _I64, _I64, _VP, _VP, _VP],
+    "cugo_b200_sample_actions": [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _I32, _VP, _VP, _VP],
 }
 _CONSTANTS = {
     "FEATURE_COUNT": "cugo_b200_feature_count",
@@ -335,6 +336,23 @@ class CugoB200Extension:
                 _ptr(roots), roots.size(0), per_root, seed_base, _ptr(ids), _ptr(actions),
                 self._stream(roots.device)), "branch_actions")
         return ids, actions
+
+
+    # -- policy sampling ---------------------------------------------------------
+    def sample_actions(self, logits: torch.Tensor, legal: torch.Tensor, game: torch.Tensor,
+                       decision: torch.Tensor, seed_base: int = 12345, greedy: bool = False):
+        """Masked Gumbel-max (or greedy) actions and their log-probabilities."""
+        if logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+            raise RuntimeError("logits must be a row-major float32 [N, >=179] tensor")
+        m = logits.size(0)
+        with torch.cuda.device(logits.device):
+            actions = torch.empty((m,), dtype=torch.int64, device=logits.device)
+            logp = torch.empty((m,), dtype=torch.float32, device=logits.device)
+            _check(self._lib.cugo_b200_sample_actions(
+                _ptr(logits), logits.stride(0), _ptr(legal), m, _ptr(game), _ptr(decision),
+                seed_base, int(greedy), _ptr(actions), _ptr(logp), self._stream(logits.device)),
+                "sample_actions")
+        return actions, logp
 
 
 _EXT: CugoB200Extension | None = None

@@ -157,6 +157,23 @@ CUGO_B200_API int cugo_b200_branch_actions(const uint8_t* roots, int64_t n_roots
                                            int64_t per_root, int64_t seed_base, int64_t* env_ids,
                                            int64_t* actions, cudaStream_t stream);
 
+/* ---- Policy sampling ----------------------------------------------------------
+ * Replaces the sampling of the reference's collect loop (python/cugo_ppo50.py:74-82:
+ * masked_fill(-1e30), softmax + multinomial, log_softmax gather) and the
+ * Gumbel-max of its sequence self-play (python/cugo_seq_selfplay50.py:126-130).
+ * logits: fp32 [m, ld] (ld >= 179, policy logits in columns 0..178); legal:
+ * bool [m, 179]; game/decision: the row's game index and decision counter.
+ * actions[i] = argmax over legal a of logits[i, a] + g(i, a) (g = 0 when
+ * greedy), logp[i] = log_softmax(masked logits)[actions[i]]; -1 and 0 for a row
+ * with no legal action.  Noise g(i, a) = -log(-log(u)), u from word (a & 3) of
+ * Philox4x32-10({game lo, game hi, decision, 3 | (a >> 2) << 8}, {seed lo, seed hi})
+ * with seed = seed_base + game. */
+CUGO_B200_API int cugo_b200_sample_actions(const float* logits, int64_t ld, const bool* legal,
+                                           int64_t m, const int64_t* game,
+                                           const int32_t* decision, int64_t seed_base,
+                                           int32_t greedy, int64_t* actions, float* logp,
+                                           cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
