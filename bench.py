@@ -366,7 +366,8 @@ def main():
         "bad_status": sp["bad"],
         "e2e": {"value": sp["e2e_games"] / sp["e2e_elapsed"], "unit": "games/s",
                 "h2d_bytes_per_step": sp["h2d"], "d2h_bytes_per_step": sp["d2h"]},
-        "roofline": {"kernel": "policy MLP forward (bf16 GEMM chain)", "bound": "tensor",
+        "roofline": {"kernel": "policy MLP forward: tcgen05 GEMM layers (gemm_kernel)",
+                     "bound": "tensor",
                      "achieved": mlp_tflops, "peak": peaks["bf16_tflops_sustained"],
                      "unit": "TFLOP/s", "frac": mlp_tflops / peaks["bf16_tflops_sustained"],
                      "traffic": None, "peak_source": peaks["source"] + " (sustained)"},

@@ -12,6 +12,7 @@
 // 5,728-byte block of legal masks with 16-byte and 4-byte vector stores.
 // Nothing is allocated; every launch goes to the caller's stream, so all
 // entry points can be captured in a CUDA graph.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -99,9 +100,23 @@ __device__ __forceinline__ void store_packet(WarpTile& t, const ObsPacket& pk, c
   t.legal[lane][2] = legal.w2;
 }
 
+__device__ __forceinline__ void store4(float* row, int q, const float* v) {
+  __stcs(reinterpret_cast<float4*>(row) + q, make_float4(v[0], v[1], v[2], v[3]));
+}
+
+__device__ __forceinline__ void store4(__nv_bfloat16* row, int q, const float* v) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]);
+  const __nv_bfloat162 hi = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 raw;
+  raw.x = *reinterpret_cast<const u32*>(&lo);
+  raw.y = *reinterpret_cast<const u32*>(&hi);
+  __stcs(reinterpret_cast<uint2*>(row) + q, raw);
+}
+
 // Cooperative write of the tile's feature rows: row `base + r` for r < rows.
-// Lane l owns float4 columns 4l, 4l+128, ... of every row.
-__device__ __forceinline__ void emit_features(const WarpTile& t, float* __restrict__ out, i64 base,
+// Lane l owns 4-column groups l, l+32, ... of every row (fp32 or bf16 rows).
+template <typename F>
+__device__ __forceinline__ void emit_features(const WarpTile& t, F* __restrict__ out, i64 base,
                                               int rows) {
   __syncwarp();
   const int lane = threadIdx.x & 31;
@@ -118,7 +133,7 @@ __device__ __forceinline__ void emit_features(const WarpTile& t, float* __restri
       bitpos[k][j] = c & 31u;
     }
   for (int r = 0; r < rows; ++r) {
-    float4* row = reinterpret_cast<float4*>(out + (base + r) * (i64)kFeatures);
+    F* row = out + (base + r) * (i64)kFeatures;
 #pragma unroll
     for (int k = 0; k < 6; ++k) {
       const int q = lane + 32 * k;
@@ -128,7 +143,7 @@ __device__ __forceinline__ void emit_features(const WarpTile& t, float* __restri
         for (int j = 0; j < 4; ++j)
           v[j] = slot[k][j] >= 0 ? t.pk.scal[r][slot[k][j]]
                                  : ((t.pk.bits[r][word[k][j]] >> bitpos[k][j]) & 1u ? 1.0f : 0.0f);
-        __stcs(row + q, make_float4(v[0], v[1], v[2], v[3]));
+        store4(row, q, v);
       }
     }
   }
@@ -178,9 +193,10 @@ __global__ void __launch_bounds__(kBlock) create_kernel(const i64* __restrict__ 
 }
 
 // observe / observe_indexed: ids == nullptr reads row i for output i.
+template <typename F>
 __global__ void __launch_bounds__(kBlock) observe_kernel(
     const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids, i64 m,
-    float* __restrict__ features, bool* __restrict__ legal, uint8_t* __restrict__ players,
+    F* __restrict__ features, bool* __restrict__ legal, uint8_t* __restrict__ players,
     bool* __restrict__ done, int16_t* __restrict__ status) {
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
@@ -351,9 +367,23 @@ static int observe_common(const uint8_t* states, int64_t n_states, const int64_t
   if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
   if (!aligned(states, 8) || !aligned(features, 16) || !aligned(legal, 4)) return CUGO_B200_ERR_ALIGN;
   if (m == 0) return CUGO_B200_OK;
-  observe_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+  observe_kernel<float><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<const u64*>(states), n_states, env_ids, m, features, legal, players, done,
       status);
+  return launch_status();
+}
+
+int cugo_b200_observe_indexed_bf16(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                                   int64_t m, void* features, bool* legal, uint8_t* players,
+                                   bool* done, int16_t* status, cudaStream_t stream) {
+  if (n_states < 0 || m < 0 || (m > 0 && !env_ids)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (!features || !legal || !players || !done || !status)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(features, 16) || !aligned(legal, 4)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  observe_kernel<__nv_bfloat16><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<const u64*>(states), n_states, env_ids, m,
+      static_cast<__nv_bfloat16*>(features), legal, players, done, status);
   return launch_status();
 }
 

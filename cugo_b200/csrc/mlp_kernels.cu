@@ -1,0 +1,548 @@
+// bf16 GEMM with fused epilogue on the 5th-generation tensor cores (sm_100a).
+//
+//   out[M, N] = act_after(act(A[M, K] . W[N, K]^T + bias[N]) + residual[M, N])
+//
+// A and W are bf16, K-major (row-major A, nn.Linear weight layout); the product
+// accumulates in fp32 in tensor memory; out is bf16 or fp32.  This is one layer
+// of the policy/value MLP (python/cugo_ppo_nets50.py:26-64 run under bf16
+// autocast): nn.Linear + bias, then ReLU/SiLU and the residual add, fused.
+//
+// Kernel (one CTA per SM, persistent over 128 x 256 output tiles):
+//   warp 0     : TMA producer — one elected thread streams 128x64 A and 256x64 W
+//                tiles (128-byte swizzle) into a 4-stage shared-memory ring;
+//   warp 1     : owns the tensor memory (2 accumulators x 256 columns) and one
+//                thread issues tcgen05.mma (M=128, N=256, K=16) per 16-wide K
+//                slice, committing each stage back to the producer and each
+//                finished tile to the epilogue;
+//   warps 2..5 : epilogue — tcgen05.ld of their 32 TMEM lanes, bias, activation,
+//                residual; each 32-row x 128-byte chunk is transposed through a
+//                swizzled shared buffer so that every warp store writes whole
+//                128-byte row segments.  A tile's epilogue overlaps the next
+//                tile's MMAs through the second accumulator.
+// Every mbarrier wait is bounded (about 2 s of %globaltimer); a wait that runs
+// out sets *error and the kernel drains and returns instead of hanging.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include "../../include/cugo_b200.h"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;            // 16 KB
+constexpr int B_BYTES = BN * BK * 2;            // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 2 * BN;          // two accumulators
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ +
+                           BN * 4 /*bias*/ + 4 * 2 * 4096 /*epilogue staging, 2 per warp*/;
+constexpr uint64_t kWaitNs = 2'000'000'000ull;
+
+enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2 };
+
+struct Epilogue {
+  const __nv_bfloat16* bias;      // [N] or null
+  const __nv_bfloat16* residual;  // [M, ldr] or null
+  int64_t ldr;
+  void* out;
+  int64_t ldo;
+  int out_fp32;
+  int act;        // applied to acc + bias, before the residual add
+  int act_after;  // applied after the residual add
+  int m, n, k;
+  int* error;
+};
+
+// ---- PTX wrappers ------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase of parity `parity` to complete; false after ~2 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = now_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 255u) == 0 && now_ns() - t0 > kWaitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1 KB apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  uint64_t d = static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;           // leading byte offset (unused here)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;   // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;           // descriptor version
+  d |= static_cast<uint64_t>(2) << 61;           // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor of kind::f16: bf16 x bf16 -> fp32, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
+  return (1u << 4)                                  // D: fp32
+         | (1u << 7) | (1u << 10)                   // A, B: bf16
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_addr(bar))
+      : "memory");
+}
+
+#define CB_TMEM_LD32(taddr, r)                                                                  \
+  asm volatile(                                                                                 \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"  \
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"        \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),    \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),             \
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),          \
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),          \
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),          \
+        "=r"(r[31])                                                                             \
+      : "r"(taddr))
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float activate(float v, int act) {
+  if (act == kActRelu) return fmaxf(v, 0.0f);
+  if (act == kActSilu) return v / (1.0f + __expf(-v));
+  return v;
+}
+
+// ---- epilogue stores through shared memory ----------------------------------------
+//
+// A thread holds one output row of the chunk (TMEM lane = row).  Rows go to a
+// per-warp 32 x 128-byte buffer (16-byte pieces XOR-swizzled by row, so the
+// row-per-thread writes and the row-major reads are both bank-conflict free),
+// then the warp stores 4 whole 128-byte row segments per instruction.  The
+// residual comes in the same way in reverse.
+
+__device__ __forceinline__ uint32_t swz(int row, int piece) {
+  return static_cast<uint32_t>(row * 128 + ((piece ^ (row & 7)) << 4));
+}
+
+template <typename T>
+__device__ __forceinline__ void write_chunk(uint8_t* stage, const float* v, const Epilogue& ep,
+                                            int row0, int col0) {
+  constexpr int E = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte piece
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    uint4 raw;
+    T* h = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      if constexpr (sizeof(T) == 2) h[e] = __float2bfloat16_rn(v[p * E + e]);
+      else h[e] = v[p * E + e];
+    }
+    *reinterpret_cast<uint4*>(stage + swz(lane, p)) = raw;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3), p = lane & 7;
+    const int grow = row0 + r, gcol = col0 + p * E;
+    if (grow < ep.m && gcol < ep.n) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(stage + swz(r, p));
+      T* dst = reinterpret_cast<T*>(ep.out) + static_cast<int64_t>(grow) * ep.ldo + gcol;
+      if (gcol + E <= ep.n) {
+        *reinterpret_cast<uint4*>(dst) = raw;
+      } else {
+        const T* h = reinterpret_cast<const T*>(&raw);
+        for (int e = 0; gcol + e < ep.n; ++e) dst[e] = h[e];
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// Starts copying the residual of a 32-row x 64-column chunk into a staging
+// buffer (cp.async, zero-filled outside the matrix); one commit group per chunk.
+__device__ __forceinline__ void prefetch_residual(uint8_t* buf, const Epilogue& ep, int row0,
+                                                  int col0) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3), p = lane & 7;
+    const int grow = row0 + r, gcol = col0 + p * 8;
+    int bytes = 0;
+    const __nv_bfloat16* src = ep.residual;
+    if (ep.residual && grow < ep.m && gcol < ep.n) {
+      bytes = 2 * (ep.n - gcol < 8 ? ep.n - gcol : 8);
+      src = ep.residual + static_cast<int64_t>(grow) * ep.ldr + gcol;
+    }
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(buf + swz(r, p))),
+                 "l"(src), "r"(bytes)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Adds the staged residual row of this lane to v (the copies are complete).
+__device__ __forceinline__ void add_residual_row(const uint8_t* buf, float* v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(buf + swz(lane, p));
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[p * 8 + e] += __bfloat162float(h[e]);
+  }
+  __syncwarp();
+}
+
+// ---- the kernel ------------------------------------------------------------------
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                const Epilogue ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* drained = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
+  float* bias_s = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);
+  uint8_t* epi_stage = smem + STAGES * STAGE_BYTES + 256 + BN * 4;  // 4 warps x 2 x 4 KB
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (ep.m + BM - 1) / BM;
+  const int tiles_n = (ep.n + BN - 1) / BN;
+  const int tiles = tiles_m * tiles_n;
+  const int k_tiles = (ep.k + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(drained, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_holder)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  bool failed = false;
+
+  if (warp == 0) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+        const int tm = t / tiles_n, tn = t - tm * tiles_n;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u)) {
+            failed = true;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          mbar_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(&map_a, &full[stage], sa, kt * BK, tm * BM);
+          tma_load_2d(&map_w, &full[stage], sa + A_BYTES, kt * BK, tn * BN);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // After a failure, wait (bounded) for copies still in flight.
+      if (failed) {
+        for (int s = 0; s < STAGES; ++s) mbar_wait(&full[s], 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int iter = 0;
+      for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++iter) {
+        const int buf = iter & 1;
+        const uint32_t use = static_cast<uint32_t>(iter >> 1);
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u)) {
+          failed = true;
+          break;
+        }
+        fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase)) {
+            failed = true;
+            break;
+          }
+          fence_after();
+          const uint32_t a_addr = smem_addr(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            mma_bf16(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
+                     (kt > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (failed) break;
+        mma_commit(&acc_full[buf]);
+      }
+      // All issued MMAs complete before the accumulators are released.
+      mma_commit(drained);
+      mbar_wait(drained, 0);
+    }
+  } else {
+    // ---- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4) ----
+    const int quad = warp & 3;
+    const int epi_tid = threadIdx.x - 64;  // 0..127
+    int iter = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
+      const int tm = t / tiles_n, tn = t - tm * tiles_n;
+      const int n0 = tn * BN;
+      const int buf = iter & 1;
+      const uint32_t use = static_cast<uint32_t>(iter >> 1);
+      // Stage this tile's bias (the previous tile's readers are past this barrier).
+      uint8_t* stage = epi_stage + quad * 8192;  // two 4 KB buffers
+      const int row0 = tm * BM + quad * 32;
+      // The first residual chunk streams in while the accumulator is computed.
+      if (ep.residual) prefetch_residual(stage, ep, row0, n0);
+      // Stage this tile's bias (the previous tile's readers are past this barrier).
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      for (int c = epi_tid; c < BN; c += 128) {
+        const int n = n0 + c;
+        bias_s[c] = (ep.bias && n < ep.n) ? __bfloat162float(ep.bias[n]) : 0.0f;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // The 128 epilogue threads agree on a timeout, so none is left on a barrier.
+      const uint32_t timed_out = mbar_wait(&acc_full[buf], use & 1u) ? 0u : 1u;
+      uint32_t any_timed_out;
+      asm volatile(
+          "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+          "bar.red.or.pred po, 1, 128, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+          : "=r"(any_timed_out)
+          : "r"(timed_out)
+          : "memory");
+      if (any_timed_out) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        failed = true;
+        break;
+      }
+      fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(buf * BN);
+      if (ep.out_fp32) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
+          tmem_wait_ld();
+          if (n0 + c0 >= ep.n) continue;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = activate(activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act), ep.act_after);
+          write_chunk<float>(stage + ((c0 >> 5) & 1) * 4096, v, ep, row0, n0 + c0);
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+          uint8_t* cur = stage + ((c0 >> 6) & 1) * 4096;
+          uint32_t r[64];
+          CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
+          CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0 + 32), (r + 32));
+          tmem_wait_ld();
+          if (ep.residual) {
+            // Next chunk's residual into the other buffer, then wait for this one.
+            if (c0 + 64 < BN) {
+              prefetch_residual(stage + (((c0 >> 6) + 1) & 1) * 4096, ep, row0, n0 + c0 + 64);
+              asm volatile("cp.async.wait_group 1;" ::: "memory");
+            } else {
+              asm volatile("cp.async.wait_group 0;" ::: "memory");
+            }
+            __syncwarp();
+          }
+          float v[64];
+#pragma unroll
+          for (int j = 0; j < 64; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
+          if (ep.residual) add_residual_row(cur, v);
+          if (ep.act_after != kActNone) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = activate(v[j], ep.act_after);
+          }
+          if (n0 + c0 < ep.n) write_chunk<__nv_bfloat16>(cur, v, ep, row0, n0 + c0);
+        }
+      }
+      fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  if (failed && ep.error) atomicExch(ep.error, 1);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// ---- host side -------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over [rows, cols] (row stride ld elements), box box_rows x 64.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+              uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
+                        const void* residual, int64_t ldr, void* out, int64_t ldo,
+                        int32_t out_fp32, int32_t act, int32_t act_after, int64_t m, int64_t n,
+                        int64_t k, int32_t* error, cudaStream_t stream) {
+  if (m < 0 || n <= 0 || k <= 0 || act < 0 || act > 2 || act_after < 0 || act_after > 2)
+    return CUGO_B200_ERR_ARG;
+  if (m == 0) return CUGO_B200_OK;
+  if (!a || !w || !out || lda < k || ldw < k || ldo < n || (residual && ldr < n))
+    return CUGO_B200_ERR_ARG;
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return CUGO_B200_ERR_ARG;
+  if (residual && out_fp32) return CUGO_B200_ERR_ARG;  // the residual stream is bf16
+  const auto al = [](const void* p, uintptr_t q) { return (reinterpret_cast<uintptr_t>(p) % q) == 0; };
+  if (!al(a, 16) || !al(w, 16) || (lda * 2) % 16 || (ldw * 2) % 16 || !al(out, 16) ||
+      (ldo * (out_fp32 ? 4 : 2)) % 16 || (residual && (!al(residual, 16) || (ldr * 2) % 16)))
+    return CUGO_B200_ERR_ALIGN;
+  CUtensorMap ma, mw;
+  if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BN)) return CUGO_B200_ERR_LAUNCH;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr_set[64] = {};
+  if (dev < 0 || dev >= 64) return CUGO_B200_ERR_LAUNCH;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+        cudaSuccess)
+      return CUGO_B200_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  Epilogue ep{static_cast<const __nv_bfloat16*>(bias), static_cast<const __nv_bfloat16*>(residual),
+              ldr, out, ldo, out_fp32, act, act_after, static_cast<int>(m), static_cast<int>(n),
+              static_cast<int>(k), error};
+  const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, ep);
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+}  // extern "C"

@@ -39,6 +39,9 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_branch_roots": [_I64, _I64, _VP, _VP],
     "cugo_b200_branch_actions": [_VP, _I64, _I64, _I64, _VP, _VP, _VP],
     "cugo_b200_sample_actions": [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _I32, _VP, _VP, _VP],
+    "cugo_b200_gemm_bf16": [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _VP, _I64, _I32, _I32, _I32,
+                            _I64, _I64, _I64, _VP, _VP],
+    "cugo_b200_observe_indexed_bf16": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
 }
 _CONSTANTS = {
     "FEATURE_COUNT": "cugo_b200_feature_count",
@@ -337,6 +340,42 @@ class CugoB200Extension:
                 self._stream(roots.device)), "branch_actions")
         return ids, actions
 
+
+    def observe_indexed_bf16(self, states, env_ids) -> list[torch.Tensor]:
+        """observe_indexed with bf16 features (the policy's input layer reads them)."""
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _same_device(states, env_ids, "states", "env_ids")
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            out = self._obs_outputs(m, states.device)
+            out[0] = torch.empty((m, self.FEATURE_COUNT), dtype=torch.bfloat16, device=states.device)
+            _check(self._lib.cugo_b200_observe_indexed_bf16(
+                _ptr(states), states.size(0), _ptr(env_ids), m, *map(_ptr, out),
+                self._stream(states.device)), "observe_indexed_bf16")
+        return out
+
+    # -- policy layers -------------------------------------------------------------
+    def linear(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+               residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+               act: int = 0, act_after: int = 0, out_dtype: torch.dtype = torch.bfloat16,
+               error: torch.Tensor | None = None) -> torch.Tensor:
+        """out = act_after(act(a @ w.T + bias) + residual) on tcgen05 tensor cores."""
+        m, k = a.shape
+        n = w.shape[0]
+        if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or w.shape[1] != k:
+            raise RuntimeError("linear expects bf16 a [m, k] and w [n, k]")
+        if a.stride(1) != 1 or w.stride(1) != 1:
+            raise RuntimeError("linear operands must be row-major")
+        if out is None:
+            out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+        with torch.cuda.device(a.device):
+            _check(self._lib.cugo_b200_gemm_bf16(
+                _ptr(a), a.stride(0), _ptr(w), w.stride(0), _ptr(bias), _ptr(residual),
+                residual.stride(0) if residual is not None else 0, _ptr(out), out.stride(0),
+                int(out.dtype == torch.float32), act, act_after, m, n, k, _ptr(error),
+                self._stream(a.device)), "gemm_bf16")
+        return out
 
     # -- policy sampling ---------------------------------------------------------
     def sample_actions(self, logits: torch.Tensor, legal: torch.Tensor, game: torch.Tensor,

@@ -1,0 +1,131 @@
+"""Single-kernel cases for timing and profiling (python -m cugo_b200.kernel_cases CASE ...).
+
+Each case builds its inputs on the GPU, runs `--warmup` untimed launches, then times
+`--iters` launches with CUDA events on the launching stream and prints one JSON line
+with the per-launch time and the achieved rate against the algorithmic bytes or
+FLOPs of one launch:
+
+  gemm      M N K      one tcgen05 layer, 2*M*N*K FLOP
+  mlp       M H B      the policy forward (B blocks of width H), flops_per_row * M
+  observe   ROWS       observe_indexed, 3,319 B per row
+  step      ROWS       step_indexed on live mid-game rows, 521 B per row
+  branch    ROOTS PER  branch_indexed, 274 B per branch
+  selfplay  SLOTS      the fused config-1 decision kernel, 4,027 B per decision
+  sample    ROWS       the Gumbel-max sampler, 180*4 + 179 + 16 B read, 12 B written per row
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import load_extension
+from .policy import ResidualMlpPolicy
+
+
+def _time(fn, warmup: int, iters: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters / 1e3
+
+
+def _mid_game(ext, rows: int, decisions: int = 6):
+    dev = torch.device("cuda")
+    idx = torch.arange(rows, device=dev, dtype=torch.int64)
+    states = ext.create(idx + 12345, idx & 1)
+    game, dec = idx.clone(), torch.zeros(rows, dtype=torch.int32, device=dev)
+    done, steps = torch.zeros_like(dec), torch.zeros(rows, dtype=torch.int64, device=dev)
+    feats = torch.empty((rows, 720), dtype=torch.float32, device=dev)
+    legal = torch.empty((rows, 179), dtype=torch.bool, device=dev)
+    for _ in range(decisions):
+        ext.selfplay_random_step(states, game, dec, done, steps, feats, legal)
+    return states, feats, legal
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("dims", nargs="*", type=int)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args()
+    ext = load_extension()
+    dev = torch.device("cuda")
+    d = args.dims
+    out: dict = {"case": args.case, "dims": d}
+    if args.case == "gemm":
+        m, n, k = d
+        a = torch.randn((m, k), device=dev).to(torch.bfloat16)
+        w = (torch.randn((n, k), device=dev) * (2.0 / k) ** 0.5).to(torch.bfloat16)
+        b = torch.zeros(n, device=dev, dtype=torch.bfloat16)
+        # bf16 rows must be a multiple of 16 bytes; other widths use fp32 rows.
+        o = torch.empty((m, n), device=dev, dtype=torch.bfloat16 if n % 8 == 0 else torch.float32)
+        sec = _time(lambda: ext.linear(a, w, b, out=o, act=1), args.warmup, args.iters)
+        out.update(seconds=sec, tflops=2 * m * n * k / sec / 1e12)
+    elif args.case == "mlp":
+        m, h, blocks = d
+        pol = ResidualMlpPolicy(h, blocks, "relu", device=dev)
+        x = torch.randn((m, 720), device=dev).to(torch.bfloat16)
+        sec = _time(lambda: pol(x), args.warmup, args.iters)
+        out.update(seconds=sec, tflops=pol.flops_per_row() * m / sec / 1e12)
+    elif args.case == "observe":
+        (rows,) = d
+        states, _, _ = _mid_game(ext, rows)
+        ids = torch.randperm(rows, device=dev)
+        sec = _time(lambda: ext.observe_indexed(states, ids), args.warmup, args.iters)
+        out.update(seconds=sec, gbs=rows * 3319 / sec / 1e9)
+    elif args.case == "step":
+        (rows,) = d
+        states, _, legal = _mid_game(ext, rows)
+        ids = torch.randperm(rows, device=dev)
+        acts = legal.to(torch.int64).argmax(1).index_select(0, ids)
+        snapshot = states.clone()
+
+        def run():
+            states.copy_(snapshot)
+            ext.step_indexed(states, ids, acts)
+
+        sec_copy = _time(lambda: states.copy_(snapshot), args.warmup, args.iters)
+        sec = _time(run, args.warmup, args.iters) - sec_copy
+        out.update(seconds=sec, gbs=rows * 521 / sec / 1e9)
+    elif args.case == "branch":
+        roots_n, per = d
+        roots = ext.branch_roots(roots_n)
+        ids, acts = ext.branch_actions(roots, per)
+        sec = _time(lambda: ext.branch_indexed(roots, ids, acts), args.warmup, args.iters)
+        out.update(seconds=sec, branches_per_s=roots_n * per / sec,
+                   gbs=roots_n * per * 274 / sec / 1e9)
+    elif args.case == "selfplay":
+        (slots,) = d
+        idx = torch.arange(slots, device=dev, dtype=torch.int64)
+        states = ext.create(idx + 12345, idx & 1)
+        game, dec = idx.clone(), torch.zeros(slots, dtype=torch.int32, device=dev)
+        done, steps = torch.zeros_like(dec), torch.zeros(slots, dtype=torch.int64, device=dev)
+        feats = torch.empty((slots, 720), dtype=torch.float32, device=dev)
+        legal = torch.empty((slots, 179), dtype=torch.bool, device=dev)
+        sec = _time(lambda: ext.selfplay_random_step(states, game, dec, done, steps, feats, legal),
+                    args.warmup, args.iters)
+        out.update(seconds=sec, decisions_per_s=slots / sec, gbs=slots * 4027 / sec / 1e9)
+    elif args.case == "sample":
+        (rows,) = d
+        logits = torch.randn((rows, 180), device=dev)
+        legal = torch.rand((rows, 179), device=dev) < 0.1
+        game = torch.arange(rows, device=dev, dtype=torch.int64)
+        dec = torch.zeros(rows, dtype=torch.int32, device=dev)
+        sec = _time(lambda: ext.sample_actions(logits, legal, game, dec), args.warmup, args.iters)
+        out.update(seconds=sec, gbs=rows * (720 + 179 + 16 + 12) / sec / 1e9)
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

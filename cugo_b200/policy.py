@@ -1,48 +1,54 @@
-"""Residual-MLP policy/value network of the self-play path.
+"""Residual-MLP policy/value network of the self-play path, on tcgen05 tensor cores.
 
 Architecture (reference python/cugo_ppo_nets50.py:26-64, ResidualMlp/PpoActor with
 norm="none"):  h = W_in x + b;  h = h + W2 act(W1 h + b1) + b2  (per block);
 out = W_out act(h) + b_out.  The reference uses SiLU; the benchmark configuration
 (config 3) uses ReLU and appends a scalar value output to the 179 policy logits.
 Weights are bf16 with fp32 accumulation, as under the reference's bf16 autocast
-(python/cugo_ppo50.py:366).
+(python/cugo_ppo50.py:366).  Every layer is one launch of the fused tcgen05 GEMM
+(libcugo_b200.so, cugo_b200_gemm_bf16): bias, activation and the residual add run
+in its epilogue, and the last block writes act(h) so the head reads it directly.
 """
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 FEATURES = 720
 ACTIONS = 179
+_ACT = {"none": 0, "relu": 1, "silu": 2}
 
 
 class ResidualMlpPolicy:
     def __init__(self, hidden: int = 512, blocks: int = 3, activation: str = "relu",
                  outputs: int = ACTIONS + 1, device: torch.device | str = "cuda",
-                 seed: int | None = 0) -> None:
+                 seed: int | None = 0, inputs: int = FEATURES) -> None:
         if activation not in ("relu", "silu"):
             raise ValueError("activation must be relu or silu")
         self.hidden, self.blocks, self.activation, self.outputs = hidden, blocks, activation, outputs
+        self.inputs = inputs
         self.device = torch.device(device)
-        shapes = [(hidden, FEATURES)] + [(hidden, hidden)] * (2 * blocks) + [(outputs, hidden)]
+        shapes = [(hidden, inputs)] + [(hidden, hidden)] * (2 * blocks) + [(outputs, hidden)]
         gen = torch.Generator().manual_seed(seed if seed is not None else 0)
         self.weights: list[torch.Tensor] = []
         self.biases: list[torch.Tensor] = []
         for shape in shapes:
             w = torch.empty(shape, dtype=torch.float32)
             # Kaiming-normal (fan_in, gain sqrt(2)), drawn on the CPU generator.
-            std = (2.0 / shape[1]) ** 0.5
-            w.normal_(0.0, std, generator=gen)
+            w.normal_(0.0, (2.0 / shape[1]) ** 0.5, generator=gen)
             self.weights.append(w.to(self.device, torch.bfloat16).contiguous())
             self.biases.append(torch.zeros(shape[0], dtype=torch.bfloat16, device=self.device))
+        self._ext = None
+        self.error = (torch.zeros(1, dtype=torch.int32, device=self.device)
+                      if self.device.type == "cuda" else None)
 
     @classmethod
     def from_state_dict(cls, state: dict[str, torch.Tensor], blocks: int, activation: str = "silu",
                         device: torch.device | str = "cuda") -> "ResidualMlpPolicy":
-        """Loads a reference ResidualMlp/PpoActor state dict (inp, blocks.i.fc1/fc2, out)."""
-        hidden = state["inp.weight"].shape[0]
+        """Loads a reference ResidualMlp/PpoActor/OracleCritic state dict
+        (inp, blocks.i.fc1/fc2, out), e.g. from a train_ppo50.py checkpoint."""
+        hidden, inputs = state["inp.weight"].shape
         outputs = state["out.weight"].shape[0]
-        self = cls(hidden, blocks, activation, outputs, device, seed=None)
+        self = cls(hidden, blocks, activation, outputs, device, seed=None, inputs=inputs)
         names = ["inp"] + [f"blocks.{i}.fc{j}" for i in range(blocks) for j in (1, 2)] + ["out"]
         for k, name in enumerate(names):
             self.weights[k] = state[f"{name}.weight"].to(self.device, torch.bfloat16).contiguous()
@@ -52,18 +58,37 @@ class ResidualMlpPolicy:
     def flops_per_row(self) -> int:
         return 2 * sum(w.shape[0] * w.shape[1] for w in self.weights)
 
-    def _act(self, x: torch.Tensor) -> torch.Tensor:
-        return F.relu(x) if self.activation == "relu" else F.silu(x)
+    def launches_per_forward(self) -> int:
+        return 2 + 2 * self.blocks
+
+    def _extension(self):
+        if self._ext is None:
+            from .ext import load_extension
+            self._ext = load_extension()
+        return self._ext
 
     @torch.no_grad()
     def forward(self, features: torch.Tensor) -> torch.Tensor:
-        """fp32 [M, 720] features -> fp32 [M, outputs] logits (and value)."""
-        x = features.to(torch.bfloat16)
+        """[M, inputs] features (bf16, or fp32 cast to bf16 as autocast does) ->
+        fp32 [M, outputs] logits (and value)."""
+        ext = self._extension()
+        x = features if features.dtype == torch.bfloat16 else features.to(torch.bfloat16)
+        x = x.contiguous()
+        m = x.size(0)
+        act = _ACT[self.activation]
         w, b = self.weights, self.biases
-        h = F.linear(x, w[0], b[0])
-        for i in range(self.blocks):
-            h = h + F.linear(self._act(F.linear(h, w[1 + 2 * i], b[1 + 2 * i])), w[2 + 2 * i],
-                             b[2 + 2 * i])
-        return F.linear(self._act(h), w[-1], b[-1]).float()
+        h = torch.empty((m, self.hidden), dtype=torch.bfloat16, device=x.device)
+        ext.linear(x, w[0], b[0], out=h, act_after=act if self.blocks == 0 else 0, error=self.error)
+        if self.blocks:
+            u = torch.empty_like(h)
+            for i in range(self.blocks):
+                ext.linear(h, w[1 + 2 * i], b[1 + 2 * i], out=u, act=act, error=self.error)
+                ext.linear(u, w[2 + 2 * i], b[2 + 2 * i], residual=h, out=h,
+                           act_after=act if i == self.blocks - 1 else 0, error=self.error)
+        # fp32 rows padded to a multiple of 16 bytes for the vector stores.
+        padded = (self.outputs + 3) // 4 * 4
+        out = torch.empty((m, padded), dtype=torch.float32, device=x.device)[:, :self.outputs]
+        ext.linear(h, w[-1], b[-1], out=out, error=self.error)
+        return out
 
     __call__ = forward

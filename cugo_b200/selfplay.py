@@ -67,7 +67,7 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     rounds = 0
     n_launch = 1
     for rounds in range(1, max_rounds + 1):
-        features, legal, _players, _done, status = ext.observe_indexed(states, active)
+        features, legal, _players, _done, status = ext.observe_indexed_bf16(states, active)
         t0 = timer.start() if timer else None
         logits = policy(features)
         if timer:
@@ -75,7 +75,7 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
         actions, _logp = ext.sample_actions(logits, legal, game_index.index_select(0, active),
                                             decision.index_select(0, active), seed_base)
         reward, new_done, new_nagari, step_status, _ = ext.step_indexed(states, active, actions)
-        n_launch += 3
+        n_launch += 3 + getattr(policy, "launches_per_forward", lambda: 0)()
         bad += ((step_status != 0) & (step_status != 9)).sum()
         decisions += active.numel()
         decision.index_add_(0, active, torch.ones_like(active, dtype=torch.int32))

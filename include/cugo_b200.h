@@ -174,6 +174,31 @@ CUGO_B200_API int cugo_b200_sample_actions(const float* logits, int64_t ld, cons
                                            int32_t greedy, int64_t* actions, float* logp,
                                            cudaStream_t stream);
 
+/* ---- Policy network layers -------------------------------------------------------
+ * One nn.Linear layer of the residual-MLP policy/value networks
+ * (python/cugo_ppo_nets50.py:26-87; run under bf16 autocast, cugo_ppo50.py:366)
+ * with its bias, activation and residual add fused, on tcgen05 tensor cores:
+ *   out = act_after(act(A . W^T + bias) + residual)
+ * A bf16 [m, k] (row stride lda), W bf16 [n, k] (ldw), bias bf16 [n] or NULL,
+ * residual bf16 [m, n] (ldr) or NULL (may alias out; bf16 out only), out bf16
+ * or fp32 [m, n] (ldo).  act/act_after: 0 none, 1 ReLU, 2 SiLU.  Pointers
+ * 16-byte aligned, row strides multiples of 16 bytes.  `error` (device int, may
+ * be NULL) is set to 1 if a pipeline wait timed out. */
+CUGO_B200_API int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw,
+                                      const void* bias, const void* residual, int64_t ldr,
+                                      void* out, int64_t ldo, int32_t out_fp32, int32_t act,
+                                      int32_t act_after, int64_t m, int64_t n, int64_t k,
+                                      int32_t* error, cudaStream_t stream);
+
+/* observe_indexed with the features written as bf16 [m, 720] (16-byte aligned):
+ * the policy's input layer reads them directly.  Same values as observe_indexed
+ * rounded to bf16 (the reference casts features to bf16 under autocast). */
+CUGO_B200_API int cugo_b200_observe_indexed_bf16(const uint8_t* states, int64_t n_states,
+                                                 const int64_t* env_ids, int64_t m,
+                                                 void* features_bf16, bool* legal,
+                                                 uint8_t* players, bool* done, int16_t* status,
+                                                 cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
