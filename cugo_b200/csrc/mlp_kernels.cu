@@ -546,3 +546,84 @@ int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, 
 }
 
 }  // extern "C"
+
+// ---- policy forward without allocation --------------------------------------------
+//
+// For callers that may not allocate device memory: an FFI host (a Go, Java or Rust
+// serving process) that hands this library only its own fixed input and output
+// buffers and keeps cudaMalloc off its request path because it synchronises the
+// device, or a runtime that has reserved all device memory up front.  The two bf16
+// activation buffers the layer chain needs live in this file-scope array instead
+// of being allocated per call; every GPU that loads the library holds it (16 MiB)
+// until the process exits.
+
+namespace {
+
+// Per buffer: rows x hidden <= kNoAllocRowsTimesHidden bf16 elements.
+constexpr int64_t kNoAllocRowsTimesHidden = int64_t{4} << 20;
+static __device__ __align__(256) __nv_bfloat16 g_noalloc_activations[2 * kNoAllocRowsTimesHidden];
+
+// Device address of g_noalloc_activations, looked up once per device (the name
+// is only a host-side stand-in in host code).
+void* noalloc_scratch(int* rc) {
+  static void* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *rc = CUGO_B200_ERR_LAUNCH;
+    return nullptr;
+  }
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_activations) != cudaSuccess || !p) {
+      *rc = CUGO_B200_ERR_LAUNCH;
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *rc = CUGO_B200_OK;
+  return addr[dev];
+}
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_policy_forward_noalloc(const void* x, int64_t ldx, int64_t m, int64_t inputs,
+                                     int64_t hidden, int32_t blocks, int64_t outputs,
+                                     const void* const* weights, const void* const* biases,
+                                     int32_t act, float* out, int64_t ldo, int32_t* error,
+                                     cudaStream_t stream) {
+  if (m < 0 || inputs <= 0 || hidden <= 0 || blocks < 0 || outputs <= 0 || !weights ||
+      (act != kActRelu && act != kActSilu))
+    return CUGO_B200_ERR_ARG;
+  if (m * hidden > kNoAllocRowsTimesHidden) return CUGO_B200_ERR_CAPACITY;
+  if (m == 0) return CUGO_B200_OK;
+  const int layers = 2 + 2 * blocks;
+  for (int l = 0; l < layers; ++l)
+    if (!weights[l]) return CUGO_B200_ERR_ARG;
+  int rc = CUGO_B200_OK;
+  void* scratch = noalloc_scratch(&rc);
+  if (rc != CUGO_B200_OK) return rc;
+  // h and u: each call writes every element it later reads (rows past m are
+  // outside the tensor maps and read as zero), so no state carries over between
+  // calls and nothing needs clearing.
+  auto* h = static_cast<__nv_bfloat16*>(scratch);
+  __nv_bfloat16* u = h + kNoAllocRowsTimesHidden;
+  const auto bias = [&](int l) { return biases ? biases[l] : nullptr; };
+  rc = cugo_b200_gemm_bf16(x, ldx, weights[0], inputs, bias(0), nullptr, 0, h, hidden, 0, 0,
+                           blocks == 0 ? act : 0, m, hidden, inputs, error, stream);
+  for (int i = 0; i < blocks && rc == CUGO_B200_OK; ++i) {
+    rc = cugo_b200_gemm_bf16(h, hidden, weights[1 + 2 * i], hidden, bias(1 + 2 * i), nullptr, 0, u,
+                             hidden, 0, act, 0, m, hidden, hidden, error, stream);
+    if (rc == CUGO_B200_OK)
+      rc = cugo_b200_gemm_bf16(u, hidden, weights[2 + 2 * i], hidden, bias(2 + 2 * i), h, hidden, h,
+                               hidden, 0, 0, i == blocks - 1 ? act : 0, m, hidden, hidden, error,
+                               stream);
+  }
+  if (rc == CUGO_B200_OK)
+    rc = cugo_b200_gemm_bf16(h, hidden, weights[layers - 1], hidden, bias(layers - 1), nullptr, 0,
+                             out, ldo, 1, 0, 0, m, outputs, hidden, error, stream);
+  return rc;
+}
+
+}  // extern "C"

@@ -45,6 +45,7 @@ typedef struct CUstream_st* cudaStream_t;
 #define CUGO_B200_ERR_ARG (-1)
 #define CUGO_B200_ERR_ALIGN (-2)
 #define CUGO_B200_ERR_LAUNCH (-3)
+#define CUGO_B200_ERR_CAPACITY (-4) /* larger than a fixed internal buffer allows */
 
 CUGO_B200_API int cugo_b200_abi_version(void);
 
@@ -189,6 +190,32 @@ CUGO_B200_API int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w,
                                       void* out, int64_t ldo, int32_t out_fp32, int32_t act,
                                       int32_t act_after, int64_t m, int64_t n, int64_t k,
                                       int32_t* error, cudaStream_t stream);
+
+/* Policy forward that allocates nothing (no counterpart in the reference).
+ * For callers that cannot allocate device memory — for example a Go/Java/Rust
+ * serving process that passes only its own fixed input and output buffers and keeps
+ * cudaMalloc (which synchronises the device) off its request path, or a runtime
+ * that reserved all device memory at start-up.  Runs the same layer chain as the
+ * Python policy (ResidualMlpPolicy.forward) through cugo_b200_gemm_bf16:
+ *   h = W[0] x + b[0]; per block h = h + W[2i+2] act(W[2i+1] h + b[2i+1]) + b[2i+2];
+ *   out = W[last] act(h) + b[last]
+ * x bf16 [m, inputs] (ldx); weights/biases: HOST arrays of 2 + 2*blocks DEVICE
+ * pointers (bf16 [out, in] weights; biases may be NULL or hold NULL entries);
+ * act 1 ReLU, 2 SiLU; out fp32 [m, outputs] (ldo, rows a multiple of 16 bytes);
+ * error as for cugo_b200_gemm_bf16.  The hidden activations live in a buffer
+ * compiled into the library (16 MiB held on every GPU that loads it until the
+ * process exits): m * hidden must not exceed 4,194,304 (e.g. 8,192 rows at hidden
+ * 512), larger calls return CUGO_B200_ERR_CAPACITY.  The first call on a device
+ * looks up that buffer's device address, so make it before any stream capture.
+ * All calls share the buffer: calls that overlap on the GPU (other streams or
+ * threads) race and must be serialised by the caller. */
+CUGO_B200_API int cugo_b200_policy_forward_noalloc(const void* x, int64_t ldx, int64_t m,
+                                                   int64_t inputs, int64_t hidden,
+                                                   int32_t blocks, int64_t outputs,
+                                                   const void* const* weights,
+                                                   const void* const* biases, int32_t act,
+                                                   float* out, int64_t ldo, int32_t* error,
+                                                   cudaStream_t stream);
 
 /* observe_indexed with the features written as bf16 [m, 720] (16-byte aligned):
  * the policy's input layer reads them directly.  Same values as observe_indexed
