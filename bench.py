@@ -293,7 +293,7 @@ def reference_arm(args, world, rank):
     if rank != 0:
         return
     threads = host_threads()
-    sample = 2048
+    sample = 16384  # about 3 s of host work per step
     for _ in range(args.warmup):
         cpu_selfplay(256, args.arch, threads)
     runs = [cpu_selfplay(sample, args.arch, threads) for _ in range(args.steps)]
@@ -376,12 +376,13 @@ def main():
         "extras": extras,
     }
     if rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_selfplay(2048, args.arch, host_threads())
+        cpu_games = 65536  # 10-20 s of host work
+        cpu = cpu_selfplay(cpu_games, args.arch, host_threads())
         out["cpu_baseline"] = {
             "value": cpu["games_per_s"], "unit": "games/s", "cores": host_threads(),
-            "kind": "reference",
-            "sample": "2048 seeded games to settlement: reference engine (oracle/_ref) + "
-                      f"{args.arch} MLP on PyTorch-CPU fp32"}
+            "kind": "reference", "seconds": cpu["seconds"],
+            "sample": f"{cpu_games} seeded games (12345 + i) to settlement: reference engine "
+                      f"(oracle/_ref) + {args.arch} MLP on PyTorch-CPU fp32"}
     if rank == 0:
         print(json.dumps(out))
     if world > 1:

@@ -116,8 +116,8 @@ __device__ __forceinline__ void store4(__nv_bfloat16* row, int q, const float* v
 // Cooperative write of the tile's feature rows: row `base + r` for r < rows.
 // Lane l owns 4-column groups l, l+32, ... of every row (fp32 or bf16 rows).
 template <typename F>
-__device__ __forceinline__ void emit_features(const WarpTile& t, F* __restrict__ out, i64 base,
-                                              int rows) {
+__device__ __forceinline__ void emit_features(const WarpTile& t, F* __restrict__ out, i64 ld,
+                                              i64 base, int rows) {
   __syncwarp();
   const int lane = threadIdx.x & 31;
   // Per lane: for each of its 24 columns, the scalar slot or (word, bit).
@@ -133,7 +133,7 @@ __device__ __forceinline__ void emit_features(const WarpTile& t, F* __restrict__
       bitpos[k][j] = c & 31u;
     }
   for (int r = 0; r < rows; ++r) {
-    F* row = out + (base + r) * (i64)kFeatures;
+    F* row = out + (base + r) * ld;
 #pragma unroll
     for (int k = 0; k < 6; ++k) {
       const int q = lane + 32 * k;
@@ -146,6 +146,28 @@ __device__ __forceinline__ void emit_features(const WarpTile& t, F* __restrict__
         store4(row, q, v);
       }
     }
+  }
+}
+
+// Cooperative write of the tile's legal masks as bf16 0/1 into columns
+// 720 .. 720 + cols - 1 of each feature row (actions >= 179 read 0): the
+// sequence policy's query input is [features, legal] (python/cugo_seq50.py:196-208).
+__device__ __forceinline__ void emit_legal_columns(const WarpTile& t, __nv_bfloat16* __restrict__ out,
+                                                   i64 ld, i64 base, int rows, int cols) {
+  const int lane = threadIdx.x & 31;
+  const int groups = cols >> 3;
+  for (int k = lane; k < rows * groups; k += 32) {
+    const int r = k / groups, g = k - r * groups;
+    u32 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const u32 a0 = 8u * g + 2u * e, a1 = a0 + 1u;
+      const u32 b0 = a0 < kActions ? static_cast<u32>((t.legal[r][a0 >> 6] >> (a0 & 63)) & 1ull) : 0u;
+      const u32 b1 = a1 < kActions ? static_cast<u32>((t.legal[r][a1 >> 6] >> (a1 & 63)) & 1ull) : 0u;
+      h[e] = (b0 ? 0x3F80u : 0u) | ((b1 ? 0x3F80u : 0u) << 16);  // bf16 1.0 = 0x3F80
+    }
+    __stcs(reinterpret_cast<uint4*>(out + (base + r) * ld + kFeatures) + g,
+           make_uint4(h[0], h[1], h[2], h[3]));
   }
 }
 
@@ -196,8 +218,8 @@ __global__ void __launch_bounds__(kBlock) create_kernel(const i64* __restrict__ 
 template <typename F>
 __global__ void __launch_bounds__(kBlock) observe_kernel(
     const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids, i64 m,
-    F* __restrict__ features, bool* __restrict__ legal, uint8_t* __restrict__ players,
-    bool* __restrict__ done, int16_t* __restrict__ status) {
+    F* __restrict__ features, i64 ld, int legal_cols, bool* __restrict__ legal,
+    uint8_t* __restrict__ players, bool* __restrict__ done, int16_t* __restrict__ status) {
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
@@ -221,7 +243,10 @@ __global__ void __launch_bounds__(kBlock) observe_kernel(
   const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
   const i64 left = m - tile_base;
   const int rows_here = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
-  emit_features(t, features, tile_base, rows_here);
+  emit_features(t, features, ld, tile_base, rows_here);
+  if constexpr (sizeof(F) == 2) {
+    if (legal_cols > 0) emit_legal_columns(t, features, ld, tile_base, rows_here, legal_cols);
+  }
   emit_legal(t, legal, tile_base, rows_here);
   if (row < m) {
     players[row] = static_cast<uint8_t>(meta.player);
@@ -368,8 +393,8 @@ static int observe_common(const uint8_t* states, int64_t n_states, const int64_t
   if (!aligned(states, 8) || !aligned(features, 16) || !aligned(legal, 4)) return CUGO_B200_ERR_ALIGN;
   if (m == 0) return CUGO_B200_OK;
   observe_kernel<float><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
-      reinterpret_cast<const u64*>(states), n_states, env_ids, m, features, legal, players, done,
-      status);
+      reinterpret_cast<const u64*>(states), n_states, env_ids, m, features, (i64)kFeatures, 0, legal,
+      players, done, status);
   return launch_status();
 }
 
@@ -383,7 +408,26 @@ int cugo_b200_observe_indexed_bf16(const uint8_t* states, int64_t n_states, cons
   if (m == 0) return CUGO_B200_OK;
   observe_kernel<__nv_bfloat16><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<const u64*>(states), n_states, env_ids, m,
-      static_cast<__nv_bfloat16*>(features), legal, players, done, status);
+      static_cast<__nv_bfloat16*>(features), (i64)kFeatures, 0, legal, players, done, status);
+  return launch_status();
+}
+
+int cugo_b200_observe_query_bf16(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                                 int64_t m, void* query, int64_t ldq, bool* legal,
+                                 uint8_t* players, bool* done, int16_t* status,
+                                 cudaStream_t stream) {
+  if (n_states < 0 || m < 0 || (m > 0 && !env_ids)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (!query || !legal || !players || !done || !status)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (ldq < (int64_t)(kFeatures + kActions)) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(query, 16) || ldq % 8 || !aligned(legal, 4))
+    return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  // Legal columns fill the row up to ldq (zeros past action 178), in groups of 8.
+  observe_kernel<__nv_bfloat16><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<const u64*>(states), n_states, env_ids, m,
+      static_cast<__nv_bfloat16*>(query), ldq, static_cast<int>(ldq - kFeatures), legal, players,
+      done, status);
   return launch_status();
 }
 

@@ -3,9 +3,12 @@
 //   out[M, N] = act_after(act(A[M, K] . W[N, K]^T + bias[N]) + residual[M, N])
 //
 // A and W are bf16, K-major (row-major A, nn.Linear weight layout); the product
-// accumulates in fp32 in tensor memory; out is bf16 or fp32.  This is one layer
-// of the policy/value MLP (python/cugo_ppo_nets50.py:26-64 run under bf16
-// autocast): nn.Linear + bias, then ReLU/SiLU and the residual add, fused.
+// accumulates in fp32 in tensor memory; out is bf16 or fp32 and the residual has
+// the output's type (an fp32 residual stream is updated in place); the bias is
+// bf16 or fp32.  This is one layer of the policy/value MLP
+// (python/cugo_ppo_nets50.py:26-64 run under bf16 autocast) or of the sequence
+// transformer (python/cugo_seq50.py:318-321): nn.Linear + bias, then
+// ReLU/SiLU/GELU and the residual add, fused.
 //
 // Kernel (one CTA per SM, persistent over 128 x 256 output tiles):
 //   warp 0     : TMA producer — one elected thread streams 128x64 A and 256x64 W
@@ -41,15 +44,16 @@ constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barrier
                            BN * 4 /*bias*/ + 4 * 2 * 4096 /*epilogue staging, 2 per warp*/;
 constexpr uint64_t kWaitNs = 2'000'000'000ull;
 
-enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2 };
+enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActGelu = 3 };
 
 struct Epilogue {
-  const __nv_bfloat16* bias;      // [N] or null
-  const __nv_bfloat16* residual;  // [M, ldr] or null
+  const void* bias;      // [N] bf16 (fp32 when bias_fp32) or null
+  const void* residual;  // [M, ldr] of the output's type, or null
   int64_t ldr;
   void* out;
   int64_t ldo;
   int out_fp32;
+  int bias_fp32;
   int act;        // applied to acc + bias, before the residual add
   int act_after;  // applied after the residual add
   int m, n, k;
@@ -172,6 +176,7 @@ __device__ __forceinline__ void tmem_wait_ld() {
 __device__ __forceinline__ float activate(float v, int act) {
   if (act == kActRelu) return fmaxf(v, 0.0f);
   if (act == kActSilu) return v / (1.0f + __expf(-v));
+  if (act == kActGelu) return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));  // exact (erf) GELU
   return v;
 }
 
@@ -222,20 +227,22 @@ __device__ __forceinline__ void write_chunk(uint8_t* stage, const float* v, cons
   __syncwarp();
 }
 
-// Starts copying the residual of a 32-row x 64-column chunk into a staging
-// buffer (cp.async, zero-filled outside the matrix); one commit group per chunk.
+// Starts copying the residual of a 32-row x 128-byte chunk (64 bf16 or 32 fp32
+// columns) into a staging buffer (cp.async, zero-filled outside the matrix); one
+// commit group per chunk.
 __device__ __forceinline__ void prefetch_residual(uint8_t* buf, const Epilogue& ep, int row0,
                                                   int col0) {
   const int lane = threadIdx.x & 31;
+  const int esz = ep.out_fp32 ? 4 : 2, per = 16 / esz;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int r = 4 * i + (lane >> 3), p = lane & 7;
-    const int grow = row0 + r, gcol = col0 + p * 8;
+    const int grow = row0 + r, gcol = col0 + p * per;
     int bytes = 0;
-    const __nv_bfloat16* src = ep.residual;
+    const uint8_t* src = static_cast<const uint8_t*>(ep.residual);
     if (ep.residual && grow < ep.m && gcol < ep.n) {
-      bytes = 2 * (ep.n - gcol < 8 ? ep.n - gcol : 8);
-      src = ep.residual + static_cast<int64_t>(grow) * ep.ldr + gcol;
+      bytes = esz * (ep.n - gcol < per ? ep.n - gcol : per);
+      src += (static_cast<int64_t>(grow) * ep.ldr + gcol) * esz;
     }
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(buf + swz(r, p))),
                  "l"(src), "r"(bytes)
@@ -245,14 +252,19 @@ __device__ __forceinline__ void prefetch_residual(uint8_t* buf, const Epilogue& 
 }
 
 // Adds the staged residual row of this lane to v (the copies are complete).
+template <typename T>
 __device__ __forceinline__ void add_residual_row(const uint8_t* buf, float* v) {
+  constexpr int E = 16 / static_cast<int>(sizeof(T));
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int p = 0; p < 8; ++p) {
     const uint4 raw = *reinterpret_cast<const uint4*>(buf + swz(lane, p));
-    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    const T* h = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[p * 8 + e] += __bfloat162float(h[e]);
+    for (int e = 0; e < E; ++e) {
+      if constexpr (sizeof(T) == 2) v[p * E + e] += __bfloat162float(h[e]);
+      else v[p * E + e] += h[e];
+    }
   }
   __syncwarp();
 }
@@ -393,7 +405,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       asm volatile("bar.sync 1, 128;" ::: "memory");
       for (int c = epi_tid; c < BN; c += 128) {
         const int n = n0 + c;
-        bias_s[c] = (ep.bias && n < ep.n) ? __bfloat162float(ep.bias[n]) : 0.0f;
+        float b = 0.0f;
+        if (ep.bias && n < ep.n)
+          b = ep.bias_fp32 ? static_cast<const float*>(ep.bias)[n]
+                           : __bfloat162float(static_cast<const __nv_bfloat16*>(ep.bias)[n]);
+        bias_s[c] = b;
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
       // The 128 epilogue threads agree on a timeout, so none is left on a barrier.
@@ -416,15 +432,30 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ep.out_fp32) {
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint8_t* cur = stage + ((c0 >> 5) & 1) * 4096;
           uint32_t r[32];
           CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
           tmem_wait_ld();
+          if (ep.residual) {
+            // Next chunk's residual into the other buffer, then wait for this one.
+            if (c0 + 32 < BN) {
+              prefetch_residual(stage + (((c0 >> 5) + 1) & 1) * 4096, ep, row0, n0 + c0 + 32);
+              asm volatile("cp.async.wait_group 1;" ::: "memory");
+            } else {
+              asm volatile("cp.async.wait_group 0;" ::: "memory");
+            }
+            __syncwarp();
+          }
           if (n0 + c0 >= ep.n) continue;
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = activate(activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act), ep.act_after);
-          write_chunk<float>(stage + ((c0 >> 5) & 1) * 4096, v, ep, row0, n0 + c0);
+          for (int j = 0; j < 32; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
+          if (ep.residual) add_residual_row<float>(cur, v);
+          if (ep.act_after != kActNone) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = activate(v[j], ep.act_after);
+          }
+          write_chunk<float>(cur, v, ep, row0, n0 + c0);
         }
       } else {
 #pragma unroll 1
@@ -447,7 +478,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[64];
 #pragma unroll
           for (int j = 0; j < 64; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
-          if (ep.residual) add_residual_row(cur, v);
+          if (ep.residual) add_residual_row<__nv_bfloat16>(cur, v);
           if (ep.act_after != kActNone) {
 #pragma unroll
             for (int j = 0; j < 64; ++j) v[j] = activate(v[j], ep.act_after);
@@ -509,20 +540,22 @@ int sm_count() {
 
 extern "C" {
 
-int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
-                        const void* residual, int64_t ldr, void* out, int64_t ldo,
-                        int32_t out_fp32, int32_t act, int32_t act_after, int64_t m, int64_t n,
-                        int64_t k, int32_t* error, cudaStream_t stream) {
-  if (m < 0 || n <= 0 || k <= 0 || act < 0 || act > 2 || act_after < 0 || act_after > 2)
+int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ldw,
+                           const void* bias, int32_t bias_fp32, const void* residual,
+                           int64_t ldr, void* out, int64_t ldo, int32_t out_fp32, int32_t act,
+                           int32_t act_after, int64_t m, int64_t n, int64_t k, int32_t* error,
+                           cudaStream_t stream) {
+  if (m < 0 || n <= 0 || k <= 0 || act < 0 || act > 3 || act_after < 0 || act_after > 3)
     return CUGO_B200_ERR_ARG;
   if (m == 0) return CUGO_B200_OK;
   if (!a || !w || !out || lda < k || ldw < k || ldo < n || (residual && ldr < n))
     return CUGO_B200_ERR_ARG;
   if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return CUGO_B200_ERR_ARG;
-  if (residual && out_fp32) return CUGO_B200_ERR_ARG;  // the residual stream is bf16
+  const int esz = out_fp32 ? 4 : 2;
   const auto al = [](const void* p, uintptr_t q) { return (reinterpret_cast<uintptr_t>(p) % q) == 0; };
   if (!al(a, 16) || !al(w, 16) || (lda * 2) % 16 || (ldw * 2) % 16 || !al(out, 16) ||
-      (ldo * (out_fp32 ? 4 : 2)) % 16 || (residual && (!al(residual, 16) || (ldr * 2) % 16)))
+      (ldo * esz) % 16 || (residual && (!al(residual, 16) || (ldr * esz) % 16)) ||
+      (bias && !al(bias, bias_fp32 ? 4 : 2)))
     return CUGO_B200_ERR_ALIGN;
   CUtensorMap ma, mw;
   if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BN)) return CUGO_B200_ERR_LAUNCH;
@@ -536,13 +569,22 @@ int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, 
       return CUGO_B200_ERR_LAUNCH;
     attr_set[dev] = true;
   }
-  Epilogue ep{static_cast<const __nv_bfloat16*>(bias), static_cast<const __nv_bfloat16*>(residual),
-              ldr, out, ldo, out_fp32, act, act_after, static_cast<int>(m), static_cast<int>(n),
-              static_cast<int>(k), error};
+  Epilogue ep{bias, residual, ldr, out, ldo, out_fp32 ? 1 : 0, bias_fp32 ? 1 : 0, act, act_after,
+              static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), error};
   const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
   gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, ep);
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
+                        const void* residual, int64_t ldr, void* out, int64_t ldo,
+                        int32_t out_fp32, int32_t act, int32_t act_after, int64_t m, int64_t n,
+                        int64_t k, int32_t* error, cudaStream_t stream) {
+  if (act > 2 || act_after > 2) return CUGO_B200_ERR_ARG;
+  if (residual && out_fp32) return CUGO_B200_ERR_ARG;  // this entry's residual stream is bf16
+  return cugo_b200_gemm_bf16_ex(a, lda, w, ldw, bias, 0, residual, ldr, out, ldo, out_fp32, act,
+                                act_after, m, n, k, error, stream);
 }
 
 }  // extern "C"

@@ -22,14 +22,18 @@ using namespace cb;
 
 namespace {
 
-constexpr int kActionsPadded = 180;  // 45 blocks of 4 actions
-
 __device__ __forceinline__ float gumbel_of(u32 word) {
   const float u = (static_cast<float>(word >> 8) + 0.5f) * (1.0f / 16777216.0f);
   return -logf(-logf(u));
 }
 
 // logits: [m, ld] fp32 (columns 0..178 are the policy logits); legal: [m, 179].
+//
+// The warp first compacts the row's legal actions (six ballots over the 179 mask
+// bytes); lane j then takes the j-th legal action (j, j + 32, ... when a row has
+// more than 32), so Philox and the two logarithms of the Gumbel noise run once per
+// legal action instead of once per action.  Illegal actions cannot win and add
+// exp(-1e30 - max) = 0 to the log-sum-exp, so leaving them out changes nothing.
 __global__ void __launch_bounds__(256) sample_kernel(const float* __restrict__ logits, int64_t ld,
                                                      const bool* __restrict__ legal, int64_t m,
                                                      const int64_t* __restrict__ game,
@@ -42,38 +46,55 @@ __global__ void __launch_bounds__(256) sample_kernel(const float* __restrict__ l
   const int lane = threadIdx.x & 31;
   const float* lrow = logits + row * ld;
   const uint8_t* grow = reinterpret_cast<const uint8_t*>(legal) + row * 179;
+  constexpr int kWords = (179 + 31) / 32;  // 6 ballots
+  u32 bits[kWords];
+  int n = 0;
+#pragma unroll
+  for (int k = 0; k < kWords; ++k) {
+    const int a = lane + 32 * k;
+    bits[k] = __ballot_sync(0xffffffffu, a < 179 && grow[a] != 0);
+    n += __popc(bits[k]);
+  }
+  if (n == 0) {
+    if (lane == 0) {
+      action_out[row] = -1;
+      logp_out[row] = 0.0f;
+    }
+    return;
+  }
   const u64 g = static_cast<u64>(__ldg(game + row));
   const u32 d = static_cast<u32>(__ldg(decision + row));
   const u64 seed = static_cast<u64>(seed_base) + g;
-  float best = -INFINITY;
+  float best = -INFINITY, mx = -INFINITY;
   int best_a = -1;
-  float mx = -INFINITY;
-  float logit_of[8];
-  int count = 0;
-  // Lane l takes action blocks l and l + 32 (4 actions each).
+  float xs[kWords];
 #pragma unroll
-  for (int pass = 0; pass < 2; ++pass) {
-    const int blk = lane + 32 * pass;
-    if (blk < kActionsPadded / 4) {
-      Philox4 r{};
-      if (!greedy) r = philox4x32_10(static_cast<u32>(g), static_cast<u32>(g >> 32), d,
-                                     3u | (static_cast<u32>(blk) << 8), static_cast<u32>(seed),
-                                     static_cast<u32>(seed >> 32));
+  for (int c = 0; c < kWords; ++c) {
+    xs[c] = -INFINITY;
+    const int j = 32 * c + lane;  // this lane's rank among the legal actions
+    if (32 * c < n && j < n) {
+      int rank = j, a = -1;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int a = 4 * blk + j;
-        float x = -1.0e30f;
-        if (a < 179 && grow[a]) x = __ldg(lrow + a);
-        logit_of[pass * 4 + j] = x;
-        if (a < 179) {
-          mx = fmaxf(mx, x);
-          const float score = greedy ? x : x + gumbel_of(r.v[j]);
-          if (grow[a] && score > best) {
-            best = score;
-            best_a = a;
-          }
-          count += grow[a] ? 1 : 0;
-        }
+      for (int k = 0; k < kWords; ++k) {
+        const int cnt = __popc(bits[k]);
+        if (a < 0 && rank < cnt) a = 32 * k + static_cast<int>(__fns(bits[k], 0u, rank + 1));
+        else if (a < 0) rank -= cnt;
+      }
+      const float x = __ldg(lrow + a);
+      float score = x;
+      if (!greedy) {
+        const Philox4 r = philox4x32_10(static_cast<u32>(g), static_cast<u32>(g >> 32), d,
+                                        3u | (static_cast<u32>(a >> 2) << 8),
+                                        static_cast<u32>(seed), static_cast<u32>(seed >> 32));
+        const int q = a & 3;
+        const u32 word = q == 0 ? r.v[0] : (q == 1 ? r.v[1] : (q == 2 ? r.v[2] : r.v[3]));
+        score = x + gumbel_of(word);
+      }
+      xs[c] = x;
+      mx = fmaxf(mx, x);
+      if (score > best) {  // ascending actions per lane: the first maximum is the lowest
+        best = score;
+        best_a = a;
       }
     }
   }
@@ -87,25 +108,17 @@ __global__ void __launch_bounds__(256) sample_kernel(const float* __restrict__ l
       best_a = oa;
     }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    count += __shfl_xor_sync(0xffffffffu, count, off);
   }
-  // log-sum-exp over the masked logits (illegal ones contribute exp(-1e30 - mx) = 0).
+  // log-sum-exp over the legal logits.
   float s = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int a = 4 * (lane + 32 * (k >> 2)) + (k & 3);
-    if (a < 179 && (lane + 32 * (k >> 2)) < kActionsPadded / 4) s += expf(logit_of[k] - mx);
-  }
+  for (int c = 0; c < kWords; ++c)
+    if (xs[c] != -INFINITY) s += expf(xs[c] - mx);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (lane == 0) {
-    if (count == 0) {
-      action_out[row] = -1;
-      logp_out[row] = 0.0f;
-    } else {
-      action_out[row] = best_a;
-      logp_out[row] = __ldg(lrow + best_a) - (mx + logf(s));
-    }
+    action_out[row] = best_a;
+    logp_out[row] = __ldg(lrow + best_a) - (mx + logf(s));
   }
 }
 

@@ -1,0 +1,491 @@
+// Decode kernels of the event-sequence policy (sm_100a).
+//
+// The sequence policy (python/cugo_seq50.py:131-339) runs one token per cache row
+// per call: an opening token, one token per committed event for each seat, and a
+// query token per decision.  Its per-layer work around the GEMMs is here:
+//
+//   decode_attention_kernel  single-query attention over a bf16 KV cache
+//                            (python/cugo_seq_attention50.py:22-62), optionally
+//                            appending the token's own key/value to its slot in
+//                            the same pass (the KV append of cached_step,
+//                            python/cugo_seq50.py:313-316);
+//   layernorm_kernel         LayerNorm of the fp32 residual stream into the bf16
+//                            operand of the next GEMM (nn.LayerNorm under
+//                            autocast: fp32 math, bf16 consumer);
+//   event_embed_kernel       event tokens (encode_events + event_in + position +
+//   start_embed_kernel       token type, python/cugo_seq50.py:91-129,271-289) as
+//                            sums of the weight columns of the token's set bits:
+//                            a token is a multi-hot vector with a few dozen ones
+//                            among 414 (274) inputs, so a gather-sum reads ~30
+//                            weight rows instead of running a K=414 GEMM.
+//
+// All of them are memory- or latency-bound; they use warp-per-row (or
+// warp-per-(query, head)) mappings with 16-byte accesses.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "../../include/cugo_b200.h"
+
+namespace {
+
+using i64 = int64_t;
+using u64 = uint64_t;
+using u32 = uint32_t;
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kDh = 32;         // head width of the decode kernel (d_model 256 / 8 heads)
+constexpr int kMaxSlots = 512;  // cache capacity the decode kernel accepts
+constexpr int kEventIn = 8 * 50 + 12 + 2;   // python/cugo_seq50.py:37
+constexpr int kStartIn = 5 * 50 + 12 + 8 + 4;  // python/cugo_seq50.py:38
+constexpr int kMaxEvents = 48;               // python/cugo_seq50.py:34
+
+__device__ __forceinline__ void bf16x8(const uint4 raw, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __bfloat1622float2(h[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+
+// ---- decode attention -------------------------------------------------------------
+//
+// One warp per (query i, head h).  Lane t owns slots t, t+32, ...: it loads the
+// slot's 64-byte key and value rows (four 16-byte loads each; a warp's loads cover
+// a contiguous 2 KB block of the cache), scores the slot in fp32 and keeps its own
+// running max, sum and weighted value sum (online softmax).  The 32 partial states
+// are then merged: a warp max, a rescale, a warp sum of the denominators and a
+// butterfly reduce-scatter of the 32-wide value sums (31 shuffles) after which
+// lane d holds output dimension d.  With an append, the lane of slot pos[i] uses
+// the new key/value from registers and writes them to the cache; the cache rows
+// of different queries must then be distinct (as in cached_step).
+__global__ void __launch_bounds__(256) decode_attention_kernel(
+    const __nv_bfloat16* __restrict__ q, i64 ldq, const __nv_bfloat16* __restrict__ k_new,
+    const __nv_bfloat16* __restrict__ v_new, i64 ldn, __nv_bfloat16* keys, __nv_bfloat16* values,
+    i64 n_rows, int heads, int slots, const i64* __restrict__ pos, i64 pos_clamp,
+    const i64* __restrict__ rows, i64 n, float scale, __nv_bfloat16* __restrict__ out, i64 ldo,
+    int32_t* error) {
+  const i64 gw = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (gw >= n * heads) return;
+  const int lane = threadIdx.x & 31;
+  const i64 i = gw / heads;
+  const int h = static_cast<int>(gw - i * heads);
+  const i64 r = rows ? __ldg(rows + i) : i;
+  i64 p = -1;
+  if (pos_clamp < 0) {
+    p = __ldg(pos + i);
+  } else if (r >= 0 && r < n_rows) {  // pos holds per-row lengths
+    p = __ldg(pos + r);
+    p = p < pos_clamp ? p : pos_clamp;
+  }
+  __nv_bfloat16* o = out + i * ldo + h * kDh;
+  if (p < 0 || p >= slots || r < 0 || r >= n_rows) {
+    o[lane] = __float2bfloat16_rn(0.0f);
+    if (lane == 0 && error) atomicExch(error, 1);
+    return;
+  }
+  float qf[kDh];
+  {
+    const uint4* qp = reinterpret_cast<const uint4*>(q + i * ldq + h * kDh);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) bf16x8(__ldg(qp + c), qf + 8 * c);
+  }
+  const i64 base = (r * heads + h) * static_cast<i64>(slots) * kDh;
+  uint4* kc = reinterpret_cast<uint4*>(keys + base);
+  uint4* vc = reinterpret_cast<uint4*>(values + base);
+  float m = -INFINITY, l = 0.0f, acc[kDh];
+#pragma unroll
+  for (int d = 0; d < kDh; ++d) acc[d] = 0.0f;
+  const int last = static_cast<int>(p);
+  for (int t0 = 0; t0 <= last; t0 += 32) {
+    const int t = t0 + lane;
+    if (t > last) break;
+    uint4 kr[4], vr[4];
+    if (k_new && t == last) {
+      const uint4* kn = reinterpret_cast<const uint4*>(k_new + i * ldn + h * kDh);
+      const uint4* vn = reinterpret_cast<const uint4*>(v_new + i * ldn + h * kDh);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        kr[c] = __ldg(kn + c);
+        vr[c] = __ldg(vn + c);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        kc[4 * t + c] = kr[c];
+        vc[4 * t + c] = vr[c];
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        kr[c] = __ldg(kc + 4 * t + c);
+        vr[c] = __ldg(vc + 4 * t + c);
+      }
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float kf[8];
+      bf16x8(kr[c], kf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(kf[e], qf[8 * c + e], s);
+    }
+    s *= scale;
+    if (s > m) {
+      const float c = expf(m - s);
+      l *= c;
+#pragma unroll
+      for (int d = 0; d < kDh; ++d) acc[d] *= c;
+      m = s;
+    }
+    const float w = expf(s - m);
+    l += w;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float vf[8];
+      bf16x8(vr[c], vf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[8 * c + e] = fmaf(w, vf[e], acc[8 * c + e]);
+    }
+  }
+  // Merge the lanes' partial softmax states.
+  const float mx = warp_max(m);
+  const float f = expf(m - mx);  // 0 for a lane without slots (m = -inf)
+  const float denom = warp_sum(l * f);
+#pragma unroll
+  for (int d = 0; d < kDh; ++d) acc[d] *= f;
+  // Butterfly reduce-scatter: after the level of width w the lane's acc[0..w-1]
+  // hold dimensions (lane & ~(w-1)) .. +w-1, summed over the lanes whose ids
+  // differ from its own only in bits >= w; at the end acc[0] is dimension
+  // `lane` summed over all 32 lanes.
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool upper = (lane & w) != 0;
+#pragma unroll
+    for (int j = 0; j < w; ++j) {
+      const float send = upper ? acc[j] : acc[j + w];
+      const float keep = upper ? acc[j + w] : acc[j];
+      acc[j] = keep + __shfl_xor_sync(kFull, send, w);
+    }
+  }
+  o[lane] = __float2bfloat16_rn(acc[0] / denom);
+}
+
+// ---- LayerNorm ----------------------------------------------------------------------
+//
+// One warp per row; lane l owns 4-column groups l, l+32, ... of the row.  Mean,
+// then the mean squared deviation from it (two passes over registers), then
+// (x - mean) * rsqrt(var + eps) * gamma + beta rounded to bf16.
+template <int V>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, i64 ldx,
+                                                        const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta, float eps,
+                                                        __nv_bfloat16* __restrict__ out, i64 ldo,
+                                                        i64 n) {
+  const i64 row = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= n) return;
+  const int lane = threadIdx.x & 31;
+  constexpr int d = 128 * V;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * ldx);
+  float4 v[V];
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    v[j] = __ldg(xr + lane + 32 * j);
+    s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  }
+  const float mean = warp_sum(s) / d;
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, e = v[j].w - mean;
+    ss += (a * a + b * b) + (c * c + e * e);
+  }
+  const float rstd = rsqrtf(warp_sum(ss) / d + eps);
+  uint2* orow = reinterpret_cast<uint2*>(out + row * ldo);
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int c4 = lane + 32 * j;
+    const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + c4);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(beta) + c4);
+    const __nv_bfloat162 lo = __floats2bfloat162_rn((v[j].x - mean) * rstd * g.x + b.x,
+                                                    (v[j].y - mean) * rstd * g.y + b.y);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn((v[j].z - mean) * rstd * g.z + b.z,
+                                                    (v[j].w - mean) * rstd * g.w + b.w);
+    uint2 raw;
+    raw.x = *reinterpret_cast<const u32*>(&lo);
+    raw.y = *reinterpret_cast<const u32*>(&hi);
+    orow[c4] = raw;
+  }
+}
+
+// ---- token embeddings ----------------------------------------------------------------
+//
+// Embedding rows are d_model = 256 * G wide; lane l owns columns g*256 + 8l .. +7
+// of every group g.  `wt` is the transposed input weight, bf16 [inputs, d_model]
+// (one 512-byte row per input column), so an active input adds one row.
+
+template <int G>
+struct Acc {
+  float v[G][8];
+};
+
+template <int G>
+__device__ __forceinline__ void acc_init(Acc<G>& a) {
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a.v[g][e] = 0.0f;
+}
+
+template <int G>
+__device__ __forceinline__ void acc_row(Acc<G>& a, const __nv_bfloat16* __restrict__ wt, int col,
+                                        float scale) {
+  const int lane = threadIdx.x & 31;
+  const uint4* src = reinterpret_cast<const uint4*>(wt + static_cast<i64>(col) * (256 * G));
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float f[8];
+    bf16x8(__ldg(src + 32 * g + lane), f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a.v[g][e] = fmaf(scale, f[e], a.v[g][e]);
+  }
+}
+
+// Adds the rows of the set bits of a 50-bit card mask (plane `plane`).
+template <int G>
+__device__ __forceinline__ void acc_mask(Acc<G>& a, const __nv_bfloat16* __restrict__ wt, u64 mask,
+                                         int plane) {
+  mask &= (1ull << 50) - 1;
+  while (mask) {
+    const int b = __ffsll(static_cast<long long>(mask)) - 1;
+    mask &= mask - 1;
+    acc_row(a, wt, plane * 50 + b, 1.0f);
+  }
+}
+
+// out row = acc + bias + pos_row + type_row, fp32.
+template <int G>
+__device__ __forceinline__ void acc_store(const Acc<G>& a, const float* __restrict__ bias,
+                                          const float* __restrict__ pos_row,
+                                          const float* __restrict__ type_row, float* out) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int c = 256 * g + 8 * lane;
+    float r[8];
+#pragma unroll
+    for (int e = 0; e < 8; e += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c + e));
+      const float4 p = __ldg(reinterpret_cast<const float4*>(pos_row + c + e));
+      const float4 t = __ldg(reinterpret_cast<const float4*>(type_row + c + e));
+      r[e] = a.v[g][e] + b.x + p.x + t.x;
+      r[e + 1] = a.v[g][e + 1] + b.y + p.y + t.y;
+      r[e + 2] = a.v[g][e + 2] + b.z + p.z + t.z;
+      r[e + 3] = a.v[g][e + 3] + b.w + p.w + t.w;
+    }
+    reinterpret_cast<float4*>(out + c)[0] = make_float4(r[0], r[1], r[2], r[3]);
+    reinterpret_cast<float4*>(out + c)[1] = make_float4(r[4], r[5], r[6], r[7]);
+  }
+}
+
+// Event token of row i: event words events[i % n_events], observer seat seats[i],
+// events before it index[i % n_events] (position 1 + min(index, 47)).  Inputs:
+// 8 card planes (played, drawn — own draws only, flipped, my gain, opponent gain,
+// my loss, opponent loss, shown), one-hot kind (clamped to 11), "mine" flag and
+// the opponent's drawn-card count (python/cugo_seq50.py:91-109).
+template <int G>
+__global__ void __launch_bounds__(256) event_embed_kernel(
+    const i64* __restrict__ events, i64 n_events, const i64* __restrict__ seats,
+    const i64* __restrict__ index, i64 n, const __nv_bfloat16* __restrict__ wt,
+    const float* __restrict__ bias, const float* __restrict__ position,
+    const float* __restrict__ type_row, float* __restrict__ out, i64 ldo) {
+  const i64 i = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (i >= n) return;
+  const i64 e = i % n_events;
+  const i64* ev = events + e * 9;
+  const i64 seat = __ldg(seats + i);
+  const i64 header = __ldg(ev + 8);
+  const bool me = (header & 0xFF) == seat;
+  const i64 kind = (header >> 8) & 0xFF;
+  const bool first = seat == 0;
+  const u64 w[8] = {static_cast<u64>(__ldg(ev + 0)), static_cast<u64>(__ldg(ev + 1)),
+                    static_cast<u64>(__ldg(ev + 2)), static_cast<u64>(__ldg(ev + 3)),
+                    static_cast<u64>(__ldg(ev + 4)), static_cast<u64>(__ldg(ev + 5)),
+                    static_cast<u64>(__ldg(ev + 6)), static_cast<u64>(__ldg(ev + 7))};
+  Acc<G> a;
+  acc_init(a);
+  acc_mask(a, wt, w[0], 0);
+  if (me) acc_mask(a, wt, w[1], 1);
+  acc_mask(a, wt, w[2], 2);
+  acc_mask(a, wt, first ? w[3] : w[4], 3);
+  acc_mask(a, wt, first ? w[4] : w[3], 4);
+  acc_mask(a, wt, first ? w[5] : w[6], 5);
+  acc_mask(a, wt, first ? w[6] : w[5], 6);
+  acc_mask(a, wt, w[7], 7);
+  acc_row(a, wt, 400 + static_cast<int>(kind < 11 ? kind : 11), 1.0f);
+  if (me) acc_row(a, wt, 412, 1.0f);
+  const int opp_drawn = me ? 0 : __popcll(w[1] & ((1ull << 50) - 1));
+  if (opp_drawn) acc_row(a, wt, 413, static_cast<float>(opp_drawn));
+  i64 at = index ? __ldg(index + e) : 0;
+  at = at < 0 ? 0 : (at > kMaxEvents - 1 ? kMaxEvents - 1 : at);
+  acc_store(a, bias, position + (1 + at) * (256 * G), type_row, out + i * ldo);
+}
+
+// Opening token of row i: start words start[i % n_start], observer seat seats[i]
+// (python/cugo_seq50.py:112-128): planes own hand, floor, my captures, opponent
+// captures, mission cards; 12 neutral-month bits; one-hot mission type (clamped
+// to 7); multiplier / 4, "first mover is me", my and the opponent's multi / 8.
+template <int G>
+__global__ void __launch_bounds__(256) start_embed_kernel(
+    const i64* __restrict__ start, i64 n_start, const i64* __restrict__ seats, i64 n,
+    const __nv_bfloat16* __restrict__ wt, const float* __restrict__ bias,
+    const float* __restrict__ pos_row, const float* __restrict__ type_row,
+    float* __restrict__ out, i64 ldo) {
+  const i64 i = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (i >= n) return;
+  const i64* st = start + (i % n_start) * 8;
+  const i64 seat = __ldg(seats + i);
+  const bool first = seat == 0;
+  const i64 header = __ldg(st + 7);
+  Acc<G> a;
+  acc_init(a);
+  acc_mask(a, wt, static_cast<u64>(__ldg(st + (first ? 0 : 1))), 0);
+  acc_mask(a, wt, static_cast<u64>(__ldg(st + 2)), 1);
+  acc_mask(a, wt, static_cast<u64>(__ldg(st + (first ? 3 : 4))), 2);
+  acc_mask(a, wt, static_cast<u64>(__ldg(st + (first ? 4 : 3))), 3);
+  acc_mask(a, wt, static_cast<u64>(__ldg(st + 5)), 4);
+  u64 neutral = static_cast<u64>(__ldg(st + 6)) & 0xFFFull;
+  while (neutral) {
+    const int b = __ffsll(static_cast<long long>(neutral)) - 1;
+    neutral &= neutral - 1;
+    acc_row(a, wt, 250 + b, 1.0f);
+  }
+  const i64 mtype = header & 0xFF;
+  acc_row(a, wt, 262 + static_cast<int>(mtype < 7 ? mtype : 7), 1.0f);
+  const float c0 = static_cast<float>((header >> 8) & 0xFF) / 4.0f;
+  const float c1 = (((header >> 16) & 1) == seat) ? 1.0f : 0.0f;
+  const i64 m24 = (header >> 24) & 0xFF, m32 = (header >> 32) & 0xFF;
+  const float c2 = static_cast<float>(first ? m24 : m32) / 8.0f;
+  const float c3 = static_cast<float>(first ? m32 : m24) / 8.0f;
+  if (c0 != 0.0f) acc_row(a, wt, 270, c0);
+  if (c1 != 0.0f) acc_row(a, wt, 271, c1);
+  if (c2 != 0.0f) acc_row(a, wt, 272, c2);
+  if (c3 != 0.0f) acc_row(a, wt, 273, c3);
+  acc_store(a, bias, pos_row, type_row, out + i * ldo);
+}
+
+bool aligned(const void* p, uintptr_t q) { return (reinterpret_cast<uintptr_t>(p) % q) == 0; }
+
+int launch_status() { return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH; }
+
+unsigned blocks_for_warps(i64 warps) { return static_cast<unsigned>((warps + 7) / 8); }
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new, const void* v_new,
+                               int64_t ldn, void* keys, void* values, int64_t n_rows,
+                               int32_t heads, int32_t slots, int32_t head_dim,
+                               const int64_t* pos, int64_t pos_clamp, const int64_t* rows,
+                               int64_t n, float scale, void* out, int64_t ldo, int32_t* error,
+                               cudaStream_t stream) {
+  if (n < 0 || heads <= 0 || slots <= 0 || slots > kMaxSlots || head_dim != kDh || n_rows <= 0)
+    return CUGO_B200_ERR_ARG;
+  if (n == 0) return CUGO_B200_OK;
+  if (!q || !keys || !values || !pos || !out || (!k_new) != (!v_new)) return CUGO_B200_ERR_ARG;
+  if (ldq < heads * kDh || ldo < heads * kDh || (k_new && ldn < heads * kDh)) return CUGO_B200_ERR_ARG;
+  if (!aligned(q, 16) || ldq % 8 || !aligned(keys, 16) || !aligned(values, 16) || !aligned(out, 2) ||
+      (k_new && (!aligned(k_new, 16) || !aligned(v_new, 16) || ldn % 8)))
+    return CUGO_B200_ERR_ALIGN;
+  decode_attention_kernel<<<blocks_for_warps(n * heads), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k_new),
+      static_cast<const __nv_bfloat16*>(v_new), ldn, static_cast<__nv_bfloat16*>(keys),
+      static_cast<__nv_bfloat16*>(values), n_rows, heads, slots, pos, pos_clamp, rows, n, scale,
+      static_cast<__nv_bfloat16*>(out), ldo, error);
+  return launch_status();
+}
+
+int cugo_b200_layernorm(const float* x, int64_t ldx, const float* gamma, const float* beta,
+                        int64_t d, float eps, void* out, int64_t ldo, int64_t n,
+                        cudaStream_t stream) {
+  if (n < 0 || (d != 128 && d != 256 && d != 512 && d != 1024) || ldx < d || ldo < d)
+    return CUGO_B200_ERR_ARG;
+  if (n == 0) return CUGO_B200_OK;
+  if (!x || !gamma || !beta || !out) return CUGO_B200_ERR_ARG;
+  if (!aligned(x, 16) || ldx % 4 || !aligned(gamma, 16) || !aligned(beta, 16) || !aligned(out, 8) ||
+      ldo % 4)
+    return CUGO_B200_ERR_ALIGN;
+  const unsigned grid = blocks_for_warps(n);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  switch (d) {
+    case 128: layernorm_kernel<1><<<grid, 256, 0, stream>>>(x, ldx, gamma, beta, eps, o, ldo, n); break;
+    case 256: layernorm_kernel<2><<<grid, 256, 0, stream>>>(x, ldx, gamma, beta, eps, o, ldo, n); break;
+    case 512: layernorm_kernel<4><<<grid, 256, 0, stream>>>(x, ldx, gamma, beta, eps, o, ldo, n); break;
+    default: layernorm_kernel<8><<<grid, 256, 0, stream>>>(x, ldx, gamma, beta, eps, o, ldo, n); break;
+  }
+  return launch_status();
+}
+
+int cugo_b200_event_embed(const int64_t* events, int64_t n_events, const int64_t* seats,
+                          const int64_t* index, int64_t n, const void* weight_t,
+                          const float* bias, const float* position, const float* token_type,
+                          int64_t d, float* out, int64_t ldo, cudaStream_t stream) {
+  if (n < 0 || (n > 0 && n_events <= 0) || (d != 256 && d != 512) || ldo < d) return CUGO_B200_ERR_ARG;
+  if (n == 0) return CUGO_B200_OK;
+  if (!events || !seats || !weight_t || !bias || !position || !token_type || !out)
+    return CUGO_B200_ERR_ARG;
+  if (!aligned(weight_t, 16) || !aligned(bias, 16) || !aligned(position, 16) ||
+      !aligned(token_type, 16) || !aligned(out, 16) || ldo % 4)
+    return CUGO_B200_ERR_ALIGN;
+  const unsigned grid = blocks_for_warps(n);
+  const auto* w = static_cast<const __nv_bfloat16*>(weight_t);
+  if (d == 256)
+    event_embed_kernel<1><<<grid, 256, 0, stream>>>(events, n_events, seats, index, n, w, bias,
+                                                    position, token_type, out, ldo);
+  else
+    event_embed_kernel<2><<<grid, 256, 0, stream>>>(events, n_events, seats, index, n, w, bias,
+                                                    position, token_type, out, ldo);
+  return launch_status();
+}
+
+int cugo_b200_start_embed(const int64_t* start, int64_t n_start, const int64_t* seats, int64_t n,
+                          const void* weight_t, const float* bias, const float* position0,
+                          const float* token_type, int64_t d, float* out, int64_t ldo,
+                          cudaStream_t stream) {
+  if (n < 0 || (n > 0 && n_start <= 0) || (d != 256 && d != 512) || ldo < d) return CUGO_B200_ERR_ARG;
+  if (n == 0) return CUGO_B200_OK;
+  if (!start || !seats || !weight_t || !bias || !position0 || !token_type || !out)
+    return CUGO_B200_ERR_ARG;
+  if (!aligned(weight_t, 16) || !aligned(bias, 16) || !aligned(position0, 16) ||
+      !aligned(token_type, 16) || !aligned(out, 16) || ldo % 4)
+    return CUGO_B200_ERR_ALIGN;
+  const unsigned grid = blocks_for_warps(n);
+  const auto* w = static_cast<const __nv_bfloat16*>(weight_t);
+  if (d == 256)
+    start_embed_kernel<1><<<grid, 256, 0, stream>>>(start, n_start, seats, n, w, bias, position0,
+                                                    token_type, out, ldo);
+  else
+    start_embed_kernel<2><<<grid, 256, 0, stream>>>(start, n_start, seats, n, w, bias, position0,
+                                                    token_type, out, ldo);
+  return launch_status();
+}
+
+int64_t cugo_b200_event_inputs(void) { return kEventIn; }
+int64_t cugo_b200_start_inputs(void) { return kStartIn; }
+
+}  // extern "C"

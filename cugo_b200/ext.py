@@ -42,6 +42,14 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_gemm_bf16": [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _VP, _I64, _I32, _I32, _I32,
                             _I64, _I64, _I64, _VP, _VP],
     "cugo_b200_observe_indexed_bf16": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_gemm_bf16_ex": [_VP, _I64, _VP, _I64, _VP, _I32, _VP, _I64, _VP, _I64, _I32, _I32,
+                               _I32, _I64, _I64, _I64, _VP, _VP],
+    "cugo_b200_observe_query_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
+                                   _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
+    "cugo_b200_layernorm": [_VP, _I64, _VP, _VP, _I64, ctypes.c_float, _VP, _I64, _I64, _VP],
+    "cugo_b200_event_embed": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _VP, _I64, _VP],
+    "cugo_b200_start_embed": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _VP, _I64, _VP],
 }
 _CONSTANTS = {
     "FEATURE_COUNT": "cugo_b200_feature_count",
@@ -53,6 +61,7 @@ _CONSTANTS = {
     "STATE_BYTES": "cugo_b200_state_bytes",
     "STATUS_OK": "cugo_b200_status_ok",
 }
+_EXTRA_CONSTANTS = {"EVENT_IN": "cugo_b200_event_inputs", "START_IN": "cugo_b200_start_inputs"}
 _ERRORS = {-1: "invalid argument", -2: "misaligned pointer", -3: "kernel launch failed"}
 
 _LIB: ctypes.CDLL | None = None
@@ -77,7 +86,7 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = argtypes
         fn.restype = ctypes.c_int
-    for fn_name in _CONSTANTS.values():
+    for fn_name in [*_CONSTANTS.values(), *_EXTRA_CONSTANTS.values()]:
         getattr(lib, fn_name).restype = ctypes.c_int64
         getattr(lib, fn_name).argtypes = []
     lib.cugo_b200_abi_version.restype = ctypes.c_int
@@ -128,7 +137,7 @@ class CugoB200Extension:
 
     def __init__(self, lib: ctypes.CDLL) -> None:
         self._lib = lib
-        for attr, fn_name in _CONSTANTS.items():
+        for attr, fn_name in [*_CONSTANTS.items(), *_EXTRA_CONSTANTS.items()]:
             setattr(self, attr, int(getattr(lib, fn_name)()))
 
     # -- helpers ----------------------------------------------------------------
@@ -355,12 +364,36 @@ class CugoB200Extension:
                 self._stream(states.device)), "observe_indexed_bf16")
         return out
 
+    def observe_query_bf16(self, states, env_ids, query: torch.Tensor | None = None,
+                           width: int = 904) -> list[torch.Tensor]:
+        """observe_indexed writing the sequence policy's query input bf16 [m, width]:
+        features in columns 0..719, legal as 0/1 in 720..898, zeros after."""
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _same_device(states, env_ids, "states", "env_ids")
+        m = env_ids.numel()
+        with torch.cuda.device(states.device):
+            out = self._obs_outputs(m, states.device)
+            if query is None:
+                query = torch.empty((m, width), dtype=torch.bfloat16, device=states.device)
+            if query.dtype != torch.bfloat16 or query.dim() != 2 or query.stride(1) != 1 or query.size(0) < m:
+                raise RuntimeError("query must be a row-major bf16 [m, >=899] tensor")
+            out[0] = query
+            _check(self._lib.cugo_b200_observe_query_bf16(
+                _ptr(states), states.size(0), _ptr(env_ids), m, _ptr(query), query.stride(0),
+                *map(_ptr, out[1:]), self._stream(states.device)), "observe_query_bf16")
+        return out
+
     # -- policy layers -------------------------------------------------------------
     def linear(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
                residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
                act: int = 0, act_after: int = 0, out_dtype: torch.dtype = torch.bfloat16,
                error: torch.Tensor | None = None) -> torch.Tensor:
-        """out = act_after(act(a @ w.T + bias) + residual) on tcgen05 tensor cores."""
+        """out = act_after(act(a @ w.T + bias) + residual) on tcgen05 tensor cores.
+
+        act codes: 0 none, 1 ReLU, 2 SiLU, 3 GELU (erf).  bias may be bf16 or fp32;
+        the residual has the output's dtype (an fp32 stream may be updated in place,
+        residual is out)."""
         m, k = a.shape
         n = w.shape[0]
         if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or w.shape[1] != k:
@@ -369,12 +402,104 @@ class CugoB200Extension:
             raise RuntimeError("linear operands must be row-major")
         if out is None:
             out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+        if residual is not None and residual.dtype != out.dtype:
+            raise RuntimeError("linear residual must have the output's dtype")
+        if bias is not None and bias.dtype not in (torch.bfloat16, torch.float32):
+            raise RuntimeError("linear bias must be bf16 or fp32")
         with torch.cuda.device(a.device):
-            _check(self._lib.cugo_b200_gemm_bf16(
-                _ptr(a), a.stride(0), _ptr(w), w.stride(0), _ptr(bias), _ptr(residual),
+            _check(self._lib.cugo_b200_gemm_bf16_ex(
+                _ptr(a), a.stride(0), _ptr(w), w.stride(0), _ptr(bias),
+                int(bias is not None and bias.dtype == torch.float32), _ptr(residual),
                 residual.stride(0) if residual is not None else 0, _ptr(out), out.stride(0),
                 int(out.dtype == torch.float32), act, act_after, m, n, k, _ptr(error),
                 self._stream(a.device)), "gemm_bf16")
+        return out
+
+    # -- sequence policy decode ----------------------------------------------------
+    def decode_attention(self, q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                         pos: torch.Tensor, rows: torch.Tensor | None = None,
+                         k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
+                         pos_clamp: int = -1, out: torch.Tensor | None = None,
+                         error: torch.Tensor | None = None) -> torch.Tensor:
+        """decode_attention (python/cugo_seq_attention50.py:43-57) on the native kernel.
+
+        q [n, heads, dh] bf16 (dh = 32, rows of q may be strided), keys/values
+        [rows, heads, slots, dh] bf16 contiguous, pos/rows int64 -> out [n, heads, dh].
+        k_new/v_new ([n, heads, dh]) are first written to slot pos of each row.
+        pos_clamp >= 0: pos is the per-row length array, position = min(pos[row], clamp)."""
+        n, heads, dh = q.shape
+        if q.dtype != torch.bfloat16 or keys.dtype != torch.bfloat16 or values.dtype != torch.bfloat16:
+            raise RuntimeError("decode_attention expects bf16 q, keys and values")
+        if q.stride(2) != 1 or q.stride(1) != dh or not keys.is_contiguous() or not values.is_contiguous():
+            raise RuntimeError("decode_attention: q heads must be packed, keys/values contiguous")
+        if keys.shape != values.shape or keys.dim() != 4 or keys.shape[1] != heads or keys.shape[3] != dh:
+            raise RuntimeError("decode_attention: keys/values must be [rows, heads, slots, dh]")
+        if (k_new is None) != (v_new is None):
+            raise RuntimeError("decode_attention: pass both k_new and v_new or neither")
+        ldn = 0
+        if k_new is not None:
+            if k_new.stride() != v_new.stride() or k_new.stride(2) != 1 or k_new.stride(1) != dh:
+                raise RuntimeError("decode_attention: k_new/v_new must match q's layout")
+            ldn = k_new.stride(0)
+        if out is None:
+            out = torch.empty((n, heads, dh), dtype=torch.bfloat16, device=q.device)
+        with torch.cuda.device(q.device):
+            _check(self._lib.cugo_b200_decode_attention(
+                _ptr(q), q.stride(0), _ptr(k_new), _ptr(v_new), ldn, _ptr(keys), _ptr(values),
+                keys.shape[0], heads, keys.shape[2], dh, _ptr(pos), pos_clamp, _ptr(rows), n,
+                float(dh ** -0.5), _ptr(out), out.stride(0), _ptr(error),
+                self._stream(q.device)), "decode_attention")
+        return out
+
+    def layernorm(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                  eps: float = 1e-5, out: torch.Tensor | None = None) -> torch.Tensor:
+        """nn.LayerNorm of fp32 rows into bf16 rows."""
+        n, d = x.shape
+        if x.dtype != torch.float32 or x.stride(1) != 1:
+            raise RuntimeError("layernorm expects row-major fp32 x")
+        if out is None:
+            out = torch.empty((n, d), dtype=torch.bfloat16, device=x.device)
+        with torch.cuda.device(x.device):
+            _check(self._lib.cugo_b200_layernorm(
+                _ptr(x), x.stride(0), _ptr(weight), _ptr(bias), d, float(eps), _ptr(out),
+                out.stride(0), n, self._stream(x.device)), "layernorm")
+        return out
+
+    def event_embed(self, events: torch.Tensor, seats: torch.Tensor, index: torch.Tensor | None,
+                    weight_t: torch.Tensor, bias: torch.Tensor, position: torch.Tensor,
+                    token_type: torch.Tensor, n: int | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        """Event tokens fp32 [n, d]; row i reads events[i % len(events)] and seats[i]."""
+        if events.dtype != torch.int64 or not events.is_contiguous() or events.dim() != 2 \
+                or events.size(1) != self.EVENT_WORDS:
+            raise RuntimeError("events must be a contiguous int64 [n, 9] tensor")
+        n = seats.numel() if n is None else n
+        d = weight_t.shape[1]
+        if out is None:
+            out = torch.empty((n, d), dtype=torch.float32, device=events.device)
+        with torch.cuda.device(events.device):
+            _check(self._lib.cugo_b200_event_embed(
+                _ptr(events), events.size(0), _ptr(seats), _ptr(index), n, _ptr(weight_t),
+                _ptr(bias), _ptr(position), _ptr(token_type), d, _ptr(out), out.stride(0),
+                self._stream(events.device)), "event_embed")
+        return out
+
+    def start_embed(self, start: torch.Tensor, seats: torch.Tensor, weight_t: torch.Tensor,
+                    bias: torch.Tensor, position0: torch.Tensor, token_type: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        """Opening tokens fp32 [n, d]; row i reads start[i % len(start)] and seats[i]."""
+        if start.dtype != torch.int64 or not start.is_contiguous() or start.dim() != 2 \
+                or start.size(1) != self.START_WORDS:
+            raise RuntimeError("start must be a contiguous int64 [n, 8] tensor")
+        n = seats.numel()
+        d = weight_t.shape[1]
+        if out is None:
+            out = torch.empty((n, d), dtype=torch.float32, device=start.device)
+        with torch.cuda.device(start.device):
+            _check(self._lib.cugo_b200_start_embed(
+                _ptr(start), start.size(0), _ptr(seats), n, _ptr(weight_t), _ptr(bias),
+                _ptr(position0), _ptr(token_type), d, _ptr(out), out.stride(0),
+                self._stream(start.device)), "start_embed")
         return out
 
     # -- policy sampling ---------------------------------------------------------

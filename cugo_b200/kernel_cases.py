@@ -12,6 +12,9 @@ FLOPs of one launch:
   branch    ROOTS PER  branch_indexed, 274 B per branch
   selfplay  SLOTS      the fused config-1 decision kernel, 4,027 B per decision
   sample    ROWS       the Gumbel-max sampler, 180*4 + 179 + 16 B read, 12 B written per row
+  attention N R        decode attention with KV append over a [R, 8, 50, 32] bf16 cache,
+                       N queries at uniform positions 0..49: (pos + 3) * 1,024 B per query
+  seqwave   W WAVES    sequence self-play (4-layer d256 policy), WAVES waves of W games
 """
 from __future__ import annotations
 
@@ -114,6 +117,35 @@ def main() -> None:
         sec = _time(lambda: ext.selfplay_random_step(states, game, dec, done, steps, feats, legal),
                     args.warmup, args.iters)
         out.update(seconds=sec, decisions_per_s=slots / sec, gbs=slots * 4027 / sec / 1e9)
+    elif args.case == "attention":
+        n, r = d
+        slots, heads, dh = 50, 8, 32
+        g = torch.Generator(device="cpu").manual_seed(0)
+        kc = torch.randn((r, heads, slots, dh), generator=g).to(dev, torch.bfloat16)
+        vc = torch.randn((r, heads, slots, dh), generator=g).to(dev, torch.bfloat16)
+        qkv = torch.randn((n, 3 * heads * dh), generator=g).to(dev, torch.bfloat16)
+        pos = torch.randint(0, slots, (n,), generator=g).to(dev)
+        rows = torch.randperm(r, generator=g)[:n].to(dev)
+        q, kn, vn = (qkv[:, i * 256:(i + 1) * 256].view(n, heads, dh) for i in range(3))
+        sec = _time(lambda: ext.decode_attention(q, kc, vc, pos, rows, k_new=kn, v_new=vn),
+                    args.warmup, args.iters)
+        nbytes = int(((pos + 3) * 1024).sum())
+        out.update(seconds=sec, gbs=nbytes / sec / 1e9, bytes_per_launch=nbytes)
+    elif args.case == "seqwave":
+        from .seq import SeqDecoder
+        from .seq_selfplay import SeqWaveSelfPlay
+        w, waves = d
+        sp = SeqWaveSelfPlay(SeqDecoder.from_state_dict(SeqDecoder.random_state(0)), wave=w)
+        sp.play_wave(0)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        steps = [sp.play_wave(g * w) for g in range(1, waves + 1)]
+        b.record()
+        torch.cuda.synchronize()
+        sec = a.elapsed_time(b) / 1e3
+        out.update(seconds=sec, games_per_s=w * waves / sec, steps=steps)
+        sp.release()
     elif args.case == "sample":
         (rows,) = d
         logits = torch.randn((rows, 180), device=dev)

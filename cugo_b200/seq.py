@@ -1,0 +1,238 @@
+"""Incremental inference of the event-sequence policy on the native kernels.
+
+`SeqDecoder` runs the decode half of the reference's ``SeqNet``
+(python/cugo_seq50.py:131-339) in "hybrid" mode: opening, event and query tokens
+and ``cached_step`` — one new token per cache row through the pre-LN transformer
+layers with the token's key/value appended to the row's KV cache — and the
+``readout`` head.  Per layer:
+
+    a   = LayerNorm1(x)                       layernorm kernel        (fp32 -> bf16)
+    qkv = a . W_in^T + b_in                   tcgen05 GEMM            (bf16 [n, 3d])
+    att = attend(q; cache + appended k, v)    decode-attention kernel (bf16 [n, d])
+    x  += att . W_out^T + b_out               tcgen05 GEMM, fp32 residual in place
+    a   = LayerNorm2(x)
+    f   = GELU(a . W_1^T + b_1)               tcgen05 GEMM, GELU epilogue
+    x  += f . W_2^T + b_2                     tcgen05 GEMM, fp32 residual in place
+
+Numerics follow the reference under bf16 autocast: GEMM operands bf16 with fp32
+accumulation, LayerNorm and softmax in fp32, the residual stream x in fp32 (the
+reference's x becomes fp32 when its fp32 position/type parameters are added),
+the KV cache bf16.  Opening and event tokens are multi-hot vectors; they are
+embedded by gather-sum kernels over the transposed input weights.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .ext import load_extension
+
+MAX_EVENTS = 48  # python/cugo_seq50.py:34
+FEATURES = 720
+ACTIONS = 179
+QUERY_IN = FEATURES + ACTIONS  # hybrid query input (python/cugo_seq50.py:152-153)
+QUERY_LD = 904                 # query rows padded to a multiple of 16 bytes
+ACT_GELU = 3
+
+
+def decode_attention(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, pos: torch.Tensor,
+                     use_triton: bool = True, rows: torch.Tensor | None = None) -> torch.Tensor:
+    """Drop-in for the reference's decode_attention (python/cugo_seq_attention50.py:43-57):
+    q [n, heads, 32]; keys/values [rows, heads, slots, 32] bf16 (contiguous); pos, rows
+    int64 [n] (rows defaults to 0..n-1) -> [n, heads, 32] in q's dtype.  `use_triton` is
+    accepted for signature compatibility; the native kernel always runs (q is read as
+    bf16, as the reference's callers pass it under autocast)."""
+    del use_triton
+    out = load_extension().decode_attention(q.to(torch.bfloat16), keys, values, pos.contiguous(),
+                                            None if rows is None else rows.contiguous())
+    return out if q.dtype == torch.bfloat16 else out.to(q.dtype)
+
+
+@dataclass
+class _Layer:
+    norm1_w: torch.Tensor
+    norm1_b: torch.Tensor
+    w_in: torch.Tensor   # bf16 [3d, d]
+    b_in: torch.Tensor   # fp32 [3d]
+    w_out: torch.Tensor  # bf16 [d, d]
+    b_out: torch.Tensor
+    norm2_w: torch.Tensor
+    norm2_b: torch.Tensor
+    w1: torch.Tensor     # bf16 [ffn, d]
+    b1: torch.Tensor
+    w2: torch.Tensor     # bf16 [d, ffn]
+    b2: torch.Tensor
+
+
+class SeqKVCache:
+    """Keys/values of every cached token per row and layer (python/cugo_seq50.py:325-339):
+    k, v bf16 [layers, rows, heads, slots, dh]; length int64 [rows]."""
+
+    def __init__(self, decoder: "SeqDecoder", rows: int, slots: int = MAX_EVENTS + 2) -> None:
+        dev = decoder.device
+        self.heads, self.slots = decoder.heads, slots
+        shape = (decoder.layers, rows, decoder.heads, slots, decoder.d_model // decoder.heads)
+        self.k = torch.zeros(shape, dtype=torch.bfloat16, device=dev)
+        self.v = torch.zeros_like(self.k)
+        self.length = torch.zeros(rows, dtype=torch.int64, device=dev)
+        self.rows = rows
+
+
+class SeqDecoder:
+    """SeqNet's incremental API (start_token, event_token, query_token,
+    cached_step, readout) on tcgen05 GEMMs and the decode kernels."""
+
+    def __init__(self, params: dict[str, torch.Tensor], layers: int, heads: int,
+                 device: torch.device | str = "cuda", eps: float = 1e-5) -> None:
+        self.ext = load_extension()
+        self.device = torch.device(device)
+        dev = self.device
+        f32 = dict(dtype=torch.float32, device=dev)
+
+        def bf16(t: torch.Tensor) -> torch.Tensor:
+            return t.detach().to(dev, torch.bfloat16).contiguous()
+
+        def fp32(t: torch.Tensor) -> torch.Tensor:
+            return t.detach().to(**f32).contiguous()
+
+        p = params
+        self.layers, self.heads, self.eps = layers, heads, eps
+        self.d_model = p["position"].shape[1]
+        d = self.d_model
+        if d // heads != 32:
+            raise ValueError("the decode kernel needs 32-wide heads")
+        self.position = fp32(p["position"])        # [MAX_EVENTS + 1, d]
+        self.token_type = fp32(p["token_type"])    # [3, d]
+        self.event_wt = bf16(p["event_in.weight"].t())   # [414, d]
+        self.event_b = fp32(p["event_in.bias"])
+        self.start_wt = bf16(p["start_in.weight"].t())   # [274, d]
+        self.start_b = fp32(p["start_in.bias"])
+        q0 = p["query_in.0.weight"]
+        if q0.shape[1] != QUERY_IN:
+            raise ValueError("only the hybrid query (720 features + 179 legal) is supported")
+        w = torch.zeros((q0.shape[0], QUERY_LD), dtype=torch.float32)
+        w[:, :QUERY_IN] = q0.detach().float().cpu()
+        self.q_w0 = bf16(w)
+        self.q_b0 = fp32(p["query_in.0.bias"])
+        self.q_w1 = bf16(p["query_in.2.weight"])
+        # query_in(...) + token_type[2]: the type row folds into the fp32 bias.
+        self.q_b1 = fp32(p["query_in.2.bias"].detach().float().cpu() + p["token_type"].detach().float().cpu()[2])
+        self.blocks: list[_Layer] = []
+        for i in range(layers):
+            pre = f"encoder.layers.{i}."
+            self.blocks.append(_Layer(
+                fp32(p[pre + "norm1.weight"]), fp32(p[pre + "norm1.bias"]),
+                bf16(p[pre + "self_attn.in_proj_weight"]), fp32(p[pre + "self_attn.in_proj_bias"]),
+                bf16(p[pre + "self_attn.out_proj.weight"]), fp32(p[pre + "self_attn.out_proj.bias"]),
+                fp32(p[pre + "norm2.weight"]), fp32(p[pre + "norm2.bias"]),
+                bf16(p[pre + "linear1.weight"]), fp32(p[pre + "linear1.bias"]),
+                bf16(p[pre + "linear2.weight"]), fp32(p[pre + "linear2.bias"])))
+        self.norm_w, self.norm_b = fp32(p["norm.weight"]), fp32(p["norm.bias"])
+        self.h_w0, self.h_b0 = bf16(p["head.0.weight"]), fp32(p["head.0.bias"])
+        h2 = p["head.2.weight"]
+        self.outputs = h2.shape[0]
+        self.out_ld = (self.outputs + 3) // 4 * 4  # fp32 rows in 16-byte multiples
+        self.h_w1, self.h_b1 = bf16(h2), fp32(p["head.2.bias"])
+
+    # -- construction -------------------------------------------------------------
+    @classmethod
+    def from_state_dict(cls, state: dict[str, torch.Tensor], heads: int = 8,
+                        device: torch.device | str = "cuda") -> "SeqDecoder":
+        """Loads a reference SeqNet(mode="hybrid") state dict (weights rounded to bf16)."""
+        layers = len({k.split(".")[2] for k in state if k.startswith("encoder.layers.")})
+        return cls(state, layers, heads, device)
+
+    @staticmethod
+    def random_state(seed: int = 0, d_model: int = 256, layers: int = 4, ffn: int = 1024,
+                     outputs: int = ACTIONS) -> dict[str, torch.Tensor]:
+        """A SeqNet-shaped state dict drawn from torch.manual_seed(seed): nn.Linear's
+        default U(-1/sqrt(in), 1/sqrt(in)) weights and biases, N(0, 0.02) position and
+        token-type tables, LayerNorm weight 1 and bias 0 (python/cugo_seq50.py:154-166)."""
+        g = torch.Generator().manual_seed(seed)
+
+        def lin(name: str, out_f: int, in_f: int) -> dict[str, torch.Tensor]:
+            b = 1.0 / math.sqrt(in_f)
+            return {name + ".weight": (torch.rand((out_f, in_f), generator=g) * 2 - 1) * b,
+                    name + ".bias": (torch.rand((out_f,), generator=g) * 2 - 1) * b}
+
+        d = d_model
+        st: dict[str, torch.Tensor] = {}
+        st.update(lin("event_in", d, 8 * 50 + 12 + 2))
+        st.update(lin("start_in", d, 5 * 50 + 12 + 8 + 4))
+        st.update(lin("query_in.0", 2 * d, QUERY_IN))
+        st.update(lin("query_in.2", d, 2 * d))
+        st["position"] = torch.randn((MAX_EVENTS + 1, d), generator=g) * 0.02
+        st["token_type"] = torch.randn((3, d), generator=g) * 0.02
+        for i in range(layers):
+            pre = f"encoder.layers.{i}."
+            inp = lin(pre + "self_attn.in_proj", 3 * d, d)
+            st[pre + "self_attn.in_proj_weight"] = inp[pre + "self_attn.in_proj.weight"]
+            st[pre + "self_attn.in_proj_bias"] = inp[pre + "self_attn.in_proj.bias"]
+            st.update(lin(pre + "self_attn.out_proj", d, d))
+            st.update(lin(pre + "linear1", ffn, d))
+            st.update(lin(pre + "linear2", d, ffn))
+            for nm in ("norm1", "norm2"):
+                st[pre + nm + ".weight"] = torch.ones(d)
+                st[pre + nm + ".bias"] = torch.zeros(d)
+        st["norm.weight"], st["norm.bias"] = torch.ones(d), torch.zeros(d)
+        st.update(lin("head.0", d, d))
+        st.update(lin("head.2", outputs, d))
+        return {k: v.to(torch.bfloat16).float() for k, v in st.items()}
+
+    def new_cache(self, rows: int, slots: int = MAX_EVENTS + 2) -> SeqKVCache:
+        return SeqKVCache(self, rows, slots)
+
+    # -- tokens --------------------------------------------------------------------
+    def start_token(self, start: torch.Tensor, seat: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        """SeqNet.start_token (python/cugo_seq50.py:271-274): fp32 [n, d];
+        row i reads start[i % len(start)]."""
+        return self.ext.start_embed(start, seat, self.start_wt, self.start_b, self.position[0],
+                                    self.token_type[0], out=out)
+
+    def event_token(self, words: torch.Tensor, seat: torch.Tensor, index: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        """SeqNet.event_token (python/cugo_seq50.py:276-282): fp32 [n, d] for n =
+        len(seat); row i reads words[i % len(words)] and index[i % len(words)]."""
+        return self.ext.event_embed(words, seat, index, self.event_wt, self.event_b, self.position,
+                                    self.token_type[1], out=out)
+
+    def query_token(self, query: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """SeqNet.query_token (python/cugo_seq50.py:284-286) from the bf16 [n, 904]
+        query input that observe_query_bf16 writes: fp32 [n, d]."""
+        h = self.ext.linear(query, self.q_w0, self.q_b0, act=ACT_GELU)
+        return self.ext.linear(h, self.q_w1, self.q_b1, out=out, out_dtype=torch.float32)
+
+    # -- decode --------------------------------------------------------------------
+    def cached_step(self, cache: SeqKVCache, x: torch.Tensor, slots: int | None = None,
+                    rows: torch.Tensor | None = None) -> torch.Tensor:
+        """SeqNet.cached_step (python/cugo_seq50.py:291-322) on x fp32 [n, d], updated
+        in place and returned.  Token i goes to slot min(cache.length[row], slots - 1)
+        of its cache row (rows[i], default i) and attends slots 0.. that one."""
+        ext = self.ext
+        n, d = x.shape
+        heads, dh = self.heads, d // self.heads
+        t = cache.slots if slots is None else min(slots, cache.slots)
+        for i, L in enumerate(self.blocks):
+            a = ext.layernorm(x, L.norm1_w, L.norm1_b, self.eps)
+            qkv = ext.linear(a, L.w_in, L.b_in)
+            q = qkv[:, :d].view(n, heads, dh)
+            k = qkv[:, d:2 * d].view(n, heads, dh)
+            v = qkv[:, 2 * d:].view(n, heads, dh)
+            att = ext.decode_attention(q, cache.k[i], cache.v[i], cache.length, rows=rows, k_new=k,
+                                       v_new=v, pos_clamp=t - 1)
+            ext.linear(att.view(n, d), L.w_out, L.b_out, residual=x, out=x)
+            a = ext.layernorm(x, L.norm2_w, L.norm2_b, self.eps)
+            f = ext.linear(a, L.w1, L.b1, act=ACT_GELU)
+            ext.linear(f, L.w2, L.b2, residual=x, out=x)
+        return x
+
+    def readout(self, h: torch.Tensor) -> torch.Tensor:
+        """SeqNet.readout (python/cugo_seq50.py:288-289, head(norm(h))): fp32 [n, outputs]."""
+        a = self.ext.layernorm(h, self.norm_w, self.norm_b, self.eps)
+        z = self.ext.linear(a, self.h_w0, self.h_b0, act=ACT_GELU)
+        out = torch.empty((h.shape[0], self.out_ld), dtype=torch.float32, device=h.device)
+        self.ext.linear(z, self.h_w1, self.h_b1, out=out[:, :self.outputs])
+        return out[:, :self.outputs]

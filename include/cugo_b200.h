@@ -191,6 +191,18 @@ CUGO_B200_API int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w,
                                       int32_t act_after, int64_t m, int64_t n, int64_t k,
                                       int32_t* error, cudaStream_t stream);
 
+/* The same layer for the sequence transformer's blocks (python/cugo_seq50.py:
+ * 318-321, nn.Linear under autocast with an fp32 residual stream x):
+ * bias is fp32 when bias_fp32 != 0; the residual has the output's type, so with
+ * out_fp32 an fp32 residual stream is updated in place (residual == out);
+ * act/act_after may also be 3 = GELU (erf form, nn.GELU()). */
+CUGO_B200_API int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ldw,
+                                         const void* bias, int32_t bias_fp32,
+                                         const void* residual, int64_t ldr, void* out,
+                                         int64_t ldo, int32_t out_fp32, int32_t act,
+                                         int32_t act_after, int64_t m, int64_t n, int64_t k,
+                                         int32_t* error, cudaStream_t stream);
+
 /* Policy forward that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory — for example a Go/Java/Rust
  * serving process that passes only its own fixed input and output buffers and keeps
@@ -225,6 +237,73 @@ CUGO_B200_API int cugo_b200_observe_indexed_bf16(const uint8_t* states, int64_t 
                                                  void* features_bf16, bool* legal,
                                                  uint8_t* players, bool* done, int16_t* status,
                                                  cudaStream_t stream);
+
+/* observe_indexed writing the sequence policy's hybrid query input in one pass
+ * (python/cugo_seq50.py:196-208: cat(features, legal) cast to bf16): query bf16
+ * [m, ldq] with features in columns 0..719, legal as 0/1 in 720..898 and zeros
+ * in 899..ldq-1 (ldq >= 899, a multiple of 8, e.g. 904); legal/players/done/
+ * status as observe_indexed. */
+CUGO_B200_API int cugo_b200_observe_query_bf16(const uint8_t* states, int64_t n_states,
+                                               const int64_t* env_ids, int64_t m, void* query,
+                                               int64_t ldq, bool* legal, uint8_t* players,
+                                               bool* done, int16_t* status, cudaStream_t stream);
+
+/* ---- Sequence policy decode ------------------------------------------------------
+ * Single-query attention over a KV cache, replacing decode_attention and its
+ * Triton _decode_kernel (python/cugo_seq_attention50.py:22-62), optionally fused
+ * with cached_step's KV append (python/cugo_seq50.py:313-316).
+ * q bf16: query i, head h at q + i*ldq + h*head_dim; keys/values bf16 [n_rows,
+ * heads, slots, head_dim]; rows int64 [n] cache row of query i (NULL: row i);
+ * pos int64: with pos_clamp < 0, pos[i] is query i's position (attend slots
+ * 0..pos[i], as decode_attention's pos); with pos_clamp >= 0, pos is the cache's
+ * per-row length array and the position is min(pos[rows[i]], pos_clamp) (the
+ * clamp cached_step applies); out bf16 at out + i*ldo + h*head_dim;
+ * scale = head_dim^-0.5 as the reference passes it.  With k_new/v_new (bf16,
+ * row stride ldn, same head layout as q) the token's key/value are first
+ * written to slot pos[i] of its row, which it then attends; the rows of one call
+ * must then be distinct.  head_dim must be 32, slots <= 512; a query whose pos
+ * or row is out of range gets zeros and sets *error (device int, may be NULL). */
+CUGO_B200_API int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new,
+                                             const void* v_new, int64_t ldn, void* keys,
+                                             void* values, int64_t n_rows, int32_t heads,
+                                             int32_t slots, int32_t head_dim,
+                                             const int64_t* pos, int64_t pos_clamp,
+                                             const int64_t* rows, int64_t n, float scale,
+                                             void* out, int64_t ldo, int32_t* error,
+                                             cudaStream_t stream);
+
+/* nn.LayerNorm(d) of fp32 rows (eps as given, biased variance) into bf16 rows,
+ * the operand of the next GEMM (norm1/norm2/norm of the sequence transformer,
+ * python/cugo_seq50.py:311,321; python/cugo_seq50.py:226).  d in {128, 256, 512,
+ * 1024}; x, gamma, beta fp32, 16-byte aligned; out bf16 (8-byte aligned). */
+CUGO_B200_API int cugo_b200_layernorm(const float* x, int64_t ldx, const float* gamma,
+                                      const float* beta, int64_t d, float eps, void* out,
+                                      int64_t ldo, int64_t n, cudaStream_t stream);
+
+/* Event tokens (SeqNet.event_token, python/cugo_seq50.py:276-282 with
+ * encode_events :91-109): out[i] = event_in(tokens(events[i % n_events],
+ * seats[i])) + position[1 + min(index[i % n_events], 47)] + token_type_row.
+ * weight_t is the transposed event_in weight, bf16 [414, d]; bias, position
+ * ([49, d]) and token_type_row fp32; out fp32 [n, ldo]; d in {256, 512}.
+ * index may be NULL (0). */
+CUGO_B200_API int cugo_b200_event_embed(const int64_t* events, int64_t n_events,
+                                        const int64_t* seats, const int64_t* index, int64_t n,
+                                        const void* weight_t, const float* bias,
+                                        const float* position, const float* token_type,
+                                        int64_t d, float* out, int64_t ldo, cudaStream_t stream);
+
+/* Opening tokens (SeqNet.start_token, python/cugo_seq50.py:271-274 with
+ * encode_start :112-128): out[i] = start_in(tokens(start[i % n_start], seats[i]))
+ * + position0 + token_type_row.  weight_t bf16 [274, d] (transposed start_in
+ * weight); other arguments as cugo_b200_event_embed. */
+CUGO_B200_API int cugo_b200_start_embed(const int64_t* start, int64_t n_start,
+                                        const int64_t* seats, int64_t n, const void* weight_t,
+                                        const float* bias, const float* position0,
+                                        const float* token_type, int64_t d, float* out,
+                                        int64_t ldo, cudaStream_t stream);
+
+CUGO_B200_API int64_t cugo_b200_event_inputs(void); /* EVENT_IN = 414 */
+CUGO_B200_API int64_t cugo_b200_start_inputs(void); /* START_IN = 274 */
 
 #ifdef __cplusplus
 }
