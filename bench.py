@@ -76,10 +76,8 @@ def barrier(world):
 
 
 def all_reduce(values, world, op="sum"):
-    t = torch.tensor(values, dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX)
-    return t.tolist()
+    from cugo_b200.shard import all_reduce as _all_reduce
+    return _all_reduce(values, world, op, device="cuda")
 
 
 # ---- clocks ---------------------------------------------------------------------------
@@ -141,8 +139,8 @@ def selfplay_bench(args, world, rank, ext, policy):
     total_steps = args.warmup + args.steps
     # Game blocks for every step, resident in HBM before timing: rank r, step s
     # plays games (s * world + r) * g .. + g.
-    blocks = [torch.arange(g, dtype=torch.int64, device=dev) + (s * world + rank) * g
-              for s in range(total_steps)]
+    from cugo_b200.shard import game_block
+    blocks = [game_block(s, rank, world, g, dev) for s in range(total_steps)]
     for s in range(args.warmup):
         play_batch(ext, policy, blocks[s])
     barrier(world)
@@ -376,7 +374,7 @@ def main():
         "extras": extras,
     }
     if rank == 0 and not args.no_cpu_baseline:
-        cpu_games = 65536  # 10-20 s of host work
+        cpu_games = 98304  # 10-20 s of host work
         cpu = cpu_selfplay(cpu_games, args.arch, host_threads())
         out["cpu_baseline"] = {
             "value": cpu["games_per_s"], "unit": "games/s", "cores": host_threads(),

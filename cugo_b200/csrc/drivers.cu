@@ -116,8 +116,8 @@ __global__ void __launch_bounds__(kBlock) selfplay_step_kernel(
   Game g;
 #pragma unroll
   for (int w = 0; w < kRowWords; ++w) g.w[w] = t.rows[lane][w];
-  __syncwarp();
-  ObsPacket pk;
+  __syncwarp();  // rows are in registers: the tile now holds packets
+  const PacketRef pk{t.pk.bits[lane], t.pk.scal[lane]};
   ObsMeta meta;
   u32 action = 0xffffu;
   i64 game = 0;
@@ -139,11 +139,7 @@ __global__ void __launch_bounds__(kBlock) selfplay_step_kernel(
     for (u32 k = 0; k < kScalarColumns; ++k) pk.scal[k] = 0.0f;
     meta.legal = Legal{};
   }
-  // Packets to shared memory, then the cooperative feature/mask writes.
-#pragma unroll
-  for (int k = 0; k < (int)kBitWords; ++k) t.pk.bits[lane][k] = pk.bits[k];
-#pragma unroll
-  for (int k = 0; k < (int)kScalarColumns; ++k) t.pk.scal[lane][k] = pk.scal[k];
+  // Packets are in shared memory; the cooperative feature/mask writes follow.
   t.legal[lane][0] = meta.legal.w0;
   t.legal[lane][1] = meta.legal.w1;
   t.legal[lane][2] = meta.legal.w2;

@@ -317,9 +317,17 @@ CB_HD void stage_pending_view(Game& v, const Peek& p) {
 constexpr u32 kScalarColumns = 37;
 constexpr u32 kBitWords = 24;
 
+// Where a packet is written: a thread's own slice of a shared-memory tile in the
+// kernels (no registers or local memory held for it), or an ObsPacket on the host.
+struct PacketRef {
+  u32* bits;    // [kBitWords]
+  float* scal;  // [kScalarColumns]
+};
+
 struct ObsPacket {
   u32 bits[kBitWords];
   float scal[kScalarColumns];
+  CB_HD PacketRef ref() { return PacketRef{bits, scal}; }
 };
 
 // Slot of a non-binary feature column in ObsPacket::scal, or -1.
@@ -397,7 +405,7 @@ struct PacketInputs {
 };
 
 // pack_policy_observation50 + encode_torch_packet50 for the observer's seat.
-CB_HD void pack_observation(const Game& g, const PacketInputs& in, ObsPacket& pk) {
+CB_HD void pack_observation(const Game& g, const PacketInputs& in, PacketRef pk) {
   for (u32 i = 0; i < kBitWords; ++i) pk.bits[i] = 0;
   const u32 me = observer_seat(g), op = me ^ 1u;
   const Mask own_hand = g.hand(me), opp_hand = g.hand(op);
@@ -436,7 +444,7 @@ CB_HD void pack_observation(const Game& g, const PacketInputs& in, ObsPacket& pk
   put_bits(b, 396, in.choices & kFullDeck);
   const bool first = ((g.actor() ^ g.turn()) & 1u) == me;
   put_flag(b, 446, first);
-  if (in.decision >= 1u && in.decision <= 5u) put_flag(b, 446 + in.decision, true);
+  for (u32 k = 1; k <= 5u; ++k) put_flag(b, 446 + k, in.decision == k);  // constant columns
   put_flag(b, 469, (g.owner1() & gukjin_pi_flag(me)) != 0);
   put_flag(b, 470, (g.owner1() & gukjin_pi_flag(op)) != 0);
   put_bits(b, 479, g.neutral_ppuk() & 0xfffu);
@@ -509,7 +517,7 @@ CB_HD void pack_observation(const Game& g, const PacketInputs& in, ObsPacket& pk
 
 // The packet of an observation whose pending probe failed: an all-zero
 // observation except the pending action and the revealed card.
-CB_HD void pack_failed_probe(u32 primary, u32 revealed, ObsPacket& pk) {
+CB_HD void pack_failed_probe(u32 primary, u32 revealed, PacketRef pk) {
   for (u32 i = 0; i < kBitWords; ++i) pk.bits[i] = 0;
   for (u32 i = 0; i < kScalarColumns; ++i) pk.scal[i] = 0.0f;
   pk.scal[18] = primary < kPrimaryActions
@@ -561,7 +569,7 @@ CB_HD LegalInfo torch_legal(const Game& g) {
 }
 
 // make_torch_packet50 + encode: the observation of one row.
-CB_HD void observe_game(const Game& g, ObsPacket& pk, ObsMeta& meta) {
+CB_HD void observe_game(const Game& g, PacketRef pk, ObsMeta& meta) {
   meta.done = g.done() ? 1u : 0u;
   const LegalInfo li = torch_legal(g);
   meta.legal = li.legal;

@@ -55,13 +55,25 @@ __device__ __forceinline__ i64 lane_source(const i64* ids, i64 row, i64 m, i64 n
 }
 
 // Gathers the warp's 32 source rows into the tile (zero rows for missing ids).
+// Asynchronous 8-byte copies (cp.async) put all 32 rows in flight at once
+// instead of a load -> shared store chain per word.
 __device__ __forceinline__ void gather_rows(WarpTile& t, const u64* __restrict__ src, i64 my_src) {
   const int lane = threadIdx.x & 31;
 #pragma unroll 8
   for (int r = 0; r < 32; ++r) {
     const i64 id = __shfl_sync(kFull, my_src, r);
-    if (lane < kRowWords) t.rows[r][lane] = id >= 0 ? __ldg(src + id * kRowWords + lane) : 0ull;
+    if (lane < kRowWords) {
+      if (id >= 0) {
+        const u32 dst = static_cast<u32>(__cvta_generic_to_shared(&t.rows[r][lane]));
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst),
+                     "l"(src + id * kRowWords + lane)
+                     : "memory");
+      } else {
+        t.rows[r][lane] = 0ull;
+      }
+    }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncwarp();
 }
 
@@ -89,12 +101,14 @@ __device__ __forceinline__ void store_game(WarpTile& t, Game g) {
   for (int k = 0; k < kRowWords; ++k) t.rows[lane][k] = g.w[k];
 }
 
-__device__ __forceinline__ void store_packet(WarpTile& t, const ObsPacket& pk, const Legal& legal) {
+// This lane's packet slice of the tile (valid once every lane has loaded its row).
+__device__ __forceinline__ PacketRef lane_packet(WarpTile& t) {
   const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int k = 0; k < (int)kBitWords; ++k) t.pk.bits[lane][k] = pk.bits[k];
-#pragma unroll
-  for (int k = 0; k < (int)kScalarColumns; ++k) t.pk.scal[lane][k] = pk.scal[k];
+  return PacketRef{t.pk.bits[lane], t.pk.scal[lane]};
+}
+
+__device__ __forceinline__ void store_legal(WarpTile& t, const Legal& legal) {
+  const int lane = threadIdx.x & 31;
   t.legal[lane][0] = legal.w0;
   t.legal[lane][1] = legal.w1;
   t.legal[lane][2] = legal.w2;
@@ -226,8 +240,8 @@ __global__ void __launch_bounds__(kBlock) observe_kernel(
   gather_rows(t, states, src);
   Game g;
   load_game(t, g);
-  __syncwarp();
-  ObsPacket pk;
+  __syncwarp();  // rows are in registers: the tile now holds packets
+  const PacketRef pk = lane_packet(t);
   ObsMeta meta;
   if (src >= 0) {
     observe_game(g, pk, meta);
@@ -239,7 +253,7 @@ __global__ void __launch_bounds__(kBlock) observe_kernel(
     meta.done = 1;
     meta.status = -1;
   }
-  store_packet(t, pk, meta.legal);
+  store_legal(t, meta.legal);
   const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
   const i64 left = m - tile_base;
   const int rows_here = left >= 32 ? 32 : (left > 0 ? (int)left : 0);

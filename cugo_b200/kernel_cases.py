@@ -15,6 +15,7 @@ FLOPs of one launch:
   attention N R        decode attention with KV append over a [R, 8, 50, 32] bf16 cache,
                        N queries at uniform positions 0..49: (pos + 3) * 1,024 B per query
   seqwave   W WAVES    sequence self-play (4-layer d256 policy), WAVES waves of W games
+  seqops    W          each op of one sequence decision step at wave size W, timed alone
 """
 from __future__ import annotations
 
@@ -146,6 +147,41 @@ def main() -> None:
         sec = a.elapsed_time(b) / 1e3
         out.update(seconds=sec, games_per_s=w * waves / sec, steps=steps)
         sp.release()
+    elif args.case == "seqops":
+        from .seq import SeqDecoder
+        (w,) = d
+        dec = SeqDecoder.from_state_dict(SeqDecoder.random_state(0))
+        g = torch.Generator(device="cpu").manual_seed(0)
+        cache = dec.new_cache(2 * w)
+        cache.length.copy_(torch.randint(1, 25, (2 * w,), generator=g).to(dev))
+        ops = {}
+        for n in (w, 2 * w):
+            x = torch.randn((n, 256), generator=g).to(dev)
+            a = torch.randn((n, 256), generator=g).to(dev, torch.bfloat16)
+            f = torch.randn((n, 1024), generator=g).to(dev, torch.bfloat16)
+            L = dec.blocks[0]
+            rows = torch.arange(n, device=dev)
+            qkv = ext.linear(a, L.w_in, L.b_in)
+            q, kn, vn = (qkv[:, i * 256:(i + 1) * 256].view(n, 8, 32) for i in range(3))
+            ops[f"layernorm n={n}"] = lambda x=x, L=L: ext.layernorm(x, L.norm1_w, L.norm1_b)
+            ops[f"in_proj n={n}"] = lambda a=a, L=L: ext.linear(a, L.w_in, L.b_in)
+            ops[f"attention n={n}"] = lambda q=q, kn=kn, vn=vn, rows=rows: ext.decode_attention(
+                q, cache.k[0], cache.v[0], cache.length, rows, k_new=kn, v_new=vn, pos_clamp=49)
+            ops[f"out_proj n={n}"] = lambda a=a, x=x, L=L: ext.linear(a, L.w_out, L.b_out, residual=x, out=x)
+            ops[f"linear1 n={n}"] = lambda a=a, L=L: ext.linear(a, L.w1, L.b1, act=3)
+            ops[f"linear2 n={n}"] = lambda f=f, x=x, L=L: ext.linear(f, L.w2, L.b2, residual=x, out=x)
+        qin = torch.randn((w, 904), generator=g).to(dev, torch.bfloat16)
+        ops["query_token"] = lambda: dec.query_token(qin)
+        xr = torch.randn((w, 256), generator=g).to(dev)
+        ops["readout"] = lambda: dec.readout(xr)
+        ev = torch.randint(0, 1 << 50, (w, 9), generator=g).to(dev)
+        seats = torch.cat((torch.zeros(w), torch.ones(w))).long().to(dev)
+        cnt = torch.randint(0, 40, (w,), generator=g).to(dev)
+        ops["event_token n=2w"] = lambda: dec.event_token(ev, seats, cnt)
+        res = {}
+        for name, fn in ops.items():
+            res[name] = round(_time(fn, args.warmup, args.iters) * 1e6, 2)
+        out.update(us=res)
     elif args.case == "sample":
         (rows,) = d
         logits = torch.randn((rows, 180), device=dev)

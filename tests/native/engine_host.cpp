@@ -40,7 +40,7 @@ void cugo_host_observe(const uint8_t* rows, int64_t n, float* features, uint8_t*
     const Game g = load(rows + i * kRowBytes);
     ObsPacket pk;
     ObsMeta meta;
-    observe_game(g, pk, meta);
+    observe_game(g, pk.ref(), meta);
     for (u32 c = 0; c < kFeatures; ++c) features[i * kFeatures + c] = feature_value(pk, c);
     for (u32 a = 0; a < kActions; ++a) legal[i * kActions + a] = meta.legal.has(a) ? 1 : 0;
     player[i] = static_cast<uint8_t>(meta.player);
