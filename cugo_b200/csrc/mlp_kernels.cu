@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "../../include/cugo_b200.h"
 
@@ -269,6 +270,108 @@ __device__ __forceinline__ void add_residual_row(const uint8_t* buf, float* v) {
   __syncwarp();
 }
 
+// ---- epilogue of one tile (warps 2..5, 128 threads) ----------------------------------
+
+// Starts the tile's first residual chunk and stages its bias (fp32) in shared memory.
+__device__ __forceinline__ void epilogue_begin(const Epilogue& ep, uint8_t* stage, float* bias_s,
+                                               int epi_tid, int row0, int n0) {
+  // The first residual chunk streams in while the accumulator is computed.
+  if (ep.residual) prefetch_residual(stage, ep, row0, n0);
+  // The previous tile's readers of bias_s are past this barrier.
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (int c = epi_tid; c < BN; c += 128) {
+    const int n = n0 + c;
+    float b = 0.0f;
+    if (ep.bias && n < ep.n)
+      b = ep.bias_fp32 ? static_cast<const float*>(ep.bias)[n]
+                       : __bfloat162float(static_cast<const __nv_bfloat16*>(ep.bias)[n]);
+    bias_s[c] = b;
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Waits for the accumulator; the 128 epilogue threads agree on a timeout, so none
+// is left on a named barrier.  False (after draining the residual copies) on timeout.
+__device__ __forceinline__ bool epilogue_wait(uint64_t* acc_full, uint32_t parity) {
+  const uint32_t timed_out = mbar_wait(acc_full, parity) ? 0u : 1u;
+  uint32_t any_timed_out;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, 1, 128, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(any_timed_out)
+      : "r"(timed_out)
+      : "memory");
+  if (any_timed_out) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    return false;
+  }
+  fence_after();
+  return true;
+}
+
+// TMEM -> bias -> activation -> residual -> activation -> global for this warp's
+// 32 rows x BN columns of the tile (taddr: the warp's lane quadrant and buffer).
+__device__ __forceinline__ void epilogue_tile(const Epilogue& ep, uint32_t taddr, uint8_t* stage,
+                                              const float* bias_s, int row0, int n0) {
+  if (ep.out_fp32) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint8_t* cur = stage + ((c0 >> 5) & 1) * 4096;
+      uint32_t r[32];
+      CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
+      tmem_wait_ld();
+      if (ep.residual) {
+        // Next chunk's residual into the other buffer, then wait for this one.
+        if (c0 + 32 < BN) {
+          prefetch_residual(stage + (((c0 >> 5) + 1) & 1) * 4096, ep, row0, n0 + c0 + 32);
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+          asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncwarp();
+      }
+      if (n0 + c0 >= ep.n) continue;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
+      if (ep.residual) add_residual_row<float>(cur, v);
+      if (ep.act_after != kActNone) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = activate(v[j], ep.act_after);
+      }
+      write_chunk<float>(cur, v, ep, row0, n0 + c0);
+    }
+  } else {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 64) {
+      uint8_t* cur = stage + ((c0 >> 6) & 1) * 4096;
+      uint32_t r[64];
+      CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
+      CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0 + 32), (r + 32));
+      tmem_wait_ld();
+      if (ep.residual) {
+        // Next chunk's residual into the other buffer, then wait for this one.
+        if (c0 + 64 < BN) {
+          prefetch_residual(stage + (((c0 >> 6) + 1) & 1) * 4096, ep, row0, n0 + c0 + 64);
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+          asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncwarp();
+      }
+      float v[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
+      if (ep.residual) add_residual_row<__nv_bfloat16>(cur, v);
+      if (ep.act_after != kActNone) {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) v[j] = activate(v[j], ep.act_after);
+      }
+      if (n0 + c0 < ep.n) write_chunk<__nv_bfloat16>(cur, v, ep, row0, n0 + c0);
+    }
+  }
+}
+
 // ---- the kernel ------------------------------------------------------------------
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -390,102 +493,22 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4) ----
     const int quad = warp & 3;
     const int epi_tid = threadIdx.x - 64;  // 0..127
+    uint8_t* stage = epi_stage + quad * 8192;  // two 4 KB buffers
     int iter = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
       const int tm = t / tiles_n, tn = t - tm * tiles_n;
       const int n0 = tn * BN;
       const int buf = iter & 1;
       const uint32_t use = static_cast<uint32_t>(iter >> 1);
-      // Stage this tile's bias (the previous tile's readers are past this barrier).
-      uint8_t* stage = epi_stage + quad * 8192;  // two 4 KB buffers
       const int row0 = tm * BM + quad * 32;
-      // The first residual chunk streams in while the accumulator is computed.
-      if (ep.residual) prefetch_residual(stage, ep, row0, n0);
-      // Stage this tile's bias (the previous tile's readers are past this barrier).
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      for (int c = epi_tid; c < BN; c += 128) {
-        const int n = n0 + c;
-        float b = 0.0f;
-        if (ep.bias && n < ep.n)
-          b = ep.bias_fp32 ? static_cast<const float*>(ep.bias)[n]
-                           : __bfloat162float(static_cast<const __nv_bfloat16*>(ep.bias)[n]);
-        bias_s[c] = b;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // The 128 epilogue threads agree on a timeout, so none is left on a barrier.
-      const uint32_t timed_out = mbar_wait(&acc_full[buf], use & 1u) ? 0u : 1u;
-      uint32_t any_timed_out;
-      asm volatile(
-          "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
-          "bar.red.or.pred po, 1, 128, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
-          : "=r"(any_timed_out)
-          : "r"(timed_out)
-          : "memory");
-      if (any_timed_out) {
-        asm volatile("cp.async.wait_all;" ::: "memory");
+      epilogue_begin(ep, stage, bias_s, epi_tid, row0, n0);
+      if (!epilogue_wait(&acc_full[buf], use & 1u)) {
         failed = true;
         break;
       }
-      fence_after();
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                             static_cast<uint32_t>(buf * BN);
-      if (ep.out_fp32) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          uint8_t* cur = stage + ((c0 >> 5) & 1) * 4096;
-          uint32_t r[32];
-          CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
-          tmem_wait_ld();
-          if (ep.residual) {
-            // Next chunk's residual into the other buffer, then wait for this one.
-            if (c0 + 32 < BN) {
-              prefetch_residual(stage + (((c0 >> 5) + 1) & 1) * 4096, ep, row0, n0 + c0 + 32);
-              asm volatile("cp.async.wait_group 1;" ::: "memory");
-            } else {
-              asm volatile("cp.async.wait_group 0;" ::: "memory");
-            }
-            __syncwarp();
-          }
-          if (n0 + c0 >= ep.n) continue;
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
-          if (ep.residual) add_residual_row<float>(cur, v);
-          if (ep.act_after != kActNone) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = activate(v[j], ep.act_after);
-          }
-          write_chunk<float>(cur, v, ep, row0, n0 + c0);
-        }
-      } else {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 64) {
-          uint8_t* cur = stage + ((c0 >> 6) & 1) * 4096;
-          uint32_t r[64];
-          CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
-          CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0 + 32), (r + 32));
-          tmem_wait_ld();
-          if (ep.residual) {
-            // Next chunk's residual into the other buffer, then wait for this one.
-            if (c0 + 64 < BN) {
-              prefetch_residual(stage + (((c0 >> 6) + 1) & 1) * 4096, ep, row0, n0 + c0 + 64);
-              asm volatile("cp.async.wait_group 1;" ::: "memory");
-            } else {
-              asm volatile("cp.async.wait_group 0;" ::: "memory");
-            }
-            __syncwarp();
-          }
-          float v[64];
-#pragma unroll
-          for (int j = 0; j < 64; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
-          if (ep.residual) add_residual_row<__nv_bfloat16>(cur, v);
-          if (ep.act_after != kActNone) {
-#pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] = activate(v[j], ep.act_after);
-          }
-          if (n0 + c0 < ep.n) write_chunk<__nv_bfloat16>(cur, v, ep, row0, n0 + c0);
-        }
-      }
+      epilogue_tile(ep, tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                            static_cast<uint32_t>(buf * BN),
+                    stage, bias_s, row0, n0);
       fence_before();
       mbar_arrive(&acc_empty[buf]);
     }
@@ -497,6 +520,248 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     __syncwarp();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// ---- the CTA-pair kernel (tcgen05 cta_group::2) ------------------------------------
+//
+// Two CTAs of a cluster share one 256 x 256 output tile: CTA r loads rows
+// 128r..128r+127 of the A tile and rows 128r..128r+127 of the 256-row weight panel,
+// and one thread of CTA 0 issues M=256 N=256 K=16 MMAs that read both CTAs' shared
+// memory and accumulate each CTA's 128 rows in its own tensor memory.  Per SM
+// this halves the weight bytes moved from L2 per FLOP (32 KB per 64-deep K step
+// instead of 48 KB), which is what bounds the single-CTA kernel on the policy's
+// narrow layers.  Both CTAs' copies count towards CTA 0's "full" barrier (only
+// CTA 0 posts the expected byte count); CTA 0's MMA completion arrives on the
+// "empty" and "accumulator full" barriers of both CTAs; each CTA's epilogue
+// warps signal CTA 0's "accumulator empty" barrier once per tile.
+constexpr int P_BN_HALF = BN / 2;                    // weight rows loaded per CTA
+constexpr int P_STAGES = 6;
+constexpr int P_B_BYTES = P_BN_HALF * BK * 2;        // 16 KB
+constexpr int P_STAGE_BYTES = A_BYTES + P_B_BYTES;   // 32 KB
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ +
+                             BN * 4 /*bias*/ + 4 * 2 * 4096 /*epilogue staging*/;
+static_assert(P_SMEM_BYTES <= 232448, "fits the opt-in shared memory of one CTA");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
+  return out;
+}
+
+// Tile copy whose completion is counted on the barrier at cluster address `bar`
+// (CTA 0's), as the CTA pair's MMA requires.
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar, void* dst,
+                                                 int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// Arrives on the barrier at this offset in both CTAs once the issued MMAs complete.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_addr(bar)), "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                     const __grid_constant__ CUtensorMap map_w, const Epilogue ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* acc_full = empty + P_STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;     // [2], CTA 0's counts both CTAs' warps
+  uint64_t* drained = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
+  float* bias_s = reinterpret_cast<float*>(smem + P_STAGES * P_STAGE_BYTES + 256);
+  uint8_t* epi_stage = smem + P_STAGES * P_STAGE_BYTES + 256 + BN * 4;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1), pairs = static_cast<int>(gridDim.x >> 1);
+  const int tiles_m = (ep.m + 2 * BM - 1) / (2 * BM);
+  const int tiles_n = (ep.n + BN - 1) / BN;
+  const int tiles = tiles_m * tiles_n;
+  const int k_tiles = (ep.k + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // 4 epilogue warps x 2 CTAs (used in CTA 0)
+    }
+    mbar_init(drained, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // both CTAs allocate together, same warp, same holder offset
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_holder)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA signal
+  fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  bool failed = false;
+  __shared__ int any_failed;
+  if (threadIdx.x == 0) any_failed = 0;
+  __syncthreads();
+
+  if (warp == 0) {
+    // ---- TMA producer (both CTAs) ----
+    if (lane == 0) {
+      const uint32_t full0 = peer_addr(full, 0);  // CTA 0's full[0]
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = pair; t < tiles && !failed; t += pairs) {
+        const int tm = t / tiles_n, tn = t - tm * tiles_n;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u)) {
+            failed = true;
+            break;
+          }
+          uint8_t* sa = smem + stage * P_STAGE_BYTES;
+          const uint32_t bar = full0 + static_cast<uint32_t>(stage * 8);
+          if (leader) mbar_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          tma_load_2d_pair(&map_a, bar, sa, kt * BK, tm * 2 * BM + static_cast<int>(rank) * BM);
+          tma_load_2d_pair(&map_w, bar, sa + A_BYTES, kt * BK,
+                           tn * BN + static_cast<int>(rank) * P_BN_HALF);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer (CTA 0 only) ----
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = instr_desc(2 * BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int iter = 0;
+      for (int t = pair; t < tiles && !failed; t += pairs, ++iter) {
+        const int buf = iter & 1;
+        const uint32_t use = static_cast<uint32_t>(iter >> 1);
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u)) {
+          failed = true;
+          break;
+        }
+        fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase)) {
+            failed = true;
+            break;
+          }
+          fence_after();
+          const uint32_t a_addr = smem_addr(smem + stage * P_STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            mma_bf16_pair(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
+                          (kt > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit_pair(&empty[stage]);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (failed) break;
+        mma_commit_pair(&acc_full[buf]);
+      }
+      // All issued MMAs complete before the accumulators are released.
+      mma_commit_pair_local(drained);
+      mbar_wait(drained, 0);
+    }
+  } else {
+    // ---- epilogue (both CTAs): warps 2..5 own TMEM lane quadrants (warp % 4) ----
+    const int quad = warp & 3;
+    const int epi_tid = threadIdx.x - 64;
+    uint8_t* stage = epi_stage + quad * 8192;
+    int iter = 0;
+    for (int t = pair; t < tiles; t += pairs, ++iter) {
+      const int tm = t / tiles_n, tn = t - tm * tiles_n;
+      const int n0 = tn * BN;
+      const int buf = iter & 1;
+      const uint32_t use = static_cast<uint32_t>(iter >> 1);
+      const int row0 = tm * 2 * BM + static_cast<int>(rank) * BM + quad * 32;
+      epilogue_begin(ep, stage, bias_s, epi_tid, row0, n0);
+      if (!epilogue_wait(&acc_full[buf], use & 1u)) {
+        failed = true;
+        break;
+      }
+      epilogue_tile(ep, tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                            static_cast<uint32_t>(buf * BN),
+                    stage, bias_s, row0, n0);
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(peer_addr(&acc_empty[buf], 0));
+    }
+  }
+  if (failed) {
+    any_failed = 1;
+    if (ep.error) atomicExch(ep.error, 1);
+  }
+  fence_before();
+  __syncthreads();
+  if (any_failed) {
+    // Let copies and MMAs still in flight land before the pair leaves (bounded).
+    const uint64_t t0 = now_ns();
+    while (now_ns() - t0 < 100'000ull) {
+    }
+  }
+  cluster_sync_all();  // no cross-CTA signal is outstanding past this point
+  fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(TMEM_COLS));
   }
 }
@@ -536,6 +801,35 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
+// CTA pairs of gemm_pair_kernel that fit on the device at once (clusters are placed
+// within a GPC, so this can be below half the SM count).
+int max_pairs(int dev) {
+  static int cache[64] = {};
+  if (!cache[dev]) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sm_count() & ~1), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// CUGO_B200_GEMM_SINGLE=1 selects the single-CTA kernel for every shape.
+bool pair_kernel_enabled() {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* v = getenv("CUGO_B200_GEMM_SINGLE");
+    enabled = (v && v[0] == '1') ? 0 : 1;
+  }
+  return enabled == 1;
+}
+
 }  // namespace
 
 extern "C" {
@@ -557,23 +851,37 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
       (ldo * esz) % 16 || (residual && (!al(residual, 16) || (ldr * esz) % 16)) ||
       (bias && !al(bias, bias_fp32 ? 4 : 2)))
     return CUGO_B200_ERR_ALIGN;
-  CUtensorMap ma, mw;
-  if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BN)) return CUGO_B200_ERR_LAUNCH;
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr_set[64] = {};
   if (dev < 0 || dev >= 64) return CUGO_B200_ERR_LAUNCH;
   if (!attr_set[dev]) {
     if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             P_SMEM_BYTES) != cudaSuccess)
       return CUGO_B200_ERR_LAUNCH;
     attr_set[dev] = true;
   }
   Epilogue ep{bias, residual, ldr, out, ldo, out_fp32 ? 1 : 0, bias_fp32 ? 1 : 0, act, act_after,
               static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), error};
-  const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
-  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, ep);
+  CUtensorMap ma, mw;
+  // The pair kernel halves the weight bytes each SM streams per FLOP, which pays
+  // when the K loop is long (measured: 262144x2048x2048 1,425 vs 1,317 TFLOP/s);
+  // with K <= 720 the epilogue bounds both kernels and the single one is faster.
+  const bool pair = m > BM && k >= 1024 && pair_kernel_enabled();
+  if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, pair ? P_BN_HALF : BN))
+    return CUGO_B200_ERR_LAUNCH;
+  if (pair) {
+    // 256 x 256 tiles, one CTA pair per tile, persistent over the co-resident pairs.
+    const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
+    const int64_t pairs = tiles < max_pairs(dev) ? tiles : max_pairs(dev);
+    gemm_pair_kernel<<<static_cast<unsigned>(2 * pairs), THREADS, P_SMEM_BYTES, stream>>>(ma, mw, ep);
+  } else {
+    const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+    const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+    gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, ep);
+  }
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }
 

@@ -64,16 +64,18 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // ---- decode attention -------------------------------------------------------------
 //
-// One warp per (query i, head h).  Lane t owns slots t, t+32, ...: it loads the
-// slot's 64-byte key and value rows (four 16-byte loads each; a warp's loads cover
-// a contiguous 2 KB block of the cache), scores the slot in fp32 and keeps its own
-// running max, sum and weighted value sum (online softmax).  The 32 partial states
-// are then merged: a warp max, a rescale, a warp sum of the denominators and a
-// butterfly reduce-scatter of the 32-wide value sums (31 shuffles) after which
-// lane d holds output dimension d.  With an append, the lane of slot pos[i] uses
-// the new key/value from registers and writes them to the cache; the cache rows
-// of different queries must then be distinct (as in cached_step).
-__global__ void __launch_bounds__(256) decode_attention_kernel(
+// One warp per (query i, head h).  Lanes 2j and 2j+1 own slot j of each group of 16
+// slots, each for one 16-dimension half of the head: a lane loads its 32-byte halves
+// of the slot's key and value rows, the pair adds its partial dot products with one
+// shuffle, and every lane keeps a running max, sum and weighted value sum for its
+// half (online softmax).  Two groups (32 slots) are loaded before either is used.
+// The 16 slot states are then merged: a warp max, a rescale, a warp sum of the
+// denominators and a butterfly reduce-scatter of the 16-wide value sums within each
+// half (15 shuffles), after which lane l holds dimension 16 (l & 1) + (l >> 1).
+// With an append, the lanes of slot pos[i] use the new key/value from registers
+// and write them to the cache; the cache rows of different queries must then be
+// distinct (as in cached_step).
+__global__ void __launch_bounds__(256, 3) decode_attention_kernel(
     const __nv_bfloat16* __restrict__ q, i64 ldq, const __nv_bfloat16* __restrict__ k_new,
     const __nv_bfloat16* __restrict__ v_new, i64 ldn, __nv_bfloat16* keys, __nv_bfloat16* values,
     i64 n_rows, int heads, int slots, const i64* __restrict__ pos, i64 pos_clamp,
@@ -81,7 +83,7 @@ __global__ void __launch_bounds__(256) decode_attention_kernel(
     int32_t* error) {
   const i64 gw = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (gw >= n * heads) return;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, half = lane & 1, sl = lane >> 1;
   const i64 i = gw / heads;
   const int h = static_cast<int>(gw - i * heads);
   const i64 r = rows ? __ldg(rows + i) : i;
@@ -98,90 +100,99 @@ __global__ void __launch_bounds__(256) decode_attention_kernel(
     if (lane == 0 && error) atomicExch(error, 1);
     return;
   }
-  float qf[kDh];
+  float qf[16];
   {
-    const uint4* qp = reinterpret_cast<const uint4*>(q + i * ldq + h * kDh);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) bf16x8(__ldg(qp + c), qf + 8 * c);
+    const uint4* qp = reinterpret_cast<const uint4*>(q + i * ldq + h * kDh + half * 16);
+    bf16x8(__ldg(qp), qf);
+    bf16x8(__ldg(qp + 1), qf + 8);
   }
   const i64 base = (r * heads + h) * static_cast<i64>(slots) * kDh;
-  uint4* kc = reinterpret_cast<uint4*>(keys + base);
-  uint4* vc = reinterpret_cast<uint4*>(values + base);
-  float m = -INFINITY, l = 0.0f, acc[kDh];
-#pragma unroll
-  for (int d = 0; d < kDh; ++d) acc[d] = 0.0f;
+  uint4* kc = reinterpret_cast<uint4*>(keys + base) + 2 * half;    // 4 uint4 per slot
+  uint4* vc = reinterpret_cast<uint4*>(values + base) + 2 * half;
   const int last = static_cast<int>(p);
+  float m = -INFINITY, l = 0.0f, acc[16];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) acc[d] = 0.0f;
   for (int t0 = 0; t0 <= last; t0 += 32) {
-    const int t = t0 + lane;
-    if (t > last) break;
-    uint4 kr[4], vr[4];
-    if (k_new && t == last) {
-      const uint4* kn = reinterpret_cast<const uint4*>(k_new + i * ldn + h * kDh);
-      const uint4* vn = reinterpret_cast<const uint4*>(v_new + i * ldn + h * kDh);
+    uint4 kr[2][2], vr[2][2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        kr[c] = __ldg(kn + c);
-        vr[c] = __ldg(vn + c);
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        kc[4 * t + c] = kr[c];
-        vc[4 * t + c] = vr[c];
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        kr[c] = __ldg(kc + 4 * t + c);
-        vr[c] = __ldg(vc + 4 * t + c);
+    for (int u = 0; u < 2; ++u) {
+      const int t = t0 + 16 * u + sl;
+      if (t > last) continue;
+      if (k_new && t == last) {
+        const uint4* kn = reinterpret_cast<const uint4*>(k_new + i * ldn + h * kDh + half * 16);
+        const uint4* vn = reinterpret_cast<const uint4*>(v_new + i * ldn + h * kDh + half * 16);
+        kr[u][0] = __ldg(kn);
+        kr[u][1] = __ldg(kn + 1);
+        vr[u][0] = __ldg(vn);
+        vr[u][1] = __ldg(vn + 1);
+        kc[4 * t] = kr[u][0];
+        kc[4 * t + 1] = kr[u][1];
+        vc[4 * t] = vr[u][0];
+        vc[4 * t + 1] = vr[u][1];
+      } else {
+        kr[u][0] = __ldg(kc + 4 * t);
+        kr[u][1] = __ldg(kc + 4 * t + 1);
+        vr[u][0] = __ldg(vc + 4 * t);
+        vr[u][1] = __ldg(vc + 4 * t + 1);
       }
     }
-    float s = 0.0f;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float kf[8];
-      bf16x8(kr[c], kf);
+    for (int u = 0; u < 2; ++u) {
+      const int t = t0 + 16 * u + sl;
+      float s = 0.0f;
+      if (t <= last) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s = fmaf(kf[e], qf[8 * c + e], s);
-    }
-    s *= scale;
-    if (s > m) {
-      const float c = expf(m - s);
-      l *= c;
+        for (int c = 0; c < 2; ++c) {
+          float kf[8];
+          bf16x8(kr[u][c], kf);
 #pragma unroll
-      for (int d = 0; d < kDh; ++d) acc[d] *= c;
-      m = s;
-    }
-    const float w = expf(s - m);
-    l += w;
+          for (int e = 0; e < 8; ++e) s = fmaf(kf[e], qf[8 * c + e], s);
+        }
+      }
+      s += __shfl_xor_sync(kFull, s, 1);  // both halves of the slot
+      if (t <= last) {
+        s *= scale;
+        if (s > m) {
+          const float c = expf(m - s);
+          l *= c;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float vf[8];
-      bf16x8(vr[c], vf);
+          for (int d = 0; d < 16; ++d) acc[d] *= c;
+          m = s;
+        }
+        const float w = expf(s - m);
+        l += w;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[8 * c + e] = fmaf(w, vf[e], acc[8 * c + e]);
+        for (int c = 0; c < 2; ++c) {
+          float vf[8];
+          bf16x8(vr[u][c], vf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[8 * c + e] = fmaf(w, vf[e], acc[8 * c + e]);
+        }
+      }
     }
   }
-  // Merge the lanes' partial softmax states.
+  // Merge the slot states (both lanes of a slot hold the same m and l).
   const float mx = warp_max(m);
   const float f = expf(m - mx);  // 0 for a lane without slots (m = -inf)
-  const float denom = warp_sum(l * f);
+  const float denom = warp_sum(half == 0 ? l * f : 0.0f);
 #pragma unroll
-  for (int d = 0; d < kDh; ++d) acc[d] *= f;
-  // Butterfly reduce-scatter: after the level of width w the lane's acc[0..w-1]
-  // hold dimensions (lane & ~(w-1)) .. +w-1, summed over the lanes whose ids
-  // differ from its own only in bits >= w; at the end acc[0] is dimension
-  // `lane` summed over all 32 lanes.
+  for (int d = 0; d < 16; ++d) acc[d] *= f;
+  // Butterfly reduce-scatter over lane bits 4..1 (same half): after the level of
+  // width w the lane's acc[0..w-1] hold its half's dimensions
+  // ((lane >> 1) & ~(w-1)) .. +w-1 summed over the lanes that differ from it only
+  // in bits >= 2w of the lane id.
 #pragma unroll
-  for (int w = 16; w >= 1; w >>= 1) {
-    const bool upper = (lane & w) != 0;
+  for (int w = 8; w >= 1; w >>= 1) {
+    const bool upper = (lane & (2 * w)) != 0;
 #pragma unroll
     for (int j = 0; j < w; ++j) {
       const float send = upper ? acc[j] : acc[j + w];
       const float keep = upper ? acc[j + w] : acc[j];
-      acc[j] = keep + __shfl_xor_sync(kFull, send, w);
+      acc[j] = keep + __shfl_xor_sync(kFull, send, 2 * w);
     }
   }
-  o[lane] = __float2bfloat16_rn(acc[0] / denom);
+  o[half * 16 + sl] = __float2bfloat16_rn(acc[0] / denom);
 }
 
 // ---- LayerNorm ----------------------------------------------------------------------
