@@ -17,10 +17,11 @@
 //                thread issues tcgen05.mma (M=128, N=256, K=16) per 16-wide K
 //                slice, committing each stage back to the producer and each
 //                finished tile to the epilogue;
-//   warps 2..5 : epilogue — tcgen05.ld of their 32 TMEM lanes, bias, activation,
-//                residual; each 32-row x 128-byte chunk is transposed through a
-//                swizzled shared buffer so that every warp store writes whole
-//                128-byte row segments.  A tile's epilogue overlaps the next
+//   warps 2..9 : epilogue — two warps per TMEM lane quadrant, each taking half of
+//                the tile's 256 columns: tcgen05.ld of their 32 TMEM lanes, bias,
+//                activation, residual; each 32-row x 64-byte chunk is transposed
+//                through a swizzled shared buffer so that every warp store writes
+//                whole 64-byte row segments.  A tile's epilogue overlaps the next
 //                tile's MMAs through the second accumulator.
 // Every mbarrier wait is bounded (about 2 s of %globaltimer); a wait that runs
 // out sets *error and the kernel drains and returns instead of hanging.
@@ -39,10 +40,14 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
 constexpr int B_BYTES = BN * BK * 2;            // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;                    // two per TMEM lane quadrant
+constexpr int EPI_THREADS = 32 * EPI_WARPS;
+constexpr int THREADS = 64 + EPI_THREADS;
+constexpr int EPI_BUF = 2048;                   // one 32-row x 64-byte chunk
+constexpr int EPI_STAGE_BYTES = EPI_WARPS * 2 * EPI_BUF;  // double-buffered per warp
 constexpr uint32_t TMEM_COLS = 2 * BN;          // two accumulators
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ +
-                           BN * 4 /*bias*/ + 4 * 2 * 4096 /*epilogue staging, 2 per warp*/;
+                           BN * 4 /*bias*/ + EPI_STAGE_BYTES;
 constexpr uint64_t kWaitNs = 2'000'000'000ull;
 
 enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActGelu = 3 };
@@ -118,6 +123,25 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Tile store from shared memory (the async proxy reads the staging buffer).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(x), "r"(y)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until at most N of this thread's tile stores still read shared memory.
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -181,54 +205,54 @@ __device__ __forceinline__ float activate(float v, int act) {
   return v;
 }
 
+#define CB_TMEM_LD16(taddr, r)                                                                  \
+  asm volatile(                                                                                 \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"  \
+      "%14,%15}, [%16];"                                                                        \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),    \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),             \
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])                                                   \
+      : "r"(taddr))
+
 // ---- epilogue stores through shared memory ----------------------------------------
 //
-// A thread holds one output row of the chunk (TMEM lane = row).  Rows go to a
-// per-warp 32 x 128-byte buffer (16-byte pieces XOR-swizzled by row, so the
-// row-per-thread writes and the row-major reads are both bank-conflict free),
-// then the warp stores 4 whole 128-byte row segments per instruction.  The
-// residual comes in the same way in reverse.
+// A thread holds one output row of the chunk (TMEM lane = row): 64 bytes, i.e. 32
+// bf16 or 16 fp32 columns.  Rows go to a per-warp 32 x 64-byte buffer whose 16-byte
+// pieces are XOR-swizzled by row pair — the layout of a TMA tile with 64-byte
+// swizzle, so the row-per-thread writes are bank-conflict free and one TMA store
+// writes the chunk.  The residual comes in through the same layout (cp.async).
 
 __device__ __forceinline__ uint32_t swz(int row, int piece) {
-  return static_cast<uint32_t>(row * 128 + ((piece ^ (row & 7)) << 4));
+  return static_cast<uint32_t>(row * 64 + ((piece ^ ((row >> 1) & 3)) << 4));
 }
 
+// Writes this lane's row of the chunk into the staging buffer and has lane 0 store
+// the 32 x 64-byte chunk with one TMA tile store (rows or columns outside the
+// matrix are clipped by the tensor map).  The buffer's previous store has been
+// waited for by the caller.
 template <typename T>
-__device__ __forceinline__ void write_chunk(uint8_t* stage, const float* v, const Epilogue& ep,
+__device__ __forceinline__ void store_chunk(uint8_t* stage, const float* v, const CUtensorMap* map_out,
                                             int row0, int col0) {
-  constexpr int E = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte piece
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int p = 0; p < 8; ++p) {
+  for (int p = 0; p < 4; ++p) {
     uint4 raw;
-    T* h = reinterpret_cast<T*>(&raw);
+    if constexpr (sizeof(T) == 2) {
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      if constexpr (sizeof(T) == 2) h[e] = __float2bfloat16_rn(v[p * E + e]);
-      else h[e] = v[p * E + e];
+      for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[p * 8 + 2 * e], v[p * 8 + 2 * e + 1]);
+    } else {
+      raw = make_uint4(__float_as_uint(v[p * 4]), __float_as_uint(v[p * 4 + 1]),
+                       __float_as_uint(v[p * 4 + 2]), __float_as_uint(v[p * 4 + 3]));
     }
     *reinterpret_cast<uint4*>(stage + swz(lane, p)) = raw;
   }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the TMA unit
   __syncwarp();
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = 4 * i + (lane >> 3), p = lane & 7;
-    const int grow = row0 + r, gcol = col0 + p * E;
-    if (grow < ep.m && gcol < ep.n) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(stage + swz(r, p));
-      T* dst = reinterpret_cast<T*>(ep.out) + static_cast<int64_t>(grow) * ep.ldo + gcol;
-      if (gcol + E <= ep.n) {
-        *reinterpret_cast<uint4*>(dst) = raw;
-      } else {
-        const T* h = reinterpret_cast<const T*>(&raw);
-        for (int e = 0; gcol + e < ep.n; ++e) dst[e] = h[e];
-      }
-    }
-  }
-  __syncwarp();
+  if (lane == 0) tma_store_2d(map_out, stage, col0, row0);
 }
 
-// Starts copying the residual of a 32-row x 128-byte chunk (64 bf16 or 32 fp32
+// Starts copying the residual of a 32-row x 64-byte chunk (32 bf16 or 16 fp32
 // columns) into a staging buffer (cp.async, zero-filled outside the matrix); one
 // commit group per chunk.
 __device__ __forceinline__ void prefetch_residual(uint8_t* buf, const Epilogue& ep, int row0,
@@ -236,8 +260,8 @@ __device__ __forceinline__ void prefetch_residual(uint8_t* buf, const Epilogue& 
   const int lane = threadIdx.x & 31;
   const int esz = ep.out_fp32 ? 4 : 2, per = 16 / esz;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = 4 * i + (lane >> 3), p = lane & 7;
+  for (int i = 0; i < 4; ++i) {
+    const int r = 8 * i + (lane >> 2), p = lane & 3;
     const int grow = row0 + r, gcol = col0 + p * per;
     int bytes = 0;
     const uint8_t* src = static_cast<const uint8_t*>(ep.residual);
@@ -258,28 +282,44 @@ __device__ __forceinline__ void add_residual_row(const uint8_t* buf, float* v) {
   constexpr int E = 16 / static_cast<int>(sizeof(T));
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int p = 0; p < 8; ++p) {
+  for (int p = 0; p < 4; ++p) {
     const uint4 raw = *reinterpret_cast<const uint4*>(buf + swz(lane, p));
-    const T* h = reinterpret_cast<const T*>(&raw);
+    if constexpr (sizeof(T) == 2) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      if constexpr (sizeof(T) == 2) v[p * E + e] += __bfloat162float(h[e]);
-      else v[p * E + e] += h[e];
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        v[p * 8 + 2 * e] += f.x;
+        v[p * 8 + 2 * e + 1] += f.y;
+      }
+    } else {
+      const float* h = reinterpret_cast<const float*>(&raw);
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[p * E + e] += h[e];
     }
   }
   __syncwarp();
 }
 
-// ---- epilogue of one tile (warps 2..5, 128 threads) ----------------------------------
+// ---- epilogue of one tile (warps 2..9, 256 threads) ----------------------------------
 
-// Starts the tile's first residual chunk and stages its bias (fp32) in shared memory.
+// Epilogue warp w owns TMEM lanes 32 (w % 4) .. +31 (the hardware's lane quadrant
+// for warp w) and columns 128 ((w - 2) / 4) .. +127 of the tile.
+__device__ __forceinline__ int epi_quad(int warp) { return warp & 3; }
+__device__ __forceinline__ int epi_col0(int warp) { return ((warp - 2) >> 2) * (BN / 2); }
+
+// Starts the warp's first residual chunk and stages the tile's bias (fp32) in
+// shared memory.
 __device__ __forceinline__ void epilogue_begin(const Epilogue& ep, uint8_t* stage, float* bias_s,
-                                               int epi_tid, int row0, int n0) {
-  // The first residual chunk streams in while the accumulator is computed.
-  if (ep.residual) prefetch_residual(stage, ep, row0, n0);
+                                               int epi_tid, int row0, int n0, int cbase) {
+  // The previous tile's stores have read the staging buffers; then the first
+  // residual chunk streams in while the accumulator is computed.
+  if ((threadIdx.x & 31) == 0) tma_store_wait_read<0>();
+  __syncwarp();
+  if (ep.residual) prefetch_residual(stage, ep, row0, n0 + cbase);
   // The previous tile's readers of bias_s are past this barrier.
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  for (int c = epi_tid; c < BN; c += 128) {
+  asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory");
+  for (int c = epi_tid; c < BN; c += EPI_THREADS) {
     const int n = n0 + c;
     float b = 0.0f;
     if (ep.bias && n < ep.n)
@@ -287,19 +327,19 @@ __device__ __forceinline__ void epilogue_begin(const Epilogue& ep, uint8_t* stag
                        : __bfloat162float(static_cast<const __nv_bfloat16*>(ep.bias)[n]);
     bias_s[c] = b;
   }
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory");
 }
 
-// Waits for the accumulator; the 128 epilogue threads agree on a timeout, so none
-// is left on a named barrier.  False (after draining the residual copies) on timeout.
+// Waits for the accumulator; the epilogue threads agree on a timeout, so none is
+// left on a named barrier.  False (after draining the residual copies) on timeout.
 __device__ __forceinline__ bool epilogue_wait(uint64_t* acc_full, uint32_t parity) {
   const uint32_t timed_out = mbar_wait(acc_full, parity) ? 0u : 1u;
   uint32_t any_timed_out;
   asm volatile(
       "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
-      "bar.red.or.pred po, 1, 128, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+      "bar.red.or.pred po, 1, %2, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
       : "=r"(any_timed_out)
-      : "r"(timed_out)
+      : "r"(timed_out), "n"(EPI_THREADS)
       : "memory");
   if (any_timed_out) {
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -310,84 +350,77 @@ __device__ __forceinline__ bool epilogue_wait(uint64_t* acc_full, uint32_t parit
 }
 
 // TMEM -> bias -> activation -> residual -> activation -> global for this warp's
-// 32 rows x BN columns of the tile (taddr: the warp's lane quadrant and buffer).
-__device__ __forceinline__ void epilogue_tile(const Epilogue& ep, uint32_t taddr, uint8_t* stage,
-                                              const float* bias_s, int row0, int n0) {
-  if (ep.out_fp32) {
+// 32 rows x 128 columns (tile columns cbase .. cbase + 127; taddr: the warp's lane
+// quadrant and accumulator buffer), in 64-byte-row chunks of CW columns.
+template <typename T>
+__device__ __forceinline__ void epilogue_cols(const Epilogue& ep, const CUtensorMap* map_out,
+                                              uint32_t taddr, uint8_t* stage, const float* bias_s,
+                                              int row0, int n0, int cbase) {
+  constexpr int CW = 64 / static_cast<int>(sizeof(T));
+  constexpr int CHUNKS = (BN / 2) / CW;
+  const int lane = threadIdx.x & 31;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint8_t* cur = stage + ((c0 >> 5) & 1) * 4096;
-      uint32_t r[32];
+  for (int c = 0; c < CHUNKS; ++c) {
+    const int c0 = cbase + c * CW;
+    uint8_t* cur = stage + (c & 1) * EPI_BUF;
+    uint32_t r[CW];
+    if constexpr (CW == 32) {
       CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
-      tmem_wait_ld();
-      if (ep.residual) {
-        // Next chunk's residual into the other buffer, then wait for this one.
-        if (c0 + 32 < BN) {
-          prefetch_residual(stage + (((c0 >> 5) + 1) & 1) * 4096, ep, row0, n0 + c0 + 32);
-          asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-          asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
-        __syncwarp();
-      }
-      if (n0 + c0 >= ep.n) continue;
-      float v[32];
+    } else {
+      CB_TMEM_LD16(taddr + static_cast<uint32_t>(c0), r);
+    }
+    tmem_wait_ld();
+    if (ep.residual) {
+      // This chunk's residual has landed (it was started one chunk earlier).
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncwarp();
+    }
+    const bool live = n0 + c0 < ep.n;
+    float v[CW];
+    if (live) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
-      if (ep.residual) add_residual_row<float>(cur, v);
+      for (int j = 0; j < CW; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
+      if (ep.residual) add_residual_row<T>(cur, v);  // ends with __syncwarp
       if (ep.act_after != kActNone) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = activate(v[j], ep.act_after);
+        for (int j = 0; j < CW; ++j) v[j] = activate(v[j], ep.act_after);
       }
-      write_chunk<float>(cur, v, ep, row0, n0 + c0);
     }
-  } else {
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 64) {
-      uint8_t* cur = stage + ((c0 >> 6) & 1) * 4096;
-      uint32_t r[64];
-      CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0), r);
-      CB_TMEM_LD32(taddr + static_cast<uint32_t>(c0 + 32), (r + 32));
-      tmem_wait_ld();
-      if (ep.residual) {
-        // Next chunk's residual into the other buffer, then wait for this one.
-        if (c0 + 64 < BN) {
-          prefetch_residual(stage + (((c0 >> 6) + 1) & 1) * 4096, ep, row0, n0 + c0 + 64);
-          asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-          asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
-        __syncwarp();
-      }
-      float v[64];
-#pragma unroll
-      for (int j = 0; j < 64; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
-      if (ep.residual) add_residual_row<__nv_bfloat16>(cur, v);
-      if (ep.act_after != kActNone) {
-#pragma unroll
-        for (int j = 0; j < 64; ++j) v[j] = activate(v[j], ep.act_after);
-      }
-      if (n0 + c0 < ep.n) write_chunk<__nv_bfloat16>(cur, v, ep, row0, n0 + c0);
-    }
+    // The previous chunk's store must have read the other buffer before the next
+    // residual lands there (and this buffer's store, two chunks back, long before).
+    if (lane == 0) tma_store_wait_read<0>();
+    __syncwarp();
+    if (ep.residual && c + 1 < CHUNKS)
+      prefetch_residual(stage + ((c + 1) & 1) * EPI_BUF, ep, row0, n0 + c0 + CW);
+    if (live) store_chunk<T>(cur, v, map_out, row0, n0 + c0);
   }
+}
+
+__device__ __forceinline__ void epilogue_tile(const Epilogue& ep, const CUtensorMap* map_out,
+                                              uint32_t taddr, uint8_t* stage, const float* bias_s,
+                                              int row0, int n0, int cbase) {
+  if (ep.out_fp32) epilogue_cols<float>(ep, map_out, taddr, stage, bias_s, row0, n0, cbase);
+  else epilogue_cols<__nv_bfloat16>(ep, map_out, taddr, stage, bias_s, row0, n0, cbase);
 }
 
 // ---- the kernel ------------------------------------------------------------------
 
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-                const Epilogue ep) {
+                const __grid_constant__ CUtensorMap map_out, const Epilogue ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // Layout: operand stages | epilogue staging (1 KB aligned, as the 64-byte TMA
+  // swizzle of the stores requires) | barriers | bias.
+  uint8_t* epi_stage = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint64_t* drained = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
-  float* bias_s = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);
-  uint8_t* epi_stage = smem + STAGES * STAGE_BYTES + 256 + BN * 4;  // 4 warps x 2 x 4 KB
+  float* bias_s = reinterpret_cast<float*>(epi_stage + EPI_STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -403,7 +436,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], EPI_WARPS);
     }
     mbar_init(drained, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -490,10 +523,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_wait(drained, 0);
     }
   } else {
-    // ---- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4) ----
-    const int quad = warp & 3;
-    const int epi_tid = threadIdx.x - 64;  // 0..127
-    uint8_t* stage = epi_stage + quad * 8192;  // two 4 KB buffers
+    // ---- epilogue: warps 2..9 (two per TMEM lane quadrant) ----
+    const int quad = epi_quad(warp);
+    const int cbase = epi_col0(warp);
+    const int epi_tid = threadIdx.x - 64;  // 0..255
+    uint8_t* stage = epi_stage + (warp - 2) * 2 * EPI_BUF;
     int iter = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
       const int tm = t / tiles_n, tn = t - tm * tiles_n;
@@ -501,17 +535,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int buf = iter & 1;
       const uint32_t use = static_cast<uint32_t>(iter >> 1);
       const int row0 = tm * BM + quad * 32;
-      epilogue_begin(ep, stage, bias_s, epi_tid, row0, n0);
+      epilogue_begin(ep, stage, bias_s, epi_tid, row0, n0, cbase);
       if (!epilogue_wait(&acc_full[buf], use & 1u)) {
         failed = true;
         break;
       }
-      epilogue_tile(ep, tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                            static_cast<uint32_t>(buf * BN),
-                    stage, bias_s, row0, n0);
+      epilogue_tile(ep, &map_out,
+                    tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                        static_cast<uint32_t>(buf * BN),
+                    stage, bias_s, row0, n0, cbase);
       fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) tma_store_wait_all();  // stores complete before the CTA leaves
   }
   if (failed && ep.error) atomicExch(ep.error, 1);
   fence_before();
@@ -541,7 +578,7 @@ constexpr int P_STAGES = 6;
 constexpr int P_B_BYTES = P_BN_HALF * BK * 2;        // 16 KB
 constexpr int P_STAGE_BYTES = A_BYTES + P_B_BYTES;   // 32 KB
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ +
-                             BN * 4 /*bias*/ + 4 * 2 * 4096 /*epilogue staging*/;
+                             BN * 4 /*bias*/ + EPI_STAGE_BYTES;
 static_assert(P_SMEM_BYTES <= 232448, "fits the opt-in shared memory of one CTA");
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -601,18 +638,19 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
-                     const __grid_constant__ CUtensorMap map_w, const Epilogue ep) {
+                     const __grid_constant__ CUtensorMap map_w,
+                     const __grid_constant__ CUtensorMap map_out, const Epilogue ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint8_t* epi_stage = smem + P_STAGES * P_STAGE_BYTES;  // 1 KB aligned (see gemm_kernel)
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_STAGE_BYTES);
   uint64_t* empty = full + P_STAGES;
   uint64_t* acc_full = empty + P_STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;     // [2], CTA 0's counts both CTAs' warps
   uint64_t* drained = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
-  float* bias_s = reinterpret_cast<float*>(smem + P_STAGES * P_STAGE_BYTES + 256);
-  uint8_t* epi_stage = smem + P_STAGES * P_STAGE_BYTES + 256 + BN * 4;
+  float* bias_s = reinterpret_cast<float*>(epi_stage + EPI_STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -631,7 +669,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);  // 4 epilogue warps x 2 CTAs (used in CTA 0)
+      mbar_init(&acc_empty[b], 2 * EPI_WARPS);  // both CTAs' epilogue warps (used in CTA 0)
     }
     mbar_init(drained, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -721,10 +759,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_wait(drained, 0);
     }
   } else {
-    // ---- epilogue (both CTAs): warps 2..5 own TMEM lane quadrants (warp % 4) ----
-    const int quad = warp & 3;
+    // ---- epilogue (both CTAs): warps 2..9 (two per TMEM lane quadrant) ----
+    const int quad = epi_quad(warp);
+    const int cbase = epi_col0(warp);
     const int epi_tid = threadIdx.x - 64;
-    uint8_t* stage = epi_stage + quad * 8192;
+    uint8_t* stage = epi_stage + (warp - 2) * 2 * EPI_BUF;
     int iter = 0;
     for (int t = pair; t < tiles; t += pairs, ++iter) {
       const int tm = t / tiles_n, tn = t - tm * tiles_n;
@@ -732,18 +771,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int buf = iter & 1;
       const uint32_t use = static_cast<uint32_t>(iter >> 1);
       const int row0 = tm * 2 * BM + static_cast<int>(rank) * BM + quad * 32;
-      epilogue_begin(ep, stage, bias_s, epi_tid, row0, n0);
+      epilogue_begin(ep, stage, bias_s, epi_tid, row0, n0, cbase);
       if (!epilogue_wait(&acc_full[buf], use & 1u)) {
         failed = true;
         break;
       }
-      epilogue_tile(ep, tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                            static_cast<uint32_t>(buf * BN),
-                    stage, bias_s, row0, n0);
+      epilogue_tile(ep, &map_out,
+                    tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                        static_cast<uint32_t>(buf * BN),
+                    stage, bias_s, row0, n0, cbase);
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(peer_addr(&acc_empty[buf], 0));
     }
+    if (lane == 0) tma_store_wait_all();  // stores complete before the CTA leaves
   }
   if (failed) {
     any_failed = 1;
@@ -780,7 +821,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map over [rows, cols] (row stride ld elements), box box_rows x 64.
+// 2-D bf16 tensor map over [rows, cols] (row stride ld elements), box box_rows x 64
+// with 128-byte swizzle (the MMA operand layout).
 bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
               uint32_t box_rows) {
   auto fn = encode_fn();
@@ -792,6 +834,21 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor map of the output [rows, cols] (bf16 or fp32, row stride ld elements) for
+// the epilogue's stores: box 32 rows x 64 bytes with 64-byte swizzle.
+bool make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int64_t ld, bool fp32) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const int esz = fp32 ? 4 : 2;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * esz)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(64 / esz), 32};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base,
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int sm_count() {
@@ -865,7 +922,8 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
   }
   Epilogue ep{bias, residual, ldr, out, ldo, out_fp32 ? 1 : 0, bias_fp32 ? 1 : 0, act, act_after,
               static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), error};
-  CUtensorMap ma, mw;
+  CUtensorMap ma, mw, mo;
+  if (!make_out_map(&mo, out, m, n, ldo, out_fp32 != 0)) return CUGO_B200_ERR_LAUNCH;
   // The pair kernel halves the weight bytes each SM streams per FLOP, which pays
   // when the K loop is long (measured: 262144x2048x2048 1,425 vs 1,317 TFLOP/s);
   // with K <= 720 the epilogue bounds both kernels and the single one is faster.
@@ -876,11 +934,12 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
     // 256 x 256 tiles, one CTA pair per tile, persistent over the co-resident pairs.
     const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
     const int64_t pairs = tiles < max_pairs(dev) ? tiles : max_pairs(dev);
-    gemm_pair_kernel<<<static_cast<unsigned>(2 * pairs), THREADS, P_SMEM_BYTES, stream>>>(ma, mw, ep);
+    gemm_pair_kernel<<<static_cast<unsigned>(2 * pairs), THREADS, P_SMEM_BYTES, stream>>>(ma, mw, mo,
+                                                                                          ep);
   } else {
     const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, ep);
+    gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mo, ep);
   }
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }

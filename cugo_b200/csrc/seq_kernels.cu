@@ -262,29 +262,79 @@ __device__ __forceinline__ void acc_init(Acc<G>& a) {
     for (int e = 0; e < 8; ++e) a.v[g][e] = 0.0f;
 }
 
-template <int G>
-__device__ __forceinline__ void acc_row(Acc<G>& a, const __nv_bfloat16* __restrict__ wt, int col,
-                                        float scale) {
+// Adds the weight rows of every set bit of masks[k] (input column bases[k] + bit).
+// The columns are taken eight at a time and their rows loaded together, so a token
+// costs a few L2 round trips instead of one per active input.  The masks are the
+// same for the whole warp, so the index walk is warp-uniform.
+template <int G, int NM>
+__device__ __forceinline__ void acc_masks(Acc<G>& a, const __nv_bfloat16* __restrict__ wt,
+                                          u64 (&masks)[NM], const int (&bases)[NM]) {
   const int lane = threadIdx.x & 31;
-  const uint4* src = reinterpret_cast<const uint4*>(wt + static_cast<i64>(col) * (256 * G));
+  int k = 0;
+  for (;;) {
+    int col[8];
+    int cnt = 0;
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float f[8];
-    bf16x8(__ldg(src + 32 * g + lane), f);
+    for (int j = 0; j < 8; ++j) {
+      while (k < NM && masks[k] == 0) ++k;
+      col[j] = -1;
+      if (k < NM) {
+        const int b = __ffsll(static_cast<long long>(masks[k])) - 1;
+        masks[k] &= masks[k] - 1;
+        col[j] = bases[k] + b;
+        ++cnt;
+      }
+    }
+    uint4 raw[8][G];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) a.v[g][e] = fmaf(scale, f[e], a.v[g][e]);
+    for (int j = 0; j < 8; ++j) {
+      if (col[j] >= 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(wt + static_cast<i64>(col[j]) * (256 * G));
+#pragma unroll
+        for (int g = 0; g < G; ++g) raw[j][g] = __ldg(src + 32 * g + lane);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (col[j] >= 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float f[8];
+          bf16x8(raw[j][g], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a.v[g][e] += f[e];
+        }
+      }
+    }
+    if (cnt < 8) break;
   }
 }
 
-// Adds the rows of the set bits of a 50-bit card mask (plane `plane`).
-template <int G>
-__device__ __forceinline__ void acc_mask(Acc<G>& a, const __nv_bfloat16* __restrict__ wt, u64 mask,
-                                         int plane) {
-  mask &= (1ull << 50) - 1;
-  while (mask) {
-    const int b = __ffsll(static_cast<long long>(mask)) - 1;
-    mask &= mask - 1;
-    acc_row(a, wt, plane * 50 + b, 1.0f);
+// Adds scale[j] x row col[j] for the (up to 5) scalar inputs, loaded together.
+template <int G, int N>
+__device__ __forceinline__ void acc_scaled(Acc<G>& a, const __nv_bfloat16* __restrict__ wt,
+                                           const int (&col)[N], const float (&scale)[N]) {
+  const int lane = threadIdx.x & 31;
+  uint4 raw[N][G];
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    if (scale[j] != 0.0f) {
+      const uint4* src = reinterpret_cast<const uint4*>(wt + static_cast<i64>(col[j]) * (256 * G));
+#pragma unroll
+      for (int g = 0; g < G; ++g) raw[j][g] = __ldg(src + 32 * g + lane);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    if (scale[j] != 0.0f) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float f[8];
+        bf16x8(raw[j][g], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a.v[g][e] = fmaf(scale[j], f[e], a.v[g][e]);
+      }
+    }
   }
 }
 
@@ -339,18 +389,16 @@ __global__ void __launch_bounds__(256) event_embed_kernel(
                     static_cast<u64>(__ldg(ev + 6)), static_cast<u64>(__ldg(ev + 7))};
   Acc<G> a;
   acc_init(a);
-  acc_mask(a, wt, w[0], 0);
-  if (me) acc_mask(a, wt, w[1], 1);
-  acc_mask(a, wt, w[2], 2);
-  acc_mask(a, wt, first ? w[3] : w[4], 3);
-  acc_mask(a, wt, first ? w[4] : w[3], 4);
-  acc_mask(a, wt, first ? w[5] : w[6], 5);
-  acc_mask(a, wt, first ? w[6] : w[5], 6);
-  acc_mask(a, wt, w[7], 7);
-  acc_row(a, wt, 400 + static_cast<int>(kind < 11 ? kind : 11), 1.0f);
-  if (me) acc_row(a, wt, 412, 1.0f);
-  const int opp_drawn = me ? 0 : __popcll(w[1] & ((1ull << 50) - 1));
-  if (opp_drawn) acc_row(a, wt, 413, static_cast<float>(opp_drawn));
+  constexpr u64 k50 = (1ull << 50) - 1;
+  u64 masks[8] = {w[0] & k50, me ? (w[1] & k50) : 0ull, w[2] & k50, (first ? w[3] : w[4]) & k50,
+                  (first ? w[4] : w[3]) & k50, (first ? w[5] : w[6]) & k50,
+                  (first ? w[6] : w[5]) & k50, w[7] & k50};
+  const int bases[8] = {0, 50, 100, 150, 200, 250, 300, 350};
+  acc_masks(a, wt, masks, bases);
+  const int opp_drawn = me ? 0 : __popcll(w[1] & k50);
+  const int cols[3] = {400 + static_cast<int>(kind < 11 ? kind : 11), 412, 413};
+  const float scales[3] = {1.0f, me ? 1.0f : 0.0f, static_cast<float>(opp_drawn)};
+  acc_scaled(a, wt, cols, scales);
   i64 at = index ? __ldg(index + e) : 0;
   at = at < 0 ? 0 : (at > kMaxEvents - 1 ? kMaxEvents - 1 : at);
   acc_store(a, bias, position + (1 + at) * (256 * G), type_row, out + i * ldo);
@@ -374,28 +422,23 @@ __global__ void __launch_bounds__(256) start_embed_kernel(
   const i64 header = __ldg(st + 7);
   Acc<G> a;
   acc_init(a);
-  acc_mask(a, wt, static_cast<u64>(__ldg(st + (first ? 0 : 1))), 0);
-  acc_mask(a, wt, static_cast<u64>(__ldg(st + 2)), 1);
-  acc_mask(a, wt, static_cast<u64>(__ldg(st + (first ? 3 : 4))), 2);
-  acc_mask(a, wt, static_cast<u64>(__ldg(st + (first ? 4 : 3))), 3);
-  acc_mask(a, wt, static_cast<u64>(__ldg(st + 5)), 4);
-  u64 neutral = static_cast<u64>(__ldg(st + 6)) & 0xFFFull;
-  while (neutral) {
-    const int b = __ffsll(static_cast<long long>(neutral)) - 1;
-    neutral &= neutral - 1;
-    acc_row(a, wt, 250 + b, 1.0f);
-  }
+  constexpr u64 k50 = (1ull << 50) - 1;
+  u64 masks[6] = {static_cast<u64>(__ldg(st + (first ? 0 : 1))) & k50,
+                  static_cast<u64>(__ldg(st + 2)) & k50,
+                  static_cast<u64>(__ldg(st + (first ? 3 : 4))) & k50,
+                  static_cast<u64>(__ldg(st + (first ? 4 : 3))) & k50,
+                  static_cast<u64>(__ldg(st + 5)) & k50,
+                  static_cast<u64>(__ldg(st + 6)) & 0xFFFull};
+  const int bases[6] = {0, 50, 100, 150, 200, 250};
+  acc_masks(a, wt, masks, bases);
   const i64 mtype = header & 0xFF;
-  acc_row(a, wt, 262 + static_cast<int>(mtype < 7 ? mtype : 7), 1.0f);
-  const float c0 = static_cast<float>((header >> 8) & 0xFF) / 4.0f;
-  const float c1 = (((header >> 16) & 1) == seat) ? 1.0f : 0.0f;
   const i64 m24 = (header >> 24) & 0xFF, m32 = (header >> 32) & 0xFF;
-  const float c2 = static_cast<float>(first ? m24 : m32) / 8.0f;
-  const float c3 = static_cast<float>(first ? m32 : m24) / 8.0f;
-  if (c0 != 0.0f) acc_row(a, wt, 270, c0);
-  if (c1 != 0.0f) acc_row(a, wt, 271, c1);
-  if (c2 != 0.0f) acc_row(a, wt, 272, c2);
-  if (c3 != 0.0f) acc_row(a, wt, 273, c3);
+  const int cols[5] = {262 + static_cast<int>(mtype < 7 ? mtype : 7), 270, 271, 272, 273};
+  const float scales[5] = {1.0f, static_cast<float>((header >> 8) & 0xFF) / 4.0f,
+                           (((header >> 16) & 1) == seat) ? 1.0f : 0.0f,
+                           static_cast<float>(first ? m24 : m32) / 8.0f,
+                           static_cast<float>(first ? m32 : m24) / 8.0f};
+  acc_scaled(a, wt, cols, scales);
   acc_store(a, bias, pos_row, type_row, out + i * ldo);
 }
 
