@@ -237,6 +237,57 @@ def branching_bench(ext, roots_n=65_536, per_root=256, reps=3):
     return dict(roots=roots_n, branches=n, seconds=sec, branches_per_s=n / sec)
 
 
+# ---- config 3 with the 4x2048 policy, config 4: sequence self-play -----------------------
+
+def arch_bench(ext, arch: str, games: int, warmup: int = 1, steps: int = 2) -> dict:
+    """Config 3 repeated with another residual-MLP architecture (
+    "the same run is repeated with the 4x2048 residual MLP")."""
+    from cugo_b200.policy import ResidualMlpPolicy
+    from cugo_b200.selfplay import RoundTimer, play_batch
+
+    hidden, blocks = ARCHS[arch]
+    policy = ResidualMlpPolicy(hidden, blocks, "relu", device="cuda", seed=0)
+    dev = torch.device("cuda")
+    for s in range(warmup):
+        play_batch(ext, policy, torch.arange(games, dtype=torch.int64, device=dev) + s * games)
+    timer = RoundTimer(enabled=True)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    res = [play_batch(ext, policy, torch.arange(games, dtype=torch.int64, device=dev) + s * games,
+                      timer=timer) for s in range(warmup, warmup + steps)]
+    b.record()
+    torch.cuda.synchronize()
+    sec = a.elapsed_time(b) / 1e3
+    mlp_ms, _, mlp_rows = timer.total_ms()
+    tflops = policy.flops_per_row() * mlp_rows / (mlp_ms / 1e3) / 1e12 if mlp_ms > 0 else 0.0
+    return {"arch": arch, "games": games * steps, "seconds": sec,
+            "games_per_s": sum(r.games for r in res) / sec,
+            "decisions_per_s": sum(r.decisions for r in res) / sec,
+            "mlp_tflops": tflops}
+
+
+def seq_bench(wave: int = 4096, waves: int = 4) -> dict:
+    """Config 4: event-sequence policy (4 pre-LN layers, d 256, 8x32 heads, FFN 1024,
+    bf16 KV cache) self-play in waves of `wave` games, one CUDA graph per step."""
+    from cugo_b200.seq import SeqDecoder
+    from cugo_b200.seq_selfplay import SeqWaveSelfPlay
+
+    sp = SeqWaveSelfPlay(SeqDecoder.from_state_dict(SeqDecoder.random_state(0)), wave=wave)
+    sp.play_wave(0)  # capture + warm-up
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    steps = [sp.play_wave(g * wave) for g in range(1, waves + 1)]
+    b.record()
+    torch.cuda.synchronize()
+    sec = a.elapsed_time(b) / 1e3
+    sp.release()
+    return {"wave": wave, "waves": waves, "games": wave * waves, "seconds": sec,
+            "games_per_s": wave * waves / sec, "decision_steps_per_wave": steps,
+            "policy": "SeqNet hybrid, 4 layers, d 256, 8x32 heads, FFN 1024, random init seed 0"}
+
+
 # ---- CPU: the reference engine (oracle/_ref) + a PyTorch-CPU policy --------------------
 
 def cpu_selfplay(games: int, arch: str, threads: int, policy_cpu=None) -> dict:
@@ -334,6 +385,9 @@ def main():
     if not args.no_extras:
         extras["engine_only"] = engine_only_bench(ext)
         extras["branching"] = branching_bench(ext)
+        if args.arch != "2048x4":
+            extras["config3_2048x4"] = arch_bench(ext, "2048x4", args.games)
+        extras["config4_seq"] = seq_bench()
     peaks = measured_peaks()
     if "engine_only" in extras:
         e = extras["engine_only"]
@@ -368,7 +422,11 @@ def main():
                      "bound": "tensor",
                      "achieved": mlp_tflops, "peak": peaks["bf16_tflops_sustained"],
                      "unit": "TFLOP/s", "frac": mlp_tflops / peaks["bf16_tflops_sustained"],
-                     "traffic": None, "peak_source": peaks["source"] + " (sustained)"},
+                     # ncu dram__bytes_read + write per gemm_kernel launch, averaged over
+                     # the 8 layers of a 262,144-row 3x512 forward (4,784 MB / 8).
+                     "traffic": 598e6 if args.arch == "512x3" else None,
+                     "traffic_unit": "bytes per launch",
+                     "peak_source": peaks["source"] + " (sustained)"},
         "clocks": sp["clocks"],
         "gpu_launches": sp["launches"],
         "extras": extras,

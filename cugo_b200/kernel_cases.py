@@ -174,7 +174,13 @@ def main() -> None:
         ops["query_token"] = lambda: dec.query_token(qin)
         xr = torch.randn((w, 256), generator=g).to(dev)
         ops["readout"] = lambda: dec.readout(xr)
-        ev = torch.randint(0, 1 << 50, (w, 9), generator=g).to(dev)
+        # Event words shaped like real ones: one card in each of the first seven
+        # masks, none shown, actor and kind in the header word.
+        cards = torch.randint(0, 50, (w, 9), generator=g)
+        ev = torch.bitwise_left_shift(torch.ones_like(cards), cards)
+        ev[:, 7] = 0
+        ev[:, 8] = torch.randint(0, 2, (w,), generator=g) | (torch.randint(0, 12, (w,), generator=g) << 8)
+        ev = ev.to(dev)
         seats = torch.cat((torch.zeros(w), torch.ones(w))).long().to(dev)
         cnt = torch.randint(0, 40, (w,), generator=g).to(dev)
         ops["event_token n=2w"] = lambda: dec.event_token(ev, seats, cnt)
