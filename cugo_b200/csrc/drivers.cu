@@ -11,6 +11,7 @@
 #include <stdint.h>
 
 #include "engine/driver.cuh"
+#include "tile.cuh"
 #include "engine/env.cuh"
 #include "../../include/cugo_b200.h"
 
@@ -18,7 +19,7 @@ using namespace cb;
 
 namespace {
 
-constexpr int kBlock = 128;
+using namespace cb::tile;
 constexpr u64 kFnvOffset = 0xcbf29ce484222325ull;
 constexpr u64 kFnvPrime = 0x100000001b3ull;
 
@@ -82,42 +83,63 @@ __global__ void __launch_bounds__(kBlock) rollout_kernel(
   status_out[k] = static_cast<int16_t>(st);
 }
 
-// One decision of every slot: a finished game is replaced by the slot's next
-// game (index + n_slots), then observe -> random legal pick -> step.  Features
-// and masks of the decision are written like observe() writes them.
-struct SlotTile {
-  union {
-    u64 rows[32][kRowWords];
-    struct {
-      u32 bits[32][kBitWords + 1];
-      float scal[32][kScalarColumns];
-    } pk;
-  };
-  u64 legal[32][3];
-};
+// Replaces every finished game by the slot's next game (index + n_slots, decision
+// counter 0, completed + 1).  A block scans 4,096 slots (the done byte of each
+// row), queues the finished ones in shared memory and deals them with consecutive
+// threads, so a warp's deal work is not repeated for one finished lane among
+// thirty-one live ones, as it would be inside the decision kernel.
+constexpr int kResetSpan = 4096;
 
-__global__ void __launch_bounds__(kBlock) selfplay_step_kernel(
+__global__ void __launch_bounds__(256) reset_finished_kernel(
+    u64* __restrict__ states, i64 n_slots, i64 seed_base, i64* __restrict__ slot_game,
+    int32_t* __restrict__ slot_decision, int32_t* __restrict__ slot_completed) {
+  __shared__ int32_t queue[kResetSpan];
+  __shared__ int count;
+  if (threadIdx.x == 0) count = 0;
+  __syncthreads();
+  const i64 first = (i64)blockIdx.x * kResetSpan;
+  const uint8_t* bytes = reinterpret_cast<const uint8_t*>(states);
+  for (int k = threadIdx.x; k < kResetSpan; k += blockDim.x) {
+    const i64 slot = first + k;
+    if (slot < n_slots && bytes[slot * kRowBytes + kDoneByte] != 0)
+      queue[atomicAdd(&count, 1)] = static_cast<int32_t>(k);
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < count; q += blockDim.x) {
+    const i64 slot = first + queue[q];
+    const i64 game = slot_game[slot] + n_slots;
+    Game g;
+    create_game(g, static_cast<u64>(seed_base + game), static_cast<u32>(game & 1));
+    zero_padding(g);
+    u64* row = states + slot * kRowWords;
+#pragma unroll
+    for (int w = 0; w < kRowWords; ++w) row[w] = g.w[w];
+    slot_game[slot] = game;
+    slot_decision[slot] = 0;
+    slot_completed[slot] += 1;
+  }
+}
+
+// One decision of every slot after the resets: observe -> random legal pick ->
+// step (a game finished at its deal takes no action).  Features and masks of the
+// decision are written like observe() writes them.  The warp tile scheme is the
+// batch environment's (tile.cuh): asynchronous row gathers, packets written into
+// the tile, cooperative feature/mask stores, one bulk copy of a full tile of rows
+// back in place.
+__global__ void __launch_bounds__(kBlock, 4) selfplay_step_kernel(
     u64* __restrict__ states, i64 n_slots, i64 seed_base, i64* __restrict__ slot_game,
     int32_t* __restrict__ slot_decision, int32_t* __restrict__ slot_completed,
     int64_t* __restrict__ slot_steps, float* __restrict__ features, bool* __restrict__ legal_out) {
-  __shared__ SlotTile tiles[kBlock / 32];
-  SlotTile& t = tiles[threadIdx.x >> 5];
-  const int lane = threadIdx.x & 31;
+  (void)slot_completed;
+  WarpTile& t = my_tile();
   const i64 slot = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
   const i64 my_src = slot < n_slots ? slot : -1;
-  // Gather the 32 rows.
-#pragma unroll 8
-  for (int r = 0; r < 32; ++r) {
-    const i64 id = __shfl_sync(0xffffffffu, my_src, r);
-    if (lane < kRowWords) t.rows[r][lane] = id >= 0 ? __ldg(states + id * kRowWords + lane) : 0ull;
-  }
-  __syncwarp();
+  gather_rows(t, states, my_src);
   Game g;
-#pragma unroll
-  for (int w = 0; w < kRowWords; ++w) g.w[w] = t.rows[lane][w];
+  load_game(t, g);
   __syncwarp();  // rows are in registers: the tile now holds packets
-  const PacketRef pk{t.pk.bits[lane], t.pk.scal[lane]};
+  const PacketRef pk = lane_packet(t);
   ObsMeta meta;
   u32 action = 0xffffu;
   i64 game = 0;
@@ -125,12 +147,6 @@ __global__ void __launch_bounds__(kBlock) selfplay_step_kernel(
   if (slot < n_slots) {
     game = slot_game[slot];
     decision = static_cast<u32>(slot_decision[slot]);
-    if (g.done()) {
-      slot_completed[slot] += 1;
-      game += n_slots;
-      decision = 0;
-      create_game(g, static_cast<u64>(seed_base + game), static_cast<u32>(game & 1));
-    }
     observe_game(g, pk, meta);
     const u32 r0 = game_draw(static_cast<u64>(game), decision, 0u, static_cast<u64>(seed_base + game)).v[0];
     action = pick_set_bit(meta.legal.w0, meta.legal.w1, meta.legal.w2, r0);
@@ -139,50 +155,12 @@ __global__ void __launch_bounds__(kBlock) selfplay_step_kernel(
     for (u32 k = 0; k < kScalarColumns; ++k) pk.scal[k] = 0.0f;
     meta.legal = Legal{};
   }
-  // Packets are in shared memory; the cooperative feature/mask writes follow.
-  t.legal[lane][0] = meta.legal.w0;
-  t.legal[lane][1] = meta.legal.w1;
-  t.legal[lane][2] = meta.legal.w2;
-  __syncwarp();
+  store_legal(t, meta.legal);
   const i64 left = n_slots - tile_base;
   const int rows_here = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
-  for (int r = 0; r < rows_here; ++r) {
-    float4* row = reinterpret_cast<float4*>(features + (tile_base + r) * (i64)kFeatures);
-#pragma unroll
-    for (int k = 0; k < 6; ++k) {
-      const int q = lane + 32 * k;
-      if (q < (int)(kFeatures / 4)) {
-        float v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const u32 c = 4u * q + j;
-          const int s = scalar_slot(c);
-          v[j] = s >= 0 ? t.pk.scal[r][s] : ((t.pk.bits[r][c >> 5] >> (c & 31u)) & 1u ? 1.0f : 0.0f);
-        }
-        __stcs(row + q, make_float4(v[0], v[1], v[2], v[3]));
-      }
-    }
-  }
-  {
-    uint8_t* block = reinterpret_cast<uint8_t*>(legal_out) + tile_base * (i64)kActions;
-    const int bytes = rows_here * (int)kActions;
-    const int words = bytes >> 2;
-    for (int wi = lane; wi < words; wi += 32) {
-      u32 v = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int b = 4 * wi + j;
-        const int r = b / (int)kActions, a = b - r * (int)kActions;
-        v |= static_cast<u32>((t.legal[r][a >> 6] >> (a & 63)) & 1ull) << (8 * j);
-      }
-      reinterpret_cast<u32*>(block)[wi] = v;
-    }
-    for (int b = 4 * words + lane; b < bytes; b += 32) {
-      const int r = b / (int)kActions, a = b - r * (int)kActions;
-      block[b] = static_cast<uint8_t>((t.legal[r][a >> 6] >> (a & 63)) & 1ull);
-    }
-  }
-  __syncwarp();
+  emit_features(t, features, (i64)kFeatures, tile_base, rows_here);
+  emit_legal(t, legal_out, tile_base, rows_here);
+  __syncwarp();  // emission done: the tile holds rows again
   if (slot < n_slots) {
     if (action != 0xffffu) {
       step_game(g, action);
@@ -192,15 +170,8 @@ __global__ void __launch_bounds__(kBlock) selfplay_step_kernel(
     slot_game[slot] = game;
     slot_decision[slot] = static_cast<int32_t>(decision);
   }
-  zero_padding(g);
-#pragma unroll
-  for (int w = 0; w < kRowWords; ++w) t.rows[lane][w] = g.w[w];
-  __syncwarp();
-#pragma unroll 8
-  for (int r = 0; r < 32; ++r) {
-    const i64 id = __shfl_sync(0xffffffffu, my_src, r);
-    if (id >= 0 && lane < kRowWords) states[id * kRowWords + lane] = t.rows[r][lane];
-  }
+  store_game(t, g);
+  store_tile(t, states, tile_base, n_slots, my_src);
 }
 
 // Branching roots: game r advanced by k_r < 21 random-legal decisions, stopping
@@ -287,6 +258,9 @@ int cugo_b200_selfplay_random_step(uint8_t* states, int64_t n_slots, int64_t see
       (reinterpret_cast<uintptr_t>(legal) & 3u))
     return CUGO_B200_ERR_ALIGN;
   if (n_slots == 0) return CUGO_B200_OK;
+  reset_finished_kernel<<<static_cast<unsigned>((n_slots + kResetSpan - 1) / kResetSpan), 256, 0,
+                          stream>>>(reinterpret_cast<u64*>(states), n_slots, seed_base, slot_game,
+                                    slot_decision, slot_completed);
   selfplay_step_kernel<<<blocks_for(n_slots), kBlock, 0, stream>>>(
       reinterpret_cast<u64*>(states), n_slots, seed_base, slot_game, slot_decision, slot_completed,
       slot_steps, features, legal);

@@ -909,16 +909,32 @@ CB_HD Mask mission_set(u32 type, u32 index) {
   if (type == kMissionNormal) return month_cards(index);
   if (type != kMissionHard && type != kMissionTriple) return 0;
   // Hard sets 0..13; the triple list skips hard set 4 and orders 5.. differently.
-  constexpr Mask kShared[5] = {cards_of(21, 33, 37), cards_of(1, 5, 9), cards_of(13, 17, 25),
-                               cards_of(4, 12, 29), cards_of(32, 41, 47)};
-  constexpr Mask kTail[9] = {cards_of(20, 24, 36), cards_of(0, 8, 28),  cards_of(0, 8, 40),
-                             cards_of(0, 28, 40),  cards_of(8, 28, 40), cards_of(4, 12, 45),
-                             cards_of(4, 29, 45),  cards_of(12, 29, 45), cards_of(4, 24, 45)};
+  // (Switches rather than local arrays: a runtime-indexed local table would be
+  // copied to every thread's stack.)
   if (type == kMissionTriple && index >= 4u) ++index;
-  if (index < 5u) return kShared[index];
+  if (index < 5u) {
+    switch (index) {
+      case 0: return cards_of(21, 33, 37);
+      case 1: return cards_of(1, 5, 9);
+      case 2: return cards_of(13, 17, 25);
+      case 3: return cards_of(4, 12, 29);
+      default: return cards_of(32, 41, 47);
+    }
+  }
   if (index > 13u) return 0;
-  // Hard 5..13 read kTail[0..8]; triple 5..13 read kTail[8, 0..7].
-  return type == kMissionTriple ? kTail[(index - 5u + 8u) % 9u] : kTail[index - 5u];
+  // Hard 5..13 read tail sets 0..8; triple 5..13 read tail sets 8, 0..7.
+  const u32 tail = type == kMissionTriple ? (index - 5u + 8u) % 9u : index - 5u;
+  switch (tail) {
+    case 0: return cards_of(20, 24, 36);
+    case 1: return cards_of(0, 8, 28);
+    case 2: return cards_of(0, 8, 40);
+    case 3: return cards_of(0, 28, 40);
+    case 4: return cards_of(8, 28, 40);
+    case 5: return cards_of(4, 12, 45);
+    case 6: return cards_of(4, 29, 45);
+    case 7: return cards_of(12, 29, 45);
+    default: return cards_of(4, 24, 45);
+  }
 }
 
 CB_HD void create_game(Game& g, u64 seed, u32 first) {
@@ -963,10 +979,14 @@ CB_HD void create_game(Game& g, u64 seed, u32 first) {
   u64 mrng = deal_rng ^ 0x6d697373696f6e35ull;
   const u32 kind = bounded_draw(mrng, 5u);
   const u32 mult = 2u + bounded_draw(mrng, 3u);
-  constexpr u32 kTypes[5] = {kMissionEasy, kMissionNormal, kMissionHard, kMissionAll, kMissionTriple};
-  constexpr u32 kOptions[5] = {11u, 12u, 14u, 0u, 13u};
-  const u32 type = kTypes[kind];
-  const u32 index = kOptions[kind] == 0 ? 0u : bounded_draw(mrng, kOptions[kind]);
+  // kind 0..4 -> Easy (11 sets), Normal (12), Hard (14), All (none), Triple (13).
+  const u32 type = kind == 0 ? kMissionEasy
+                 : kind == 1 ? kMissionNormal
+                 : kind == 2 ? kMissionHard
+                 : kind == 3 ? kMissionAll
+                             : kMissionTriple;
+  const u32 options = kind == 0 ? 11u : kind == 1 ? 12u : kind == 2 ? 14u : kind == 3 ? 0u : 13u;
+  const u32 index = options == 0 ? 0u : bounded_draw(mrng, options);
   g.set_mission_type(type);
   g.set_mission_mult(type == kMissionTriple ? 0u : mult);
   g.set_mission(mission_set(type, index));

@@ -13,6 +13,7 @@
 namespace cb {
 
 constexpr int kRowBytes = 248;
+constexpr int kDoneByte = 239;  // TorchEnv50::done (word 29, bits 56..63)
 constexpr int kRowWords = 31;
 
 // Decision kinds as the policy sees them (cugo/game/policy50.h:36-42,
