@@ -198,23 +198,26 @@ def engine_only_bench(ext, slots=1 << 20, decisions=64, warm=3):
     steps = torch.zeros(slots, dtype=torch.int64, device=dev)
     feats = torch.empty((slots, 720), dtype=torch.float32, device=dev)
     legal = torch.empty((slots, 179), dtype=torch.bool, device=dev)
+    actions = torch.empty((slots,), dtype=torch.int64, device=dev)
     for _ in range(warm):
-        ext.selfplay_random_step(states, slot_game, slot_dec, completed, steps, feats, legal)
+        ext.selfplay_random_step(states, slot_game, slot_dec, completed, steps, feats, legal,
+                                 actions=actions)
     completed.zero_()
     steps.zero_()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(decisions):
-        ext.selfplay_random_step(states, slot_game, slot_dec, completed, steps, feats, legal)
+        ext.selfplay_random_step(states, slot_game, slot_dec, completed, steps, feats, legal,
+                                 actions=actions)
     b.record()
     torch.cuda.synchronize()
     sec = a.elapsed_time(b) / 1e3
     dec = int(steps.sum())
     games = int(completed.sum())
     return dict(slots=slots, decisions_per_slot=decisions, seconds=sec,
-                steps_per_s=dec / sec, games_per_s=games / sec, launches=decisions,
-                launch_ms=sec * 1e3 / decisions, decisions_per_launch=dec / decisions)
+                steps_per_s=dec / sec, games_per_s=games / sec, launches=3 * decisions,
+                ms_per_decision_step=sec * 1e3 / decisions, decisions_per_step=dec / decisions)
 
 
 def branching_bench(ext, roots_n=65_536, per_root=256, reps=3):

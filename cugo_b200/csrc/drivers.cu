@@ -17,6 +17,9 @@
 
 using namespace cb;
 
+// In-place step without per-row outputs (env_kernels.cu).
+int cb_step_in_place(uint8_t* states, int64_t n, const int64_t* actions, cudaStream_t stream);
+
 namespace {
 
 using namespace cb::tile;
@@ -120,36 +123,38 @@ __global__ void __launch_bounds__(256) reset_finished_kernel(
   }
 }
 
-// One decision of every slot after the resets: observe -> random legal pick ->
-// step (a game finished at its deal takes no action).  Features and masks of the
-// decision are written like observe() writes them.  The warp tile scheme is the
-// batch environment's (tile.cuh): asynchronous row gathers, packets written into
-// the tile, cooperative feature/mask stores, one bulk copy of a full tile of rows
-// back in place.
-__global__ void __launch_bounds__(kBlock, 4) selfplay_step_kernel(
-    u64* __restrict__ states, i64 n_slots, i64 seed_base, i64* __restrict__ slot_game,
-    int32_t* __restrict__ slot_decision, int32_t* __restrict__ slot_completed,
-    int64_t* __restrict__ slot_steps, float* __restrict__ features, bool* __restrict__ legal_out) {
-  (void)slot_completed;
+// The observation and random legal pick of every slot after the resets: features
+// and masks written like observe() writes them, actions[slot] = the pick (-1 for a
+// game finished at its deal), decision and step counters advanced.  The step itself
+// is a second launch (the in-place step kernel): the rule code of observe and step
+// in one kernel overflows the instruction cache (ncu: "no instruction" was the top
+// stall of the fused kernel, 4.6 cycles per issued instruction).
+__global__ void __launch_bounds__(kBlock, 5) selfplay_pick_kernel(
+    const u64* __restrict__ states, i64 n_slots, i64 seed_base, const i64* __restrict__ slot_game,
+    int32_t* __restrict__ slot_decision, int64_t* __restrict__ slot_steps,
+    float* __restrict__ features, bool* __restrict__ legal_out, i64* __restrict__ actions) {
   WarpTile& t = my_tile();
   const i64 slot = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
-  const i64 my_src = slot < n_slots ? slot : -1;
-  gather_rows(t, states, my_src);
+  gather_rows(t, states, slot < n_slots ? slot : -1);
   Game g;
   load_game(t, g);
   __syncwarp();  // rows are in registers: the tile now holds packets
   const PacketRef pk = lane_packet(t);
   ObsMeta meta;
-  u32 action = 0xffffu;
-  i64 game = 0;
-  u32 decision = 0;
   if (slot < n_slots) {
-    game = slot_game[slot];
-    decision = static_cast<u32>(slot_decision[slot]);
     observe_game(g, pk, meta);
+    const i64 game = slot_game[slot];
+    const u32 decision = static_cast<u32>(slot_decision[slot]);
     const u32 r0 = game_draw(static_cast<u64>(game), decision, 0u, static_cast<u64>(seed_base + game)).v[0];
-    action = pick_set_bit(meta.legal.w0, meta.legal.w1, meta.legal.w2, r0);
+    const u32 action = pick_set_bit(meta.legal.w0, meta.legal.w1, meta.legal.w2, r0);
+    if (action != 0xffffu) {
+      slot_decision[slot] = static_cast<int32_t>(decision + 1u);
+      slot_steps[slot] += 1;
+      actions[slot] = static_cast<i64>(action);
+    } else {
+      actions[slot] = -1;  // "not legal": the step leaves the row unchanged
+    }
   } else {
     for (u32 k = 0; k < kBitWords; ++k) pk.bits[k] = 0;
     for (u32 k = 0; k < kScalarColumns; ++k) pk.scal[k] = 0.0f;
@@ -160,18 +165,6 @@ __global__ void __launch_bounds__(kBlock, 4) selfplay_step_kernel(
   const int rows_here = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
   emit_features(t, features, (i64)kFeatures, tile_base, rows_here);
   emit_legal(t, legal_out, tile_base, rows_here);
-  __syncwarp();  // emission done: the tile holds rows again
-  if (slot < n_slots) {
-    if (action != 0xffffu) {
-      step_game(g, action);
-      ++decision;
-      slot_steps[slot] += 1;
-    }
-    slot_game[slot] = game;
-    slot_decision[slot] = static_cast<int32_t>(decision);
-  }
-  store_game(t, g);
-  store_tile(t, states, tile_base, n_slots, my_src);
 }
 
 // Branching roots: game r advanced by k_r < 21 random-legal decisions, stopping
@@ -249,22 +242,23 @@ int cugo_b200_rollout_random(int64_t game0, int64_t n, int64_t seed_base, int32_
 int cugo_b200_selfplay_random_step(uint8_t* states, int64_t n_slots, int64_t seed_base,
                                    int64_t* slot_game, int32_t* slot_decision,
                                    int32_t* slot_completed, int64_t* slot_steps, float* features,
-                                   bool* legal, cudaStream_t stream) {
+                                   bool* legal, int64_t* actions, cudaStream_t stream) {
   if (n_slots < 0) return CUGO_B200_ERR_ARG;
   if (n_slots > 0 && (!states || !slot_game || !slot_decision || !slot_completed || !slot_steps ||
-                      !features || !legal))
+                      !features || !legal || !actions))
     return CUGO_B200_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(states) & 7u) || (reinterpret_cast<uintptr_t>(features) & 15u) ||
-      (reinterpret_cast<uintptr_t>(legal) & 3u))
+      (reinterpret_cast<uintptr_t>(legal) & 3u) || (reinterpret_cast<uintptr_t>(actions) & 7u))
     return CUGO_B200_ERR_ALIGN;
   if (n_slots == 0) return CUGO_B200_OK;
   reset_finished_kernel<<<static_cast<unsigned>((n_slots + kResetSpan - 1) / kResetSpan), 256, 0,
                           stream>>>(reinterpret_cast<u64*>(states), n_slots, seed_base, slot_game,
                                     slot_decision, slot_completed);
-  selfplay_step_kernel<<<blocks_for(n_slots), kBlock, 0, stream>>>(
-      reinterpret_cast<u64*>(states), n_slots, seed_base, slot_game, slot_decision, slot_completed,
-      slot_steps, features, legal);
-  return launch_status();
+  selfplay_pick_kernel<<<blocks_for(n_slots), kBlock, 0, stream>>>(
+      reinterpret_cast<const u64*>(states), n_slots, seed_base, slot_game, slot_decision, slot_steps,
+      features, legal, actions);
+  if (launch_status() != CUGO_B200_OK) return CUGO_B200_ERR_LAUNCH;
+  return cb_step_in_place(states, n_slots, actions, stream);
 }
 
 int cugo_b200_branch_roots(int64_t n_roots, int64_t seed_base, uint8_t* roots, cudaStream_t stream) {

@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
   if (children) store_tile(t, children, tile_base, m, row < m ? row : -1);
   else if (!ids) store_tile(t, states, tile_base, m, src);  // in place, rows in order
   else scatter_rows(t, states, src);
-  if (row < m) {
+  if (row < m && reward) {  // internal callers may skip the per-row outputs
     reward[row] = static_cast<float>(out.reward0);
     done[row] = out.done != 0;
     nagari[row] = out.nagari != 0;
@@ -278,6 +278,20 @@ int cugo_b200_observe_indexed(const uint8_t* states, int64_t n_states, const int
   return observe_common(states, n_states, env_ids, m, features, legal, players, done, status,
                         stream);
 }
+
+}  // extern "C"
+
+// In-place step of rows 0..n-1 with actions[i] and no per-row outputs, for the
+// drivers in other translation units (not part of the C ABI).
+int cb_step_in_place(uint8_t* states, int64_t n, const int64_t* actions, cudaStream_t stream) {
+  if (n <= 0) return CUGO_B200_OK;
+  step_kernel<<<blocks_for(n, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<u64*>(states), n, nullptr, actions, n, nullptr, nullptr, nullptr, nullptr,
+      nullptr, nullptr, nullptr);
+  return launch_status();
+}
+
+extern "C" {
 
 static int step_common(uint8_t* states, int64_t n_states, const int64_t* env_ids,
                        const int64_t* actions, int64_t m, uint8_t* children, float* reward,

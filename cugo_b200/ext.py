@@ -35,7 +35,7 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_stock_indexed": [_VP, _I64, _VP, _I64, _VP, _VP],
     "cugo_b200_start": [_VP, _I64, _VP, _VP],
     "cugo_b200_rollout_random": [_I64, _I64, _I64, _I32, _U32, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
-    "cugo_b200_selfplay_random_step": [_VP, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_selfplay_random_step": [_VP, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_branch_roots": [_I64, _I64, _VP, _VP],
     "cugo_b200_branch_actions": [_VP, _I64, _I64, _I64, _VP, _VP, _VP],
     "cugo_b200_sample_actions": [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _I32, _VP, _VP, _VP],
@@ -322,13 +322,18 @@ class CugoB200Extension:
         return out
 
     def selfplay_random_step(self, states, slot_game, slot_decision, slot_completed, slot_steps,
-                             features, legal, seed_base: int = 12345) -> None:
+                             features, legal, seed_base: int = 12345,
+                             actions: torch.Tensor | None = None) -> torch.Tensor:
+        """One config-1 decision of every slot; returns the drawn actions."""
         n = states.size(0)
         with torch.cuda.device(states.device):
+            if actions is None:
+                actions = torch.empty((n,), dtype=torch.int64, device=states.device)
             _check(self._lib.cugo_b200_selfplay_random_step(
                 _ptr(states), n, seed_base, _ptr(slot_game), _ptr(slot_decision),
-                _ptr(slot_completed), _ptr(slot_steps), _ptr(features), _ptr(legal),
+                _ptr(slot_completed), _ptr(slot_steps), _ptr(features), _ptr(legal), _ptr(actions),
                 self._stream(states.device)), "selfplay_random_step")
+        return actions
 
     def branch_roots(self, n_roots: int, seed_base: int = 12345,
                      device: torch.device | str = "cuda") -> torch.Tensor:

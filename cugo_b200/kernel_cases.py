@@ -115,7 +115,9 @@ def main() -> None:
         done, steps = torch.zeros_like(dec), torch.zeros(slots, dtype=torch.int64, device=dev)
         feats = torch.empty((slots, 720), dtype=torch.float32, device=dev)
         legal = torch.empty((slots, 179), dtype=torch.bool, device=dev)
-        sec = _time(lambda: ext.selfplay_random_step(states, game, dec, done, steps, feats, legal),
+        acts = torch.empty((slots,), dtype=torch.int64, device=dev)
+        sec = _time(lambda: ext.selfplay_random_step(states, game, dec, done, steps, feats, legal,
+                                                     actions=acts),
                     args.warmup, args.iters)
         out.update(seconds=sec, decisions_per_s=slots / sec, gbs=slots * 4027 / sec / 1e9)
     elif args.case == "attention":

@@ -139,12 +139,13 @@ CUGO_B200_API int cugo_b200_rollout_random(int64_t game0, int64_t n, int64_t see
 /* One decision of every slot: a finished game is replaced by game index +
  * n_slots (counted in slot_completed), then the slot's observation is written to
  * features/legal exactly as observe() writes it, a random legal action is drawn
- * and stepped (counted in slot_steps). */
+ * and stepped (counted in slot_steps).  actions: int64 [n_slots] scratch that
+ * receives the drawn actions (-1 where a game ended at its deal). */
 CUGO_B200_API int cugo_b200_selfplay_random_step(uint8_t* states, int64_t n_slots,
                                                  int64_t seed_base, int64_t* slot_game,
                                                  int32_t* slot_decision, int32_t* slot_completed,
                                                  int64_t* slot_steps, float* features, bool* legal,
-                                                 cudaStream_t stream);
+                                                 int64_t* actions, cudaStream_t stream);
 
 /* Branching roots: game r advanced by k_r random-legal decisions, k_r uniform in
  * 0..20 (stream 2, decision 0xFFFF), stopping before a decision that would end
