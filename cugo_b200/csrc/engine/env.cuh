@@ -688,8 +688,10 @@ CB_HD void commit_pending(Game& g) {
   g.set_held(1, g.held(1) | g.hand(1));
   const u32 kind = g.pa_kind();
   switch (kind) {
-    case kActPlay: commit_regular(g, g.pa_card(), false); break;
-    case kActShake: commit_regular(g, g.pa_card(), true); break;
+    case kActPlay:
+    case kActShake:  // one call site: plays and shakes of a warp share one inlined copy
+      commit_regular(g, g.pa_card(), kind == kActShake);
+      break;
     case kActBonus: commit_bonus(g, g.pa_card()); break;
     case kActBomb:
     case kActGrenade:

@@ -54,6 +54,17 @@ __device__ __forceinline__ i64 lane_source(const i64* ids, i64 row, i64 m, i64 n
 // instead of a load -> shared store chain per word.
 __device__ __forceinline__ void gather_rows(WarpTile& t, const u64* __restrict__ src, i64 my_src) {
   const int lane = threadIdx.x & 31;
+  // Branching reads one parent for many children: when every lane names the same
+  // row, fetch it once and replicate it in shared memory.
+  const i64 id0 = __shfl_sync(kFull, my_src, 0);
+  if (__all_sync(kFull, my_src == id0) && id0 >= 0) {
+    const u64 w = lane < kRowWords ? __ldg(src + id0 * kRowWords + lane) : 0ull;
+#pragma unroll 8
+    for (int r = 0; r < 32; ++r)
+      if (lane < kRowWords) t.rows[r][lane] = w;
+    __syncwarp();
+    return;
+  }
 #pragma unroll 8
   for (int r = 0; r < 32; ++r) {
     const i64 id = __shfl_sync(kFull, my_src, r);
@@ -96,7 +107,9 @@ __device__ __forceinline__ bool store_tile_bulk(const WarpTile& t, u64* __restri
                  "r"(32u * kRowWords * 8u)
                  : "memory");
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    // The tile may be reused (or the warp may exit) once the copy has read it;
+    // its global writes complete with the grid.
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
   }
   __syncwarp();
   return true;
