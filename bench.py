@@ -25,7 +25,7 @@ import subprocess
 import sys
 import tempfile
 import time
-from datetime import timedelta
+from datetime import datetime, timedelta
 from pathlib import Path
 
 import numpy as np
@@ -88,6 +88,10 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index: int):
+        # Started before the warm-up: nvidia-smi's start-up queries the driver, and
+        # started right at the timed region it slowed the first ~0.2 s of it.
+        # Samples are kept for the timed window only (host timestamps).
+        self.window: tuple[float, float] | None = None
         self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
         target = str(device_index)
         try:
@@ -97,18 +101,34 @@ class ClockSampler:
             pass
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", target], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+                ["nvidia-smi", f"--query-gpu=timestamp,{self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", target], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+
+    def mark(self, start: float, end: float) -> None:
+        """The timed region's host wall-clock window (time.time())."""
+        self.window = (start, end)
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         self.proc.wait(timeout=10)
-        rows = [r.split(", ") for r in self.path.read_text().splitlines() if r.count(",") >= 8]
+        rows = [r.split(", ") for r in self.path.read_text().splitlines() if r.count(",") >= 9]
         self.path.unlink(missing_ok=True)
+
+        def stamp(r):
+            try:
+                return datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                return None
+
+        if self.window is not None:
+            lo, hi = self.window
+            inside = [r for r in rows if (t := stamp(r)) is not None and lo - 0.05 <= t <= hi + 0.05]
+            rows = inside or rows
+        rows = [r[1:] for r in rows]
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -141,6 +161,8 @@ def selfplay_bench(args, world, rank, ext, policy):
     # plays games (s * world + r) * g .. + g.
     from cugo_b200.shard import game_block
     blocks = [game_block(s, rank, world, g, dev) for s in range(total_steps)]
+    clocks = ClockSampler(torch.cuda.current_device())
+    time.sleep(0.5)  # let nvidia-smi finish starting before any timing
     for s in range(args.warmup):
         play_batch(ext, policy, blocks[s])
     barrier(world)
@@ -148,12 +170,13 @@ def selfplay_bench(args, world, rank, ext, policy):
     launches: list[int] = []
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     results = []
-    clocks = ClockSampler(torch.cuda.current_device())
+    t_start = time.time()
     start.record()
     for s in range(args.warmup, total_steps):
         results.append(play_batch(ext, policy, blocks[s], timer=timer, launches=launches))
     stop.record()
     barrier(world)
+    clocks.mark(t_start, time.time())
     clk = clocks.stop()
     elapsed = start.elapsed_time(stop) / 1e3
     games = sum(r.games for r in results)

@@ -46,7 +46,8 @@ constexpr int THREADS = 64 + EPI_THREADS;
 constexpr int EPI_BUF = 2048;                   // one 32-row x 64-byte chunk
 constexpr int EPI_STAGE_BYTES = EPI_WARPS * 2 * EPI_BUF;  // double-buffered per warp
 constexpr uint32_t TMEM_COLS = 2 * BN;          // two accumulators
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ +
+constexpr int BAR_BYTES = 512;  // mbarriers and the TMEM address
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + BAR_BYTES +
                            BN * 4 /*bias*/ + EPI_STAGE_BYTES;
 constexpr uint64_t kWaitNs = 2'000'000'000ull;
 
@@ -252,28 +253,23 @@ __device__ __forceinline__ void store_chunk(uint8_t* stage, const float* v, cons
   if (lane == 0) tma_store_2d(map_out, stage, col0, row0);
 }
 
-// Starts copying the residual of a 32-row x 64-byte chunk (32 bf16 or 16 fp32
-// columns) into a staging buffer (cp.async, zero-filled outside the matrix); one
-// commit group per chunk.
-__device__ __forceinline__ void prefetch_residual(uint8_t* buf, const Epilogue& ep, int row0,
-                                                  int col0) {
-  const int lane = threadIdx.x & 31;
-  const int esz = ep.out_fp32 ? 4 : 2, per = 16 / esz;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = 8 * i + (lane >> 2), p = lane & 3;
-    const int grow = row0 + r, gcol = col0 + p * per;
-    int bytes = 0;
-    const uint8_t* src = static_cast<const uint8_t*>(ep.residual);
-    if (ep.residual && grow < ep.m && gcol < ep.n) {
-      bytes = esz * (ep.n - gcol < per ? ep.n - gcol : per);
-      src += (static_cast<int64_t>(grow) * ep.ldr + gcol) * esz;
-    }
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(buf + swz(r, p))),
-                 "l"(src), "r"(bytes)
-                 : "memory");
+// Residual chunks (32 rows x 64 bytes, the output's type) arrive by TMA tile loads
+// into the same swizzled staging layout, one mbarrier per staging buffer; rows or
+// columns outside the matrix read as zero.  Lane 0 issues, every lane waits.
+__device__ __forceinline__ void residual_load(const CUtensorMap* map_res, uint64_t* bar,
+                                              uint8_t* buf, int col0, int row0) {
+  if ((threadIdx.x & 31) == 0) {
+    mbar_expect_tx(bar, EPI_BUF);
+    tma_load_2d(map_res, bar, buf, col0, row0);
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Waits for a residual chunk in buffer b (bounded); false after a timeout.  Bit b of
+// `phases` is the parity buffer b's barrier completes next.
+__device__ __forceinline__ bool residual_wait(uint64_t* bar, uint32_t& phases, int b) {
+  const bool ok = mbar_wait(bar, (phases >> b) & 1u);
+  phases ^= 1u << b;
+  return ok;
 }
 
 // Adds the staged residual row of this lane to v (the copies are complete).
@@ -303,6 +299,16 @@ __device__ __forceinline__ void add_residual_row(const uint8_t* buf, float* v) {
 
 // ---- epilogue of one tile (warps 2..9, 256 threads) ----------------------------------
 
+// A warp's epilogue resources: tensor maps of the output and the residual, and the
+// residual barriers of its two staging buffers with their phases.
+struct EpiWarp {
+  const CUtensorMap* map_out;
+  const CUtensorMap* map_res;
+  uint64_t* res_bar;     // [2]
+  uint32_t res_phases;   // bit b: parity of buffer b's next completion
+  bool ok;               // false once a residual wait timed out
+};
+
 // Epilogue warp w owns TMEM lanes 32 (w % 4) .. +31 (the hardware's lane quadrant
 // for warp w) and columns 128 ((w - 2) / 4) .. +127 of the tile.
 __device__ __forceinline__ int epi_quad(int warp) { return warp & 3; }
@@ -310,13 +316,14 @@ __device__ __forceinline__ int epi_col0(int warp) { return ((warp - 2) >> 2) * (
 
 // Starts the warp's first residual chunk and stages the tile's bias (fp32) in
 // shared memory.
-__device__ __forceinline__ void epilogue_begin(const Epilogue& ep, uint8_t* stage, float* bias_s,
-                                               int epi_tid, int row0, int n0, int cbase) {
+__device__ __forceinline__ void epilogue_begin(const Epilogue& ep, EpiWarp& io, uint8_t* stage,
+                                               float* bias_s, int epi_tid, int row0, int n0,
+                                               int cbase) {
   // The previous tile's stores have read the staging buffers; then the first
   // residual chunk streams in while the accumulator is computed.
   if ((threadIdx.x & 31) == 0) tma_store_wait_read<0>();
   __syncwarp();
-  if (ep.residual) prefetch_residual(stage, ep, row0, n0 + cbase);
+  if (ep.residual) residual_load(io.map_res, &io.res_bar[0], stage, n0 + cbase, row0);
   // The previous tile's readers of bias_s are past this barrier.
   asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory");
   for (int c = epi_tid; c < BN; c += EPI_THREADS) {
@@ -341,10 +348,7 @@ __device__ __forceinline__ bool epilogue_wait(uint64_t* acc_full, uint32_t parit
       : "=r"(any_timed_out)
       : "r"(timed_out), "n"(EPI_THREADS)
       : "memory");
-  if (any_timed_out) {
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    return false;
-  }
+  if (any_timed_out) return false;
   fence_after();
   return true;
 }
@@ -353,9 +357,9 @@ __device__ __forceinline__ bool epilogue_wait(uint64_t* acc_full, uint32_t parit
 // 32 rows x 128 columns (tile columns cbase .. cbase + 127; taddr: the warp's lane
 // quadrant and accumulator buffer), in 64-byte-row chunks of CW columns.
 template <typename T>
-__device__ __forceinline__ void epilogue_cols(const Epilogue& ep, const CUtensorMap* map_out,
-                                              uint32_t taddr, uint8_t* stage, const float* bias_s,
-                                              int row0, int n0, int cbase) {
+__device__ __forceinline__ void epilogue_cols(const Epilogue& ep, EpiWarp& io, uint32_t taddr,
+                                              uint8_t* stage, const float* bias_s, int row0, int n0,
+                                              int cbase) {
   constexpr int CW = 64 / static_cast<int>(sizeof(T));
   constexpr int CHUNKS = (BN / 2) / CW;
   const int lane = threadIdx.x & 31;
@@ -371,9 +375,8 @@ __device__ __forceinline__ void epilogue_cols(const Epilogue& ep, const CUtensor
     }
     tmem_wait_ld();
     if (ep.residual) {
-      // This chunk's residual has landed (it was started one chunk earlier).
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-      __syncwarp();
+      // This chunk's residual (started one chunk earlier) has landed.
+      if (!residual_wait(&io.res_bar[c & 1], io.res_phases, c & 1)) io.ok = false;
     }
     const bool live = n0 + c0 < ep.n;
     float v[CW];
@@ -391,23 +394,25 @@ __device__ __forceinline__ void epilogue_cols(const Epilogue& ep, const CUtensor
     if (lane == 0) tma_store_wait_read<0>();
     __syncwarp();
     if (ep.residual && c + 1 < CHUNKS)
-      prefetch_residual(stage + ((c + 1) & 1) * EPI_BUF, ep, row0, n0 + c0 + CW);
-    if (live) store_chunk<T>(cur, v, map_out, row0, n0 + c0);
+      residual_load(io.map_res, &io.res_bar[(c + 1) & 1], stage + ((c + 1) & 1) * EPI_BUF,
+                    n0 + c0 + CW, row0);
+    if (live) store_chunk<T>(cur, v, io.map_out, row0, n0 + c0);
   }
 }
 
-__device__ __forceinline__ void epilogue_tile(const Epilogue& ep, const CUtensorMap* map_out,
-                                              uint32_t taddr, uint8_t* stage, const float* bias_s,
-                                              int row0, int n0, int cbase) {
-  if (ep.out_fp32) epilogue_cols<float>(ep, map_out, taddr, stage, bias_s, row0, n0, cbase);
-  else epilogue_cols<__nv_bfloat16>(ep, map_out, taddr, stage, bias_s, row0, n0, cbase);
+__device__ __forceinline__ void epilogue_tile(const Epilogue& ep, EpiWarp& io, uint32_t taddr,
+                                              uint8_t* stage, const float* bias_s, int row0, int n0,
+                                              int cbase) {
+  if (ep.out_fp32) epilogue_cols<float>(ep, io, taddr, stage, bias_s, row0, n0, cbase);
+  else epilogue_cols<__nv_bfloat16>(ep, io, taddr, stage, bias_s, row0, n0, cbase);
 }
 
 // ---- the kernel ------------------------------------------------------------------
 
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-                const __grid_constant__ CUtensorMap map_out, const Epilogue ep) {
+                const __grid_constant__ CUtensorMap map_out,
+                const __grid_constant__ CUtensorMap map_res, const Epilogue ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -419,8 +424,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* acc_full = empty + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint64_t* drained = acc_empty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
-  float* bias_s = reinterpret_cast<float*>(epi_stage + EPI_STAGE_BYTES + 256);
+  uint64_t* res_bars = drained + 1;  // [EPI_WARPS][2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(res_bars + 2 * EPI_WARPS);
+  float* bias_s = reinterpret_cast<float*>(epi_stage + EPI_STAGE_BYTES + BAR_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -439,6 +445,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&acc_empty[b], EPI_WARPS);
     }
     mbar_init(drained, 1);
+    for (int b = 0; b < 2 * EPI_WARPS; ++b) mbar_init(&res_bars[b], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -528,6 +535,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int cbase = epi_col0(warp);
     const int epi_tid = threadIdx.x - 64;  // 0..255
     uint8_t* stage = epi_stage + (warp - 2) * 2 * EPI_BUF;
+    EpiWarp io{&map_out, &map_res, res_bars + 2 * (warp - 2), 0u, true};
     int iter = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
       const int tm = t / tiles_n, tn = t - tm * tiles_n;
@@ -535,22 +543,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int buf = iter & 1;
       const uint32_t use = static_cast<uint32_t>(iter >> 1);
       const int row0 = tm * BM + quad * 32;
-      epilogue_begin(ep, stage, bias_s, epi_tid, row0, n0, cbase);
+      epilogue_begin(ep, io, stage, bias_s, epi_tid, row0, n0, cbase);
       if (!epilogue_wait(&acc_full[buf], use & 1u)) {
         failed = true;
         break;
       }
-      epilogue_tile(ep, &map_out,
+      epilogue_tile(ep, io,
                     tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                         static_cast<uint32_t>(buf * BN),
                     stage, bias_s, row0, n0, cbase);
+      if (!io.ok) failed = true;
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
     if (lane == 0) tma_store_wait_all();  // stores complete before the CTA leaves
   }
-  if (failed && ep.error) atomicExch(ep.error, 1);
+  if (failed) {
+    if (ep.error) atomicExch(ep.error, 1);
+    // Let copies still in flight land before the CTA leaves (bounded).
+    const uint64_t t0 = now_ns();
+    while (now_ns() - t0 < 100'000ull) {
+    }
+  }
   fence_before();
   __syncthreads();
   fence_after();
@@ -577,7 +592,7 @@ constexpr int P_BN_HALF = BN / 2;                    // weight rows loaded per C
 constexpr int P_STAGES = 6;
 constexpr int P_B_BYTES = P_BN_HALF * BK * 2;        // 16 KB
 constexpr int P_STAGE_BYTES = A_BYTES + P_B_BYTES;   // 32 KB
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ +
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + BAR_BYTES +
                              BN * 4 /*bias*/ + EPI_STAGE_BYTES;
 static_assert(P_SMEM_BYTES <= 232448, "fits the opt-in shared memory of one CTA");
 
@@ -639,7 +654,8 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_w,
-                     const __grid_constant__ CUtensorMap map_out, const Epilogue ep) {
+                     const __grid_constant__ CUtensorMap map_out,
+                     const __grid_constant__ CUtensorMap map_res, const Epilogue ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -649,8 +665,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   uint64_t* acc_full = empty + P_STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;     // [2], CTA 0's counts both CTAs' warps
   uint64_t* drained = acc_empty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
-  float* bias_s = reinterpret_cast<float*>(epi_stage + EPI_STAGE_BYTES + 256);
+  uint64_t* res_bars = drained + 1;  // [EPI_WARPS][2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(res_bars + 2 * EPI_WARPS);
+  float* bias_s = reinterpret_cast<float*>(epi_stage + EPI_STAGE_BYTES + BAR_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -672,6 +689,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_init(&acc_empty[b], 2 * EPI_WARPS);  // both CTAs' epilogue warps (used in CTA 0)
     }
     mbar_init(drained, 1);
+    for (int b = 0; b < 2 * EPI_WARPS; ++b) mbar_init(&res_bars[b], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {  // both CTAs allocate together, same warp, same holder offset
@@ -764,6 +782,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int cbase = epi_col0(warp);
     const int epi_tid = threadIdx.x - 64;
     uint8_t* stage = epi_stage + (warp - 2) * 2 * EPI_BUF;
+    EpiWarp io{&map_out, &map_res, res_bars + 2 * (warp - 2), 0u, true};
     int iter = 0;
     for (int t = pair; t < tiles; t += pairs, ++iter) {
       const int tm = t / tiles_n, tn = t - tm * tiles_n;
@@ -771,15 +790,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int buf = iter & 1;
       const uint32_t use = static_cast<uint32_t>(iter >> 1);
       const int row0 = tm * 2 * BM + static_cast<int>(rank) * BM + quad * 32;
-      epilogue_begin(ep, stage, bias_s, epi_tid, row0, n0, cbase);
+      epilogue_begin(ep, io, stage, bias_s, epi_tid, row0, n0, cbase);
       if (!epilogue_wait(&acc_full[buf], use & 1u)) {
         failed = true;
         break;
       }
-      epilogue_tile(ep, &map_out,
+      epilogue_tile(ep, io,
                     tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                         static_cast<uint32_t>(buf * BN),
                     stage, bias_s, row0, n0, cbase);
+      if (!io.ok) failed = true;
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(peer_addr(&acc_empty[buf], 0));
@@ -922,8 +942,14 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
   }
   Epilogue ep{bias, residual, ldr, out, ldo, out_fp32 ? 1 : 0, bias_fp32 ? 1 : 0, act, act_after,
               static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), error};
-  CUtensorMap ma, mw, mo;
+  CUtensorMap ma, mw, mo, mr;
   if (!make_out_map(&mo, out, m, n, ldo, out_fp32 != 0)) return CUGO_B200_ERR_LAUNCH;
+  if (residual) {
+    if (!make_out_map(&mr, const_cast<void*>(residual), m, n, ldr, out_fp32 != 0))
+      return CUGO_B200_ERR_LAUNCH;
+  } else {
+    mr = mo;  // unused
+  }
   // The pair kernel halves the weight bytes each SM streams per FLOP, which pays
   // when the K loop is long (measured: 262144x2048x2048 1,425 vs 1,317 TFLOP/s);
   // with K <= 720 the epilogue bounds both kernels and the single one is faster.
@@ -934,12 +960,12 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
     // 256 x 256 tiles, one CTA pair per tile, persistent over the co-resident pairs.
     const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
     const int64_t pairs = tiles < max_pairs(dev) ? tiles : max_pairs(dev);
-    gemm_pair_kernel<<<static_cast<unsigned>(2 * pairs), THREADS, P_SMEM_BYTES, stream>>>(ma, mw, mo,
-                                                                                          ep);
+    gemm_pair_kernel<<<static_cast<unsigned>(2 * pairs), THREADS, P_SMEM_BYTES, stream>>>(
+        ma, mw, mo, mr, ep);
   } else {
     const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mo, ep);
+    gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mo, mr, ep);
   }
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }
