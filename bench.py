@@ -414,6 +414,9 @@ def main():
         if args.arch != "2048x4":
             extras["config3_2048x4"] = arch_bench(ext, "2048x4", args.games)
         extras["config4_seq"] = seq_bench()
+        from cugo_b200.kernel_cases import ppo_case
+        extras["ppo_update"] = {"minibatch": 32768, "networks": "3x512 actor + critic (SiLU)",
+                                **ppo_case(32768, warmup=3, iters=10)}
     peaks = measured_peaks()
     if "engine_only" in extras:
         e = extras["engine_only"]

@@ -16,6 +16,9 @@ FLOPs of one launch:
                        N queries at uniform positions 0..49: (pos + 3) * 1,024 B per query
   seqwave   W WAVES    sequence self-play (4-layer d256 policy), WAVES waves of W games
   seqops    W          each op of one sequence decision step at wave size W, timed alone
+  ppo       B          one PPO minibatch step (3x512 actor + critic, B rows) on the fused
+                       networks, and the same step with plain PyTorch modules under bf16
+                       autocast (cuBLAS) for comparison
 """
 from __future__ import annotations
 
@@ -52,6 +55,78 @@ def _mid_game(ext, rows: int, decisions: int = 6):
     for _ in range(decisions):
         ext.selfplay_random_step(states, game, dec, done, steps, feats, legal)
     return states, feats, legal
+
+
+def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
+    """One PPO minibatch step (3x512 actor + critic, b rows) on the fused networks,
+    eager and CUDA-graphed, and the same step with plain PyTorch modules under bf16
+    autocast (cuBLAS), eager and graphed.  FLOPs: 3 x 2 x b x weights (forward,
+    data gradient, weight gradient)."""
+    from .ppo import GraphedPpoStep, Minibatch, PpoStep, critic_input, fused_actor, fused_critic
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cpu").manual_seed(0)
+    legal = torch.rand((b, 179), generator=g) < 0.1
+    legal[:, 0] = True
+    mb = Minibatch(features=torch.rand((b, 720), generator=g).to(dev, torch.bfloat16),
+                   legal=legal.to(dev), actions=torch.zeros(b, dtype=torch.int64, device=dev),
+                   logp_old=torch.full((b,), -2.0, device=dev),
+                   opp_hand=torch.randint(0, 1 << 50, (b,), generator=g).to(dev),
+                   adv=torch.randn(b, generator=g).to(dev), ret=torch.randn(b, generator=g).to(dev))
+    actor, critic = fused_actor().to(dev), fused_critic().to(dev)
+    opt = torch.optim.Adam(list(actor.parameters()) + list(critic.parameters()), lr=3e-4,
+                           capturable=True)
+    step = PpoStep(actor, critic, opt)
+    sec_eager = _time(lambda: step.step(mb), warmup, iters)
+    graphed = GraphedPpoStep(step, mb)
+    sec = _time(lambda: graphed(mb), warmup, iters)
+
+    def torch_mlp(inputs, outputs):
+        layers = [torch.nn.Linear(inputs, 512)] + [torch.nn.Linear(512, 512) for _ in range(6)]
+        layers.append(torch.nn.Linear(512, outputs))
+        return torch.nn.ModuleList(layers).to(dev)
+
+    def run_torch(net, x):
+        h = net[0](x)
+        for i in range(3):
+            h = h + net[2 + 2 * i](torch.nn.functional.silu(net[1 + 2 * i](h)))
+        return net[-1](torch.nn.functional.silu(h))
+
+    ta, tc = torch_mlp(720, 179), torch_mlp(770, 1)
+    topt = torch.optim.Adam(list(ta.parameters()) + list(tc.parameters()), lr=3e-4,
+                            capturable=True)
+    cin = critic_input(mb.features, mb.opp_hand)
+
+    def torch_step():
+        topt.zero_grad(set_to_none=False)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = run_torch(ta, mb.features.float()).float()
+            value = run_torch(tc, cin.float()).float().squeeze(-1)
+        lp = torch.log_softmax(logits.masked_fill(~mb.legal, -1.0e30), 1)
+        ratio = (lp.gather(1, mb.actions.unsqueeze(1)).squeeze(1) - mb.logp_old).exp()
+        pl = -torch.min(ratio * mb.adv, ratio.clamp(0.8, 1.2) * mb.adv).mean()
+        ent = -(lp.exp() * lp).sum(1).mean()
+        loss = pl - 0.05 * ent + 0.5 * torch.nn.functional.smooth_l1_loss(value, mb.ret)
+        loss.backward()
+        for grp in (list(ta.parameters()), list(tc.parameters())):
+            torch.nn.utils.clip_grad_norm_(grp, 1.0, foreach=True)
+        topt.step()
+
+    sec_torch_eager = _time(torch_step, warmup, iters)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            torch_step()
+    torch.cuda.current_stream().wait_stream(side)
+    tgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(tgraph):
+        torch_step()
+    sec_torch = _time(tgraph.replay, warmup, iters)
+    flops = 3 * 2 * b * sum(p.numel() for n, p in list(actor.named_parameters()) +
+                            list(critic.named_parameters()) if n.endswith("weight"))
+    return dict(seconds=sec, tflops=flops / sec / 1e12, eager_seconds=sec_eager,
+                torch_autocast_seconds=sec_torch, torch_autocast_tflops=flops / sec_torch / 1e12,
+                torch_autocast_eager_seconds=sec_torch_eager)
 
 
 def main() -> None:
@@ -202,6 +277,9 @@ def main() -> None:
             res[name] = round(_time(graph.replay, args.warmup, args.iters) * 1e6 / 20, 2)
             del graph
         out.update(us=res)
+    elif args.case == "ppo":
+        (b,) = d
+        out.update(ppo_case(b, args.warmup, args.iters))
     elif args.case == "sample":
         (rows,) = d
         logits = torch.randn((rows, 180), device=dev)

@@ -1,0 +1,316 @@
+"""PPO update path on the native GEMMs: the actor/critic training step of the
+reference's PpoUpdater (python/cugo_ppo50.py:514-745) with residual-MLP networks
+whose forward runs on the fused tcgen05 GEMM.
+
+FusedResidualMlp has the parameter layout of the reference's ResidualMlp with
+norm="none" (python/cugo_ppo_nets50.py:26-64: inp, blocks.i.fc1/fc2, out), so
+PpoActor / OracleCritic state dicts load one to one.  Its autograd function:
+
+  forward   h = inp(x); per block z = fc1(h), u = act(z), h = h + fc2(u);
+            out = head(act(h)) -- every Linear is one launch of the fused GEMM
+            (bias and residual in the epilogue, fp32 bias, bf16 activations);
+  backward  data gradients on the same GEMM with the transposed weights (the
+            residual add of dh fused into the epilogue), weight gradients
+            dW = dY^T X on cuBLAS (a plain library GEMM: the reduction runs over
+            the minibatch), act' and bias sums in torch.
+
+Numerics follow the reference under bf16 autocast: bf16 operands and saved
+activations, fp32 accumulation, bf16-rounded weight gradients accumulated into
+fp32 parameters.  Data parallelism: gradients of every rank are averaged with one
+all-reduce of a flat bucket (NCCL on the GPU box, any torch.distributed backend).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+from torch import nn
+
+from .ext import load_extension
+
+FEATURES, ACTIONS, ORACLE_FEATURES = 720, 179, 50
+_ACT = {"relu": 1, "silu": 2}
+
+
+def _pad8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+def _act(z: torch.Tensor, kind: str) -> torch.Tensor:
+    return F.silu(z) if kind == "silu" else F.relu(z)
+
+
+def _act_backward(grad: torch.Tensor, z: torch.Tensor, kind: str) -> torch.Tensor:
+    """grad * act'(z), one fused elementwise kernel (bf16 in and out)."""
+    if kind == "relu":
+        return torch.ops.aten.threshold_backward(grad, z, 0)
+    return torch.ops.aten.silu_backward(grad, z)
+
+
+class _Block(nn.Module):
+    def __init__(self, hidden: int) -> None:
+        super().__init__()
+        self.norm = nn.Identity()
+        self.fc1 = nn.Linear(hidden, hidden)
+        self.fc2 = nn.Linear(hidden, hidden)
+
+
+class _FusedMlpFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, net: "FusedResidualMlp", *params):
+        ext = net.ext
+        kind, act = net.activation, _ACT[net.activation]
+        m = x.shape[0]
+        dev = x.device
+        ws = [p.detach().to(torch.bfloat16) for p in params[0::2]]
+        bs = [p.detach() for p in params[1::2]]  # fp32 biases, used by the epilogue as is
+        # Input rows padded to a multiple of 16 bytes (the TMA row-stride rule).
+        kin = _pad8(x.shape[1])
+        xb = torch.zeros((m, kin), dtype=torch.bfloat16, device=dev)
+        xb[:, :x.shape[1]] = x
+        w_in = torch.zeros((ws[0].shape[0], kin), dtype=torch.bfloat16, device=dev)
+        w_in[:, :ws[0].shape[1]] = ws[0]
+        h = ext.linear(xb, w_in, bs[0])
+        saved = [xb]
+        for i in range(net.n_blocks):
+            w1, b1, w2, b2 = ws[1 + 2 * i], bs[1 + 2 * i], ws[2 + 2 * i], bs[2 + 2 * i]
+            z = ext.linear(h, w1, b1)
+            u = _act(z, kind)
+            h_next = ext.linear(u, w2, b2, residual=h)
+            saved += [h, z, u]
+            h = h_next
+        g = _act(h, kind)
+        out_w, out_b = ws[-1], bs[-1]
+        n_out = out_w.shape[0]
+        ld = (n_out + 3) // 4 * 4
+        out = torch.empty((m, ld), dtype=torch.float32, device=dev)
+        ext.linear(g, out_w, out_b, out=out[:, :n_out])
+        saved += [h, g]
+        ctx.save_for_backward(*saved)
+        ctx.net = net
+        ctx.weights = ws
+        ctx.in_features = x.shape[1]
+        return out[:, :n_out].contiguous()
+
+    @staticmethod
+    def backward(ctx, dout):
+        net = ctx.net
+        ext = net.ext
+        kind = net.activation
+        ws = ctx.weights
+        saved = list(ctx.saved_tensors)
+        xb = saved[0]
+        h_last, g = saved[-2], saved[-1]
+        grads_w: list[torch.Tensor] = [None] * len(ws)
+        grads_b: list[torch.Tensor] = [None] * len(ws)
+        # Head: out = g W^T + b.
+        dy = dout.to(torch.bfloat16)
+        grads_w[-1] = torch.matmul(dy.t(), g).float()
+        grads_b[-1] = dout.sum(0, dtype=torch.float32)
+        dg = torch.matmul(dy, ws[-1])  # [M, H]; K = outputs is small: cuBLAS
+        dh = _act_backward(dg, h_last, kind)
+        for i in reversed(range(net.n_blocks)):
+            h, z, u = saved[1 + 3 * i], saved[2 + 3 * i], saved[3 + 3 * i]
+            w1, w2 = ws[1 + 2 * i], ws[2 + 2 * i]
+            # h_next = h + u W2^T + b2
+            grads_w[2 + 2 * i] = torch.matmul(dh.t(), u).float()
+            grads_b[2 + 2 * i] = dh.sum(0, dtype=torch.float32)
+            du = ext.linear(dh, w2.t().contiguous())              # dh W2, on the tcgen05 GEMM
+            dz = _act_backward(du, z, kind)
+            grads_w[1 + 2 * i] = torch.matmul(dz.t(), h).float()
+            grads_b[1 + 2 * i] = dz.sum(0, dtype=torch.float32)
+            dh = ext.linear(dz, w1.t().contiguous(), residual=dh)  # dh + dz W1
+        gw_in = torch.matmul(dh.t(), xb).float()
+        grads_w[0] = gw_in[:, :ctx.in_features].contiguous()
+        grads_b[0] = dh.sum(0, dtype=torch.float32)
+        out = []
+        for gw, gb in zip(grads_w, grads_b):
+            out += [gw, gb]
+        return (None, None, *out)
+
+
+class FusedResidualMlp(nn.Module):
+    """ResidualMlp (norm "none") whose forward and data gradients run on the fused
+    tcgen05 GEMM.  squeeze: return [M] for a single output (OracleCritic)."""
+
+    def __init__(self, inputs: int, outputs: int, hidden: int = 512, blocks: int = 3,
+                 activation: str = "silu", squeeze: bool = False, zero_out: bool = False) -> None:
+        super().__init__()
+        if activation not in _ACT:
+            raise ValueError("activation must be relu or silu")
+        self.activation, self.n_blocks, self.squeeze = activation, blocks, squeeze
+        self.inp = nn.Linear(inputs, hidden)
+        self.blocks = nn.Sequential(*(_Block(hidden) for _ in range(blocks)))
+        self.norm = nn.Identity()
+        self.out = nn.Linear(hidden, outputs)
+        # The reference's norm="none" initialisation: zero residual branches; the
+        # actor also zeroes its output layer (python/cugo_ppo_nets50.py:34-36,61-62).
+        for b in self.blocks:
+            nn.init.zeros_(b.fc2.weight)
+            nn.init.zeros_(b.fc2.bias)
+        if zero_out:
+            nn.init.zeros_(self.out.weight)
+            nn.init.zeros_(self.out.bias)
+        self._ext = None
+
+    @property
+    def ext(self):
+        if self._ext is None:
+            self._ext = load_extension()
+        return self._ext
+
+    def linears(self) -> list[nn.Linear]:
+        return [self.inp] + [l for b in self.blocks for l in (b.fc1, b.fc2)] + [self.out]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        params = [t for l in self.linears() for t in (l.weight, l.bias)]
+        out = _FusedMlpFunction.apply(x.to(torch.bfloat16), self, *params)
+        return out.squeeze(-1) if self.squeeze and out.shape[-1] == 1 else out
+
+
+def fused_actor(hidden: int = 512, blocks: int = 3) -> FusedResidualMlp:
+    """PpoActor's shape: 720 features -> 179 logits, zero-initialised output layer."""
+    return FusedResidualMlp(FEATURES, ACTIONS, hidden, blocks, "silu", zero_out=True)
+
+
+def fused_critic(hidden: int = 512, blocks: int = 3) -> FusedResidualMlp:
+    """OracleCritic's shape without stock planes: 770 inputs -> one value."""
+    return FusedResidualMlp(FEATURES + ORACLE_FEATURES, 1, hidden, blocks, "silu", squeeze=True)
+
+
+def critic_input(features: torch.Tensor, opp_hand: torch.Tensor) -> torch.Tensor:
+    """[features, one-hot plane of the opponent's hand] as bf16 (the reference's
+    _critic_input, python/cugo_ppo50.py:478-482, without stock planes)."""
+    bits = torch.arange(ORACLE_FEATURES, device=opp_hand.device)
+    plane = ((opp_hand.view(-1, 1) >> bits) & 1).to(torch.bfloat16)
+    return torch.cat((features.to(torch.bfloat16), plane), 1)
+
+
+def allreduce_gradients(params: list[torch.Tensor], world: int) -> None:
+    """Averages the gradients of `params` over the ranks with one all-reduce of a
+    flat bucket (the data-parallel step of the update; a no-op for one rank)."""
+    if world <= 1:
+        return
+    grads = [p.grad for p in params if p.grad is not None]
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    dist.all_reduce(flat)
+    flat.div_(world)
+    off = 0
+    for g in grads:
+        g.copy_(flat[off:off + g.numel()].view_as(g))
+        off += g.numel()
+
+
+@dataclass
+class Minibatch:
+    features: torch.Tensor  # bf16 [B, 720]
+    legal: torch.Tensor     # bool [B, 179]
+    actions: torch.Tensor   # int64 [B]
+    logp_old: torch.Tensor  # fp32 [B]
+    opp_hand: torch.Tensor  # int64 [B]
+    adv: torch.Tensor       # fp32 [B]
+    ret: torch.Tensor       # fp32 [B]
+
+
+class PpoStep:
+    """One PPO minibatch update (python/cugo_ppo50.py:558-623, the plain policy
+    target): clipped surrogate, entropy bonus, smooth-L1 value loss, gradient
+    clipping per network, the optimizer step and the running statistics
+    (policy, value, entropy, KL, clip fraction, count)."""
+
+    def __init__(self, actor: nn.Module, critic: nn.Module, optimizer: torch.optim.Optimizer,
+                 clip: float = 0.2, value_coef: float = 0.5, grad_clip: float = 1.0,
+                 world: int = 1) -> None:
+        self.actor, self.critic, self.optimizer = actor, critic, optimizer
+        self.clip, self.value_coef, self.grad_clip, self.world = clip, value_coef, grad_clip, world
+        self.groups = [list(actor.parameters()), list(critic.parameters())]
+        dev = next(actor.parameters()).device
+        self.entropy_coef = torch.zeros((), device=dev)
+        self.sums = torch.zeros(6, device=dev)
+
+    def losses(self, mb: Minibatch):
+        logits = self.actor(mb.features).float()
+        value = self.critic(critic_input(mb.features, mb.opp_hand)).float()
+        log_probs = torch.log_softmax(logits.masked_fill(~mb.legal, -1.0e30), dim=1)
+        new_logp = log_probs.gather(1, mb.actions.unsqueeze(1)).squeeze(1)
+        log_ratio = new_logp - mb.logp_old
+        ratio = log_ratio.exp()
+        surrogate = torch.minimum(ratio * mb.adv, ratio.clamp(1 - self.clip, 1 + self.clip) * mb.adv)
+        policy_loss = -surrogate.mean()
+        entropy = -(log_probs.exp() * log_probs).sum(1).mean()
+        value_loss = F.smooth_l1_loss(value, mb.ret)
+        return policy_loss, value_loss, entropy, ratio, log_ratio
+
+    def step(self, mb: Minibatch) -> None:
+        """One update, eager (every kernel launched from Python)."""
+        self.optimizer.zero_grad(set_to_none=False)
+        policy_loss, value_loss, entropy, ratio, log_ratio = self.losses(mb)
+        loss = policy_loss - self.entropy_coef * entropy + self.value_coef * value_loss
+        loss.backward()
+        allreduce_gradients([p for g in self.groups for p in g], self.world)
+        for group in self.groups:
+            nn.utils.clip_grad_norm_(group, self.grad_clip, foreach=True)
+        self.optimizer.step()
+        with torch.no_grad():
+            kl = ((ratio - 1) - log_ratio).mean()
+            self.sums += torch.stack((policy_loss.detach(), value_loss.detach(), entropy.detach(), kl,
+                                      ((ratio - 1).abs() > self.clip).float().mean(),
+                                      torch.ones_like(kl)))
+
+
+class GraphedPpoStep:
+    """PpoStep captured once as a CUDA graph over static minibatch buffers and
+    replayed per minibatch, as the reference's PpoUpdater._run does
+    (python/cugo_ppo50.py:625-657): three warm-up steps on a side stream, the
+    weights and optimizer moments restored, one captured step.  The optimizer must
+    be capturable (torch.optim.Adam(..., capturable=True)); data-parallel runs
+    (world > 1) step eagerly."""
+
+    def __init__(self, step: PpoStep, template: Minibatch) -> None:
+        self.step = step
+        self.static = Minibatch(*(t.clone() for t in (
+            template.features, template.legal, template.actions, template.logp_old,
+            template.opp_hand, template.adv, template.ret)))
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    def _capture(self) -> None:
+        st = self.step
+        params = [p for g in st.groups for p in g]
+        saved_sums = st.sums.clone()
+        weights = [p.detach().clone() for p in params]
+        moments = {p: {k: v.clone() for k, v in st.optimizer.state[p].items() if torch.is_tensor(v)}
+                   for p in params if p in st.optimizer.state}
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                st.step(self.static)
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.no_grad():  # undo the warm-up updates in place (the graph keeps these tensors)
+            for p, w in zip(params, weights):
+                p.copy_(w)
+            for p in params:
+                before = moments.get(p)
+                for k, v in st.optimizer.state[p].items():
+                    if torch.is_tensor(v):
+                        v.copy_(before[k]) if before is not None else v.zero_()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            st.step(self.static)
+        st.sums.copy_(saved_sums)
+
+    def __call__(self, mb: Minibatch) -> None:
+        if self.step.world > 1:
+            self.step.step(mb)
+            return
+        for dst, src in zip((self.static.features, self.static.legal, self.static.actions,
+                             self.static.logp_old, self.static.opp_hand, self.static.adv,
+                             self.static.ret),
+                            (mb.features, mb.legal, mb.actions, mb.logp_old, mb.opp_hand, mb.adv,
+                             mb.ret)):
+            dst.copy_(src)
+        if self.graph is None:
+            self._capture()
+        self.graph.replay()

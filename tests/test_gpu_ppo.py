@@ -1,0 +1,139 @@
+"""GPU: the PPO update path (python/cugo_ppo50.py:514-745) on the fused GEMMs.
+
+Gradients of FusedResidualMlp are compared with the same network in plain PyTorch:
+their error against the exact fp32 gradients must be no larger (x1.5) than that of
+the reference's own bf16-autocast backward, plus 1e-3 of the gradient scale.  A full
+PPO minibatch step is compared with a restatement of the reference's step under
+autocast: the three losses within 1e-2 relative and, per network, the clipped
+gradients at cosine similarity >= 0.999.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from tests.torch_reference import TorchResidualMlp, ppo_losses_reference
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def _twins(inputs, outputs, hidden=512, blocks=3, activation="silu", seed=0, squeeze=False):
+    from cugo_b200.ppo import FusedResidualMlp
+    torch.manual_seed(seed)
+    ref = TorchResidualMlp(inputs, outputs, hidden, blocks, activation).to(DEV)
+    with torch.no_grad():
+        for p in ref.parameters():  # non-zero everywhere so every gradient flows
+            p.copy_((torch.randn_like(p) * (1.0 / p.shape[-1]) ** 0.5).to(torch.bfloat16).float())
+    fused = FusedResidualMlp(inputs, outputs, hidden, blocks, activation, squeeze=squeeze).to(DEV)
+    fused.load_state_dict(ref.state_dict())  # same parameter names as the reference module
+    return fused, ref
+
+
+def _grads(module):
+    return [p.grad.detach().float().clone() for p in module.parameters()]
+
+
+@pytest.mark.parametrize("inputs,outputs,activation", [(720, 179, "silu"), (770, 1, "silu"),
+                                                      (720, 179, "relu")])
+def test_fused_mlp_gradients_match_torch(inputs, outputs, activation):
+    fused, ref = _twins(inputs, outputs, activation=activation)
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn((4096, inputs), generator=g).to(DEV, torch.bfloat16)
+    r = torch.randn((4096, outputs), generator=g).to(DEV)
+    (fused(x).float() * r).sum().backward()
+    ours = _grads(fused)
+    (ref(x.float()) * r).sum().backward()
+    exact = _grads(ref)
+    ref.zero_grad()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = ref(x.float())
+    (out.float() * r).sum().backward()
+    auto = _grads(ref)
+    for (name, _), a, e, h in zip(fused.named_parameters(), ours, exact, auto):
+        scale = float(e.abs().max())
+        err, err_ref = float((a - e).abs().max()), float((h - e).abs().max())
+        assert err <= 1.5 * err_ref + 1e-3 * scale, (name, err, err_ref, scale)
+
+
+def test_critic_input_and_squeeze():
+    from cugo_b200.ppo import critic_input, fused_critic
+    feats = torch.rand((5, 720), device=DEV).to(torch.bfloat16)
+    hand = torch.tensor([0, 1, 3, (1 << 49), (1 << 50) - 1], device=DEV)
+    x = critic_input(feats, hand)
+    assert x.shape == (5, 770)
+    assert torch.equal(x[:, :720], feats)
+    for i, h in enumerate(hand.tolist()):
+        assert x[i, 720:].tolist() == [float((h >> b) & 1) for b in range(50)]
+    assert fused_critic().to(DEV)(x).shape == (5,)
+
+
+def test_ppo_step_matches_reference_step():
+    from cugo_b200.ppo import Minibatch, PpoStep, critic_input
+    actor, actor_ref = _twins(720, 179, seed=2)
+    critic, critic_ref = _twins(770, 1, seed=3, squeeze=True)
+    g = torch.Generator().manual_seed(4)
+    b = 8192
+    legal = torch.rand((b, 179), generator=g) < 0.1
+    legal[:, 0] = True
+    logits0 = torch.randn((b, 179), generator=g)
+    actions = torch.multinomial(torch.softmax(logits0.masked_fill(~legal, -1e30), 1), 1).squeeze(1)
+    mb = Minibatch(features=torch.rand((b, 720), generator=g).to(DEV, torch.bfloat16),
+                   legal=legal.to(DEV), actions=actions.to(DEV),
+                   logp_old=(torch.randn(b, generator=g) * 0.1 - 2.0).to(DEV),
+                   opp_hand=torch.randint(0, 1 << 50, (b,), generator=g).to(DEV),
+                   adv=torch.randn(b, generator=g).to(DEV), ret=torch.randn(b, generator=g).to(DEV))
+    opt = torch.optim.Adam(list(actor.parameters()) + list(critic.parameters()), lr=3e-4)
+    step = PpoStep(actor, critic, opt)
+    step.entropy_coef.fill_(0.05)
+    ours = step.losses(mb)
+    # reference step under autocast (python/cugo_ppo50.py:566-603)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        logits = actor_ref(mb.features.float()).float()
+        value = critic_ref(critic_input(mb.features, mb.opp_hand).float()).float().squeeze(-1)
+    pl, vl, ent = ppo_losses_reference(logits, value, mb.legal, mb.actions, mb.logp_old, mb.adv, mb.ret, 0.2)
+    for a, r in zip(ours[:3], (pl, vl, ent)):
+        assert abs(float(a) - float(r)) <= 1e-2 * abs(float(r)) + 1e-4, (float(a), float(r))
+    loss_ref = pl - 0.05 * ent + 0.5 * vl
+    loss_ref.backward()
+    step.step(mb)  # backward + clip + Adam on the fused networks
+    for fused, ref in ((actor, actor_ref), (critic, critic_ref)):
+        torch.nn.utils.clip_grad_norm_(list(ref.parameters()), 1.0)
+        a = torch.cat([p.grad.flatten() for p in fused.parameters()])
+        r = torch.cat([p.grad.flatten() for p in ref.parameters()])
+        cos = float(torch.dot(a, r) / (a.norm() * r.norm()))
+        assert cos >= 0.999, cos
+    assert int(step.sums[5]) == 1
+
+
+def test_graphed_step_equals_eager_step():
+    from cugo_b200.ppo import GraphedPpoStep, Minibatch, PpoStep
+    nets = []
+    for _ in range(2):
+        actor, _ = _twins(720, 179, seed=5)
+        critic, _ = _twins(770, 1, seed=6, squeeze=True)
+        opt = torch.optim.Adam(list(actor.parameters()) + list(critic.parameters()), lr=3e-4,
+                               capturable=True)
+        nets.append((actor, critic, PpoStep(actor, critic, opt)))
+    g = torch.Generator().manual_seed(7)
+    b = 4096
+
+    def batch():
+        legal = torch.rand((b, 179), generator=g) < 0.2
+        legal[:, 0] = True
+        return Minibatch(features=torch.rand((b, 720), generator=g).to(DEV, torch.bfloat16),
+                         legal=legal.to(DEV), actions=torch.zeros(b, dtype=torch.int64, device=DEV),
+                         logp_old=torch.full((b,), -1.5, device=DEV),
+                         opp_hand=torch.randint(0, 1 << 50, (b,), generator=g).to(DEV),
+                         adv=torch.randn(b, generator=g).to(DEV), ret=torch.randn(b, generator=g).to(DEV))
+
+    batches = [batch() for _ in range(3)]
+    graphed = GraphedPpoStep(nets[1][2], batches[0])
+    for mb in batches:
+        nets[0][2].step(mb)
+        graphed(mb)
+    torch.cuda.synchronize()
+    for a, b2 in zip(list(nets[0][0].parameters()) + list(nets[0][1].parameters()),
+                     list(nets[1][0].parameters()) + list(nets[1][1].parameters())):
+        assert torch.allclose(a, b2, rtol=1e-5, atol=1e-6)
+    assert torch.allclose(nets[0][2].sums, nets[1][2].sums, rtol=1e-5, atol=1e-6)

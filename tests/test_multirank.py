@@ -65,6 +65,32 @@ def _rank_main(rank: int, port: int, out_dir: str) -> None:
         dist.destroy_process_group()
 
 
+def _grad_rank_main(rank: int, port: int, out_dir: str) -> None:
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        from cugo_b200.ppo import allreduce_gradients
+        params = [torch.nn.Parameter(torch.zeros(3, 4)), torch.nn.Parameter(torch.zeros(5))]
+        params[0].grad = torch.full((3, 4), float(rank + 1))
+        params[1].grad = torch.arange(5, dtype=torch.float32) * (rank + 1)
+        allreduce_gradients(params, WORLD)
+        if rank == 0:
+            np.save(Path(out_dir) / "grads.npy",
+                    np.concatenate([params[0].grad.numpy().ravel(), params[1].grad.numpy()]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_allreduce_averages_over_ranks():
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.start_processes(_grad_rank_main, args=(_free_port(), tmp), nprocs=WORLD, join=True,
+                           start_method="spawn")
+        got = np.load(Path(tmp) / "grads.npy")
+    expect = np.concatenate([np.full(12, 1.5), np.arange(5) * 1.5])
+    assert np.allclose(got, expect)
+
+
 def test_blocks_are_disjoint_and_contiguous():
     seen = torch.cat([game_block(s, r, WORLD, GAMES, "cpu") for s in range(STEPS) for r in range(WORLD)])
     assert torch.equal(seen.sort().values, torch.arange(STEPS * WORLD * GAMES))
