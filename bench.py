@@ -166,18 +166,22 @@ def selfplay_bench(args, world, rank, ext, policy):
     for s in range(args.warmup):
         play_batch(ext, policy, blocks[s])
     barrier(world)
-    timer = RoundTimer(enabled=True)
     launches: list[int] = []
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     results = []
     t_start = time.time()
     start.record()
     for s in range(args.warmup, total_steps):
-        results.append(play_batch(ext, policy, blocks[s], timer=timer, launches=launches))
+        results.append(play_batch(ext, policy, blocks[s], launches=launches))
     stop.record()
     barrier(world)
     clocks.mark(t_start, time.time())
     clk = clocks.stop()
+    # The policy's in-loop rate, from CUDA events around every forward of one more
+    # (untimed) step: the events' host work is kept out of the timed region.
+    timer = RoundTimer(enabled=True)
+    play_batch(ext, policy, blocks[args.warmup], timer=timer)
+    torch.cuda.synchronize()
     elapsed = start.elapsed_time(stop) / 1e3
     games = sum(r.games for r in results)
     decisions = sum(r.decisions for r in results)
