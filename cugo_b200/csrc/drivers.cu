@@ -167,6 +167,54 @@ __global__ void __launch_bounds__(kBlock, 5) selfplay_pick_kernel(
   emit_legal(t, legal_out, tile_base, rows_here);
 }
 
+// Redeal of a row for the observer `seat` (the reference's _redeal,
+// python/cugo_ppo50.py:125-149, on the device): the opponent's hand keeps its cards
+// shown by a shake and gets the rest — as many cards as before — drawn uniformly
+// from the cards the observer cannot see (those hand cards and the stock); the stock
+// is what remains; `held` (every card ever in that hand) follows the new hand; the
+// stock's draw stream gets a new seed in [-2^62, 2^62).  Draws: Philox4x32-10 with
+// counter {row lo, row hi, attempt, 8 + k} and key {seed lo, seed hi}: a uniform
+// subset by successive picks of the floor(r * left / 2^32)-th remaining card.
+__global__ void __launch_bounds__(256) redeal_kernel(u64* __restrict__ rows, i64 n,
+                                                     const i64* __restrict__ seats, i64 seed,
+                                                     u32 attempt) {
+  const i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  u64* w = rows + i * kRowWords;
+  const bool s0 = __ldg(seats + i) == 0;  // observer seat 0: the opponent is seat 1
+  const int hw = s0 ? 1 : 0, held_w = s0 ? 21 : 20, rev_w = s0 ? 23 : 22;
+  const u64 hand = w[hw], stock = w[3];
+  const u64 fixed = hand & w[rev_w];
+  const u64 held = w[held_w];
+  const u64 free = hand & ~fixed;
+  u64 left = free | stock;
+  const u32 count = popc(free);
+  u64 picked = 0;
+  u32 remaining = popc(left);
+  const u64 key = static_cast<u64>(seed);
+  Philox4 r{};
+  for (u32 k = 0; k < count; ++k) {
+    if ((k & 3u) == 0)
+      r = philox4x32_10(static_cast<u32>(i), static_cast<u32>(static_cast<u64>(i) >> 32), attempt,
+                        8u + (k >> 2), static_cast<u32>(key), static_cast<u32>(key >> 32));
+    const u32 word = r.v[0] * ((k & 3u) == 0) + r.v[1] * ((k & 3u) == 1) + r.v[2] * ((k & 3u) == 2) +
+                     r.v[3] * ((k & 3u) == 3);
+    const u32 rank = static_cast<u32>((static_cast<u64>(word) * remaining) >> 32);
+    const u64 bit = u64{1} << nth_card(left, rank);
+    picked |= bit;
+    left &= ~bit;
+    --remaining;
+  }
+  const u64 new_hand = fixed | picked;
+  w[3] = (free | stock) & ~picked;
+  w[hw] = new_hand;
+  w[held_w] = (held & ~hand) | new_hand;
+  const Philox4 s = philox4x32_10(static_cast<u32>(i), static_cast<u32>(static_cast<u64>(i) >> 32),
+                                  attempt, 7u, static_cast<u32>(key), static_cast<u32>(key >> 32));
+  const u64 bits63 = ((static_cast<u64>(s.v[0]) << 32) | s.v[1]) >> 1;  // [0, 2^63)
+  w[6] = bits63 - (u64{1} << 62);  // as int64: [-2^62, 2^62)
+}
+
 // Branching roots: game r advanced by k_r < 21 random-legal decisions, stopping
 // before a decision that would finish the game.
 __global__ void __launch_bounds__(kBlock) branch_roots_kernel(i64 n_roots, i64 seed_base,
@@ -259,6 +307,16 @@ int cugo_b200_selfplay_random_step(uint8_t* states, int64_t n_slots, int64_t see
       features, legal, actions);
   if (launch_status() != CUGO_B200_OK) return CUGO_B200_ERR_LAUNCH;
   return cb_step_in_place(states, n_slots, actions, stream);
+}
+
+int cugo_b200_redeal(uint8_t* rows, int64_t n, const int64_t* seats, int64_t seed, int32_t attempt,
+                     cudaStream_t stream) {
+  if (n < 0 || (n > 0 && (!rows || !seats)) || attempt < 0) return CUGO_B200_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(rows) & 7u) return CUGO_B200_ERR_ALIGN;
+  if (n == 0) return CUGO_B200_OK;
+  redeal_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<u64*>(rows), n, seats, seed, static_cast<u32>(attempt));
+  return launch_status();
 }
 
 int cugo_b200_branch_roots(int64_t n_roots, int64_t seed_base, uint8_t* roots, cudaStream_t stream) {

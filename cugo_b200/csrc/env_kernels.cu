@@ -52,7 +52,8 @@ template <typename F>
 __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) observe_kernel(
     const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids, i64 m,
     F* __restrict__ features, i64 ld, int legal_cols, bool* __restrict__ legal,
-    uint8_t* __restrict__ players, bool* __restrict__ done, int16_t* __restrict__ status) {
+    uint8_t* __restrict__ players, bool* __restrict__ done, int16_t* __restrict__ status,
+    int hand_plane = 0) {
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
@@ -72,15 +73,19 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) observe_kernel(
     meta.done = 1;
     meta.status = -1;
   }
-  store_legal(t, meta.legal);
+  // With hand_plane the extra columns carry the hand of the mover's opponent.
+  store_legal(t, hand_plane ? Legal{src >= 0 ? g.hand(meta.player ^ 1u) : 0ull, 0ull, 0ull}
+                            : meta.legal);
   const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
   const i64 left = m - tile_base;
   const int rows_here = left >= 32 ? 32 : (left > 0 ? (int)left : 0);
   emit_features(t, features, ld, tile_base, rows_here);
   if constexpr (sizeof(F) == 2) {
-    if (legal_cols > 0) emit_legal_columns(t, features, ld, tile_base, rows_here, legal_cols);
+    if (legal_cols > 0)
+      emit_legal_columns(t, features, ld, tile_base, rows_here, legal_cols,
+                         hand_plane ? 50u : kActions);
   }
-  emit_legal(t, legal, tile_base, rows_here);
+  if (legal) emit_legal(t, legal, tile_base, rows_here);
   if (row < m) {
     players[row] = static_cast<uint8_t>(meta.player);
     done[row] = meta.done != 0;
@@ -263,6 +268,22 @@ int cugo_b200_observe_query_bf16(const uint8_t* states, int64_t n_states, const 
       reinterpret_cast<const u64*>(states), n_states, env_ids, m,
       static_cast<__nv_bfloat16*>(query), ldq, static_cast<int>(ldq - kFeatures), legal, players,
       done, status);
+  return launch_status();
+}
+
+int cugo_b200_observe_critic_bf16(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                                  int64_t m, void* critic_in, int64_t ldc, uint8_t* players,
+                                  bool* done, int16_t* status, cudaStream_t stream) {
+  if (n_states < 0 || m < 0 || (m > 0 && !env_ids)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (!critic_in || !players || !done || !status)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (ldc < (int64_t)(kFeatures + 50)) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(critic_in, 16) || ldc % 8) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  observe_kernel<__nv_bfloat16><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<const u64*>(states), n_states, env_ids, m,
+      static_cast<__nv_bfloat16*>(critic_in), ldc, static_cast<int>(ldc - kFeatures), nullptr,
+      players, done, status, 1);
   return launch_status();
 }
 

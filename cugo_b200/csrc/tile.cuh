@@ -199,11 +199,14 @@ __device__ __forceinline__ void emit_features(const WarpTile& t, F* __restrict__
   }
 }
 
-// Cooperative write of the tile's legal masks as bf16 0/1 into columns
-// 720 .. 720 + cols - 1 of each feature row (actions >= 179 read 0): the
-// sequence policy's query input is [features, legal] (python/cugo_seq50.py:196-208).
+// Cooperative write of bits 0 .. nbits-1 of the tile's per-row `legal` words as
+// bf16 0/1 into columns 720 .. 720 + cols - 1 of each feature row (bits past nbits
+// read 0): the legal mask for the sequence policy's query input [features, legal]
+// (python/cugo_seq50.py:196-208), or the opponent's hand plane for the critic's
+// input [features, hand] (python/cugo_ppo50.py:478-482).
 __device__ __forceinline__ void emit_legal_columns(const WarpTile& t, __nv_bfloat16* __restrict__ out,
-                                                   i64 ld, i64 base, int rows, int cols) {
+                                                   i64 ld, i64 base, int rows, int cols,
+                                                   u32 nbits = kActions) {
   const int lane = threadIdx.x & 31;
   const int groups = cols >> 3;
   for (int k = lane; k < rows * groups; k += 32) {
@@ -212,8 +215,8 @@ __device__ __forceinline__ void emit_legal_columns(const WarpTile& t, __nv_bfloa
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const u32 a0 = 8u * g + 2u * e, a1 = a0 + 1u;
-      const u32 b0 = a0 < kActions ? static_cast<u32>((t.legal[r][a0 >> 6] >> (a0 & 63)) & 1ull) : 0u;
-      const u32 b1 = a1 < kActions ? static_cast<u32>((t.legal[r][a1 >> 6] >> (a1 & 63)) & 1ull) : 0u;
+      const u32 b0 = a0 < nbits ? static_cast<u32>((t.legal[r][a0 >> 6] >> (a0 & 63)) & 1ull) : 0u;
+      const u32 b1 = a1 < nbits ? static_cast<u32>((t.legal[r][a1 >> 6] >> (a1 & 63)) & 1ull) : 0u;
       h[e] = (b0 ? 0x3F80u : 0u) | ((b1 ? 0x3F80u : 0u) << 16);  // bf16 1.0 = 0x3F80
     }
     __stcs(reinterpret_cast<uint4*>(out + (base + r) * ld + kFeatures) + g,

@@ -45,6 +45,8 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_gemm_bf16_ex": [_VP, _I64, _VP, _I64, _VP, _I32, _VP, _I64, _VP, _I64, _I32, _I32,
                                _I32, _I64, _I64, _I64, _VP, _VP],
     "cugo_b200_observe_query_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_observe_critic_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP],
+    "cugo_b200_redeal": [_VP, _I64, _VP, _I64, _I32, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
     "cugo_b200_layernorm": [_VP, _I64, _VP, _VP, _I64, ctypes.c_float, _VP, _I64, _I64, _VP],
@@ -388,6 +390,31 @@ class CugoB200Extension:
                 _ptr(states), states.size(0), _ptr(env_ids), m, _ptr(query), query.stride(0),
                 *map(_ptr, out[1:]), self._stream(states.device)), "observe_query_bf16")
         return out
+
+    def observe_critic_bf16(self, states, env_ids, width: int = 776) -> list[torch.Tensor]:
+        """The oracle critic's input rows bf16 [m, width] (mover's features, the hand
+        plane of the mover's opponent, zeros) plus players, done, status."""
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        m = env_ids.numel()
+        dev = states.device
+        with torch.cuda.device(dev):
+            rows = torch.empty((m, width), dtype=torch.bfloat16, device=dev)
+            players = torch.empty((m,), dtype=torch.uint8, device=dev)
+            done = torch.empty((m,), dtype=torch.bool, device=dev)
+            status = torch.empty((m,), dtype=torch.int16, device=dev)
+            _check(self._lib.cugo_b200_observe_critic_bf16(
+                _ptr(states), states.size(0), _ptr(env_ids), m, _ptr(rows), width, _ptr(players),
+                _ptr(done), _ptr(status), self._stream(dev)), "observe_critic_bf16")
+        return [rows, players, done, status]
+
+    def redeal(self, rows: torch.Tensor, seats: torch.Tensor, seed: int, attempt: int = 0) -> None:
+        """Redeals the rows in place for observer seats (the reference's _redeal)."""
+        self._states(rows)
+        _check_cuda_1d(seats, torch.int64, "seats")
+        with torch.cuda.device(rows.device):
+            _check(self._lib.cugo_b200_redeal(_ptr(rows), rows.size(0), _ptr(seats), seed, attempt,
+                                              self._stream(rows.device)), "redeal")
 
     # -- policy layers -------------------------------------------------------------
     def linear(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,

@@ -66,13 +66,20 @@ class _FusedMlpFunction(torch.autograd.Function):
         dev = x.device
         ws = [p.detach().to(torch.bfloat16) for p in params[0::2]]
         bs = [p.detach() for p in params[1::2]]  # fp32 biases, used by the epilogue as is
-        # Input rows padded to a multiple of 16 bytes (the TMA row-stride rule).
-        kin = _pad8(x.shape[1])
-        xb = torch.zeros((m, kin), dtype=torch.bfloat16, device=dev)
-        xb[:, :x.shape[1]] = x
-        w_in = torch.zeros((ws[0].shape[0], kin), dtype=torch.bfloat16, device=dev)
-        w_in[:, :ws[0].shape[1]] = ws[0]
-        h = ext.linear(xb, w_in, bs[0])
+        # Row strides must be multiples of 16 bytes (the TMA rule): the input is read in
+        # place when its rows already are (e.g. the 776-wide critic rows that
+        # observe_critic_bf16 writes), else copied into padded rows; the input
+        # layer's weight is padded likewise.  K stays the true input width.
+        k_in = ws[0].shape[1]
+        if x.dtype == torch.bfloat16 and x.stride(1) == 1 and x.stride(0) % 8 == 0:
+            xb = x[:, :k_in]
+        else:
+            xp = torch.zeros((m, _pad8(k_in)), dtype=torch.bfloat16, device=dev)
+            xp[:, :k_in] = x[:, :k_in]
+            xb = xp[:, :k_in]
+        w_pad = torch.zeros((ws[0].shape[0], _pad8(k_in)), dtype=torch.bfloat16, device=dev)
+        w_pad[:, :k_in] = ws[0]
+        h = ext.linear(xb, w_pad[:, :k_in], bs[0])
         saved = [xb]
         for i in range(net.n_blocks):
             w1, b1, w2, b2 = ws[1 + 2 * i], bs[1 + 2 * i], ws[2 + 2 * i], bs[2 + 2 * i]
@@ -91,7 +98,6 @@ class _FusedMlpFunction(torch.autograd.Function):
         ctx.save_for_backward(*saved)
         ctx.net = net
         ctx.weights = ws
-        ctx.in_features = x.shape[1]
         return out[:, :n_out].contiguous()
 
     @staticmethod
@@ -122,8 +128,7 @@ class _FusedMlpFunction(torch.autograd.Function):
             grads_w[1 + 2 * i] = torch.matmul(dz.t(), h).float()
             grads_b[1 + 2 * i] = dz.sum(0, dtype=torch.float32)
             dh = ext.linear(dz, w1.t().contiguous(), residual=dh)  # dh + dz W1
-        gw_in = torch.matmul(dh.t(), xb).float()
-        grads_w[0] = gw_in[:, :ctx.in_features].contiguous()
+        grads_w[0] = torch.matmul(dh.t(), xb).float()
         grads_b[0] = dh.sum(0, dtype=torch.float32)
         out = []
         for gw, gb in zip(grads_w, grads_b):
@@ -136,7 +141,8 @@ class FusedResidualMlp(nn.Module):
     tcgen05 GEMM.  squeeze: return [M] for a single output (OracleCritic)."""
 
     def __init__(self, inputs: int, outputs: int, hidden: int = 512, blocks: int = 3,
-                 activation: str = "silu", squeeze: bool = False, zero_out: bool = False) -> None:
+                 activation: str = "silu", squeeze: bool = False, zero_out: bool = False,
+                 value_bins: int = 0, value_top: float = 640.0) -> None:
         super().__init__()
         if activation not in _ACT:
             raise ValueError("activation must be relu or silu")
@@ -153,7 +159,20 @@ class FusedResidualMlp(nn.Module):
         if zero_out:
             nn.init.zeros_(self.out.weight)
             nn.init.zeros_(self.out.bias)
+        # OracleCritic's value head (python/cugo_ppo_nets50.py:67-91): one output, or a
+        # distribution over symlog-spaced returns whose mean is the value.
+        self.stock, self.value_bins = False, value_bins
+        if value_bins:
+            u = torch.linspace(-1.0, 1.0, value_bins, dtype=torch.float64) * torch.log1p(
+                torch.tensor(value_top, dtype=torch.float64))
+            self.register_buffer("support", (torch.sign(u) * torch.expm1(u.abs())).float(),
+                                 persistent=False)
         self._ext = None
+
+    def value(self, out: torch.Tensor) -> torch.Tensor:
+        if not self.value_bins:
+            return out.float()
+        return (torch.softmax(out.float(), -1) * self.support).sum(-1)
 
     @property
     def ext(self):
@@ -166,7 +185,8 @@ class FusedResidualMlp(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         params = [t for l in self.linears() for t in (l.weight, l.bias)]
-        out = _FusedMlpFunction.apply(x.to(torch.bfloat16), self, *params)
+        out = _FusedMlpFunction.apply(x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16),
+                                      self, *params)
         return out.squeeze(-1) if self.squeeze and out.shape[-1] == 1 else out
 
 
@@ -175,9 +195,12 @@ def fused_actor(hidden: int = 512, blocks: int = 3) -> FusedResidualMlp:
     return FusedResidualMlp(FEATURES, ACTIONS, hidden, blocks, "silu", zero_out=True)
 
 
-def fused_critic(hidden: int = 512, blocks: int = 3) -> FusedResidualMlp:
-    """OracleCritic's shape without stock planes: 770 inputs -> one value."""
-    return FusedResidualMlp(FEATURES + ORACLE_FEATURES, 1, hidden, blocks, "silu", squeeze=True)
+def fused_critic(hidden: int = 512, blocks: int = 3, value_bins: int = 0,
+                 value_top: float = 640.0) -> FusedResidualMlp:
+    """OracleCritic's shape without stock planes: 770 inputs -> one value (or
+    value_bins logits of the return distribution)."""
+    return FusedResidualMlp(FEATURES + ORACLE_FEATURES, value_bins or 1, hidden, blocks, "silu",
+                            squeeze=not value_bins, value_bins=value_bins, value_top=value_top)
 
 
 def critic_input(features: torch.Tensor, opp_hand: torch.Tensor) -> torch.Tensor:

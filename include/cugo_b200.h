@@ -249,6 +249,26 @@ CUGO_B200_API int cugo_b200_observe_query_bf16(const uint8_t* states, int64_t n_
                                                int64_t ldq, bool* legal, uint8_t* players,
                                                bool* done, int16_t* status, cudaStream_t stream);
 
+/* observe_indexed writing the oracle critic's input in one pass (python/cugo_ppo50.py:
+ * 478-482, _critic_input without stock planes, as action_values and _child_values
+ * build it, :86-104, 214-225): critic_in bf16 [m, ldc] with the mover's features in
+ * columns 0..719, the hand of the mover's opponent as 0/1 in 720..769 and zeros in
+ * 770..ldc-1 (ldc >= 770, a multiple of 8, e.g. 776); players/done/status as
+ * observe_indexed. */
+CUGO_B200_API int cugo_b200_observe_critic_bf16(const uint8_t* states, int64_t n_states,
+                                                const int64_t* env_ids, int64_t m, void* critic_in,
+                                                int64_t ldc, uint8_t* players, bool* done,
+                                                int16_t* status, cudaStream_t stream);
+
+/* Redeal rows in place for an observer (python/cugo_ppo50.py:125-149, _redeal): the
+ * opponent of seats[i] keeps the hand cards shown by a shake and gets the rest anew,
+ * as many as before, uniformly from the cards seats[i] cannot see (those cards and
+ * the stock); the stock is the remainder; the opponent's held set follows; the stock's
+ * RNG word is reseeded in [-2^62, 2^62).  Randomness: Philox4x32-10 keyed by seed,
+ * counter {row, attempt, stream}.  Rows must be distinct. */
+CUGO_B200_API int cugo_b200_redeal(uint8_t* rows, int64_t n, const int64_t* seats, int64_t seed,
+                                   int32_t attempt, cudaStream_t stream);
+
 /* ---- Sequence policy decode ------------------------------------------------------
  * Single-query attention over a KV cache, replacing decode_attention and its
  * Triton _decode_kernel (python/cugo_seq_attention50.py:22-62), optionally fused
