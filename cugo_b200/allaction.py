@@ -8,9 +8,10 @@ arguments and results.
                   hand plane of the mover's opponent), score it with the critic on
                   the fused GEMM; a finished child scores its final reward.
   redeal_worlds   copies of rows in which the observer's opponent holds another
-                  hand consistent with everything the observer saw (the redeal runs
-                  on the device, cugo_b200_redeal), kept when the observer's
-                  features and legal actions are unchanged.
+                  hand consistent with everything the observer saw, kept when the
+                  observer's features and legal actions are unchanged: redeal,
+                  observe and compare run on the device in one launch
+                  (cugo_b200_redeal_worlds).
   world_values    Q averaged over redealt worlds, each child scored by the critic
                   (depth 1) or by greedy play to the end (depth 0).
 
@@ -34,6 +35,15 @@ ROLLOUT_CHECK = 4    # python/cugo_ppo50.py:180
 CRITIC_LD = 776      # 720 features + 50 hand bits, rows padded to 16 bytes
 
 
+def _chunk(net: nn.Module | None) -> int:
+    """Children per critic pass: Q_CHUNK at the reference's 2,048-wide hidden layer,
+    proportionally more for narrower networks (the same activation memory, fewer
+    host round trips)."""
+    inp = getattr(net, "inp", None)
+    hidden = getattr(inp, "out_features", 2048) if inp is not None else 2048
+    return Q_CHUNK * max(1, 2048 // max(1, hidden))
+
+
 def _critic_rows(ext: Any, critic: nn.Module, child: torch.Tensor):
     """Critic values of the children and the mover of each (python/cugo_ppo50.py:97-101)."""
     if getattr(critic, "stock", False):
@@ -55,8 +65,9 @@ def action_values(ext: Any, critic: nn.Module, states: torch.Tensor, env_rows: t
     rows, acts = torch.nonzero(branch, as_tuple=True)
     q = torch.full(branch.shape, float("nan"), dtype=torch.float16, device=branch.device)
     me = seat.index_select(0, rows)
-    for i in range(0, rows.numel(), Q_CHUNK):
-        r, a, m = rows[i:i + Q_CHUNK], acts[i:i + Q_CHUNK], me[i:i + Q_CHUNK]
+    chunk = _chunk(critic)
+    for i in range(0, rows.numel(), chunk):
+        r, a, m = rows[i:i + chunk], acts[i:i + chunk], me[i:i + chunk]
         child, reward0, done = ext.branch_indexed(states, env_rows.index_select(0, r), a)[:3]
         v, mover = _critic_rows(ext, critic, child)
         v = torch.where(mover == m, v, -v)  # zero-sum: the opponent's value is ours negated
@@ -70,27 +81,13 @@ def redeal_worlds(ext: Any, states: torch.Tensor, env_rows: torch.Tensor, seat: 
                   worlds: int, tries: int = 8, seed: int = 0) -> torch.Tensor:
     """[worlds * R, 248] copies of the rows, world-major, each redealt so the
     observer's features and legal actions are unchanged; a row that fails `tries`
-    times keeps the real deal (python/cugo_ppo50.py:152-177).  Attempt t of a
-    candidate row draws from Philox (seed, t, candidate index)."""
+    times keeps the real deal (python/cugo_ppo50.py:152-177).  One kernel launch
+    (cugo_b200_redeal_worlds) runs the attempts of every world row; attempt t of
+    world row w draws from Philox (seed, t, w)."""
     ext = ext or load_extension()
     if states.shape[1] != ext.STATE_BYTES:
         raise RuntimeError("state rows must be TorchEnv50 images")
-    base = states.index_select(0, env_rows)
-    f0, l0 = ext.observe_indexed(base, torch.arange(base.shape[0], device=base.device))[:2]
-    out = base.repeat(worlds, 1)
-    seat_k, ref_f, ref_l = seat.repeat(worlds), f0.repeat(worlds, 1), l0.repeat(worlds, 1)
-    todo = torch.arange(out.shape[0], device=base.device)
-    for attempt in range(tries):
-        if todo.numel() == 0:
-            break
-        cand = out.index_select(0, todo)  # still the real deal for every row left to do
-        ext.redeal(cand, seat_k.index_select(0, todo), seed, attempt)
-        f, l = ext.observe_indexed(cand, torch.arange(cand.shape[0], device=cand.device))[:2]
-        good = (f == ref_f.index_select(0, todo)).all(1) & (l == ref_l.index_select(0, todo)).all(1)
-        keep = torch.nonzero(good).squeeze(1)
-        out.index_copy_(0, todo.index_select(0, keep), cand.index_select(0, keep))
-        todo = todo.index_select(0, torch.nonzero(~good).squeeze(1))
-    return out
+    return ext.redeal_worlds(states, env_rows, seat, worlds, seed=seed, tries=tries)
 
 
 def _greedy(ext: Any, model: nn.Module, features: torch.Tensor, legal: torch.Tensor,
@@ -162,8 +159,9 @@ def _world_q(ext: Any, actor: nn.Module, opponent: nn.Module | None, critic: nn.
     seat_k, pool_k, branch_k = seat.repeat(worlds), vs_pool.repeat(worlds), branch.repeat(worlds, 1)
     rows, acts = torch.nonzero(branch_k, as_tuple=True)
     q = torch.zeros(branch_k.shape, device=branch.device)
-    for i in range(0, rows.numel(), Q_CHUNK):
-        r, a = rows[i:i + Q_CHUNK], acts[i:i + Q_CHUNK]
+    chunk = _chunk(critic if depth == 1 else actor)
+    for i in range(0, rows.numel(), chunk):
+        r, a = rows[i:i + chunk], acts[i:i + chunk]
         me, pool = seat_k.index_select(0, r), pool_k.index_select(0, r)
         child, reward0, done = ext.branch_indexed(w, r, a)[:3]
         if depth == 1:

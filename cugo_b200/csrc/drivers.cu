@@ -167,52 +167,129 @@ __global__ void __launch_bounds__(kBlock, 5) selfplay_pick_kernel(
   emit_legal(t, legal_out, tile_base, rows_here);
 }
 
-// Redeal of a row for the observer `seat` (the reference's _redeal,
+// Redeal of a row for the observer seat (the reference's _redeal,
 // python/cugo_ppo50.py:125-149, on the device): the opponent's hand keeps its cards
 // shown by a shake and gets the rest — as many cards as before — drawn uniformly
 // from the cards the observer cannot see (those hand cards and the stock); the stock
 // is what remains; `held` (every card ever in that hand) follows the new hand; the
 // stock's draw stream gets a new seed in [-2^62, 2^62).  Draws: Philox4x32-10 with
-// counter {row lo, row hi, attempt, 8 + k} and key {seed lo, seed hi}: a uniform
-// subset by successive picks of the floor(r * left / 2^32)-th remaining card.
+// counter {ctr lo, ctr hi, attempt, 8 + k / 4} and key {seed lo, seed hi}, word
+// k % 4: a uniform subset by successive picks of the floor(r * left / 2^32)-th
+// remaining card; the seed from counter {ctr lo, ctr hi, attempt, 7}.
+// W: a pointer to the row in memory or the row's words in registers (constant
+// indices only, so a register row stays in registers).
+template <typename W>
+__device__ __forceinline__ void redeal_row(W& w, bool s0, i64 ctr, i64 seed, u32 attempt) {
+  const u64 hand = s0 ? w[1] : w[0];
+  const u64 held = s0 ? w[21] : w[20];
+  const u64 fixed = hand & (s0 ? w[23] : w[22]);
+  const u64 free = hand & ~fixed;
+  const u64 unknown = free | w[3];
+  u64 left = unknown, picked = 0;
+  const u32 count = popc(free);
+  u32 remaining = popc(left);
+  const u32 c0 = static_cast<u32>(ctr), c1 = static_cast<u32>(static_cast<u64>(ctr) >> 32);
+  const u32 k0 = static_cast<u32>(seed), k1 = static_cast<u32>(static_cast<u64>(seed) >> 32);
+  Philox4 r{};
+  for (u32 k = 0; k < count; ++k) {
+    if ((k & 3u) == 0) r = philox4x32_10(c0, c1, attempt, 8u + (k >> 2), k0, k1);
+    const u32 q = k & 3u;
+    const u32 word = q == 0 ? r.v[0] : (q == 1 ? r.v[1] : (q == 2 ? r.v[2] : r.v[3]));
+    const u64 bit = u64{1} << nth_card(left, static_cast<u32>((static_cast<u64>(word) * remaining) >> 32));
+    picked |= bit;
+    left &= ~bit;
+    --remaining;
+  }
+  const u64 new_hand = fixed | picked;
+  const u64 new_held = (held & ~hand) | new_hand;
+  w[3] = unknown & ~picked;
+  if (s0) {
+    w[1] = new_hand;
+    w[21] = new_held;
+  } else {
+    w[0] = new_hand;
+    w[20] = new_held;
+  }
+  const Philox4 sd = philox4x32_10(c0, c1, attempt, 7u, k0, k1);
+  const u64 bits63 = ((static_cast<u64>(sd.v[0]) << 32) | sd.v[1]) >> 1;  // [0, 2^63)
+  w[6] = bits63 - (u64{1} << 62);  // as int64: [-2^62, 2^62)
+}
+
+// One attempt on rows in place; the Philox counter is the row index.
 __global__ void __launch_bounds__(256) redeal_kernel(u64* __restrict__ rows, i64 n,
                                                      const i64* __restrict__ seats, i64 seed,
                                                      u32 attempt) {
   const i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   u64* w = rows + i * kRowWords;
-  const bool s0 = __ldg(seats + i) == 0;  // observer seat 0: the opponent is seat 1
-  const int hw = s0 ? 1 : 0, held_w = s0 ? 21 : 20, rev_w = s0 ? 23 : 22;
-  const u64 hand = w[hw], stock = w[3];
-  const u64 fixed = hand & w[rev_w];
-  const u64 held = w[held_w];
-  const u64 free = hand & ~fixed;
-  u64 left = free | stock;
-  const u32 count = popc(free);
-  u64 picked = 0;
-  u32 remaining = popc(left);
-  const u64 key = static_cast<u64>(seed);
-  Philox4 r{};
-  for (u32 k = 0; k < count; ++k) {
-    if ((k & 3u) == 0)
-      r = philox4x32_10(static_cast<u32>(i), static_cast<u32>(static_cast<u64>(i) >> 32), attempt,
-                        8u + (k >> 2), static_cast<u32>(key), static_cast<u32>(key >> 32));
-    const u32 word = r.v[0] * ((k & 3u) == 0) + r.v[1] * ((k & 3u) == 1) + r.v[2] * ((k & 3u) == 2) +
-                     r.v[3] * ((k & 3u) == 3);
-    const u32 rank = static_cast<u32>((static_cast<u64>(word) * remaining) >> 32);
-    const u64 bit = u64{1} << nth_card(left, rank);
-    picked |= bit;
-    left &= ~bit;
-    --remaining;
+  redeal_row(w, __ldg(seats + i) == 0, i, seed, attempt);
+}
+
+// The observer's view of a row for the acceptance test: the observation packet
+// (features) and the legal mask, in a lane-private shared-memory row.
+constexpr int kViewWords = kBitWords + kScalarColumns + 6;  // 67: odd, conflict-free rows
+
+// Redealt worlds (the reference's redeal_worlds loop, python/cugo_ppo50.py:152-177,
+// in one launch): world row w = k * r + b is a copy of states[env_ids[b]] in which
+// the observer (seats[b]) keeps its view: attempts a = 0 .. tries - 1 redeal the
+// real deal with counter w, and the first whose observation packet and legal mask
+// equal the real deal's is kept; after `tries` failures the row is the real deal.
+// accepted[w] (optional) gets the attempt kept, or -1.  The real deal's view sits
+// in dynamic shared memory; the row stays in registers and only the five words a
+// redeal touches are restored between attempts.
+__global__ void __launch_bounds__(kBlock, 3) redeal_worlds_kernel(
+    const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids, i64 r,
+    const i64* __restrict__ seats, i64 total, i64 seed, int tries, u64* __restrict__ out,
+    int8_t* __restrict__ accepted) {
+  extern __shared__ u32 view_smem[];
+  WarpTile& t = my_tile();
+  u32* view = view_smem + threadIdx.x * kViewWords;
+  const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
+  const i64 b = row < total ? row % r : -1;
+  const i64 src = b >= 0 ? lane_source(ids, b, r, n_states) : -1;
+  gather_rows(t, states, src);
+  Game g;
+  load_game(t, g);
+  __syncwarp();
+  const bool s0 = src >= 0 && __ldg(seats + b) == 0;
+  const u64 h0 = g.w[0], h1 = g.w[1], st = g.w[3], rng = g.w[6], hd0 = g.w[20], hd1 = g.w[21];
+  const PacketRef pk = lane_packet(t);
+  int kept = -1;
+  const int last = src >= 0 ? tries : -1;
+  for (int a = -1; a < last; ++a) {
+    if (a >= 0) {
+      g.w[0] = h0; g.w[1] = h1; g.w[3] = st; g.w[6] = rng; g.w[20] = hd0; g.w[21] = hd1;
+      redeal_row(g.w, s0, row, seed, static_cast<u32>(a));
+    }
+    ObsMeta meta;
+    observe_game(g, pk, meta);
+    const u32 lw[6] = {static_cast<u32>(meta.legal.w0), static_cast<u32>(meta.legal.w0 >> 32),
+                       static_cast<u32>(meta.legal.w1), static_cast<u32>(meta.legal.w1 >> 32),
+                       static_cast<u32>(meta.legal.w2), static_cast<u32>(meta.legal.w2 >> 32)};
+    if (a < 0) {  // the real deal's view
+      for (u32 k = 0; k < kBitWords; ++k) view[k] = pk.bits[k];
+      for (u32 k = 0; k < kScalarColumns; ++k) view[kBitWords + k] = __float_as_uint(pk.scal[k]);
+      for (int k = 0; k < 6; ++k) view[kBitWords + kScalarColumns + k] = lw[k];
+      continue;
+    }
+    bool same = true;
+    for (u32 k = 0; k < kBitWords; ++k) same &= view[k] == pk.bits[k];
+    for (u32 k = 0; k < kScalarColumns; ++k) same &= __uint_as_float(view[kBitWords + k]) == pk.scal[k];
+    for (int k = 0; k < 6; ++k) same &= view[kBitWords + kScalarColumns + k] == lw[k];
+    if (same) {
+      kept = a;
+      break;
+    }
   }
-  const u64 new_hand = fixed | picked;
-  w[3] = (free | stock) & ~picked;
-  w[hw] = new_hand;
-  w[held_w] = (held & ~hand) | new_hand;
-  const Philox4 s = philox4x32_10(static_cast<u32>(i), static_cast<u32>(static_cast<u64>(i) >> 32),
-                                  attempt, 7u, static_cast<u32>(key), static_cast<u32>(key >> 32));
-  const u64 bits63 = ((static_cast<u64>(s.v[0]) << 32) | s.v[1]) >> 1;  // [0, 2^63)
-  w[6] = bits63 - (u64{1} << 62);  // as int64: [-2^62, 2^62)
+  if (kept < 0) {
+    g.w[0] = h0; g.w[1] = h1; g.w[3] = st; g.w[6] = rng; g.w[20] = hd0; g.w[21] = hd1;
+    if (src < 0)
+      for (int k = 0; k < kRowWords; ++k) g.w[k] = 0;
+  }
+  __syncwarp();  // every lane is done with its packet before rows overwrite the tile
+  store_game(t, g);
+  store_tile(t, out, (i64)blockIdx.x * kBlock + (threadIdx.x & ~31), total, row < total ? row : -1);
+  if (row < total && accepted) accepted[row] = static_cast<int8_t>(kept);
 }
 
 // Branching roots: game r advanced by k_r < 21 random-legal decisions, stopping
@@ -316,6 +393,31 @@ int cugo_b200_redeal(uint8_t* rows, int64_t n, const int64_t* seats, int64_t see
   if (n == 0) return CUGO_B200_OK;
   redeal_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
       reinterpret_cast<u64*>(rows), n, seats, seed, static_cast<u32>(attempt));
+  return launch_status();
+}
+
+int cugo_b200_redeal_worlds(const uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                            int64_t r, const int64_t* seats, int64_t worlds, int64_t seed,
+                            int32_t tries, uint8_t* out, int8_t* accepted, cudaStream_t stream) {
+  if (n_states < 0 || r < 0 || worlds < 0 || tries < 0 || tries > 127) return CUGO_B200_ERR_ARG;
+  const int64_t total = r * worlds;
+  if (total > 0 && (!env_ids || !seats || !out || (n_states > 0 && !states))) return CUGO_B200_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(states) & 7u) || (reinterpret_cast<uintptr_t>(out) & 7u))
+    return CUGO_B200_ERR_ALIGN;
+  if (total == 0) return CUGO_B200_OK;
+  constexpr int kViewBytes = kBlock * kViewWords * 4;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUGO_B200_ERR_LAUNCH;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(redeal_worlds_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kViewBytes) != cudaSuccess)
+      return CUGO_B200_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  redeal_worlds_kernel<<<blocks_for(total), kBlock, kViewBytes, stream>>>(
+      reinterpret_cast<const u64*>(states), n_states, env_ids, r, seats, total, seed, tries,
+      reinterpret_cast<u64*>(out), accepted);
   return launch_status();
 }
 

@@ -199,11 +199,31 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// SiLU as v * sigmoid(v) with the fast exponential and divide: a few instructions
+// per element where IEEE division costs a dozen and an out-of-line slow path.  The
+// error (a few fp32 ulp) is far below the bf16 rounding of the stored result.
+__device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+
 __device__ __forceinline__ float activate(float v, int act) {
   if (act == kActRelu) return fmaxf(v, 0.0f);
-  if (act == kActSilu) return v / (1.0f + __expf(-v));
+  if (act == kActSilu) return silu_fast(v);
   if (act == kActGelu) return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));  // exact (erf) GELU
   return v;
+}
+
+// The activation over a chunk, the choice made once per chunk.
+template <int CW>
+__device__ __forceinline__ void activate_chunk(float* v, int act) {
+  if (act == kActRelu) {
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] = fmaxf(v[j], 0.0f);
+  } else if (act == kActSilu) {
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] = silu_fast(v[j]);
+  } else if (act == kActGelu) {
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] = activate(v[j], kActGelu);
+  }
 }
 
 #define CB_TMEM_LD16(taddr, r)                                                                  \
@@ -382,12 +402,10 @@ __device__ __forceinline__ void epilogue_cols(const Epilogue& ep, EpiWarp& io, u
     float v[CW];
     if (live) {
 #pragma unroll
-      for (int j = 0; j < CW; ++j) v[j] = activate(__uint_as_float(r[j]) + bias_s[c0 + j], ep.act);
+      for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(r[j]) + bias_s[c0 + j];
+      activate_chunk<CW>(v, ep.act);
       if (ep.residual) add_residual_row<T>(cur, v);  // ends with __syncwarp
-      if (ep.act_after != kActNone) {
-#pragma unroll
-        for (int j = 0; j < CW; ++j) v[j] = activate(v[j], ep.act_after);
-      }
+      activate_chunk<CW>(v, ep.act_after);
     }
     // The previous chunk's store must have read the other buffer before the next
     // residual lands there (and this buffer's store, two chunks back, long before).
@@ -967,6 +985,89 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
     gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mo, mr, ep);
   }
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+}  // extern "C"
+
+namespace {
+
+// One-output layer (the scalar value head, python/cugo_ppo_nets50.py:82):
+// out[r] = a[r, :k] . w[:k] + bias.  A GEMM tile would spend 255 of its 256
+// columns on nothing, so this is a row reduction at HBM speed instead: a warp per
+// row, each lane holding its 16-byte pieces of w in registers (k <= 2,048 and a
+// multiple of 8), four rows in flight per warp, a fixed shuffle tree (the result
+// does not depend on the launch shape).
+constexpr int kDotMaxPieces = 8;  // 8 x 8 bf16 per lane: k <= 2,048
+
+__global__ void __launch_bounds__(256) rowdot_kernel(const __nv_bfloat16* __restrict__ a,
+                                                     int64_t lda, const float* __restrict__ w,
+                                                     const float* __restrict__ bias, int64_t m,
+                                                     int k, float* __restrict__ out, int64_t ldo) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int pieces = k >> 3;
+  float wr[kDotMaxPieces][8];
+#pragma unroll
+  for (int j = 0; j < kDotMaxPieces; ++j) {
+    const int p = lane + 32 * j;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) wr[j][e] = p < pieces ? __ldg(w + 8 * p + e) : 0.0f;
+  }
+  const float b = bias ? __ldg(bias) : 0.0f;
+  for (int64_t r0 = warp * 4; r0 < m; r0 += warps * 4) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < kDotMaxPieces; ++j) {
+      const int p = lane + 32 * j;
+      if (32 * j >= pieces) break;
+      uint4 raw[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        raw[q] = (p < pieces && r0 + q < m)
+                     ? __ldcs(reinterpret_cast<const uint4*>(a + (r0 + q) * lda) + p)
+                     : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          acc[q] = fmaf(f.x, wr[j][2 * e], acc[q]);
+          acc[q] = fmaf(f.y, wr[j][2 * e + 1], acc[q]);
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], off);
+    }
+    if (lane < 4 && r0 + lane < m) {
+      const float v = lane == 0 ? acc[0] : (lane == 1 ? acc[1] : (lane == 2 ? acc[2] : acc[3]));
+      out[(r0 + lane) * ldo] = v + b;
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_rowdot_bf16(const void* a, int64_t lda, const float* w, const float* bias,
+                          int64_t m, int64_t k, float* out, int64_t ldo, cudaStream_t stream) {
+  if (m < 0 || k <= 0 || k > 8 * 32 * kDotMaxPieces || k % 8 || lda < k || ldo < 1)
+    return CUGO_B200_ERR_ARG;
+  if (m == 0) return CUGO_B200_OK;
+  if (!a || !w || !out) return CUGO_B200_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(a) & 15u) || lda % 8 || (reinterpret_cast<uintptr_t>(w) & 3u))
+    return CUGO_B200_ERR_ALIGN;
+  const int64_t warps_needed = (m + 3) / 4;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8 * 8;  // 8 blocks of 8 warps per SM
+  const int64_t warps = warps_needed < cap ? warps_needed : cap;
+  rowdot_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(a), lda, w, bias, m, static_cast<int>(k), out, ldo);
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }
 

@@ -47,6 +47,8 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_observe_query_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_observe_critic_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP],
     "cugo_b200_redeal": [_VP, _I64, _VP, _I64, _I32, _VP],
+    "cugo_b200_redeal_worlds": [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I32, _VP, _VP, _VP],
+    "cugo_b200_rowdot_bf16": [_VP, _I64, _VP, _VP, _I64, _I64, _VP, _I64, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
     "cugo_b200_layernorm": [_VP, _I64, _VP, _VP, _I64, ctypes.c_float, _VP, _I64, _I64, _VP],
@@ -396,6 +398,7 @@ class CugoB200Extension:
         plane of the mover's opponent, zeros) plus players, done, status."""
         self._states(states)
         _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _same_device(states, env_ids, "states", "env_ids")
         m = env_ids.numel()
         dev = states.device
         with torch.cuda.device(dev):
@@ -445,6 +448,42 @@ class CugoB200Extension:
                 residual.stride(0) if residual is not None else 0, _ptr(out), out.stride(0),
                 int(out.dtype == torch.float32), act, act_after, m, n, k, _ptr(error),
                 self._stream(a.device)), "gemm_bf16")
+        return out
+
+    def redeal_worlds(self, states, env_ids, seats, worlds: int, seed: int = 0, tries: int = 8,
+                      with_attempts: bool = False):
+        """[worlds * R, 248] redealt copies of states[env_ids] keeping each observer's
+        view (one launch); with_attempts also returns the int8 attempt kept (-1: none)."""
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _check_cuda_1d(seats, torch.int64, "seats")
+        _same_device(states, env_ids, "states", "env_ids")
+        r = env_ids.numel()
+        if seats.numel() != r:
+            raise RuntimeError("redeal_worlds: one seat per env id")
+        dev = states.device
+        with torch.cuda.device(dev):
+            out = torch.empty((worlds * r, self.STATE_BYTES), dtype=torch.uint8, device=dev)
+            acc = torch.empty((worlds * r,), dtype=torch.int8, device=dev) if with_attempts else None
+            _check(self._lib.cugo_b200_redeal_worlds(
+                _ptr(states), states.size(0), _ptr(env_ids), r, _ptr(seats), worlds, seed, tries,
+                _ptr(out), _ptr(acc), self._stream(dev)), "redeal_worlds")
+        return (out, acc) if with_attempts else out
+
+    def rowdot(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """out[r] = a[r] . w + bias: a one-output layer, bf16 a [m, k], fp32 w [k]."""
+        m, k = a.shape
+        if a.dtype != torch.bfloat16 or a.stride(1) != 1 or w.dtype != torch.float32:
+            raise RuntimeError("rowdot expects row-major bf16 a and fp32 w")
+        if not w.is_contiguous() or w.numel() != k:
+            raise RuntimeError("rowdot: w must be a contiguous [k] vector")
+        if out is None:
+            out = torch.empty((m,), dtype=torch.float32, device=a.device)
+        with torch.cuda.device(a.device):
+            _check(self._lib.cugo_b200_rowdot_bf16(
+                _ptr(a), a.stride(0), _ptr(w), _ptr(bias), m, k, _ptr(out),
+                out.stride(0), self._stream(a.device)), "rowdot_bf16")
         return out
 
     # -- sequence policy decode ----------------------------------------------------

@@ -16,6 +16,10 @@ FLOPs of one launch:
                        N queries at uniform positions 0..49: (pos + 3) * 1,024 B per query
   seqwave   W WAVES    sequence self-play (4-layer d256 policy), WAVES waves of W games
   seqops    W          each op of one sequence decision step at wave size W, timed alone
+  allaction R          all-action Q of R mid-game decisions (every legal action branched,
+                       3x512 critic) and 4 redealt worlds per decision: action_values,
+                       the reference's composition of the same ops, redeal_worlds,
+                       world_values (depth 1), observe_critic_bf16 at 1,804 B per child
   ppo       B          one PPO minibatch step (3x512 actor + critic, B rows) on the fused
                        networks, and the same step with plain PyTorch modules under bf16
                        autocast (cuBLAS) for comparison
@@ -127,6 +131,50 @@ def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
     return dict(seconds=sec, tflops=flops / sec / 1e12, eager_seconds=sec_eager,
                 torch_autocast_seconds=sec_torch, torch_autocast_tflops=flops / sec_torch / 1e12,
                 torch_autocast_eager_seconds=sec_torch_eager)
+
+
+def allaction_case(r: int, warmup: int = 3, iters: int = 10) -> dict:
+    """All-action values of r mid-game decisions (python/cugo_ppo50.py:87-104) and
+    their redealt-world versions (:152-270), timed end to end on the device."""
+    from .allaction import action_values, redeal_worlds, world_values
+    from .ppo import critic_input, fused_critic
+    ext = load_extension()
+    dev = torch.device("cuda")
+    states, _, legal = _mid_game(ext, r)
+    ids = torch.arange(r, device=dev)
+    _, legal, players, done, _ = ext.observe_indexed(states, ids)
+    keep = torch.nonzero(~done).squeeze(1)
+    env_rows, seat, branch = keep, players.index_select(0, keep).long(), legal.index_select(0, keep)
+    children = int(branch.sum())
+    critic = fused_critic().to(dev)
+    scale = 10.0
+    with torch.no_grad():
+        sec_q = _time(lambda: action_values(ext, critic, states, env_rows, seat, branch, scale),
+                      warmup, iters)
+
+        def composed():  # the reference's steps on the same native ops and critic
+            rows, acts = torch.nonzero(branch, as_tuple=True)
+            child = ext.branch_indexed(states, env_rows.index_select(0, rows), acts)[0]
+            cids = torch.arange(child.shape[0], device=dev)
+            features, _, mover, _, _ = ext.observe_indexed(child, cids)
+            opp = ext.hands_indexed(child, cids).gather(1, (1 - mover.long()).unsqueeze(1)).squeeze(1)
+            return critic(critic_input(features, opp))
+
+        sec_ref = _time(composed, warmup, iters)
+        rows, acts = torch.nonzero(branch, as_tuple=True)
+        child = ext.branch_indexed(states, env_rows.index_select(0, rows), acts)[0]
+        cids = torch.arange(child.shape[0], device=dev)
+        sec_obs = _time(lambda: ext.observe_critic_bf16(child, cids), warmup, iters)
+        sec_redeal = _time(lambda: redeal_worlds(ext, states, env_rows, seat, 4), warmup, iters)
+        vs_pool = torch.zeros(seat.shape[0], dtype=torch.bool, device=dev)
+        sec_world = _time(lambda: world_values(ext, None, None, states, env_rows, seat, vs_pool,
+                                               branch, scale, 4, critic=critic, depth=1),
+                          max(1, warmup // 2), max(2, iters // 2))
+    return dict(decisions=int(keep.numel()), children=children, action_values_seconds=sec_q,
+                children_per_s=children / sec_q, reference_composition_seconds=sec_ref,
+                observe_critic_seconds=sec_obs, observe_critic_gbs=children * 1804 / sec_obs / 1e9,
+                redeal_worlds4_seconds=sec_redeal, world_values4_seconds=sec_world,
+                world_children_per_s=4 * children / sec_world)
 
 
 def main() -> None:
@@ -277,6 +325,9 @@ def main() -> None:
             res[name] = round(_time(graph.replay, args.warmup, args.iters) * 1e6 / 20, 2)
             del graph
         out.update(us=res)
+    elif args.case == "allaction":
+        (r,) = d
+        out.update(allaction_case(r, args.warmup, args.iters))
     elif args.case == "ppo":
         (b,) = d
         out.update(ppo_case(b, args.warmup, args.iters))

@@ -204,6 +204,15 @@ CUGO_B200_API int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void*
                                          int32_t act_after, int64_t m, int64_t n, int64_t k,
                                          int32_t* error, cudaStream_t stream);
 
+/* One-output layer (the scalar value head of OracleCritic, python/cugo_ppo_nets50.py:
+ * 67-87: nn.Linear(hidden, 1) under autocast): out[r * ldo] = a[r, :k] . w + *bias,
+ * a bf16 [m, k] (lda, 16-byte aligned rows), w fp32 [k] (the bf16-rounded weight
+ * row), bias fp32 scalar or NULL; k a multiple of 8, at most 2,048.  A row
+ * reduction at HBM speed instead of a 256-column GEMM tile. */
+CUGO_B200_API int cugo_b200_rowdot_bf16(const void* a, int64_t lda, const float* w,
+                                        const float* bias, int64_t m, int64_t k, float* out,
+                                        int64_t ldo, cudaStream_t stream);
+
 /* Policy forward that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory — for example a Go/Java/Rust
  * serving process that passes only its own fixed input and output buffers and keeps
@@ -268,6 +277,20 @@ CUGO_B200_API int cugo_b200_observe_critic_bf16(const uint8_t* states, int64_t n
  * counter {row, attempt, stream}.  Rows must be distinct. */
 CUGO_B200_API int cugo_b200_redeal(uint8_t* rows, int64_t n, const int64_t* seats, int64_t seed,
                                    int32_t attempt, cudaStream_t stream);
+
+/* Redealt worlds in one launch (the loop of redeal_worlds, python/cugo_ppo50.py:
+ * 152-177): out [worlds * r, 248] world-major, world row w = k * r + b a copy of
+ * states[env_ids[b]] redealt for observer seats[b] so that the observer's
+ * features and legal actions are unchanged.  Attempt a (0 .. tries - 1, tries <=
+ * 127) is cugo_b200_redeal's draw with Philox counter w; the first attempt whose
+ * observation and legal mask equal the real deal's is kept; a row that fails
+ * every attempt keeps the real deal.  accepted (optional, int8 [worlds * r]) gets
+ * the attempt kept or -1.  A bad env id gives a zero row. */
+CUGO_B200_API int cugo_b200_redeal_worlds(const uint8_t* states, int64_t n_states,
+                                          const int64_t* env_ids, int64_t r,
+                                          const int64_t* seats, int64_t worlds, int64_t seed,
+                                          int32_t tries, uint8_t* out, int8_t* accepted,
+                                          cudaStream_t stream);
 
 /* ---- Sequence policy decode ------------------------------------------------------
  * Single-query attention over a KV cache, replacing decode_attention and its

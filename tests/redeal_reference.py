@@ -23,12 +23,14 @@ def _bits(mask: int) -> list[int]:
     return [c for c in range(64) if (mask >> c) & 1]
 
 
-def redeal(rows: np.ndarray, seats: np.ndarray, seed: int, attempt: int) -> np.ndarray:
-    """Redealt copies of [n, 248] uint8 rows for observer seats [n]."""
+def redeal(rows: np.ndarray, seats: np.ndarray, seed: int, attempt: int,
+           counters: np.ndarray | None = None) -> np.ndarray:
+    """Redealt copies of [n, 248] uint8 rows for observer seats [n]; row i draws
+    with Philox counter counters[i] (default i)."""
     out = np.ascontiguousarray(rows, dtype=np.uint8).copy()
     words = out.view(np.uint64)
     n = out.shape[0]
-    idx = np.arange(n, dtype=np.uint64)
+    idx = (np.arange(n) if counters is None else np.asarray(counters)).astype(np.uint64)
     key = np.uint64(seed & (2**64 - 1))
     k0, k1 = key & np.uint64(0xFFFFFFFF), key >> np.uint64(32)
     lo, hi = idx & np.uint64(0xFFFFFFFF), idx >> np.uint64(32)
@@ -57,3 +59,28 @@ def redeal(rows: np.ndarray, seats: np.ndarray, seed: int, attempt: int) -> np.n
         bits63 = ((int(sw[0][i]) << 32) | int(sw[1][i])) >> 1
         words[i, RNG] = np.uint64((bits63 - (1 << 62)) & (2**64 - 1))
     return out
+
+
+def redeal_worlds(oracle, states: np.ndarray, env_rows: np.ndarray, seats: np.ndarray, worlds: int,
+                  seed: int, tries: int):
+    """The reference's redeal_worlds (python/cugo_ppo50.py:152-177) with the redeal
+    above: world row w = k * R + b starts as states[env_rows[b]]; attempt a redeals
+    it with counter w and is kept when the oracle's features and legal mask of the
+    observer equal the real deal's.  Returns (rows, attempt kept or -1)."""
+    base = np.ascontiguousarray(states[env_rows])
+    out = np.tile(base, (worlds, 1))
+    seat_k = np.tile(np.asarray(seats), worlds)
+    f0, l0 = oracle.observe(base, threads=1)[:2]
+    ref_f, ref_l = np.tile(f0, (worlds, 1)), np.tile(l0, (worlds, 1))
+    kept = np.full(out.shape[0], -1, dtype=np.int8)
+    todo = np.arange(out.shape[0])
+    for a in range(tries):
+        if todo.size == 0:
+            break
+        cand = redeal(out[todo], seat_k[todo], seed, a, counters=todo)
+        f, l = oracle.observe(cand, threads=1)[:2]
+        good = (f == ref_f[todo]).all(1) & (l == ref_l[todo]).all(1)
+        out[todo[good]] = cand[good]
+        kept[todo[good]] = a
+        todo = todo[~good]
+    return out, kept

@@ -78,6 +78,22 @@ def test_redeal_matches_restatement(ext, seed, attempt):
     assert np.array_equal(rows.cpu().numpy(), expect)
 
 
+@pytest.mark.parametrize("worlds,tries,seed", [(3, 8, 9), (2, 1, -4), (4, 0, 1)])
+def test_redeal_worlds_match_restatement(ext, oracle, worlds, tries, seed):
+    states, _, players = _roots(ext, 700, 61)
+    g = torch.Generator(device="cpu").manual_seed(worlds)
+    env_rows = torch.randint(0, states.shape[0], (300,), generator=g).to(DEV)
+    seats = players.index_select(0, env_rows)
+    out, kept = ext.redeal_worlds(states, env_rows, seats, worlds, seed=seed, tries=tries,
+                                  with_attempts=True)
+    e_out, e_kept = rr.redeal_worlds(oracle, states.cpu().numpy(), env_rows.cpu().numpy(),
+                                     seats.cpu().numpy(), worlds, seed, tries)
+    assert np.array_equal(kept.cpu().numpy(), e_kept)
+    assert np.array_equal(out.cpu().numpy(), e_out)
+    if tries:
+        assert (e_kept >= 0).mean() > 0.85
+
+
 def test_redeal_worlds_keep_the_observer_view(ext):
     from cugo_b200.allaction import redeal_worlds
     states, _, players = _roots(ext, 1024, 5)

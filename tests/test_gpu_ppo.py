@@ -56,6 +56,49 @@ def test_fused_mlp_gradients_match_torch(inputs, outputs, activation):
         assert err <= 1.5 * err_ref + 1e-3 * scale, (name, err, err_ref, scale)
 
 
+@pytest.mark.parametrize("inputs,outputs,activation", [(720, 179, "relu"), (770, 1, "silu"),
+                                                      (770, 51, "silu")])
+def test_inference_forward_matches_torch(inputs, outputs, activation):
+    """Without autograd the activations run in the GEMM epilogues and a scalar head is a
+    row reduction: the error against the fp32 module stays within that of the
+    reference's bf16 autocast forward (x1.5 + 1e-3 of the output scale), and a
+    second call (cached weights) is identical."""
+    fused, ref = _twins(inputs, outputs, activation=activation, squeeze=outputs == 1)
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn((3000, inputs), generator=g).to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        ours = fused(x).float().reshape(3000, outputs)
+        again = fused(x).float().reshape(3000, outputs)
+        exact = ref(x.float())
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            auto = ref(x.float()).float()
+    assert torch.equal(ours, again)
+    scale = float(exact.abs().max())
+    err, err_ref = float((ours - exact).abs().max()), float((auto - exact).abs().max())
+    assert err <= 1.5 * err_ref + 1e-3 * scale, (err, err_ref, scale)
+    with torch.no_grad():  # an in-place update of a weight is seen by the next call
+        fused.out.weight.mul_(2.0)
+        fused.out.bias.zero_()
+        ref.out.weight.mul_(2.0)
+        ref.out.bias.zero_()
+        moved = fused(x).float().reshape(3000, outputs)
+        exact2 = ref(x.float())
+    assert float((moved - exact2).abs().max()) <= 2 * err + 2e-3 * float(exact2.abs().max())
+
+
+def test_rowdot_matches_fp32():
+    from cugo_b200 import load_extension
+    ext = load_extension()
+    g = torch.Generator().manual_seed(6)
+    for m, k, ld in ((1, 8, 8), (37, 512, 520), (5000, 2048, 2048), (4099, 776, 776)):
+        a = torch.randn((m, ld), generator=g).to(DEV, torch.bfloat16)
+        w = torch.randn(k, generator=g).to(DEV)
+        b = torch.randn(1, generator=g).to(DEV)
+        out = ext.rowdot(a[:, :k], w, b)
+        expect = a[:, :k].double() @ w.double() + b.double()
+        assert torch.allclose(out.double(), expect, rtol=1e-5, atol=1e-4 * k ** 0.5)
+
+
 def test_critic_input_and_squeeze():
     from cugo_b200.ppo import critic_input, fused_critic
     feats = torch.rand((5, 720), device=DEV).to(torch.bfloat16)
