@@ -421,6 +421,9 @@ def main():
         from cugo_b200.kernel_cases import ppo_case
         extras["ppo_update"] = {"minibatch": 32768, "networks": "3x512 actor + critic (SiLU)",
                                 **ppo_case(32768, warmup=3, iters=10)}
+        from cugo_b200.kernel_cases import allaction_case
+        extras["all_action_q"] = {"critic": "3x512 OracleCritic layout (SiLU), every legal action",
+                                  **allaction_case(16384, warmup=3, iters=10)}
     peaks = measured_peaks()
     if "engine_only" in extras:
         e = extras["engine_only"]
