@@ -65,7 +65,22 @@ struct Epilogue {
   int act_after;  // applied after the residual add
   int m, n, k;
   int* error;
+  // Optional device-resident row window {first row, rows} of the M rows the maps
+  // cover (read by the kernel, so a CUDA graph can change it between replays);
+  // null: all M rows.
+  const int32_t* window;
 };
+
+// The window's first row and row count, clamped to [0, M].
+__device__ __forceinline__ void row_window(const Epilogue& ep, int& r0, int& rows) {
+  r0 = 0;
+  rows = ep.m;
+  if (ep.window) {
+    const int w0 = __ldg(ep.window), w1 = __ldg(ep.window + 1);
+    r0 = w0 < 0 ? 0 : (w0 > ep.m ? ep.m : w0);
+    rows = w1 < 0 ? 0 : (w1 > ep.m - r0 ? ep.m - r0 : w1);
+  }
+}
 
 // ---- PTX wrappers ------------------------------------------------------------------
 
@@ -448,7 +463,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles_m = (ep.m + BM - 1) / BM;
+  int r0, m_rows;
+  row_window(ep, r0, m_rows);
+  const int tiles_m = (m_rows + BM - 1) / BM;
   const int tiles_n = (ep.n + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
   const int k_tiles = (ep.k + BK - 1) / BK;
@@ -492,7 +509,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           uint8_t* sa = smem + stage * STAGE_BYTES;
           mbar_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(&map_a, &full[stage], sa, kt * BK, tm * BM);
+          tma_load_2d(&map_a, &full[stage], sa, kt * BK, r0 + tm * BM);
           tma_load_2d(&map_w, &full[stage], sa + A_BYTES, kt * BK, tn * BN);
           if (++stage == STAGES) {
             stage = 0;
@@ -560,7 +577,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int n0 = tn * BN;
       const int buf = iter & 1;
       const uint32_t use = static_cast<uint32_t>(iter >> 1);
-      const int row0 = tm * BM + quad * 32;
+      const int row0 = r0 + tm * BM + quad * 32;
       epilogue_begin(ep, io, stage, bias_s, epi_tid, row0, n0, cbase);
       if (!epilogue_wait(&acc_full[buf], use & 1u)) {
         failed = true;
@@ -925,15 +942,10 @@ bool pair_kernel_enabled() {
   return enabled == 1;
 }
 
-}  // namespace
-
-extern "C" {
-
-int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ldw,
-                           const void* bias, int32_t bias_fp32, const void* residual,
-                           int64_t ldr, void* out, int64_t ldo, int32_t out_fp32, int32_t act,
-                           int32_t act_after, int64_t m, int64_t n, int64_t k, int32_t* error,
-                           cudaStream_t stream) {
+int gemm_launch(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
+                int32_t bias_fp32, const void* residual, int64_t ldr, void* out, int64_t ldo,
+                int32_t out_fp32, int32_t act, int32_t act_after, int64_t m, int64_t n, int64_t k,
+                const int32_t* window, int32_t* error, cudaStream_t stream) {
   if (m < 0 || n <= 0 || k <= 0 || act < 0 || act > 3 || act_after < 0 || act_after > 3)
     return CUGO_B200_ERR_ARG;
   if (m == 0) return CUGO_B200_OK;
@@ -959,7 +971,7 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
     attr_set[dev] = true;
   }
   Epilogue ep{bias, residual, ldr, out, ldo, out_fp32 ? 1 : 0, bias_fp32 ? 1 : 0, act, act_after,
-              static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), error};
+              static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), error, window};
   CUtensorMap ma, mw, mo, mr;
   if (!make_out_map(&mo, out, m, n, ldo, out_fp32 != 0)) return CUGO_B200_ERR_LAUNCH;
   if (residual) {
@@ -971,7 +983,7 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
   // The pair kernel halves the weight bytes each SM streams per FLOP, which pays
   // when the K loop is long (measured: 262144x2048x2048 1,425 vs 1,317 TFLOP/s);
   // with K <= 720 the epilogue bounds both kernels and the single one is faster.
-  const bool pair = m > BM && k >= 1024 && pair_kernel_enabled();
+  const bool pair = !window && m > BM && k >= 1024 && pair_kernel_enabled();
   if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, pair ? P_BN_HALF : BN))
     return CUGO_B200_ERR_LAUNCH;
   if (pair) {
@@ -986,6 +998,29 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
     gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mo, mr, ep);
   }
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ldw,
+                           const void* bias, int32_t bias_fp32, const void* residual,
+                           int64_t ldr, void* out, int64_t ldo, int32_t out_fp32, int32_t act,
+                           int32_t act_after, int64_t m, int64_t n, int64_t k, int32_t* error,
+                           cudaStream_t stream) {
+  return gemm_launch(a, lda, w, ldw, bias, bias_fp32, residual, ldr, out, ldo, out_fp32, act,
+                     act_after, m, n, k, nullptr, error, stream);
+}
+
+int cugo_b200_gemm_bf16_window(const void* a, int64_t lda, const void* w, int64_t ldw,
+                               const void* bias, int32_t bias_fp32, const void* residual,
+                               int64_t ldr, void* out, int64_t ldo, int32_t out_fp32,
+                               int32_t act, int32_t act_after, int64_t m, int64_t n, int64_t k,
+                               const int32_t* window, int32_t* error, cudaStream_t stream) {
+  if (!window || (reinterpret_cast<uintptr_t>(window) & 3u)) return CUGO_B200_ERR_ARG;
+  return gemm_launch(a, lda, w, ldw, bias, bias_fp32, residual, ldr, out, ldo, out_fp32, act,
+                     act_after, m, n, k, window, error, stream);
 }
 
 }  // extern "C"

@@ -44,6 +44,8 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_observe_indexed_bf16": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_gemm_bf16_ex": [_VP, _I64, _VP, _I64, _VP, _I32, _VP, _I64, _VP, _I64, _I32, _I32,
                                _I32, _I64, _I64, _I64, _VP, _VP],
+    "cugo_b200_gemm_bf16_window": [_VP, _I64, _VP, _I64, _VP, _I32, _VP, _I64, _VP, _I64, _I32,
+                                   _I32, _I32, _I64, _I64, _I64, _VP, _VP, _VP],
     "cugo_b200_observe_query_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_observe_critic_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP],
     "cugo_b200_redeal": [_VP, _I64, _VP, _I64, _I32, _VP],
@@ -423,7 +425,8 @@ class CugoB200Extension:
     def linear(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
                residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
                act: int = 0, act_after: int = 0, out_dtype: torch.dtype = torch.bfloat16,
-               error: torch.Tensor | None = None) -> torch.Tensor:
+               error: torch.Tensor | None = None,
+               window: torch.Tensor | None = None) -> torch.Tensor:
         """out = act_after(act(a @ w.T + bias) + residual) on tcgen05 tensor cores.
 
         act codes: 0 none, 1 ReLU, 2 SiLU, 3 GELU (erf).  bias may be bf16 or fp32;
@@ -441,13 +444,19 @@ class CugoB200Extension:
             raise RuntimeError("linear residual must have the output's dtype")
         if bias is not None and bias.dtype not in (torch.bfloat16, torch.float32):
             raise RuntimeError("linear bias must be bf16 or fp32")
-        with torch.cuda.device(a.device):
-            _check(self._lib.cugo_b200_gemm_bf16_ex(
-                _ptr(a), a.stride(0), _ptr(w), w.stride(0), _ptr(bias),
+        args = (_ptr(a), a.stride(0), _ptr(w), w.stride(0), _ptr(bias),
                 int(bias is not None and bias.dtype == torch.float32), _ptr(residual),
                 residual.stride(0) if residual is not None else 0, _ptr(out), out.stride(0),
-                int(out.dtype == torch.float32), act, act_after, m, n, k, _ptr(error),
-                self._stream(a.device)), "gemm_bf16")
+                int(out.dtype == torch.float32), act, act_after, m, n, k)
+        with torch.cuda.device(a.device):
+            if window is None:
+                _check(self._lib.cugo_b200_gemm_bf16_ex(*args, _ptr(error), self._stream(a.device)),
+                       "gemm_bf16")
+            else:
+                if window.dtype != torch.int32 or window.numel() < 2 or not window.is_cuda:
+                    raise RuntimeError("linear window must be a CUDA int32 tensor {first row, rows}")
+                _check(self._lib.cugo_b200_gemm_bf16_window(*args, _ptr(window), _ptr(error),
+                                                            self._stream(a.device)), "gemm_bf16_window")
         return out
 
     def redeal_worlds(self, states, env_ids, seats, worlds: int, seed: int = 0, tries: int = 8,

@@ -20,6 +20,9 @@ FLOPs of one launch:
                        3x512 critic) and 4 redealt worlds per decision: action_values,
                        the reference's composition of the same ops, redeal_worlds,
                        world_values (depth 1), observe_critic_bf16 at 1,804 B per child
+  evaluate  PAIRS      paired evaluation of two 3x512 SiLU actors (2 x PAIRS games to the
+                       end): the fused evaluator (one CUDA graph per decision step) and
+                       the reference's host-compacting loop over the same ops and networks
   ppo       B          one PPO minibatch step (3x512 actor + critic, B rows) on the fused
                        networks, and the same step with plain PyTorch modules under bf16
                        autocast (cuBLAS) for comparison
@@ -177,6 +180,68 @@ def allaction_case(r: int, warmup: int = 3, iters: int = 10) -> dict:
                 world_children_per_s=4 * children / sec_world)
 
 
+def evaluate_case(pairs: int, warmup: int = 1, iters: int = 3) -> dict:
+    """evaluate_paired (python/cugo_eval50.py:137-361): games/s of the fused evaluator
+    and of the reference's loop structure (compaction and per-policy index copies every
+    step, three host synchronisations per step) on the same native ops and networks."""
+    import time
+    from .evaluate import evaluate_paired, make_seeds
+    from .ppo import FusedResidualMlp
+    ext = load_extension()
+    dev = torch.device("cuda")
+    nets = []
+    for seed in (1, 2):
+        torch.manual_seed(seed)
+        net = FusedResidualMlp(720, 179, 512, 3, "silu").to(dev)
+        with torch.no_grad():
+            for p in net.parameters():
+                p.copy_(torch.randn_like(p) * (1.0 / p.shape[-1]) ** 0.5)
+        nets.append(net)
+    a, b = nets
+
+    def reference_loop(offset: int) -> float:
+        seeds, first = make_seeds(pairs, offset, dev)
+        states = ext.create(torch.cat((seeds, seeds)), torch.cat((first, first)))
+        a_seat = (torch.arange(2 * pairs, device=dev) >= pairs).long()
+        active = torch.arange(2 * pairs, device=dev)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            for _ in range(128):
+                features, legal, players, done, _ = ext.observe_indexed(states, active)
+                keep = torch.nonzero(~done).squeeze(1)
+                active, features, legal = active[keep], features[keep], legal[keep]
+                if active.numel() == 0:
+                    break
+                use_a = players[keep].long() == a_seat[active]
+                actions = torch.empty(active.numel(), dtype=torch.int64, device=dev)
+                for net, rows in ((a, torch.nonzero(use_a).squeeze(1)),
+                                  (b, torch.nonzero(~use_a).squeeze(1))):
+                    if rows.numel():
+                        logits = net(features[rows]).float().masked_fill(~legal[rows], -1.0e30)
+                        actions.index_copy_(0, rows, logits.argmax(1))
+                _, new_done = ext.step_indexed(states, active, actions)[:2]
+                active = active[torch.nonzero(~new_done).squeeze(1)]
+                if active.numel() == 0:
+                    break
+        torch.cuda.synchronize()
+        return time.perf_counter() - t0
+
+    for i in range(warmup):
+        evaluate_paired(ext, a, b, pairs, 1000 + i, 128)
+        reference_loop(1000 + i)
+    ours, ref, steps = [], [], 0
+    for i in range(iters):
+        s = evaluate_paired(ext, a, b, pairs, 2000 + i, 128)
+        ours.append(s.seconds)
+        steps = s.decision_steps
+        ref.append(reference_loop(2000 + i))
+    sec, sec_ref = min(ours), min(ref)
+    return dict(pairs=pairs, games=2 * pairs, decision_steps=steps, seconds=sec,
+                games_per_s=2 * pairs / sec, reference_loop_seconds=sec_ref,
+                reference_loop_games_per_s=2 * pairs / sec_ref)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case")
@@ -328,6 +393,9 @@ def main() -> None:
     elif args.case == "allaction":
         (r,) = d
         out.update(allaction_case(r, args.warmup, args.iters))
+    elif args.case == "evaluate":
+        (p,) = d
+        out.update(evaluate_case(p, args.warmup, args.iters))
     elif args.case == "ppo":
         (b,) = d
         out.update(ppo_case(b, args.warmup, args.iters))

@@ -204,6 +204,20 @@ CUGO_B200_API int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void*
                                          int32_t act_after, int64_t m, int64_t n, int64_t k,
                                          int32_t* error, cudaStream_t stream);
 
+/* cugo_b200_gemm_bf16_ex over a row window read from device memory when the
+ * kernel starts: window = int32 {first row, rows} (clamped to [0, m]); only those
+ * rows of a and out (and residual) are touched, the others keep their values
+ * except that the last 128-row tile of the window may also write the up to 127
+ * rows that follow it.  For CUDA graphs whose row counts change between replays
+ * (m, the maps' extent, stays fixed).  No counterpart in the reference. */
+CUGO_B200_API int cugo_b200_gemm_bf16_window(const void* a, int64_t lda, const void* w,
+                                             int64_t ldw, const void* bias, int32_t bias_fp32,
+                                             const void* residual, int64_t ldr, void* out,
+                                             int64_t ldo, int32_t out_fp32, int32_t act,
+                                             int32_t act_after, int64_t m, int64_t n, int64_t k,
+                                             const int32_t* window, int32_t* error,
+                                             cudaStream_t stream);
+
 /* One-output layer (the scalar value head of OracleCritic, python/cugo_ppo_nets50.py:
  * 67-87: nn.Linear(hidden, 1) under autocast): out[r * ldo] = a[r, :k] . w + *bias,
  * a bf16 [m, k] (lda, 16-byte aligned rows), w fp32 [k] (the bf16-rounded weight
