@@ -19,6 +19,15 @@
 //                            among 414 (274) inputs, so a gather-sum reads ~30
 //                            weight rows instead of running a K=414 GEMM.
 //
+//   encode_events_kernel     the observer-relative event tokens themselves
+//                            (encode_events, python/cugo_seq50.py:91-109) for
+//                            callers that feed them to their own layers;
+//   games_attention_kernel   the attention of the training forward over whole
+//                            games (SeqNet.forward_games, python/cugo_seq50.py:
+//                            240-265): per (game, seat) sequence the opening,
+//                            causal event tokens and one query per decision that
+//                            sees the events visible at that decision and itself.
+//
 // All of them are memory- or latency-bound; they use warp-per-row (or
 // warp-per-(query, head)) mappings with 16-byte accesses.
 #include <cuda_bf16.h>
@@ -448,6 +457,202 @@ int launch_status() { return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : 
 
 unsigned blocks_for_warps(i64 warps) { return static_cast<unsigned>((warps + 7) / 8); }
 
+// encode_events (python/cugo_seq50.py:91-109): token (b, e) for e < length of
+// sequence b, 414 columns: 8 card planes of 50 (played, drawn — the observer's own
+// draws only, flipped, my gain, opponent gain, my loss, opponent loss, shown), the
+// event kind one-hot (clamped to 11), "mine" and the opponent's drawn-card count;
+// valid[b, e] = e < count[b].  Positions past the count are encoded from their
+// (zero) words as the reference does.  A warp per token, lanes over columns.
+template <typename T>
+__global__ void __launch_bounds__(256) encode_events_kernel(
+    const i64* __restrict__ events, i64 max_events, const i64* __restrict__ count,
+    const i64* __restrict__ seats, i64 b_rows, int length, T* __restrict__ out,
+    bool* __restrict__ valid) {
+  const i64 tok = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (tok >= b_rows * length) return;
+  const i64 b = tok / length;
+  const int e = static_cast<int>(tok - b * length);
+  const i64* ev = events + (b * max_events + e) * 9;
+  const i64 seat = __ldg(seats + b);
+  const i64 header = __ldg(ev + 8);
+  const bool me = (header & 0xFF) == seat;
+  const int kind = static_cast<int>((header >> 8) & 0xFF);
+  const bool first = seat == 0;
+  constexpr u64 k50 = (1ull << 50) - 1;
+  const u64 w1 = static_cast<u64>(__ldg(ev + 1));
+  const u64 masks[8] = {static_cast<u64>(__ldg(ev + 0)) & k50, me ? (w1 & k50) : 0ull,
+                        static_cast<u64>(__ldg(ev + 2)) & k50,
+                        static_cast<u64>(__ldg(ev + (first ? 3 : 4))) & k50,
+                        static_cast<u64>(__ldg(ev + (first ? 4 : 3))) & k50,
+                        static_cast<u64>(__ldg(ev + (first ? 5 : 6))) & k50,
+                        static_cast<u64>(__ldg(ev + (first ? 6 : 5))) & k50,
+                        static_cast<u64>(__ldg(ev + 7)) & k50};
+  const float opp_drawn = me ? 0.0f : static_cast<float>(__popcll(w1 & k50));
+  const int hot = 400 + (kind < 11 ? kind : 11);
+  T* row = out + tok * kEventIn;
+  for (int c = lane; c < kEventIn; c += 32) {
+    float v;
+    if (c < 400) {
+      const int slot = c / 50;
+      u64 m = masks[0];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) m = slot == k ? masks[k] : m;
+      v = static_cast<float>((m >> (c - 50 * slot)) & 1ull);
+    } else if (c < 412) {
+      v = c == hot ? 1.0f : 0.0f;
+    } else {
+      v = c == 412 ? (me ? 1.0f : 0.0f) : opp_drawn;
+    }
+    if constexpr (sizeof(T) == 2) row[c] = __float2bfloat16_rn(v);
+    else row[c] = v;
+  }
+  if (lane == 0 && valid) valid[tok] = e < __ldg(count + b);
+}
+
+// Attention of SeqNet.forward_games (python/cugo_seq50.py:240-265, _encode :200-222)
+// for 8 heads of 32.  Token rows of the [qkv] buffer come in three blocks: the S
+// openings (row s), the S x L events (row S + s L + e) and the S x Q decision
+// queries (row S + S L + s Q + q).  The opening sees itself; event e sees the
+// opening and events 0..e; query q sees the opening, the first min(seen[s, q], L)
+// events and itself.
+//
+// One block per sequence (grid-stride): the keys and values of its opening and
+// events — the keys every token of the sequence shares — are staged once in shared
+// memory.  A warp item is (head, 32 consecutive tokens of the sequence), one token
+// per lane: the lane holds its q (and, for a query, its own k and v) in registers
+// and walks the shared keys in order with an online softmax.  At each step every
+// lane reads the same key and value rows (shared-memory broadcasts), so the item
+// runs without shuffles; lanes whose token sees fewer keys idle through the tail.
+constexpr int kKvPitch = 256 + 8;  // bf16 per staged row (528 bytes)
+constexpr int kGamesBlock = 128;
+
+__device__ __forceinline__ void load_head(const __nv_bfloat16* p, float* f) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) bf16x8(__ldg(reinterpret_cast<const uint4*>(p) + q), f + 8 * q);
+}
+
+__global__ void __launch_bounds__(kGamesBlock, 4) games_attention_kernel(
+    const __nv_bfloat16* __restrict__ qkv, i64 ldq, int n_seq, int length, int queries,
+    const i64* __restrict__ seen, float scale, __nv_bfloat16* __restrict__ out, i64 ldo) {
+  extern __shared__ uint4 kv_raw[];
+  const int pre = 1 + length;  // opening + events
+  __nv_bfloat16* kp = reinterpret_cast<__nv_bfloat16*>(kv_raw);
+  __nv_bfloat16* vp = kp + pre * kKvPitch;
+  const int warp = threadIdx.x >> 5, warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int tokens = pre + queries;
+  const int groups = (tokens + 31) >> 5;
+  const i64 ev0 = n_seq, q0 = (i64)n_seq + (i64)n_seq * length;
+  for (int s = blockIdx.x; s < n_seq; s += gridDim.x) {
+    __syncthreads();  // the previous sequence's readers are done with the stage
+    for (int idx = threadIdx.x; idx < pre * 64; idx += blockDim.x) {
+      const int row = idx >> 6, piece = idx & 63, part = piece >> 5, p = piece & 31;
+      const i64 g = row == 0 ? (i64)s : ev0 + (i64)s * length + (row - 1);
+      const uint4 val = __ldg(reinterpret_cast<const uint4*>(qkv + g * ldq + 256 * (1 + part)) + p);
+      reinterpret_cast<uint4*>((part ? vp : kp) + row * kKvPitch)[p] = val;
+    }
+    __syncthreads();
+    for (int item = warp; item < groups * 8; item += warps) {
+      const int h = item & 7;
+      const int i = (item >> 3) * 32 + lane;  // this lane's token
+      const bool live = i < tokens;
+      i64 r = 0;
+      int n_pre = 0;
+      bool self = false;
+      if (live) {
+        if (i == 0) {
+          r = s;
+          n_pre = 1;
+        } else if (i <= length) {
+          r = ev0 + (i64)s * length + (i - 1);
+          n_pre = i + 1;
+        } else {
+          const int q = i - pre;
+          r = q0 + (i64)s * queries + q;
+          i64 sn = __ldg(seen + (i64)s * queries + q);
+          sn = sn < 0 ? 0 : (sn > length ? length : sn);
+          n_pre = 1 + static_cast<int>(sn);
+          self = true;
+        }
+      }
+      const __nv_bfloat16* row = qkv + r * ldq + h * kDh;
+      float qv[kDh], acc[kDh];
+      if (live) load_head(row, qv);
+#pragma unroll
+      for (int d = 0; d < kDh; ++d) {
+        qv[d] = live ? qv[d] * scale : 0.0f;
+        acc[d] = 0.0f;
+      }
+      float m = -INFINITY, l = 0.0f;
+      int n_max = n_pre;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) n_max = max(n_max, __shfl_xor_sync(kFull, n_max, o));
+      for (int j = 0; j < n_max; ++j) {
+        const __nv_bfloat16* krow = kp + j * kKvPitch + h * kDh;
+        float part[4];  // four independent chains instead of one 32-long one
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          float kf[8];
+          bf16x8(reinterpret_cast<const uint4*>(krow)[p], kf);
+          part[p] = 0.0f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) part[p] = fmaf(qv[8 * p + e], kf[e], part[p]);
+        }
+        const float dot = (part[0] + part[1]) + (part[2] + part[3]);
+        if (j < n_pre) {
+          if (dot > m) {  // a new maximum: rescale what has been summed (rare after a few keys)
+            const float c = __expf(m - dot);  // 0 on the first key (m = -inf)
+            l *= c;
+#pragma unroll
+            for (int d = 0; d < kDh; ++d) acc[d] *= c;
+            m = dot;
+          }
+          const float pj = __expf(dot - m);
+          l += pj;
+          const __nv_bfloat16* vrow = vp + j * kKvPitch + h * kDh;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            float vf[8];
+            bf16x8(reinterpret_cast<const uint4*>(vrow)[p], vf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[8 * p + e] = fmaf(pj, vf[e], acc[8 * p + e]);
+          }
+        }
+      }
+      if (self) {  // a query's own key and value, from its row
+        float kf[kDh], vf[kDh];
+        load_head(row + 256, kf);
+        load_head(row + 512, vf);
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int d = 0; d < kDh; ++d) part[d & 3] = fmaf(qv[d], kf[d], part[d & 3]);
+        const float dot = (part[0] + part[1]) + (part[2] + part[3]);
+        const float m_new = fmaxf(m, dot);
+        const float c = __expf(m - m_new), pj = __expf(dot - m_new);
+        l = fmaf(l, c, pj);
+#pragma unroll
+        for (int d = 0; d < kDh; ++d) acc[d] = fmaf(acc[d], c, pj * vf[d]);
+      }
+      if (live) {
+        const float inv = 1.0f / l;
+        __nv_bfloat16* o = out + r * ldo + h * kDh;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          uint4 raw;
+          __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            hh[e] = __floats2bfloat162_rn(acc[8 * p + 2 * e] * inv, acc[8 * p + 2 * e + 1] * inv);
+          reinterpret_cast<uint4*>(o)[p] = raw;
+        }
+      }
+    }
+  }
+}
+
+// Dynamic shared memory of games_attention_kernel for `length` events.
+constexpr int games_smem_bytes(int length) { return 2 * (1 + length) * kKvPitch * 2; }
+
 }  // namespace
 
 extern "C" {
@@ -541,5 +746,53 @@ int cugo_b200_start_embed(const int64_t* start, int64_t n_start, const int64_t* 
 
 int64_t cugo_b200_event_inputs(void) { return kEventIn; }
 int64_t cugo_b200_start_inputs(void) { return kStartIn; }
+
+int cugo_b200_encode_events(const int64_t* events, int64_t max_events, const int64_t* count,
+                            const int64_t* seats, int64_t b_rows, int32_t length, void* tokens,
+                            int32_t tokens_bf16, bool* valid, cudaStream_t stream) {
+  if (b_rows < 0 || length < 0 || length > max_events || max_events <= 0) return CUGO_B200_ERR_ARG;
+  const i64 n = b_rows * length;
+  if (n == 0) return CUGO_B200_OK;
+  if (!events || !count || !seats || !tokens) return CUGO_B200_ERR_ARG;
+  const unsigned grid = static_cast<unsigned>((n * 32 + 255) / 256);
+  if (tokens_bf16)
+    encode_events_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        events, max_events, count, seats, b_rows, length, static_cast<__nv_bfloat16*>(tokens), valid);
+  else
+    encode_events_kernel<float><<<grid, 256, 0, stream>>>(events, max_events, count, seats, b_rows,
+                                                          length, static_cast<float*>(tokens), valid);
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+int cugo_b200_games_attention(const void* qkv, int64_t ldq, int64_t n_seq, int32_t length,
+                              int32_t queries, const int64_t* seen, float scale, void* out,
+                              int64_t ldo, cudaStream_t stream) {
+  if (n_seq < 0 || n_seq > INT32_MAX || length < 0 || length > kMaxEvents || queries < 0 ||
+      ldq < 768 || ldo < 256)
+    return CUGO_B200_ERR_ARG;
+  if (n_seq == 0) return CUGO_B200_OK;
+  if (!qkv || !out || (queries > 0 && !seen)) return CUGO_B200_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(qkv) & 15u) || ldq % 8 || (reinterpret_cast<uintptr_t>(out) & 15u) ||
+      ldo % 8)
+    return CUGO_B200_ERR_ALIGN;
+  const int smem = games_smem_bytes(length);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUGO_B200_ERR_LAUNCH;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(games_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             games_smem_bytes(kMaxEvents)) != cudaSuccess)
+      return CUGO_B200_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const i64 cap = static_cast<i64>(sms) * 4;
+  const unsigned grid = static_cast<unsigned>(n_seq < cap ? n_seq : cap);
+  games_attention_kernel<<<grid, kGamesBlock, smem, stream>>>(
+      static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<int>(n_seq), length, queries, seen,
+      scale, static_cast<__nv_bfloat16*>(out), ldo);
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
 
 }  // extern "C"

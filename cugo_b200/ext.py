@@ -50,6 +50,9 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_observe_critic_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP],
     "cugo_b200_redeal": [_VP, _I64, _VP, _I64, _I32, _VP],
     "cugo_b200_redeal_worlds": [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I32, _VP, _VP, _VP],
+    "cugo_b200_encode_events": [_VP, _I64, _VP, _VP, _I64, _I32, _VP, _I32, _VP, _VP],
+    "cugo_b200_games_attention": [_VP, _I64, _I64, _I32, _I32, _VP, ctypes.c_float, _VP, _I64,
+                                  _VP],
     "cugo_b200_rowdot_bf16": [_VP, _I64, _VP, _VP, _I64, _I64, _VP, _I64, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
@@ -478,6 +481,43 @@ class CugoB200Extension:
                 _ptr(states), states.size(0), _ptr(env_ids), r, _ptr(seats), worlds, seed, tries,
                 _ptr(out), _ptr(acc), self._stream(dev)), "redeal_worlds")
         return (out, acc) if with_attempts else out
+
+    def encode_events(self, events: torch.Tensor, count: torch.Tensor, seats: torch.Tensor,
+                      length: int, dtype: torch.dtype = torch.float32):
+        """encode_events (python/cugo_seq50.py:91-109): tokens [B, length, 414] of dtype
+        (fp32 or bf16) and the validity mask [B, length]."""
+        if events.dtype != torch.int64 or events.dim() != 3 or events.size(2) != self.EVENT_WORDS \
+                or not events.is_contiguous():
+            raise RuntimeError("events must be a contiguous int64 [B, max_events, 9] tensor")
+        if dtype not in (torch.float32, torch.bfloat16):
+            raise RuntimeError("encode_events writes fp32 or bf16 tokens")
+        _check_cuda_1d(count, torch.int64, "count")
+        _check_cuda_1d(seats, torch.int64, "seats")
+        b = events.size(0)
+        dev = events.device
+        with torch.cuda.device(dev):
+            tokens = torch.empty((b, length, self.EVENT_IN), dtype=dtype, device=dev)
+            valid = torch.empty((b, length), dtype=torch.bool, device=dev)
+            _check(self._lib.cugo_b200_encode_events(
+                _ptr(events), events.size(1), _ptr(count), _ptr(seats), b, length, _ptr(tokens),
+                int(dtype == torch.bfloat16), _ptr(valid), self._stream(dev)), "encode_events")
+        return tokens, valid
+
+    def games_attention(self, qkv: torch.Tensor, n_seq: int, length: int, queries: int,
+                        seen: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Attention of SeqNet.forward_games over the three token blocks of qkv."""
+        if qkv.dtype != torch.bfloat16 or qkv.dim() != 2 or qkv.stride(1) != 1:
+            raise RuntimeError("qkv must be row-major bf16 [rows, 768]")
+        rows = n_seq * (1 + length + queries)
+        if qkv.size(0) != rows:
+            raise RuntimeError("games_attention: qkv must hold n_seq * (1 + length + queries) rows")
+        if out is None:
+            out = torch.empty((rows, 256), dtype=torch.bfloat16, device=qkv.device)
+        with torch.cuda.device(qkv.device):
+            _check(self._lib.cugo_b200_games_attention(
+                _ptr(qkv), qkv.stride(0), n_seq, length, queries, _ptr(seen), 32 ** -0.5, _ptr(out),
+                out.stride(0), self._stream(qkv.device)), "games_attention")
+        return out
 
     def rowdot(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
                out: torch.Tensor | None = None) -> torch.Tensor:

@@ -20,6 +20,10 @@ FLOPs of one launch:
                        3x512 critic) and 4 redealt worlds per decision: action_values,
                        the reference's composition of the same ops, redeal_worlds,
                        world_values (depth 1), observe_critic_bf16 at 1,804 B per child
+  seqgames  S L Q      the sequence training forward over S (game, seat) sequences of L
+                       events and Q decisions (4-layer d256 policy): native forward_games
+                       and the reference's formulation in PyTorch (bf16 autocast, SDPA
+                       with the boolean mask), each timed with CUDA events
   evaluate  PAIRS      paired evaluation of two 3x512 SiLU actors (2 x PAIRS games to the
                        end): the fused evaluator (one CUDA graph per decision step) and
                        the reference's host-compacting loop over the same ops and networks
@@ -178,6 +182,102 @@ def allaction_case(r: int, warmup: int = 3, iters: int = 10) -> dict:
                 observe_critic_seconds=sec_obs, observe_critic_gbs=children * 1804 / sec_obs / 1e9,
                 redeal_worlds4_seconds=sec_redeal, world_values4_seconds=sec_world,
                 world_children_per_s=4 * children / sec_world)
+
+
+def seqgames_case(s_n: int, length: int, q_n: int, warmup: int = 3, iters: int = 10) -> dict:
+    """SeqNet.forward_games (python/cugo_seq50.py:240-265) on the native kernels and, for
+    comparison, the same function as the reference formulates it in PyTorch under bf16
+    autocast (token embeddings as Linear layers, scaled_dot_product_attention with a
+    [S, 1, T, T] boolean mask), on seeded synthetic histories."""
+    from types import SimpleNamespace
+    from .seq import SeqDecoder
+    f = torch.nn.functional
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(0)
+    k50 = (1 << 50) - 1
+    # Events as the engine writes them: each of the 8 card words holds 0-2 cards.
+    cards = torch.randint(0, 50, (s_n, 48, 8, 2), generator=g)
+    keep = torch.randint(0, 2, (s_n, 48, 8, 2), generator=g)
+    bits = (torch.ones_like(cards) << cards) * keep
+    ev = torch.zeros((s_n, 48, 9), dtype=torch.int64)
+    ev[..., :8] = bits[..., 0] | bits[..., 1]
+    ev[..., 8] = torch.randint(0, 2, (s_n, 48), generator=g) | (torch.randint(0, 12, (s_n, 48), generator=g) << 8)
+    count = torch.full((s_n,), length, dtype=torch.int64)
+    start = torch.randint(0, 1 << 62, (s_n, 8), generator=g) & k50
+    start[:, 6] &= (1 << 12) - 1
+    start[:, 7] &= 0xFFFF
+    seat = torch.arange(s_n) & 1
+    seen = torch.randint(0, length + 1, (s_n, q_n), generator=g).sort(1).values
+    feats = torch.rand((s_n, q_n, 720), generator=g).to(torch.bfloat16)
+    legal = torch.rand((s_n, q_n, 179), generator=g) < 0.1
+    t = {k: v.to(dev) for k, v in dict(events=ev, count=count, start=start, seat=seat, seen=seen,
+                                        feats=feats, legal=legal).items()}
+    hist = SimpleNamespace(events=t["events"], count=t["count"], start=t["start"], seat=t["seat"])
+    state = SeqDecoder.random_state(seed=0)
+    dec = SeqDecoder.from_state_dict(state, device=dev)
+    p = {k: v.to(dev) for k, v in state.items()}
+
+    def native():
+        return dec.forward_games(hist, t["feats"], t["legal"], t["seen"], length=length)
+
+    # The reference's formulation: multi-hot tokens through Linear layers, SDPA with a mask.
+    bits = torch.arange(50, device=dev)
+    tt = length + 1 + q_n
+    allowed = torch.zeros(s_n, tt, tt, dtype=torch.bool, device=dev)
+    allowed[:, :, 0] = True
+    allowed[:, 1:length + 1, 1:length + 1] = torch.ones(length, length, dtype=torch.bool, device=dev).tril()
+    allowed[:, length + 1:, 1:length + 1] = torch.arange(length, device=dev).view(1, 1, -1) < t["seen"].unsqueeze(-1)
+    allowed[:, length + 1:, length + 1:] = torch.eye(q_n, dtype=torch.bool, device=dev)
+    mask = allowed.unsqueeze(1)
+
+    def lin(x, n):
+        return f.linear(x, p[n + ".weight"], p[n + ".bias"])
+
+    def torch_forward():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            e = t["events"][:, :length]
+            sv = t["seat"].view(-1, 1)
+            mine = (e[..., 8] & 0xFF) == sv
+            s0 = sv == 0
+            slots = (e[..., 0], torch.where(mine, e[..., 1], 0), e[..., 2],
+                     torch.where(s0, e[..., 3], e[..., 4]), torch.where(s0, e[..., 4], e[..., 3]),
+                     torch.where(s0, e[..., 5], e[..., 6]), torch.where(s0, e[..., 6], e[..., 5]), e[..., 7])
+            planes = [((m.unsqueeze(-1) >> bits) & 1).to(torch.bfloat16) for m in slots]
+            kind = f.one_hot(((e[..., 8] >> 8) & 0xFF).clamp_max(11), 12).to(torch.bfloat16)
+            drawn = torch.where(mine, 0, ((e[..., 1].unsqueeze(-1) >> bits) & 1).sum(-1))
+            tok = torch.cat((*planes, kind, mine.unsqueeze(-1).to(torch.bfloat16),
+                             drawn.unsqueeze(-1).to(torch.bfloat16)), -1)
+            st = t["start"]
+            sp = ((torch.stack((st[:, 0], st[:, 2], st[:, 3], st[:, 4], st[:, 5]), -1).unsqueeze(-1) >> bits) & 1)
+            stok = torch.cat((sp.flatten(-2).float(), ((st[:, 6:7] >> bits[:12]) & 1).float(),
+                              f.one_hot((st[:, 7] & 0xFF).clamp_max(7), 8).float(),
+                              torch.zeros((s_n, 4), device=dev)), -1)
+            x = torch.cat(((lin(stok, "start_in") + p["position"][0] + p["token_type"][0]).unsqueeze(1),
+                           lin(tok, "event_in") + p["position"][1:length + 1] + p["token_type"][1],
+                           lin(f.gelu(lin(torch.cat((t["feats"], t["legal"].to(torch.bfloat16)), -1),
+                                          "query_in.0")), "query_in.2") + p["token_type"][2]), 1)
+            for i in range(4):
+                pre = f"encoder.layers.{i}."
+                a = f.layer_norm(x, (256,), p[pre + "norm1.weight"], p[pre + "norm1.bias"])
+                qkv = f.linear(a, p[pre + "self_attn.in_proj_weight"], p[pre + "self_attn.in_proj_bias"])
+                q, k, v = (z.reshape(s_n, tt, 8, 32).transpose(1, 2) for z in qkv.chunk(3, -1))
+                att = f.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+                x = x + lin(att.transpose(1, 2).reshape(s_n, tt, 256), pre + "self_attn.out_proj")
+                a = f.layer_norm(x, (256,), p[pre + "norm2.weight"], p[pre + "norm2.bias"])
+                x = x + lin(f.gelu(lin(a, pre + "linear1")), pre + "linear2")
+            h = f.layer_norm(x[:, length + 1:], (256,), p["norm.weight"], p["norm.bias"])
+            return lin(f.gelu(lin(h, "head.0")), "head.2").float()
+
+    with torch.no_grad():
+        sec = _time(native, warmup, iters)
+        sec_torch = _time(torch_forward, warmup, iters)
+    rows = s_n * tt
+    layer_flops = 2 * rows * (256 * 768 + 256 * 256 + 2 * 256 * 1024) * 4
+    query_flops = 2 * s_n * q_n * (899 * 512 + 512 * 256 + 256 * 256 + 256 * 179)
+    flops = layer_flops + query_flops
+    return dict(sequences=s_n, length=length, queries=q_n, tokens=rows, seconds=sec,
+                decisions_per_s=s_n * q_n / sec, tflops=flops / sec / 1e12,
+                torch_autocast_seconds=sec_torch, torch_autocast_decisions_per_s=s_n * q_n / sec_torch)
 
 
 def evaluate_case(pairs: int, warmup: int = 1, iters: int = 3) -> dict:
@@ -393,6 +493,9 @@ def main() -> None:
     elif args.case == "allaction":
         (r,) = d
         out.update(allaction_case(r, args.warmup, args.iters))
+    elif args.case == "seqgames":
+        s_n, length, q_n = d
+        out.update(seqgames_case(s_n, length, q_n, args.warmup, args.iters))
     elif args.case == "evaluate":
         (p,) = d
         out.update(evaluate_case(p, args.warmup, args.iters))

@@ -50,6 +50,15 @@ def decode_attention(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, 
     return out if q.dtype == torch.bfloat16 else out.to(q.dtype)
 
 
+def encode_events(h, length: int, dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
+    """Drop-in for the reference's encode_events (python/cugo_seq50.py:91-109) on the
+    device: h has .events int64 [B, MAX_EVENTS, 9], .count [B], .seat [B]; returns the
+    observer-relative tokens [B, length, 414] (fp32 or bf16) and their validity mask."""
+    ext = load_extension()
+    return ext.encode_events(h.events.contiguous(), h.count.contiguous(), h.seat.contiguous(),
+                             length, dtype)
+
+
 @dataclass
 class _Layer:
     norm1_w: torch.Tensor
@@ -228,6 +237,51 @@ class SeqDecoder:
             f = ext.linear(a, L.w1, L.b1, act=ACT_GELU)
             ext.linear(f, L.w2, L.b2, residual=x, out=x)
         return x
+
+    # -- training forward over whole games ---------------------------------------
+    def forward_games(self, hist, features: torch.Tensor, legal: torch.Tensor,
+                      seen: torch.Tensor, length: int | None = None) -> torch.Tensor:
+        """SeqNet.forward_games (python/cugo_seq50.py:240-265): every decision of each
+        (game, seat) sequence at once.  hist has .events int64 [S, MAX_EVENTS, 9],
+        .count [S] (the game's events), .start [S, 8], .seat [S]; features [S, Q, 720],
+        legal [S, Q, 179], seen int64 [S, Q] (events visible at each decision).
+        Returns fp32 [S, Q, outputs].
+
+        Token rows live in three blocks — S openings, S x L events, S x Q queries —
+        embedded straight into the fp32 residual stream by the start/event gather-sum
+        kernels and the query MLP; each layer is LayerNorm, the QKV GEMM, the games
+        attention kernel (opening, causal events, queries over their visible events
+        and themselves), the out-projection and FFN GEMMs with the residual in their
+        epilogues; the head reads the query rows only."""
+        ext, d = self.ext, self.d_model
+        s_n, q_n = seen.shape
+        L = max(1, int(hist.count.max())) if length is None else max(1, length)
+        if L > MAX_EVENTS:
+            raise ValueError(f"length {L} exceeds {MAX_EVENTS} events")
+        dev = self.device
+        n_ev, n_q = s_n * L, s_n * q_n
+        x = torch.empty((s_n + n_ev + n_q, d), dtype=torch.float32, device=dev)
+        seat = hist.seat.to(dev, torch.int64).contiguous()
+        self.start_token(hist.start.to(dev).contiguous(), seat, out=x[:s_n])
+        if n_ev:
+            words = hist.events[:, :L].to(dev).reshape(n_ev, self.ext.EVENT_WORDS).contiguous()
+            index = torch.arange(L, device=dev).repeat(s_n)
+            self.event_token(words, seat.repeat_interleave(L), index, out=x[s_n:s_n + n_ev])
+        if n_q:
+            query = torch.zeros((n_q, QUERY_LD), dtype=torch.bfloat16, device=dev)
+            query[:, :FEATURES] = features.reshape(n_q, FEATURES)
+            query[:, FEATURES:QUERY_IN] = legal.reshape(n_q, ACTIONS)
+            self.query_token(query, out=x[s_n + n_ev:])
+        seen_flat = seen.to(dev, torch.int64).reshape(-1).contiguous()
+        for blk in self.blocks:
+            a = ext.layernorm(x, blk.norm1_w, blk.norm1_b, self.eps)
+            qkv = ext.linear(a, blk.w_in, blk.b_in)
+            att = ext.games_attention(qkv, s_n, L, q_n, seen_flat)
+            ext.linear(att, blk.w_out, blk.b_out, residual=x, out=x)
+            a = ext.layernorm(x, blk.norm2_w, blk.norm2_b, self.eps)
+            f = ext.linear(a, blk.w1, blk.b1, act=ACT_GELU)
+            ext.linear(f, blk.w2, blk.b2, residual=x, out=x)
+        return self.readout(x[s_n + n_ev:]).reshape(s_n, q_n, self.outputs)
 
     def readout(self, h: torch.Tensor) -> torch.Tensor:
         """SeqNet.readout (python/cugo_seq50.py:288-289, head(norm(h))): fp32 [n, outputs]."""

@@ -360,6 +360,28 @@ CUGO_B200_API int cugo_b200_start_embed(const int64_t* start, int64_t n_start,
                                         const float* token_type, int64_t d, float* out,
                                         int64_t ldo, cudaStream_t stream);
 
+/* encode_events (python/cugo_seq50.py:91-109): observer-relative event tokens
+ * [b_rows, length, 414] (fp32, or bf16 when tokens_bf16) of events int64
+ * [b_rows, max_events, 9] for observer seats[b]; valid (optional) bool
+ * [b_rows, length] = e < count[b].  Values are 0/1 and the opponent's drawn-card
+ * count, exact in either type. */
+CUGO_B200_API int cugo_b200_encode_events(const int64_t* events, int64_t max_events,
+                                          const int64_t* count, const int64_t* seats,
+                                          int64_t b_rows, int32_t length, void* tokens,
+                                          int32_t tokens_bf16, bool* valid, cudaStream_t stream);
+
+/* Attention of SeqNet.forward_games (python/cugo_seq50.py:240-265), 8 heads of 32
+ * (d 256): qkv bf16 [rows, ldq >= 768] (q | k | v) holds the token rows in three
+ * blocks: n_seq openings, then n_seq x length events (sequence-major), then
+ * n_seq x queries decision queries; out bf16 [rows, ldo] gets each row's attention
+ * output.  The opening sees itself, event e the opening and events 0..e, query q of
+ * sequence s the opening, events 0 .. min(seen[s * queries + q], length) - 1 and
+ * itself.  length <= 48; qkv and out 16-byte aligned, ldq and ldo multiples of 8. */
+CUGO_B200_API int cugo_b200_games_attention(const void* qkv, int64_t ldq, int64_t n_seq,
+                                            int32_t length, int32_t queries, const int64_t* seen,
+                                            float scale, void* out, int64_t ldo,
+                                            cudaStream_t stream);
+
 CUGO_B200_API int64_t cugo_b200_event_inputs(void); /* EVENT_IN = 414 */
 CUGO_B200_API int64_t cugo_b200_start_inputs(void); /* START_IN = 274 */
 

@@ -51,3 +51,84 @@ def query_input(features: torch.Tensor, legal: torch.Tensor, width: int = 904) -
     out[:, :720] = features.to(torch.bfloat16)
     out[:, 720:899] = legal.to(torch.bfloat16)
     return out
+
+
+# ---- the training forward over whole games (python/cugo_seq50.py:91-128, 200-265) ----
+
+def _planes(masks: torch.Tensor, width: int = 50) -> torch.Tensor:
+    """[..., width] 0/1 float planes of the low `width` bits of int64 masks."""
+    shifts = torch.arange(width, device=masks.device)
+    return ((masks.unsqueeze(-1) >> shifts) & 1).float()
+
+
+def event_tokens(events: torch.Tensor, seat: torch.Tensor, length: int) -> torch.Tensor:
+    """Observer-relative event tokens [B, length, 414] (fp32): eight card planes
+    (played, own draws, flipped, my gain, their gain, my loss, their loss, shown),
+    the kind one-hot clamped to 11, the "mine" flag and the opponent's draw count."""
+    ev = events[:, :length]
+    sv = seat.view(-1, 1)
+    mine = (ev[..., 8] & 0xFF) == sv
+    kind = ((ev[..., 8] >> 8) & 0xFF).clamp_max(11)
+    s0 = sv == 0
+    pick = lambda a, b: torch.where(s0, ev[..., a], ev[..., b])  # noqa: E731
+    slots = [ev[..., 0], torch.where(mine, ev[..., 1], torch.zeros_like(ev[..., 1])), ev[..., 2],
+             pick(3, 4), pick(4, 3), pick(5, 6), pick(6, 5), ev[..., 7]]
+    drawn = torch.where(mine, torch.zeros_like(kind), _planes(ev[..., 1]).sum(-1).long())
+    onehot = torch.nn.functional.one_hot(kind, 12).float()
+    return torch.cat([_planes(m) for m in slots] + [onehot, mine.float().unsqueeze(-1),
+                                                    drawn.float().unsqueeze(-1)], -1)
+
+
+def start_tokens(start: torch.Tensor, seat: torch.Tensor) -> torch.Tensor:
+    """Opening tokens [B, 274] (fp32): hand, floor, my and their captures, mission
+    cards, 12 neutral months, mission type one-hot (clamped to 7), multiplier / 4,
+    "I move first", my and their multi / 8."""
+    s0 = seat == 0
+    side = lambda a, b: torch.where(s0, start[:, a], start[:, b])  # noqa: E731
+    planes = _planes(torch.stack((side(0, 1), start[:, 2], side(3, 4), side(4, 3), start[:, 5]), -1))
+    head = start[:, 7]
+    mine_multi = torch.where(s0, (head >> 24) & 0xFF, (head >> 32) & 0xFF)
+    their_multi = torch.where(s0, (head >> 32) & 0xFF, (head >> 24) & 0xFF)
+    scal = torch.stack((((head >> 8) & 0xFF).float() / 4.0, (((head >> 16) & 1) == seat).float(),
+                        mine_multi.float() / 8.0, their_multi.float() / 8.0), -1)
+    return torch.cat((planes.flatten(-2), _planes(start[:, 6], 12),
+                      torch.nn.functional.one_hot((head & 0xFF).clamp_max(7), 8).float(), scal), -1)
+
+
+def forward_games(p: dict, events, count, start, seat, features, legal, seen, length: int,
+                  heads: int = HEADS) -> torch.Tensor:
+    """SeqNet.forward_games with state dict p (hybrid mode) in plain torch: tokens
+    [opening, length events, one query per decision]; the opening sees itself,
+    events are causal, a query sees the opening, its visible events and itself;
+    pre-LN layers (GELU FFN), then LayerNorm and the head on the query rows."""
+    f = torch.nn.functional
+    s_n, q_n = seen.shape
+    d = p["position"].shape[1]
+    lin = lambda x, n: f.linear(x, p[n + ".weight"], p[n + ".bias"])  # noqa: E731
+    x0 = lin(start_tokens(start, seat), "start_in") + p["position"][0] + p["token_type"][0]
+    xe = lin(event_tokens(events, seat, length), "event_in") + p["position"][1:length + 1] \
+        + p["token_type"][1]
+    xq = lin(f.gelu(lin(torch.cat((features.float(), legal.float()), -1), "query_in.0")),
+             "query_in.2") + p["token_type"][2]
+    x = torch.cat((x0.unsqueeze(1), xe, xq), 1)
+    t = 1 + length + q_n
+    allowed = torch.zeros(s_n, t, t, dtype=torch.bool, device=x.device)
+    allowed[:, :, 0] = True
+    allowed[:, 1:length + 1, 1:length + 1] = torch.ones(length, length, dtype=torch.bool,
+                                                        device=x.device).tril()
+    allowed[:, length + 1:, 1:length + 1] = torch.arange(length, device=x.device).view(1, 1, -1) \
+        < seen.unsqueeze(-1)
+    allowed[:, length + 1:, length + 1:] = torch.eye(q_n, dtype=torch.bool, device=x.device)
+    dh = d // heads
+    for i in range(len({k.split(".")[2] for k in p if k.startswith("encoder.layers.")})):
+        pre = f"encoder.layers.{i}."
+        a = f.layer_norm(x, (d,), p[pre + "norm1.weight"], p[pre + "norm1.bias"])
+        qkv = f.linear(a, p[pre + "self_attn.in_proj_weight"], p[pre + "self_attn.in_proj_bias"])
+        q, k, v = (z.reshape(s_n, t, heads, dh).transpose(1, 2) for z in qkv.chunk(3, -1))
+        sc = (q @ k.transpose(-1, -2)) * dh ** -0.5
+        att = torch.softmax(sc.masked_fill(~allowed.unsqueeze(1), float("-inf")), -1) @ v
+        x = x + lin(att.transpose(1, 2).reshape(s_n, t, d), pre + "self_attn.out_proj")
+        a = f.layer_norm(x, (d,), p[pre + "norm2.weight"], p[pre + "norm2.bias"])
+        x = x + lin(f.gelu(lin(a, pre + "linear1")), pre + "linear2")
+    h = f.layer_norm(x[:, length + 1:], (d,), p["norm.weight"], p["norm.bias"])
+    return lin(f.gelu(lin(h, "head.0")), "head.2")
