@@ -31,6 +31,7 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include "../../include/cugo_b200.h"
 
@@ -1114,6 +1115,463 @@ int cugo_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, 
   if (residual && out_fp32) return CUGO_B200_ERR_ARG;  // this entry's residual stream is bf16
   return cugo_b200_gemm_bf16_ex(a, lda, w, ldw, bias, 0, residual, ldr, out, ldo, out_fp32, act,
                                 act_after, m, n, k, error, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+// ---- the whole residual MLP in one kernel (hidden width 512) ------------------------
+//
+//   h = x W0^T + b0;  per block: h = h + act(h W1^T + b1) W2^T + b2;  out = act(h) Wo^T + bo
+//
+// (python/cugo_ppo_nets50.py:26-64, norm "none").  At hidden 512 every layer of the
+// layer-per-launch path is bound by moving activations through HBM (a 512-wide bf16
+// row is 1 KB in and 1 KB out per layer for 0.5 MFLOP); here a CTA keeps its 128-row
+// tile's activations on chip for the whole network:
+//   shared memory  ACT: the tile's 128 x 512 bf16 activations (128 KB) in the
+//                  128-byte-swizzled K-major layout the MMA reads (8 chunks of 64
+//                  columns), rewritten in place layer after layer; during the input
+//                  layer its chunks hold the x tiles streamed in by TMA, after the
+//                  head it stages the fp32 output for TMA stores;
+//                  a 3-stage ring of 256 x 64 weight tiles (32 KB each) fed by TMA;
+//   tensor memory  the fp32 accumulator of a whole layer, 128 lanes x 512 columns.
+// A block's residual never leaves the chip: the fc1 epilogue reads h from ACT, writes
+// h + b2 into the accumulator columns it has just drained (tcgen05.st) and u = act(z)
+// over h in ACT, so the fc2 MMAs accumulate u W2^T on top of h + b2.
+// Warp roles as in gemm_kernel: warp 0 the TMA producer (weights run ahead of the
+// MMAs; x tiles wait for the previous tile's output stores to leave ACT), warp 1 the
+// MMA issuer and TMEM owner, warps 2..9 the epilogue (two per TMEM lane quadrant,
+// 256 columns each).  Every wait is bounded as in gemm_kernel.
+constexpr int F_H = 512;
+constexpr int F_CHUNKS = F_H / BK;            // 8
+constexpr int F_CHUNK_BYTES = BM * BK * 2;    // 16 KB
+constexpr int F_ACT_BYTES = F_CHUNKS * F_CHUNK_BYTES;
+constexpr int F_WSTAGES = 3;
+constexpr int F_W_BYTES = BN * BK * 2;        // 32 KB
+constexpr int F_MAX_BLOCKS = 4;
+constexpr int F_MAX_LAYERS = 2 + 2 * F_MAX_BLOCKS;
+constexpr int F_MAX_KIN = 1024;
+constexpr int F_SMEM_BYTES = F_ACT_BYTES + F_WSTAGES * F_W_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+static_assert(F_SMEM_BYTES <= 232448, "fits the opt-in shared memory of one CTA");
+
+struct FusedMaps {
+  CUtensorMap x;                    // bf16 [m, k_in], box 64 x 128
+  CUtensorMap w[F_MAX_LAYERS];      // bf16 [n, k] per layer, box 64 x 256
+  CUtensorMap out;                  // fp32 [m, n_out], box 16 x 32, 64-byte swizzle
+};
+
+struct FusedArgs {
+  const float* bias[F_MAX_LAYERS];  // fp32 [n] or null
+  int blocks, m, k_in, n_out, n_mma, act;
+  int* error;
+};
+
+// ACT address of 16-byte piece p (0..7) of row r in chunk kc: the TMA 128-byte swizzle.
+__device__ __forceinline__ uint8_t* act_piece(uint8_t* act, int kc, int r, int p) {
+  return act + kc * F_CHUNK_BYTES + r * 128 + ((p ^ (r & 7)) << 4);
+}
+
+// Row r's 32 columns col0 .. col0 + 31 (col0 a multiple of 32) as bf16 into ACT.
+__device__ __forceinline__ void act_store32(uint8_t* act, int r, int col0, const float* v) {
+  const int kc = col0 >> 6, p0 = (col0 & 63) >> 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 raw;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+    *reinterpret_cast<uint4*>(act_piece(act, kc, r, p0 + j)) = raw;
+  }
+}
+
+__device__ __forceinline__ void act_load32(uint8_t* act, int r, int col0, float* v) {
+  const int kc = col0 >> 6, p0 = (col0 & 63) >> 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(act_piece(act, kc, r, p0 + j));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      v[8 * j + 2 * e] = f.x;
+      v[8 * j + 2 * e + 1] = f.y;
+    }
+  }
+}
+
+#define CB_TMEM_ST32(taddr, r)                                                                  \
+  asm volatile(                                                                                 \
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"   \
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"( \
+          taddr),                                                                               \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),   \
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),        \
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),      \
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),      \
+      "r"(r[29]), "r"(r[30]), "r"(r[31])                                                        \
+      : "memory")
+
+__device__ __forceinline__ float fused_bias(const float* b, int col) {
+  return b ? __ldg(b + col) : 0.0f;
+}
+
+// An epilogue phase is done: its TMEM reads/writes and ACT writes are visible to the
+// MMAs that follow (one arrive per epilogue warp).
+__device__ __forceinline__ void fused_phase_done(uint64_t* act_ready) {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(act_ready);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    fused_mlp_kernel(const __grid_constant__ FusedMaps maps, const __grid_constant__ FusedArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* act = smem;
+  uint8_t* wring = smem + F_ACT_BYTES;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(wring + F_WSTAGES * F_W_BYTES);
+  uint64_t* wempty = wfull + F_WSTAGES;
+  uint64_t* xfull = wempty + F_WSTAGES;  // [8]
+  uint64_t* xempty = xfull + F_CHUNKS;   // [8]
+  uint64_t* acc_full = xempty + F_CHUNKS;
+  uint64_t* act_ready = acc_full + 1;
+  uint64_t* act_free = act_ready + 1;
+  uint64_t* drained = act_free + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles = (args.m + BM - 1) / BM;
+  const int kc0 = (args.k_in + BK - 1) / BK;
+  const int hidden_layers = 2 * args.blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < F_WSTAGES; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    for (int s = 0; s < F_CHUNKS; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(act_ready, EPI_WARPS);
+    mbar_init(act_free, EPI_WARPS);
+    mbar_init(drained, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_holder)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  bool failed = false;
+
+  if (warp == 0) {
+    // ---- TMA producer: per tile the layers' weight tiles in MMA order, the x tiles
+    // into the ACT chunks ----
+    if (lane == 0) {
+      int ws = 0;
+      uint32_t wph = 0, xuse = 0;
+      auto load_w = [&](int layer, int kc, int nh) -> bool {
+        if (!mbar_wait(&wempty[ws], wph ^ 1u)) return false;
+        mbar_expect_tx(&wfull[ws], F_W_BYTES);
+        tma_load_2d(&maps.w[layer], &wfull[ws], wring + ws * F_W_BYTES, kc * BK, nh * BN);
+        if (++ws == F_WSTAGES) {
+          ws = 0;
+          wph ^= 1u;
+        }
+        return true;
+      };
+      int iter = 0;
+      for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++iter) {
+        const int row0 = t * BM;
+        for (int kc = 0; kc < kc0 && !failed; ++kc) {
+          if (!load_w(0, kc, 0) || !load_w(0, kc, 1)) {
+            failed = true;
+            break;
+          }
+          const int slot = kc & (F_CHUNKS - 1);
+          // ACT is free once the previous tile's output stores have read it; a slot's
+          // second x tile of this tile waits for the MMAs of its first.
+          if (kc == 0 && iter > 0 && !mbar_wait(act_free, (iter - 1) & 1)) {
+            failed = true;
+            break;
+          }
+          if (kc >= F_CHUNKS && !mbar_wait(&xempty[slot], ((xuse >> slot) & 1u) ^ 1u)) {
+            failed = true;
+            break;
+          }
+          mbar_expect_tx(&xfull[slot], F_CHUNK_BYTES);
+          tma_load_2d(&maps.x, &xfull[slot], act + slot * F_CHUNK_BYTES, kc * BK, row0);
+          xuse ^= 1u << slot;
+        }
+        for (int l = 1; l <= hidden_layers && !failed; ++l)
+          for (int kc = 0; kc < F_CHUNKS && !failed; ++kc)
+            if (!load_w(l, kc, 0) || !load_w(l, kc, 1)) failed = true;
+        for (int kc = 0; kc < F_CHUNKS && !failed; ++kc)
+          if (!load_w(hidden_layers + 1, kc, 0)) failed = true;
+      }
+      if (failed) {
+        for (int s = 0; s < F_WSTAGES; ++s) mbar_wait(&wfull[s], 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t idesc_h = instr_desc(BM, BN);
+      const uint32_t idesc_o = instr_desc(BM, args.n_mma);
+      int ws = 0;
+      uint32_t wph = 0, xuse = 0, ready = 0;
+      auto wait_ready = [&]() -> bool {
+        const bool ok = mbar_wait(act_ready, ready & 1u);
+        ++ready;
+        fence_after();
+        return ok;
+      };
+      // One 64-deep K step: a_addr the A chunk, into accumulator column block nh.
+      auto k_step = [&](uint32_t a_addr, int nh, uint32_t idesc, bool first) -> bool {
+        if (!mbar_wait(&wfull[ws], wph)) return false;
+        fence_after();
+        const uint32_t b_addr = smem_addr(wring + ws * F_W_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          mma_bf16(tmem_base + static_cast<uint32_t>(nh * BN), sw128_desc(a_addr + kk * 32),
+                   sw128_desc(b_addr + kk * 32), idesc, (first && kk == 0) ? 0u : 1u);
+        mma_commit(&wempty[ws]);
+        if (++ws == F_WSTAGES) {
+          ws = 0;
+          wph ^= 1u;
+        }
+        return true;
+      };
+      int iter = 0;
+      for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++iter) {
+        // The previous tile's head epilogue has drained the accumulator.
+        if (iter > 0 && !wait_ready()) {
+          failed = true;
+          break;
+        }
+        for (int kc = 0; kc < kc0 && !failed; ++kc) {
+          const int slot = kc & (F_CHUNKS - 1);
+          if (!mbar_wait(&xfull[slot], (xuse >> slot) & 1u)) {
+            failed = true;
+            break;
+          }
+          xuse ^= 1u << slot;
+          fence_after();
+          const uint32_t a_addr = smem_addr(act + slot * F_CHUNK_BYTES);
+          if (!k_step(a_addr, 0, idesc_h, kc == 0) || !k_step(a_addr, 1, idesc_h, kc == 0)) {
+            failed = true;
+            break;
+          }
+          mma_commit(&xempty[slot]);
+        }
+        if (failed) break;
+        mma_commit(acc_full);
+        for (int l = 1; l <= hidden_layers && !failed; ++l) {
+          if (!wait_ready()) {
+            failed = true;
+            break;
+          }
+          // fc2 (even l) accumulates onto h + b2, which its epilogue left in TMEM.
+          const bool fresh = (l & 1) == 1;
+          for (int kc = 0; kc < F_CHUNKS && !failed; ++kc) {
+            const uint32_t a_addr = smem_addr(act + kc * F_CHUNK_BYTES);
+            if (!k_step(a_addr, 0, idesc_h, fresh && kc == 0) ||
+                !k_step(a_addr, 1, idesc_h, fresh && kc == 0))
+              failed = true;
+          }
+          if (!failed) mma_commit(acc_full);
+        }
+        if (failed || !wait_ready()) {
+          failed = true;
+          break;
+        }
+        for (int kc = 0; kc < F_CHUNKS && !failed; ++kc)
+          if (!k_step(smem_addr(act + kc * F_CHUNK_BYTES), 0, idesc_o, kc == 0)) failed = true;
+        if (!failed) mma_commit(acc_full);
+      }
+      mma_commit(drained);
+      mbar_wait(drained, 0);
+    }
+  } else {
+    // ---- epilogue: warps 2..9 ----
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;  // this thread's row of the tile
+    const uint32_t tq = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    uint8_t* stage = act + (warp - 2) * 2 * EPI_BUF;  // output staging, after the head MMAs
+    uint32_t full_ph = 0;
+    auto wait_full = [&]() -> bool {
+      const bool ok = mbar_wait(acc_full, full_ph & 1u);
+      ++full_ph;
+      fence_after();
+      return ok;
+    };
+    const int act_code = args.act;
+    int iter = 0;
+    for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++iter) {
+      const int row0 = t * BM;
+      // Input layer: h = x W0^T + b0 (+ act when there are no blocks).
+      if (!wait_full()) {
+        failed = true;
+        break;
+      }
+      for (int c = 0; c < 8; ++c) {
+        const int col0 = half * 256 + c * 32;
+        uint32_t raw[32];
+        CB_TMEM_LD32(tq + static_cast<uint32_t>(col0), raw);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + fused_bias(args.bias[0], col0 + j);
+        if (args.blocks == 0) activate_chunk<32>(v, act_code);
+        act_store32(act, r, col0, v);
+      }
+      fused_phase_done(act_ready);
+      for (int l = 1; l <= hidden_layers && !failed; ++l) {
+        if (!wait_full()) {
+          failed = true;
+          break;
+        }
+        const bool fc1 = (l & 1) == 1;
+        const bool last = l == hidden_layers;
+        for (int c = 0; c < 8; ++c) {
+          const int col0 = half * 256 + c * 32;
+          uint32_t raw[32];
+          CB_TMEM_LD32(tq + static_cast<uint32_t>(col0), raw);
+          tmem_wait_ld();
+          float v[32];
+          if (fc1) {
+            // u = act(h W1^T + b1) over h in ACT; h + b2 into the accumulator for fc2.
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + fused_bias(args.bias[l], col0 + j);
+            activate_chunk<32>(v, act_code);
+            float h[32];
+            act_load32(act, r, col0, h);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              raw[j] = __float_as_uint(h[j] + fused_bias(args.bias[l + 1], col0 + j));
+            CB_TMEM_ST32(tq + static_cast<uint32_t>(col0), raw);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+            if (last) activate_chunk<32>(v, act_code);
+          }
+          act_store32(act, r, col0, v);
+        }
+        fused_phase_done(act_ready);
+      }
+      if (failed) break;
+      // Head: out = act(h) Wo^T + bo, fp32, through the ACT staging and TMA stores.
+      if (!wait_full()) {
+        failed = true;
+        break;
+      }
+      const int chunks = args.n_mma / 16;
+      int used = 0;
+      for (int c = half; c < chunks; c += 2, ++used) {
+        const int col0 = c * 16;
+        uint32_t raw[16];
+        CB_TMEM_LD16(tq + static_cast<uint32_t>(col0), raw);
+        tmem_wait_ld();
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          v[j] = __uint_as_float(raw[j]) +
+                 (col0 + j < args.n_out ? fused_bias(args.bias[hidden_layers + 1], col0 + j) : 0.0f);
+        uint8_t* buf = stage + (used & 1) * EPI_BUF;
+        // The store that last read this buffer (two chunks back) is done with it.
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        if (col0 < args.n_out) store_chunk<float>(buf, v, &maps.out, row0 + quad * 32, col0);
+      }
+      if (lane == 0) tma_store_wait_read<0>();  // ACT may take the next tile's x
+      __syncwarp();
+      fence_before();
+      if (lane == 0) {
+        mbar_arrive(act_ready);
+        mbar_arrive(act_free);
+      }
+    }
+    if (lane == 0) tma_store_wait_all();
+  }
+  if (failed) {
+    if (args.error) atomicExch(args.error, 1);
+    const uint64_t t0 = now_ns();
+    while (now_ns() - t0 < 100'000ull) {
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512));
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
+                        const void* const* weights, const float* const* biases, int64_t n_out,
+                        int32_t act, float* out, int64_t ldo, int32_t* error, cudaStream_t stream) {
+  if (m < 0 || k_in <= 0 || k_in > F_MAX_KIN || blocks < 0 || blocks > F_MAX_BLOCKS ||
+      n_out <= 0 || n_out > BN || !weights || act < 0 || act > 2)
+    return CUGO_B200_ERR_ARG;
+  if (m == 0) return CUGO_B200_OK;
+  if (m > INT32_MAX || !x || !out || ldx < k_in || ldo < n_out) return CUGO_B200_ERR_ARG;
+  const int layers = 2 + 2 * blocks;
+  for (int l = 0; l < layers; ++l)
+    if (!weights[l]) return CUGO_B200_ERR_ARG;
+  const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al(x) || ldx % 8 || !al(out) || ldo % 4 || k_in % 8) return CUGO_B200_ERR_ALIGN;
+  for (int l = 0; l < layers; ++l)
+    if (!al(weights[l])) return CUGO_B200_ERR_ALIGN;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr_set[64] = {};
+  if (dev < 0 || dev >= 64) return CUGO_B200_ERR_LAUNCH;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(fused_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             F_SMEM_BYTES) != cudaSuccess)
+      return CUGO_B200_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  FusedMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (!make_map(&maps.x, x, m, k_in, ldx, BM)) return CUGO_B200_ERR_LAUNCH;
+  if (!make_map(&maps.w[0], weights[0], F_H, k_in, k_in, BN)) return CUGO_B200_ERR_LAUNCH;
+  for (int l = 1; l < layers - 1; ++l)
+    if (!make_map(&maps.w[l], weights[l], F_H, F_H, F_H, BN)) return CUGO_B200_ERR_LAUNCH;
+  if (!make_map(&maps.w[layers - 1], weights[layers - 1], n_out, F_H, F_H, BN))
+    return CUGO_B200_ERR_LAUNCH;
+  if (!make_out_map(&maps.out, out, m, n_out, ldo, true)) return CUGO_B200_ERR_LAUNCH;
+  FusedArgs args{};
+  for (int l = 0; l < layers; ++l) args.bias[l] = biases ? biases[l] : nullptr;
+  args.blocks = blocks;
+  args.m = static_cast<int>(m);
+  args.k_in = static_cast<int>(k_in);
+  args.n_out = static_cast<int>(n_out);
+  args.n_mma = static_cast<int>((n_out + 15) / 16 * 16);
+  args.act = act;
+  args.error = error;
+  const int64_t tiles = (m + BM - 1) / BM;
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  fused_mlp_kernel<<<grid, THREADS, F_SMEM_BYTES, stream>>>(maps, args);
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }
 
 }  // extern "C"

@@ -53,6 +53,8 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_encode_events": [_VP, _I64, _VP, _VP, _I64, _I32, _VP, _I32, _VP, _VP],
     "cugo_b200_games_attention": [_VP, _I64, _I64, _I32, _I32, _VP, ctypes.c_float, _VP, _I64,
                                   _VP],
+    "cugo_b200_mlp_fused": [_VP, _I64, _I64, _I64, _I32, _VP, _VP, _I64, _I32, _VP, _I64, _VP,
+                            _VP],
     "cugo_b200_rowdot_bf16": [_VP, _I64, _VP, _VP, _I64, _I64, _VP, _I64, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
@@ -517,6 +519,33 @@ class CugoB200Extension:
             _check(self._lib.cugo_b200_games_attention(
                 _ptr(qkv), qkv.stride(0), n_seq, length, queries, _ptr(seen), 32 ** -0.5, _ptr(out),
                 out.stride(0), self._stream(qkv.device)), "games_attention")
+        return out
+
+    def mlp_fused(self, x: torch.Tensor, weights: list[torch.Tensor],
+                  biases: list[torch.Tensor | None], act: int, out: torch.Tensor | None = None,
+                  error: torch.Tensor | None = None) -> torch.Tensor:
+        """The whole hidden-512 residual MLP in one kernel: fp32 [m, n_out] outputs.
+        weights bf16 contiguous [out, in] (input layer, fc1/fc2 per block, head),
+        biases fp32 (or None)."""
+        m, k_in = x.shape
+        if x.dtype != torch.bfloat16 or x.stride(1) != 1:
+            raise RuntimeError("mlp_fused expects row-major bf16 x")
+        if any(w.dtype != torch.bfloat16 or not w.is_contiguous() for w in weights):
+            raise RuntimeError("mlp_fused expects contiguous bf16 weights")
+        if weights[0].shape[0] != 512 or weights[0].shape[1] != k_in:
+            raise RuntimeError("mlp_fused expects hidden 512 and an input weight [512, k_in]")
+        if any(b is not None and (b.dtype != torch.float32 or not b.is_contiguous()) for b in biases):
+            raise RuntimeError("mlp_fused expects contiguous fp32 biases")
+        n_out = weights[-1].shape[0]
+        if out is None:
+            out = torch.empty((m, (n_out + 3) // 4 * 4), dtype=torch.float32,
+                              device=x.device)[:, :n_out]
+        wp = (ctypes.c_void_p * len(weights))(*[w.data_ptr() for w in weights])
+        bp = (ctypes.c_void_p * len(biases))(*[b.data_ptr() if b is not None else None for b in biases])
+        with torch.cuda.device(x.device):
+            _check(self._lib.cugo_b200_mlp_fused(
+                _ptr(x), x.stride(0), m, k_in, (len(weights) - 2) // 2, wp, bp, n_out, act,
+                _ptr(out), out.stride(0), _ptr(error), self._stream(x.device)), "mlp_fused")
         return out
 
     def rowdot(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,

@@ -5,17 +5,37 @@ norm="none"):  h = W_in x + b;  h = h + W2 act(W1 h + b1) + b2  (per block);
 out = W_out act(h) + b_out.  The reference uses SiLU; the benchmark configuration
 (config 3) uses ReLU and appends a scalar value output to the 179 policy logits.
 Weights are bf16 with fp32 accumulation, as under the reference's bf16 autocast
-(python/cugo_ppo50.py:366).  Every layer is one launch of the fused tcgen05 GEMM
-(libcugo_b200.so, cugo_b200_gemm_bf16): bias, activation and the residual add run
-in its epilogue, and the last block writes act(h) so the head reads it directly.
+(python/cugo_ppo50.py:366).  Every layer is one launch of the tcgen05 GEMM
+(cugo_b200_gemm_bf16) with bias, activation and the residual add in its epilogue,
+the last block writing act(h) for the head; at hidden 512 the whole network can
+instead run as one launch of the fused MLP kernel (cugo_b200_mlp_fused: a 128-row
+tile's activations stay in shared and tensor memory from the input layer to the
+head), selected by fused_mlp_supported.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
 FEATURES = 720
 ACTIONS = 179
 _ACT = {"none": 0, "relu": 1, "silu": 2}
+
+
+# Whether hidden-512 networks run on the whole-network kernel when the environment
+# does not say (CUGO_B200_MLP_FUSED=1 selects it, =0 the layer-per-launch path).
+FUSED_MLP_DEFAULT = False
+
+
+def fused_mlp_supported(hidden: int, blocks: int, inputs: int, outputs: int) -> bool:
+    """Whether the whole-network kernel (cugo_b200_mlp_fused) runs this shape: hidden
+    512, at most 4 blocks, inputs a multiple of 8 up to 1,024, at most 256 outputs,
+    and it is selected (CUGO_B200_MLP_FUSED, else FUSED_MLP_DEFAULT)."""
+    env = os.environ.get("CUGO_B200_MLP_FUSED")
+    wanted = FUSED_MLP_DEFAULT if env is None else env == "1"
+    return (wanted and hidden == 512 and blocks <= 4 and inputs % 8 == 0 and inputs <= 1024
+            and outputs <= 256)
 
 
 class ResidualMlpPolicy:
@@ -59,6 +79,8 @@ class ResidualMlpPolicy:
         return 2 * sum(w.shape[0] * w.shape[1] for w in self.weights)
 
     def launches_per_forward(self) -> int:
+        if fused_mlp_supported(self.hidden, self.blocks, self.inputs, self.outputs):
+            return 1
         return 2 + 2 * self.blocks
 
     def _extension(self):
@@ -66,6 +88,13 @@ class ResidualMlpPolicy:
             from .ext import load_extension
             self._ext = load_extension()
         return self._ext
+
+    def _fp32_biases(self) -> list[torch.Tensor]:
+        key = tuple((b.data_ptr(), b._version) for b in self.biases)
+        if getattr(self, "_bkey", None) != key:
+            self._b32 = [b.float().contiguous() for b in self.biases]
+            self._bkey = key
+        return self._b32
 
     @torch.no_grad()
     def forward(self, features: torch.Tensor) -> torch.Tensor:
@@ -77,6 +106,8 @@ class ResidualMlpPolicy:
         m = x.size(0)
         act = _ACT[self.activation]
         w, b = self.weights, self.biases
+        if fused_mlp_supported(self.hidden, self.blocks, self.inputs, self.outputs):
+            return ext.mlp_fused(x, w, self._fp32_biases(), act, error=self.error)
         h = torch.empty((m, self.hidden), dtype=torch.bfloat16, device=x.device)
         ext.linear(x, w[0], b[0], out=h, act_after=act if self.blocks == 0 else 0, error=self.error)
         if self.blocks:

@@ -193,38 +193,45 @@ class FusedResidualMlp(nn.Module):
         return out.squeeze(-1) if self.squeeze and out.shape[-1] == 1 else out
 
     def _weights(self, params: list[torch.Tensor]):
-        """bf16 weights (the input layer's padded to 16-byte rows) and fp32 biases,
-        converted once per parameter update (tracked by the tensors' versions)."""
+        """bf16 weights (the input layer's zero-padded to 16-byte rows, contiguous)
+        and fp32 biases, converted once per parameter update (tracked by the tensors'
+        versions)."""
         key = tuple((p.data_ptr(), p._version) for p in params)
         if getattr(self, "_wkey", None) != key:
-            ws = [p.detach().to(torch.bfloat16) for p in params[0::2]]
+            ws = [p.detach().to(torch.bfloat16).contiguous() for p in params[0::2]]
             k_in = ws[0].shape[1]
             w_in = torch.zeros((ws[0].shape[0], _pad8(k_in)), dtype=torch.bfloat16, device=ws[0].device)
             w_in[:, :k_in] = ws[0]
-            ws[0] = w_in[:, :k_in]
-            self._wcache = (ws, [p.detach() for p in params[1::2]])
+            ws[0] = w_in
+            self._wcache = (ws, [p.detach().contiguous() for p in params[1::2]])
             self._wkey = key
         return self._wcache
 
     def _infer(self, x: torch.Tensor, params: list[torch.Tensor]) -> torch.Tensor:
-        """Forward without autograd: the activation of every fc1 and the last
-        block's closing activation run in the GEMM epilogues (one launch per layer)."""
+        """Forward without autograd: one GEMM launch per layer with the activations in
+        the epilogues and a scalar head as a row reduction, or, where
+        fused_mlp_supported selects it, the whole network in one fused-MLP launch.  The input
+        is read in place when its rows are 16-byte multiples at least as wide as the
+        zero-padded input weight (e.g. the 776-column rows of observe_critic_bf16)."""
+        from .policy import fused_mlp_supported
         ext = self.ext
         act = _ACT[self.activation]
         ws, bs = self._weights(params)
-        m, k_in = x.shape[0], ws[0].shape[1]
-        if x.stride(1) == 1 and x.stride(0) % 8 == 0:
-            xb = x[:, :k_in]
+        m, k_pad = x.shape[0], ws[0].shape[1]
+        k_in = self.inp.in_features
+        if x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.shape[1] >= k_pad:
+            xb = x[:, :k_pad]
         else:
-            xp = torch.zeros((m, _pad8(k_in)), dtype=torch.bfloat16, device=x.device)
-            xp[:, :k_in] = x[:, :k_in]
-            xb = xp[:, :k_in]
+            xb = torch.zeros((m, k_pad), dtype=torch.bfloat16, device=x.device)
+            xb[:, :k_in] = x[:, :k_in]
+        n_out = ws[-1].shape[0]
+        if fused_mlp_supported(ws[0].shape[0], self.n_blocks, k_pad, n_out):
+            return ext.mlp_fused(xb, ws, bs, act)
         h = ext.linear(xb, ws[0], bs[0], act=act if self.n_blocks == 0 else 0)
         for i in range(self.n_blocks):
             u = ext.linear(h, ws[1 + 2 * i], bs[1 + 2 * i], act=act)
             h = ext.linear(u, ws[2 + 2 * i], bs[2 + 2 * i], residual=h,
                            act_after=act if i == self.n_blocks - 1 else 0)
-        n_out = ws[-1].shape[0]
         if n_out == 1 and ws[-1].shape[1] % 8 == 0 and ws[-1].shape[1] <= 2048:
             # Scalar value head: a row reduction instead of a 256-column GEMM tile.
             w_row = ws[-1].reshape(-1).float()  # the bf16-rounded weights, as the GEMM uses

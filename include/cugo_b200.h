@@ -227,6 +227,21 @@ CUGO_B200_API int cugo_b200_rowdot_bf16(const void* a, int64_t lda, const float*
                                         const float* bias, int64_t m, int64_t k, float* out,
                                         int64_t ldo, cudaStream_t stream);
 
+/* The whole residual MLP of hidden width 512 in one kernel (python/cugo_ppo_nets50.py:
+ * 26-64, norm "none"): h = W[0] x + b[0]; per block h = h + W[2i+2] act(W[2i+1] h +
+ * b[2i+1]) + b[2i+2]; out = W[last] act(h) + b[last].  The activations of each
+ * 128-row tile stay in shared and tensor memory across all layers.  x bf16 [m, k_in]
+ * (ldx; k_in a multiple of 8, at most 1,024); weights: HOST array of 2 + 2 * blocks
+ * DEVICE pointers to contiguous bf16 [out, in] weights (hidden 512, blocks <= 4,
+ * n_out <= 256); biases: HOST array of fp32 device pointers (or NULL / NULL
+ * entries); act 0 none, 1 ReLU, 2 SiLU; out fp32 [m, n_out] (ldo a multiple of 4);
+ * error as for cugo_b200_gemm_bf16.  All pointers 16-byte aligned. */
+CUGO_B200_API int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in,
+                                      int32_t blocks, const void* const* weights,
+                                      const float* const* biases, int64_t n_out, int32_t act,
+                                      float* out, int64_t ldo, int32_t* error,
+                                      cudaStream_t stream);
+
 /* Policy forward that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory — for example a Go/Java/Rust
  * serving process that passes only its own fixed input and output buffers and keeps

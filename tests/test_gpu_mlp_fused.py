@@ -1,0 +1,84 @@
+"""GPU: the whole-network MLP kernel (cugo_b200_mlp_fused) against the fp32 forward of
+the same bf16 weights (python/cugo_ppo_nets50.py:26-64, norm "none") and the
+layer-per-launch path.
+
+Tolerance: the error against the exact fp32 forward is no larger than 1.25x that of
+the reference's own bf16-autocast forward (+1e-3), at most 1e-2 of the output scale;
+the argmax agrees wherever the top-2 margin exceeds 4x the error.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from tests.torch_reference import mlp_forward_autocast, mlp_forward_fp32
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+ACT = {"relu": 1, "silu": 2}
+
+
+def _net(k_in, blocks, n_out, seed):
+    g = torch.Generator().manual_seed(seed)
+    shapes = [(512, k_in)] + [(512, 512)] * (2 * blocks) + [(n_out, 512)]
+    ws = [(torch.randn(s, generator=g) * (2.0 / s[1]) ** 0.5).to(DEV, torch.bfloat16) for s in shapes]
+    bs = [(torch.randn(s[0], generator=g) * 0.05).to(DEV) for s in shapes]
+    return ws, bs
+
+
+@pytest.mark.parametrize("m,k_in,blocks,n_out,act", [
+    (1000, 720, 3, 180, "relu"), (129, 720, 3, 179, "silu"), (70000, 720, 3, 180, "relu"),
+    (300, 512, 0, 64, "relu"), (1000, 1024, 4, 256, "silu"), (1, 720, 1, 1, "relu"),
+    (4099, 776, 3, 1, "silu"), (257, 8, 2, 16, "relu")])
+def test_fused_mlp_matches_fp32(ext, m, k_in, blocks, n_out, act):
+    ws, bs = _net(k_in, blocks, n_out, seed=m + k_in)
+    g = torch.Generator().manual_seed(1)
+    x = torch.rand((m, k_in), generator=g).to(DEV, torch.bfloat16)
+    err_flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ext.mlp_fused(x, ws, bs, ACT[act], error=err_flag)
+    torch.cuda.synchronize()
+    assert int(err_flag) == 0
+    assert out.shape == (m, n_out)
+    exact = mlp_forward_fp32(ws, bs, x, blocks, act)
+    auto = mlp_forward_autocast(ws, bs, x, blocks, act)
+    scale = max(1.0, float(exact.abs().max()))
+    err = float((out - exact).abs().max())
+    err_ref = float((auto - exact).abs().max())
+    assert err <= 1.25 * err_ref + 1e-3, (err, err_ref)
+    assert err <= 1e-2 * scale, (err, scale)
+    if n_out > 1:
+        top2 = exact.topk(2, dim=1).values
+        clear = (top2[:, 0] - top2[:, 1]) > 4 * err
+        assert torch.equal(out.argmax(1)[clear], exact.argmax(1)[clear])
+
+
+def test_fused_mlp_is_deterministic_and_respects_strides(ext):
+    ws, bs = _net(720, 3, 180, seed=3)
+    g = torch.Generator().manual_seed(2)
+    big = torch.rand((3000, 728), generator=g).to(DEV, torch.bfloat16)
+    x = big[:, :720]  # row stride 728
+    out = torch.full((3000, 184), 7.0, device=DEV)
+    ext.mlp_fused(x, ws, bs, 1, out=out[:, :180])
+    again = ext.mlp_fused(x.contiguous(), ws, bs, 1)
+    assert torch.equal(out[:, :180], again)
+    assert bool((out[:, 180:] == 7.0).all())
+    nob = ext.mlp_fused(x, ws, [None] * len(ws), 1)
+    exact = mlp_forward_fp32(ws, [torch.zeros_like(b) for b in bs], x, 3, "relu")
+    assert float((nob - exact).abs().max()) <= 1e-2 * max(1.0, float(exact.abs().max()))
+
+
+def test_policy_routes_through_the_fused_kernel(ext, monkeypatch):
+    from cugo_b200.policy import ResidualMlpPolicy
+    pol = ResidualMlpPolicy(512, 3, "relu", device=DEV, seed=0)
+    monkeypatch.setenv("CUGO_B200_MLP_FUSED", "1")
+    assert pol.launches_per_forward() == 1
+    g = torch.Generator().manual_seed(4)
+    x = torch.rand((5000, 720), generator=g).to(DEV)
+    fused = pol(x)
+    monkeypatch.setenv("CUGO_B200_MLP_FUSED", "0")
+    assert pol.launches_per_forward() == 8
+    layers = pol(x)
+    exact = mlp_forward_fp32(pol.weights, pol.biases, x, 3, "relu")
+    scale = max(1.0, float(exact.abs().max()))
+    assert float((fused - layers).abs().max()) <= 1e-2 * scale
+    assert float((fused - exact).abs().max()) <= 1e-2 * scale

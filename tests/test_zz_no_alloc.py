@@ -8,7 +8,8 @@ into the library.  This test calls it directly with ctypes and checks its logits
 against the regular policy forward (ResidualMlpPolicy, which allocates its
 activations with torch) on two calls in a row with different batches, so stale
 contents of the shared buffer would show, and checks that an oversized batch is
-refused.  The regular forward runs the same kernels in the same order, so the
+refused.  The regular forward is taken on its layer-per-launch path
+(CUGO_B200_MLP_FUSED=0), which runs the same GEMM kernels in the same order, so the
 tolerance is the GEMM tests' single-layer bound, 1% relative + 1e-2 absolute.
 
 Collected last (file name) so a first-failure stop has already run the rest.
@@ -61,7 +62,8 @@ def _noalloc(fn, pol, x):
     return rc, out, int(error.item())
 
 
-def test_noalloc_forward_matches_policy_on_consecutive_calls():
+def test_noalloc_forward_matches_policy_on_consecutive_calls(monkeypatch):
+    monkeypatch.setenv("CUGO_B200_MLP_FUSED", "0")
     fn = _entry()
     pol = _policy()
     g = torch.Generator().manual_seed(5)
