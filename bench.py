@@ -149,6 +149,22 @@ def measured_peaks() -> dict:
             "source": "fallback"}
 
 
+def mlp_traffic(arch: str, policy) -> float | None:
+    """DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+    dominant policy kernel on a 262,144-row forward: the fused kernel's, scaled from a
+    65,536-row capture by the rows (traffic is the input and output rows); the
+    layer-per-launch path's, 4,784 MB over its 8 launches."""
+    if arch != "512x3":
+        return None
+    if policy.launches_per_forward() == 1:
+        return None if FUSED_TRAFFIC_65536 is None else FUSED_TRAFFIC_65536 * 4
+    return 598e6
+
+
+# ncu DRAM bytes of one fused_mlp_kernel launch on 65,536 rows of the 3x512 policy.
+FUSED_TRAFFIC_65536 = 116.3e6
+
+
 # ---- config 3: policy self-play --------------------------------------------------------
 
 def selfplay_bench(args, world, rank, ext, policy):
@@ -454,13 +470,13 @@ def main():
         "bad_status": sp["bad"],
         "e2e": {"value": sp["e2e_games"] / sp["e2e_elapsed"], "unit": "games/s",
                 "h2d_bytes_per_step": sp["h2d"], "d2h_bytes_per_step": sp["d2h"]},
-        "roofline": {"kernel": "policy MLP forward: tcgen05 GEMM layers (gemm_kernel)",
+        "roofline": {"kernel": ("policy MLP forward: whole-network CTA-pair kernel (fused_mlp_kernel)"
+                                if policy.launches_per_forward() == 1 else
+                                "policy MLP forward: tcgen05 GEMM layers (gemm_kernel)"),
                      "bound": "tensor",
                      "achieved": mlp_tflops, "peak": peaks["bf16_tflops_sustained"],
                      "unit": "TFLOP/s", "frac": mlp_tflops / peaks["bf16_tflops_sustained"],
-                     # ncu dram__bytes_read + write per gemm_kernel launch, averaged over
-                     # the 8 layers of a 262,144-row 3x512 forward (4,784 MB / 8).
-                     "traffic": 598e6 if args.arch == "512x3" else None,
+                     "traffic": mlp_traffic(args.arch, policy),
                      "traffic_unit": "bytes per launch",
                      "peak_source": peaks["source"] + " (sustained)"},
         "clocks": sp["clocks"],

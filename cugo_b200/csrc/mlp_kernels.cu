@@ -1127,28 +1127,36 @@ namespace {
 //
 // (python/cugo_ppo_nets50.py:26-64, norm "none").  At hidden 512 every layer of the
 // layer-per-launch path is bound by moving activations through HBM (a 512-wide bf16
-// row is 1 KB in and 1 KB out per layer for 0.5 MFLOP); here a CTA keeps its 128-row
-// tile's activations on chip for the whole network:
-//   shared memory  ACT: the tile's 128 x 512 bf16 activations (128 KB) in the
+// row is 1 KB in and 1 KB out per layer for 0.5 MFLOP); here the activations stay on
+// chip for the whole network.  A CTA pair (cluster of 2, tcgen05 cta_group::2) owns a
+// 256-row tile, 128 rows per CTA:
+//   shared memory  ACT: the CTA's 128 x 512 bf16 activations (128 KB) in the
 //                  128-byte-swizzled K-major layout the MMA reads (8 chunks of 64
 //                  columns), rewritten in place layer after layer; during the input
 //                  layer its chunks hold the x tiles streamed in by TMA, after the
 //                  head it stages the fp32 output for TMA stores;
-//                  a 3-stage ring of 256 x 64 weight tiles (32 KB each) fed by TMA;
+//                  a 6-stage ring of weight tiles: each stage is this CTA's half
+//                  (128 rows x 64) of a 256-row tile (16 KB), so each SM streams
+//                  half of every weight tile and the bytes in flight cover twice the
+//                  MMA work a single CTA's would;
 //   tensor memory  the fp32 accumulator of a whole layer, 128 lanes x 512 columns.
 // A block's residual never leaves the chip: the fc1 epilogue reads h from ACT, writes
 // h + b2 into the accumulator columns it has just drained (tcgen05.st) and u = act(z)
 // over h in ACT, so the fc2 MMAs accumulate u W2^T on top of h + b2.
-// Warp roles as in gemm_kernel: warp 0 the TMA producer (weights run ahead of the
-// MMAs; x tiles wait for the previous tile's output stores to leave ACT), warp 1 the
-// MMA issuer and TMEM owner, warps 2..9 the epilogue (two per TMEM lane quadrant,
-// 256 columns each).  Every wait is bounded as in gemm_kernel.
+// Warp roles: warp 0 of each CTA the TMA producer of its half (weights run ahead of
+// the MMAs; x tiles wait for the previous tile's output stores to leave ACT), warp 1
+// of CTA 0 the MMA issuer (M = 256 MMAs reading both CTAs' shared memory), warps 2..9
+// of each CTA the epilogue of its 128 rows (two warps per TMEM lane quadrant, 256
+// columns each).  Copies count on CTA 0's "full" barriers; MMA completions arrive on
+// both CTAs' barriers; both CTAs' epilogue warps signal CTA 0's "ready" barrier.
+// Every wait is bounded as in gemm_kernel.
 constexpr int F_H = 512;
 constexpr int F_CHUNKS = F_H / BK;            // 8
 constexpr int F_CHUNK_BYTES = BM * BK * 2;    // 16 KB
 constexpr int F_ACT_BYTES = F_CHUNKS * F_CHUNK_BYTES;
-constexpr int F_WSTAGES = 3;
-constexpr int F_W_BYTES = BN * BK * 2;        // 32 KB
+constexpr int F_WSTAGES = 6;
+constexpr int F_W_ROWS = BN / 2;              // weight rows per CTA per stage
+constexpr int F_W_BYTES = F_W_ROWS * BK * 2;  // 16 KB
 constexpr int F_MAX_BLOCKS = 4;
 constexpr int F_MAX_LAYERS = 2 + 2 * F_MAX_BLOCKS;
 constexpr int F_MAX_KIN = 1024;
@@ -1157,7 +1165,7 @@ static_assert(F_SMEM_BYTES <= 232448, "fits the opt-in shared memory of one CTA"
 
 struct FusedMaps {
   CUtensorMap x;                    // bf16 [m, k_in], box 64 x 128
-  CUtensorMap w[F_MAX_LAYERS];      // bf16 [n, k] per layer, box 64 x 256
+  CUtensorMap w[F_MAX_LAYERS];      // bf16 [n, k] per layer, box 64 x 128 (head: n_mma / 2)
   CUtensorMap out;                  // fp32 [m, n_out], box 16 x 32, 64-byte swizzle
 };
 
@@ -1212,21 +1220,26 @@ __device__ __forceinline__ void act_load32(uint8_t* act, int r, int col0, float*
       "r"(r[29]), "r"(r[30]), "r"(r[31])                                                        \
       : "memory")
 
-__device__ __forceinline__ float fused_bias(const float* b, int col) {
-  return b ? __ldg(b + col) : 0.0f;
+// The 32 biases col0 .. col0 + 31 of a layer: lane j loads column col0 + j once and the
+// values reach every lane by shuffles (no per-element loads in the epilogue).
+__device__ __forceinline__ void fused_bias32(const float* b, int col0, float* out) {
+  const int lane = threadIdx.x & 31;
+  const float mine = b ? __ldg(b + col0 + lane) : 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) out[j] = __shfl_sync(0xffffffffu, mine, j);
 }
 
 // An epilogue phase is done: its TMEM reads/writes and ACT writes are visible to the
-// MMAs that follow (one arrive per epilogue warp).
-__device__ __forceinline__ void fused_phase_done(uint64_t* act_ready) {
+// pair's MMAs that follow (one arrive per epilogue warp on CTA 0's barrier).
+__device__ __forceinline__ void fused_phase_done(uint32_t ready0) {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   fence_before();
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(act_ready);
+  if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(ready0);
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     fused_mlp_kernel(const __grid_constant__ FusedMaps maps, const __grid_constant__ FusedArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1238,16 +1251,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* xfull = wempty + F_WSTAGES;  // [8]
   uint64_t* xempty = xfull + F_CHUNKS;   // [8]
   uint64_t* acc_full = xempty + F_CHUNKS;
-  uint64_t* act_ready = acc_full + 1;
-  uint64_t* act_free = act_ready + 1;
+  uint64_t* act_ready = acc_full + 1;    // CTA 0's counts both CTAs' epilogue warps
+  uint64_t* act_free = act_ready + 1;    // this CTA's ACT is free for the next x tiles
   uint64_t* drained = act_free + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles = (args.m + BM - 1) / BM;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1), pairs = static_cast<int>(gridDim.x >> 1);
+  const int tiles = (args.m + 2 * BM - 1) / (2 * BM);
   const int kc0 = (args.k_in + BK - 1) / BK;
   const int hidden_layers = 2 * args.blocks;
+  const int head_rows = args.n_mma / 2;  // head weight rows per CTA
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < F_WSTAGES; ++s) {
@@ -1259,49 +1276,56 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&xempty[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(act_ready, EPI_WARPS);
+    mbar_init(act_ready, 2 * EPI_WARPS);
     mbar_init(act_free, EPI_WARPS);
     mbar_init(drained, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+  if (warp == 1) {  // both CTAs allocate together, same warp, same holder offset
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_holder)),
                  "r"(512));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
   }
   fence_before();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA signal
   fence_after();
   const uint32_t tmem_base = *tmem_holder;
   bool failed = false;
+  __shared__ int any_failed;
+  if (threadIdx.x == 0) any_failed = 0;
+  __syncthreads();
 
   if (warp == 0) {
-    // ---- TMA producer: per tile the layers' weight tiles in MMA order, the x tiles
-    // into the ACT chunks ----
+    // ---- TMA producer (both CTAs): this CTA's halves of the weight tiles in MMA
+    // order, its 128 rows of the x tiles into its ACT chunks ----
     if (lane == 0) {
+      const uint32_t wfull0 = peer_addr(wfull, 0), xfull0 = peer_addr(xfull, 0);
       int ws = 0;
       uint32_t wph = 0, xuse = 0;
-      auto load_w = [&](int layer, int kc, int nh) -> bool {
+      auto load_w = [&](int layer, int kc, int row0, int tx_bytes) -> bool {
         if (!mbar_wait(&wempty[ws], wph ^ 1u)) return false;
-        mbar_expect_tx(&wfull[ws], F_W_BYTES);
-        tma_load_2d(&maps.w[layer], &wfull[ws], wring + ws * F_W_BYTES, kc * BK, nh * BN);
+        if (leader) mbar_expect_tx(&wfull[ws], static_cast<uint32_t>(tx_bytes));
+        tma_load_2d_pair(&maps.w[layer], wfull0 + static_cast<uint32_t>(ws * 8),
+                         wring + ws * F_W_BYTES, kc * BK, row0);
         if (++ws == F_WSTAGES) {
           ws = 0;
           wph ^= 1u;
         }
         return true;
       };
+      const int rh = static_cast<int>(rank) * F_W_ROWS;  // this CTA's rows of a 256-row tile
       int iter = 0;
-      for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++iter) {
-        const int row0 = t * BM;
+      for (int t = pair; t < tiles && !failed; t += pairs, ++iter) {
+        const int row0 = t * 2 * BM + static_cast<int>(rank) * BM;
         for (int kc = 0; kc < kc0 && !failed; ++kc) {
-          if (!load_w(0, kc, 0) || !load_w(0, kc, 1)) {
+          if (!load_w(0, kc, rh, 2 * F_W_BYTES) || !load_w(0, kc, BN + rh, 2 * F_W_BYTES)) {
             failed = true;
             break;
           }
           const int slot = kc & (F_CHUNKS - 1);
-          // ACT is free once the previous tile's output stores have read it; a slot's
+          // ACT is free once this CTA's previous output stores have read it; a slot's
           // second x tile of this tile waits for the MMAs of its first.
           if (kc == 0 && iter > 0 && !mbar_wait(act_free, (iter - 1) & 1)) {
             failed = true;
@@ -1311,25 +1335,26 @@ __global__ void __launch_bounds__(THREADS, 1)
             failed = true;
             break;
           }
-          mbar_expect_tx(&xfull[slot], F_CHUNK_BYTES);
-          tma_load_2d(&maps.x, &xfull[slot], act + slot * F_CHUNK_BYTES, kc * BK, row0);
+          if (leader) mbar_expect_tx(&xfull[slot], 2 * F_CHUNK_BYTES);
+          tma_load_2d_pair(&maps.x, xfull0 + static_cast<uint32_t>(slot * 8),
+                           act + slot * F_CHUNK_BYTES, kc * BK, row0);
           xuse ^= 1u << slot;
         }
         for (int l = 1; l <= hidden_layers && !failed; ++l)
           for (int kc = 0; kc < F_CHUNKS && !failed; ++kc)
-            if (!load_w(l, kc, 0) || !load_w(l, kc, 1)) failed = true;
+            if (!load_w(l, kc, rh, 2 * F_W_BYTES) || !load_w(l, kc, BN + rh, 2 * F_W_BYTES))
+              failed = true;
         for (int kc = 0; kc < F_CHUNKS && !failed; ++kc)
-          if (!load_w(hidden_layers + 1, kc, 0)) failed = true;
-      }
-      if (failed) {
-        for (int s = 0; s < F_WSTAGES; ++s) mbar_wait(&wfull[s], 0);
+          if (!load_w(hidden_layers + 1, kc, static_cast<int>(rank) * head_rows,
+                      args.n_mma * BK * 2))
+            failed = true;
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer ----
-    if (lane == 0) {
-      constexpr uint32_t idesc_h = instr_desc(BM, BN);
-      const uint32_t idesc_o = instr_desc(BM, args.n_mma);
+    // ---- MMA issuer (CTA 0 only) ----
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc_h = instr_desc(2 * BM, BN);
+      const uint32_t idesc_o = instr_desc(2 * BM, args.n_mma);
       int ws = 0;
       uint32_t wph = 0, xuse = 0, ready = 0;
       auto wait_ready = [&]() -> bool {
@@ -1345,9 +1370,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t b_addr = smem_addr(wring + ws * F_W_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          mma_bf16(tmem_base + static_cast<uint32_t>(nh * BN), sw128_desc(a_addr + kk * 32),
-                   sw128_desc(b_addr + kk * 32), idesc, (first && kk == 0) ? 0u : 1u);
-        mma_commit(&wempty[ws]);
+          mma_bf16_pair(tmem_base + static_cast<uint32_t>(nh * BN), sw128_desc(a_addr + kk * 32),
+                        sw128_desc(b_addr + kk * 32), idesc, (first && kk == 0) ? 0u : 1u);
+        mma_commit_pair(&wempty[ws]);
         if (++ws == F_WSTAGES) {
           ws = 0;
           wph ^= 1u;
@@ -1355,8 +1380,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       int iter = 0;
-      for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++iter) {
-        // The previous tile's head epilogue has drained the accumulator.
+      for (int t = pair; t < tiles && !failed; t += pairs, ++iter) {
+        // Both CTAs' head epilogues of the previous tile have drained the accumulators.
         if (iter > 0 && !wait_ready()) {
           failed = true;
           break;
@@ -1374,10 +1399,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             failed = true;
             break;
           }
-          mma_commit(&xempty[slot]);
+          mma_commit_pair(&xempty[slot]);
         }
         if (failed) break;
-        mma_commit(acc_full);
+        mma_commit_pair(acc_full);
         for (int l = 1; l <= hidden_layers && !failed; ++l) {
           if (!wait_ready()) {
             failed = true;
@@ -1391,7 +1416,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 !k_step(a_addr, 1, idesc_h, fresh && kc == 0))
               failed = true;
           }
-          if (!failed) mma_commit(acc_full);
+          if (!failed) mma_commit_pair(acc_full);
         }
         if (failed || !wait_ready()) {
           failed = true;
@@ -1399,17 +1424,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int kc = 0; kc < F_CHUNKS && !failed; ++kc)
           if (!k_step(smem_addr(act + kc * F_CHUNK_BYTES), 0, idesc_o, kc == 0)) failed = true;
-        if (!failed) mma_commit(acc_full);
+        if (!failed) mma_commit_pair(acc_full);
       }
-      mma_commit(drained);
+      // All issued MMAs complete before the accumulators are released.
+      mma_commit_pair_local(drained);
       mbar_wait(drained, 0);
     }
   } else {
-    // ---- epilogue: warps 2..9 ----
+    // ---- epilogue (both CTAs): warps 2..9 ----
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int r = quad * 32 + lane;  // this thread's row of the tile
+    const int r = quad * 32 + lane;  // this thread's row of the CTA's 128 rows
     const uint32_t tq = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t ready0 = peer_addr(act_ready, 0);
     uint8_t* stage = act + (warp - 2) * 2 * EPI_BUF;  // output staging, after the head MMAs
     uint32_t full_ph = 0;
     auto wait_full = [&]() -> bool {
@@ -1420,8 +1447,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     const int act_code = args.act;
     int iter = 0;
-    for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++iter) {
-      const int row0 = t * BM;
+    for (int t = pair; t < tiles && !failed; t += pairs, ++iter) {
+      const int row0 = t * 2 * BM + static_cast<int>(rank) * BM;
       // Input layer: h = x W0^T + b0 (+ act when there are no blocks).
       if (!wait_full()) {
         failed = true;
@@ -1430,15 +1457,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = 0; c < 8; ++c) {
         const int col0 = half * 256 + c * 32;
         uint32_t raw[32];
-        CB_TMEM_LD32(tq + static_cast<uint32_t>(col0), raw);
-        tmem_wait_ld();
         float v[32];
+        CB_TMEM_LD32(tq + static_cast<uint32_t>(col0), raw);
+        fused_bias32(args.bias[0], col0, v);
+        tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + fused_bias(args.bias[0], col0 + j);
+        for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(raw[j]);
         if (args.blocks == 0) activate_chunk<32>(v, act_code);
         act_store32(act, r, col0, v);
       }
-      fused_phase_done(act_ready);
+      fused_phase_done(ready0);
       for (int l = 1; l <= hidden_layers && !failed; ++l) {
         if (!wait_full()) {
           failed = true;
@@ -1449,28 +1477,31 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 0; c < 8; ++c) {
           const int col0 = half * 256 + c * 32;
           uint32_t raw[32];
-          CB_TMEM_LD32(tq + static_cast<uint32_t>(col0), raw);
-          tmem_wait_ld();
           float v[32];
+          CB_TMEM_LD32(tq + static_cast<uint32_t>(col0), raw);
           if (fc1) {
             // u = act(h W1^T + b1) over h in ACT; h + b2 into the accumulator for fc2.
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + fused_bias(args.bias[l], col0 + j);
-            activate_chunk<32>(v, act_code);
             float h[32];
-            act_load32(act, r, col0, h);
+            fused_bias32(args.bias[l + 1], col0, h);
+            float hb[32];
+            act_load32(act, r, col0, hb);
+            fused_bias32(args.bias[l], col0, v);
+            tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              raw[j] = __float_as_uint(h[j] + fused_bias(args.bias[l + 1], col0 + j));
+            for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(raw[j]);
+            activate_chunk<32>(v, act_code);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) raw[j] = __float_as_uint(hb[j] + h[j]);
             CB_TMEM_ST32(tq + static_cast<uint32_t>(col0), raw);
           } else {
+            tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
             if (last) activate_chunk<32>(v, act_code);
           }
           act_store32(act, r, col0, v);
         }
-        fused_phase_done(act_ready);
+        fused_phase_done(ready0);
       }
       if (failed) break;
       // Head: out = act(h) Wo^T + bo, fp32, through the ACT staging and TMA stores.
@@ -1479,17 +1510,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       const int chunks = args.n_mma / 16;
+      const float* bo = args.bias[hidden_layers + 1];
       int used = 0;
       for (int c = half; c < chunks; c += 2, ++used) {
         const int col0 = c * 16;
         uint32_t raw[16];
         CB_TMEM_LD16(tq + static_cast<uint32_t>(col0), raw);
+        const float bl = (bo && lane < 16 && col0 + lane < args.n_out) ? __ldg(bo + col0 + lane) : 0.0f;
         tmem_wait_ld();
         float v[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          v[j] = __uint_as_float(raw[j]) +
-                 (col0 + j < args.n_out ? fused_bias(args.bias[hidden_layers + 1], col0 + j) : 0.0f);
+        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(raw[j]) + __shfl_sync(0xffffffffu, bl, j);
         uint8_t* buf = stage + (used & 1) * EPI_BUF;
         // The store that last read this buffer (two chunks back) is done with it.
         if (lane == 0) tma_store_wait_read<1>();
@@ -1500,25 +1531,48 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       fence_before();
       if (lane == 0) {
-        mbar_arrive(act_ready);
+        mbar_arrive_cluster(ready0);
         mbar_arrive(act_free);
       }
     }
     if (lane == 0) tma_store_wait_all();
   }
   if (failed) {
+    any_failed = 1;
     if (args.error) atomicExch(args.error, 1);
+  }
+  fence_before();
+  __syncthreads();
+  if (any_failed) {
+    // Let copies and MMAs still in flight land before the pair leaves (bounded).
     const uint64_t t0 = now_ns();
     while (now_ns() - t0 < 100'000ull) {
     }
   }
-  fence_before();
-  __syncthreads();
+  cluster_sync_all();  // no cross-CTA signal is outstanding past this point
   fence_after();
   if (warp == 1) {
     __syncwarp();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512));
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512));
   }
+}
+
+// CTA pairs of fused_mlp_kernel that fit on the device at once.
+int fused_max_pairs(int dev) {
+  static int cache[64] = {};
+  if (!cache[dev]) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sm_count() & ~1), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = F_SMEM_BYTES;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fused_mlp_kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
 }
 
 }  // namespace
@@ -1550,13 +1604,17 @@ int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int
       return CUGO_B200_ERR_LAUNCH;
     attr_set[dev] = true;
   }
+  // The head's MMA width: n_out rounded up to 16, at least 32 (a multiple of 16 per
+  // CTA of the pair, in whole 8-row swizzle atoms).
+  const int n_mma = n_out <= 32 ? 32 : static_cast<int>((n_out + 15) / 16 * 16);
   FusedMaps maps;
   memset(&maps, 0, sizeof(maps));
   if (!make_map(&maps.x, x, m, k_in, ldx, BM)) return CUGO_B200_ERR_LAUNCH;
-  if (!make_map(&maps.w[0], weights[0], F_H, k_in, k_in, BN)) return CUGO_B200_ERR_LAUNCH;
+  if (!make_map(&maps.w[0], weights[0], F_H, k_in, k_in, F_W_ROWS)) return CUGO_B200_ERR_LAUNCH;
   for (int l = 1; l < layers - 1; ++l)
-    if (!make_map(&maps.w[l], weights[l], F_H, F_H, F_H, BN)) return CUGO_B200_ERR_LAUNCH;
-  if (!make_map(&maps.w[layers - 1], weights[layers - 1], n_out, F_H, F_H, BN))
+    if (!make_map(&maps.w[l], weights[l], F_H, F_H, F_H, F_W_ROWS)) return CUGO_B200_ERR_LAUNCH;
+  if (!make_map(&maps.w[layers - 1], weights[layers - 1], n_out, F_H, F_H,
+                static_cast<uint32_t>(n_mma / 2)))
     return CUGO_B200_ERR_LAUNCH;
   if (!make_out_map(&maps.out, out, m, n_out, ldo, true)) return CUGO_B200_ERR_LAUNCH;
   FusedArgs args{};
@@ -1565,12 +1623,13 @@ int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int
   args.m = static_cast<int>(m);
   args.k_in = static_cast<int>(k_in);
   args.n_out = static_cast<int>(n_out);
-  args.n_mma = static_cast<int>((n_out + 15) / 16 * 16);
+  args.n_mma = n_mma;
   args.act = act;
   args.error = error;
-  const int64_t tiles = (m + BM - 1) / BM;
-  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  fused_mlp_kernel<<<grid, THREADS, F_SMEM_BYTES, stream>>>(maps, args);
+  const int64_t tiles = (m + 2 * BM - 1) / (2 * BM);
+  const int64_t cap = fused_max_pairs(dev);
+  const int64_t pairs = tiles < cap ? tiles : cap;
+  fused_mlp_kernel<<<static_cast<unsigned>(2 * pairs), THREADS, F_SMEM_BYTES, stream>>>(maps, args);
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }
 

@@ -25,7 +25,7 @@ _ACT = {"none": 0, "relu": 1, "silu": 2}
 
 # Whether hidden-512 networks run on the whole-network kernel when the environment
 # does not say (CUGO_B200_MLP_FUSED=1 selects it, =0 the layer-per-launch path).
-FUSED_MLP_DEFAULT = False
+FUSED_MLP_DEFAULT = True
 
 
 def fused_mlp_supported(hidden: int, blocks: int, inputs: int, outputs: int) -> bool:
