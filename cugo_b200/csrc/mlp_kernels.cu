@@ -1145,9 +1145,9 @@ namespace {
 // over h in ACT, so the fc2 MMAs accumulate u W2^T on top of h + b2.
 // Warp roles: warp 0 of each CTA the TMA producer of its half (weights run ahead of
 // the MMAs; x tiles wait for the previous tile's output stores to leave ACT), warp 1
-// of CTA 0 the MMA issuer (M = 256 MMAs reading both CTAs' shared memory), warps 2..9
-// of each CTA the epilogue of its 128 rows (two warps per TMEM lane quadrant, 256
-// columns each).  Copies count on CTA 0's "full" barriers; MMA completions arrive on
+// of CTA 0 the MMA issuer (M = 256 MMAs reading both CTAs' shared memory), the other
+// F_EPI_WARPS warps of each CTA the epilogue of its 128 rows (F_EPI_WARPS / 4 per
+// TMEM lane quadrant, each a contiguous group of columns, 16 columns at a time).  Copies count on CTA 0's "full" barriers; MMA completions arrive on
 // both CTAs' barriers; both CTAs' epilogue warps signal CTA 0's "ready" barrier.
 // Every wait is bounded as in gemm_kernel.
 constexpr int F_H = 512;
@@ -1161,6 +1161,18 @@ constexpr int F_MAX_BLOCKS = 4;
 constexpr int F_MAX_LAYERS = 2 + 2 * F_MAX_BLOCKS;
 constexpr int F_MAX_KIN = 1024;
 constexpr int F_SMEM_BYTES = F_ACT_BYTES + F_WSTAGES * F_W_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+// Epilogue warps per CTA: F_EPI_WARPS / 4 per TMEM lane quadrant, each draining
+// 512 / (F_EPI_WARPS / 4) columns in 16-column chunks.
+#ifndef CB_FUSED_EPI_WARPS
+#define CB_FUSED_EPI_WARPS 16
+#endif
+constexpr int F_EPI_WARPS = CB_FUSED_EPI_WARPS;
+constexpr int F_THREADS = 64 + 32 * F_EPI_WARPS;
+constexpr int F_GROUPS = F_EPI_WARPS / 4;        // column groups per quadrant
+constexpr int F_GROUP_COLS = F_H / F_GROUPS;
+constexpr int F_CW = 16;                         // columns per epilogue chunk
+static_assert(F_EPI_WARPS % 4 == 0 && F_GROUP_COLS % F_CW == 0, "epilogue split");
+static_assert(F_EPI_WARPS * 2 * EPI_BUF <= F_ACT_BYTES, "output staging fits in ACT");
 static_assert(F_SMEM_BYTES <= 232448, "fits the opt-in shared memory of one CTA");
 
 struct FusedMaps {
@@ -1180,11 +1192,11 @@ __device__ __forceinline__ uint8_t* act_piece(uint8_t* act, int kc, int r, int p
   return act + kc * F_CHUNK_BYTES + r * 128 + ((p ^ (r & 7)) << 4);
 }
 
-// Row r's 32 columns col0 .. col0 + 31 (col0 a multiple of 32) as bf16 into ACT.
-__device__ __forceinline__ void act_store32(uint8_t* act, int r, int col0, const float* v) {
+// Row r's 16 columns col0 .. col0 + 15 (col0 a multiple of 16) as bf16 into ACT.
+__device__ __forceinline__ void act_store16(uint8_t* act, int r, int col0, const float* v) {
   const int kc = col0 >> 6, p0 = (col0 & 63) >> 3;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < 2; ++j) {
     uint4 raw;
     __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
@@ -1193,10 +1205,10 @@ __device__ __forceinline__ void act_store32(uint8_t* act, int r, int col0, const
   }
 }
 
-__device__ __forceinline__ void act_load32(uint8_t* act, int r, int col0, float* v) {
+__device__ __forceinline__ void act_load16(uint8_t* act, int r, int col0, float* v) {
   const int kc = col0 >> 6, p0 = (col0 & 63) >> 3;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < 2; ++j) {
     const uint4 raw = *reinterpret_cast<const uint4*>(act_piece(act, kc, r, p0 + j));
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
@@ -1208,26 +1220,23 @@ __device__ __forceinline__ void act_load32(uint8_t* act, int r, int col0, float*
   }
 }
 
-#define CB_TMEM_ST32(taddr, r)                                                                  \
+// The 16 biases col0 .. col0 + 15 (columns from `limit` on read 0): lanes 0..15 load
+// one each and shuffles hand them to every lane.
+__device__ __forceinline__ void fused_bias16(const float* b, int col0, int limit, float* out) {
+  const int lane = threadIdx.x & 31;
+  const float mine = (b && lane < 16 && col0 + lane < limit) ? __ldg(b + col0 + lane) : 0.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) out[j] = __shfl_sync(0xffffffffu, mine, j);
+}
+
+#define CB_TMEM_ST16(taddr, r)                                                                  \
   asm volatile(                                                                                 \
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"   \
-      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"( \
-          taddr),                                                                               \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"   \
+      "%13,%14,%15,%16};" ::"r"(taddr),                                                         \
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),   \
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),        \
-      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),      \
-      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),      \
-      "r"(r[29]), "r"(r[30]), "r"(r[31])                                                        \
+      "r"(r[15])                                                                                \
       : "memory")
-
-// The 32 biases col0 .. col0 + 31 of a layer: lane j loads column col0 + j once and the
-// values reach every lane by shuffles (no per-element loads in the epilogue).
-__device__ __forceinline__ void fused_bias32(const float* b, int col0, float* out) {
-  const int lane = threadIdx.x & 31;
-  const float mine = b ? __ldg(b + col0 + lane) : 0.0f;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) out[j] = __shfl_sync(0xffffffffu, mine, j);
-}
 
 // An epilogue phase is done: its TMEM reads/writes and ACT writes are visible to the
 // pair's MMAs that follow (one arrive per epilogue warp on CTA 0's barrier).
@@ -1239,7 +1248,7 @@ __device__ __forceinline__ void fused_phase_done(uint32_t ready0) {
   if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(ready0);
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
     fused_mlp_kernel(const __grid_constant__ FusedMaps maps, const __grid_constant__ FusedArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1276,8 +1285,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_init(&xempty[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(act_ready, 2 * EPI_WARPS);
-    mbar_init(act_free, EPI_WARPS);
+    mbar_init(act_ready, 2 * F_EPI_WARPS);
+    mbar_init(act_free, F_EPI_WARPS);
     mbar_init(drained, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1431,10 +1440,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_wait(drained, 0);
     }
   } else {
-    // ---- epilogue (both CTAs): warps 2..9 ----
+    // ---- epilogue (both CTAs): warps 2 .. 1 + F_EPI_WARPS ----
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int r = quad * 32 + lane;  // this thread's row of the CTA's 128 rows
+    const int group = (warp - 2) >> 2;  // this warp's columns: group * F_GROUP_COLS ..
+    const int r = quad * 32 + lane;     // this thread's row of the CTA's 128 rows
     const uint32_t tq = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t ready0 = peer_addr(act_ready, 0);
     uint8_t* stage = act + (warp - 2) * 2 * EPI_BUF;  // output staging, after the head MMAs
@@ -1454,17 +1463,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         failed = true;
         break;
       }
-      for (int c = 0; c < 8; ++c) {
-        const int col0 = half * 256 + c * 32;
-        uint32_t raw[32];
-        float v[32];
-        CB_TMEM_LD32(tq + static_cast<uint32_t>(col0), raw);
-        fused_bias32(args.bias[0], col0, v);
+      for (int c = 0; c < F_GROUP_COLS / F_CW; ++c) {
+        const int col0 = group * F_GROUP_COLS + c * F_CW;
+        uint32_t raw[F_CW];
+        float v[F_CW];
+        CB_TMEM_LD16(tq + static_cast<uint32_t>(col0), raw);
+        fused_bias16(args.bias[0], col0, F_H, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(raw[j]);
-        if (args.blocks == 0) activate_chunk<32>(v, act_code);
-        act_store32(act, r, col0, v);
+        for (int j = 0; j < F_CW; ++j) v[j] += __uint_as_float(raw[j]);
+        if (args.blocks == 0) activate_chunk<F_CW>(v, act_code);
+        act_store16(act, r, col0, v);
       }
       fused_phase_done(ready0);
       for (int l = 1; l <= hidden_layers && !failed; ++l) {
@@ -1474,32 +1483,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         const bool fc1 = (l & 1) == 1;
         const bool last = l == hidden_layers;
-        for (int c = 0; c < 8; ++c) {
-          const int col0 = half * 256 + c * 32;
-          uint32_t raw[32];
-          float v[32];
-          CB_TMEM_LD32(tq + static_cast<uint32_t>(col0), raw);
+        for (int c = 0; c < F_GROUP_COLS / F_CW; ++c) {
+          const int col0 = group * F_GROUP_COLS + c * F_CW;
+          uint32_t raw[F_CW];
+          float v[F_CW];
+          CB_TMEM_LD16(tq + static_cast<uint32_t>(col0), raw);
           if (fc1) {
             // u = act(h W1^T + b1) over h in ACT; h + b2 into the accumulator for fc2.
-            float h[32];
-            fused_bias32(args.bias[l + 1], col0, h);
-            float hb[32];
-            act_load32(act, r, col0, hb);
-            fused_bias32(args.bias[l], col0, v);
+            float b2[F_CW], h[F_CW];
+            fused_bias16(args.bias[l + 1], col0, F_H, b2);
+            act_load16(act, r, col0, h);
+            fused_bias16(args.bias[l], col0, F_H, v);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(raw[j]);
-            activate_chunk<32>(v, act_code);
+            for (int j = 0; j < F_CW; ++j) v[j] += __uint_as_float(raw[j]);
+            activate_chunk<F_CW>(v, act_code);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) raw[j] = __float_as_uint(hb[j] + h[j]);
-            CB_TMEM_ST32(tq + static_cast<uint32_t>(col0), raw);
+            for (int j = 0; j < F_CW; ++j) raw[j] = __float_as_uint(h[j] + b2[j]);
+            CB_TMEM_ST16(tq + static_cast<uint32_t>(col0), raw);
           } else {
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
-            if (last) activate_chunk<32>(v, act_code);
+            for (int j = 0; j < F_CW; ++j) v[j] = __uint_as_float(raw[j]);
+            if (last) activate_chunk<F_CW>(v, act_code);
           }
-          act_store32(act, r, col0, v);
+          act_store16(act, r, col0, v);
         }
         fused_phase_done(ready0);
       }
@@ -1512,15 +1520,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int chunks = args.n_mma / 16;
       const float* bo = args.bias[hidden_layers + 1];
       int used = 0;
-      for (int c = half; c < chunks; c += 2, ++used) {
+      for (int c = group; c < chunks; c += F_GROUPS, ++used) {
         const int col0 = c * 16;
         uint32_t raw[16];
-        CB_TMEM_LD16(tq + static_cast<uint32_t>(col0), raw);
-        const float bl = (bo && lane < 16 && col0 + lane < args.n_out) ? __ldg(bo + col0 + lane) : 0.0f;
-        tmem_wait_ld();
         float v[16];
+        CB_TMEM_LD16(tq + static_cast<uint32_t>(col0), raw);
+        fused_bias16(bo, col0, args.n_out, v);
+        tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(raw[j]) + __shfl_sync(0xffffffffu, bl, j);
+        for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(raw[j]);
         uint8_t* buf = stage + (used & 1) * EPI_BUF;
         // The store that last read this buffer (two chunks back) is done with it.
         if (lane == 0) tma_store_wait_read<1>();
@@ -1563,7 +1571,7 @@ int fused_max_pairs(int dev) {
   if (!cache[dev]) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(sm_count() & ~1), 1, 1);
-    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.blockDim = dim3(F_THREADS, 1, 1);
     cfg.dynamicSmemBytes = F_SMEM_BYTES;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, fused_mlp_kernel, &cfg) != cudaSuccess || n <= 0) {
@@ -1629,7 +1637,7 @@ int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int
   const int64_t tiles = (m + 2 * BM - 1) / (2 * BM);
   const int64_t cap = fused_max_pairs(dev);
   const int64_t pairs = tiles < cap ? tiles : cap;
-  fused_mlp_kernel<<<static_cast<unsigned>(2 * pairs), THREADS, F_SMEM_BYTES, stream>>>(maps, args);
+  fused_mlp_kernel<<<static_cast<unsigned>(2 * pairs), F_THREADS, F_SMEM_BYTES, stream>>>(maps, args);
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }
 
