@@ -470,7 +470,8 @@ def main():
         "bad_status": sp["bad"],
         "e2e": {"value": sp["e2e_games"] / sp["e2e_elapsed"], "unit": "games/s",
                 "h2d_bytes_per_step": sp["h2d"], "d2h_bytes_per_step": sp["d2h"]},
-        "roofline": {"kernel": ("policy MLP forward: whole-network CTA-pair kernel (fused_mlp_kernel)"
+        "roofline": {"kernel": ("policy MLP forward + sampling: whole-network CTA-pair kernel "
+                                "(fused_mlp_kernel with its sampling head)"
                                 if policy.launches_per_forward() == 1 else
                                 "policy MLP forward: tcgen05 GEMM layers (gemm_kernel)"),
                      "bound": "tensor",

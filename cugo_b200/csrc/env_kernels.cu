@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) observe_kernel(
     const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids, i64 m,
     F* __restrict__ features, i64 ld, int legal_cols, bool* __restrict__ legal,
     uint8_t* __restrict__ players, bool* __restrict__ done, int16_t* __restrict__ status,
-    int hand_plane = 0) {
+    int hand_plane = 0, u64* __restrict__ legal_bits = nullptr) {
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
@@ -90,6 +90,11 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) observe_kernel(
     players[row] = static_cast<uint8_t>(meta.player);
     done[row] = meta.done != 0;
     status[row] = static_cast<int16_t>(meta.status);
+    if (legal_bits) {  // the mask as three words: bit a of word a / 64
+      legal_bits[row * 3 + 0] = meta.legal.w0;
+      legal_bits[row * 3 + 1] = meta.legal.w1;
+      legal_bits[row * 3 + 2] = meta.legal.w2;
+    }
   }
 }
 
@@ -249,6 +254,23 @@ int cugo_b200_observe_indexed_bf16(const uint8_t* states, int64_t n_states, cons
   observe_kernel<__nv_bfloat16><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<const u64*>(states), n_states, env_ids, m,
       static_cast<__nv_bfloat16*>(features), (i64)kFeatures, 0, legal, players, done, status);
+  return launch_status();
+}
+
+int cugo_b200_observe_indexed_bf16_bits(const uint8_t* states, int64_t n_states,
+                                        const int64_t* env_ids, int64_t m, void* features,
+                                        uint64_t* legal_bits, uint8_t* players, bool* done,
+                                        int16_t* status, cudaStream_t stream) {
+  if (n_states < 0 || m < 0 || (m > 0 && !env_ids)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (!features || !legal_bits || !players || !done || !status)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(features, 16) || !aligned(legal_bits, 8))
+    return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  observe_kernel<__nv_bfloat16><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<const u64*>(states), n_states, env_ids, m,
+      static_cast<__nv_bfloat16*>(features), (i64)kFeatures, 0, nullptr, players, done, status, 0,
+      reinterpret_cast<u64*>(legal_bits));
   return launch_status();
 }
 

@@ -34,6 +34,8 @@
 #include <string.h>
 
 #include "../../include/cugo_b200.h"
+#include "engine/driver.cuh"
+#include "gumbel.cuh"
 
 namespace {
 
@@ -1185,7 +1187,67 @@ struct FusedArgs {
   const float* bias[F_MAX_LAYERS];  // fp32 [n] or null
   int blocks, m, k_in, n_out, n_mma, act;
   int* error;
+  int write_out;                    // store the outputs (maps.out) or not
+  // Sampling head (actions != null): masked Gumbel-max over the first 179 outputs,
+  // with the noise and tie rules of cugo_b200_sample_actions.
+  const uint64_t* legal_bits;       // [m, 3]: bit a of word a / 64
+  const int64_t* game;              // [m]
+  const int32_t* decision;          // [m]
+  int64_t seed_base;
+  int greedy;
+  int64_t* actions;                 // [m]
+  float* logp;                      // [m]
 };
+
+constexpr int F_ACTIONS = 179;
+
+// A thread's running state of the sampling head over the columns it has seen.
+struct SampleState {
+  float best;   // best score (logit + noise), lowest action on ties
+  int best_a;   // -1: no legal action seen
+  float best_x; // the logit of best_a
+  float mx;     // running maximum of the legal logits
+  float sum;    // sum of exp(x - mx) over the legal logits
+};
+
+// Folds 16 outputs col0 .. col0 + 15 of the thread's row into the state (legal
+// actions only); bits: the row's legal actions col0 .. col0 + 15.
+__device__ __forceinline__ void sample_chunk(const FusedArgs& args, uint64_t gid, uint32_t dec,
+                                             int col0, uint32_t bits, const float* v,
+                                             SampleState& st) {
+  const uint64_t seed = static_cast<uint64_t>(args.seed_base) + gid;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int a0 = col0 + 4 * q;
+    const uint32_t nib = (bits >> (4 * q)) & 0xfu;
+    bool lg[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) lg[e] = (nib >> e) & 1u;
+    if (!nib) continue;
+    cb::Philox4 ph{};
+    if (!args.greedy)
+      ph = cb::philox4x32_10(static_cast<uint32_t>(gid), static_cast<uint32_t>(gid >> 32), dec,
+                             3u | (static_cast<uint32_t>(a0 >> 2) << 8), static_cast<uint32_t>(seed),
+                             static_cast<uint32_t>(seed >> 32));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (!lg[e]) continue;
+      const float x = v[4 * q + e];
+      const float score = args.greedy ? x : x + cb::gumbel_of(ph.v[e]);
+      if (score > st.best) {  // columns ascend within a thread: the first maximum is kept
+        st.best = score;
+        st.best_a = a0 + e;
+        st.best_x = x;
+      }
+      if (x > st.mx) {
+        st.sum = st.sum * expf(st.mx - x) + 1.0f;  // exp(-inf) = 0 on the first legal logit
+        st.mx = x;
+      } else {
+        st.sum += expf(x - st.mx);
+      }
+    }
+  }
+}
 
 // ACT address of 16-byte piece p (0..7) of row r in chunk kc: the TMA 128-byte swizzle.
 __device__ __forceinline__ uint8_t* act_piece(uint8_t* act, int kc, int r, int p) {
@@ -1263,7 +1325,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
   uint64_t* act_ready = acc_full + 1;    // CTA 0's counts both CTAs' epilogue warps
   uint64_t* act_free = act_ready + 1;    // this CTA's ACT is free for the next x tiles
   uint64_t* drained = act_free + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
+  uint64_t* sample_ready = drained + 1;  // [4]: a quadrant's other column groups posted
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sample_ready + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1288,6 +1351,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
     mbar_init(act_ready, 2 * F_EPI_WARPS);
     mbar_init(act_free, F_EPI_WARPS);
     mbar_init(drained, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&sample_ready[q], F_GROUPS - 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {  // both CTAs allocate together, same warp, same holder offset
@@ -1519,6 +1583,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
       }
       const int chunks = args.n_mma / 16;
       const float* bo = args.bias[hidden_layers + 1];
+      const int64_t row_g = static_cast<int64_t>(row0) + r;
+      const bool sampling = args.actions != nullptr;
+      const bool live = sampling && row_g < args.m;
+      const uint64_t gid = live ? static_cast<uint64_t>(__ldg(args.game + row_g)) : 0;
+      const uint32_t dec = live ? static_cast<uint32_t>(__ldg(args.decision + row_g)) : 0;
+      SampleState st{-INFINITY, -1, 0.0f, -INFINITY, 0.0f};
+      uint64_t lw[3] = {0ull, 0ull, 0ull};
+      if (live) {
+        const uint64_t* p = args.legal_bits + row_g * 3;
+        lw[0] = __ldg(p);
+        lw[1] = __ldg(p + 1);
+        lw[2] = __ldg(p + 2);
+      }
       int used = 0;
       for (int c = group; c < chunks; c += F_GROUPS, ++used) {
         const int col0 = c * 16;
@@ -1529,13 +1606,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(raw[j]);
-        uint8_t* buf = stage + (used & 1) * EPI_BUF;
-        // The store that last read this buffer (two chunks back) is done with it.
-        if (lane == 0) tma_store_wait_read<1>();
-        __syncwarp();
-        if (col0 < args.n_out) store_chunk<float>(buf, v, &maps.out, row0 + quad * 32, col0);
+        if (live && col0 < F_ACTIONS) {
+          const int wi = col0 >> 6;  // the word holding actions col0 .. col0 + 15
+          const uint64_t w = wi == 0 ? lw[0] : (wi == 1 ? lw[1] : lw[2]);
+          sample_chunk(args, gid, dec, col0, static_cast<uint32_t>(w >> (col0 & 63)) & 0xffffu, v,
+                       st);
+        }
+        if (args.write_out) {
+          uint8_t* buf = stage + (used & 1) * EPI_BUF;
+          // The store that last read this buffer (two chunks back) is done with it.
+          if (lane == 0) tma_store_wait_read<1>();
+          __syncwarp();
+          if (col0 < args.n_out) store_chunk<float>(buf, v, &maps.out, row0 + quad * 32, col0);
+        }
       }
-      if (lane == 0) tma_store_wait_read<0>();  // ACT may take the next tile's x
+      if (sampling) {
+        // The quadrant's column groups meet in ACT (past the output staging): groups
+        // 1.. post their state, group 0 combines and writes the row's action and log p.
+        float4* post = reinterpret_cast<float4*>(act + F_EPI_WARPS * 2 * EPI_BUF);
+        if (group > 0) {
+          post[(r * F_GROUPS + group) * 2] = make_float4(st.best, __int_as_float(st.best_a), st.best_x, st.mx);
+          post[(r * F_GROUPS + group) * 2 + 1] = make_float4(st.sum, 0.0f, 0.0f, 0.0f);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sample_ready[quad]);
+        } else {
+          if (!mbar_wait(&sample_ready[quad], static_cast<uint32_t>(iter & 1))) failed = true;
+          if (!failed && live) {
+            for (int g2 = 1; g2 < F_GROUPS; ++g2) {
+              const float4 p0 = post[(r * F_GROUPS + g2) * 2];
+              const float4 p1 = post[(r * F_GROUPS + g2) * 2 + 1];
+              const int a = __float_as_int(p0.y);
+              if (a >= 0 && (p0.x > st.best || (p0.x == st.best && (st.best_a < 0 || a < st.best_a)))) {
+                st.best = p0.x;
+                st.best_a = a;
+                st.best_x = p0.z;
+              }
+              if (p0.w != -INFINITY) {
+                const float m2 = fmaxf(st.mx, p0.w);
+                st.sum = st.sum * expf(st.mx - m2) + p1.x * expf(p0.w - m2);
+                st.mx = m2;
+              }
+            }
+            args.actions[row_g] = st.best_a;
+            args.logp[row_g] = st.best_a < 0 ? 0.0f : st.best_x - (st.mx + logf(st.sum));
+          }
+        }
+      }
+      if (lane == 0 && args.write_out) tma_store_wait_read<0>();  // ACT may take the next tile's x
       __syncwarp();
       fence_before();
       if (lane == 0) {
@@ -1587,19 +1704,28 @@ int fused_max_pairs(int dev) {
 
 extern "C" {
 
-int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
-                        const void* const* weights, const float* const* biases, int64_t n_out,
-                        int32_t act, float* out, int64_t ldo, int32_t* error, cudaStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// Both entry points: out may be null when sampling (actions != null).
+int fused_launch(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
+                 const void* const* weights, const float* const* biases, int64_t n_out,
+                 int32_t act, float* out, int64_t ldo, const uint64_t* legal, const int64_t* game,
+                 const int32_t* decision, int64_t seed_base, int32_t greedy, int64_t* actions,
+                 float* logp, int32_t* error, cudaStream_t stream) {
   if (m < 0 || k_in <= 0 || k_in > F_MAX_KIN || blocks < 0 || blocks > F_MAX_BLOCKS ||
       n_out <= 0 || n_out > BN || !weights || act < 0 || act > 2)
     return CUGO_B200_ERR_ARG;
   if (m == 0) return CUGO_B200_OK;
-  if (m > INT32_MAX || !x || !out || ldx < k_in || ldo < n_out) return CUGO_B200_ERR_ARG;
+  if (m > INT32_MAX || !x || (!out && !actions) || ldx < k_in || (out && ldo < n_out))
+    return CUGO_B200_ERR_ARG;
+  if (actions && (!logp || !legal || !game || !decision || n_out < F_ACTIONS)) return CUGO_B200_ERR_ARG;
   const int layers = 2 + 2 * blocks;
   for (int l = 0; l < layers; ++l)
     if (!weights[l]) return CUGO_B200_ERR_ARG;
   const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (!al(x) || ldx % 8 || !al(out) || ldo % 4 || k_in % 8) return CUGO_B200_ERR_ALIGN;
+  if (!al(x) || ldx % 8 || (out && (!al(out) || ldo % 4)) || k_in % 8) return CUGO_B200_ERR_ALIGN;
   for (int l = 0; l < layers; ++l)
     if (!al(weights[l])) return CUGO_B200_ERR_ALIGN;
   int dev = 0;
@@ -1624,8 +1750,16 @@ int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int
   if (!make_map(&maps.w[layers - 1], weights[layers - 1], n_out, F_H, F_H,
                 static_cast<uint32_t>(n_mma / 2)))
     return CUGO_B200_ERR_LAUNCH;
-  if (!make_out_map(&maps.out, out, m, n_out, ldo, true)) return CUGO_B200_ERR_LAUNCH;
+  if (out && !make_out_map(&maps.out, out, m, n_out, ldo, true)) return CUGO_B200_ERR_LAUNCH;
   FusedArgs args{};
+  args.write_out = out ? 1 : 0;
+  args.legal_bits = legal;
+  args.game = game;
+  args.decision = decision;
+  args.seed_base = seed_base;
+  args.greedy = greedy;
+  args.actions = actions;
+  args.logp = logp;
   for (int l = 0; l < layers; ++l) args.bias[l] = biases ? biases[l] : nullptr;
   args.blocks = blocks;
   args.m = static_cast<int>(m);
@@ -1639,6 +1773,57 @@ int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int
   const int64_t pairs = tiles < cap ? tiles : cap;
   fused_mlp_kernel<<<static_cast<unsigned>(2 * pairs), F_THREADS, F_SMEM_BYTES, stream>>>(maps, args);
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+// Packs bool masks [m, 179] into three words per row (bit a of word a / 64).
+__global__ void __launch_bounds__(256) pack_legal_kernel(const bool* __restrict__ legal, int64_t m,
+                                                         uint64_t* __restrict__ bits) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= m) return;  // whole warps
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(legal) + row * F_ACTIONS;
+  uint32_t w[6];
+#pragma unroll
+  for (int k = 0; k < 6; ++k) {
+    const int a = 32 * k + lane;
+    w[k] = __ballot_sync(0xffffffffu, a < F_ACTIONS && src[a] != 0);
+  }
+  if (lane < 3)
+    bits[row * 3 + lane] = (static_cast<uint64_t>(lane == 0 ? w[1] : lane == 1 ? w[3] : w[5]) << 32) |
+                           (lane == 0 ? w[0] : lane == 1 ? w[2] : w[4]);
+}
+
+}  // namespace
+
+extern "C" {
+
+int cugo_b200_pack_legal(const bool* legal, int64_t m, uint64_t* bits, cudaStream_t stream) {
+  if (m < 0 || (m > 0 && (!legal || !bits))) return CUGO_B200_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(bits) & 7u) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  pack_legal_kernel<<<static_cast<unsigned>((m * 32 + 255) / 256), 256, 0, stream>>>(legal, m, bits);
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
+}
+
+int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
+                        const void* const* weights, const float* const* biases, int64_t n_out,
+                        int32_t act, float* out, int64_t ldo, int32_t* error, cudaStream_t stream) {
+  if (m > 0 && !out) return CUGO_B200_ERR_ARG;
+  return fused_launch(x, ldx, m, k_in, blocks, weights, biases, n_out, act, out, ldo, nullptr,
+                      nullptr, nullptr, 0, 0, nullptr, nullptr, error, stream);
+}
+
+int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
+                               const void* const* weights, const float* const* biases,
+                               int64_t n_out, int32_t act, const uint64_t* legal_bits,
+                               const int64_t* game,
+                               const int32_t* decision, int64_t seed_base, int32_t greedy,
+                               int64_t* actions, float* logp, float* out, int64_t ldo,
+                               int32_t* error, cudaStream_t stream) {
+  if (m > 0 && (!actions || !logp)) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (reinterpret_cast<uintptr_t>(legal_bits) & 7u)) return CUGO_B200_ERR_ALIGN;
+  return fused_launch(x, ldx, m, k_in, blocks, weights, biases, n_out, act, out, ldo, legal_bits,
+                      game, decision, seed_base, greedy, actions, logp, error, stream);
 }
 
 }  // extern "C"

@@ -16,16 +16,12 @@
 #include <stdint.h>
 
 #include "engine/driver.cuh"
+#include "gumbel.cuh"
 #include "../../include/cugo_b200.h"
 
 using namespace cb;
 
 namespace {
-
-__device__ __forceinline__ float gumbel_of(u32 word) {
-  const float u = (static_cast<float>(word >> 8) + 0.5f) * (1.0f / 16777216.0f);
-  return -logf(-logf(u));
-}
 
 // logits: [m, ld] fp32 (columns 0..178 are the policy logits); legal: [m, 179].
 //

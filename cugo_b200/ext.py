@@ -55,6 +55,10 @@ _SIGNATURES: dict[str, list] = {
                                   _VP],
     "cugo_b200_mlp_fused": [_VP, _I64, _I64, _I64, _I32, _VP, _VP, _I64, _I32, _VP, _I64, _VP,
                             _VP],
+    "cugo_b200_mlp_fused_sample": [_VP, _I64, _I64, _I64, _I32, _VP, _VP, _I64, _I32, _VP, _VP,
+                                   _VP, _I64, _I32, _VP, _VP, _VP, _I64, _VP, _VP],
+    "cugo_b200_pack_legal": [_VP, _I64, _VP, _VP],
+    "cugo_b200_observe_indexed_bf16_bits": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_rowdot_bf16": [_VP, _I64, _VP, _VP, _I64, _I64, _VP, _I64, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
@@ -380,6 +384,36 @@ class CugoB200Extension:
                 self._stream(states.device)), "observe_indexed_bf16")
         return out
 
+    def observe_indexed_bf16_bits(self, states, env_ids) -> list[torch.Tensor]:
+        """observe_indexed_bf16 with the legal mask as int64 [m, 3] bit words (bit a of
+        word a / 64) in place of the bool mask: [features, legal_bits, players, done,
+        status]."""
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        _same_device(states, env_ids, "states", "env_ids")
+        m = env_ids.numel()
+        dev = states.device
+        with torch.cuda.device(dev):
+            out = self._obs_outputs(m, dev)
+            out[0] = torch.empty((m, self.FEATURE_COUNT), dtype=torch.bfloat16, device=dev)
+            out[1] = torch.empty((m, 3), dtype=torch.int64, device=dev)
+            _check(self._lib.cugo_b200_observe_indexed_bf16_bits(
+                _ptr(states), states.size(0), _ptr(env_ids), m, *map(_ptr, out),
+                self._stream(dev)), "observe_indexed_bf16_bits")
+        return out
+
+    def pack_legal(self, legal: torch.Tensor) -> torch.Tensor:
+        """bool [m, 179] legal masks as int64 [m, 3] bit words."""
+        if legal.dtype != torch.bool or not legal.is_contiguous() or legal.dim() != 2 \
+                or legal.shape[1] != self.ACTION_COUNT:
+            raise RuntimeError("legal must be a contiguous bool [m, 179] tensor")
+        m = legal.shape[0]
+        bits = torch.empty((m, 3), dtype=torch.int64, device=legal.device)
+        with torch.cuda.device(legal.device):
+            _check(self._lib.cugo_b200_pack_legal(_ptr(legal), m, _ptr(bits),
+                                                  self._stream(legal.device)), "pack_legal")
+        return bits
+
     def observe_query_bf16(self, states, env_ids, query: torch.Tensor | None = None,
                            width: int = 904) -> list[torch.Tensor]:
         """observe_indexed writing the sequence policy's query input bf16 [m, width]:
@@ -547,6 +581,42 @@ class CugoB200Extension:
                 _ptr(x), x.stride(0), m, k_in, (len(weights) - 2) // 2, wp, bp, n_out, act,
                 _ptr(out), out.stride(0), _ptr(error), self._stream(x.device)), "mlp_fused")
         return out
+
+    def mlp_fused_sample(self, x: torch.Tensor, weights: list[torch.Tensor],
+                         biases: list[torch.Tensor | None], act: int, legal: torch.Tensor,
+                         game: torch.Tensor, decision: torch.Tensor, seed_base: int = 12345,
+                         greedy: bool = False, want_logits: bool = False):
+        """The hidden-512 MLP and the masked Gumbel-max sampling of its first 179
+        outputs in one kernel: (actions int64 [m], logp fp32 [m], logits or None).
+        legal: bool [m, 179], or the int64 [m, 3] bit words of observe_indexed_bf16_bits."""
+        m, k_in = x.shape
+        if x.dtype != torch.bfloat16 or x.stride(1) != 1:
+            raise RuntimeError("mlp_fused_sample expects row-major bf16 x")
+        if any(w.dtype != torch.bfloat16 or not w.is_contiguous() for w in weights):
+            raise RuntimeError("mlp_fused_sample expects contiguous bf16 weights")
+        if weights[0].shape[0] != 512 or weights[0].shape[1] != k_in:
+            raise RuntimeError("mlp_fused_sample expects hidden 512 and an input weight [512, k_in]")
+        if legal.dtype == torch.bool:
+            legal = self.pack_legal(legal)
+        if legal.dtype != torch.int64 or not legal.is_contiguous() or legal.shape != (m, 3):
+            raise RuntimeError("legal must be a bool [m, 179] mask or its int64 [m, 3] bit words")
+        _check_cuda_1d(game, torch.int64, "game")
+        _check_cuda_1d(decision, torch.int32, "decision")
+        n_out = weights[-1].shape[0]
+        dev = x.device
+        actions = torch.empty((m,), dtype=torch.int64, device=dev)
+        logp = torch.empty((m,), dtype=torch.float32, device=dev)
+        out = (torch.empty((m, (n_out + 3) // 4 * 4), dtype=torch.float32, device=dev)[:, :n_out]
+               if want_logits else None)
+        wp = (ctypes.c_void_p * len(weights))(*[w.data_ptr() for w in weights])
+        bp = (ctypes.c_void_p * len(biases))(*[b.data_ptr() if b is not None else None for b in biases])
+        with torch.cuda.device(dev):
+            _check(self._lib.cugo_b200_mlp_fused_sample(
+                _ptr(x), x.stride(0), m, k_in, (len(weights) - 2) // 2, wp, bp, n_out, act,
+                _ptr(legal), _ptr(game), _ptr(decision), seed_base, int(greedy), _ptr(actions),
+                _ptr(logp), _ptr(out), out.stride(0) if out is not None else 0, None,
+                self._stream(dev)), "mlp_fused_sample")
+        return actions, logp, out
 
     def rowdot(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
                out: torch.Tensor | None = None) -> torch.Tensor:

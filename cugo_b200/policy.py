@@ -78,6 +78,10 @@ class ResidualMlpPolicy:
     def flops_per_row(self) -> int:
         return 2 * sum(w.shape[0] * w.shape[1] for w in self.weights)
 
+    def launches_per_step(self) -> int:
+        """Kernel launches of forward_sample (the policy and the sampler)."""
+        return 1 if self.samples_in_kernel() else self.launches_per_forward() + 1
+
     def launches_per_forward(self) -> int:
         if fused_mlp_supported(self.hidden, self.blocks, self.inputs, self.outputs):
             return 1
@@ -123,3 +127,25 @@ class ResidualMlpPolicy:
         return out
 
     __call__ = forward
+
+    def samples_in_kernel(self) -> bool:
+        """Whether forward_sample runs as one fused kernel (and takes bit-word masks)."""
+        return fused_mlp_supported(self.hidden, self.blocks, self.inputs, self.outputs) \
+            and self.outputs >= ACTIONS
+
+    @torch.no_grad()
+    def forward_sample(self, features: torch.Tensor, legal: torch.Tensor, game: torch.Tensor,
+                       decision: torch.Tensor, seed_base: int = 12345, greedy: bool = False):
+        """Actions and log-probabilities of the masked Gumbel-max sampler over this
+        policy's logits (cugo_b200_sample_actions' definition): in the fused MLP's
+        head when it runs this shape, else the forward followed by the sampler.
+        legal: bool [m, 179], or (fused head only) its int64 [m, 3] bit words."""
+        ext = self._extension()
+        x = features if features.dtype == torch.bfloat16 else features.to(torch.bfloat16)
+        x = x.contiguous()
+        if self.samples_in_kernel():
+            actions, logp, _ = ext.mlp_fused_sample(x, self.weights, self._fp32_biases(),
+                                                    _ACT[self.activation], legal, game, decision,
+                                                    seed_base, greedy)
+            return actions, logp
+        return ext.sample_actions(self.forward(x), legal, game, decision, seed_base, greedy=greedy)

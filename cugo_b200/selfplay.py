@@ -67,15 +67,21 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     rounds = 0
     n_launch = 1
     for rounds in range(1, max_rounds + 1):
-        features, legal, _players, _done, status = ext.observe_indexed_bf16(states, active)
+        fused = getattr(policy, "samples_in_kernel", lambda: False)()
+        # A fused policy step reads the legal mask as bit words.
+        observe = ext.observe_indexed_bf16_bits if fused else ext.observe_indexed_bf16
+        features, legal, _players, _done, status = observe(states, active)
+        game_ids = game_index.index_select(0, active)
+        dec = decision.index_select(0, active)
         t0 = timer.start() if timer else None
-        logits = policy(features)
+        if hasattr(policy, "forward_sample"):  # policy and sampling in one launch where fused
+            actions, _logp = policy.forward_sample(features, legal, game_ids, dec, seed_base)
+        else:
+            actions, _logp = ext.sample_actions(policy(features), legal, game_ids, dec, seed_base)
         if timer:
             timer.stop(t0, active.numel())
-        actions, _logp = ext.sample_actions(logits, legal, game_index.index_select(0, active),
-                                            decision.index_select(0, active), seed_base)
         reward, new_done, new_nagari, step_status, _ = ext.step_indexed(states, active, actions)
-        n_launch += 3 + getattr(policy, "launches_per_forward", lambda: 0)()
+        n_launch += 2 + getattr(policy, "launches_per_step", lambda: 1)()
         bad += ((step_status != 0) & (step_status != 9)).sum()
         decisions += active.numel()
         decision.index_add_(0, active, torch.ones_like(active, dtype=torch.int32))

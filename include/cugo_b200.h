@@ -242,6 +242,29 @@ CUGO_B200_API int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int
                                       float* out, int64_t ldo, int32_t* error,
                                       cudaStream_t stream);
 
+/* cugo_b200_mlp_fused with the policy's sampling in the same kernel (the reference's
+ * _act, python/cugo_ppo50.py:74-82, with Gumbel-max instead of torch.multinomial):
+ * per row, the masked Gumbel-max action over the first 179 outputs and its log
+ * probability, as cugo_b200_sample_actions computes them from the same logits (the
+ * same Philox noise, lowest action on ties, -1 and log p 0 for a row without a legal
+ * action).  legal_bits uint64 [m, 3] (bit a of word a / 64: what
+ * cugo_b200_observe_indexed_bf16_bits writes, or cugo_b200_pack_legal makes from a
+ * bool mask), game int64 [m], decision int32 [m], actions int64 [m], logp fp32 [m];
+ * n_out >= 179; out (fp32 [m, ldo]) may be NULL when the logits are not needed. */
+CUGO_B200_API int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t m,
+                                             int64_t k_in, int32_t blocks,
+                                             const void* const* weights,
+                                             const float* const* biases, int64_t n_out,
+                                             int32_t act, const uint64_t* legal_bits,
+                                             const int64_t* game, const int32_t* decision,
+                                             int64_t seed_base, int32_t greedy, int64_t* actions,
+                                             float* logp, float* out, int64_t ldo,
+                                             int32_t* error, cudaStream_t stream);
+
+/* Packs bool legal masks [m, 179] into uint64 [m, 3] (bit a of word a / 64). */
+CUGO_B200_API int cugo_b200_pack_legal(const bool* legal, int64_t m, uint64_t* bits,
+                                       cudaStream_t stream);
+
 /* Policy forward that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory — for example a Go/Java/Rust
  * serving process that passes only its own fixed input and output buffers and keeps
@@ -267,6 +290,14 @@ CUGO_B200_API int cugo_b200_policy_forward_noalloc(const void* x, int64_t ldx, i
                                                    const void* const* biases, int32_t act,
                                                    float* out, int64_t ldo, int32_t* error,
                                                    cudaStream_t stream);
+
+/* observe_indexed_bf16 with the legal mask written as bits, uint64 [m, 3] (bit a of
+ * word a / 64), for the fused MLP's sampling head; no bool mask is written. */
+CUGO_B200_API int cugo_b200_observe_indexed_bf16_bits(const uint8_t* states, int64_t n_states,
+                                                      const int64_t* env_ids, int64_t m,
+                                                      void* features_bf16, uint64_t* legal_bits,
+                                                      uint8_t* players, bool* done,
+                                                      int16_t* status, cudaStream_t stream);
 
 /* observe_indexed with the features written as bf16 [m, 720] (16-byte aligned):
  * the policy's input layer reads them directly.  Same values as observe_indexed

@@ -82,3 +82,44 @@ def test_policy_routes_through_the_fused_kernel(ext, monkeypatch):
     scale = max(1.0, float(exact.abs().max()))
     assert float((fused - layers).abs().max()) <= 1e-2 * scale
     assert float((fused - exact).abs().max()) <= 1e-2 * scale
+
+
+@pytest.mark.parametrize("m,n_out,greedy,density", [(70000, 180, False, 0.1), (1000, 179, True, 0.3),
+                                                   (333, 256, False, 0.02), (129, 180, False, 0.0)])
+def test_fused_sampling_head_matches_the_sampler(ext, m, n_out, greedy, density):
+    """Actions equal cugo_b200_sample_actions on the kernel's own logits (same noise,
+    same tie rule); log p within 1e-5 (the log-sum-exp adds in another order)."""
+    ws, bs = _net(720, 3, n_out, seed=m)
+    g = torch.Generator().manual_seed(7)
+    x = torch.rand((m, 720), generator=g).to(DEV, torch.bfloat16)
+    legal = torch.rand((m, 179), generator=g) < density
+    legal[::7, :] = False  # rows without a legal action: -1, log p 0
+    legal[1::7, 5] = True
+    legal = legal.to(DEV)
+    game = torch.randint(0, 1 << 40, (m,), generator=g).to(DEV)
+    decision = torch.randint(0, 60, (m,), generator=g, dtype=torch.int32).to(DEV)
+    actions, logp, logits = ext.mlp_fused_sample(x, ws, bs, 2, legal, game, decision, seed_base=99,
+                                                 greedy=greedy, want_logits=True)
+    assert torch.equal(logits, ext.mlp_fused(x, ws, bs, 2))
+    ref_a, ref_lp = ext.sample_actions(logits.contiguous() if n_out % 4 else logits, legal, game,
+                                       decision, seed_base=99, greedy=greedy)
+    assert torch.equal(actions, ref_a)
+    assert float((logp - ref_lp).abs().max()) <= 1e-5 * max(1.0, float(ref_lp.abs().max()))
+    assert bool((actions[::7] == -1).all()) and bool((logp[::7] == 0).all())
+    a2, lp2, none = ext.mlp_fused_sample(x, ws, bs, 2, legal, game, decision, seed_base=99,
+                                         greedy=greedy)
+    assert none is None and torch.equal(a2, actions) and torch.equal(lp2, logp)
+
+
+def test_observe_bits_and_pack_legal_agree_with_the_bool_mask(ext):
+    idx = torch.arange(5000, device=DEV, dtype=torch.int64)
+    states = ext.create(idx + 31, idx & 1)
+    ids = torch.randint(0, 5000, (7777,), device=DEV)
+    ids[3] = 9999  # out of range: an empty mask
+    f, legal, p, d, st = ext.observe_indexed_bf16(states, ids)
+    f2, bits, p2, d2, st2 = ext.observe_indexed_bf16_bits(states, ids)
+    assert torch.equal(f, f2) and torch.equal(p, p2) and torch.equal(d, d2) and torch.equal(st, st2)
+    assert torch.equal(bits, ext.pack_legal(legal))
+    a = torch.arange(179, device=DEV)
+    words = bits.gather(1, (a // 64).expand(bits.shape[0], -1))
+    assert torch.equal(((words >> (a % 64)) & 1).bool(), legal)
