@@ -102,11 +102,26 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) observe_kernel(
 //   ids == nullptr: row i steps state i in place.
 //   children != nullptr: the stepped copy goes to children[i] (branch); the
 //   parent row is not written; a bad id gives a zero child.
+// The bookkeeping of a self-play round folded into the step (step_compact): per row
+// of game id, decision[id] += 1; a finished game's reward0[id] and nagari[id]; a
+// status other than OK and "finished" counted in *bad; the ids of games still
+// running appended to next_ids (warp-aggregated, so their order varies from run to
+// run; every game's play is independent of its row), *next_count their number.
+struct RoundTail {
+  int32_t* decision;
+  float* reward0;
+  bool* nagari;
+  i64* bad;
+  i64* next_ids;
+  int32_t* next_count;
+};
+
 __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
     u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids,
     const i64* __restrict__ actions, i64 m, u64* __restrict__ children,
     float* __restrict__ reward, bool* __restrict__ done, bool* __restrict__ nagari,
-    int16_t* __restrict__ status, bool* __restrict__ committed, i64* __restrict__ events) {
+    int16_t* __restrict__ status, bool* __restrict__ committed, i64* __restrict__ events,
+    RoundTail tail = RoundTail{}) {
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
@@ -130,6 +145,26 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
   if (children) store_tile(t, children, tile_base, m, row < m ? row : -1);
   else if (!ids) store_tile(t, states, tile_base, m, src);  // in place, rows in order
   else scatter_rows(t, states, src);
+  if (tail.next_ids) {  // ids are distinct (one row per game)
+    const i64 id = src;
+    const bool fin = src >= 0 && out.done != 0;
+    if (src >= 0) {
+      tail.decision[id] += 1;
+      if (fin) {
+        tail.reward0[id] = static_cast<float>(out.reward0);
+        tail.nagari[id] = out.nagari != 0;
+      }
+      const u32 st = static_cast<u32>(out.status);
+      if (st != kOk && st != kFinished) atomicAdd(reinterpret_cast<unsigned long long*>(tail.bad), 1ull);
+    }
+    const bool keep = src >= 0 && !fin;
+    const unsigned mask = __ballot_sync(kFull, keep);
+    const int lane = threadIdx.x & 31;
+    int base = 0;
+    if (lane == 0 && mask) base = atomicAdd(tail.next_count, __popc(mask));
+    base = __shfl_sync(kFull, base, 0);
+    if (keep) tail.next_ids[base + __popc(mask & ((1u << lane) - 1u))] = id;
+  }
   if (row < m && reward) {  // internal callers may skip the per-row outputs
     reward[row] = static_cast<float>(out.reward0);
     done[row] = out.done != 0;
@@ -364,6 +399,24 @@ int cugo_b200_step_indexed(uint8_t* states, int64_t n_states, const int64_t* env
   if (m > 0 && !env_ids) return CUGO_B200_ERR_ARG;
   return step_common(states, n_states, env_ids, actions, m, nullptr, reward, done, nagari, status,
                      committed, nullptr, stream);
+}
+
+int cugo_b200_step_compact(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                           const int64_t* actions, int64_t m, int32_t* decision, float* reward0,
+                           bool* nagari, int64_t* bad, int64_t* next_ids, int32_t* next_count,
+                           cudaStream_t stream) {
+  if (n_states < 0 || m < 0) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (!env_ids || !actions || !decision || !reward0 || !nagari || !bad || !next_ids ||
+                !next_count))
+    return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  RoundTail tail{decision, reward0, nagari, bad, next_ids, next_count};
+  step_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+      reinterpret_cast<u64*>(states), n_states, env_ids, actions, m, nullptr, nullptr, nullptr,
+      nullptr, nullptr, nullptr, nullptr, tail);
+  return launch_status();
 }
 
 int cugo_b200_step_events_indexed(uint8_t* states, int64_t n_states, const int64_t* env_ids,

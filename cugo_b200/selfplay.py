@@ -61,16 +61,20 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     decision = torch.zeros(g, dtype=torch.int32, device=device)
     reward0 = torch.zeros(g, dtype=torch.float32, device=device)
     nagari = torch.zeros(g, dtype=torch.bool, device=device)
-    bad = torch.zeros((), dtype=torch.int64, device=device)
+    bad = torch.zeros(1, dtype=torch.int64, device=device)
     active = torch.arange(g, device=device)
+    # The games still running after a round, written by the step kernel (ping-pong).
+    ids_buf = (torch.empty(g, dtype=torch.int64, device=device),
+               torch.empty(g, dtype=torch.int64, device=device))
+    count = torch.zeros(1, dtype=torch.int32, device=device)
     decisions = 0
     rounds = 0
     n_launch = 1
+    fused = getattr(policy, "samples_in_kernel", lambda: False)()
+    # A fused policy step reads the legal mask as bit words.
+    observe = ext.observe_indexed_bf16_bits if fused else ext.observe_indexed_bf16
     for rounds in range(1, max_rounds + 1):
-        fused = getattr(policy, "samples_in_kernel", lambda: False)()
-        # A fused policy step reads the legal mask as bit words.
-        observe = ext.observe_indexed_bf16_bits if fused else ext.observe_indexed_bf16
-        features, legal, _players, _done, status = observe(states, active)
+        features, legal, _players, _done, _status = observe(states, active)
         game_ids = game_index.index_select(0, active)
         dec = decision.index_select(0, active)
         t0 = timer.start() if timer else None
@@ -80,16 +84,15 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
             actions, _logp = ext.sample_actions(policy(features), legal, game_ids, dec, seed_base)
         if timer:
             timer.stop(t0, active.numel())
-        reward, new_done, new_nagari, step_status, _ = ext.step_indexed(states, active, actions)
+        nxt = ids_buf[rounds & 1]
+        count.zero_()
+        ext.step_compact(states, active, actions, decision, reward0, nagari, bad, nxt, count)
         n_launch += 2 + getattr(policy, "launches_per_step", lambda: 1)()
-        bad += ((step_status != 0) & (step_status != 9)).sum()
         decisions += active.numel()
-        decision.index_add_(0, active, torch.ones_like(active, dtype=torch.int32))
-        reward0.index_copy_(0, active, torch.where(new_done, reward, 0.0))
-        nagari.index_copy_(0, active, new_done & new_nagari)
-        active = active.index_select(0, torch.nonzero(~new_done).squeeze(1))
-        if active.numel() == 0:
+        live = int(count.item())  # the round's one device->host read
+        if live == 0:
             break
+        active = nxt[:live]
     else:
         raise RuntimeError(f"games did not finish within {max_rounds} rounds")
     if launches is not None:
