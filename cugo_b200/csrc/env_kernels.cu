@@ -104,16 +104,15 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) observe_kernel(
 //   parent row is not written; a bad id gives a zero child.
 // The bookkeeping of a self-play round folded into the step (step_compact): per row
 // of game id, decision[id] += 1; a finished game's reward0[id] and nagari[id]; a
-// status other than OK and "finished" counted in *bad; the ids of games still
-// running appended to next_ids (warp-aggregated, so their order varies from run to
-// run; every game's play is independent of its row), *next_count their number.
+// status other than OK and "finished" counted in *bad; per warp, the ballot of its
+// rows still running (keep[warp]), from which compact_scan_kernel and
+// compact_scatter_kernel build the next id list in the same order.
 struct RoundTail {
   int32_t* decision;
   float* reward0;
   bool* nagari;
   i64* bad;
-  i64* next_ids;
-  int32_t* next_count;
+  uint32_t* keep;  // [ceil(m / 32)]
 };
 
 __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
@@ -145,7 +144,7 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
   if (children) store_tile(t, children, tile_base, m, row < m ? row : -1);
   else if (!ids) store_tile(t, states, tile_base, m, src);  // in place, rows in order
   else scatter_rows(t, states, src);
-  if (tail.next_ids) {  // ids are distinct (one row per game)
+  if (tail.keep) {  // ids are distinct (one row per game)
     const i64 id = src;
     const bool fin = src >= 0 && out.done != 0;
     if (src >= 0) {
@@ -157,13 +156,9 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
       const u32 st = static_cast<u32>(out.status);
       if (st != kOk && st != kFinished) atomicAdd(reinterpret_cast<unsigned long long*>(tail.bad), 1ull);
     }
-    const bool keep = src >= 0 && !fin;
-    const unsigned mask = __ballot_sync(kFull, keep);
-    const int lane = threadIdx.x & 31;
-    int base = 0;
-    if (lane == 0 && mask) base = atomicAdd(tail.next_count, __popc(mask));
-    base = __shfl_sync(kFull, base, 0);
-    if (keep) tail.next_ids[base + __popc(mask & ((1u << lane) - 1u))] = id;
+    const unsigned mask = __ballot_sync(kFull, src >= 0 && !fin);
+    const i64 w = ((i64)blockIdx.x * kBlock + (threadIdx.x & ~31)) >> 5;
+    if ((threadIdx.x & 31) == 0 && w * 32 < m) tail.keep[w] = mask;
   }
   if (row < m && reward) {  // internal callers may skip the per-row outputs
     reward[row] = static_cast<float>(out.reward0);
@@ -176,6 +171,56 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
       for (int k = 0; k < (int)kEventWords; ++k) events[row * kEventWords + k] = ev[k];
     }
   }
+}
+
+// Exclusive prefix over the warps' running counts (one block): offsets[w], and
+// the total in *count.
+__global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __restrict__ keep,
+                                                            i64 warps, int32_t* __restrict__ offsets,
+                                                            int32_t* __restrict__ count) {
+  __shared__ int32_t sums[32];
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const i64 per = (warps + blockDim.x - 1) / blockDim.x;  // consecutive warps per thread
+  const i64 w0 = t * per;
+  int32_t mine = 0;
+  for (i64 w = w0; w < w0 + per && w < warps; ++w) mine += __popc(__ldg(keep + w));
+  int32_t incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t v = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) sums[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    int32_t v = lane < (int)(blockDim.x >> 5) ? sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t u = __shfl_up_sync(kFull, v, o);
+      if (lane >= o) v += u;
+    }
+    sums[lane] = v;  // inclusive over warps 0..lane
+  }
+  __syncthreads();
+  int32_t run = incl - mine + (wid > 0 ? sums[wid - 1] : 0);
+  for (i64 w = w0; w < w0 + per && w < warps; ++w) {
+    offsets[w] = run;
+    run += __popc(__ldg(keep + w));
+  }
+  if (t == blockDim.x - 1) *count = run;
+}
+
+// next_ids[offsets[w] + rank of the row among its warp's running rows] = ids[row].
+__global__ void __launch_bounds__(256) compact_scatter_kernel(const uint32_t* __restrict__ keep,
+                                                              const int32_t* __restrict__ offsets,
+                                                              const i64* __restrict__ ids, i64 m,
+                                                              i64* __restrict__ next_ids) {
+  const i64 row = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= m) return;
+  const uint32_t mask = __ldg(keep + (row >> 5));
+  const int lane = static_cast<int>(row & 31);
+  if ((mask >> lane) & 1u)
+    next_ids[__ldg(offsets + (row >> 5)) + __popc(mask & ((1u << lane) - 1u))] = __ldg(ids + row);
 }
 
 __global__ void __launch_bounds__(kBlock) clone_kernel(const u64* __restrict__ states, i64 n_states,
@@ -404,18 +449,27 @@ int cugo_b200_step_indexed(uint8_t* states, int64_t n_states, const int64_t* env
 int cugo_b200_step_compact(uint8_t* states, int64_t n_states, const int64_t* env_ids,
                            const int64_t* actions, int64_t m, int32_t* decision, float* reward0,
                            bool* nagari, int64_t* bad, int64_t* next_ids, int32_t* next_count,
-                           cudaStream_t stream) {
+                           int32_t* scratch, cudaStream_t stream) {
   if (n_states < 0 || m < 0) return CUGO_B200_ERR_ARG;
   if (m > 0 && (!env_ids || !actions || !decision || !reward0 || !nagari || !bad || !next_ids ||
-                !next_count))
+                !next_count || !scratch))
     return CUGO_B200_ERR_ARG;
   if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
-  if (!aligned(states, 8)) return CUGO_B200_ERR_ALIGN;
-  if (m == 0) return CUGO_B200_OK;
-  RoundTail tail{decision, reward0, nagari, bad, next_ids, next_count};
+  if (!aligned(states, 8) || !aligned(scratch, 4)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) {
+    cudaMemsetAsync(next_count, 0, sizeof(int32_t), stream);
+    return launch_status();
+  }
+  const i64 warps = (m + 31) / 32;
+  uint32_t* keep = reinterpret_cast<uint32_t*>(scratch);
+  int32_t* offsets = scratch + warps;
+  RoundTail tail{decision, reward0, nagari, bad, keep};
   step_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<u64*>(states), n_states, env_ids, actions, m, nullptr, nullptr, nullptr,
       nullptr, nullptr, nullptr, nullptr, tail);
+  compact_scan_kernel<<<1, 1024, 0, stream>>>(keep, warps, offsets, next_count);
+  compact_scatter_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, stream>>>(
+      keep, offsets, env_ids, m, next_ids);
   return launch_status();
 }
 

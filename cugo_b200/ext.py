@@ -59,7 +59,8 @@ _SIGNATURES: dict[str, list] = {
                                    _VP, _I64, _I32, _VP, _VP, _VP, _I64, _VP, _VP],
     "cugo_b200_pack_legal": [_VP, _I64, _VP, _VP],
     "cugo_b200_observe_indexed_bf16_bits": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
-    "cugo_b200_step_compact": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_step_compact": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
+                               _VP],
     "cugo_b200_rowdot_bf16": [_VP, _I64, _VP, _VP, _I64, _I64, _VP, _I64, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
@@ -404,20 +405,25 @@ class CugoB200Extension:
         return out
 
     def step_compact(self, states, env_ids, actions, decision, reward0, nagari, bad, next_ids,
-                     next_count) -> None:
+                     next_count, scratch: torch.Tensor | None = None) -> None:
         """step_indexed plus a self-play round's bookkeeping (see the C declaration):
         decision int32, reward0 fp32, nagari bool indexed by game id; bad int64 [1];
-        next_ids int64 [>= m] and next_count int32 [1] (zeroed by the caller) receive
-        the games still running."""
+        next_ids int64 [>= m] and next_count int32 [1] receive the games still running,
+        in order; scratch int32 [>= 2 * ceil(m / 32)] (allocated when not given)."""
         self._indexed_args(states, env_ids, actions)
         m = env_ids.numel()
         if next_ids.numel() < m or next_ids.dtype != torch.int64 or next_count.dtype != torch.int32:
             raise RuntimeError("step_compact: next_ids int64 [>= m], next_count int32 [1]")
+        need = 2 * ((m + 31) // 32)
+        if scratch is None:
+            scratch = torch.empty(max(need, 1), dtype=torch.int32, device=states.device)
+        if scratch.dtype != torch.int32 or scratch.numel() < need:
+            raise RuntimeError("step_compact: scratch int32 [>= 2 * ceil(m / 32)]")
         with torch.cuda.device(states.device):
             _check(self._lib.cugo_b200_step_compact(
                 _ptr(states), states.size(0), _ptr(env_ids), _ptr(actions), m, _ptr(decision),
                 _ptr(reward0), _ptr(nagari), _ptr(bad), _ptr(next_ids), _ptr(next_count),
-                self._stream(states.device)), "step_compact")
+                _ptr(scratch), self._stream(states.device)), "step_compact")
 
     def pack_legal(self, legal: torch.Tensor) -> torch.Tensor:
         """bool [m, 179] legal masks as int64 [m, 3] bit words."""

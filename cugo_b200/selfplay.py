@@ -67,6 +67,7 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     ids_buf = (torch.empty(g, dtype=torch.int64, device=device),
                torch.empty(g, dtype=torch.int64, device=device))
     count = torch.zeros(1, dtype=torch.int32, device=device)
+    scratch = torch.empty(2 * ((g + 31) // 32), dtype=torch.int32, device=device)
     decisions = 0
     rounds = 0
     n_launch = 1
@@ -85,8 +86,7 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
         if timer:
             timer.stop(t0, active.numel())
         nxt = ids_buf[rounds & 1]
-        count.zero_()
-        ext.step_compact(states, active, actions, decision, reward0, nagari, bad, nxt, count)
+        ext.step_compact(states, active, actions, decision, reward0, nagari, bad, nxt, count, scratch)
         n_launch += 2 + getattr(policy, "launches_per_step", lambda: 1)()
         decisions += active.numel()
         live = int(count.item())  # the round's one device->host read

@@ -91,13 +91,15 @@ CUGO_B200_API int cugo_b200_step_indexed(uint8_t* states, int64_t n_states, cons
  * loop, python/cugo_ppo50.py:321-450): for row i of game id = env_ids[i] (distinct
  * ids), decision[id] += 1; a game that finishes gets reward0[id] (player 0's reward)
  * and nagari[id]; each status other than OK (0) and "finished" (9) adds 1 to *bad;
- * the ids of the games still running are appended to next_ids, *next_count (which the
- * caller zeroes) their number.  The order of next_ids varies from run to run. */
+ * next_ids gets the ids of the games still running, in their env_ids order, and
+ * *next_count their number.  scratch: int32 [2 * ceil(m / 32)] of the caller's
+ * (per-warp masks and offsets); three launches, no allocation. */
 CUGO_B200_API int cugo_b200_step_compact(uint8_t* states, int64_t n_states,
                                          const int64_t* env_ids, const int64_t* actions,
                                          int64_t m, int32_t* decision, float* reward0,
                                          bool* nagari, int64_t* bad, int64_t* next_ids,
-                                         int32_t* next_count, cudaStream_t stream);
+                                         int32_t* next_count, int32_t* scratch,
+                                         cudaStream_t stream);
 
 /* step_events_indexed (torch50_ext.cu:626-660): step_indexed plus the committed
  * action's event record, int64 [m, 9] (zero when nothing was committed). */

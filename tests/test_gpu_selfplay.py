@@ -48,7 +48,7 @@ def test_step_compact_matches_step_indexed(ext):
     assert torch.equal(reward0, exp_r) and torch.equal(nag, exp_n)
     assert int(bad) == int(((status != 0) & (status != 9)).sum()) > 0
     live = int(count)
-    assert torch.equal(nxt[:live].sort().values, ids[~done].sort().values)
+    assert torch.equal(nxt[:live], ids[~done])  # in order
     assert bool(done.any()) and bool((status == 9).any())
 
 
