@@ -53,7 +53,12 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) observe_kernel(
     const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids, i64 m,
     F* __restrict__ features, i64 ld, int legal_cols, bool* __restrict__ legal,
     uint8_t* __restrict__ players, bool* __restrict__ done, int16_t* __restrict__ status,
-    int hand_plane = 0, u64* __restrict__ legal_bits = nullptr) {
+    int hand_plane = 0, u64* __restrict__ legal_bits = nullptr,
+    const int32_t* __restrict__ m_dev = nullptr) {
+  if (m_dev) {  // a device-resident row count (rows past it are left alone)
+    const i64 md = __ldg(m_dev);
+    m = md < 0 ? 0 : (md < m ? md : m);
+  }
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
@@ -112,8 +117,15 @@ struct RoundTail {
   float* reward0;
   bool* nagari;
   i64* bad;
-  uint32_t* keep;  // [ceil(m / 32)]
+  uint32_t* keep;        // [ceil(m / 32)]
+  const int32_t* m_dev;  // optional device-resident row count (at most m)
 };
+
+__device__ __forceinline__ i64 device_rows(const int32_t* m_dev, i64 m) {
+  if (!m_dev) return m;
+  const i64 md = __ldg(m_dev);
+  return md < 0 ? 0 : (md < m ? md : m);
+}
 
 __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
     u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids,
@@ -121,6 +133,7 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
     float* __restrict__ reward, bool* __restrict__ done, bool* __restrict__ nagari,
     int16_t* __restrict__ status, bool* __restrict__ committed, i64* __restrict__ events,
     RoundTail tail = RoundTail{}) {
+  m = device_rows(tail.m_dev, m);
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
@@ -176,9 +189,11 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
 // Exclusive prefix over the warps' running counts (one block): offsets[w], and
 // the total in *count.
 __global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __restrict__ keep,
-                                                            i64 warps, int32_t* __restrict__ offsets,
+                                                            i64 m, const int32_t* __restrict__ m_dev,
+                                                            int32_t* __restrict__ offsets,
                                                             int32_t* __restrict__ count) {
   __shared__ int32_t sums[32];
+  const i64 warps = (device_rows(m_dev, m) + 31) / 32;
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const i64 per = (warps + blockDim.x - 1) / blockDim.x;  // consecutive warps per thread
   const i64 w0 = t * per;
@@ -214,9 +229,10 @@ __global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __re
 __global__ void __launch_bounds__(256) compact_scatter_kernel(const uint32_t* __restrict__ keep,
                                                               const int32_t* __restrict__ offsets,
                                                               const i64* __restrict__ ids, i64 m,
+                                                              const int32_t* __restrict__ m_dev,
                                                               i64* __restrict__ next_ids) {
   const i64 row = (i64)blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= m) return;
+  if (row >= device_rows(m_dev, m)) return;
   const uint32_t mask = __ldg(keep + (row >> 5));
   const int lane = static_cast<int>(row & 31);
   if ((mask >> lane) & 1u)
@@ -340,7 +356,8 @@ int cugo_b200_observe_indexed_bf16(const uint8_t* states, int64_t n_states, cons
 int cugo_b200_observe_indexed_bf16_bits(const uint8_t* states, int64_t n_states,
                                         const int64_t* env_ids, int64_t m, void* features,
                                         uint64_t* legal_bits, uint8_t* players, bool* done,
-                                        int16_t* status, cudaStream_t stream) {
+                                        int16_t* status, const int32_t* m_dev,
+                                        cudaStream_t stream) {
   if (n_states < 0 || m < 0 || (m > 0 && !env_ids)) return CUGO_B200_ERR_ARG;
   if (m > 0 && (!features || !legal_bits || !players || !done || !status)) return CUGO_B200_ERR_ARG;
   if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
@@ -350,7 +367,7 @@ int cugo_b200_observe_indexed_bf16_bits(const uint8_t* states, int64_t n_states,
   observe_kernel<__nv_bfloat16><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<const u64*>(states), n_states, env_ids, m,
       static_cast<__nv_bfloat16*>(features), (i64)kFeatures, 0, nullptr, players, done, status, 0,
-      reinterpret_cast<u64*>(legal_bits));
+      reinterpret_cast<u64*>(legal_bits), m_dev);
   return launch_status();
 }
 
@@ -449,7 +466,7 @@ int cugo_b200_step_indexed(uint8_t* states, int64_t n_states, const int64_t* env
 int cugo_b200_step_compact(uint8_t* states, int64_t n_states, const int64_t* env_ids,
                            const int64_t* actions, int64_t m, int32_t* decision, float* reward0,
                            bool* nagari, int64_t* bad, int64_t* next_ids, int32_t* next_count,
-                           int32_t* scratch, cudaStream_t stream) {
+                           int32_t* scratch, const int32_t* m_dev, cudaStream_t stream) {
   if (n_states < 0 || m < 0) return CUGO_B200_ERR_ARG;
   if (m > 0 && (!env_ids || !actions || !decision || !reward0 || !nagari || !bad || !next_ids ||
                 !next_count || !scratch))
@@ -460,16 +477,17 @@ int cugo_b200_step_compact(uint8_t* states, int64_t n_states, const int64_t* env
     cudaMemsetAsync(next_count, 0, sizeof(int32_t), stream);
     return launch_status();
   }
-  const i64 warps = (m + 31) / 32;
+  const i64 warps = (m + 31) / 32;  // capacity; the kernels use the device count
   uint32_t* keep = reinterpret_cast<uint32_t*>(scratch);
   int32_t* offsets = scratch + warps;
-  RoundTail tail{decision, reward0, nagari, bad, keep};
+  if (m_dev == next_count) return CUGO_B200_ERR_ARG;  // the count is rewritten mid-call
+  RoundTail tail{decision, reward0, nagari, bad, keep, m_dev};
   step_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<u64*>(states), n_states, env_ids, actions, m, nullptr, nullptr, nullptr,
       nullptr, nullptr, nullptr, nullptr, tail);
-  compact_scan_kernel<<<1, 1024, 0, stream>>>(keep, warps, offsets, next_count);
+  compact_scan_kernel<<<1, 1024, 0, stream>>>(keep, m, m_dev, offsets, next_count);
   compact_scatter_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, stream>>>(
-      keep, offsets, env_ids, m, next_ids);
+      keep, offsets, env_ids, m, m_dev, next_ids);
   return launch_status();
 }
 

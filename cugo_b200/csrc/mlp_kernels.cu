@@ -1197,6 +1197,7 @@ struct FusedArgs {
   int greedy;
   int64_t* actions;                 // [m]
   float* logp;                      // [m]
+  const int32_t* m_dev;             // optional device-resident row count (at most m)
 };
 
 constexpr int F_ACTIONS = 179;
@@ -1333,7 +1334,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   const int pair = static_cast<int>(blockIdx.x >> 1), pairs = static_cast<int>(gridDim.x >> 1);
-  const int tiles = (args.m + 2 * BM - 1) / (2 * BM);
+  int m_rows = args.m;
+  if (args.m_dev) {
+    const int md = __ldg(args.m_dev);
+    m_rows = md < 0 ? 0 : (md < m_rows ? md : m_rows);
+  }
+  const int tiles = (m_rows + 2 * BM - 1) / (2 * BM);
   const int kc0 = (args.k_in + BK - 1) / BK;
   const int hidden_layers = 2 * args.blocks;
   const int head_rows = args.n_mma / 2;  // head weight rows per CTA
@@ -1585,7 +1591,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
       const float* bo = args.bias[hidden_layers + 1];
       const int64_t row_g = static_cast<int64_t>(row0) + r;
       const bool sampling = args.actions != nullptr;
-      const bool live = sampling && row_g < args.m;
+      const bool live = sampling && row_g < m_rows;
       const uint64_t gid = live ? static_cast<uint64_t>(__ldg(args.game + row_g)) : 0;
       const uint32_t dec = live ? static_cast<uint32_t>(__ldg(args.decision + row_g)) : 0;
       SampleState st{-INFINITY, -1, 0.0f, -INFINITY, 0.0f};
@@ -1713,7 +1719,7 @@ int fused_launch(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t bl
                  const void* const* weights, const float* const* biases, int64_t n_out,
                  int32_t act, float* out, int64_t ldo, const uint64_t* legal, const int64_t* game,
                  const int32_t* decision, int64_t seed_base, int32_t greedy, int64_t* actions,
-                 float* logp, int32_t* error, cudaStream_t stream) {
+                 float* logp, const int32_t* m_dev, int32_t* error, cudaStream_t stream) {
   if (m < 0 || k_in <= 0 || k_in > F_MAX_KIN || blocks < 0 || blocks > F_MAX_BLOCKS ||
       n_out <= 0 || n_out > BN || !weights || act < 0 || act > 2)
     return CUGO_B200_ERR_ARG;
@@ -1760,6 +1766,7 @@ int fused_launch(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t bl
   args.greedy = greedy;
   args.actions = actions;
   args.logp = logp;
+  args.m_dev = m_dev;
   for (int l = 0; l < layers; ++l) args.bias[l] = biases ? biases[l] : nullptr;
   args.blocks = blocks;
   args.m = static_cast<int>(m);
@@ -1810,7 +1817,7 @@ int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int
                         int32_t act, float* out, int64_t ldo, int32_t* error, cudaStream_t stream) {
   if (m > 0 && !out) return CUGO_B200_ERR_ARG;
   return fused_launch(x, ldx, m, k_in, blocks, weights, biases, n_out, act, out, ldo, nullptr,
-                      nullptr, nullptr, 0, 0, nullptr, nullptr, error, stream);
+                      nullptr, nullptr, 0, 0, nullptr, nullptr, nullptr, error, stream);
 }
 
 int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
@@ -1819,11 +1826,11 @@ int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t m, int64_t k_
                                const int64_t* game,
                                const int32_t* decision, int64_t seed_base, int32_t greedy,
                                int64_t* actions, float* logp, float* out, int64_t ldo,
-                               int32_t* error, cudaStream_t stream) {
+                               const int32_t* m_dev, int32_t* error, cudaStream_t stream) {
   if (m > 0 && (!actions || !logp)) return CUGO_B200_ERR_ARG;
   if (m > 0 && (reinterpret_cast<uintptr_t>(legal_bits) & 7u)) return CUGO_B200_ERR_ALIGN;
   return fused_launch(x, ldx, m, k_in, blocks, weights, biases, n_out, act, out, ldo, legal_bits,
-                      game, decision, seed_base, greedy, actions, logp, error, stream);
+                      game, decision, seed_base, greedy, actions, logp, m_dev, error, stream);
 }
 
 }  // extern "C"

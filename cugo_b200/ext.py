@@ -56,11 +56,12 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_mlp_fused": [_VP, _I64, _I64, _I64, _I32, _VP, _VP, _I64, _I32, _VP, _I64, _VP,
                             _VP],
     "cugo_b200_mlp_fused_sample": [_VP, _I64, _I64, _I64, _I32, _VP, _VP, _I64, _I32, _VP, _VP,
-                                   _VP, _I64, _I32, _VP, _VP, _VP, _I64, _VP, _VP],
+                                   _VP, _I64, _I32, _VP, _VP, _VP, _I64, _VP, _VP, _VP],
     "cugo_b200_pack_legal": [_VP, _I64, _VP, _VP],
-    "cugo_b200_observe_indexed_bf16_bits": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
+    "cugo_b200_observe_indexed_bf16_bits": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP,
+                                            _VP],
     "cugo_b200_step_compact": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
-                               _VP],
+                               _VP, _VP],
     "cugo_b200_rowdot_bf16": [_VP, _I64, _VP, _VP, _I64, _I64, _VP, _I64, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
@@ -386,7 +387,8 @@ class CugoB200Extension:
                 self._stream(states.device)), "observe_indexed_bf16")
         return out
 
-    def observe_indexed_bf16_bits(self, states, env_ids) -> list[torch.Tensor]:
+    def observe_indexed_bf16_bits(self, states, env_ids,
+                                  m_dev: torch.Tensor | None = None) -> list[torch.Tensor]:
         """observe_indexed_bf16 with the legal mask as int64 [m, 3] bit words (bit a of
         word a / 64) in place of the bool mask: [features, legal_bits, players, done,
         status]."""
@@ -400,12 +402,13 @@ class CugoB200Extension:
             out[0] = torch.empty((m, self.FEATURE_COUNT), dtype=torch.bfloat16, device=dev)
             out[1] = torch.empty((m, 3), dtype=torch.int64, device=dev)
             _check(self._lib.cugo_b200_observe_indexed_bf16_bits(
-                _ptr(states), states.size(0), _ptr(env_ids), m, *map(_ptr, out),
+                _ptr(states), states.size(0), _ptr(env_ids), m, *map(_ptr, out), _ptr(m_dev),
                 self._stream(dev)), "observe_indexed_bf16_bits")
         return out
 
     def step_compact(self, states, env_ids, actions, decision, reward0, nagari, bad, next_ids,
-                     next_count, scratch: torch.Tensor | None = None) -> None:
+                     next_count, scratch: torch.Tensor | None = None,
+                     m_dev: torch.Tensor | None = None) -> None:
         """step_indexed plus a self-play round's bookkeeping (see the C declaration):
         decision int32, reward0 fp32, nagari bool indexed by game id; bad int64 [1];
         next_ids int64 [>= m] and next_count int32 [1] receive the games still running,
@@ -423,7 +426,7 @@ class CugoB200Extension:
             _check(self._lib.cugo_b200_step_compact(
                 _ptr(states), states.size(0), _ptr(env_ids), _ptr(actions), m, _ptr(decision),
                 _ptr(reward0), _ptr(nagari), _ptr(bad), _ptr(next_ids), _ptr(next_count),
-                _ptr(scratch), self._stream(states.device)), "step_compact")
+                _ptr(scratch), _ptr(m_dev), self._stream(states.device)), "step_compact")
 
     def pack_legal(self, legal: torch.Tensor) -> torch.Tensor:
         """bool [m, 179] legal masks as int64 [m, 3] bit words."""
@@ -608,7 +611,8 @@ class CugoB200Extension:
     def mlp_fused_sample(self, x: torch.Tensor, weights: list[torch.Tensor],
                          biases: list[torch.Tensor | None], act: int, legal: torch.Tensor,
                          game: torch.Tensor, decision: torch.Tensor, seed_base: int = 12345,
-                         greedy: bool = False, want_logits: bool = False):
+                         greedy: bool = False, want_logits: bool = False,
+                         m_dev: torch.Tensor | None = None):
         """The hidden-512 MLP and the masked Gumbel-max sampling of its first 179
         outputs in one kernel: (actions int64 [m], logp fp32 [m], logits or None).
         legal: bool [m, 179], or the int64 [m, 3] bit words of observe_indexed_bf16_bits."""
@@ -637,7 +641,7 @@ class CugoB200Extension:
             _check(self._lib.cugo_b200_mlp_fused_sample(
                 _ptr(x), x.stride(0), m, k_in, (len(weights) - 2) // 2, wp, bp, n_out, act,
                 _ptr(legal), _ptr(game), _ptr(decision), seed_base, int(greedy), _ptr(actions),
-                _ptr(logp), _ptr(out), out.stride(0) if out is not None else 0, None,
+                _ptr(logp), _ptr(out), out.stride(0) if out is not None else 0, _ptr(m_dev), None,
                 self._stream(dev)), "mlp_fused_sample")
         return actions, logp, out
 

@@ -50,11 +50,20 @@ class RoundTimer:
         return ms, len(self.pairs), sum(r for _, _, r in self.pairs)
 
 
+CHECK_EVERY = 4  # rounds between host reads of the running count (device-count loop)
+
+
 def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
                max_rounds: int = 128, timer: RoundTimer | None = None,
                launches: list[int] | None = None) -> BatchResult:
     """Plays games `game_index` (seed = seed_base + index, first player index & 1) to
-    the end with policy-sampled actions."""
+    the end with policy-sampled actions.
+
+    With a fused policy step (policy.samples_in_kernel()) the rounds run without host
+    round trips: each round's kernels read the running count that the previous
+    round's step left in device memory (buffers keep the batch's full size), and the
+    host reads the count every CHECK_EVERY rounds.  Otherwise the host reads the
+    count after every round and sizes the next round's launches by it."""
     device = game_index.device
     g = game_index.numel()
     states = ext.create(game_index + seed_base, game_index & 1)
@@ -62,39 +71,52 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     reward0 = torch.zeros(g, dtype=torch.float32, device=device)
     nagari = torch.zeros(g, dtype=torch.bool, device=device)
     bad = torch.zeros(1, dtype=torch.int64, device=device)
-    active = torch.arange(g, device=device)
-    # The games still running after a round, written by the step kernel (ping-pong).
-    ids_buf = (torch.empty(g, dtype=torch.int64, device=device),
-               torch.empty(g, dtype=torch.int64, device=device))
-    count = torch.zeros(1, dtype=torch.int32, device=device)
+    # The running games' positions, written by the step kernel (ping-pong), their counts.
+    # Entries past the count stay valid positions (they are gathered, not used).
+    ids_buf = (torch.arange(g, device=device), torch.zeros(g, dtype=torch.int64, device=device))
+    counts = torch.tensor([g, 0], dtype=torch.int32, device=device)
     scratch = torch.empty(2 * ((g + 31) // 32), dtype=torch.int32, device=device)
-    decisions = 0
-    rounds = 0
-    n_launch = 1
     fused = getattr(policy, "samples_in_kernel", lambda: False)()
-    # A fused policy step reads the legal mask as bit words.
-    observe = ext.observe_indexed_bf16_bits if fused else ext.observe_indexed_bf16
+    # The policy timer needs each round's row count: it reads the count every round.
+    sync_each = not fused or timer is not None
+    per_round = 2 + getattr(policy, "launches_per_step", lambda: 1)()
+    n_launch = 1
+    rounds = 0
+    live = g
     for rounds in range(1, max_rounds + 1):
-        features, legal, _players, _done, _status = observe(states, active)
-        game_ids = game_index.index_select(0, active)
-        dec = decision.index_select(0, active)
-        t0 = timer.start() if timer else None
-        if hasattr(policy, "forward_sample"):  # policy and sampling in one launch where fused
-            actions, _logp = policy.forward_sample(features, legal, game_ids, dec, seed_base)
+        k = (rounds - 1) & 1
+        active, nxt = ids_buf[k], ids_buf[1 - k]
+        c_in, c_out = counts[k:k + 1], counts[1 - k:2 - k]
+        if not fused:
+            active = active[:live]
+        if fused:  # observe with bit-word masks, one policy kernel, step: no host reads
+            features, legal, _p, _d, _s = ext.observe_indexed_bf16_bits(states, active, m_dev=c_in)
+            game_ids, dec = game_index.index_select(0, active), decision.index_select(0, active)
+            t0 = timer.start() if timer else None
+            actions, _logp = policy.forward_sample(features, legal, game_ids, dec, seed_base,
+                                                   m_dev=c_in)
         else:
-            actions, _logp = ext.sample_actions(policy(features), legal, game_ids, dec, seed_base)
+            features, legal, _p, _d, _s = ext.observe_indexed_bf16(states, active)
+            game_ids, dec = game_index.index_select(0, active), decision.index_select(0, active)
+            t0 = timer.start() if timer else None
+            if hasattr(policy, "forward_sample"):
+                actions, _logp = policy.forward_sample(features, legal, game_ids, dec, seed_base)
+            else:
+                actions, _logp = ext.sample_actions(policy(features), legal, game_ids, dec,
+                                                    seed_base)
         if timer:
-            timer.stop(t0, active.numel())
-        nxt = ids_buf[rounds & 1]
-        ext.step_compact(states, active, actions, decision, reward0, nagari, bad, nxt, count, scratch)
-        n_launch += 2 + getattr(policy, "launches_per_step", lambda: 1)()
-        decisions += active.numel()
-        live = int(count.item())  # the round's one device->host read
-        if live == 0:
-            break
-        active = nxt[:live]
+            timer.stop(t0, live)
+        ext.step_compact(states, active, actions, decision, reward0, nagari, bad, nxt, c_out,
+                         scratch, m_dev=c_in if fused else None)
+        n_launch += per_round
+        if sync_each or rounds % CHECK_EVERY == 0:
+            live = int(c_out.item())
+            if live == 0:
+                break
     else:
         raise RuntimeError(f"games did not finish within {max_rounds} rounds")
     if launches is not None:
         launches.append(n_launch)
-    return BatchResult(g, decisions, rounds, int(bad), reward0, nagari)
+    decisions = int(decision.sum())
+    played = int(decision.max()) if g else 0  # every live game decides once per round
+    return BatchResult(g, decisions, played, int(bad), reward0, nagari)

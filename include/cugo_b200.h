@@ -93,13 +93,15 @@ CUGO_B200_API int cugo_b200_step_indexed(uint8_t* states, int64_t n_states, cons
  * and nagari[id]; each status other than OK (0) and "finished" (9) adds 1 to *bad;
  * next_ids gets the ids of the games still running, in their env_ids order, and
  * *next_count their number.  scratch: int32 [2 * ceil(m / 32)] of the caller's
- * (per-warp masks and offsets); three launches, no allocation. */
+ * (per-warp masks and offsets); three launches, no allocation.  m_dev (optional, not
+ * next_count): a device-resident int32 row count; only rows below min(m, *m_dev)
+ * are stepped. */
 CUGO_B200_API int cugo_b200_step_compact(uint8_t* states, int64_t n_states,
                                          const int64_t* env_ids, const int64_t* actions,
                                          int64_t m, int32_t* decision, float* reward0,
                                          bool* nagari, int64_t* bad, int64_t* next_ids,
                                          int32_t* next_count, int32_t* scratch,
-                                         cudaStream_t stream);
+                                         const int32_t* m_dev, cudaStream_t stream);
 
 /* step_events_indexed (torch50_ext.cu:626-660): step_indexed plus the committed
  * action's event record, int64 [m, 9] (zero when nothing was committed). */
@@ -265,7 +267,10 @@ CUGO_B200_API int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int
  * action).  legal_bits uint64 [m, 3] (bit a of word a / 64: what
  * cugo_b200_observe_indexed_bf16_bits writes, or cugo_b200_pack_legal makes from a
  * bool mask), game int64 [m], decision int32 [m], actions int64 [m], logp fp32 [m];
- * n_out >= 179; out (fp32 [m, ldo]) may be NULL when the logits are not needed. */
+ * n_out >= 179; out (fp32 [m, ldo]) may be NULL when the logits are not needed.
+ * m_dev (optional): a device-resident int32 row count, read when the kernel starts;
+ * only rows below min(m, *m_dev) are computed (a loop can launch without reading the
+ * count back).  No counterpart in the reference. */
 CUGO_B200_API int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t m,
                                              int64_t k_in, int32_t blocks,
                                              const void* const* weights,
@@ -274,7 +279,8 @@ CUGO_B200_API int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t
                                              const int64_t* game, const int32_t* decision,
                                              int64_t seed_base, int32_t greedy, int64_t* actions,
                                              float* logp, float* out, int64_t ldo,
-                                             int32_t* error, cudaStream_t stream);
+                                             const int32_t* m_dev, int32_t* error,
+                                             cudaStream_t stream);
 
 /* Packs bool legal masks [m, 179] into uint64 [m, 3] (bit a of word a / 64). */
 CUGO_B200_API int cugo_b200_pack_legal(const bool* legal, int64_t m, uint64_t* bits,
@@ -307,12 +313,15 @@ CUGO_B200_API int cugo_b200_policy_forward_noalloc(const void* x, int64_t ldx, i
                                                    cudaStream_t stream);
 
 /* observe_indexed_bf16 with the legal mask written as bits, uint64 [m, 3] (bit a of
- * word a / 64), for the fused MLP's sampling head; no bool mask is written. */
+ * word a / 64), for the fused MLP's sampling head; no bool mask is written.  m_dev
+ * (optional): a device-resident int32 row count; rows from min(m, *m_dev) on are left
+ * alone. */
 CUGO_B200_API int cugo_b200_observe_indexed_bf16_bits(const uint8_t* states, int64_t n_states,
                                                       const int64_t* env_ids, int64_t m,
                                                       void* features_bf16, uint64_t* legal_bits,
                                                       uint8_t* players, bool* done,
-                                                      int16_t* status, cudaStream_t stream);
+                                                      int16_t* status, const int32_t* m_dev,
+                                                      cudaStream_t stream);
 
 /* observe_indexed with the features written as bf16 [m, 720] (16-byte aligned):
  * the policy's input layer reads them directly.  Same values as observe_indexed

@@ -92,3 +92,18 @@ def test_play_batch_matches_the_separate_ops_loop(ext, activation):
     # The reference loop's forward runs the same fused kernel, so its logits, and with
     # them every sampled action, are identical.
     assert torch.equal(res.nagari, nag) and torch.equal(res.reward0, r0)
+
+
+def test_device_count_loop_equals_the_synchronised_loop(ext):
+    """The same batch with the running count read back every round (the timer's path)
+    and every CHECK_EVERY rounds (kernels reading the count from device memory)."""
+    from cugo_b200.policy import ResidualMlpPolicy
+    from cugo_b200.selfplay import RoundTimer, play_batch
+    pol = ResidualMlpPolicy(512, 3, "relu", device=DEV, seed=6)
+    games = torch.arange(7000, device=DEV)
+    timer = RoundTimer(enabled=True)
+    a = play_batch(ext, pol, games, timer=timer)
+    b = play_batch(ext, pol, games)
+    assert (a.decisions, a.rounds, a.bad_status) == (b.decisions, b.rounds, b.bad_status)
+    assert torch.equal(a.reward0, b.reward0) and torch.equal(a.nagari, b.nagari)
+    assert timer.total_ms()[2] == a.decisions  # the timer saw every round's rows
