@@ -24,6 +24,9 @@ FLOPs of one launch:
                        events and Q decisions (4-layer d256 policy): native forward_games
                        and the reference's formulation in PyTorch (bf16 autocast, SDPA
                        with the boolean mask), each timed with CUDA events
+  ppoiter   GAMES [H B] one train_ppo50.py iteration at its defaults (3x512 SiLU actor and
+                       critic, 2 epochs of 32,768-row minibatches, GAE 0.95): collection
+                       with recorded transitions and the update, seconds each
   evaluate  PAIRS      paired evaluation of two 3x512 SiLU actors (2 x PAIRS games to the
                        end): the fused evaluator (one CUDA graph per decision step) and
                        the reference's host-compacting loop over the same ops and networks
@@ -280,6 +283,28 @@ def seqgames_case(s_n: int, length: int, q_n: int, warmup: int = 3, iters: int =
                 torch_autocast_seconds=sec_torch, torch_autocast_decisions_per_s=s_n * q_n / sec_torch)
 
 
+def ppoiter_case(games: int, hidden: int = 512, blocks: int = 3, warmup: int = 1,
+                 iters: int = 2) -> dict:
+    """One PPO iteration (python/train_ppo50.py defaults; hidden/blocks of both
+    networks) on the native kernels."""
+    from .ppo import fused_actor, fused_critic
+    from .train import PpoTrainer, RolloutStorage, iteration
+    ext = load_extension()
+    dev = torch.device("cuda")
+    torch.manual_seed(0)
+    actor, critic = fused_actor(hidden, blocks).to(dev), fused_critic(hidden, blocks).to(dev)
+    trainer = PpoTrainer(actor, critic)
+    storage = RolloutStorage(games * 24, dev)
+    for i in range(warmup):
+        iteration(ext, trainer, storage, games, 1000 + i)
+    runs = [iteration(ext, trainer, storage, games, 2000 + i) for i in range(iters)]
+    best = min(runs, key=lambda r: r["seconds"])
+    st = best.pop("stats")
+    best.update(updates=st.updates, rows_per_s=best["rows"] / best["seconds"],
+                games_per_s_collect=games / best["collect_seconds"])
+    return best
+
+
 def evaluate_case(pairs: int, warmup: int = 1, iters: int = 3) -> dict:
     """evaluate_paired (python/cugo_eval50.py:137-361): games/s of the fused evaluator
     and of the reference's loop structure (compaction and per-policy index copies every
@@ -496,6 +521,9 @@ def main() -> None:
     elif args.case == "seqgames":
         s_n, length, q_n = d
         out.update(seqgames_case(s_n, length, q_n, args.warmup, args.iters))
+    elif args.case == "ppoiter":
+        games, hidden, blocks = (list(d) + [512, 3])[:3] if len(d) < 3 else d
+        out.update(ppoiter_case(games, hidden, blocks, args.warmup, args.iters))
     elif args.case == "evaluate":
         (p,) = d
         out.update(evaluate_case(p, args.warmup, args.iters))

@@ -303,6 +303,7 @@ class PpoStep:
         dev = next(actor.parameters()).device
         self.entropy_coef = torch.zeros((), device=dev)
         self.sums = torch.zeros(6, device=dev)
+        self.last_kl = torch.zeros((), device=dev)  # the latest minibatch's KL estimate
 
     def losses(self, mb: Minibatch):
         logits = self.actor(mb.features).float()
@@ -329,6 +330,7 @@ class PpoStep:
         self.optimizer.step()
         with torch.no_grad():
             kl = ((ratio - 1) - log_ratio).mean()
+            self.last_kl.copy_(kl)
             self.sums += torch.stack((policy_loss.detach(), value_loss.detach(), entropy.detach(), kl,
                                       ((ratio - 1).abs() > self.clip).float().mean(),
                                       torch.ones_like(kl)))
