@@ -437,6 +437,10 @@ def main():
         from cugo_b200.kernel_cases import ppo_case
         extras["ppo_update"] = {"minibatch": 32768, "networks": "3x512 actor + critic (SiLU)",
                                 **ppo_case(32768, warmup=3, iters=10)}
+        from cugo_b200.kernel_cases import ppoiter_case
+        extras["ppo_iteration"] = {"games": 65536, "networks": "3x512 actor + critic (SiLU)",
+                                   "epochs": 2, "minibatch": 32768,
+                                   **ppoiter_case(65536, 512, 3, warmup=1, iters=1)}
         from cugo_b200.kernel_cases import allaction_case
         extras["all_action_q"] = {"critic": "3x512 OracleCritic layout (SiLU), every legal action",
                                   **allaction_case(16384, warmup=3, iters=10)}
