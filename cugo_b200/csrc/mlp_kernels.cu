@@ -1191,8 +1191,10 @@ struct FusedArgs {
   // Sampling head (actions != null): masked Gumbel-max over the first 179 outputs,
   // with the noise and tie rules of cugo_b200_sample_actions.
   const uint64_t* legal_bits;       // [m, 3]: bit a of word a / 64
-  const int64_t* game;              // [m]
-  const int32_t* decision;          // [m]
+  const int64_t* game;              // [m], or [n_games] read through rows
+  const int32_t* decision;          // [m], or [n_games] read through rows
+  const int64_t* rows;              // optional [m]: row r's entry of game and decision
+  int64_t n_games;
   int64_t seed_base;
   int greedy;
   int64_t* actions;                 // [m]
@@ -1592,11 +1594,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
       const int64_t row_g = static_cast<int64_t>(row0) + r;
       const bool sampling = args.actions != nullptr;
       const bool live = sampling && row_g < m_rows;
-      const uint64_t gid = live ? static_cast<uint64_t>(__ldg(args.game + row_g)) : 0;
-      const uint32_t dec = live ? static_cast<uint32_t>(__ldg(args.decision + row_g)) : 0;
+      // The row's game: its own entry, or entry rows[row] (one outside the arrays is a
+      // row without legal actions).
+      int64_t gi = row_g;
+      bool known = live;
+      if (live && args.rows) {
+        gi = __ldg(args.rows + row_g);
+        known = gi >= 0 && gi < args.n_games;
+      }
+      const uint64_t gid = known ? static_cast<uint64_t>(__ldg(args.game + gi)) : 0;
+      const uint32_t dec = known ? static_cast<uint32_t>(__ldg(args.decision + gi)) : 0;
       SampleState st{-INFINITY, -1, 0.0f, -INFINITY, 0.0f};
       uint64_t lw[3] = {0ull, 0ull, 0ull};
-      if (live) {
+      if (known) {
         const uint64_t* p = args.legal_bits + row_g * 3;
         lw[0] = __ldg(p);
         lw[1] = __ldg(p + 1);
@@ -1718,8 +1728,9 @@ namespace {
 int fused_launch(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
                  const void* const* weights, const float* const* biases, int64_t n_out,
                  int32_t act, float* out, int64_t ldo, const uint64_t* legal, const int64_t* game,
-                 const int32_t* decision, int64_t seed_base, int32_t greedy, int64_t* actions,
-                 float* logp, const int32_t* m_dev, int32_t* error, cudaStream_t stream) {
+                 const int32_t* decision, const int64_t* rows, int64_t n_games, int64_t seed_base,
+                 int32_t greedy, int64_t* actions, float* logp, const int32_t* m_dev,
+                 int32_t* error, cudaStream_t stream) {
   if (m < 0 || k_in <= 0 || k_in > F_MAX_KIN || blocks < 0 || blocks > F_MAX_BLOCKS ||
       n_out <= 0 || n_out > BN || !weights || act < 0 || act > 2)
     return CUGO_B200_ERR_ARG;
@@ -1727,6 +1738,7 @@ int fused_launch(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t bl
   if (m > INT32_MAX || !x || (!out && !actions) || ldx < k_in || (out && ldo < n_out))
     return CUGO_B200_ERR_ARG;
   if (actions && (!logp || !legal || !game || !decision || n_out < F_ACTIONS)) return CUGO_B200_ERR_ARG;
+  if (rows && (!actions || n_games < 0)) return CUGO_B200_ERR_ARG;
   const int layers = 2 + 2 * blocks;
   for (int l = 0; l < layers; ++l)
     if (!weights[l]) return CUGO_B200_ERR_ARG;
@@ -1762,6 +1774,8 @@ int fused_launch(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t bl
   args.legal_bits = legal;
   args.game = game;
   args.decision = decision;
+  args.rows = rows;
+  args.n_games = n_games;
   args.seed_base = seed_base;
   args.greedy = greedy;
   args.actions = actions;
@@ -1817,20 +1831,22 @@ int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int64_t k_in, int
                         int32_t act, float* out, int64_t ldo, int32_t* error, cudaStream_t stream) {
   if (m > 0 && !out) return CUGO_B200_ERR_ARG;
   return fused_launch(x, ldx, m, k_in, blocks, weights, biases, n_out, act, out, ldo, nullptr,
-                      nullptr, nullptr, 0, 0, nullptr, nullptr, nullptr, error, stream);
+                      nullptr, nullptr, nullptr, 0, 0, 0, nullptr, nullptr, nullptr, error, stream);
 }
 
 int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
                                const void* const* weights, const float* const* biases,
                                int64_t n_out, int32_t act, const uint64_t* legal_bits,
-                               const int64_t* game,
-                               const int32_t* decision, int64_t seed_base, int32_t greedy,
-                               int64_t* actions, float* logp, float* out, int64_t ldo,
-                               const int32_t* m_dev, int32_t* error, cudaStream_t stream) {
+                               const int64_t* game, const int32_t* decision,
+                               const int64_t* rows, int64_t n_games, int64_t seed_base,
+                               int32_t greedy, int64_t* actions, float* logp, float* out,
+                               int64_t ldo, const int32_t* m_dev, int32_t* error,
+                               cudaStream_t stream) {
   if (m > 0 && (!actions || !logp)) return CUGO_B200_ERR_ARG;
   if (m > 0 && (reinterpret_cast<uintptr_t>(legal_bits) & 7u)) return CUGO_B200_ERR_ALIGN;
   return fused_launch(x, ldx, m, k_in, blocks, weights, biases, n_out, act, out, ldo, legal_bits,
-                      game, decision, seed_base, greedy, actions, logp, m_dev, error, stream);
+                      game, decision, rows, n_games, seed_base, greedy, actions, logp, m_dev,
+                      error, stream);
 }
 
 }  // extern "C"

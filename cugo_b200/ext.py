@@ -56,7 +56,8 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_mlp_fused": [_VP, _I64, _I64, _I64, _I32, _VP, _VP, _I64, _I32, _VP, _I64, _VP,
                             _VP],
     "cugo_b200_mlp_fused_sample": [_VP, _I64, _I64, _I64, _I32, _VP, _VP, _I64, _I32, _VP, _VP,
-                                   _VP, _I64, _I32, _VP, _VP, _VP, _I64, _VP, _VP, _VP],
+                                   _VP, _VP, _I64, _I64, _I32, _VP, _VP, _VP, _I64, _VP, _VP,
+                                   _VP],
     "cugo_b200_pack_legal": [_VP, _I64, _VP, _VP],
     "cugo_b200_observe_indexed_bf16_bits": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP,
                                             _VP],
@@ -612,10 +613,12 @@ class CugoB200Extension:
                          biases: list[torch.Tensor | None], act: int, legal: torch.Tensor,
                          game: torch.Tensor, decision: torch.Tensor, seed_base: int = 12345,
                          greedy: bool = False, want_logits: bool = False,
-                         m_dev: torch.Tensor | None = None):
+                         m_dev: torch.Tensor | None = None, rows: torch.Tensor | None = None):
         """The hidden-512 MLP and the masked Gumbel-max sampling of its first 179
         outputs in one kernel: (actions int64 [m], logp fp32 [m], logits or None).
-        legal: bool [m, 179], or the int64 [m, 3] bit words of observe_indexed_bf16_bits."""
+        legal: bool [m, 179], or the int64 [m, 3] bit words of observe_indexed_bf16_bits.
+        rows (optional int64 [m]): row r's game and decision are game[rows[r]] and
+        decision[rows[r]] (an entry outside the arrays samples nothing: -1, log p 0)."""
         m, k_in = x.shape
         if x.dtype != torch.bfloat16 or x.stride(1) != 1:
             raise RuntimeError("mlp_fused_sample expects row-major bf16 x")
@@ -629,6 +632,12 @@ class CugoB200Extension:
             raise RuntimeError("legal must be a bool [m, 179] mask or its int64 [m, 3] bit words")
         _check_cuda_1d(game, torch.int64, "game")
         _check_cuda_1d(decision, torch.int32, "decision")
+        if rows is not None:
+            _check_cuda_1d(rows, torch.int64, "rows")
+            if rows.numel() != m or game.numel() != decision.numel():
+                raise RuntimeError("rows needs one entry per row and game, decision of one length")
+        elif game.numel() != m or decision.numel() != m:
+            raise RuntimeError("game and decision need one entry per row")
         n_out = weights[-1].shape[0]
         dev = x.device
         actions = torch.empty((m,), dtype=torch.int64, device=dev)
@@ -640,7 +649,8 @@ class CugoB200Extension:
         with torch.cuda.device(dev):
             _check(self._lib.cugo_b200_mlp_fused_sample(
                 _ptr(x), x.stride(0), m, k_in, (len(weights) - 2) // 2, wp, bp, n_out, act,
-                _ptr(legal), _ptr(game), _ptr(decision), seed_base, int(greedy), _ptr(actions),
+                _ptr(legal), _ptr(game), _ptr(decision), _ptr(rows), game.numel(), seed_base,
+                int(greedy), _ptr(actions),
                 _ptr(logp), _ptr(out), out.stride(0) if out is not None else 0, _ptr(m_dev), None,
                 self._stream(dev)), "mlp_fused_sample")
         return actions, logp, out

@@ -136,20 +136,23 @@ class ResidualMlpPolicy:
     @torch.no_grad()
     def forward_sample(self, features: torch.Tensor, legal: torch.Tensor, game: torch.Tensor,
                        decision: torch.Tensor, seed_base: int = 12345, greedy: bool = False,
-                       m_dev: torch.Tensor | None = None):
+                       m_dev: torch.Tensor | None = None, rows: torch.Tensor | None = None):
         """Actions and log-probabilities of the masked Gumbel-max sampler over this
         policy's logits (cugo_b200_sample_actions' definition): in the fused MLP's
         head when it runs this shape, else the forward followed by the sampler.
         legal: bool [m, 179], or (fused head only) its int64 [m, 3] bit words; m_dev
-        (fused head only): a device-resident row count, rows past it are skipped."""
+        (fused head only): a device-resident row count, rows past it are skipped; rows:
+        row r's game and decision are game[rows[r]], decision[rows[r]]."""
         ext = self._extension()
         x = features if features.dtype == torch.bfloat16 else features.to(torch.bfloat16)
         x = x.contiguous()
         if self.samples_in_kernel():
             actions, logp, _ = ext.mlp_fused_sample(x, self.weights, self._fp32_biases(),
                                                     _ACT[self.activation], legal, game, decision,
-                                                    seed_base, greedy, m_dev=m_dev)
+                                                    seed_base, greedy, m_dev=m_dev, rows=rows)
             return actions, logp
         if m_dev is not None:
             raise RuntimeError("a device-resident row count needs the fused policy step")
+        if rows is not None:
+            game, decision = game.index_select(0, rows), decision.index_select(0, rows)
         return ext.sample_actions(self.forward(x), legal, game, decision, seed_base, greedy=greedy)

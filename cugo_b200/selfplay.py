@@ -79,7 +79,8 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     fused = getattr(policy, "samples_in_kernel", lambda: False)()
     # The policy timer needs each round's row count: it reads the count every round.
     sync_each = not fused or timer is not None
-    per_round = 2 + getattr(policy, "launches_per_step", lambda: 1)()
+    # observe, the policy step, and step_compact's step, scan and scatter kernels
+    per_round = 4 + getattr(policy, "launches_per_step", lambda: 1)()
     n_launch = 1
     rounds = 0
     live = g
@@ -91,10 +92,10 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
             active = active[:live]
         if fused:  # observe with bit-word masks, one policy kernel, step: no host reads
             features, legal, _p, _d, _s = ext.observe_indexed_bf16_bits(states, active, m_dev=c_in)
-            game_ids, dec = game_index.index_select(0, active), decision.index_select(0, active)
             t0 = timer.start() if timer else None
-            actions, _logp = policy.forward_sample(features, legal, game_ids, dec, seed_base,
-                                                   m_dev=c_in)
+            # The kernel reads each row's game index and decision counter through active.
+            actions, _logp = policy.forward_sample(features, legal, game_index, decision, seed_base,
+                                                   m_dev=c_in, rows=active)
         else:
             features, legal, _p, _d, _s = ext.observe_indexed_bf16(states, active)
             game_ids, dec = game_index.index_select(0, active), decision.index_select(0, active)

@@ -268,6 +268,9 @@ CUGO_B200_API int cugo_b200_mlp_fused(const void* x, int64_t ldx, int64_t m, int
  * cugo_b200_observe_indexed_bf16_bits writes, or cugo_b200_pack_legal makes from a
  * bool mask), game int64 [m], decision int32 [m], actions int64 [m], logp fp32 [m];
  * n_out >= 179; out (fp32 [m, ldo]) may be NULL when the logits are not needed.
+ * rows (optional, int64 [m]): game and decision then hold n_games entries and row r
+ * reads entry rows[r] (a batch's running games without a gather); a row whose entry
+ * is outside [0, n_games) gets action -1 and log p 0.
  * m_dev (optional): a device-resident int32 row count, read when the kernel starts;
  * only rows below min(m, *m_dev) are computed (a loop can launch without reading the
  * count back).  No counterpart in the reference. */
@@ -277,6 +280,7 @@ CUGO_B200_API int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t
                                              const float* const* biases, int64_t n_out,
                                              int32_t act, const uint64_t* legal_bits,
                                              const int64_t* game, const int32_t* decision,
+                                             const int64_t* rows, int64_t n_games,
                                              int64_t seed_base, int32_t greedy, int64_t* actions,
                                              float* logp, float* out, int64_t ldo,
                                              const int32_t* m_dev, int32_t* error,

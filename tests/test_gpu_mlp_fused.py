@@ -111,6 +111,30 @@ def test_fused_sampling_head_matches_the_sampler(ext, m, n_out, greedy, density)
     assert none is None and torch.equal(a2, actions) and torch.equal(lp2, logp)
 
 
+def test_fused_sampling_head_reads_game_and_decision_through_rows(ext):
+    """rows[r] selects row r's game index and decision counter; an entry outside the
+    arrays samples nothing (-1, log p 0)."""
+    ws, bs = _net(720, 3, 180, seed=21)
+    g = torch.Generator().manual_seed(8)
+    m, n_games = 3000, 5000
+    x = torch.rand((m, 720), generator=g).to(DEV, torch.bfloat16)
+    legal = (torch.rand((m, 179), generator=g) < 0.1).to(DEV)
+    game = torch.randint(0, 1 << 40, (n_games,), generator=g).to(DEV)
+    decision = torch.randint(0, 60, (n_games,), generator=g, dtype=torch.int32).to(DEV)
+    rows = torch.randperm(n_games, generator=g)[:m].to(DEV)
+    rows[5], rows[6] = -1, n_games  # outside the arrays
+    a, lp, _ = ext.mlp_fused_sample(x, ws, bs, 1, legal, game, decision, seed_base=7, rows=rows)
+    safe = rows.clamp(0, n_games - 1)
+    ra, rlp, _ = ext.mlp_fused_sample(x, ws, bs, 1, legal, game.index_select(0, safe),
+                                      decision.index_select(0, safe), seed_base=7)
+    ok = torch.ones(m, dtype=torch.bool, device=DEV)
+    ok[5:7] = False
+    assert torch.equal(a[ok], ra[ok]) and torch.equal(lp[ok], rlp[ok])
+    assert bool((a[~ok] == -1).all()) and bool((lp[~ok] == 0).all())
+    with pytest.raises(RuntimeError):
+        ext.mlp_fused_sample(x, ws, bs, 1, legal, game, decision, rows=rows[:10])
+
+
 def test_observe_bits_and_pack_legal_agree_with_the_bool_mask(ext):
     idx = torch.arange(5000, device=DEV, dtype=torch.int64)
     states = ext.create(idx + 31, idx & 1)
