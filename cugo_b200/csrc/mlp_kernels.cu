@@ -1444,15 +1444,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
         fence_after();
         return ok;
       };
-      // One 64-deep K step: a_addr the A chunk, into accumulator column block nh.
-      auto k_step = [&](uint32_t a_addr, int nh, uint32_t idesc, bool first) -> bool {
+      // One 64-deep K step: a_addr the A chunk, into accumulator column block nh; only
+      // the first `sub` 16-deep MMAs when the rest of the chunk is past K (zero fill).
+      auto k_step = [&](uint32_t a_addr, int nh, uint32_t idesc, bool first,
+                        int sub = BK / 16) -> bool {
         if (!mbar_wait(&wfull[ws], wph)) return false;
         fence_after();
         const uint32_t b_addr = smem_addr(wring + ws * F_W_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          mma_bf16_pair(tmem_base + static_cast<uint32_t>(nh * BN), sw128_desc(a_addr + kk * 32),
-                        sw128_desc(b_addr + kk * 32), idesc, (first && kk == 0) ? 0u : 1u);
+          if (kk < sub)
+            mma_bf16_pair(tmem_base + static_cast<uint32_t>(nh * BN), sw128_desc(a_addr + kk * 32),
+                          sw128_desc(b_addr + kk * 32), idesc, (first && kk == 0) ? 0u : 1u);
         mma_commit_pair(&wempty[ws]);
         if (++ws == F_WSTAGES) {
           ws = 0;
@@ -1476,7 +1479,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
           xuse ^= 1u << slot;
           fence_after();
           const uint32_t a_addr = smem_addr(act + slot * F_CHUNK_BYTES);
-          if (!k_step(a_addr, 0, idesc_h, kc == 0) || !k_step(a_addr, 1, idesc_h, kc == 0)) {
+          const int rest = (args.k_in - kc * BK + 15) / 16;  // 16-deep steps left in K
+          const int sub = rest < BK / 16 ? rest : BK / 16;
+          if (!k_step(a_addr, 0, idesc_h, kc == 0, sub) || !k_step(a_addr, 1, idesc_h, kc == 0, sub)) {
             failed = true;
             break;
           }
