@@ -1141,12 +1141,16 @@ namespace {
 //                  (128 rows x 64) of a 256-row tile (16 KB), so each SM streams
 //                  half of every weight tile and the bytes in flight cover twice the
 //                  MMA work a single CTA's would;
-//   tensor memory  the fp32 accumulator of a whole layer, 128 lanes x 512 columns.
+//   tensor memory  the fp32 accumulator of a whole layer, 128 lanes x 512 columns;
+//                  the head's (at most 256 columns) in the upper half, so the next
+//                  tile's input-layer MMAs into the lower half overlap the head
+//                  epilogue, and the sampling head's column groups meet there too.
 // A block's residual never leaves the chip: the fc1 epilogue reads h from ACT, writes
 // h + b2 into the accumulator columns it has just drained (tcgen05.st) and u = act(z)
 // over h in ACT, so the fc2 MMAs accumulate u W2^T on top of h + b2.
 // Warp roles: warp 0 of each CTA the TMA producer of its half (weights run ahead of
-// the MMAs; x tiles wait for the previous tile's output stores to leave ACT), warp 1
+// the MMAs; x tiles wait for the previous tile's head MMAs, and for its output stores
+// to leave ACT when there are any), warp 1
 // of CTA 0 the MMA issuer (M = 256 MMAs reading both CTAs' shared memory), the other
 // F_EPI_WARPS warps of each CTA the epilogue of its 128 rows (F_EPI_WARPS / 4 per
 // TMEM lane quadrant, each a contiguous group of columns, 16 columns at a time).  Copies count on CTA 0's "full" barriers; MMA completions arrive on
@@ -1174,7 +1178,11 @@ constexpr int F_GROUPS = F_EPI_WARPS / 4;        // column groups per quadrant
 constexpr int F_GROUP_COLS = F_H / F_GROUPS;
 constexpr int F_CW = 16;                         // columns per epilogue chunk
 static_assert(F_EPI_WARPS % 4 == 0 && F_GROUP_COLS % F_CW == 0, "epilogue split");
-static_assert(F_EPI_WARPS * 2 * EPI_BUF <= F_ACT_BYTES, "output staging fits in ACT");
+// The head's output staging sits in the upper half of ACT (chunks F_STAGE_CHUNK ..),
+// so the next tile's first x chunks can load while the head stores.
+constexpr int F_STAGE_CHUNK = F_CHUNKS / 2;
+static_assert(F_EPI_WARPS * 2 * EPI_BUF <= F_ACT_BYTES - F_STAGE_CHUNK * F_CHUNK_BYTES,
+              "output staging fits in the upper half of ACT");
 static_assert(F_SMEM_BYTES <= 232448, "fits the opt-in shared memory of one CTA");
 
 struct FusedMaps {
@@ -1343,6 +1351,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
   }
   const int tiles = (m_rows + 2 * BM - 1) / (2 * BM);
   const int kc0 = (args.k_in + BK - 1) / BK;
+  const int kfirst = kc0 < F_CHUNKS ? kc0 : F_CHUNKS;  // input chunks in the first pass
   const int hidden_layers = 2 * args.blocks;
   const int head_rows = args.n_mma / 2;  // head weight rows per CTA
 
@@ -1400,27 +1409,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
       int iter = 0;
       for (int t = pair; t < tiles && !failed; t += pairs, ++iter) {
         const int row0 = t * 2 * BM + static_cast<int>(rank) * BM;
-        for (int kc = 0; kc < kc0 && !failed; ++kc) {
-          if (!load_w(0, kc, rh, 2 * F_W_BYTES) || !load_w(0, kc, BN + rh, 2 * F_W_BYTES)) {
-            failed = true;
-            break;
-          }
+        // The input layer in the MMA's order: its first (up to) eight 64-column chunks
+        // for accumulator half 0, the same chunks for half 1, then the rest of K
+        // (chunk kc in ACT slot kc - 8) for half 0 and half 1.
+        auto load_x = [&](int kc) -> bool {
           const int slot = kc & (F_CHUNKS - 1);
-          // ACT is free once this CTA's previous output stores have read it; a slot's
-          // second x tile of this tile waits for the MMAs of its first.
-          if (kc == 0 && iter > 0 && !mbar_wait(act_free, (iter - 1) & 1)) {
-            failed = true;
-            break;
+          if (iter > 0) {
+            // ACT takes this tile's x once the previous tile's head MMAs have read it;
+            // when the head stores outputs (through the upper chunks of ACT), chunks
+            // from free_at on also wait for those stores to leave.  (A tile with
+            // stores waits act_free exactly once, so no phase is skipped.)
+            const int free_at = kfirst - 1 < F_STAGE_CHUNK ? kfirst - 1 : F_STAGE_CHUNK;
+            if (kc == 0 && !(args.write_out && free_at == 0) &&
+                !mbar_wait(acc_full, static_cast<uint32_t>(iter * (hidden_layers + 2) - 1) & 1u))
+              return false;
+            if (args.write_out && kc == free_at && !mbar_wait(act_free, (iter - 1) & 1)) return false;
           }
-          if (kc >= F_CHUNKS && !mbar_wait(&xempty[slot], ((xuse >> slot) & 1u) ^ 1u)) {
-            failed = true;
-            break;
-          }
+          // A slot's second x tile of this tile waits for the MMAs of its first.
+          if (kc >= F_CHUNKS && !mbar_wait(&xempty[slot], ((xuse >> slot) & 1u) ^ 1u)) return false;
           if (leader) mbar_expect_tx(&xfull[slot], 2 * F_CHUNK_BYTES);
           tma_load_2d_pair(&maps.x, xfull0 + static_cast<uint32_t>(slot * 8),
                            act + slot * F_CHUNK_BYTES, kc * BK, row0);
           xuse ^= 1u << slot;
+          return true;
+        };
+        // x chunk 8 + i goes into slot i as soon as half 1 has read chunk i, X_LAG
+        // half-1 weight tiles later (the ring keeps the MMAs fed meanwhile).
+        constexpr int X_LAG = 3;
+        int next_x = F_CHUNKS;
+        for (int kc = 0; kc < kfirst && !failed; ++kc)
+          if (!load_w(0, kc, rh, 2 * F_W_BYTES) || !load_x(kc)) failed = true;
+        for (int kc = 0; kc < kfirst && !failed; ++kc) {
+          if (!load_w(0, kc, BN + rh, 2 * F_W_BYTES)) failed = true;
+          if (!failed && kc >= X_LAG && next_x < kc0 && next_x - F_CHUNKS <= kc - X_LAG)
+            if (!load_x(next_x++)) failed = true;
         }
+        for (; next_x < kc0 && !failed; ++next_x)
+          if (!load_x(next_x)) failed = true;
+        for (int nh = 0; nh < 2 && !failed; ++nh)
+          for (int kc = F_CHUNKS; kc < kc0 && !failed; ++kc)
+            if (!load_w(0, kc, nh * BN + rh, 2 * F_W_BYTES)) failed = true;
         for (int l = 1; l <= hidden_layers && !failed; ++l)
           for (int kc = 0; kc < F_CHUNKS && !failed; ++kc)
             if (!load_w(l, kc, rh, 2 * F_W_BYTES) || !load_w(l, kc, BN + rh, 2 * F_W_BYTES))
@@ -1465,27 +1493,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
       };
       int iter = 0;
       for (int t = pair; t < tiles && !failed; t += pairs, ++iter) {
-        // Both CTAs' head epilogues of the previous tile have drained the accumulators.
-        if (iter > 0 && !wait_ready()) {
-          failed = true;
-          break;
-        }
-        for (int kc = 0; kc < kc0 && !failed; ++kc) {
-          const int slot = kc & (F_CHUNKS - 1);
-          if (!mbar_wait(&xfull[slot], (xuse >> slot) & 1u)) {
-            failed = true;
-            break;
+        // Input layer, half 0 then half 1 over the resident x chunks, then the rest
+        // of K.  Half 0 (columns 0..255) is free: the previous tile's last hidden
+        // epilogue drained it before the head MMAs, whose accumulator is in half 1.
+        // So these MMAs run while the previous tile's head epilogue samples; half 1
+        // waits for it.
+        for (int part = 0; part < 2 && !failed; ++part) {
+          const int k0 = part ? F_CHUNKS : 0, k1 = part ? kc0 : kfirst;
+          for (int nh = 0; nh < 2 && !failed; ++nh) {
+            if (part == 0 && nh == 1 && iter > 0 && !wait_ready()) {
+              failed = true;
+              break;
+            }
+            for (int kc = k0; kc < k1 && !failed; ++kc) {
+              const int slot = kc & (F_CHUNKS - 1);
+              if (nh == 0) {
+                if (!mbar_wait(&xfull[slot], (xuse >> slot) & 1u)) {
+                  failed = true;
+                  break;
+                }
+                xuse ^= 1u << slot;
+                fence_after();
+              }
+              const int rest = (args.k_in - kc * BK + 15) / 16;  // 16-deep steps left in K
+              if (!k_step(smem_addr(act + slot * F_CHUNK_BYTES), nh, idesc_h, kc == 0,
+                          rest < BK / 16 ? rest : BK / 16)) {
+                failed = true;
+                break;
+              }
+              if (nh == 1) mma_commit_pair(&xempty[slot]);  // the chunk's last reader
+            }
           }
-          xuse ^= 1u << slot;
-          fence_after();
-          const uint32_t a_addr = smem_addr(act + slot * F_CHUNK_BYTES);
-          const int rest = (args.k_in - kc * BK + 15) / 16;  // 16-deep steps left in K
-          const int sub = rest < BK / 16 ? rest : BK / 16;
-          if (!k_step(a_addr, 0, idesc_h, kc == 0, sub) || !k_step(a_addr, 1, idesc_h, kc == 0, sub)) {
-            failed = true;
-            break;
-          }
-          mma_commit_pair(&xempty[slot]);
         }
         if (failed) break;
         mma_commit_pair(acc_full);
@@ -1508,8 +1546,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
           failed = true;
           break;
         }
+        // The head accumulates into half 1, so the next tile's half 0 need not wait
+        // for the head epilogue.
         for (int kc = 0; kc < F_CHUNKS && !failed; ++kc)
-          if (!k_step(smem_addr(act + kc * F_CHUNK_BYTES), 0, idesc_o, kc == 0)) failed = true;
+          if (!k_step(smem_addr(act + kc * F_CHUNK_BYTES), 1, idesc_o, kc == 0)) failed = true;
         if (!failed) mma_commit_pair(acc_full);
       }
       // All issued MMAs complete before the accumulators are released.
@@ -1523,7 +1563,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
     const int r = quad * 32 + lane;     // this thread's row of the CTA's 128 rows
     const uint32_t tq = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t ready0 = peer_addr(act_ready, 0);
-    uint8_t* stage = act + (warp - 2) * 2 * EPI_BUF;  // output staging, after the head MMAs
+    uint8_t* stage = act + F_STAGE_CHUNK * F_CHUNK_BYTES + (warp - 2) * 2 * EPI_BUF;  // after the head MMAs
     uint32_t full_ph = 0;
     auto wait_full = [&]() -> bool {
       const bool ok = mbar_wait(acc_full, full_ph & 1u);
@@ -1622,7 +1662,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
         const int col0 = c * 16;
         uint32_t raw[16];
         float v[16];
-        CB_TMEM_LD16(tq + static_cast<uint32_t>(col0), raw);
+        CB_TMEM_LD16(tq + static_cast<uint32_t>(BN + col0), raw);  // the head is in half 1
         fused_bias16(bo, col0, args.n_out, v);
         tmem_wait_ld();
 #pragma unroll
@@ -1642,34 +1682,51 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
         }
       }
       if (sampling) {
-        // The quadrant's column groups meet in ACT (past the output staging): groups
-        // 1.. post their state, group 0 combines and writes the row's action and log p.
-        float4* post = reinterpret_cast<float4*>(act + F_EPI_WARPS * 2 * EPI_BUF);
+        // The quadrant's column groups meet in tensor memory: group g > 0 posts its
+        // state over the first columns of its own first chunk (read already), group 0
+        // combines and writes the row's action and log p.  Shared memory stays free
+        // for the next tile's x.
+        const uint32_t post = tq + static_cast<uint32_t>(BN);
+        uint32_t raw[16];
         if (group > 0) {
-          post[(r * F_GROUPS + group) * 2] = make_float4(st.best, __int_as_float(st.best_a), st.best_x, st.mx);
-          post[(r * F_GROUPS + group) * 2 + 1] = make_float4(st.sum, 0.0f, 0.0f, 0.0f);
+          raw[0] = __float_as_uint(st.best);
+          raw[1] = static_cast<uint32_t>(st.best_a);
+          raw[2] = __float_as_uint(st.best_x);
+          raw[3] = __float_as_uint(st.mx);
+          raw[4] = __float_as_uint(st.sum);
+#pragma unroll
+          for (int j = 5; j < 16; ++j) raw[j] = 0u;
+          CB_TMEM_ST16(post + static_cast<uint32_t>(group * 16), raw);
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sample_ready[quad]);
         } else {
-          if (!mbar_wait(&sample_ready[quad], static_cast<uint32_t>(iter & 1))) failed = true;
-          if (!failed && live) {
+          // Decided by the whole warp: the TMEM loads below are warp-collective.
+          const bool ok = __all_sync(0xffffffffu, mbar_wait(&sample_ready[quad], static_cast<uint32_t>(iter & 1)));
+          if (!ok) failed = true;
+          if (ok) {
+            fence_after();
             for (int g2 = 1; g2 < F_GROUPS; ++g2) {
-              const float4 p0 = post[(r * F_GROUPS + g2) * 2];
-              const float4 p1 = post[(r * F_GROUPS + g2) * 2 + 1];
-              const int a = __float_as_int(p0.y);
-              if (a >= 0 && (p0.x > st.best || (p0.x == st.best && (st.best_a < 0 || a < st.best_a)))) {
-                st.best = p0.x;
+              CB_TMEM_LD16(post + static_cast<uint32_t>(g2 * 16), raw);
+              tmem_wait_ld();
+              const float best = __uint_as_float(raw[0]), mx = __uint_as_float(raw[3]);
+              const int a = static_cast<int>(raw[1]);
+              if (a >= 0 && (best > st.best || (best == st.best && (st.best_a < 0 || a < st.best_a)))) {
+                st.best = best;
                 st.best_a = a;
-                st.best_x = p0.z;
+                st.best_x = __uint_as_float(raw[2]);
               }
-              if (p0.w != -INFINITY) {
-                const float m2 = fmaxf(st.mx, p0.w);
-                st.sum = st.sum * expf(st.mx - m2) + p1.x * expf(p0.w - m2);
+              if (mx != -INFINITY) {
+                const float m2 = fmaxf(st.mx, mx);
+                st.sum = st.sum * expf(st.mx - m2) + __uint_as_float(raw[4]) * expf(mx - m2);
                 st.mx = m2;
               }
             }
-            args.actions[row_g] = st.best_a;
-            args.logp[row_g] = st.best_a < 0 ? 0.0f : st.best_x - (st.mx + logf(st.sum));
+            if (live) {
+              args.actions[row_g] = st.best_a;
+              args.logp[row_g] = st.best_a < 0 ? 0.0f : st.best_x - (st.mx + logf(st.sum));
+            }
           }
         }
       }

@@ -7,6 +7,8 @@ FLOPs of one launch:
 
   gemm      M N K      one tcgen05 layer, 2*M*N*K FLOP
   mlp       M H B      the policy forward (B blocks of width H), flops_per_row * M
+  mlpsample M H B      the self-play policy step: forward and masked Gumbel-max sampling
+                       (one fused launch at H = 512), flops_per_row * M
   observe   ROWS       observe_indexed, 3,319 B per row
   step      ROWS       step_indexed on live mid-game rows, 521 B per row
   branch    ROOTS PER  branch_indexed, 274 B per branch
@@ -393,6 +395,16 @@ def main() -> None:
         x = torch.randn((m, 720), device=dev).to(torch.bfloat16)
         sec = _time(lambda: pol(x), args.warmup, args.iters)
         out.update(seconds=sec, tflops=pol.flops_per_row() * m / sec / 1e12)
+    elif args.case == "mlpsample":  # the self-play policy step: MLP + sampling head
+        m, h, blocks = d
+        pol = ResidualMlpPolicy(h, blocks, "relu", device=dev)
+        x = torch.randn((m, 720), device=dev).to(torch.bfloat16)
+        bits = ext.pack_legal(torch.rand((m, 179), device=dev) < 0.1)
+        game = torch.arange(m, device=dev, dtype=torch.int64)
+        dec = torch.zeros(m, dtype=torch.int32, device=dev)
+        sec = _time(lambda: pol.forward_sample(x, bits, game, dec), args.warmup, args.iters)
+        out.update(seconds=sec, tflops=pol.flops_per_row() * m / sec / 1e12,
+                   fused=pol.samples_in_kernel())
     elif args.case == "observe":
         (rows,) = d
         states, _, _ = _mid_game(ext, rows)
