@@ -167,6 +167,8 @@ FUSED_TRAFFIC_65536 = 116.3e6
 
 # ---- config 3: policy self-play --------------------------------------------------------
 
+PREWARM_S = 1.0  # untimed play before the warm-up steps (see selfplay_bench)
+
 def selfplay_bench(args, world, rank, ext, policy):
     from cugo_b200.selfplay import RoundTimer, play_batch
 
@@ -179,6 +181,16 @@ def selfplay_bench(args, world, rank, ext, policy):
     blocks = [game_block(s, rank, world, g, dev) for s in range(total_steps)]
     clocks = ClockSampler(torch.cuda.current_device())
     time.sleep(0.5)  # let nvidia-smi finish starting before any timing
+    # The first ~0.5 s of GPU work in a fresh process runs 5-25% slower on these
+    # boards (measured: the first timed steps against the end-to-end steps of the
+    # same run), so the same batch is played for PREWARM_S of wall time before the
+    # W warm-up steps.  Nothing from it is kept or counted.
+    t_warm = time.perf_counter()
+    for _ in range(64):
+        play_batch(ext, policy, blocks[0])
+        torch.cuda.synchronize()
+        if time.perf_counter() - t_warm >= PREWARM_S:
+            break
     for s in range(args.warmup):
         play_batch(ext, policy, blocks[s])
     barrier(world)
@@ -469,7 +481,8 @@ def main():
         "config": {"workload": f"config3-ppo-selfplay-{args.arch}", "games_per_gpu": args.games,
                    "policy": f"{args.arch} residual MLP, ReLU, 179 logits + value",
                    "parallelism": f"dp{world} (disjoint seed blocks)",
-                   "l2": "inputs exceed L2 (fp32 features of 262,144 games = 755 MB per round)"},
+                   "l2": "inputs exceed L2 (fp32 features of 262,144 games = 755 MB per round)",
+                   "prewarm_s": PREWARM_S},
         "decisions_per_s": sp["decisions"] / sp["elapsed"],
         "bad_status": sp["bad"],
         "e2e": {"value": sp["e2e_games"] / sp["e2e_elapsed"], "unit": "games/s",

@@ -3,8 +3,9 @@
 
 Each decision round observes the live games, runs the policy, samples an action
 per game with the Philox-addressed Gumbel-max kernel and steps the games; the live
-set is compacted after every round (one device->host read of its size, as the
-reference's compaction does).
+set is compacted after every round.  The reference reads the live count back after
+every round; with the fused policy step the kernels read it from device memory and
+the host only polls copies of it (see play_batch).
 """
 from __future__ import annotations
 
@@ -51,6 +52,7 @@ class RoundTimer:
 
 
 CHECK_EVERY = 4  # rounds between host reads of the running count (device-count loop)
+LOOKAHEAD = 2    # reads in flight: the host waits on a read only this many checks later
 
 
 def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
@@ -61,9 +63,13 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
 
     With a fused policy step (policy.samples_in_kernel()) the rounds run without host
     round trips: each round's kernels read the running count that the previous
-    round's step left in device memory (buffers keep the batch's full size), and the
-    host reads the count every CHECK_EVERY rounds.  Otherwise the host reads the
-    count after every round and sizes the next round's launches by it."""
+    round's step left in device memory (buffers keep the batch's full size).  Every
+    CHECK_EVERY rounds the count is copied to pinned host memory behind an event; the
+    host looks at a copy only once its event has completed (or LOOKAHEAD later
+    copies are queued), so the device never waits for the host.  Rounds launched
+    after the count reached zero see zero rows and change nothing.  Otherwise the
+    host reads the count after every round and sizes the next round's launches by
+    it."""
     device = game_index.device
     g = game_index.numel()
     states = ext.create(game_index + seed_base, game_index & 1)
@@ -84,6 +90,11 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     n_launch = 1
     rounds = 0
     live = g
+    # Copies of the running count in flight: (event, pinned slot).
+    seen = torch.empty(LOOKAHEAD + 1, dtype=torch.int32, pin_memory=device.type == "cuda")
+    pending: list[tuple[torch.cuda.Event, int]] = []
+    n_copies = 0
+    finished = False
     for rounds in range(1, max_rounds + 1):
         k = (rounds - 1) & 1
         active, nxt = ids_buf[k], ids_buf[1 - k]
@@ -110,12 +121,29 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
         ext.step_compact(states, active, actions, decision, reward0, nagari, bad, nxt, c_out,
                          scratch, m_dev=c_in if fused else None)
         n_launch += per_round
-        if sync_each or rounds % CHECK_EVERY == 0:
+        if sync_each:
             live = int(c_out.item())
             if live == 0:
                 break
+        elif rounds % CHECK_EVERY == 0:
+            slot = n_copies % (LOOKAHEAD + 1)
+            n_copies += 1
+            seen[slot:slot + 1].copy_(c_out, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            pending.append((ev, slot))
+            while pending and (len(pending) > LOOKAHEAD or pending[0][0].query()):
+                ev0, slot0 = pending.pop(0)
+                ev0.synchronize()
+                if int(seen[slot0]) == 0:
+                    finished = True
+                    break
+            if finished:
+                break
     else:
-        raise RuntimeError(f"games did not finish within {max_rounds} rounds")
+        # The last round's count says whether the games ended within the limit.
+        if max_rounds == 0 or int(c_out.item()) != 0:
+            raise RuntimeError(f"games did not finish within {max_rounds} rounds")
     if launches is not None:
         launches.append(n_launch)
     decisions = int(decision.sum())
