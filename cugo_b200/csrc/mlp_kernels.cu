@@ -1222,40 +1222,40 @@ struct SampleState {
 };
 
 // Folds 16 outputs col0 .. col0 + 15 of the thread's row into the state (legal
-// actions only); bits: the row's legal actions col0 .. col0 + 15.
+// actions only); bits: the row's legal actions col0 .. col0 + 15.  The loop runs over
+// the set bits in ascending order (the order, and so the result, of a scan over all
+// 16 columns), so a warp pays for its lanes' legal actions, not for every column.
 __device__ __forceinline__ void sample_chunk(const FusedArgs& args, uint64_t gid, uint32_t dec,
                                              int col0, uint32_t bits, const float* v,
                                              SampleState& st) {
   const uint64_t seed = static_cast<uint64_t>(args.seed_base) + gid;
+  while (bits) {
+    const int e = __ffs(bits) - 1;
+    bits &= bits - 1;
+    float x = v[0];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int a0 = col0 + 4 * q;
-    const uint32_t nib = (bits >> (4 * q)) & 0xfu;
-    bool lg[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) lg[e] = (nib >> e) & 1u;
-    if (!nib) continue;
-    cb::Philox4 ph{};
-    if (!args.greedy)
-      ph = cb::philox4x32_10(static_cast<uint32_t>(gid), static_cast<uint32_t>(gid >> 32), dec,
-                             3u | (static_cast<uint32_t>(a0 >> 2) << 8), static_cast<uint32_t>(seed),
-                             static_cast<uint32_t>(seed >> 32));
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (!lg[e]) continue;
-      const float x = v[4 * q + e];
-      const float score = args.greedy ? x : x + cb::gumbel_of(ph.v[e]);
-      if (score > st.best) {  // columns ascend within a thread: the first maximum is kept
-        st.best = score;
-        st.best_a = a0 + e;
-        st.best_x = x;
-      }
-      if (x > st.mx) {
-        st.sum = st.sum * expf(st.mx - x) + 1.0f;  // exp(-inf) = 0 on the first legal logit
-        st.mx = x;
-      } else {
-        st.sum += expf(x - st.mx);
-      }
+    for (int j = 1; j < 16; ++j) x = e == j ? v[j] : x;  // v[e] without local memory
+    const int a = col0 + e;
+    float score = x;
+    if (!args.greedy) {
+      const cb::Philox4 ph = cb::philox4x32_10(
+          static_cast<uint32_t>(gid), static_cast<uint32_t>(gid >> 32), dec,
+          3u | (static_cast<uint32_t>(a >> 2) << 8), static_cast<uint32_t>(seed),
+          static_cast<uint32_t>(seed >> 32));
+      const int w = a & 3;
+      const uint32_t r = w == 0 ? ph.v[0] : (w == 1 ? ph.v[1] : (w == 2 ? ph.v[2] : ph.v[3]));
+      score = x + cb::gumbel_of(r);
+    }
+    if (score > st.best) {  // ascending actions: the first maximum is kept
+      st.best = score;
+      st.best_a = a;
+      st.best_x = x;
+    }
+    if (x > st.mx) {
+      st.sum = st.sum * expf(st.mx - x) + 1.0f;  // exp(-inf) = 0 on the first legal logit
+      st.mx = x;
+    } else {
+      st.sum += expf(x - st.mx);
     }
   }
 }
