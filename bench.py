@@ -102,7 +102,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu=timestamp,{self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", target], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+                 "-lms", "200", "-i", target], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
 
