@@ -156,13 +156,18 @@ def mlp_traffic(arch: str, policy) -> float | None:
     layer-per-launch path's, 4,784 MB over its 8 launches."""
     if arch != "512x3":
         return None
+    if policy.samples_in_kernel():
+        return FUSED_SAMPLE_TRAFFIC_65536 * 4
     if policy.launches_per_forward() == 1:
-        return None if FUSED_TRAFFIC_65536 is None else FUSED_TRAFFIC_65536 * 4
+        return FUSED_TRAFFIC_65536 * 4
     return 598e6
 
 
-# ncu DRAM bytes of one fused_mlp_kernel launch on 65,536 rows of the 3x512 policy.
+# ncu DRAM bytes of one fused_mlp_kernel launch on 65,536 rows of the 3x512 policy:
+# writing the logits, and with the sampling head (features, legal words, game index
+# and decision counter in; action and log p out).
 FUSED_TRAFFIC_65536 = 116.3e6
+FUSED_SAMPLE_TRAFFIC_65536 = 104.5e6
 
 
 # ---- config 3: policy self-play --------------------------------------------------------
