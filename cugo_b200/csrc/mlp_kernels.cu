@@ -1778,13 +1778,7 @@ int fused_max_pairs(int dev) {
   return cache[dev];
 }
 
-}  // namespace
 
-extern "C" {
-
-}  // extern "C"
-
-namespace {
 
 // Both entry points: out may be null when sampling (actions != null).
 int fused_launch(const void* x, int64_t ldx, int64_t m, int64_t k_in, int32_t blocks,
