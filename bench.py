@@ -445,7 +445,9 @@ def main():
     policy = ResidualMlpPolicy(hidden, blocks, "relu", device="cuda", seed=0)
     sp = selfplay_bench(args, world, rank, ext, policy)
     extras = {}
-    if not args.no_extras:
+    # Extras and the CPU baseline are single-GPU measurements: at N > 1 every rank
+    # would repeat them while all GPUs are held.
+    if not args.no_extras and world == 1:
         extras["engine_only"] = engine_only_bench(ext)
         extras["branching"] = branching_bench(ext)
         if args.arch != "2048x4":
@@ -506,7 +508,7 @@ def main():
         "gpu_launches": sp["launches"],
         "extras": extras,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_games = 98304  # 10-20 s of host work
         cpu = cpu_selfplay(cpu_games, args.arch, host_threads())
         out["cpu_baseline"] = {
