@@ -24,6 +24,7 @@ from dataclasses import dataclass
 from typing import Any
 
 import torch
+import torch.distributed as dist
 from torch import nn
 
 from .evaluate import make_seeds
@@ -208,7 +209,13 @@ class TrainStats:
 
 class PpoTrainer:
     """The update of one iteration (python/cugo_ppo50.py:514-745, PpoUpdater.update with
-    the plain policy target) over the fused networks."""
+    the plain policy target) over the fused networks.
+
+    Data parallel (world > 1, one process per GPU, process group initialised): each
+    rank updates on its own rollout and PpoStep averages the gradients.  The ranks
+    must take the same collective steps, so every epoch runs the smallest number of
+    whole minibatches any rank has, and the early stop compares the KL averaged over
+    the ranks."""
 
     def __init__(self, actor: nn.Module, critic: nn.Module, lr: float = 3e-4,
                  minibatch: int = 32768, clip: float = 0.2, value_coef: float = 0.5,
@@ -218,7 +225,23 @@ class PpoTrainer:
         self.optimizer = torch.optim.Adam(params, lr=lr, capturable=use_graph)
         self.step = PpoStep(actor, critic, self.optimizer, clip, value_coef, grad_clip, world)
         self.use_graph = use_graph
+        self.world = world
         self.graphed: GraphedPpoStep | None = None
+
+    def _steps_per_epoch(self, n: int, device: torch.device) -> int:
+        steps = n // self.minibatch
+        if self.world > 1:
+            t = torch.tensor([steps], dtype=torch.int64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            steps = int(t)
+        return steps
+
+    def _kl(self) -> float:
+        kl = self.step.last_kl.detach().reshape(1).clone()
+        if self.world > 1:
+            dist.all_reduce(kl)
+            kl /= self.world
+        return float(kl)
 
     @torch.no_grad()
     def values(self, data: Rollout, chunk: int = 65536) -> torch.Tensor:
@@ -242,10 +265,11 @@ class PpoTrainer:
         st.entropy_coef.fill_(entropy_coef)
         st.sums.zero_()
         updates, stop = 0, False
+        steps = self._steps_per_epoch(n, data.actions.device)
         for _ in range(epochs):
             perm = torch.randperm(n, device=data.actions.device)
-            for i in range(0, n - self.minibatch + 1, self.minibatch):
-                idx = perm[i:i + self.minibatch]
+            for j in range(steps):
+                idx = perm[j * self.minibatch:(j + 1) * self.minibatch]
                 mb = Minibatch(data.features.index_select(0, idx), data.legal.index_select(0, idx),
                                data.actions.index_select(0, idx), data.logp.index_select(0, idx),
                                data.opp_hand.index_select(0, idx), adv.index_select(0, idx),
@@ -257,7 +281,7 @@ class PpoTrainer:
                 else:
                     st.step(mb)
                 updates += 1
-                if target_kl > 0 and updates % 8 == 0 and float(st.last_kl) > 1.5 * target_kl:
+                if target_kl > 0 and updates % 8 == 0 and self._kl() > 1.5 * target_kl:
                     stop = True
                     break
             if stop:
@@ -266,7 +290,7 @@ class PpoTrainer:
         count = max(1.0, s[5])
         return TrainStats(policy_loss=s[0] / count, value_loss=s[1] / count, entropy=s[2] / count,
                           kl=s[3] / count, clipfrac=s[4] / count, explained_var=explained_var,
-                          updates=updates, epochs=updates / max(1, n // self.minibatch))
+                          updates=updates, epochs=updates / max(1, steps))
 
 
 def iteration(ext: Any, trainer: PpoTrainer, storage: RolloutStorage, games: int,
@@ -275,7 +299,8 @@ def iteration(ext: Any, trainer: PpoTrainer, storage: RolloutStorage, games: int
               gae_lambda: float = 0.95) -> dict:
     """One train_ppo50.py iteration (its defaults: 65,536 games, 2 epochs, minibatch
     32,768, GAE 0.95, reward scale 32): collection and update, timed on the host
-    around device synchronisations."""
+    around device synchronisations.  Data parallel: each rank passes its own
+    seed_offset (disjoint games) and a trainer built with world = the number of ranks."""
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     data = collect(ext, trainer.actor, games, seed_offset, reward_scale, storage)
