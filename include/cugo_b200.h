@@ -47,6 +47,7 @@ typedef struct CUstream_st* cudaStream_t;
 #define CUGO_B200_ERR_LAUNCH (-3)
 #define CUGO_B200_ERR_CAPACITY (-4) /* larger than a fixed internal buffer allows */
 
+/* Version of this C ABI (1).  No counterpart in the reference. */
 CUGO_B200_API int cugo_b200_abi_version(void);
 
 /* Contract constants (python/csrc/torch50_ext.cpp:61-71). */
@@ -143,7 +144,9 @@ CUGO_B200_API int cugo_b200_start(const uint8_t* states, int64_t n, int64_t* out
  * Philox4x32-10(counter {i lo, i hi, d, stream}, key {seed lo, seed hi}).
  */
 
-/* Plays games game0 .. game0+n-1 to the end (at most max_decisions steps each):
+/* Plays games game0 .. game0+n-1 to the end (at most max_decisions steps each; the
+ * loop of python/torch50_smoke.py:13-59 run_games with random-legal actions, in one
+ * launch):
  * final rows [n, 248], player 0's reward, decisions taken, events committed,
  * FNV-1a 64 hash of the start record and every event record, last step status
  * (-2 when a game had no legal action). */
@@ -153,7 +156,8 @@ CUGO_B200_API int cugo_b200_rollout_random(int64_t game0, int64_t n, int64_t see
                                            int32_t* decisions, int32_t* events, uint64_t* hashes,
                                            int16_t* last_status, cudaStream_t stream);
 
-/* One decision of every slot: a finished game is replaced by game index +
+/* One decision of every slot (config 1: the run_games loop, python/torch50_smoke.py:
+ * 13-59, as one launch per decision): a finished game is replaced by game index +
  * n_slots (counted in slot_completed), then the slot's observation is written to
  * features/legal exactly as observe() writes it, a random legal action is drawn
  * and stepped (counted in slot_steps).  actions: int64 [n_slots] scratch that
@@ -164,7 +168,9 @@ CUGO_B200_API int cugo_b200_selfplay_random_step(uint8_t* states, int64_t n_slot
                                                  int64_t* slot_steps, float* features, bool* legal,
                                                  int64_t* actions, cudaStream_t stream);
 
-/* Branching roots: game r advanced by k_r random-legal decisions, k_r uniform in
+/* Branching roots for the branch benchmark (python/branch50_smoke.py:66-195, whose
+ * parents are fresh games advanced by one step): game r advanced by k_r random-legal
+ * decisions, k_r uniform in
  * 0..20 (stream 2, decision 0xFFFF), stopping before a decision that would end
  * the game. */
 CUGO_B200_API int cugo_b200_branch_roots(int64_t n_roots, int64_t seed_base, uint8_t* roots,
@@ -286,7 +292,8 @@ CUGO_B200_API int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t
                                              const int32_t* m_dev, int32_t* error,
                                              cudaStream_t stream);
 
-/* Packs bool legal masks [m, 179] into uint64 [m, 3] (bit a of word a / 64). */
+/* Packs bool legal masks [m, 179] into uint64 [m, 3] (bit a of word a / 64), the
+ * form the fused sampling head reads.  No counterpart in the reference. */
 CUGO_B200_API int cugo_b200_pack_legal(const bool* legal, int64_t m, uint64_t* bits,
                                        cudaStream_t stream);
 
@@ -316,8 +323,9 @@ CUGO_B200_API int cugo_b200_policy_forward_noalloc(const void* x, int64_t ldx, i
                                                    float* out, int64_t ldo, int32_t* error,
                                                    cudaStream_t stream);
 
-/* observe_indexed_bf16 with the legal mask written as bits, uint64 [m, 3] (bit a of
- * word a / 64), for the fused MLP's sampling head; no bool mask is written.  m_dev
+/* observe_indexed_bf16 (observe_indexed, torch50_ext.cu:520-544, with bf16 features)
+ * with the legal mask written as bits, uint64 [m, 3] (bit a of word a / 64), for the
+ * fused MLP's sampling head; no bool mask is written.  m_dev
  * (optional): a device-resident int32 row count; rows from min(m, *m_dev) on are left
  * alone. */
 CUGO_B200_API int cugo_b200_observe_indexed_bf16_bits(const uint8_t* states, int64_t n_states,
@@ -456,6 +464,7 @@ CUGO_B200_API int cugo_b200_games_attention(const void* qkv, int64_t ldq, int64_
                                             float scale, void* out, int64_t ldo,
                                             cudaStream_t stream);
 
+/* Token widths of the sequence policy (python/cugo_seq50.py:37-38). */
 CUGO_B200_API int64_t cugo_b200_event_inputs(void); /* EVENT_IN = 414 */
 CUGO_B200_API int64_t cugo_b200_start_inputs(void); /* START_IN = 274 */
 
