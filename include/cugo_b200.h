@@ -170,9 +170,8 @@ CUGO_B200_API int cugo_b200_selfplay_random_step(uint8_t* states, int64_t n_slot
 
 /* Branching roots for the branch benchmark (python/branch50_smoke.py:66-195, whose
  * parents are fresh games advanced by one step): game r advanced by k_r random-legal
- * decisions, k_r uniform in
- * 0..20 (stream 2, decision 0xFFFF), stopping before a decision that would end
- * the game. */
+ * decisions, k_r uniform in 0..20 (stream 2, decision 0xFFFF), stopping before a
+ * decision that would end the game. */
 CUGO_B200_API int cugo_b200_branch_roots(int64_t n_roots, int64_t seed_base, uint8_t* roots,
                                          cudaStream_t stream);
 
