@@ -173,22 +173,29 @@ FUSED_SAMPLE_TRAFFIC_65536 = 104.5e6
 # ---- config 3: policy self-play --------------------------------------------------------
 
 PREWARM_S = 1.0  # untimed play before the warm-up steps (see selfplay_bench)
+REPEATS = 3      # timed regions of K steps per measurement; the median is reported
+
 
 def selfplay_bench(args, world, rank, ext, policy):
+    """Config 3 timed two ways, each over REPEATS regions of exactly K steps,
+    interleaved (device-timed region, then end-to-end region, three times) so both
+    see the same clocks; the median region of each is reported, the max over ranks
+    of each region."""
     from cugo_b200.selfplay import RoundTimer, play_batch
+    from cugo_b200.shard import all_gather, game_block
 
     g = args.games
     dev = torch.device("cuda")
     total_steps = args.warmup + args.steps
     # Game blocks for every step, resident in HBM before timing: rank r, step s
     # plays games (s * world + r) * g .. + g.
-    from cugo_b200.shard import game_block
     blocks = [game_block(s, rank, world, g, dev) for s in range(total_steps)]
+    host_blocks = [b.cpu().pin_memory() for b in blocks[args.warmup:]]
+    reward_host = torch.empty(g, dtype=torch.float32).pin_memory()
     clocks = ClockSampler(torch.cuda.current_device())
     time.sleep(0.5)  # let nvidia-smi finish starting before any timing
     # The first ~0.5 s of GPU work in a fresh process runs 5-25% slower on these
-    # boards (measured: the first timed steps against the end-to-end steps of the
-    # same run), so the same batch is played for PREWARM_S of wall time before the
+    # boards, so the same batch is played for PREWARM_S of wall time before the
     # W warm-up steps.  Nothing from it is kept or counted.
     t_warm = time.perf_counter()
     for _ in range(64):
@@ -198,16 +205,31 @@ def selfplay_bench(args, world, rank, ext, policy):
             break
     for s in range(args.warmup):
         play_batch(ext, policy, blocks[s])
-    barrier(world)
-    launches: list[int] = []
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    results = []
+    regions = []  # (device seconds, results, launches, e2e wall seconds)
     t_start = time.time()
-    start.record()
-    for s in range(args.warmup, total_steps):
-        results.append(play_batch(ext, policy, blocks[s], launches=launches))
-    stop.record()
-    barrier(world)
+    for _ in range(REPEATS):
+        # Inputs resident in HBM, CUDA events on the launching stream.
+        barrier(world)
+        launches: list[int] = []
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        results = [play_batch(ext, policy, blocks[s], launches=launches)
+                   for s in range(args.warmup, total_steps)]
+        stop.record()
+        barrier(world)
+        elapsed = start.elapsed_time(stop) / 1e3
+        # End to end through the public API, host wall clock: each step's game
+        # indices copied from pinned host memory, its rewards read back.
+        barrier(world)
+        t0 = time.perf_counter()
+        for hb in host_blocks:
+            idx = hb.to(dev, non_blocking=True)
+            r = play_batch(ext, policy, idx)
+            reward_host.copy_(r.reward0, non_blocking=True)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        barrier(world)
+        regions.append((elapsed, results, sum(launches), wall))
     clocks.mark(t_start, time.time())
     clk = clocks.stop()
     # The policy's in-loop rate, from CUDA events around every forward of one more
@@ -215,35 +237,29 @@ def selfplay_bench(args, world, rank, ext, policy):
     timer = RoundTimer(enabled=True)
     play_batch(ext, policy, blocks[args.warmup], timer=timer)
     torch.cuda.synchronize()
-    elapsed = start.elapsed_time(stop) / 1e3
+    mlp_ms, mlp_launches, mlp_rows = timer.total_ms()
+
+    dev_max = [all_reduce([r[0]], world, op="max")[0] for r in regions]
+    e2e_max = [all_reduce([r[3]], world, op="max")[0] for r in regions]
+    pick = sorted(range(REPEATS), key=lambda i: dev_max[i])[REPEATS // 2]
+    _, results, n_launch, _ = regions[pick]
     games = sum(r.games for r in results)
     decisions = sum(r.decisions for r in results)
     bad = sum(r.bad_status for r in results)
     tot_games, tot_dec, tot_bad = all_reduce([games, decisions, bad], world)
-    (max_elapsed,) = all_reduce([elapsed], world, op="max")
-    mlp_ms, mlp_launches, mlp_rows = timer.total_ms()
-
-    # End to end through the public API: game indices from pinned host memory,
-    # rewards read back every step.
-    host_blocks = [b.cpu().pin_memory() for b in blocks[args.warmup:]]
-    reward_host = torch.empty(g, dtype=torch.float32).pin_memory()
-    barrier(world)
-    t0 = time.perf_counter()
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record()
-    for hb in host_blocks:
-        idx = hb.to(dev, non_blocking=True)
-        r = play_batch(ext, policy, idx)
-        reward_host.copy_(r.reward0, non_blocking=True)
-    e_stop.record()
-    barrier(world)
-    e_elapsed = e_start.elapsed_time(e_stop) / 1e3
-    (e_max,) = all_reduce([e_elapsed], world, op="max")
-    _wall = time.perf_counter() - t0
-    return dict(games=tot_games, decisions=tot_dec, bad=tot_bad, elapsed=max_elapsed,
+    own_dev = statistics.median(r[0] for r in regions)
+    own_e2e = statistics.median(r[3] for r in regions)
+    per_rank = [{"rank": i, "ms_per_step": v[0] * 1e3 / args.steps,
+                 "e2e_ms_per_step": v[1] * 1e3 / args.steps, "sm_mhz": v[2] if v[2] >= 0 else None,
+                 "regions_ms_per_step": [round(x * 1e3 / args.steps, 3) for x in v[3:]]}
+                for i, v in enumerate(all_gather(
+                    [own_dev, own_e2e, clk["sm_mhz"] if clk["sm_mhz"] is not None else -1.0,
+                     *[r[0] for r in regions]], world))]
+    return dict(games=tot_games, decisions=tot_dec, bad=tot_bad, elapsed=dev_max[pick],
                 mlp_ms=mlp_ms, mlp_launches=mlp_launches, mlp_rows=mlp_rows,
-                launches=sum(launches), clocks=clk, e2e_elapsed=e_max,
-                e2e_games=tot_games, h2d=g * 8, d2h=g * 4)
+                launches=n_launch, clocks=clk, e2e_elapsed=statistics.median(e2e_max),
+                e2e_games=tot_games, h2d=g * 8, d2h=g * 4, per_rank=per_rank,
+                regions_s=dev_max, e2e_regions_s=e2e_max)
 
 
 # ---- config 1 and 2: engine only -----------------------------------------------------
@@ -353,21 +369,61 @@ def seq_bench(wave: int = 4096, waves: int = 4) -> dict:
 
 # ---- CPU: the reference engine (oracle/_ref) + a PyTorch-CPU policy --------------------
 
-def cpu_selfplay(games: int, arch: str, threads: int, policy_cpu=None) -> dict:
-    """Plays `games` seeded games with the reference's own engine compiled from its
-    sources (oracle/_ref) and the same residual MLP on PyTorch-CPU (fp32)."""
+CPU_SAMPLE_GAMES = 16384  # games per CPU sample, in the reference arm and in cpu_baseline
+
+
+def cpu_actor(arch: str):
+    """The reference's own PpoActor class (python/cugo_ppo_nets50.py:26-64, staged
+    unmodified by baseline/build_ref.py) in fp32, norm "none", with the weights of
+    the GPU arm's policy (Kaiming-normal, seed 0; its 179 logit rows).  Returns the
+    module and a description.  Without the staged modules the same layer stack is
+    run with torch.nn.functional (and the description says so)."""
+    from cugo_b200.policy import ResidualMlpPolicy
+
+    hidden, blocks = ARCHS[arch]
+    pol = ResidualMlpPolicy(hidden, blocks, "relu", device="cpu", seed=0)
+    ws = [w.float() for w in pol.weights]
+    bs = [b.float() for b in pol.biases]
+    try:
+        from baseline import build_ref
+        ref_py = str(build_ref.reference_python())
+        if ref_py not in sys.path:
+            sys.path.insert(0, ref_py)
+        from cugo_ppo_nets50 import PpoActor
+    except (ImportError, RuntimeError):
+        def forward(x):
+            f = torch.nn.functional
+            h = f.linear(x, ws[0], bs[0])
+            for i in range(blocks):
+                h = h + f.linear(f.silu(f.linear(h, ws[1 + 2 * i], bs[1 + 2 * i])), ws[2 + 2 * i],
+                                 bs[2 + 2 * i])
+            return f.linear(f.silu(h), ws[-1][:179], bs[-1][:179])
+        return forward, f"{arch} residual MLP (SiLU, functional restatement of PpoActor)"
+    actor = PpoActor(hidden, blocks, norm="none")
+    layers = [actor.inp] + [l for b in actor.blocks for l in (b.fc1, b.fc2)] + [actor.out]
+    with torch.no_grad():
+        for layer, w, b in zip(layers, ws, bs):
+            layer.weight.copy_(w[:layer.out_features])
+            layer.bias.copy_(b[:layer.out_features])
+    return actor.eval(), f"the reference's PpoActor({hidden}, {blocks}) class, fp32"
+
+
+def cpu_selfplay(games: int, arch: str, threads: int, actor=None) -> dict:
+    """Plays `games` seeded games (game i: seed 12345 + i, first player i & 1) to
+    settlement on the host: the reference's own engine compiled from its sources
+    (oracle/_ref, one shard per thread), the reference PpoActor on PyTorch-CPU and
+    masked Gumbel-max sampling with the GPU arm's Philox noise definition (counter
+    {game, decision}, oracle/philox_np.py).  Games ended at the deal are settled
+    before the first decision, as on the GPU."""
     from oracle import ref
+    from oracle.philox_np import gumbel_noise
 
     torch.set_num_threads(threads)
-    hidden, blocks = ARCHS[arch]
-    if policy_cpu is None:
-        from cugo_b200.policy import ResidualMlpPolicy
-        policy_cpu = ResidualMlpPolicy(hidden, blocks, "relu", device="cpu")
-        policy_cpu.weights = [w.float() for w in policy_cpu.weights]
-        policy_cpu.biases = [b.float() for b in policy_cpu.biases]
+    if actor is None:
+        actor = cpu_actor(arch)[0]
     idx = np.arange(games, dtype=np.int64)
     rows = ref.create(idx + SEED_BASE, idx & 1, threads=threads)
-    rng = np.random.default_rng(0)
+    decision = np.zeros(games, dtype=np.int64)
     t0 = time.perf_counter()
     live = np.ones(games, dtype=bool)
     decisions = 0
@@ -378,20 +434,14 @@ def cpu_selfplay(games: int, arch: str, threads: int, policy_cpu=None) -> dict:
             break
         sel = np.nonzero(live)[0]
         with torch.no_grad():
-            x = torch.from_numpy(f[sel])
-            w, bb = policy_cpu.weights, policy_cpu.biases
-            h = torch.nn.functional.linear(x, w[0], bb[0])
-            for i in range(blocks):
-                h = h + torch.nn.functional.linear(
-                    torch.relu(torch.nn.functional.linear(h, w[1 + 2 * i], bb[1 + 2 * i])),
-                    w[2 + 2 * i], bb[2 + 2 * i])
-            logits = torch.nn.functional.linear(torch.relu(h), w[-1], bb[-1]).numpy()[:, :179]
-        gumbel = -np.log(-np.log(rng.random(logits.shape)))
-        score = np.where(legal[sel], logits + gumbel, -np.inf)
+            logits = actor(torch.from_numpy(f[sel])).numpy()
+        noise = gumbel_noise(sel.astype(np.uint64), decision[sel], SEED_BASE)
+        score = np.where(legal[sel], logits + noise, -np.inf)
         acts = np.zeros(games, dtype=np.int64)
         acts[sel] = score.argmax(1)
-        stepped = ref.step(rows, acts, threads=threads)[0]
-        rows[sel] = stepped[sel]
+        stepped = ref.step(rows[sel], acts[sel], threads=threads)[0]
+        rows[sel] = stepped
+        decision[sel] += 1
         decisions += sel.size
     sec = time.perf_counter() - t0
     return dict(games=games, decisions=decisions, seconds=sec, games_per_s=games / sec)
@@ -401,27 +451,34 @@ def host_threads() -> int:
     return max(1, len(os.sched_getaffinity(0)))
 
 
+def workload_config(args, world: int) -> dict:
+    """The `config` of both arms' JSON lines (one definition, so they are equal)."""
+    return {"workload": f"config3-ppo-selfplay-{args.arch}", "games_per_gpu": args.games,
+            "policy": f"{args.arch} residual MLP, 179 logits",
+            "parallelism": f"dp{world} (disjoint seed blocks)",
+            "l2": "inputs exceed L2 (fp32 features of 262,144 games = 755 MB per round)"}
+
+
 def reference_arm(args, world, rank):
     if rank != 0:
         return
     threads = host_threads()
-    sample = 16384  # about 3 s of host work per step
+    actor, actor_desc = cpu_actor(args.arch)
     for _ in range(args.warmup):
-        cpu_selfplay(256, args.arch, threads)
-    runs = [cpu_selfplay(sample, args.arch, threads) for _ in range(args.steps)]
+        cpu_selfplay(256, args.arch, threads, actor)
+    runs = [cpu_selfplay(CPU_SAMPLE_GAMES, args.arch, threads, actor) for _ in range(args.steps)]
     games = sum(r["games"] for r in runs)
     sec = sum(r["seconds"] for r in runs)
     value = games / sec
-    desc = (f"{sample} seeded games per step played to settlement on {threads} host threads: "
-            f"the reference's own engine (include/cugo/**, compiled by oracle/Makefile) + "
-            f"the {args.arch} ReLU residual MLP on PyTorch-CPU fp32 + Gumbel-max sampling")
+    desc = (f"{CPU_SAMPLE_GAMES} seeded games per step played to settlement on {threads} host "
+            f"threads: the reference's own engine (include/cugo/**, compiled by oracle/Makefile), "
+            f"{actor_desc} on PyTorch-CPU, masked Gumbel-max with Philox noise")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "games/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": sec * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded deals 12345 + i)",
-        "config": {"workload": f"config3-ppo-selfplay-{args.arch}", "games_per_step": sample,
-                   "host_threads": threads},
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": value, "unit": "games/s", "cores": threads, "kind": "reference",
                          "sample": desc},
         "e2e": {"value": value, "unit": "games/s", "h2d_bytes_per_step": 0,
@@ -453,16 +510,23 @@ def main():
         if args.arch != "2048x4":
             extras["config3_2048x4"] = arch_bench(ext, "2048x4", args.games)
         extras["config4_seq"] = seq_bench()
-        from cugo_b200.kernel_cases import ppo_case
+        from bench_cases import ppo_case
         extras["ppo_update"] = {"minibatch": 32768, "networks": "3x512 actor + critic (SiLU)",
                                 **ppo_case(32768, warmup=3, iters=10)}
-        from cugo_b200.kernel_cases import ppoiter_case
+        from bench_cases import ppoiter_case
         extras["ppo_iteration"] = {"games": 65536, "networks": "3x512 actor + critic (SiLU)",
                                    "epochs": 2, "minibatch": 32768,
                                    **ppoiter_case(65536, 512, 3, warmup=1, iters=1)}
-        from cugo_b200.kernel_cases import allaction_case
+        from bench_cases import allaction_case
         extras["all_action_q"] = {"critic": "3x512 OracleCritic layout (SiLU), every legal action",
                                   **allaction_case(16384, warmup=3, iters=10)}
+        from baseline import build_ref
+        if build_ref.available():
+            from bench_cases import reference_gpu_case
+            extras["reference_gpu"] = reference_gpu_case(args.games, warmup=1, iters=2)
+        else:
+            extras["reference_gpu"] = {"unavailable": "baseline/_ref not staged "
+                                                      "(python -m baseline.build_ref)"}
     peaks = measured_peaks()
     if "engine_only" in extras:
         e = extras["engine_only"]
@@ -485,15 +549,20 @@ def main():
         "ms_per_step": sp["elapsed"] * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded deals (seed 12345 + game), Kaiming-normal bf16 weights (seed 0)",
-        "config": {"workload": f"config3-ppo-selfplay-{args.arch}", "games_per_gpu": args.games,
-                   "policy": f"{args.arch} residual MLP, ReLU, 179 logits + value",
-                   "parallelism": f"dp{world} (disjoint seed blocks)",
-                   "l2": "inputs exceed L2 (fp32 features of 262,144 games = 755 MB per round)",
-                   "prewarm_s": PREWARM_S},
+        "config": workload_config(args, world),
+        "timing": {"regions": REPEATS, "reported": "median region (max over ranks) of each kind",
+                   "order": "device-timed and end-to-end regions interleaved",
+                   "prewarm_s": PREWARM_S, "policy_activation": "relu",
+                   "ms_per_step_regions": [round(x * 1e3 / args.steps, 3) for x in sp["regions_s"]],
+                   "e2e_ms_per_step_regions": [round(x * 1e3 / args.steps, 3)
+                                               for x in sp["e2e_regions_s"]]},
+        "per_rank": sp["per_rank"],
         "decisions_per_s": sp["decisions"] / sp["elapsed"],
         "bad_status": sp["bad"],
         "e2e": {"value": sp["e2e_games"] / sp["e2e_elapsed"], "unit": "games/s",
-                "h2d_bytes_per_step": sp["h2d"], "d2h_bytes_per_step": sp["d2h"]},
+                "h2d_bytes_per_step": sp["h2d"], "d2h_bytes_per_step": sp["d2h"],
+                "clock": "host wall clock (perf_counter) around K steps, synchronised, "
+                         "max over ranks"},
         "roofline": {"kernel": ("policy MLP forward + sampling: whole-network CTA-pair kernel "
                                 "(fused_mlp_kernel with its sampling head)"
                                 if policy.launches_per_forward() == 1 else
@@ -509,13 +578,19 @@ def main():
         "extras": extras,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_games = 98304  # 10-20 s of host work
-        cpu = cpu_selfplay(cpu_games, args.arch, host_threads())
+        # The reference arm's measurement, repeated here: the same sample size, engine,
+        # actor class and noise; three samples (10-20 s of host work).
+        threads = host_threads()
+        actor, actor_desc = cpu_actor(args.arch)
+        cpu_selfplay(256, args.arch, threads, actor)
+        runs = [cpu_selfplay(CPU_SAMPLE_GAMES, args.arch, threads, actor) for _ in range(3)]
+        sec = sum(r["seconds"] for r in runs)
         out["cpu_baseline"] = {
-            "value": cpu["games_per_s"], "unit": "games/s", "cores": host_threads(),
-            "kind": "reference", "seconds": cpu["seconds"],
-            "sample": f"{cpu_games} seeded games (12345 + i) to settlement: reference engine "
-                      f"(oracle/_ref) + {args.arch} MLP on PyTorch-CPU fp32"}
+            "value": 3 * CPU_SAMPLE_GAMES / sec, "unit": "games/s", "cores": threads,
+            "kind": "reference", "seconds": sec,
+            "sample": f"3 x {CPU_SAMPLE_GAMES} seeded games (12345 + i) to settlement: the "
+                      f"reference engine (oracle/_ref), {actor_desc} on PyTorch-CPU, masked "
+                      f"Gumbel-max with Philox noise"}
     if rank == 0:
         print(json.dumps(out))
     if world > 1:

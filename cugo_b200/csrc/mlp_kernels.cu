@@ -33,6 +33,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "../../include/cugo_b200.h"
 #include "engine/driver.cuh"
 #include "gumbel.cuh"
@@ -1923,25 +1925,31 @@ namespace {
 constexpr int64_t kNoAllocRowsTimesHidden = int64_t{4} << 20;
 static __device__ __align__(256) __nv_bfloat16 g_noalloc_activations[2 * kNoAllocRowsTimesHidden];
 
-// Device address of g_noalloc_activations, looked up once per device (the name
-// is only a host-side stand-in in host code).
+// Device address of g_noalloc_activations, looked up once per device with that
+// device current (the name is only a host-side stand-in in host code).  The
+// entries are atomic: two host threads making their first call on one device at
+// the same time both look the address up and store the same value.  The cache
+// outlives a cudaDeviceReset (after which the module is loaded again and the
+// array may move), so resetting a device after its first call here is not
+// supported.
 void* noalloc_scratch(int* rc) {
-  static void* addr[64] = {};
+  constexpr int kMaxDevices = 64;
+  static std::atomic<void*> addr[kMaxDevices];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     *rc = CUGO_B200_ERR_LAUNCH;
     return nullptr;
   }
-  if (!addr[dev]) {
-    void* p = nullptr;
+  void* p = addr[dev].load(std::memory_order_acquire);
+  if (!p) {
     if (cudaGetSymbolAddress(&p, g_noalloc_activations) != cudaSuccess || !p) {
       *rc = CUGO_B200_ERR_LAUNCH;
       return nullptr;
     }
-    addr[dev] = p;
+    addr[dev].store(p, std::memory_order_release);
   }
   *rc = CUGO_B200_OK;
-  return addr[dev];
+  return p;
 }
 
 }  // namespace
@@ -1956,7 +1964,10 @@ int cugo_b200_policy_forward_noalloc(const void* x, int64_t ldx, int64_t m, int6
   if (m < 0 || inputs <= 0 || hidden <= 0 || blocks < 0 || outputs <= 0 || !weights ||
       (act != kActRelu && act != kActSilu))
     return CUGO_B200_ERR_ARG;
-  if (m * hidden > kNoAllocRowsTimesHidden) return CUGO_B200_ERR_CAPACITY;
+  // rows x hidden against the buffer without forming the product (which can wrap
+  // for caller-supplied sizes).
+  if (hidden > kNoAllocRowsTimesHidden || m > kNoAllocRowsTimesHidden / hidden)
+    return CUGO_B200_ERR_CAPACITY;
   if (m == 0) return CUGO_B200_OK;
   const int layers = 2 + 2 * blocks;
   for (int l = 0; l < layers; ++l)

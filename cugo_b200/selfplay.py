@@ -55,9 +55,22 @@ CHECK_EVERY = 4  # rounds between host reads of the running count (device-count 
 LOOKAHEAD = 2    # reads in flight: the host waits on a read only this many checks later
 
 
+def _log_actions(log: torch.Tensor, active: torch.Tensor, count: torch.Tensor,
+                 decision: torch.Tensor, actions: torch.Tensor) -> None:
+    """log[game, decision] = action for the first `count` running positions (count is
+    a device tensor: no host read).  Positions past it write a spare last element."""
+    flat = log.view(-1)
+    width = log.shape[1]
+    valid = torch.arange(active.numel(), device=active.device) < count
+    d = decision.index_select(0, active).long()
+    at = torch.where(valid & (d < width), active * width + d, flat.numel() - 1)
+    flat.index_put_((at,), actions[:active.numel()].to(flat.dtype))
+
+
 def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
                max_rounds: int = 128, timer: RoundTimer | None = None,
-               launches: list[int] | None = None) -> BatchResult:
+               launches: list[int] | None = None,
+               actions_log: torch.Tensor | None = None) -> BatchResult:
     """Plays games `game_index` (seed = seed_base + index, first player index & 1) to
     the end with policy-sampled actions.
 
@@ -69,7 +82,11 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     copies are queued), so the device never waits for the host.  Rounds launched
     after the count reached zero see zero rows and change nothing.  Otherwise the
     host reads the count after every round and sizes the next round's launches by
-    it."""
+    it.
+
+    actions_log (optional, for checking): int64 [games + 1, width]; entry [i, d]
+    receives the action game i chose at its decision d (the extra last row takes the
+    writes of positions past the running count)."""
     device = game_index.device
     g = game_index.numel()
     states = ext.create(game_index + seed_base, game_index & 1)
@@ -118,6 +135,9 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
                                                     seed_base)
         if timer:
             timer.stop(t0, live)
+        if actions_log is not None:
+            _log_actions(actions_log, active, c_in if fused else torch.tensor(live, device=device),
+                         decision, actions)
         ext.step_compact(states, active, actions, decision, reward0, nagari, bad, nxt, c_out,
                          scratch, m_dev=c_in if fused else None)
         n_launch += per_round

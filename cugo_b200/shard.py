@@ -31,3 +31,14 @@ def all_reduce(values: list[float], world: int, op: str = "sum",
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX)
     return t.tolist()
+
+
+def all_gather(values: list[float], world: int,
+               device: torch.device | str = "cuda") -> list[list[float]]:
+    """Every rank's list of statistics (float64), in rank order."""
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if world == 1:
+        return [t.tolist()]
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [p.tolist() for p in parts]

@@ -311,9 +311,11 @@ CUGO_B200_API int cugo_b200_pack_legal(const bool* legal, int64_t m, uint64_t* b
  * compiled into the library (16 MiB held on every GPU that loads it until the
  * process exits): m * hidden must not exceed 4,194,304 (e.g. 8,192 rows at hidden
  * 512), larger calls return CUGO_B200_ERR_CAPACITY.  The first call on a device
- * looks up that buffer's device address, so make it before any stream capture.
- * All calls share the buffer: calls that overlap on the GPU (other streams or
- * threads) race and must be serialised by the caller. */
+ * looks up that buffer's device address, so make it before any stream capture;
+ * the address is kept for the life of the process, so a device must not be reset
+ * (cudaDeviceReset) after its first call.  All calls share the buffer: calls that
+ * overlap on the GPU (other streams or threads) race and must be serialised by the
+ * caller. */
 CUGO_B200_API int cugo_b200_policy_forward_noalloc(const void* x, int64_t ldx, int64_t m,
                                                    int64_t inputs, int64_t hidden,
                                                    int32_t blocks, int64_t outputs,

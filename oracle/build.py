@@ -1,6 +1,9 @@
 """Builds oracle/_ref/libcugo_ref.so from the reference's sources (TEST
 INFRASTRUCTURE ONLY): `make -C oracle REF=<reference>`.  Needs the reference tree
-(present in the build container, absent on GPU boxes, which use the prebuilt file)."""
+(present in the build container, absent on GPU boxes, which use the prebuilt file).
+
+The reference tree is found through CUGO_REFERENCE, else as a directory named
+`reference` beside this repository's root."""
 from __future__ import annotations
 
 import os
@@ -8,7 +11,15 @@ import subprocess
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_REF = Path(os.environ.get("CUGO_REFERENCE", "/root/reference"))
+
+
+def reference_root() -> Path:
+    """The reference checkout: $CUGO_REFERENCE, else <repository root>/../reference."""
+    env = os.environ.get("CUGO_REFERENCE")
+    return Path(env) if env else HERE.parent.parent / "reference"
+
+
+DEFAULT_REF = reference_root()
 
 
 def reference_present(ref: Path = DEFAULT_REF) -> bool:

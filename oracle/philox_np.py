@@ -1,4 +1,6 @@
-"""Vectorised numpy Philox4x32-10 (Salmon et al., SC'11) for test expectations."""
+"""Vectorised numpy Philox4x32-10 (Salmon et al., SC'11) and the samplers' Gumbel noise
+(TEST AND CPU-BASELINE INFRASTRUCTURE ONLY: the expectations of tests/ and the noise
+of bench.py's CPU baseline; the product draws its noise on the device)."""
 from __future__ import annotations
 
 import numpy as np

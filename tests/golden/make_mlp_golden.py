@@ -17,7 +17,11 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("CUGO_REFERENCE", "/root/reference")) / "python"
+sys.path.insert(0, str(HERE.parents[1]))
+
+from oracle.build import reference_root  # noqa: E402
+
+REF = reference_root() / "python"
 
 
 def main() -> None:

@@ -27,8 +27,11 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("CUGO_REFERENCE", "/root/reference")) / "python"
 sys.path.insert(0, str(ROOT))
+
+from oracle.build import reference_root  # noqa: E402
+
+REF = reference_root() / "python"
 
 from oracle import ref  # noqa: E402
 

@@ -30,8 +30,11 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("CUGO_REFERENCE", "/root/reference")) / "python"
 sys.path.insert(0, str(ROOT))
+
+from oracle.build import reference_root  # noqa: E402
+
+REF = reference_root() / "python"
 sys.path.insert(0, str(ROOT / "tests"))
 
 from oracle import ref  # noqa: E402

@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from tests.philox_np import philox4x32_10
+from oracle.philox_np import philox4x32_10
 
 HAND0, HAND1, STOCK, RNG, HELD0, HELD1, REV0, REV1 = 0, 1, 3, 6, 20, 21, 22, 23
 

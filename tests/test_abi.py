@@ -72,3 +72,18 @@ def test_loader_requires_cuda(monkeypatch):
     monkeypatch.setattr(ext_mod, "_EXT", None)
     with pytest.raises(RuntimeError, match="PyTorch CUDA is not available"):
         ext_mod.load_extension()
+
+
+def test_noalloc_forward_capacity_check_does_not_wrap():
+    """Sizes whose product wraps a 64-bit integer (2^33 rows x 2^31 hidden) are
+    refused as over capacity before anything is read or launched, like any batch
+    larger than the built-in activation buffer."""
+    fn = load_library().cugo_b200_policy_forward_noalloc
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+    fn.argtypes = [vp, i64, i64, i64, i64, i32, i64, vp, vp, i32, vp, i64, vp, vp]
+    fn.restype = ctypes.c_int
+    weights = (ctypes.c_void_p * 8)(*([0x1000] * 8))
+    w = ctypes.cast(weights, ctypes.c_void_p)
+    err_capacity = -4
+    for m, hidden in ((1 << 33, 1 << 31), (1 << 62, 4), (1, (4 << 20) + 1), ((4 << 20) // 512 + 1, 512)):
+        assert fn(None, 720, m, 720, hidden, 3, 180, w, None, 1, None, 180, None, None) == err_capacity

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.philox_np import gumbel_noise
+from oracle.philox_np import gumbel_noise
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda:0")

@@ -107,3 +107,28 @@ def test_device_count_loop_equals_the_synchronised_loop(ext):
     assert (a.decisions, a.rounds, a.bad_status) == (b.decisions, b.rounds, b.bad_status)
     assert torch.equal(a.reward0, b.reward0) and torch.equal(a.nagari, b.nagari)
     assert timer.total_ms()[2] == a.decisions  # the timer saw every round's rows
+
+
+@pytest.mark.parametrize("games_from", [0, 500000])
+def test_play_batch_replays_on_the_oracle(ext, oracle, games_from):
+    """play_batch's recorded actions, replayed game by game on the reference's own
+    engine (oracle/_ref): identical final rewards, nagari flags and decision counts,
+    and no bad status on either side."""
+    import numpy as np
+
+    from cugo_b200.policy import ResidualMlpPolicy
+    from cugo_b200.selfplay import play_batch
+    from tests.replay import replay_on_oracle
+    pol = ResidualMlpPolicy(512, 3, "relu", device=DEV, seed=0)
+    g = 8192
+    games = torch.arange(games_from, games_from + g, device=DEV)
+    log = torch.full((g + 1, 64), -1, dtype=torch.int64, device=DEV)
+    res = play_batch(ext, pol, games, actions_log=log)
+    assert res.bad_status == 0
+    per_game = int((log[:g] >= 0).sum())
+    assert per_game == res.decisions
+    r0, nag, dec, bad = replay_on_oracle(oracle, games.cpu().numpy(), log[:g].cpu().numpy())
+    assert bad == 0
+    assert int(dec.sum()) == res.decisions
+    assert np.array_equal(r0, res.reward0.cpu().numpy())
+    assert np.array_equal(nag, res.nagari.cpu().numpy())
