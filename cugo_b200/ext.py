@@ -69,6 +69,13 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_layernorm": [_VP, _I64, _VP, _VP, _I64, ctypes.c_float, _VP, _I64, _I64, _VP],
     "cugo_b200_event_embed": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _VP, _I64, _VP],
     "cugo_b200_start_embed": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _VP, _I64, _VP],
+    "cugo_b200_record_transitions": [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP,
+                                     _VP, _VP, _I32, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
+                                     _VP, _VP, _VP, _VP],
+    "cugo_b200_stock_planes_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _I32, _VP],
+    "cugo_b200_wave_tail": [_I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
+                            _VP, _VP, _VP, _VP, _VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP,
+                            _VP, _VP, _VP, _I64, _VP],
 }
 _CONSTANTS = {
     "FEATURE_COUNT": "cugo_b200_feature_count",
@@ -428,6 +435,67 @@ class CugoB200Extension:
                 _ptr(states), states.size(0), _ptr(env_ids), _ptr(actions), m, _ptr(decision),
                 _ptr(reward0), _ptr(nagari), _ptr(bad), _ptr(next_ids), _ptr(next_count),
                 _ptr(scratch), _ptr(m_dev), self._stream(states.device)), "step_compact")
+
+    def record_transitions(self, states, active, m_dev, features, legal_bits, players, actions,
+                           logp, learner, sizes, parity: int, store: dict, overflow) -> None:
+        """Appends one collection round to a device-resident transition store (see the C
+        declaration): round row i < min(active.numel(), *m_dev) goes to store row
+        sizes[parity] + i; sizes[parity ^ 1] gets the new size.  store: bf16
+        "features" [cap, 720], bool "legal" [cap, 179], int64 "actions", "opp_hand",
+        "stock", "env_ids", "seat", fp32 "logp", bool "learner" [cap]."""
+        self._states(states)
+        m = active.numel()
+        cap = store["actions"].numel()
+        if features.dtype != torch.bfloat16 or features.stride(1) != 1 or features.shape[0] < m:
+            raise RuntimeError("record_transitions: features bf16 [>= m, 720] with unit stride")
+        if sizes.dtype != torch.int64 or sizes.numel() != 2:
+            raise RuntimeError("record_transitions: sizes int64 [2]")
+        with torch.cuda.device(states.device):
+            _check(self._lib.cugo_b200_record_transitions(
+                _ptr(states), states.size(0), _ptr(active), m, _ptr(m_dev), _ptr(features),
+                features.stride(0), _ptr(legal_bits), _ptr(players), _ptr(actions), _ptr(logp),
+                _ptr(learner), _ptr(sizes), parity, cap, _ptr(store["features"]),
+                _ptr(store["legal"]), _ptr(store["actions"]), _ptr(store["logp"]),
+                _ptr(store["opp_hand"]), _ptr(store["stock"]), _ptr(store["env_ids"]),
+                _ptr(store["seat"]), _ptr(store["learner"]), _ptr(overflow),
+                self._stream(states.device)), "record_transitions")
+
+    def stock_planes_bf16(self, states, env_ids, rows: torch.Tensor, first_column: int = 770) -> None:
+        """Sets the one-hot planes of the next 8 stock draws (columns first_column ..
+        + 400) in bf16 critic rows written by observe_critic_bf16 for the same ids."""
+        self._states(states)
+        _check_cuda_1d(env_ids, torch.int64, "env_ids")
+        if rows.dtype != torch.bfloat16 or rows.stride(1) != 1 or rows.shape[0] != env_ids.numel():
+            raise RuntimeError("stock_planes_bf16: rows bf16 [m, >= first_column + 400]")
+        with torch.cuda.device(states.device):
+            _check(self._lib.cugo_b200_stock_planes_bf16(
+                _ptr(states), states.size(0), _ptr(env_ids), env_ids.numel(), _ptr(rows),
+                rows.stride(0), first_column, self._stream(states.device)), "stock_planes_bf16")
+
+    def wave_tail(self, obs_done, obs_status, players, actions, logp, step_out, wave: dict,
+                  records: dict | None = None, learner: torch.Tensor | None = None) -> None:
+        """The end of one sequence self-play decision step (see the C declaration).
+        step_out: step_events_indexed's [reward0, done, nagari, status, committed,
+        events]; wave: the wave's device state ("final_reward0", "final_nagari",
+        "finished", "bad", "running", "events", "count", "cache_length", "decision",
+        "step_index"); records: [max_steps, w] "actions", "seat", "count", "logp",
+        "valid" (optional); learner: bool [w], whether the learner chose each action
+        (optional)."""
+        w = actions.numel()
+        reward0, new_done, nagari, status, committed, events = step_out
+        rec = records or {}
+        max_steps = rec["actions"].shape[0] if records else 0
+        with torch.cuda.device(actions.device):
+            _check(self._lib.cugo_b200_wave_tail(
+                w, _ptr(obs_done), _ptr(obs_status), _ptr(players), _ptr(actions), _ptr(logp),
+                _ptr(reward0), _ptr(new_done), _ptr(nagari), _ptr(status), _ptr(committed),
+                _ptr(events), _ptr(learner), _ptr(wave["final_reward0"]), _ptr(wave["final_nagari"]),
+                _ptr(wave["finished"]), _ptr(wave["bad"]), _ptr(wave["running"]),
+                _ptr(wave["events"]), wave["events"].shape[1], _ptr(wave["count"]),
+                _ptr(wave["cache_length"]), _ptr(wave["decision"]), _ptr(wave["step_index"]),
+                _ptr(rec.get("actions")), _ptr(rec.get("seat")), _ptr(rec.get("count")),
+                _ptr(rec.get("logp")), _ptr(rec.get("valid")), max_steps,
+                self._stream(actions.device)), "wave_tail")
 
     def pack_legal(self, legal: torch.Tensor) -> torch.Tensor:
         """bool [m, 179] legal masks as int64 [m, 3] bit words."""

@@ -246,20 +246,33 @@ def fused_actor(hidden: int = 512, blocks: int = 3) -> FusedResidualMlp:
     return FusedResidualMlp(FEATURES, ACTIONS, hidden, blocks, "silu", zero_out=True)
 
 
+STOCK_FEATURES = 8 * 50  # one-hot planes of the next 8 stock draws
+
+
 def fused_critic(hidden: int = 512, blocks: int = 3, value_bins: int = 0,
-                 value_top: float = 640.0) -> FusedResidualMlp:
-    """OracleCritic's shape without stock planes: 770 inputs -> one value (or
-    value_bins logits of the return distribution)."""
-    return FusedResidualMlp(FEATURES + ORACLE_FEATURES, value_bins or 1, hidden, blocks, "silu",
-                            squeeze=not value_bins, value_bins=value_bins, value_top=value_top)
+                 value_top: float = 640.0, stock: bool = False) -> FusedResidualMlp:
+    """OracleCritic's shape (python/cugo_ppo_nets50.py:67-91): 770 inputs, or 1,170
+    with the stock planes -> one value (or value_bins logits of the return
+    distribution)."""
+    inputs = FEATURES + ORACLE_FEATURES + (STOCK_FEATURES if stock else 0)
+    net = FusedResidualMlp(inputs, value_bins or 1, hidden, blocks, "silu",
+                           squeeze=not value_bins, value_bins=value_bins, value_top=value_top)
+    net.stock = stock
+    return net
 
 
-def critic_input(features: torch.Tensor, opp_hand: torch.Tensor) -> torch.Tensor:
-    """[features, one-hot plane of the opponent's hand] as bf16 (the reference's
-    _critic_input, python/cugo_ppo50.py:478-482, without stock planes)."""
-    bits = torch.arange(ORACLE_FEATURES, device=opp_hand.device)
-    plane = ((opp_hand.view(-1, 1) >> bits) & 1).to(torch.bfloat16)
-    return torch.cat((features.to(torch.bfloat16), plane), 1)
+def critic_input(features: torch.Tensor, opp_hand: torch.Tensor,
+                 stock: torch.Tensor | None = None) -> torch.Tensor:
+    """[features, one-hot plane of the opponent's hand, (one-hot planes of the next
+    8 stock draws, stock_indexed's packing, 0xFF = none)] as bf16 (the reference's
+    _critic_input, python/cugo_ppo50.py:478-482)."""
+    dev = opp_hand.device
+    bits = torch.arange(ORACLE_FEATURES, device=dev)
+    parts = [features.to(torch.bfloat16), ((opp_hand.view(-1, 1) >> bits) & 1).to(torch.bfloat16)]
+    if stock is not None:
+        cards = (stock.view(-1, 1) >> torch.arange(0, 64, 8, device=dev)) & 0xFF
+        parts.append((cards.unsqueeze(-1) == bits).flatten(1).to(torch.bfloat16))
+    return torch.cat(parts, 1)
 
 
 def allreduce_gradients(params: list[torch.Tensor], world: int) -> None:
@@ -286,6 +299,11 @@ class Minibatch:
     opp_hand: torch.Tensor  # int64 [B]
     adv: torch.Tensor       # fp32 [B]
     ret: torch.Tensor       # fp32 [B]
+    stock: torch.Tensor | None = None  # int64 [B], for a critic with stock planes
+
+    def tensors(self) -> tuple[torch.Tensor, ...]:
+        return tuple(t for t in (self.features, self.legal, self.actions, self.logp_old,
+                                 self.opp_hand, self.adv, self.ret, self.stock) if t is not None)
 
 
 class PpoStep:
@@ -307,7 +325,8 @@ class PpoStep:
 
     def losses(self, mb: Minibatch):
         logits = self.actor(mb.features).float()
-        value = self.critic(critic_input(mb.features, mb.opp_hand)).float()
+        stock = mb.stock if getattr(self.critic, "stock", False) else None
+        value = self.critic(critic_input(mb.features, mb.opp_hand, stock)).float()
         log_probs = torch.log_softmax(logits.masked_fill(~mb.legal, -1.0e30), dim=1)
         new_logp = log_probs.gather(1, mb.actions.unsqueeze(1)).squeeze(1)
         log_ratio = new_logp - mb.logp_old
@@ -346,9 +365,7 @@ class GraphedPpoStep:
 
     def __init__(self, step: PpoStep, template: Minibatch) -> None:
         self.step = step
-        self.static = Minibatch(*(t.clone() for t in (
-            template.features, template.legal, template.actions, template.logp_old,
-            template.opp_hand, template.adv, template.ret)))
+        self.static = Minibatch(*(t.clone() for t in template.tensors()))
         self.graph: torch.cuda.CUDAGraph | None = None
 
     def _capture(self) -> None:
@@ -381,11 +398,7 @@ class GraphedPpoStep:
         if self.step.world > 1:
             self.step.step(mb)
             return
-        for dst, src in zip((self.static.features, self.static.legal, self.static.actions,
-                             self.static.logp_old, self.static.opp_hand, self.static.adv,
-                             self.static.ret),
-                            (mb.features, mb.legal, mb.actions, mb.logp_old, mb.opp_hand, mb.adv,
-                             mb.ret)):
+        for dst, src in zip(self.static.tensors(), mb.tensors(), strict=True):
             dst.copy_(src)
         if self.graph is None:
             self._capture()

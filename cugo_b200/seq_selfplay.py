@@ -1,20 +1,33 @@
-"""GPU-resident self-play of the event-sequence policy in fixed-size waves.
+"""GPU-resident self-play of the event-sequence policy in fixed-size waves, the
+driver behind the reference's WaveCollector (python/cugo_seq_selfplay50.py:36-238),
+on the native engine and decode kernels.
 
-The driver of the reference's WaveCollector (python/cugo_seq_selfplay50.py:36-238),
-on the native engine and decode kernels: every tensor a decision step touches has
-a fixed shape (finished games stay in the batch, masked), so one decision step —
-observe, query token through the cached transformer, readout, Gumbel-max sample,
-engine step, event record, event tokens for both seats into the KV cache — is
-captured once as a CUDA graph and replayed; the wave reset (deal, opening tokens)
-is a second graph.  The host replays graphs and checks every fourth step from the
-16th whether the wave has finished (the reference's cadence).
+A wave is `wave` games played together in fixed-shape buffers (finished games stay
+in the batch and are skipped by the kernels' bookkeeping).  Two CUDA graphs:
 
-Differences from the reference driver, by design of the benchmark: games are
-dealt by the shared driver definition (game i: seed seed_base + i, first player
-i & 1) and actions are sampled with the Philox Gumbel noise of
-cugo_b200_sample_actions (counter {game, decision}) instead of torch.rand_like,
-so runs are reproducible; the pool opponent of the reference (a frozen second
-network for a subset of games) is not part of this driver.
+  reset  deal the wave's games, their opening records and opening tokens (both
+         seats' caches; the pool opponent's cache for pool games), zero the logs
+  step   observe every game into the query rows; the query token through the
+         cached transformer on the mover's cache row and the readout (and, in pool
+         games where the opponent moves, the opponent network on its own cache);
+         Gumbel-max sampling; the engine step with its event words; the event's
+         tokens into both seats' caches (and the opponent's); then one wave-tail
+         kernel does the rest of the step's bookkeeping on the device: bad-status
+         counts, final rewards, the event log, the per-decision records, the cache
+         lengths, event counts and decision counters, and the wave's running count
+
+The host replays the step graph and, every 4 steps, queues a copy of the running
+count into pinned memory behind an event; it reads a copy once its event has
+completed (or two newer copies are queued), so replays continue while earlier
+copies are in flight, and the wave ends at the first copy that shows no running
+game.  Steps replayed after the last game ended change nothing.
+
+Sampling uses the Philox Gumbel noise of cugo_b200_sample_actions (counter {game,
+decision}) instead of torch.rand_like, so a wave is reproducible.  Games are dealt
+by the shared driver definition (game i: seed seed_base + i, first player i & 1).
+Pool games are the first `pool_games` of each wave; there the learner plays seat
+(i >> 1) & 1 of game i and the frozen opponent the other seat, and only the
+learner's decisions are marked valid in the records.
 """
 from __future__ import annotations
 
@@ -22,11 +35,17 @@ import torch
 
 from .seq import MAX_EVENTS, QUERY_LD, SeqDecoder
 
+POLL_EVERY = 4
+LOOKAHEAD = 2
+
 
 class SeqWaveSelfPlay:
     def __init__(self, decoder: SeqDecoder, wave: int = 4096, max_steps: int = 64,
-                 seed_base: int = 12345, record: bool = True, graphs: bool = True) -> None:
+                 seed_base: int = 12345, record: bool = True, graphs: bool = True,
+                 opponent: SeqDecoder | None = None, pool_games: int = 0) -> None:
         self.dec, self.ext = decoder, decoder.ext
+        self.opponent = opponent
+        self.pool = min(pool_games, wave) if opponent is not None else 0
         dev = decoder.device
         self.w, self.max_steps, self.seed_base, self.record = wave, max_steps, seed_base, record
         w = wave
@@ -35,87 +54,124 @@ class SeqWaveSelfPlay:
         self.seats2 = torch.cat((torch.zeros(w, **i64), torch.ones(w, **i64)))
         self.game0 = torch.zeros(1, **i64)
         self.states = torch.zeros((w, self.ext.STATE_BYTES), dtype=torch.uint8, device=dev)
-        self.events = torch.zeros((w, MAX_EVENTS, self.ext.EVENT_WORDS), **i64)
-        self.count = torch.zeros(w, **i64)
         self.start = torch.zeros((w, self.ext.START_WORDS), **i64)
-        self.decision = torch.zeros(w, dtype=torch.int32, device=dev)
         self.cache = decoder.new_cache(2 * w)  # row = seat * w + game
         self.query = torch.zeros((w, QUERY_LD), dtype=torch.bfloat16, device=dev)
-        self.final_reward0 = torch.zeros(w, device=dev)
-        self.final_nagari = torch.zeros(w, dtype=torch.bool, device=dev)
-        self.finished = torch.zeros(w, dtype=torch.bool, device=dev)
         self.started = torch.zeros(w, dtype=torch.bool, device=dev)
-        self.bad = torch.zeros((), **i64)
-        self.step_index = torch.zeros(1, **i64)
-        s = max_steps
+        # Device state the wave-tail kernel updates.
+        self.state = {
+            "final_reward0": torch.zeros(w, device=dev),
+            "final_nagari": torch.zeros(w, dtype=torch.bool, device=dev),
+            "finished": torch.zeros(w, dtype=torch.bool, device=dev),
+            "bad": torch.zeros(1, **i64),
+            "running": torch.zeros(1, dtype=torch.int32, device=dev),
+            "events": torch.zeros((w, MAX_EVENTS, self.ext.EVENT_WORDS), **i64),
+            "count": torch.zeros(w, **i64),
+            "cache_length": self.cache.length,
+            "decision": torch.zeros(w, dtype=torch.int32, device=dev),
+            "step_index": torch.zeros(1, **i64),
+        }
+        self.records = None
         if record:  # what the trainer stores per decision (python/cugo_seq_selfplay50.py:68-75)
+            s = max_steps
             self.rec_query = torch.zeros((s, w, QUERY_LD), dtype=torch.bfloat16, device=dev)
-            self.rec_logp = torch.zeros((s, w), device=dev)
-            self.rec_long = {k: torch.zeros((s, w), **i64) for k in ("actions", "seat", "count")}
-            self.rec_valid = torch.zeros((s, w), dtype=torch.bool, device=dev)
+            self.records = {"actions": torch.zeros((s, w), **i64), "seat": torch.zeros((s, w), **i64),
+                            "count": torch.zeros((s, w), **i64),
+                            "logp": torch.zeros((s, w), device=dev),
+                            "valid": torch.zeros((s, w), dtype=torch.bool, device=dev)}
+        if self.pool:
+            p = self.pool
+            self.opp_cache = opponent.new_cache(p)  # row = pool game (the opponent's seat)
+            self.learner_seat = (self.ids[:p] >> 1) & 1
+            self.opp_seat = 1 - self.learner_seat
+            self.learner = torch.ones(w, dtype=torch.bool, device=dev)
         self.graphs = graphs
         self._reset_graph: torch.cuda.CUDAGraph | None = None
         self._step_graph: torch.cuda.CUDAGraph | None = None
+        pin = dev.type == "cuda"
+        self._seen = torch.zeros(LOOKAHEAD + 1, dtype=torch.int32, pin_memory=pin)
 
-    # -- the two captured bodies -------------------------------------------------
+    # -- readable views of the wave's device state -----------------------------------
+    @property
+    def events(self) -> torch.Tensor:
+        return self.state["events"]
+
+    @property
+    def count(self) -> torch.Tensor:
+        return self.state["count"]
+
+    @property
+    def final_reward0(self) -> torch.Tensor:
+        return self.state["final_reward0"]
+
+    @property
+    def final_nagari(self) -> torch.Tensor:
+        return self.state["final_nagari"]
+
+    @property
+    def finished(self) -> torch.Tensor:
+        return self.state["finished"]
+
+    @property
+    def decision(self) -> torch.Tensor:
+        return self.state["decision"]
+
+    # -- the two captured bodies -------------------------------------------------------
     def _reset(self) -> None:
-        ext, dec, w = self.ext, self.dec, self.w
+        ext, dec, st = self.ext, self.dec, self.state
         games = self.game0 + self.ids
         self.states.copy_(ext.create(self.seed_base + games, games & 1))
         self.start.copy_(ext.start(self.states))
-        self.events.zero_()
-        self.count.zero_()
-        self.decision.zero_()
+        for name in ("events", "count", "decision", "final_reward0", "final_nagari", "bad",
+                     "step_index"):
+            st[name].zero_()
         done = ext.observe_query_bf16(self.states, self.ids, query=self.query)[3]
         self.started.copy_(~done)
-        self.finished.copy_(done)
-        self.final_reward0.zero_()
-        self.final_nagari.zero_()
-        self.bad.zero_()
-        self.step_index.zero_()
-        if self.record:
-            self.rec_valid.zero_()
+        st["finished"].copy_(done)
+        st["running"].copy_(self.started.sum())
+        if self.records is not None:
+            self.records["valid"].zero_()
         self.cache.length.zero_()
-        x = dec.start_token(self.start, self.seats2)
-        dec.cached_step(self.cache, x, slots=1)
+        dec.cached_step(self.cache, dec.start_token(self.start, self.seats2), slots=1)
         self.cache.length.fill_(1)
+        if self.pool:
+            p = self.pool
+            self.opp_cache.length.zero_()
+            opp = self.opponent
+            opp.cached_step(self.opp_cache, opp.start_token(self.start[:p], self.opp_seat), slots=1)
+            self.opp_cache.length.fill_(1)
 
     def _step(self) -> None:
-        ext, dec, w, ids = self.ext, self.dec, self.w, self.ids
+        ext, dec, w, ids, st = self.ext, self.dec, self.w, self.ids, self.state
         query, legal, players, done, status = ext.observe_query_bf16(self.states, ids, query=self.query)
-        active = ~done
-        self.bad += (active & ((status != 0) | ~legal.any(1))).sum()
-        player = players.long()
-        # One query per game on the mover's cache row.
+        seat = players.long() & 1
         x = dec.query_token(query)
-        dec.cached_step(self.cache, x, rows=(player & 1) * w + ids)
+        dec.cached_step(self.cache, x, rows=seat * w + ids)
         logits = dec.readout(x)
-        actions, logp = ext.sample_actions(logits, legal, self.game0 + ids, self.decision,
+        if self.pool:
+            p, opp = self.pool, self.opponent
+            xo = opp.query_token(query[:p])
+            opp.cached_step(self.opp_cache, xo)
+            theirs = seat[:p] != self.learner_seat
+            logits[:p] = torch.where(theirs.unsqueeze(1), opp.readout(xo)[:, :logits.shape[1]],
+                                     logits[:p])
+            self.learner[:p] = ~theirs
+        actions, logp = ext.sample_actions(logits, legal, self.game0 + ids, st["decision"],
                                            seed_base=self.seed_base)
-        if self.record:
-            at = self.step_index
-            self.rec_query.index_copy_(0, at, query.unsqueeze(0))
-            self.rec_logp.index_copy_(0, at, logp.unsqueeze(0))
-            for name, value in (("actions", actions), ("seat", player), ("count", self.count)):
-                self.rec_long[name].index_copy_(0, at, value.unsqueeze(0))
-            self.rec_valid.index_copy_(0, at, active.unsqueeze(0))
-        reward0, new_done, nagari, step_status, committed, events = ext.step_events_indexed(
-            self.states, ids, actions)
-        self.bad += (active & (step_status != 0)).sum()
-        finished_now = active & new_done
-        self.final_reward0.copy_(torch.where(finished_now, reward0, self.final_reward0))
-        self.final_nagari |= finished_now & nagari
-        self.finished |= finished_now
-        commit = active & committed
-        slot = self.count.clamp_max(MAX_EVENTS - 1)
-        self.events[ids, slot] = torch.where(commit.unsqueeze(1), events, self.events[ids, slot])
-        # The event's token for both seats (row i of 2w reads event i % w).
-        x2 = dec.event_token(events, self.seats2, self.count)
-        dec.cached_step(self.cache, x2)
-        self.cache.length += commit.repeat(2).long()
-        self.count += commit.long()
-        self.decision += active.int()
-        self.step_index += 1
+        if self.records is not None:
+            self.rec_query.index_copy_(0, st["step_index"].clamp_max(self.max_steps - 1),
+                                       query.unsqueeze(0))
+        step_out = ext.step_events_indexed(self.states, ids, actions)
+        events = step_out[5]
+        # The event's tokens for both seats (row i of 2w reads event i % w), at the
+        # games' event counts before this step.
+        dec.cached_step(self.cache, dec.event_token(events, self.seats2, st["count"]))
+        if self.pool:
+            p, opp = self.pool, self.opponent
+            opp.cached_step(self.opp_cache, opp.event_token(events[:p], self.opp_seat, st["count"][:p]))
+            self.opp_cache.length += (step_out[4][:p] & ~done[:p]).long()
+        ext.wave_tail(done, status, players, actions, logp, step_out, st, self.records,
+                      learner=self.learner if self.pool else None)
 
     def _capture(self) -> None:
         if self._step_graph is not None:
@@ -134,9 +190,9 @@ class SeqWaveSelfPlay:
         with torch.cuda.graph(self._step_graph):
             self._step()
 
-    # -- one wave ----------------------------------------------------------------
+    # -- one wave ------------------------------------------------------------------------
     def play_wave(self, game0: int) -> int:
-        """Plays games game0 .. game0 + wave - 1 to the end; returns the steps taken."""
+        """Plays games game0 .. game0 + wave - 1 to the end; returns the steps run."""
         self.game0.fill_(game0)
         if self.graphs:
             self._capture()
@@ -144,23 +200,38 @@ class SeqWaveSelfPlay:
             self._reset_graph.replay()
         else:
             self._reset()
-        steps = self.max_steps
-        for k in range(self.max_steps):
-            if self.graphs:
-                self._step_graph.replay()
-            else:
-                self._step()
-            if (k + 1) % 4 == 0 and k + 1 >= 16 and bool(self.finished.all()):
-                steps = k + 1
+        pending: list[tuple[torch.cuda.Event, int, int]] = []
+        copies, steps, ended = 0, 0, None
+        for k in range(1, self.max_steps + 1):
+            self._step_graph.replay() if self.graphs else self._step()
+            steps = k
+            if k % POLL_EVERY:
+                continue
+            slot = copies % (LOOKAHEAD + 1)
+            copies += 1
+            self._seen[slot:slot + 1].copy_(self.state["running"], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            pending.append((ev, slot, k))
+            while pending and (len(pending) > LOOKAHEAD or pending[0][0].query()):
+                ev0, slot0, at = pending.pop(0)
+                ev0.synchronize()
+                if int(self._seen[slot0]) == 0:
+                    ended = at
+                    break
+            if ended is not None:
                 break
-        else:
-            if not bool(self.finished.all()):
-                raise RuntimeError(f"games did not finish within {self.max_steps} steps")
-        if int(self.bad):
-            raise RuntimeError(f"{int(self.bad)} bad observe/step results in a wave")
-        if int(self.count.max()) > MAX_EVENTS:
+        torch.cuda.synchronize()
+        st = self.state
+        running, bad, longest = (int(v) for v in torch.stack(
+            (st["running"][0].long(), st["bad"][0], st["count"].max())).tolist())
+        if running:
+            raise RuntimeError(f"games did not finish within {self.max_steps} steps")
+        if bad:
+            raise RuntimeError(f"{bad} bad observe/step results in a wave")
+        if longest > MAX_EVENTS:
             raise RuntimeError("event log overflow")
-        return steps
+        return ended if ended is not None else steps
 
     def release(self) -> None:
         self._reset_graph = None

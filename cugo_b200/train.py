@@ -1,21 +1,32 @@
-"""One PPO iteration of train_ppo50.py on the native kernels: self-play collection with
-recorded transitions, then the update (python/cugo_ppo50.py:321-450 collect,
-:484-509 gae_advantages, :514-745 PpoUpdater.update), same arguments and results
-for the plain policy target.
+"""One PPO iteration of train_ppo50.py on the native kernels: self-play collection
+into a device-resident transition store, then the update.  The entry points keep
+the reference's names and arguments (python/cugo_ppo50.py: RolloutStorage :273,
+collect :321, gae_advantages :484, the update of PpoUpdater :514-745 for the plain
+policy target), so train_ppo50.py's loop can call them.
 
-collect    every decision round observes the running games (bf16 features, bool legal
-           masks), runs the actor and samples its action in one fused kernel where the
-           actor is a hidden-512 FusedResidualMlp (masked Gumbel-max from Philox
-           instead of torch.multinomial over the softmax: the same distribution,
-           reproducible), records features, legal mask, action, behaviour log p, the
-           opponent's hand, game and seat, and steps the games; the returns are the
-           final scores from each row's seat, divided by reward_scale.
-update     critic values of every row (the fused inference path), GAE(lambda) along
-           each (game, seat) sequence, then `epochs` passes of shuffled minibatches
-           through the PPO step captured as a CUDA graph (GraphedPpoStep), stopping
-           early when the minibatch KL exceeds 1.5 x target_kl (checked every 8).
-The pool opponent, all-action Q targets and belief head of the reference are not
-part of this iteration.
+Collection.  The games of an iteration stay in one fixed batch of rows; the running
+ones are a device-resident list (rounds.RunningSet) that the step kernel rewrites
+every round.  A decision round is:
+  observe        bf16 features and legal bit words of the running games
+  act            the learner's sampled actions (masked Gumbel-max; one fused
+                 kernel for a hidden-512 actor), and in pool games the frozen
+                 opponent's actions where it is to move
+  record         one kernel appends the round to the store at its device-resident
+                 size: features, legal mask, action, log p, the opponent's hand and
+                 the next stock draws read from the game row, game and seat, and
+                 whether the learner moved
+  step           the step kernel with the round's bookkeeping (decision counters,
+                 final rewards, the next running list)
+With a fused actor nothing in a round waits for the host; the host polls copies of
+the running count and of the store size every 4 rounds, and grows the store when a
+copy shows it could fill before the next poll.  Opponent rows are dropped from the
+store once, after the last round.  Sampling noise is Philox Gumbel noise addressed
+by (deal seed, the game's decision count) instead of torch.multinomial: the same
+distribution, reproducible.
+
+GAE runs over a dense [sequences, longest] matrix of TD residuals (rows grouped
+by (game, seat)), the backward recursion taking one column of every sequence at
+a time.
 """
 from __future__ import annotations
 
@@ -30,16 +41,21 @@ from torch import nn
 from .evaluate import make_seeds
 from .ext import load_extension
 from .ppo import GraphedPpoStep, Minibatch, PpoStep, critic_input
+from .rounds import RunningSet, choose_actions, fused_sampler_params
+
+DONE_BYTE = 239  # TorchEnv50::done: a deal can end the game before any decision
+CHECK_EVERY = 4
 
 
 @dataclass
 class Rollout:
-    """python/cugo_ppo50.py:52-66 (without the stock planes and pool statistics)."""
+    """python/cugo_ppo50.py:52-66, with the rows' games and seats."""
     features: torch.Tensor  # bf16 [N, 720]
     legal: torch.Tensor     # bool [N, 179]
     actions: torch.Tensor   # int64 [N]
     logp: torch.Tensor      # fp32 [N], behaviour log-prob
     opp_hand: torch.Tensor  # int64 [N]
+    stock: torch.Tensor     # int64 [N], the next 8 stock draws (stock_indexed's packing)
     env_ids: torch.Tensor   # int64 [N], the row's game
     seat: torch.Tensor      # int64 [N]
     returns: torch.Tensor   # fp32 [N], scaled final score for the acting player
@@ -48,155 +64,199 @@ class Rollout:
     nagari: int
     decision_steps: int
     mean_abs_reward0: float
+    learner_score: float = float("nan")  # mean scaled score of learner seats in pool games
 
 
 class RolloutStorage:
-    """Fixed transition buffers reused every iteration, grown by a quarter when a
-    collection outgrows them (python/cugo_ppo50.py:273-318)."""
+    """Device-resident transition store (the reference's RolloutStorage name and
+    constructor).  Its size lives in device memory, written by the record kernel
+    round by round; `size` is the host copy after a collection.  capacity grows by
+    a quarter (at least the needed rows) when a collection would outgrow it."""
 
-    def __init__(self, capacity: int, device: torch.device) -> None:
-        self.device, self.size, self.capacity = device, 0, 0
-        self.tensors: tuple[torch.Tensor, ...] = ()
-        self._allocate(capacity)
+    COLUMNS = (("features", torch.bfloat16, 720), ("legal", torch.bool, 179),
+               ("actions", torch.int64, 0), ("logp", torch.float32, 0),
+               ("opp_hand", torch.int64, 0), ("stock", torch.int64, 0),
+               ("env_ids", torch.int64, 0), ("seat", torch.int64, 0),
+               ("learner", torch.bool, 0))
 
-    def _allocate(self, capacity: int) -> None:
-        d, old = self.device, self.tensors
-        self.tensors = (
-            torch.empty((capacity, 720), dtype=torch.bfloat16, device=d),
-            torch.empty((capacity, 179), dtype=torch.bool, device=d),
-            torch.empty(capacity, dtype=torch.int64, device=d),
-            torch.empty(capacity, dtype=torch.float32, device=d),
-            torch.empty(capacity, dtype=torch.int64, device=d),
-            torch.empty(capacity, dtype=torch.int64, device=d),
-            torch.empty(capacity, dtype=torch.int64, device=d),
-        )
-        for new_t, old_t in zip(self.tensors, old):
-            new_t[:self.size].copy_(old_t[:self.size])
+    def __init__(self, capacity: int, device: torch.device, all_actions: bool = False) -> None:
+        if all_actions:
+            raise ValueError("all-action Q targets are not part of this collection")
+        self.device = torch.device(device)
+        self.all_actions = False
+        self.capacity, self.size = 0, 0
+        self.sizes = torch.zeros(2, dtype=torch.int64, device=self.device)
+        self.overflow = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.parity = 0
+        self.columns: dict[str, torch.Tensor] = {}
+        self.reserve(capacity)
+
+    def reserve(self, capacity: int, keep: int = 0) -> None:
+        """Reallocates every column with `capacity` rows, keeping the first `keep`."""
+        old = self.columns
+        self.columns = {}
+        for name, dtype, width in self.COLUMNS:
+            shape = (capacity, width) if width else (capacity,)
+            col = torch.empty(shape, dtype=dtype, device=self.device)
+            if keep:
+                col[:keep].copy_(old[name][:keep])
+            self.columns[name] = col
         self.capacity = capacity
 
-    def append(self, *parts: torch.Tensor) -> None:
-        n = parts[0].shape[0]
-        if self.size + n > self.capacity:
-            self._allocate(int((self.size + n) * 1.25))
-        for t, part in zip(self.tensors, parts):
-            t[self.size:self.size + n].copy_(part)
-        self.size += n
+    def clear(self) -> None:
+        self.sizes.zero_()
+        self.overflow.zero_()
+        self.parity, self.size = 0, 0
+
+    def device_size(self) -> torch.Tensor:
+        """The size after the last recorded round, int64 [1] in device memory."""
+        return self.sizes[self.parity:self.parity + 1]
 
     def views(self) -> tuple[torch.Tensor, ...]:
-        return tuple(t[:self.size] for t in self.tensors)
-
-
-def _act_sample(ext: Any, actor: nn.Module, features: torch.Tensor, legal: torch.Tensor,
-                game: torch.Tensor, decision: torch.Tensor, seed_base: int):
-    """Sampled actions and their log-probabilities under the actor: one fused launch
-    for a hidden-512 FusedResidualMlp, else the actor's forward and the sampler."""
-    from .policy import fused_mlp_supported
-    infer = getattr(actor, "_weights", None)
-    if infer is not None:
-        params = [t for l in actor.linears() for t in (l.weight, l.bias)]
-        ws, bs = actor._weights(params)
-        if fused_mlp_supported(ws[0].shape[0], actor.n_blocks, ws[0].shape[1], ws[-1].shape[0]) \
-                and ws[-1].shape[0] >= 179 and ws[0].shape[1] == features.shape[1]:
-            from .ppo import _ACT
-            actions, logp, _ = ext.mlp_fused_sample(features, ws, bs, _ACT[actor.activation],
-                                                    ext.pack_legal(legal), game, decision,
-                                                    seed_base)
-            return actions, logp
-    out = actor(features)
-    logits = (out[0] if isinstance(out, tuple) else out).float().contiguous()
-    return ext.sample_actions(logits, legal, game, decision, seed_base)
+        c = self.columns
+        return tuple(c[k][:self.size] for k in ("features", "legal", "actions", "logp",
+                                                 "opp_hand", "stock", "env_ids", "seat"))
 
 
 @torch.no_grad()
-def collect(ext: Any, actor: nn.Module, games: int, seed_offset: int, reward_scale: float,
-            storage: RolloutStorage, max_steps: int = 128) -> Rollout:
-    """Self-play games with recorded transitions (python/cugo_ppo50.py:321-450,
-    without pool opponents): seeds make_seeds(games, seed_offset); games finished
-    before any decision are left out; a bad status or a running game without a
-    legal action raises."""
+def collect(ext: Any, actor: nn.Module, pool: list[nn.Module], games: int, seed_offset: int,
+            pool_fraction: float, pool_greedy: bool, reward_scale: float,
+            storage: RolloutStorage, max_steps: int = 128, critic: nn.Module | None = None,
+            **q_options: Any) -> Rollout:
+    """Self-play games (seeds make_seeds(games, seed_offset)) recorded into `storage`.
+
+    pool / pool_fraction / pool_greedy: one pool member, drawn for the iteration,
+    plays a random seat against the learner in each game with probability
+    pool_fraction (greedily or sampled); only the learner's decisions are kept.
+    Games that a deal already finished are left out.  A running game without a
+    legal action, or a step with a bad status, raises after the collection.
+    critic and the all-action options (q_options) belong to the all-action
+    targets, which this store does not hold."""
     ext = ext or load_extension()
-    device = torch.device("cuda")
-    seeds, first = make_seeds(games, seed_offset, device)
+    dev = torch.device("cuda")
+    seeds, first = make_seeds(games, seed_offset, dev)
     states = ext.create(seeds, first)
-    final_reward0 = torch.zeros(games, device=device)
-    final_nagari = torch.zeros(games, dtype=torch.bool, device=device)
-    started = torch.zeros(games, dtype=torch.bool, device=device)
-    active = torch.arange(games, device=device)
-    storage.size = 0
-    steps = 0
-    bad = torch.zeros((), dtype=torch.int64, device=device)
+    opponent = pool[int(torch.randint(len(pool), ()))] if pool and pool_fraction > 0.0 else None
+    learner_seat = torch.randint(2, (games,), device=dev)
+    vs_pool = (torch.rand(games, device=dev) < pool_fraction) if opponent is not None else None
+    started = states[:, DONE_BYTE] == 0
+    run = RunningSet(ext, states, torch.nonzero(started).squeeze(1), CHECK_EVERY)
+    storage.clear()
+    f_actor = fused_sampler_params(actor, 720)
+    f_opp = fused_sampler_params(opponent, 720) if opponent is not None else None
+    device_count = f_actor is not None and (opponent is None or f_opp is not None)
     actor.eval()
-    for _ in range(max_steps):
-        features, legal, players, done, status = ext.observe_indexed_bf16(states, active)
-        keep = ~done & (status == int(ext.STATUS_OK)) & legal.any(dim=1)
-        if steps == 0:
-            rows = torch.nonzero(keep).squeeze(1)
-            active, features, legal, players = (t.index_select(0, rows)
-                                                for t in (active, features, legal, players))
-            started.index_fill_(0, active, True)
-        else:
-            bad += (~keep).sum()
-        if active.numel() == 0:
+    if opponent is not None:
+        opponent.eval()
+    while not run.done and run.rounds < max_steps:
+        if not device_count and run.read_count() == 0:
             break
-        seat = players.to(torch.int64)
-        # Noise counter {deal seed, decision}: independent across games and iterations.
-        dec = torch.full((active.numel(),), steps, dtype=torch.int32, device=device)
-        actions, logp = _act_sample(ext, actor, features, legal, seeds.index_select(0, active), dec, 0)
-        steps += 1
-        opp_hand = ext.hands_indexed(states, active).gather(1, (1 - seat).unsqueeze(1)).squeeze(1)
-        storage.append(features, legal, actions, logp, opp_hand, active, seat)
-        reward0, new_done, nagari, step_status, _ = ext.step_indexed(states, active, actions)
-        bad += (step_status != int(ext.STATUS_OK)).sum()
-        final_reward0.index_copy_(0, active, torch.where(new_done, reward0, 0.0))
-        final_nagari.index_copy_(0, active, new_done & nagari)
-        active = active.index_select(0, torch.nonzero(~new_done).squeeze(1))
-        if active.numel() == 0:
+        active, count = run.active, run.count
+        if not device_count:
+            active = active[:run.bound]
+        features, bits, players, _, _ = ext.observe_indexed_bf16_bits(
+            states, active, m_dev=count if device_count else None)
+        actions, logp = choose_actions(ext, actor, f_actor, features, bits, active, seeds,
+                                run.decision, count, False, 0)
+        learner = None
+        if opponent is not None:
+            theirs = choose_actions(ext, opponent, f_opp, features, bits, active, seeds, run.decision,
+                             count, pool_greedy, 1)[0]
+            learner = ~vs_pool.index_select(0, active) | (
+                players.long() == learner_seat.index_select(0, active))
+            actions = torch.where(learner, actions, theirs)
+        ext.record_transitions(states, active, count if device_count else None, features, bits,
+                               players, actions, logp, learner, storage.sizes, storage.parity,
+                               storage.columns, storage.overflow)
+        storage.parity ^= 1
+        run.step(actions, device_count)
+        if device_count and run.poll(storage.device_size()):
             break
+        # Grow the store when the newest size seen, plus a full batch for every
+        # round that may have run since, could exceed the capacity.
+        seen_rows = run.last_seen[1] if device_count else int(storage.device_size().item())
+        ahead = (CHECK_EVERY * (run.lookahead + 1) + 1) if device_count else 1
+        if seen_rows + ahead * run.bound > storage.capacity:
+            torch.cuda.synchronize()
+            size = int(storage.device_size().item())
+            storage.reserve(max(int(storage.capacity * 1.25), size + (ahead + 1) * run.bound), keep=size)
     else:
-        raise RuntimeError(f"games did not finish within {max_steps} steps")
-    if int(bad):
+        if not run.done and run.read_count() != 0:
+            raise RuntimeError(f"games did not finish within {max_steps} steps")
+    storage.size = int(storage.device_size().item())
+    if int(storage.overflow.item()):
+        raise RuntimeError("transition store overflow")
+    if int(run.bad.item()):
         raise RuntimeError("an active game had no legal action, a bad status or a failed step")
-    features, legal, actions, logp, opp_hand, env_ids, seat = storage.views()
-    reward = final_reward0.index_select(0, env_ids)
-    returns = torch.where(seat == 0, reward, -reward) / reward_scale
-    return Rollout(features, legal, actions, logp, opp_hand, env_ids, seat, returns, games,
-                   terminal=int((started & ~final_nagari).sum()),
-                   nagari=int((started & final_nagari).sum()), decision_steps=steps,
-                   mean_abs_reward0=float(final_reward0[started].abs().mean()))
+    if opponent is not None:  # keep the learner's decisions only, in round order
+        keep = torch.nonzero(storage.columns["learner"][:storage.size]).squeeze(1)
+        for name, _, _ in RolloutStorage.COLUMNS:
+            col = storage.columns[name]
+            col[:keep.numel()].copy_(col.index_select(0, keep))
+        storage.size = keep.numel()
+    features, legal, actions, logp, opp_hand, stock, env_ids, seat = storage.views()
+    reward0 = run.reward0
+    mine = torch.where(seat == 0, 1.0, -1.0)
+    returns = mine * reward0.index_select(0, env_ids) / reward_scale
+    n_started = int(started.sum())
+    learner_score = float("nan")
+    if opponent is not None:
+        pool_games = started & vs_pool
+        if bool(pool_games.any()):
+            own = torch.where(learner_seat == 0, reward0, -reward0)
+            learner_score = float(own[pool_games].mean())
+    return Rollout(features, legal, actions, logp, opp_hand, stock, env_ids, seat, returns, games,
+                   terminal=int((started & ~run.nagari).sum()),
+                   nagari=int((started & run.nagari).sum()), decision_steps=run.rounds,
+                   mean_abs_reward0=float(reward0[started].abs().mean()) if n_started else 0.0,
+                   learner_score=learner_score)
 
 
 def gae_advantages(values: torch.Tensor, returns: torch.Tensor, env_ids: torch.Tensor,
                    seat: torch.Tensor, lam: float) -> torch.Tensor:
-    """GAE(lambda) with gamma 1 along each (game, seat) sequence of own decisions
-    (python/cugo_ppo50.py:484-509): delta_t = V(next own decision) - V(t), the last
-    decision's next value is the return; lam >= 1 gives return - V.  Rows are in
-    step order within each game."""
+    """GAE(lambda), gamma 1, over each (game, seat) sequence of own decisions (the
+    reference's definition, python/cugo_ppo50.py:484-509): residual_t = V(the seat's
+    next decision) - V(t), or return - V(t) at the seat's last decision;
+    A_t = residual_t + lam * A_(t+1) within the sequence; lam >= 1 gives return - V.
+    Rows must be in decision order within each sequence (as collect stores them).
+
+    The sequences are laid out as the rows of a dense [sequences, longest] matrix
+    of residuals (a stable sort groups each sequence's rows in order; a row's column
+    is its index in the sequence, padding is zero), the recursion runs backwards
+    over the columns on all sequences at once, and each row reads its entry back."""
     if lam >= 1.0:
         return returns - values
     n = values.numel()
-    order = torch.sort(env_ids * 2 + seat, stable=True).indices
-    key = (env_ids * 2 + seat).index_select(0, order)
-    nxt_same = torch.zeros(n, dtype=torch.bool, device=values.device)
-    nxt_same[:-1] = key[1:] == key[:-1]
-    v = values.index_select(0, order)
-    ret = returns.index_select(0, order)
-    delta = torch.where(nxt_same, torch.roll(v, -1), ret) - v
-    # Distance of each row to the end of its sequence.
-    pos = torch.arange(n, device=values.device)
-    end = torch.where(nxt_same, n, pos).flip(0).cummin(0).values.flip(0)
-    dist = end - pos
-    adv = torch.zeros_like(v)
-    for d in range(int(dist.max()) + 1 if n else 0):
-        rows = torch.nonzero(dist == d).squeeze(1)
-        adv[rows] = delta[rows] + (lam * adv[rows + 1] if d else 0.0)
-    out = torch.empty_like(adv)
-    out[order] = adv
+    if n == 0:
+        return values.clone()
+    dev = values.device
+    key = env_ids * 2 + seat
+    order = torch.sort(key, stable=True).indices
+    k = key.index_select(0, order)
+    v = values.index_select(0, order).float()
+    last = torch.ones(n, dtype=torch.bool, device=dev)
+    last[:-1] = k[1:] != k[:-1]
+    nxt = torch.cat((v[1:], v[:1]))
+    resid = torch.where(last, returns.index_select(0, order).float(), nxt) - v
+    head = torch.ones(n, dtype=torch.bool, device=dev)
+    head[1:] = last[:-1]
+    idx = torch.arange(n, device=dev)
+    col = idx - torch.where(head, idx, 0).cummax(0).values
+    seq = torch.cumsum(head.long(), 0) - 1
+    width = int(col.max()) + 1
+    dense = torch.zeros((int(seq[-1]) + 1, width + 1), dtype=torch.float32, device=dev)
+    dense[seq, col] = resid
+    for c in range(width - 1, -1, -1):
+        dense[:, c].add_(dense[:, c + 1], alpha=lam)
+    out = torch.empty_like(values)
+    out[order] = dense[seq, col].to(values.dtype)
     return out
 
 
 @dataclass
 class TrainStats:
-    """python/cugo_ppo50.py:460-476 (the plain-target fields)."""
+    """python/cugo_ppo50.py:460-476 (the plain-target fields).  With several ranks
+    the statistics cover every rank's rows (sums all-reduced)."""
     policy_loss: float
     value_loss: float
     entropy: float
@@ -228,28 +288,42 @@ class PpoTrainer:
         self.world = world
         self.graphed: GraphedPpoStep | None = None
 
-    def _steps_per_epoch(self, n: int, device: torch.device) -> int:
-        steps = n // self.minibatch
+    def _reduce(self, t: torch.Tensor, op=None) -> torch.Tensor:
         if self.world > 1:
-            t = torch.tensor([steps], dtype=torch.int64, device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MIN)
-            steps = int(t)
-        return steps
+            dist.all_reduce(t, op=op or dist.ReduceOp.SUM)
+        return t
+
+    def _steps_per_epoch(self, n: int, device: torch.device) -> int:
+        t = torch.tensor([n // self.minibatch], dtype=torch.int64, device=device)
+        return int(self._reduce(t, dist.ReduceOp.MIN if self.world > 1 else None))
 
     def _kl(self) -> float:
-        kl = self.step.last_kl.detach().reshape(1).clone()
-        if self.world > 1:
-            dist.all_reduce(kl)
-            kl /= self.world
-        return float(kl)
+        kl = self._reduce(self.step.last_kl.detach().reshape(1).clone())
+        return float(kl) / self.world
 
     @torch.no_grad()
     def values(self, data: Rollout, chunk: int = 65536) -> torch.Tensor:
         self.critic.eval()
         n = data.actions.numel()
-        return torch.cat([self.critic(critic_input(data.features[i:i + chunk],
-                                                   data.opp_hand[i:i + chunk])).float().reshape(-1)
-                          for i in range(0, n, chunk)]) if n else torch.zeros(0, device=data.returns.device)
+        if n == 0:
+            return torch.zeros(0, device=data.returns.device)
+        stock = data.stock if getattr(self.critic, "stock", False) else None
+        parts = [self.critic(critic_input(data.features[i:i + chunk], data.opp_hand[i:i + chunk],
+                                          None if stock is None else stock[i:i + chunk]))
+                 for i in range(0, n, chunk)]
+        return torch.cat([p.float().reshape(-1) for p in parts])
+
+    def _explained_variance(self, returns: torch.Tensor, values: torch.Tensor) -> float:
+        """1 - Var(return - V) / Var(return), over every rank's rows."""
+        r, e = returns.double(), (returns - values).double()
+        m = torch.stack((torch.tensor(float(r.numel()), dtype=torch.float64, device=r.device),
+                         r.sum(), (r * r).sum(), e.sum(), (e * e).sum()))
+        n, rs, rq, es, eq = self._reduce(m).tolist()
+        if n < 2:
+            return float("nan")
+        var_r = (rq - rs * rs / n) / (n - 1)
+        var_e = (eq - es * es / n) / (n - 1)
+        return 1.0 - var_e / max(var_r, 1e-8)
 
     def update(self, data: Rollout, epochs: int, entropy_coef: float, target_kl: float,
                gae_lambda: float = 1.0) -> TrainStats:
@@ -257,8 +331,7 @@ class PpoTrainer:
         values = self.values(data)
         adv = gae_advantages(values, data.returns, data.env_ids, data.seat, gae_lambda)
         ret = adv + values
-        explained_var = 1.0 - float((data.returns - values).var() /
-                                    data.returns.var().clamp_min(1e-8))
+        explained_var = self._explained_variance(data.returns, values)
         self.actor.train()
         self.critic.train()
         st = self.step
@@ -266,6 +339,7 @@ class PpoTrainer:
         st.sums.zero_()
         updates, stop = 0, False
         steps = self._steps_per_epoch(n, data.actions.device)
+        with_stock = bool(getattr(self.critic, "stock", False))
         for _ in range(epochs):
             perm = torch.randperm(n, device=data.actions.device)
             for j in range(steps):
@@ -273,7 +347,8 @@ class PpoTrainer:
                 mb = Minibatch(data.features.index_select(0, idx), data.legal.index_select(0, idx),
                                data.actions.index_select(0, idx), data.logp.index_select(0, idx),
                                data.opp_hand.index_select(0, idx), adv.index_select(0, idx),
-                               ret.index_select(0, idx))
+                               ret.index_select(0, idx),
+                               data.stock.index_select(0, idx) if with_stock else None)
                 if self.use_graph:
                     if self.graphed is None:
                         self.graphed = GraphedPpoStep(st, mb)
@@ -286,7 +361,7 @@ class PpoTrainer:
                     break
             if stop:
                 break
-        s = st.sums.tolist()
+        s = self._reduce(st.sums.detach().double().clone()).tolist()
         count = max(1.0, s[5])
         return TrainStats(policy_loss=s[0] / count, value_loss=s[1] / count, entropy=s[2] / count,
                           kl=s[3] / count, clipfrac=s[4] / count, explained_var=explained_var,
@@ -296,14 +371,16 @@ class PpoTrainer:
 def iteration(ext: Any, trainer: PpoTrainer, storage: RolloutStorage, games: int,
               seed_offset: int, reward_scale: float = 32.0, epochs: int = 2,
               entropy_coef: float = 0.05, target_kl: float = 0.03,
-              gae_lambda: float = 0.95) -> dict:
+              gae_lambda: float = 0.95, pool: list[nn.Module] | None = None,
+              pool_fraction: float = 0.0, pool_greedy: bool = False) -> dict:
     """One train_ppo50.py iteration (its defaults: 65,536 games, 2 epochs, minibatch
     32,768, GAE 0.95, reward scale 32): collection and update, timed on the host
     around device synchronisations.  Data parallel: each rank passes its own
     seed_offset (disjoint games) and a trainer built with world = the number of ranks."""
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    data = collect(ext, trainer.actor, games, seed_offset, reward_scale, storage)
+    data = collect(ext, trainer.actor, pool or [], games, seed_offset, pool_fraction, pool_greedy,
+                   reward_scale, storage)
     torch.cuda.synchronize()
     t1 = time.perf_counter()
     stats = trainer.update(data, epochs, entropy_coef, target_kl, gae_lambda)

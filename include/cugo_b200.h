@@ -465,6 +465,64 @@ CUGO_B200_API int cugo_b200_games_attention(const void* qkv, int64_t ldq, int64_
                                             float scale, void* out, int64_t ldo,
                                             cudaStream_t stream);
 
+/* One decision round of a training collection appended to a device-resident
+ * transition store (no reference counterpart: it replaces the per-round
+ * hands_indexed, stock_indexed, index_select and RolloutStorage.append of
+ * python/cugo_ppo50.py:394-412).  Round row i < min(m, *m_dev) (m_dev optional)
+ * plays game row active[i] of states; its bf16 features (row i of features, ldf
+ * elements apart, 16-byte aligned), legal bit words (uint64 [m, 3], bit a of word
+ * a / 64), player (players[i]), action, behaviour log p and learner flag (learner
+ * NULL: every row is the learner's) go to store row sizes[parity] + i, with the
+ * opponent's hand (hand word 1 - player of the game row) and the next 8 stock draws
+ * (stock_indexed's packing) read from the game row; the legal bits are written as
+ * a bool [capacity, 179] mask, features as bf16 [capacity, 720].
+ * sizes[parity ^ 1] = sizes[parity] + rows: the store's size moves between the
+ * two slots of sizes (int64 [2]) round by round.  Rows past capacity are not
+ * written and set *overflow (optional) to 1. */
+CUGO_B200_API int cugo_b200_record_transitions(
+    const uint8_t* states, int64_t n_states, const int64_t* active, int64_t m,
+    const int32_t* m_dev, const void* features, int64_t ldf, const uint64_t* legal_bits,
+    const uint8_t* players, const int64_t* actions, const float* logp, const bool* learner,
+    int64_t* sizes, int32_t parity, int64_t capacity, void* out_features, bool* out_legal,
+    int64_t* out_actions, float* out_logp, int64_t* out_opp_hand, int64_t* out_stock,
+    int64_t* out_env, int64_t* out_seat, bool* out_learner, int32_t* overflow,
+    cudaStream_t stream);
+
+/* The oracle critic's stock planes (python/cugo_ppo_nets50.py:104-110 stock_planes
+ * of ext.stock_indexed, as python/cugo_ppo50.py:478-482 appends them): in bf16 row i
+ * (ld elements apart) of rows, column first_column + 50 k + c is set to 1 where the
+ * k-th of the next 8 stock draws of game row env_ids[i] is card c < 50 (env_ids
+ * NULL: row i); other columns are not written (observe_critic_bf16 zero-fills the
+ * row past the hand plane).  An invalid id leaves its row alone. */
+CUGO_B200_API int cugo_b200_stock_planes_bf16(const uint8_t* states, int64_t n_states,
+                                              const int64_t* env_ids, int64_t m, void* rows,
+                                              int64_t ld, int32_t first_column,
+                                              cudaStream_t stream);
+
+/* The end of one decision step of the sequence self-play wave for its w games (no
+ * reference counterpart: it replaces the tensor bookkeeping of WaveCollector._step,
+ * python/cugo_seq_selfplay50.py:108-163).  Inputs per game g: the step's observe
+ * outputs (done, status, player), the sampled action (-1: no legal action) and its
+ * log p, and the outputs of step_events_indexed.  A game that was running:
+ * counts a bad observe (status != 0 or no legal action) and a bad step (status != 0)
+ * into *bad; when it finishes, final_reward0/final_nagari/finished are set and
+ * *running drops by one; a committed event is written to slot min(count, max_events
+ * - 1) of its event log (int64 [w, max_events, 9]), then count[g] and the KV-cache
+ * lengths of both seats (cache_length[g], cache_length[w + g]) grow by one;
+ * decision[g] grows by one.  Records (optional, [max_steps, w], rec_actions NULL:
+ * none) at row *step_index: action, player, count before the step, log p, and
+ * whether the game was running and the learner moved (learner, optional: per game,
+ * whether the learner's network chose the action; NULL: always).  *step_index then
+ * grows by one. */
+CUGO_B200_API int cugo_b200_wave_tail(
+    int64_t w, const bool* obs_done, const int16_t* obs_status, const uint8_t* players,
+    const int64_t* actions, const float* logp, const float* reward0, const bool* new_done,
+    const bool* nagari, const int16_t* status, const bool* committed, const int64_t* step_events,
+    const bool* learner, float* final_reward0, bool* final_nagari, bool* finished, int64_t* bad, int32_t* running,
+    int64_t* events, int32_t max_events, int64_t* count, int64_t* cache_length, int32_t* decision,
+    int64_t* step_index, int64_t* rec_actions, int64_t* rec_seat, int64_t* rec_count,
+    float* rec_logp, bool* rec_valid, int64_t max_steps, cudaStream_t stream);
+
 /* Token widths of the sequence policy (python/cugo_seq50.py:37-38). */
 CUGO_B200_API int64_t cugo_b200_event_inputs(void); /* EVENT_IN = 414 */
 CUGO_B200_API int64_t cugo_b200_start_inputs(void); /* START_IN = 274 */

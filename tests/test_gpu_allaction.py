@@ -210,3 +210,38 @@ def test_world_values_average_the_worlds(ext):
     q2 = world_values(ext, None, None, states, env_rows, players, vs_pool, legal, SCALE, 3,
                       critic=critic, depth=1, first=2, seed=21)
     assert torch.equal(torch.isnan(q2), ~legal) and bool(torch.isfinite(q2[legal]).all())
+
+
+def test_action_values_with_a_stock_critic(ext):
+    """OracleCritic(stock=True) (python/cugo_ppo_nets50.py:67-87): the critic rows get the
+    one-hot planes of the next 8 stock draws in the observe pass (observe_critic_bf16
+    then stock_planes_bf16), equal to the reference's composition with stock_indexed."""
+    from cugo_b200.allaction import action_values
+    from cugo_b200.ppo import critic_input, fused_critic
+    states, legal, players = _roots(ext, 1200, 29)
+    r = states.shape[0]
+    torch.manual_seed(8)
+    critic = fused_critic(hidden=256, blocks=2, stock=True).to(DEV)
+    with torch.no_grad():
+        for p in critic.parameters():
+            p.copy_(torch.randn_like(p) * (1.0 / p.shape[-1]) ** 0.5)
+    env_rows = torch.arange(r, device=DEV)
+    q = action_values(ext, critic, states, env_rows, players, legal, SCALE)
+    rows, acts = torch.nonzero(legal, as_tuple=True)
+    m = players.index_select(0, rows)
+    child, reward0, done = ext.branch_indexed(states, rows, acts)[:3]
+    ids = torch.arange(child.shape[0], device=DEV)
+    features, _, mover, _, _ = ext.observe_indexed(child, ids)
+    mover = mover.long()
+    opp = ext.hands_indexed(child, ids).gather(1, (1 - mover).unsqueeze(1)).squeeze(1)
+    stock = ext.stock_indexed(child, ids)
+    crit_rows, _, _, _ = ext.observe_critic_bf16(child, ids, width=1176)
+    ext.stock_planes_bf16(child, ids, crit_rows)
+    assert torch.equal(crit_rows[:, :1170], critic_input(features, opp, stock))
+    assert not crit_rows[:, 1170:].any()
+    with torch.no_grad():
+        v = critic.value(critic(critic_input(features, opp, stock)))
+    v = torch.where(mover == m, v, -v)
+    final = torch.where(m == 0, reward0, -reward0) / SCALE
+    expect = torch.where(done, final, v).to(torch.float16)
+    assert torch.equal(q[rows, acts], expect)

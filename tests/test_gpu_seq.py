@@ -268,7 +268,7 @@ def test_wave_selfplay_graph_replay_equals_eager(ext):
         steps = sp.play_wave(game0=1000)
         torch.cuda.synchronize()
         runs.append((steps, sp.final_reward0.clone(), sp.count.clone(), sp.events.clone(),
-                     sp.rec_long["actions"].clone(), sp.finished.clone()))
+                     sp.records["actions"].clone(), sp.finished.clone()))
         sp.release()
     (s0, *a), (s1, *b) = runs
     assert s0 == s1
@@ -277,31 +277,57 @@ def test_wave_selfplay_graph_replay_equals_eager(ext):
     assert bool(runs[0][5].all())
 
 
-def test_wave_selfplay_records_replay_on_the_engine(ext):
-    sp = _wave(graphs=True)
-    sp.play_wave(game0=77)
-    torch.cuda.synchronize()
+def _replay_wave(ext, sp, game0):
+    """Replays a wave's recorded actions on fresh deals with step_events_indexed:
+    (count, events, final reward, decisions, valid-as-expected) per game."""
     w = sp.w
-    games = 77 + torch.arange(w, device=DEV)
+    games = game0 + torch.arange(w, device=DEV)
     states = ext.create(12345 + games, games & 1)
     events = torch.zeros_like(sp.events)
     count = torch.zeros(w, dtype=torch.int64, device=DEV)
     reward = torch.zeros(w, device=DEV)
+    decisions = torch.zeros(w, dtype=torch.int32, device=DEV)
     ids = torch.arange(w, device=DEV)
-    valid, acts = sp.rec_valid, sp.rec_long["actions"]
-    for s in range(int(valid.any(1).nonzero().max()) + 1):
-        rows = ids[valid[s]]
-        r0, done, _, status, committed, ev = ext.step_events_indexed(states, rows, acts[s, rows])
+    acts = sp.records["actions"]
+    expect_valid = torch.zeros_like(sp.records["valid"])
+    learner_seat = (ids >> 1) & 1
+    for s in range(acts.shape[0]):
+        _, _, players, done, _ = ext.observe_indexed(states, ids)
+        rows = ids[~done]
+        if rows.numel() == 0:
+            break
+        mover = players[rows].long()
+        mine = (rows >= sp.pool) | (mover == learner_seat[rows])
+        expect_valid[s, rows] = mine
+        r0, fin, _, status, committed, ev = ext.step_events_indexed(states, rows, acts[s, rows])
         assert bool((status == 0).all())
         c = rows[committed]
         events[c, count[c]] = ev[committed]
         count[c] += 1
-        fin = rows[done]
-        reward[fin] = r0[done]
+        decisions[rows] += 1
+        reward[rows[fin]] = r0[fin]
+    assert bool(ext.observe(states)[3].all())
+    return count, events, reward, decisions, expect_valid
+
+
+@pytest.mark.parametrize("pool", [0, 128])
+def test_wave_selfplay_records_replay_on_the_engine(ext, pool):
+    """The wave-tail kernel's bookkeeping (event log, counts, final rewards, decision
+    counters, records) against a replay of the recorded actions; with pool games the
+    opponent decoder moves for its seat and only the learner's decisions are valid."""
+    from cugo_b200.seq_selfplay import SeqWaveSelfPlay
+    opponent = _decoder(seed=5) if pool else None
+    sp = SeqWaveSelfPlay(_decoder(seed=0), wave=512, graphs=True, opponent=opponent,
+                         pool_games=pool)
+    sp.play_wave(game0=77)
     torch.cuda.synchronize()
+    count, events, reward, decisions, expect_valid = _replay_wave(ext, sp, 77)
     assert torch.equal(count, sp.count)
     assert torch.equal(events, sp.events)
     assert torch.equal(reward, sp.final_reward0)
-    # every game ended; a game's recorded decisions are exactly its steps
-    assert bool(ext.observe(states)[3].all())
-    assert torch.equal(valid.sum(0).int(), sp.decision)
+    assert torch.equal(decisions, sp.decision)
+    assert torch.equal(expect_valid, sp.records["valid"])
+    assert torch.equal(sp.cache.length, torch.cat((count, count)) + 1)
+    if pool:
+        assert int(sp.records["valid"][:, :pool].sum()) < int(decisions[:pool].sum())
+    sp.release()

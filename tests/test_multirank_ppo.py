@@ -2,7 +2,9 @@
 gloo).  Ranks whose rollouts hold different numbers of minibatches must still take
 the same collective steps: every epoch runs the smallest count, the KL early stop
 uses the KL averaged over the ranks, and the averaged gradients keep the networks
-identical on every rank."""
+identical on every rank.  The returned statistics (losses, entropy, KL, clip
+fraction, explained variance) are reduced over the ranks, so every rank reports the
+same values for the shared update."""
 from __future__ import annotations
 
 import os
@@ -49,6 +51,7 @@ def _rollout(n: int, seed: int):
     return Rollout(features=torch.rand((n, 720), generator=g).to(torch.bfloat16), legal=legal,
                    actions=actions, logp=torch.full((n,), -2.0),
                    opp_hand=torch.randint(0, 1 << 50, (n,), generator=g),
+                   stock=torch.full((n,), -1, dtype=torch.int64),
                    env_ids=torch.arange(n) // 4, seat=torch.arange(n) % 2,
                    returns=torch.randn(n, generator=g), games=n // 4, terminal=n // 4, nagari=0,
                    decision_steps=4, mean_abs_reward0=1.0)
@@ -73,8 +76,13 @@ def _rank_main(rank: int, port: int, out_dir: str) -> None:
                               list(actor.parameters()) + list(critic.parameters())])
             parts = [torch.zeros_like(flat) for _ in range(WORLD)]
             dist.all_gather(parts, flat)
+            st = torch.tensor([stats.policy_loss, stats.value_loss, stats.entropy, stats.kl,
+                               stats.clipfrac, stats.explained_var], dtype=torch.float64)
+            st_parts = [torch.zeros_like(st) for _ in range(WORLD)]
+            dist.all_gather(st_parts, st)
             results.append([stats.updates, float((parts[0] - parts[1]).abs().max()),
-                            float((flat - _flat_init()).abs().max())])
+                            float((flat - _flat_init()).abs().max()),
+                            float((st_parts[0] - st_parts[1]).abs().max())])
         np.save(Path(out_dir) / f"rank{rank}.npy", np.array(results, dtype=np.float64))
     finally:
         dist.destroy_process_group()
@@ -97,3 +105,4 @@ def test_data_parallel_update_keeps_ranks_in_step():
     for r in (r0, r1):
         assert np.all(r[:, 1] == 0.0)   # identical parameters on the two ranks
         assert np.all(r[:, 2] > 0.0)    # and they did change
+        assert np.all(r[:, 3] == 0.0)   # the statistics cover both ranks' rows: equal on each
