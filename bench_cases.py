@@ -335,9 +335,15 @@ def reference_gpu_case(games: int = 262144, warmup: int = 1, iters: int = 2) -> 
     sec_t = _events_time(lambda: triton_attn(qc, kc, vc, pos, True, rows), warmup + 3, iters + 8)
     sec_o = _events_time(lambda: ext.decode_attention(q, kc, vc, pos, rows), warmup + 3, iters + 8)
 
+    # The reference's append (python/cugo_seq50.py:310-318): index_put_ of the new key
+    # and value at (row * heads + head, pos) of the [rows * heads, slots, dh] cache.
+    flat_rows = (rows.view(n, 1) * heads + torch.arange(heads, device=dev).view(1, heads)).flatten()
+    flat_pos = pos.repeat_interleave(heads)
+    kn2, vn2 = kn.reshape(n * heads, dh), vn.reshape(n * heads, dh)
+
     def ref_append_attend():
-        kc.index_put_((rows, slice(None), pos), kn)
-        vc.index_put_((rows, slice(None), pos), vn)
+        kc.view(-1, slots, dh).index_put_((flat_rows, flat_pos), kn2)
+        vc.view(-1, slots, dh).index_put_((flat_rows, flat_pos), vn2)
         return triton_attn(qc, kc, vc, pos, True, rows)
 
     sec_ta = _events_time(ref_append_attend, warmup + 3, iters + 8)

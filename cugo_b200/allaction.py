@@ -129,11 +129,13 @@ def redeal_worlds(ext: Any, states: torch.Tensor, env_rows: torch.Tensor, seat: 
     return ext.redeal_worlds(states, env_rows, seat, worlds, seed=seed, tries=tries)
 
 
-def _greedy_actions(ext: Any, model: nn.Module, features, bits, rows, count, decision):
+def _greedy_actions(ext: Any, model: nn.Module, features, bits, rows, count, decision, positions):
     """The model's masked argmax (lowest action on ties, the reference's greedy _act,
-    python/cugo_ppo50.py:73-82) for the running rows."""
+    python/cugo_ppo50.py:73-82) for the running rows (positions: the batch's row
+    numbers, which stand in for the noise address greedy play does not use)."""
     fused = fused_sampler_params(model, features.shape[1])
-    return choose_actions(ext, model, fused, features, bits, rows, rows, decision, count, True, 0)[0]
+    return choose_actions(ext, model, fused, features, bits, rows, positions, decision, count, True,
+                          0)[0]
 
 
 @torch.no_grad()
@@ -144,7 +146,7 @@ def greedy_to_end(ext: Any, actor: nn.Module, opponent: nn.Module | None, child:
     games (pool[i]) the opponent network plays the seat that is not me[i]
     (python/cugo_ppo50.py:183-211).  Children that already ended keep reward0."""
     ext = ext or load_extension()
-    run = RunningSet(ext, child, torch.nonzero(~done).squeeze(1))
+    run = RunningSet(ext, child, ~done)
     rivals = opponent is not None and bool(pool.any())
     device_count = fused_sampler_params(actor, 720) is not None and (
         not rivals or fused_sampler_params(opponent, 720) is not None)
@@ -156,9 +158,11 @@ def greedy_to_end(ext: Any, actor: nn.Module, opponent: nn.Module | None, child:
             active = active[:run.bound]
         features, bits, players, _, _ = ext.observe_indexed_bf16_bits(
             child, active, m_dev=count if device_count else None)
-        actions = _greedy_actions(ext, actor, features, bits, active, count, run.decision)
+        actions = _greedy_actions(ext, actor, features, bits, active, count, run.decision,
+                                  run.positions)
         if rivals:
-            theirs = _greedy_actions(ext, opponent, features, bits, active, count, run.decision)
+            theirs = _greedy_actions(ext, opponent, features, bits, active, count, run.decision,
+                                     run.positions)
             rival_moves = pool.index_select(0, active) & (players.long() != me.index_select(0, active))
             actions = torch.where(rival_moves, theirs, actions)
         run.step(actions, device_count)

@@ -125,14 +125,38 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase of parity `parity` to complete; false after ~2 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Waits for the phase of parity `parity` to complete; false once limit_ns (~2 s by
+// default) have passed on the global timer.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitNs) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = now_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_test(bar, parity)) return true;
-    if ((i & 255u) == 0 && now_ns() - t0 > kWaitNs) return false;
+    if ((i & 255u) == 0 && now_ns() - t0 > limit_ns) return false;
   }
+}
+
+// The timeout path of the bounded wait, run on purpose: thread 0 waits on an
+// mbarrier that no thread arrives on, the wait gives up after limit_ns, *error is
+// set and the time waited recorded; then the one expected arrival completes the
+// phase so the barrier is left settled, and the kernel returns.
+__global__ void wait_timeout_probe_kernel(uint64_t limit_ns, int* error,
+                                          unsigned long long* waited_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) mbar_init(&bar, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = now_ns();
+    const bool completed = mbar_wait(&bar, 0, limit_ns);
+    const uint64_t t1 = now_ns();
+    if (!completed && error) atomicExch(error, 1);
+    if (waited_ns) *waited_ns = t1 - t0;
+    mbar_arrive(&bar);
+    mbar_wait(&bar, 0, limit_ns);
+  }
+  __syncthreads();
 }
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
@@ -1905,6 +1929,18 @@ int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t m, int64_t k_
   return fused_launch(x, ldx, m, k_in, blocks, weights, biases, n_out, act, out, ldo, legal_bits,
                       game, decision, rows, n_games, seed_base, greedy, actions, logp, m_dev,
                       error, stream);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int cugo_b200_wait_timeout_probe(int64_t limit_ns, int32_t* error, int64_t* waited_ns,
+                                 cudaStream_t stream) {
+  if (limit_ns <= 0 || limit_ns > 1'000'000'000 || !error) return CUGO_B200_ERR_ARG;
+  wait_timeout_probe_kernel<<<1, 32, 0, stream>>>(
+      static_cast<uint64_t>(limit_ns), error, reinterpret_cast<unsigned long long*>(waited_ns));
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }
 
 }  // extern "C"

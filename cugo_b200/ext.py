@@ -72,6 +72,7 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_record_transitions": [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP,
                                      _VP, _VP, _I32, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
                                      _VP, _VP, _VP, _VP],
+    "cugo_b200_wait_timeout_probe": [_I64, _VP, _VP, _VP],
     "cugo_b200_stock_planes_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _I32, _VP],
     "cugo_b200_wave_tail": [_I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
                             _VP, _VP, _VP, _VP, _VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP,
@@ -459,6 +460,18 @@ class CugoB200Extension:
                 _ptr(store["opp_hand"]), _ptr(store["stock"]), _ptr(store["env_ids"]),
                 _ptr(store["seat"]), _ptr(store["learner"]), _ptr(overflow),
                 self._stream(states.device)), "record_transitions")
+
+    def wait_timeout_probe(self, limit_ns: int, device: torch.device | str = "cuda"):
+        """Runs the bounded mbarrier wait of the GEMM kernels on a barrier nothing
+        arrives on: returns (error flag int32 [1], nanoseconds waited int64 [1])."""
+        device = torch.device(device)
+        with torch.cuda.device(device):
+            error = torch.zeros(1, dtype=torch.int32, device=device)
+            waited = torch.zeros(1, dtype=torch.int64, device=device)
+            _check(self._lib.cugo_b200_wait_timeout_probe(limit_ns, _ptr(error), _ptr(waited),
+                                                          self._stream(device)),
+                   "wait_timeout_probe")
+        return error, waited
 
     def stock_planes_bf16(self, states, env_ids, rows: torch.Tensor, first_column: int = 770) -> None:
         """Sets the one-hot planes of the next 8 stock draws (columns first_column ..

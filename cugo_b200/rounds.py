@@ -21,37 +21,44 @@ import torch
 from torch import nn
 
 
-class RunningSet:
-    """The running games of `states` (rows [0, g)), starting with rows `first`."""
+DONE_BYTE = 239  # TorchEnv50::done (a deal can end a game before its first decision)
 
-    def __init__(self, ext, states: torch.Tensor, first: torch.Tensor | None = None,
+
+class RunningSet:
+    """The running games of `states` (rows [0, g)): the rows where `running` (bool
+    [g], on the device; default: the rows whose done byte is 0, i.e. not ended at
+    the deal) is set, in row order.  Built on the device without a host read: a
+    stable sort puts the running rows first and their number is the count."""
+
+    def __init__(self, ext, states: torch.Tensor, running: torch.Tensor | None = None,
                  check_every: int = 4, lookahead: int = 2) -> None:
         dev = states.device
         g = states.shape[0]
         self.ext, self.states, self.g = ext, states, g
         i64 = dict(dtype=torch.int64, device=dev)
-        head = torch.arange(g, **i64)
-        n = g
-        if first is not None:
-            n = first.numel()
-            head[:n] = first  # entries past the count stay valid rows (they are read, not used)
+        if running is None:
+            running = states[:, DONE_BYTE] == 0
+        # Running rows first, in order; the rest stay valid rows (read, not used).
+        head = torch.sort((~running).to(torch.uint8), stable=True).indices
         self.ids = (head, torch.zeros(g, **i64))
-        self.counts = torch.tensor([n, 0], dtype=torch.int32, device=dev)
+        self.counts = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.counts[0:1].copy_(running.sum().view(1))
+        self.positions = torch.arange(g, **i64)
         self.decision = torch.zeros(g, dtype=torch.int32, device=dev)
         self.reward0 = torch.zeros(g, dtype=torch.float32, device=dev)
         self.nagari = torch.zeros(g, dtype=torch.bool, device=dev)
         self.bad = torch.zeros(1, **i64)
         self.scratch = torch.empty(max(1, 2 * ((g + 31) // 32)), dtype=torch.int32, device=dev)
         self.rounds = 0
-        self.bound = n  # the host's upper bound of the running count
+        self.bound = g  # the host's upper bound of the running count
         self.check_every, self.lookahead = check_every, lookahead
         pin = dev.type == "cuda"
         self._seen = torch.zeros(lookahead + 1, dtype=torch.int32, pin_memory=pin)
         self._seen_extra = torch.zeros(lookahead + 1, dtype=torch.int64, pin_memory=pin)
-        self.last_seen = (n, 0)
+        self.last_seen = (g, 0)
         self._pending: list[tuple[torch.cuda.Event, int]] = []
         self._copies = 0
-        self.done = n == 0
+        self.done = g == 0
 
     # -- the current round ---------------------------------------------------------
     @property

@@ -13,6 +13,8 @@ from dataclasses import dataclass
 
 import torch
 
+from .rounds import RunningSet
+
 
 @dataclass
 class BatchResult:
@@ -52,7 +54,6 @@ class RoundTimer:
 
 
 CHECK_EVERY = 4  # rounds between host reads of the running count (device-count loop)
-LOOKAHEAD = 2    # reads in flight: the host waits on a read only this many checks later
 
 
 def _log_actions(log: torch.Tensor, active: torch.Tensor, count: torch.Tensor,
@@ -72,61 +73,46 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
                launches: list[int] | None = None,
                actions_log: torch.Tensor | None = None) -> BatchResult:
     """Plays games `game_index` (seed = seed_base + index, first player index & 1) to
-    the end with policy-sampled actions.
+    the end with policy-sampled actions.  A game that its deal already ended takes no
+    decision and keeps reward 0 (as the reference's drivers count it).
 
-    With a fused policy step (policy.samples_in_kernel()) the rounds run without host
-    round trips: each round's kernels read the running count that the previous
-    round's step left in device memory (buffers keep the batch's full size).  Every
-    CHECK_EVERY rounds the count is copied to pinned host memory behind an event; the
-    host looks at a copy only once its event has completed (or LOOKAHEAD later
-    copies are queued), so the device never waits for the host.  Rounds launched
-    after the count reached zero see zero rows and change nothing.  Otherwise the
-    host reads the count after every round and sizes the next round's launches by
-    it.
+    The running games are a device-resident list (rounds.RunningSet).  With a fused
+    policy step (policy.samples_in_kernel()) the rounds run without host round trips:
+    each round's kernels read the running count that the previous round's step left
+    in device memory; every CHECK_EVERY rounds the host queues a copy of it and
+    looks at copies whose event has completed, so the device never waits for the
+    host.  Rounds launched after the count reached zero see zero rows and change
+    nothing.  Otherwise (or with a timer, which needs each round's rows) the host
+    reads the count after every round and sizes the next round's launches by it.
 
     actions_log (optional, for checking): int64 [games + 1, width]; entry [i, d]
     receives the action game i chose at its decision d (the extra last row takes the
     writes of positions past the running count)."""
-    device = game_index.device
     g = game_index.numel()
     states = ext.create(game_index + seed_base, game_index & 1)
-    decision = torch.zeros(g, dtype=torch.int32, device=device)
-    reward0 = torch.zeros(g, dtype=torch.float32, device=device)
-    nagari = torch.zeros(g, dtype=torch.bool, device=device)
-    bad = torch.zeros(1, dtype=torch.int64, device=device)
-    # The running games' positions, written by the step kernel (ping-pong), their counts.
-    # Entries past the count stay valid positions (they are gathered, not used).
-    ids_buf = (torch.arange(g, device=device), torch.zeros(g, dtype=torch.int64, device=device))
-    counts = torch.tensor([g, 0], dtype=torch.int32, device=device)
-    scratch = torch.empty(2 * ((g + 31) // 32), dtype=torch.int32, device=device)
+    run = RunningSet(ext, states, check_every=CHECK_EVERY)
     fused = getattr(policy, "samples_in_kernel", lambda: False)()
     # The policy timer needs each round's row count: it reads the count every round.
-    sync_each = not fused or timer is not None
+    device_count = fused and timer is None
     # observe, the policy step, and step_compact's step, scan and scatter kernels
     per_round = 4 + getattr(policy, "launches_per_step", lambda: 1)()
     n_launch = 1
-    rounds = 0
-    live = g
-    # Copies of the running count in flight: (event, pinned slot).
-    seen = torch.empty(LOOKAHEAD + 1, dtype=torch.int32, pin_memory=device.type == "cuda")
-    pending: list[tuple[torch.cuda.Event, int]] = []
-    n_copies = 0
-    finished = False
-    for rounds in range(1, max_rounds + 1):
-        k = (rounds - 1) & 1
-        active, nxt = ids_buf[k], ids_buf[1 - k]
-        c_in, c_out = counts[k:k + 1], counts[1 - k:2 - k]
-        if not fused:
-            active = active[:live]
-        if fused:  # observe with bit-word masks, one policy kernel, step: no host reads
-            features, legal, _p, _d, _s = ext.observe_indexed_bf16_bits(states, active, m_dev=c_in)
+    while not run.done and run.rounds < max_rounds:
+        if not device_count and run.read_count() == 0:
+            break
+        active, count = run.active, run.count
+        if device_count:  # observe with bit-word masks, one policy kernel: no host reads
+            features, legal, _p, _d, _s = ext.observe_indexed_bf16_bits(states, active, m_dev=count)
             t0 = timer.start() if timer else None
             # The kernel reads each row's game index and decision counter through active.
-            actions, _logp = policy.forward_sample(features, legal, game_index, decision, seed_base,
-                                                   m_dev=c_in, rows=active)
+            actions, _logp = policy.forward_sample(features, legal, game_index, run.decision,
+                                                   seed_base, m_dev=count, rows=active)
         else:
-            features, legal, _p, _d, _s = ext.observe_indexed_bf16(states, active)
-            game_ids, dec = game_index.index_select(0, active), decision.index_select(0, active)
+            active = active[:run.bound]
+            features, legal, _p, _d, _s = (ext.observe_indexed_bf16_bits(states, active) if fused
+                                           else ext.observe_indexed_bf16(states, active))
+            game_ids = game_index.index_select(0, active)
+            dec = run.decision.index_select(0, active)
             t0 = timer.start() if timer else None
             if hasattr(policy, "forward_sample"):
                 actions, _logp = policy.forward_sample(features, legal, game_ids, dec, seed_base)
@@ -134,38 +120,17 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
                 actions, _logp = ext.sample_actions(policy(features), legal, game_ids, dec,
                                                     seed_base)
         if timer:
-            timer.stop(t0, live)
+            timer.stop(t0, run.bound)
         if actions_log is not None:
-            _log_actions(actions_log, active, c_in if fused else torch.tensor(live, device=device),
-                         decision, actions)
-        ext.step_compact(states, active, actions, decision, reward0, nagari, bad, nxt, c_out,
-                         scratch, m_dev=c_in if fused else None)
+            _log_actions(actions_log, active, count, run.decision, actions)
+        run.step(actions, device_count)
         n_launch += per_round
-        if sync_each:
-            live = int(c_out.item())
-            if live == 0:
-                break
-        elif rounds % CHECK_EVERY == 0:
-            slot = n_copies % (LOOKAHEAD + 1)
-            n_copies += 1
-            seen[slot:slot + 1].copy_(c_out, non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record()
-            pending.append((ev, slot))
-            while pending and (len(pending) > LOOKAHEAD or pending[0][0].query()):
-                ev0, slot0 = pending.pop(0)
-                ev0.synchronize()
-                if int(seen[slot0]) == 0:
-                    finished = True
-                    break
-            if finished:
-                break
-    else:
-        # The last round's count says whether the games ended within the limit.
-        if max_rounds == 0 or int(c_out.item()) != 0:
-            raise RuntimeError(f"games did not finish within {max_rounds} rounds")
+        if device_count:
+            run.poll()
+    if not run.done and run.read_count() != 0:
+        raise RuntimeError(f"games did not finish within {max_rounds} rounds")
     if launches is not None:
         launches.append(n_launch)
-    decisions = int(decision.sum())
-    played = int(decision.max()) if g else 0  # every live game decides once per round
-    return BatchResult(g, decisions, played, int(bad), reward0, nagari)
+    decisions = int(run.decision.sum())
+    played = int(run.decision.max()) if g else 0  # every live game decides once per round
+    return BatchResult(g, decisions, played, int(run.bad.item()), run.reward0, run.nagari)

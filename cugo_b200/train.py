@@ -41,9 +41,8 @@ from torch import nn
 from .evaluate import make_seeds
 from .ext import load_extension
 from .ppo import GraphedPpoStep, Minibatch, PpoStep, critic_input
-from .rounds import RunningSet, choose_actions, fused_sampler_params
+from .rounds import DONE_BYTE, RunningSet, choose_actions, fused_sampler_params
 
-DONE_BYTE = 239  # TorchEnv50::done: a deal can end the game before any decision
 CHECK_EVERY = 4
 
 
@@ -140,7 +139,7 @@ def collect(ext: Any, actor: nn.Module, pool: list[nn.Module], games: int, seed_
     learner_seat = torch.randint(2, (games,), device=dev)
     vs_pool = (torch.rand(games, device=dev) < pool_fraction) if opponent is not None else None
     started = states[:, DONE_BYTE] == 0
-    run = RunningSet(ext, states, torch.nonzero(started).squeeze(1), CHECK_EVERY)
+    run = RunningSet(ext, states, started, CHECK_EVERY)
     storage.clear()
     f_actor = fused_sampler_params(actor, 720)
     f_opp = fused_sampler_params(opponent, 720) if opponent is not None else None

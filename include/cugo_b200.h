@@ -296,6 +296,16 @@ CUGO_B200_API int cugo_b200_mlp_fused_sample(const void* x, int64_t ldx, int64_t
 CUGO_B200_API int cugo_b200_pack_legal(const bool* legal, int64_t m, uint64_t* bits,
                                        cudaStream_t stream);
 
+/* Self-test of the failure-detection path of every pipeline wait in the GEMM and
+ * whole-network kernels (no counterpart in the reference): one block waits on an
+ * mbarrier that nothing arrives on, with the same bounded wait those kernels use
+ * (limited on the GPU's global timer; 0 < limit_ns <= 1 s here, ~2 s there); the
+ * wait gives up, *error (int32, device) is set to 1, *waited_ns (int64, device,
+ * optional) receives the time waited, and the kernel returns with the context
+ * usable. */
+CUGO_B200_API int cugo_b200_wait_timeout_probe(int64_t limit_ns, int32_t* error,
+                                               int64_t* waited_ns, cudaStream_t stream);
+
 /* Policy forward that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory — for example a Go/Java/Rust
  * serving process that passes only its own fixed input and output buffers and keeps

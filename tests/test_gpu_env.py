@@ -271,3 +271,31 @@ def test_ops_capture_in_cuda_graph(ext):
     assert torch.equal(feat, f_eager)
     for a, b in zip(out, eager_out):
         assert torch.equal(a, b)
+
+
+# Byte ranges of a finished row that record how the game went (the TorchEnv50 image:
+# end reason at 129, shaken months 104..107, bombs 108, bomb credits 110, ppuk count
+# 120, go count 96, Gukjin role 102, nagari 240).
+RARE_FIELDS = {"shaken": (104, 4), "bombs": (108, 2), "credits": (110, 2), "ppuk": (120, 2),
+               "go": (96, 2)}
+
+
+def test_rare_rule_paths_at_scale(ext, oracle):
+    """A million seeded random-legal games (games 0 .. 2^20 - 1), every final row,
+    reward, decision count and event hash bit-exact with the reference's engine.
+    The range holds every way a game ends — Stop, Chongtong at the deal, on the
+    floor and by a bonus replacement, three ppuk, nagari — each at least 100 times,
+    and games with shakes, bombs, bomb credits, ppuk and Go calls."""
+    games = 1 << 20
+    r = {k: n(v) for k, v in ext.rollout_random(0, games, seed_base=12345).items()}
+    o = oracle.rollout_random(0, games, seed_base=12345)
+    for key in ("reward0", "decisions", "events", "last_status", "final_rows"):
+        assert np.array_equal(r[key], o[key]), key
+    assert np.array_equal(r["hashes"].view(np.uint64), o["hashes"])
+    rows = r["final_rows"]
+    reasons = np.bincount(rows[:, 129], minlength=6)
+    # 1 Stop, 2 dealt Chongtong, 3 floor Chongtong, 4 bonus-replacement Chongtong, 5 three ppuk
+    assert all(reasons[k] >= 100 for k in (1, 2, 3, 4, 5)), reasons
+    assert int(rows[:, 240].sum()) >= 100  # nagari
+    for name, (off, width) in RARE_FIELDS.items():
+        assert int(np.any(rows[:, off:off + width] != 0, axis=1).sum()) >= 100, name

@@ -123,3 +123,43 @@ def test_reference_ppo_actor_golden(golden):
     ref = torch.from_numpy(gd["logits"])
     scale = max(1.0, float(ref.abs().max()))
     assert float((out - ref).abs().max()) <= 2e-2 * scale
+
+
+def test_policy_logit_bar_at_the_reference_init(ext, capsys):
+    """The north_star bar on the 65,536 real observation rows: max |delta logit| <= 2e-2
+    against the exact fp32 forward, with the networks at the reference's own
+    initialisation scale (PpoActor's nn.Linear default init: uniform in +-1/sqrt(fan
+    in), every layer non-zero, SiLU, 3 blocks of 512; bf16 weights), and argmax
+    agreement reported beside the reference's autocast forward.  The agreement is
+    asserted against the autocast forward's own (>= it - 0.1%); on random weights
+    near ties bound any bf16 implementation below a fixed 99.9% (see the module
+    docstring).  The measured figures are printed."""
+    from cugo_b200.policy import ResidualMlpPolicy
+
+    pol = ResidualMlpPolicy(512, 3, "silu", device=DEV, seed=0)
+    g = torch.Generator().manual_seed(0)
+    for i, (w, b) in enumerate(zip(pol.weights, pol.biases)):
+        bound = 1.0 / w.shape[1] ** 0.5
+        pol.weights[i] = ((torch.rand(w.shape, generator=g) * 2 - 1) * bound).to(DEV, torch.bfloat16)
+        pol.biases[i] = ((torch.rand(b.shape, generator=g) * 2 - 1) * bound).to(DEV, torch.bfloat16)
+    feats, legal = _observations(ext)
+    out = pol(feats)[:, :179]
+    exact = mlp_forward_fp32(pol.weights, pol.biases, feats, 3, "silu")[:, :179]
+    auto = mlp_forward_autocast(pol.weights, pol.biases, feats, 3, "silu")[:, :179]
+    live = legal.any(1)
+
+    def greedy(x):
+        return x.masked_fill(~legal, -1e30).argmax(1)
+
+    err = float((out - exact).abs().max())
+    err_auto = float((auto - exact).abs().max())
+    agree = float((greedy(out) == greedy(exact))[live].float().mean())
+    agree_auto = float((greedy(auto) == greedy(exact))[live].float().mean())
+    agree_pair = float((greedy(out) == greedy(auto))[live].float().mean())
+    with capsys.disabled():
+        print(f"\nlogit bar (65,536 rows, {int(live.sum())} with a legal action): "
+              f"max|dlogit| vs fp32 {err:.5f} (autocast {err_auto:.5f}, logit scale "
+              f"{float(exact.abs().max()):.3f}); argmax agreement vs fp32 {agree:.5f} "
+              f"(autocast {agree_auto:.5f}); vs autocast {agree_pair:.5f}")
+    assert err <= 2e-2
+    assert agree >= agree_auto - 1e-3

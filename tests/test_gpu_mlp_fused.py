@@ -147,3 +147,18 @@ def test_observe_bits_and_pack_legal_agree_with_the_bool_mask(ext):
     a = torch.arange(179, device=DEV)
     words = bits.gather(1, (a // 64).expand(bits.shape[0], -1))
     assert torch.equal(((words >> (a % 64)) & 1).bool(), legal)
+
+
+def test_bounded_wait_gives_up_and_reports(ext):
+    """The failure-detection path of the GEMM kernels' pipeline waits, on purpose: a
+    wait on an mbarrier that nothing arrives on gives up after its limit (20 ms here),
+    sets the error flag and returns; the context stays usable (a GEMM runs after)."""
+    err, waited = ext.wait_timeout_probe(20_000_000)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1
+    assert 20_000_000 <= int(waited.item()) < 1_000_000_000
+    a = torch.randn((256, 512), device=DEV).to(torch.bfloat16)
+    w = torch.randn((512, 512), device=DEV).to(torch.bfloat16)
+    out = ext.linear(a, w, None)
+    torch.cuda.synchronize()
+    assert float((out.float() - a.float() @ w.float().t()).abs().max()) < 1.0

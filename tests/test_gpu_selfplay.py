@@ -53,13 +53,14 @@ def test_step_compact_matches_step_indexed(ext):
 
 
 def _reference_loop(ext, policy, game_index, seed_base=12345, max_rounds=128):
-    """The collection loop with separate ops and torch bookkeeping."""
+    """The collection loop with separate ops and torch bookkeeping; games that the
+    deal ended take no decision (reward 0)."""
     g = game_index.numel()
     states = ext.create(game_index + seed_base, game_index & 1)
     decision = torch.zeros(g, dtype=torch.int32, device=DEV)
     reward0 = torch.zeros(g, device=DEV)
     nagari = torch.zeros(g, dtype=torch.bool, device=DEV)
-    active = torch.arange(g, device=DEV)
+    active = torch.nonzero(states[:, 239] == 0).squeeze(1)
     decisions = rounds = 0
     for rounds in range(1, max_rounds + 1):
         features, legal, _, _, _ = ext.observe_indexed_bf16(states, active)
@@ -67,7 +68,7 @@ def _reference_loop(ext, policy, game_index, seed_base=12345, max_rounds=128):
                                         game_index.index_select(0, active),
                                         decision.index_select(0, active), seed_base)
         reward, new_done, new_nagari, status, _ = ext.step_indexed(states, active, actions)
-        assert not bool(((status != 0) & (status != 9)).any())
+        assert not bool((status != 0).any())
         decisions += active.numel()
         decision.index_add_(0, active, torch.ones_like(active, dtype=torch.int32))
         reward0.index_copy_(0, active, torch.where(new_done, reward, 0.0))
