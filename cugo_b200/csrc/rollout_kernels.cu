@@ -169,11 +169,15 @@ __global__ void __launch_bounds__(256) wave_tail_kernel(
     if (active && (obs_status[g] != 0 || a < 0)) ++bad;  // no legal action or bad observe
     if (active && status[g] != 0) ++bad;
     if (s.rec_actions && step < s.max_steps) {
+      // A finished game's entries are left alone (only its valid flag is cleared),
+      // so steps replayed after the wave ended change no record.
       const int64_t at = step * w + g;
-      s.rec_actions[at] = a;
-      s.rec_seat[at] = players[g];
-      s.rec_count[at] = s.count[g];
-      s.rec_logp[at] = logp[g];
+      if (active) {
+        s.rec_actions[at] = a;
+        s.rec_seat[at] = players[g];
+        s.rec_count[at] = s.count[g];
+        s.rec_logp[at] = logp[g];
+      }
       s.rec_valid[at] = active && (learner == nullptr || learner[g]);
     }
     if (active && new_done[g]) {

@@ -56,7 +56,8 @@ class RunningSet:
         self._seen = torch.zeros(lookahead + 1, dtype=torch.int32, pin_memory=pin)
         self._seen_extra = torch.zeros(lookahead + 1, dtype=torch.int64, pin_memory=pin)
         self.last_seen = (g, 0)
-        self._pending: list[tuple[torch.cuda.Event, int]] = []
+        self.last_seen_round = 0  # the round whose start the last copy read describes
+        self._pending: list[tuple[torch.cuda.Event, int, int]] = []
         self._copies = 0
         self.done = g == 0
 
@@ -93,7 +94,8 @@ class RunningSet:
         """Every check_every rounds: queue a copy of the running count (and of
         `extra`, an int64 [1] device scalar) and look at the copies whose event has
         completed (waiting only when lookahead copies are queued).  Returns whether
-        a copy showed no running game; the latest copy read is in last_seen."""
+        a copy showed no running game; the latest copy read is in last_seen (count,
+        extra), taken when `last_seen_round` rounds had been stepped."""
         if self.done:
             return True
         if self.rounds % self.check_every:
@@ -105,11 +107,12 @@ class RunningSet:
             self._seen_extra[slot:slot + 1].copy_(extra, non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
-        self._pending.append((ev, slot))
+        self._pending.append((ev, slot, self.rounds))
         while self._pending and (len(self._pending) > self.lookahead or self._pending[0][0].query()):
-            ev0, slot0 = self._pending.pop(0)
+            ev0, slot0, round0 = self._pending.pop(0)
             ev0.synchronize()
             self.last_seen = (int(self._seen[slot0]), int(self._seen_extra[slot0]))
+            self.last_seen_round = round0
             self.bound = min(self.bound, self.last_seen[0])
             if self.last_seen[0] == 0:
                 self.done = True

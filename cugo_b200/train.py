@@ -150,17 +150,29 @@ def collect(ext: Any, actor: nn.Module, pool: list[nn.Module], games: int, seed_
     while not run.done and run.rounds < max_steps:
         if not device_count and run.read_count() == 0:
             break
+        # The store must hold this round's rows: an upper bound of its size is the
+        # newest size read back plus a full running set for every round since.
+        if device_count:
+            size_bound = run.last_seen[1] + (run.rounds - run.last_seen_round) * run.bound
+        else:
+            size_bound = int(storage.device_size().item())
+        if size_bound + run.bound > storage.capacity:
+            torch.cuda.synchronize()
+            size = int(storage.device_size().item())
+            storage.reserve(max(int(storage.capacity * 1.25),
+                                size + (CHECK_EVERY * (run.lookahead + 2)) * run.bound), keep=size)
+            run.last_seen, run.last_seen_round = (run.last_seen[0], size), run.rounds
         active, count = run.active, run.count
         if not device_count:
             active = active[:run.bound]
         features, bits, players, _, _ = ext.observe_indexed_bf16_bits(
             states, active, m_dev=count if device_count else None)
         actions, logp = choose_actions(ext, actor, f_actor, features, bits, active, seeds,
-                                run.decision, count, False, 0)
+                                       run.decision, count, False, 0)
         learner = None
         if opponent is not None:
-            theirs = choose_actions(ext, opponent, f_opp, features, bits, active, seeds, run.decision,
-                             count, pool_greedy, 1)[0]
+            theirs = choose_actions(ext, opponent, f_opp, features, bits, active, seeds,
+                                    run.decision, count, pool_greedy, 1)[0]
             learner = ~vs_pool.index_select(0, active) | (
                 players.long() == learner_seat.index_select(0, active))
             actions = torch.where(learner, actions, theirs)
@@ -171,14 +183,6 @@ def collect(ext: Any, actor: nn.Module, pool: list[nn.Module], games: int, seed_
         run.step(actions, device_count)
         if device_count and run.poll(storage.device_size()):
             break
-        # Grow the store when the newest size seen, plus a full batch for every
-        # round that may have run since, could exceed the capacity.
-        seen_rows = run.last_seen[1] if device_count else int(storage.device_size().item())
-        ahead = (CHECK_EVERY * (run.lookahead + 1) + 1) if device_count else 1
-        if seen_rows + ahead * run.bound > storage.capacity:
-            torch.cuda.synchronize()
-            size = int(storage.device_size().item())
-            storage.reserve(max(int(storage.capacity * 1.25), size + (ahead + 1) * run.bound), keep=size)
     else:
         if not run.done and run.read_count() != 0:
             raise RuntimeError(f"games did not finish within {max_steps} steps")
@@ -206,7 +210,8 @@ def collect(ext: Any, actor: nn.Module, pool: list[nn.Module], games: int, seed_
             learner_score = float(own[pool_games].mean())
     return Rollout(features, legal, actions, logp, opp_hand, stock, env_ids, seat, returns, games,
                    terminal=int((started & ~run.nagari).sum()),
-                   nagari=int((started & run.nagari).sum()), decision_steps=run.rounds,
+                   nagari=int((started & run.nagari).sum()),
+                   decision_steps=int(run.decision.max()) if games else 0,
                    mean_abs_reward0=float(reward0[started].abs().mean()) if n_started else 0.0,
                    learner_score=learner_score)
 

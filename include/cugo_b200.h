@@ -520,7 +520,8 @@ CUGO_B200_API int cugo_b200_stock_planes_bf16(const uint8_t* states, int64_t n_s
  * - 1) of its event log (int64 [w, max_events, 9]), then count[g] and the KV-cache
  * lengths of both seats (cache_length[g], cache_length[w + g]) grow by one;
  * decision[g] grows by one.  Records (optional, [max_steps, w], rec_actions NULL:
- * none) at row *step_index: action, player, count before the step, log p, and
+ * none) at row *step_index: action, player, count before the step and log p of a
+ * game that was running (a finished game's entries are not written), and
  * whether the game was running and the learner moved (learner, optional: per game,
  * whether the learner's network chose the action; NULL: always).  *step_index then
  * grows by one. */
