@@ -212,11 +212,15 @@ def selfplay_bench(args, world, rank, ext, policy):
         barrier(world)
         launches: list[int] = []
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_dev = time.perf_counter()
         start.record()
-        results = [play_batch(ext, policy, blocks[s], launches=launches)
-                   for s in range(args.warmup, total_steps)]
+        results = []
+        for s in range(args.warmup, total_steps):
+            r = play_batch(ext, policy, blocks[s], launches=launches)
+            results.append((r.games, r.decisions, r.bad_status))
         stop.record()
         barrier(world)
+        dev_wall = time.perf_counter() - t_dev
         elapsed = start.elapsed_time(stop) / 1e3
         # End to end through the public API, host wall clock: each step's game
         # indices copied from pinned host memory, its rewards read back.
@@ -229,7 +233,7 @@ def selfplay_bench(args, world, rank, ext, policy):
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         barrier(world)
-        regions.append((elapsed, results, sum(launches), wall))
+        regions.append((elapsed, results, sum(launches), wall, dev_wall))
     clocks.mark(t_start, time.time())
     clk = clocks.stop()
     # The policy's in-loop rate, from CUDA events around every forward of one more
@@ -242,10 +246,10 @@ def selfplay_bench(args, world, rank, ext, policy):
     dev_max = [all_reduce([r[0]], world, op="max")[0] for r in regions]
     e2e_max = [all_reduce([r[3]], world, op="max")[0] for r in regions]
     pick = sorted(range(REPEATS), key=lambda i: dev_max[i])[REPEATS // 2]
-    _, results, n_launch, _ = regions[pick]
-    games = sum(r.games for r in results)
-    decisions = sum(r.decisions for r in results)
-    bad = sum(r.bad_status for r in results)
+    _, results, n_launch, _, _ = regions[pick]
+    games = sum(r[0] for r in results)
+    decisions = sum(r[1] for r in results)
+    bad = sum(r[2] for r in results)
     tot_games, tot_dec, tot_bad = all_reduce([games, decisions, bad], world)
     own_dev = statistics.median(r[0] for r in regions)
     own_e2e = statistics.median(r[3] for r in regions)
@@ -259,7 +263,8 @@ def selfplay_bench(args, world, rank, ext, policy):
                 mlp_ms=mlp_ms, mlp_launches=mlp_launches, mlp_rows=mlp_rows,
                 launches=n_launch, clocks=clk, e2e_elapsed=statistics.median(e2e_max),
                 e2e_games=tot_games, h2d=g * 8, d2h=g * 4, per_rank=per_rank,
-                regions_s=dev_max, e2e_regions_s=e2e_max)
+                regions_s=dev_max, e2e_regions_s=e2e_max,
+                dev_wall_regions_s=[all_reduce([r[4]], world, op="max")[0] for r in regions])
 
 
 # ---- config 1 and 2: engine only -----------------------------------------------------
@@ -555,7 +560,9 @@ def main():
                    "prewarm_s": PREWARM_S, "policy_activation": "relu",
                    "ms_per_step_regions": [round(x * 1e3 / args.steps, 3) for x in sp["regions_s"]],
                    "e2e_ms_per_step_regions": [round(x * 1e3 / args.steps, 3)
-                                               for x in sp["e2e_regions_s"]]},
+                                               for x in sp["e2e_regions_s"]],
+                   "device_region_wall_ms_per_step": [round(x * 1e3 / args.steps, 3)
+                                                      for x in sp["dev_wall_regions_s"]]},
         "per_rank": sp["per_rank"],
         "decisions_per_s": sp["decisions"] / sp["elapsed"],
         "bad_status": sp["bad"],

@@ -16,11 +16,10 @@ in the batch and are skipped by the kernels' bookkeeping).  Two CUDA graphs:
          counts, final rewards, the event log, the per-decision records, the cache
          lengths, event counts and decision counters, and the wave's running count
 
-The host replays the step graph and, every 4 steps, queues a copy of the running
-count into pinned memory behind an event; it reads a copy once its event has
-completed (or two newer copies are queued), so replays continue while earlier
-copies are in flight, and the wave ends at the first copy that shows no running
-game.  Steps replayed after the last game ended change nothing.
+The host replays the step graph and, every 4 steps, copies the running count into
+pinned memory behind an event and reads it; the wave ends at the first copy that
+shows no running game (at most 3 steps after its last game ended; such steps change
+nothing).
 
 Sampling uses the Philox Gumbel noise of cugo_b200_sample_actions (counter {game,
 decision}) instead of torch.rand_like, so a wave is reproducible.  Games are dealt
@@ -36,7 +35,10 @@ import torch
 from .seq import MAX_EVENTS, QUERY_LD, SeqDecoder
 
 POLL_EVERY = 4
-LOOKAHEAD = 2
+# Copies of the running count the host lets run ahead of its reads.  A wave's steps
+# have a fixed shape, so every step queued past the end costs a full step: the host
+# reads each copy before queueing more (a short drain every POLL_EVERY steps).
+LOOKAHEAD = 0
 
 
 class SeqWaveSelfPlay:
