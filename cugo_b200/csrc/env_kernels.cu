@@ -186,6 +186,152 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
   }
 }
 
+// branch_indexed with identical children made once.  A child depends only on
+// (parent row, action), so a block takes kBranchEntries consecutive entries, finds
+// the distinct (parent, action) pairs among them (a shared-memory hash keyed by the
+// pair; each pair's representative is its lowest entry), steps only the distinct
+// pairs -- packed into the block's warps, 32 per warp and kBranchBlock per pass --
+// and after each pass writes the child rows and outputs of every entry whose pair
+// the pass made, from the stepped tiles in shared memory.  An entry with an invalid
+// parent id gets a zero child (status -1, done 1, as step_indexed reports it).
+constexpr int kBranchWarps = 4;
+constexpr int kBranchBlock = 32 * kBranchWarps;
+constexpr int kBranchPer = 2;  // entries per thread
+constexpr int kBranchEntries = kBranchBlock * kBranchPer;
+constexpr int kBranchHash = 2 * kBranchEntries;  // open addressing, load factor <= 1/2
+
+struct BranchShared {
+  WarpTile tiles[kBranchWarps];
+  unsigned long long keys[kBranchHash];
+  int rep[kBranchHash];              // lowest entry index holding the key
+  int16_t uniq_of[kBranchEntries];   // entry -> its pair's index among the distinct ones
+  int16_t head[kBranchEntries];      // distinct pair u -> its representative entry
+  int counts[kBranchPer * kBranchWarps];
+  float reward[kBranchBlock];        // outputs of the current pass's pairs
+  int16_t status[kBranchBlock];
+  uint8_t flags[kBranchBlock];       // done | nagari << 1 | committed << 2
+};
+
+__global__ void __launch_bounds__(kBranchBlock, 4) branch_dedup_kernel(
+    const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids,
+    const i64* __restrict__ actions, i64 m, u64* __restrict__ children,
+    float* __restrict__ reward, bool* __restrict__ done, bool* __restrict__ nagari,
+    int16_t* __restrict__ status, bool* __restrict__ committed) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  BranchShared& sh = *reinterpret_cast<BranchShared*>(smem_raw);
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const i64 base = (i64)blockIdx.x * kBranchEntries;
+  constexpr unsigned long long kEmpty = ~0ull;
+  for (int k = t; k < kBranchHash; k += kBranchBlock) {
+    sh.keys[k] = kEmpty;
+    sh.rep[k] = kBranchEntries;
+  }
+  __syncthreads();
+  // Entry e = t + kBranchBlock * j.  Pair key: parent id and action; an invalid
+  // entry (or one past m) is a pair of its own.
+  const auto insert = [&](int e) -> int {
+    const i64 src = lane_source(ids, base + e, m, n_states);
+    const u32 act = base + e < m ? torch_action(__ldg(actions + base + e)) : kNoAction;
+    const unsigned long long key =
+        src >= 0 ? (static_cast<unsigned long long>(src) << 16) | act
+                 : (0xffffull << 48) | static_cast<unsigned long long>(e);
+    u32 h = static_cast<u32>((key * 0x9E3779B97F4A7C15ull) >> 40) & (kBranchHash - 1);
+    for (;;) {
+      const unsigned long long prev = atomicCAS(&sh.keys[h], kEmpty, key);
+      if (prev == kEmpty || prev == key) break;
+      h = (h + 1) & (kBranchHash - 1);
+    }
+    atomicMin(&sh.rep[h], e);
+    return static_cast<int>(h);
+  };
+  static_assert(kBranchPer == 2, "two entries per thread");
+  const int e_a = t, e_b = t + kBranchBlock;
+  const int slot_a = insert(e_a), slot_b = insert(e_b);
+  __syncthreads();
+  // Distinct pairs numbered in entry order (a block scan over the representatives).
+  const bool head_a = sh.rep[slot_a] == e_a, head_b = sh.rep[slot_b] == e_b;
+  const unsigned ballot_a = __ballot_sync(kFull, head_a), ballot_b = __ballot_sync(kFull, head_b);
+  if (lane == 0) {
+    sh.counts[warp] = __popc(ballot_a);
+    sh.counts[kBranchWarps + warp] = __popc(ballot_b);
+  }
+  __syncthreads();
+  int before_a = 0, before_b = 0, distinct = 0;
+#pragma unroll
+  for (int c = 0; c < kBranchPer * kBranchWarps; ++c) {
+    if (c < warp) before_a += sh.counts[c];
+    if (c < kBranchWarps + warp) before_b += sh.counts[c];
+    distinct += sh.counts[c];
+  }
+  const unsigned below = (1u << lane) - 1u;
+  if (head_a) {
+    const int u = before_a + __popc(ballot_a & below);
+    sh.head[u] = static_cast<int16_t>(e_a);
+    sh.uniq_of[e_a] = static_cast<int16_t>(u);
+  }
+  if (head_b) {
+    const int u = before_b + __popc(ballot_b & below);
+    sh.head[u] = static_cast<int16_t>(e_b);
+    sh.uniq_of[e_b] = static_cast<int16_t>(u);
+  }
+  __syncthreads();
+  if (!head_a) sh.uniq_of[e_a] = sh.uniq_of[sh.rep[slot_a]];
+  if (!head_b) sh.uniq_of[e_b] = sh.uniq_of[sh.rep[slot_b]];
+  __syncthreads();
+  WarpTile& tile = sh.tiles[warp];
+  for (int pass = 0; pass * kBranchBlock < distinct; ++pass) {
+    const int first = pass * kBranchBlock;
+    // Step pairs first .. first + kBranchBlock - 1, 32 per warp.
+    if (first + warp * 32 < distinct) {
+      const int u = first + warp * 32 + lane;
+      const int e = u < distinct ? sh.head[u] : -1;
+      const i64 my_src = e >= 0 ? lane_source(ids, base + e, m, n_states) : -1;
+      gather_rows(tile, states, my_src);
+      Game g;
+      load_game(tile, g);
+      __syncwarp();
+      StepOut out{static_cast<u32>(-1), 0, 1, 0, 0};
+      if (my_src >= 0) {
+        out = step_game(g, torch_action(__ldg(actions + base + e)));
+      } else {
+        for (int k = 0; k < kRowWords; ++k) g.w[k] = 0;
+      }
+      store_game(tile, g);
+      const int q = warp * 32 + lane;
+      sh.reward[q] = static_cast<float>(out.reward0);
+      sh.status[q] = static_cast<int16_t>(static_cast<i32>(out.status));
+      sh.flags[q] = static_cast<uint8_t>((out.done != 0) | ((out.nagari != 0) << 1) |
+                                         ((out.committed != 0) << 2));
+    }
+    __syncthreads();
+    // Every entry whose pair this pass made: its child row (words across the
+    // lanes, one row per step: coalesced 248-byte stores) and its outputs.
+    for (int j = 0; j < kBranchPer; ++j) {
+      const int e0 = kBranchBlock * j + warp * 32;
+#pragma unroll 4
+      for (int r = 0; r < 32; ++r) {
+        const i64 row = base + e0 + r;
+        if (row >= m) break;
+        const int q = sh.uniq_of[e0 + r] - first;
+        if (q < 0 || q >= kBranchBlock) continue;
+        if (lane < kRowWords)
+          __stcs(children + row * kRowWords + lane, sh.tiles[q >> 5].rows[q & 31][lane]);
+      }
+      const int e = e0 + lane;
+      const int q = sh.uniq_of[e] - first;
+      if (base + e < m && q >= 0 && q < kBranchBlock) {
+        const uint8_t f = sh.flags[q];
+        reward[base + e] = sh.reward[q];
+        status[base + e] = sh.status[q];
+        done[base + e] = f & 1u;
+        nagari[base + e] = (f >> 1) & 1u;
+        committed[base + e] = (f >> 2) & 1u;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // Exclusive prefix over the warps' running counts (one block): offsets[w], and
 // the total in *count.
 __global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __restrict__ keep,
@@ -504,9 +650,25 @@ int cugo_b200_branch_indexed(const uint8_t* states, int64_t n_states, const int6
                              const int64_t* actions, int64_t m, uint8_t* children, float* reward,
                              bool* done, bool* nagari, int16_t* status, bool* committed,
                              cudaStream_t stream) {
-  if (m > 0 && (!env_ids || !children)) return CUGO_B200_ERR_ARG;
-  return step_common(const_cast<uint8_t*>(states), n_states, env_ids, actions, m, children, reward,
-                     done, nagari, status, committed, nullptr, stream);
+  if (n_states < 0 || m < 0) return CUGO_B200_ERR_ARG;
+  if (m > 0 && (!env_ids || !children || !actions || !reward || !done || !nagari || !status ||
+                !committed))
+    return CUGO_B200_ERR_ARG;
+  if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8) || !aligned(children, 8)) return CUGO_B200_ERR_ALIGN;
+  if (m == 0) return CUGO_B200_OK;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(branch_dedup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             sizeof(BranchShared)) != cudaSuccess)
+      return CUGO_B200_ERR_LAUNCH;
+    configured = true;
+  }
+  branch_dedup_kernel<<<blocks_for(m, kBranchEntries), kBranchBlock, sizeof(BranchShared),
+                        stream>>>(
+      reinterpret_cast<const u64*>(states), n_states, env_ids, actions, m,
+      reinterpret_cast<u64*>(children), reward, done, nagari, status, committed);
+  return launch_status();
 }
 
 int cugo_b200_clone_indexed(const uint8_t* states, int64_t n_states, const int64_t* env_ids,

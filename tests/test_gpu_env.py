@@ -145,6 +145,44 @@ def test_branch_children_match_oracle(ext, oracle):
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("layout", ["all_actions", "shuffled", "repeats"])
+def test_branch_entries_of_every_layout_match_oracle(ext, oracle, layout):
+    """branch_indexed makes each distinct (parent, action) child once per 256 entries
+    and copies it to the others: every entry equals the oracle's clone + step whether
+    the entries are all distinct (every legal action of consecutive rows: two passes
+    of a block), shuffled, or heavy repeats, with invalid ids and actions mixed in and
+    a ragged last block."""
+    roots = ext.branch_roots(1500, seed_base=777)
+    legal = n(ext.observe(roots)[1])
+    rows, acts = np.nonzero(legal)
+    rng = np.random.default_rng(5)
+    if layout == "shuffled":
+        perm = rng.permutation(rows.size)
+        rows, acts = rows[perm], acts[perm]
+    elif layout == "repeats":
+        pick = rng.integers(0, rows.size, size=20000)
+        pick.sort()
+        rows, acts = rows[pick], acts[pick]
+    rows, acts = rows.astype(np.int64), acts.astype(np.int64)
+    bad = rng.random(rows.size) < 0.01
+    rows[bad] = rng.choice([-1, 1500, 10**9], size=int(bad.sum()))
+    bad_act = rng.random(rows.size) < 0.01
+    acts[bad_act] = rng.choice([-1, 179, 1000], size=int(bad_act.sum()))
+    m = rows.size - 37  # a ragged last block
+    rows, acts = rows[:m], acts[:m]
+    out = [n(x) for x in ext.branch_indexed(roots, torch.from_numpy(rows).to(DEV),
+                                            torch.from_numpy(acts).to(DEV))]
+    valid = (rows >= 0) & (rows < 1500)
+    parents = np.zeros((m, 248), dtype=np.uint8)
+    parents[valid] = n(roots)[rows[valid]]
+    o = oracle.step(parents, acts)
+    assert np.array_equal(out[0][valid], o[0][valid])
+    assert not out[0][~valid].any()
+    for a, b in zip(out[1:], o[1:]):
+        assert np.array_equal(a[valid], b[valid])
+    assert (out[4][~valid] == -1).all() and out[2][~valid].all()
+
+
 def test_selfplay_step_matches_oracle(ext, oracle):
     """Config 1 at reduced size: slots 0..4095 of generation 0 follow the oracle's
     games; the features written are observe()'s."""
