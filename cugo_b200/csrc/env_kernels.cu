@@ -304,18 +304,36 @@ __global__ void __launch_bounds__(kBranchBlock, 4) branch_dedup_kernel(
                                          ((out.committed != 0) << 2));
     }
     __syncthreads();
-    // Every entry whose pair this pass made: its child row (words across the
-    // lanes, one row per step: coalesced 248-byte stores) and its outputs.
+    // Every entry whose pair this pass made: its child row and its outputs.  A
+    // whole group of 32 entries made in this pass leaves as 496 16-byte stores of
+    // its 7,936 contiguous bytes (each vector two row words, possibly of two rows);
+    // otherwise row by row, the row's words across the lanes.
     for (int j = 0; j < kBranchPer; ++j) {
       const int e0 = kBranchBlock * j + warp * 32;
+      const int q_lane = sh.uniq_of[e0 + lane] - first;
+      const bool mine = q_lane >= 0 && q_lane < kBranchBlock;
+      const i64 row0 = base + e0;
+      u64* dst = children + row0 * kRowWords;
+      if (__all_sync(kFull, mine) && row0 + 32 <= m && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+        for (int v = lane; v < 16 * kRowWords; v += 32) {  // 496 vectors of 16 bytes
+          const int w0 = 2 * v, w1 = w0 + 1;
+          const int r0 = w0 / kRowWords, r1 = w1 / kRowWords;
+          const int q0 = sh.uniq_of[e0 + r0] - first;
+          const int q1 = sh.uniq_of[e0 + r1] - first;
+          const u64 a = sh.tiles[q0 >> 5].rows[q0 & 31][w0 - r0 * kRowWords];
+          const u64 b = sh.tiles[q1 >> 5].rows[q1 & 31][w1 - r1 * kRowWords];
+          __stcs(reinterpret_cast<ulonglong2*>(dst) + v, make_ulonglong2(a, b));
+        }
+      } else {
 #pragma unroll 4
-      for (int r = 0; r < 32; ++r) {
-        const i64 row = base + e0 + r;
-        if (row >= m) break;
-        const int q = sh.uniq_of[e0 + r] - first;
-        if (q < 0 || q >= kBranchBlock) continue;
-        if (lane < kRowWords)
-          __stcs(children + row * kRowWords + lane, sh.tiles[q >> 5].rows[q & 31][lane]);
+        for (int r = 0; r < 32; ++r) {
+          const i64 row = row0 + r;
+          if (row >= m) break;
+          const int q = sh.uniq_of[e0 + r] - first;
+          if (q < 0 || q >= kBranchBlock) continue;
+          if (lane < kRowWords)
+            __stcs(children + row * kRowWords + lane, sh.tiles[q >> 5].rows[q & 31][lane]);
+        }
       }
       const int e = e0 + lane;
       const int q = sh.uniq_of[e] - first;

@@ -653,6 +653,219 @@ __global__ void __launch_bounds__(kGamesBlock, 4) games_attention_kernel(
 // Dynamic shared memory of games_attention_kernel for `length` events.
 constexpr int games_smem_bytes(int length) { return 2 * (1 + length) * kKvPitch * 2; }
 
+// ---- decode attention, staged through shared memory by bulk copies ----------------
+//
+// For caches of up to kStagedSlots slots and up to kStagedHeads heads (the sequence
+// policy's 50 slots and 8 heads).  A persistent block takes one query at a time
+// (all its heads): one thread reads the query's cache row and position and issues
+// one bulk copy (cp.async.bulk, completing on an mbarrier) of the attended key
+// slots of each head and one of the value slots -- (pos + 1) x 64 contiguous bytes
+// each -- into one of two shared-memory stages, so the next query's rows are in
+// flight while this one is computed.  Warp h then works on head h from shared
+// memory: four lanes per slot take the 32-dimension dot product of 8 slots per
+// pass, the warp forms the softmax over the slots (fp32), and lane d sums the
+// weighted values of dimension d.  With an append, the slot pos row is not copied:
+// the new key and value go to the stage from the token's own k_new / v_new and to
+// the cache in global memory.  Every wait is bounded (about 2 s on the global
+// timer); a wait that gives up sets *error and the block stops.
+constexpr int kStagedSlots = 64;
+constexpr int kStagedHeads = 8;
+constexpr int kStagedThreads = 32 * kStagedHeads;
+constexpr int kStages = 2;
+constexpr int kMaxItemsPerBlock = 256;  // queries a block takes (their rows and positions are prefetched)
+constexpr uint64_t kStagedWaitNs = 2'000'000'000ull;
+
+struct StageInfo {
+  i64 row;  // cache row, -1 for an invalid query
+  int pos;
+  int pad;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok = 0;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 255u) == 255u && global_ns() - t0 > kStagedWaitNs) return false;
+  }
+}
+
+// Persistent: block b takes queries b, b + grid, ... (at most kMaxItemsPerBlock).
+// All their cache rows and positions are read first, by the whole block, so a
+// copy is issued without a dependent load; two stages keep one query in flight
+// while one is computed, and two blocks run on each SM.
+__global__ void __launch_bounds__(kStagedThreads, 2) decode_attention_staged_kernel(
+    const __nv_bfloat16* __restrict__ q, i64 ldq, const __nv_bfloat16* __restrict__ k_new,
+    const __nv_bfloat16* __restrict__ v_new, i64 ldn, __nv_bfloat16* keys, __nv_bfloat16* values,
+    i64 n_rows, int heads, int slots, const i64* __restrict__ pos, i64 pos_clamp,
+    const i64* __restrict__ rows, i64 n, float scale, __nv_bfloat16* __restrict__ out, i64 ldo,
+    int32_t* error) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  // Layout: kStages stages x {keys, values} x heads x slots x 64 B, the per-warp
+  // slot weights, the items' rows and positions, the mbarriers.
+  const int stage_half = heads * slots * kDh;  // bf16 elements of one stage's keys
+  __nv_bfloat16* stage_kv = reinterpret_cast<__nv_bfloat16*>(smem);
+  float* weights = reinterpret_cast<float*>(smem + kStages * 2 * stage_half * 2);
+  StageInfo* info = reinterpret_cast<StageInfo*>(weights + kStagedHeads * kStagedSlots);
+  uint64_t* full = reinterpret_cast<uint64_t*>(info + kMaxItemsPerBlock);
+  const int t = threadIdx.x, lane = t & 31, h = t >> 5;
+  const i64 grid = gridDim.x;
+  const int items = n > blockIdx.x ? static_cast<int>((n - blockIdx.x + grid - 1) / grid) : 0;
+  for (int k = t; k < items; k += kStagedThreads) {
+    const i64 i = blockIdx.x + k * grid;
+    const i64 r = rows ? __ldg(rows + i) : i;
+    i64 p = -1;
+    if (r >= 0 && r < n_rows) {
+      if (pos_clamp < 0) {
+        p = __ldg(pos + i);
+      } else {
+        p = __ldg(pos + r);
+        p = p < pos_clamp ? p : pos_clamp;
+      }
+    }
+    const bool ok = p >= 0 && p < slots && r >= 0 && r < n_rows;
+    info[k].row = ok ? r : -1;
+    info[k].pos = ok ? static_cast<int>(p) : -1;
+  }
+  if (t == 0) {
+    for (int s = 0; s < kStages; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  // Thread 0: start item k's copies (the attended slots of every head) into stage s.
+  const auto issue = [&](int k, int s) {
+    const i64 r = info[k].row;
+    const int copied = r >= 0 ? (k_new ? info[k].pos : info[k].pos + 1) : 0;
+    const uint32_t bytes = static_cast<uint32_t>(copied) * kDh * 2;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full[s])),
+                 "r"(bytes * 2u * static_cast<uint32_t>(heads))
+                 : "memory");
+    if (bytes == 0) return;
+    for (int hh = 0; hh < heads; ++hh) {
+      const i64 src = (r * heads + hh) * static_cast<i64>(slots) * kDh;
+      __nv_bfloat16* kd = stage_kv + (2 * s) * stage_half + hh * slots * kDh;
+      __nv_bfloat16* vd = stage_kv + (2 * s + 1) * stage_half + hh * slots * kDh;
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+          ::"r"(smem_u32(kd)), "l"(keys + src), "r"(bytes), "r"(smem_u32(&full[s]))
+          : "memory");
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+          ::"r"(smem_u32(vd)), "l"(values + src), "r"(bytes), "r"(smem_u32(&full[s]))
+          : "memory");
+    }
+  };
+
+  if (t == 0)
+    for (int k = 0; k < kStages - 1 && k < items; ++k) issue(k, k);
+  float* wrow = weights + h * kStagedSlots;
+  bool failed = false;
+  for (int k = 0; k < items; ++k) {
+    const int s = k % kStages;
+    const uint32_t parity = static_cast<uint32_t>((k / kStages) & 1);
+    // Item k + kStages - 1 goes to the stage item k - 1 freed (at k = 0: the one
+    // stage the prologue left unused).
+    const int next = k + kStages - 1;
+    if (t == 0 && next < items) issue(next, next % kStages);
+    if (!stage_wait(&full[s], parity)) {
+      failed = true;
+      if (t == 0 && error) atomicExch(error, 1);
+      break;
+    }
+    const i64 i = blockIdx.x + k * grid;
+    const i64 r = info[k].row;
+    const int p = info[k].pos;
+    if (h < heads) {
+      __nv_bfloat16* o = out + i * ldo + h * kDh;
+      if (r < 0) {
+        o[lane] = __float2bfloat16_rn(0.0f);
+        if (lane == 0 && error) atomicExch(error, 1);
+      } else {
+        __nv_bfloat16* ks = stage_kv + (2 * s) * stage_half + h * slots * kDh;
+        __nv_bfloat16* vs = stage_kv + (2 * s + 1) * stage_half + h * slots * kDh;
+        if (k_new) {  // the token's own key and value: slot p of the stage and the cache
+          const __nv_bfloat16 kn = k_new[i * ldn + h * kDh + lane];
+          const __nv_bfloat16 vn = v_new[i * ldn + h * kDh + lane];
+          ks[p * kDh + lane] = kn;
+          vs[p * kDh + lane] = vn;
+          const i64 dst = ((r * heads + h) * static_cast<i64>(slots) + p) * kDh + lane;
+          keys[dst] = kn;
+          values[dst] = vn;
+          __syncwarp();
+        }
+        // Scores: lane 4j + c holds dimensions 8c .. 8c + 7 of slot 8 * pass + j.
+        float qf[8];
+        bf16x8(__ldg(reinterpret_cast<const uint4*>(q + i * ldq + h * kDh) + (lane & 3)), qf);
+        float mx = -INFINITY;
+        for (int t0 = 0; t0 <= p; t0 += 8) {
+          const int slot = t0 + (lane >> 2);
+          float d = 0.0f;
+          if (slot <= p) {
+            float kf[8];
+            bf16x8(reinterpret_cast<const uint4*>(ks + slot * kDh)[lane & 3], kf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d = fmaf(kf[e], qf[e], d);
+          }
+          d += __shfl_xor_sync(kFull, d, 1);
+          d += __shfl_xor_sync(kFull, d, 2);
+          if (slot <= p) {
+            d *= scale;
+            if ((lane & 3) == 0) wrow[slot] = d;
+            mx = fmaxf(mx, d);
+          }
+        }
+        mx = warp_max(mx);
+        __syncwarp();
+        float sum = 0.0f;
+        for (int j = lane; j <= p; j += 32) {
+          const float w = expf(wrow[j] - mx);
+          wrow[j] = w;
+          sum += w;
+        }
+        sum = warp_sum(sum);
+        __syncwarp();
+        // Output: lane d sums the weighted values of dimension d.
+        float acc = 0.0f;
+        for (int j = 0; j <= p; ++j) acc = fmaf(wrow[j], __bfloat162float(vs[j * kDh + lane]), acc);
+        o[lane] = __float2bfloat16_rn(acc / sum);
+      }
+    }
+    __syncthreads();  // stage s and the weights are free again
+  }
+  if (failed) {
+    // Let copies already issued land before the block's shared memory goes away.
+    __syncthreads();
+    if (t == 0)
+      for (int s = 0; s < kStages; ++s) stage_wait(&full[s], 0), stage_wait(&full[s], 1);
+  }
+  __syncthreads();
+}
+
+size_t staged_smem_bytes(int heads, int slots) {
+  return static_cast<size_t>(kStages) * 2 * heads * slots * kDh * 2 +
+         kStagedHeads * kStagedSlots * 4 + kMaxItemsPerBlock * sizeof(StageInfo) +
+         kStages * sizeof(uint64_t);
+}
+
 }  // namespace
 
 extern "C" {
@@ -671,6 +884,30 @@ int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new, co
   if (!aligned(q, 16) || ldq % 8 || !aligned(keys, 16) || !aligned(values, 16) || !aligned(out, 2) ||
       (k_new && (!aligned(k_new, 16) || !aligned(v_new, 16) || ldn % 8)))
     return CUGO_B200_ERR_ALIGN;
+  if (heads <= kStagedHeads && slots <= kStagedSlots &&
+      staged_smem_bytes(heads, slots) <= static_cast<size_t>(227 * 1024)) {
+    const size_t smem = staged_smem_bytes(heads, slots);
+    static size_t configured = 0;
+    if (smem > configured) {
+      if (cudaFuncSetAttribute(decode_attention_staged_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)) != cudaSuccess)
+        return CUGO_B200_ERR_LAUNCH;
+      configured = smem;
+    }
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    i64 grid = n < 2 * sms ? n : 2 * sms;  // two blocks per SM
+    if ((n + grid - 1) / grid > kMaxItemsPerBlock) grid = (n + kMaxItemsPerBlock - 1) / kMaxItemsPerBlock;
+    decode_attention_staged_kernel<<<static_cast<unsigned>(grid), kStagedThreads, smem, stream>>>(
+        static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k_new),
+        static_cast<const __nv_bfloat16*>(v_new), ldn, static_cast<__nv_bfloat16*>(keys),
+        static_cast<__nv_bfloat16*>(values), n_rows, heads, slots, pos, pos_clamp, rows, n, scale,
+        static_cast<__nv_bfloat16*>(out), ldo, error);
+    return launch_status();
+  }
   decode_attention_kernel<<<blocks_for_warps(n * heads), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k_new),
       static_cast<const __nv_bfloat16*>(v_new), ldn, static_cast<__nv_bfloat16*>(keys),
