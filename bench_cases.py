@@ -74,7 +74,8 @@ def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
     eager and CUDA-graphed, and the same step with plain PyTorch modules under bf16
     autocast (cuBLAS), eager and graphed.  FLOPs: 3 x 2 x b x weights (forward,
     data gradient, weight gradient)."""
-    from cugo_b200.ppo import GraphedPpoStep, Minibatch, PpoStep, critic_input, fused_actor, fused_critic
+    from cugo_b200.ppo import (GraphedPpoStep, Minibatch, NativePpoStep, PpoStep, critic_input,
+                               fused_actor, fused_critic)
     dev = torch.device("cuda")
     g = torch.Generator(device="cpu").manual_seed(0)
     legal = torch.rand((b, 179), generator=g) < 0.1
@@ -87,10 +88,16 @@ def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
     actor, critic = fused_actor().to(dev), fused_critic().to(dev)
     opt = torch.optim.Adam(list(actor.parameters()) + list(critic.parameters()), lr=3e-4,
                            capturable=True)
-    step = PpoStep(actor, critic, opt)
+    step = NativePpoStep(actor, critic, opt)
     sec_eager = _time(lambda: step.step(mb), warmup, iters)
     graphed = GraphedPpoStep(step, mb)
     sec = _time(lambda: graphed(mb), warmup, iters)
+    # The same networks on the autograd step (fused GEMMs, torch elementwise and
+    # reductions), graphed.
+    a2, c2 = fused_actor().to(dev), fused_critic().to(dev)
+    opt2 = torch.optim.Adam(list(a2.parameters()) + list(c2.parameters()), lr=3e-4, capturable=True)
+    graphed2 = GraphedPpoStep(PpoStep(a2, c2, opt2), mb)
+    sec_autograd = _time(lambda: graphed2(mb), warmup, iters)
 
     def torch_mlp(inputs, outputs):
         layers = [torch.nn.Linear(inputs, 512)] + [torch.nn.Linear(512, 512) for _ in range(6)]
@@ -137,8 +144,10 @@ def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
     flops = 3 * 2 * b * sum(p.numel() for n, p in list(actor.named_parameters()) +
                             list(critic.named_parameters()) if n.endswith("weight"))
     return dict(seconds=sec, tflops=flops / sec / 1e12, eager_seconds=sec_eager,
+                autograd_step_seconds=sec_autograd,
                 torch_autocast_seconds=sec_torch, torch_autocast_tflops=flops / sec_torch / 1e12,
-                torch_autocast_eager_seconds=sec_torch_eager)
+                torch_autocast_eager_seconds=sec_torch_eager,
+                speedup_vs_torch_autocast=sec_torch / sec)
 
 
 def allaction_case(r: int, warmup: int = 3, iters: int = 10) -> dict:

@@ -21,7 +21,7 @@ LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libcugo_b200.so"
 
 SOURCES = ["env_kernels.cu", "drivers.cu", "policy_kernels.cu", "mlp_kernels.cu", "seq_kernels.cu",
-           "rollout_kernels.cu"]
+           "rollout_kernels.cu", "update_kernels.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--cudart", "static",
               "-Xcompiler", "-fvisibility=hidden"]

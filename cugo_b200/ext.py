@@ -73,6 +73,12 @@ _SIGNATURES: dict[str, list] = {
                                      _VP, _VP, _I32, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
                                      _VP, _VP, _VP, _VP],
     "cugo_b200_wait_timeout_probe": [_I64, _VP, _VP, _VP],
+    "cugo_b200_ppo_loss": [_VP, _I64, _VP, _VP, _VP, _VP, _VP, _I64, _VP, _I64, ctypes.c_float,
+                           _VP, ctypes.c_float, _VP, _I64, _VP, _VP, _VP],
+    "cugo_b200_colsum_bf16": [_VP, _I64, _VP, _I64, _I32, _VP, _I64, _I64, _I32, _VP, _VP, _I64,
+                              _VP],
+    "cugo_b200_scalar_head_backward": [_VP, _VP, _VP, _I64, _I32, _VP, _I64, _I64, _I32, _VP, _VP,
+                                       _VP, _VP, _I64, _VP],
     "cugo_b200_stock_planes_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _I32, _VP],
     "cugo_b200_wave_tail": [_I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
                             _VP, _VP, _VP, _VP, _VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP,
@@ -89,6 +95,7 @@ _CONSTANTS = {
     "STATUS_OK": "cugo_b200_status_ok",
 }
 _EXTRA_CONSTANTS = {"EVENT_IN": "cugo_b200_event_inputs", "START_IN": "cugo_b200_start_inputs"}
+_INT64_FUNCTIONS = {"cugo_b200_colsum_scratch_floats": [_I64, _I32]}
 _ERRORS = {-1: "invalid argument", -2: "misaligned pointer", -3: "kernel launch failed"}
 
 _LIB: ctypes.CDLL | None = None
@@ -116,6 +123,9 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
     for fn_name in [*_CONSTANTS.values(), *_EXTRA_CONSTANTS.values()]:
         getattr(lib, fn_name).restype = ctypes.c_int64
         getattr(lib, fn_name).argtypes = []
+    for fn_name, argtypes in _INT64_FUNCTIONS.items():
+        getattr(lib, fn_name).restype = ctypes.c_int64
+        getattr(lib, fn_name).argtypes = argtypes
     lib.cugo_b200_abi_version.restype = ctypes.c_int
     _LIB = lib
     return lib
@@ -460,6 +470,63 @@ class CugoB200Extension:
                 _ptr(store["opp_hand"]), _ptr(store["stock"]), _ptr(store["env_ids"]),
                 _ptr(store["seat"]), _ptr(store["learner"]), _ptr(overflow),
                 self._stream(states.device)), "record_transitions")
+
+    def ppo_loss(self, logits: torch.Tensor, legal: torch.Tensor, actions: torch.Tensor,
+                 logp_old: torch.Tensor, adv: torch.Tensor, value: torch.Tensor,
+                 ret: torch.Tensor, clip: float, entropy_coef: torch.Tensor, value_coef: float,
+                 dlogits: torch.Tensor, dvalue: torch.Tensor, stats: torch.Tensor) -> None:
+        """The PPO minibatch losses and their gradients in one kernel (see the C
+        declaration): logits fp32 [b, >=179] (rows may be padded), value fp32 [b] or
+        [b, 1] (any row stride); writes dlogits bf16 [b, ldd >= 179] (pad columns 0),
+        dvalue fp32 [b] and the five statistics' means into stats fp32 [5]."""
+        b = logits.shape[0]
+        if logits.dtype != torch.float32 or logits.stride(1) != 1 or logits.shape[1] < 179:
+            raise RuntimeError("ppo_loss: logits fp32 [b, >= 179] with unit column stride")
+        if dlogits.dtype != torch.bfloat16 or dlogits.stride(1) != 1 or dlogits.shape[0] != b:
+            raise RuntimeError("ppo_loss: dlogits bf16 [b, >= 179]")
+        if legal.dtype != torch.bool or not legal.is_contiguous() or legal.shape != (b, 179):
+            raise RuntimeError("ppo_loss: legal bool [b, 179] contiguous")
+        with torch.cuda.device(logits.device):
+            _check(self._lib.cugo_b200_ppo_loss(
+                _ptr(logits), logits.stride(0), _ptr(legal), _ptr(actions), _ptr(logp_old),
+                _ptr(adv), _ptr(value), value.stride(0), _ptr(ret), b, float(clip),
+                _ptr(entropy_coef), float(value_coef), _ptr(dlogits), dlogits.stride(0),
+                _ptr(dvalue), _ptr(stats), self._stream(logits.device)), "ppo_loss")
+
+    def _colsum_scratch(self, rows: int, n: int, device: torch.device) -> torch.Tensor:
+        """The per-block partial sums' buffer, one per device, grown as needed (keep
+        the sizes a CUDA graph replays within what it saw at capture)."""
+        need = int(self._lib.cugo_b200_colsum_scratch_floats(rows, n))
+        cache = self.__dict__.setdefault("_scratch", {})
+        buf = cache.get(device)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(max(need, 1), dtype=torch.float32, device=device)
+            cache[device] = buf
+        return buf
+
+    def colsum_bf16(self, x: torch.Tensor, out: torch.Tensor, z: torch.Tensor | None = None,
+                    act: int = 0, dz: torch.Tensor | None = None) -> None:
+        """out (fp32 [n]) = column sums of bf16 x [rows, n]; with z, of dz = x * act'(z),
+        which is written to dz (bf16).  Deterministic (fixed summation order)."""
+        rows, n = x.shape
+        with torch.cuda.device(x.device):
+            scratch = self._colsum_scratch(rows, n, x.device)
+            _check(self._lib.cugo_b200_colsum_bf16(
+                _ptr(x), x.stride(0), _ptr(z), z.stride(0) if z is not None else 0, act, _ptr(dz),
+                dz.stride(0) if dz is not None else 0, rows, n, _ptr(out), _ptr(scratch),
+                scratch.numel(), self._stream(x.device)), "colsum_bf16")
+
+    def scalar_head_backward(self, dv: torch.Tensor, w: torch.Tensor, h: torch.Tensor, act: int,
+                             dh: torch.Tensor, dh_sums: torch.Tensor, dw: torch.Tensor,
+                             db: torch.Tensor) -> None:
+        """Backward of a one-output head v = w . act(h) + b (see the C declaration)."""
+        rows, n = h.shape
+        with torch.cuda.device(h.device):
+            scratch = self._colsum_scratch(rows, n, h.device)
+            _check(self._lib.cugo_b200_scalar_head_backward(
+                _ptr(dv), _ptr(w), _ptr(h), h.stride(0), act, _ptr(dh), dh.stride(0), rows, n,
+                _ptr(dh_sums), _ptr(dw), _ptr(db), _ptr(scratch), scratch.numel(),
+                self._stream(h.device)), "scalar_head_backward")
 
     def wait_timeout_probe(self, limit_ns: int, device: torch.device | str = "cuda"):
         """Runs the bounded mbarrier wait of the GEMM kernels on a barrier nothing

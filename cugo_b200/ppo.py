@@ -241,6 +241,125 @@ class FusedResidualMlp(nn.Module):
         return out[:, :n_out]
 
 
+# ---- the update's forward and backward without autograd ------------------------------
+#
+# NativePpoStep runs both networks' forward with the activations kept, the fused
+# loss kernel (cugo_b200_ppo_loss) and the backward written out layer by layer,
+# every gradient landing in the parameter's .grad buffer directly:
+#   head (actor)   dW = dy^T g (cuBLAS, fp32 out), db = colsum(dy), dg = dy W on the
+#                  tcgen05 GEMM (dy bf16 with rows padded to 184 columns)
+#   head (critic)  one kernel: dh, its column sums, dW and db of the scalar head
+#   act'(h)        fused with the column sums that are the producing layer's bias
+#                  gradient (cugo_b200_colsum_bf16)
+#   blocks         dW2 = dh^T u, du = dh W2, dz = du act'(z) (+ db1), dW1 = dz^T h,
+#                  dh += dz W1 on the GEMM (residual epilogue), db2 of the block
+#                  below = colsum(dh)
+#   input layer    dW = dh^T x
+
+_ACT_GRAD = {"relu": 1, "silu": 2}
+
+
+def _train_weights(net: "FusedResidualMlp"):
+    """bf16 weights (the input layer's padded to 16-byte rows), fp32 biases and the
+    transposed weights of the backward, cached per parameter version."""
+    params = [t for l in net.linears() for t in (l.weight, l.bias)]
+    key = tuple((p.data_ptr(), p._version) for p in params)
+    if getattr(net, "_tkey", None) != key:
+        ws, bs = net._weights(params)
+        wt = [w.t().contiguous() for w in ws[1:-1]]
+        out_w = ws[-1]
+        n_out, hidden = out_w.shape
+        wt_out = torch.zeros((hidden, _pad8(n_out)), dtype=torch.bfloat16, device=out_w.device)
+        wt_out[:, :n_out] = out_w.t()
+        net._tcache = (ws, bs, wt, wt_out)
+        net._tkey = key
+    return net._tcache
+
+
+@torch.no_grad()
+def train_forward(net: "FusedResidualMlp", x: torch.Tensor):
+    """The forward of a training step, keeping what the backward reads: returns
+    (out fp32 [m, n_out] (rows padded to 16 bytes), saved activations)."""
+    ext = net.ext
+    kind = net.activation
+    ws, bs, _, _ = _train_weights(net)
+    m = x.shape[0]
+    k_in = net.inp.in_features
+    if x.dtype == torch.bfloat16 and x.stride(1) == 1 and x.stride(0) % 8 == 0:
+        xb = x[:, :k_in]
+    else:
+        xp = torch.zeros((m, _pad8(k_in)), dtype=torch.bfloat16, device=x.device)
+        xp[:, :k_in] = x[:, :k_in]
+        xb = xp[:, :k_in]
+    h = ext.linear(xb, ws[0][:, :k_in], bs[0])
+    saved = {"x": xb, "h": [], "z": [], "u": []}
+    for i in range(net.n_blocks):
+        z = ext.linear(h, ws[1 + 2 * i], bs[1 + 2 * i])
+        u = _act(z, kind)
+        saved["h"].append(h)
+        saved["z"].append(z)
+        saved["u"].append(u)
+        h = ext.linear(u, ws[2 + 2 * i], bs[2 + 2 * i], residual=h)
+    saved["h_last"] = h
+    n_out = ws[-1].shape[0]
+    out = torch.empty((m, (n_out + 3) // 4 * 4), dtype=torch.float32, device=x.device)
+    if n_out == 1:
+        g = None
+        ext.rowdot(h if kind == "none" else _act(h, kind), ws[-1].reshape(-1).float(), bs[-1].float(),
+                   out=out[:, 0])
+    else:
+        g = _act(h, kind)
+        ext.linear(g, ws[-1], bs[-1], out=out[:, :n_out])
+    saved["g"] = g
+    return out[:, :n_out], saved
+
+
+def _grad(p: torch.Tensor) -> torch.Tensor:
+    if p.grad is None:
+        p.grad = torch.zeros_like(p)
+    return p.grad
+
+
+@torch.no_grad()
+def train_backward(net: "FusedResidualMlp", saved: dict, dy: torch.Tensor | None = None,
+                   dv: torch.Tensor | None = None) -> None:
+    """Writes every parameter's gradient into its .grad: dy bf16 [m, >= n_out] (rows
+    of 16-byte multiples; columns past n_out zero) for a matrix head, dv fp32 [m]
+    for a one-output head."""
+    ext = net.ext
+    kind = net.activation
+    act = _ACT_GRAD[kind]
+    ws, _, wt, wt_out = _train_weights(net)
+    lin = net.linears()
+    h_last = saved["h_last"]
+    m, hidden = h_last.shape
+    dh = torch.empty_like(h_last)
+    # Gradient of the bias of the layer that produced h_last.
+    below = lin[-2]
+    if dv is not None:  # one-output head: one pass over h_last
+        ext.scalar_head_backward(dv, ws[-1].reshape(-1), h_last, act, dh, _grad(below.bias),
+                                 _grad(lin[-1].weight).view(-1), _grad(lin[-1].bias))
+    else:
+        n_out = lin[-1].out_features
+        torch.mm(dy[:, :n_out].t(), saved["g"], out_dtype=torch.float32, out=_grad(lin[-1].weight))
+        sums = torch.empty(dy.shape[1], dtype=torch.float32, device=dy.device)
+        ext.colsum_bf16(dy, sums)
+        _grad(lin[-1].bias).copy_(sums[:n_out])
+        dg = ext.linear(dy[:, :n_out], wt_out[:, :n_out])
+        ext.colsum_bf16(dg, _grad(below.bias), z=h_last, act=act, dz=dh)
+    for i in reversed(range(net.n_blocks)):
+        h, z, u = saved["h"][i], saved["z"][i], saved["u"][i]
+        fc1, fc2 = lin[1 + 2 * i], lin[2 + 2 * i]
+        torch.mm(dh.t(), u, out_dtype=torch.float32, out=_grad(fc2.weight))
+        du = ext.linear(dh, wt[2 * i + 1])                      # dh W2
+        dz = torch.empty_like(du)
+        ext.colsum_bf16(du, _grad(fc1.bias), z=z, act=act, dz=dz)
+        torch.mm(dz.t(), h, out_dtype=torch.float32, out=_grad(fc1.weight))
+        dh = ext.linear(dz, wt[2 * i], residual=dh)              # dh + dz W1
+        ext.colsum_bf16(dh, _grad(lin[2 * i].bias))              # the layer below's bias
+    torch.mm(dh.t(), saved["x"], out_dtype=torch.float32, out=_grad(lin[0].weight))
+
+
 def fused_actor(hidden: int = 512, blocks: int = 3) -> FusedResidualMlp:
     """PpoActor's shape: 720 features -> 179 logits, zero-initialised output layer."""
     return FusedResidualMlp(FEATURES, ACTIONS, hidden, blocks, "silu", zero_out=True)
@@ -353,6 +472,56 @@ class PpoStep:
             self.sums += torch.stack((policy_loss.detach(), value_loss.detach(), entropy.detach(), kl,
                                       ((ratio - 1).abs() > self.clip).float().mean(),
                                       torch.ones_like(kl)))
+
+
+class NativePpoStep(PpoStep):
+    """PpoStep without autograd for two FusedResidualMlp networks (the actor with a
+    matrix head, a scalar critic): train_forward of both, the fused loss kernel,
+    train_backward of both writing the gradients, then the same clipping, optimizer
+    step and statistics.  Gradients of the hidden layers' weights are fp32 products
+    of the bf16 operands (autograd's path rounds them to bf16)."""
+
+    def __init__(self, actor: FusedResidualMlp, critic: FusedResidualMlp,
+                 optimizer: torch.optim.Optimizer, clip: float = 0.2, value_coef: float = 0.5,
+                 grad_clip: float = 1.0, world: int = 1) -> None:
+        super().__init__(actor, critic, optimizer, clip, value_coef, grad_clip, world)
+        self.stats = torch.zeros(5, device=self.sums.device)
+        self.ones = torch.ones(1, device=self.sums.device)
+
+    @staticmethod
+    def supports(actor: nn.Module, critic: nn.Module) -> bool:
+        return (isinstance(actor, FusedResidualMlp) and isinstance(critic, FusedResidualMlp)
+                and not critic.value_bins and critic.out.out_features == 1
+                and actor.out.out_features == ACTIONS and actor.inp.in_features == FEATURES)
+
+    def step(self, mb: Minibatch) -> None:
+        ext = self.actor.ext
+        logits, a_saved = train_forward(self.actor, mb.features)
+        stock = mb.stock if getattr(self.critic, "stock", False) else None
+        value, c_saved = train_forward(self.critic, critic_input(mb.features, mb.opp_hand, stock))
+        b = logits.shape[0]
+        dy = torch.empty((b, _pad8(ACTIONS)), dtype=torch.bfloat16, device=logits.device)
+        dv = torch.empty(b, dtype=torch.float32, device=logits.device)
+        ext.ppo_loss(logits, mb.legal, mb.actions, mb.logp_old, mb.adv, value, mb.ret, self.clip,
+                     self.entropy_coef, self.value_coef, dy, dv, self.stats)
+        train_backward(self.actor, a_saved, dy=dy)
+        train_backward(self.critic, c_saved, dv=dv)
+        allreduce_gradients([p for g in self.groups for p in g], self.world)
+        for group in self.groups:
+            nn.utils.clip_grad_norm_(group, self.grad_clip, foreach=True)
+        self.optimizer.step()
+        self.last_kl.copy_(self.stats[3])
+        self.sums[:5] += self.stats
+        self.sums[5:] += self.ones
+
+
+def make_ppo_step(actor: nn.Module, critic: nn.Module, optimizer: torch.optim.Optimizer,
+                  clip: float = 0.2, value_coef: float = 0.5, grad_clip: float = 1.0,
+                  world: int = 1) -> PpoStep:
+    """The native step where both networks are FusedResidualMlp (scalar critic),
+    else the autograd one."""
+    cls = NativePpoStep if NativePpoStep.supports(actor, critic) else PpoStep
+    return cls(actor, critic, optimizer, clip, value_coef, grad_clip, world)
 
 
 class GraphedPpoStep:

@@ -40,7 +40,7 @@ from torch import nn
 
 from .evaluate import make_seeds
 from .ext import load_extension
-from .ppo import GraphedPpoStep, Minibatch, PpoStep, critic_input
+from .ppo import GraphedPpoStep, Minibatch, critic_input, make_ppo_step
 from .rounds import DONE_BYTE, RunningSet, choose_actions, fused_sampler_params
 
 CHECK_EVERY = 4
@@ -287,7 +287,7 @@ class PpoTrainer:
         self.actor, self.critic, self.minibatch = actor, critic, minibatch
         params = list(actor.parameters()) + list(critic.parameters())
         self.optimizer = torch.optim.Adam(params, lr=lr, capturable=use_graph)
-        self.step = PpoStep(actor, critic, self.optimizer, clip, value_coef, grad_clip, world)
+        self.step = make_ppo_step(actor, critic, self.optimizer, clip, value_coef, grad_clip, world)
         self.use_graph = use_graph
         self.world = world
         self.graphed: GraphedPpoStep | None = None

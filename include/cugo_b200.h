@@ -306,6 +306,56 @@ CUGO_B200_API int cugo_b200_pack_legal(const bool* legal, int64_t m, uint64_t* b
 CUGO_B200_API int cugo_b200_wait_timeout_probe(int64_t limit_ns, int32_t* error,
                                                int64_t* waited_ns, cudaStream_t stream);
 
+/* ---- PPO update (PpoUpdater._step, python/cugo_ppo50.py:558-623) ----------------- */
+
+/* The plain-target PPO losses of a minibatch of b rows and their gradients in one
+ * pass (it replaces the masked log_softmax, gather, ratio, clipped surrogate,
+ * entropy and smooth-L1 value loss of python/cugo_ppo50.py:572-603 and their
+ * autograd backward): loss = mean(-min(r A, clamp(r, 1 - clip, 1 + clip) A))
+ * - entropy_coef mean(entropy) + value_coef mean(smooth_l1(value, ret)), r =
+ * exp(log p_new(action) - logp_old), log p from the logits masked to -1e30 where
+ * legal is 0.  logits fp32 [b, ldl >= 179]; legal bool [b, 179]; actions int64;
+ * logp_old, adv, ret fp32 [b]; value fp32 with row stride value_ld; entropy_coef a
+ * device fp32 scalar.  Writes d loss / d logits as bf16 [b, ldd >= 179] (columns
+ * 179 .. ldd - 1 zero), d loss / d value fp32 [b], and stats fp32 [5] = the
+ * minibatch means of the policy loss, value loss, entropy, KL estimate
+ * (r - 1) - log r and clip fraction (|r - 1| > clip). */
+CUGO_B200_API int cugo_b200_ppo_loss(const float* logits, int64_t ldl, const bool* legal,
+                                     const int64_t* actions, const float* logp_old,
+                                     const float* adv, const float* value, int64_t value_ld,
+                                     const float* ret, int64_t b, float clip,
+                                     const float* entropy_coef, float value_coef, void* dlogits,
+                                     int64_t ldd, float* dvalue, float* stats,
+                                     cudaStream_t stream);
+
+/* Column sums (fp32 [n], 8 <= n <= 2048, n a multiple of 8) of bf16 x [rows, n]
+ * (row stride ldx); with z (bf16, ldz), of dz = x * act'(z) (act 0 none, 1 ReLU,
+ * 2 SiLU), which is also written to dz (bf16, ldd).  The bias gradients of the
+ * update's backward.  scratch: the caller's fp32 buffer of at least
+ * cugo_b200_colsum_scratch_floats(rows, n) floats for the per-block partial sums,
+ * which a second launch adds up in a fixed order (the same result on every run);
+ * a smaller one returns CUGO_B200_ERR_CAPACITY.  No counterpart in the reference
+ * (torch reductions there). */
+CUGO_B200_API int cugo_b200_colsum_bf16(const void* x, int64_t ldx, const void* z, int64_t ldz,
+                                        int32_t act, void* dz, int64_t ldd, int64_t rows,
+                                        int32_t n, float* sums, float* scratch,
+                                        int64_t scratch_floats, cudaStream_t stream);
+
+/* Scratch floats cugo_b200_colsum_bf16 and cugo_b200_scalar_head_backward need for
+ * `rows` rows of n columns. */
+CUGO_B200_API int64_t cugo_b200_colsum_scratch_floats(int64_t rows, int32_t n);
+
+/* Backward of a one-output head v = w . act(h) + b over h bf16 [rows, n] (the
+ * critic's value head): dh = dv w act'(h) (bf16, ldd), dh_sums = its column sums,
+ * dw = sum_i dv_i act(h_i) (fp32 [n]), db = sum_i dv_i (fp32 [1]); dv fp32 [rows],
+ * w bf16 [n]; scratch as for cugo_b200_colsum_bf16.  No counterpart in the
+ * reference. */
+CUGO_B200_API int cugo_b200_scalar_head_backward(const float* dv, const void* w, const void* h,
+                                                 int64_t ldh, int32_t act, void* dh, int64_t ldd,
+                                                 int64_t rows, int32_t n, float* dh_sums,
+                                                 float* dw, float* db, float* scratch,
+                                                 int64_t scratch_floats, cudaStream_t stream);
+
 /* Policy forward that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory — for example a Go/Java/Rust
  * serving process that passes only its own fixed input and output buffers and keeps

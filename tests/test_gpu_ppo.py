@@ -180,3 +180,98 @@ def test_graphed_step_equals_eager_step():
                      list(nets[1][0].parameters()) + list(nets[1][1].parameters())):
         assert torch.allclose(a, b2, rtol=1e-5, atol=1e-6)
     assert torch.allclose(nets[0][2].sums, nets[1][2].sums, rtol=1e-5, atol=1e-6)
+
+
+def _minibatch(b, seed):
+    from cugo_b200.ppo import Minibatch
+    g = torch.Generator().manual_seed(seed)
+    legal = torch.rand((b, 179), generator=g) < 0.1
+    legal[:, 0] = True
+    logits0 = torch.randn((b, 179), generator=g)
+    actions = torch.multinomial(torch.softmax(logits0.masked_fill(~legal, -1e30), 1), 1).squeeze(1)
+    return Minibatch(features=torch.rand((b, 720), generator=g).to(DEV, torch.bfloat16),
+                     legal=legal.to(DEV), actions=actions.to(DEV),
+                     logp_old=(torch.randn(b, generator=g) * 0.1 - 2.0).to(DEV),
+                     opp_hand=torch.randint(0, 1 << 50, (b,), generator=g).to(DEV),
+                     adv=torch.randn(b, generator=g).to(DEV), ret=torch.randn(b, generator=g).to(DEV))
+
+
+@pytest.mark.parametrize("activation", ["silu", "relu"])
+def test_native_step_gradients_match_reference(activation):
+    """The native step (train_forward, the fused loss kernel, train_backward) against
+    the reference's step restated in PyTorch under bf16 autocast: the three losses
+    and the KL / clip-fraction statistics within 1e-2 relative, every parameter's
+    gradient (before clipping) within 1.5x the autocast gradient's own error against
+    fp32 plus 1e-3 of its scale, and per network cosine >= 0.999."""
+    from cugo_b200.ppo import NativePpoStep, critic_input, train_backward, train_forward
+    actor, actor_ref = _twins(720, 179, seed=2, activation=activation)
+    critic, critic_ref = _twins(770, 1, seed=3, squeeze=True, activation=activation)
+    mb = _minibatch(8192, 4)
+    opt = torch.optim.Adam(list(actor.parameters()) + list(critic.parameters()), lr=3e-4)
+    step = NativePpoStep(actor, critic, opt)
+    step.entropy_coef.fill_(0.05)
+    ext = actor.ext
+    logits, a_saved = train_forward(actor, mb.features)
+    value, c_saved = train_forward(critic, critic_input(mb.features, mb.opp_hand))
+    dy = torch.empty((8192, 184), dtype=torch.bfloat16, device=DEV)
+    dv = torch.empty(8192, device=DEV)
+    stats = torch.zeros(5, device=DEV)
+    ext.ppo_loss(logits, mb.legal, mb.actions, mb.logp_old, mb.adv, value, mb.ret, 0.2,
+                 step.entropy_coef, 0.5, dy, dv, stats)
+    train_backward(actor, a_saved, dy=dy)
+    train_backward(critic, c_saved, dv=dv)
+    assert not dy[:, 179:].any()
+
+    def reference(autocast: bool):
+        for net in (actor_ref, critic_ref):
+            net.zero_grad()
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+            lg = actor_ref(mb.features.float()).float()
+            v = critic_ref(critic_input(mb.features, mb.opp_hand).float()).float().squeeze(-1)
+        pl, vl, ent = ppo_losses_reference(lg, v, mb.legal, mb.actions, mb.logp_old, mb.adv, mb.ret, 0.2)
+        (pl - 0.05 * ent + 0.5 * vl).backward()
+        lp = torch.log_softmax(lg.masked_fill(~mb.legal, -1.0e30), 1).gather(
+            1, mb.actions.unsqueeze(1)).squeeze(1)
+        r = (lp - mb.logp_old).exp()
+        kl = ((r - 1) - (lp - mb.logp_old)).mean()
+        cf = ((r - 1).abs() > 0.2).float().mean()
+        grads = [p.grad.detach().float().clone() for n in (actor_ref, critic_ref) for p in n.parameters()]
+        return [float(x) for x in (pl, vl, ent, kl, cf)], grads
+
+    stats_auto, g_auto = reference(True)
+    _, g_exact = reference(False)
+    for got, want in zip(stats.tolist(), stats_auto):
+        assert abs(got - want) <= 1e-2 * abs(want) + 1e-4, (got, want)
+    ours = [p.grad.detach().float() for n in (actor, critic) for p in n.parameters()]
+    names = [f"actor.{n}" for n, _ in actor.named_parameters()] + \
+            [f"critic.{n}" for n, _ in critic.named_parameters()]
+    for name, a, h, e in zip(names, ours, g_auto, g_exact):
+        scale = float(e.abs().max())
+        err, err_ref = float((a - e).abs().max()), float((h - e).abs().max())
+        assert err <= 1.5 * err_ref + 1e-3 * scale, (name, err, err_ref, scale)
+    for k0, k1 in ((0, len(list(actor.parameters()))), (len(list(actor.parameters())), len(ours))):
+        a = torch.cat([t.flatten() for t in ours[k0:k1]])
+        r = torch.cat([t.flatten() for t in g_exact[k0:k1]])
+        assert float(torch.dot(a, r) / (a.norm() * r.norm())) >= 0.999
+
+
+def test_native_graphed_step_equals_eager_step():
+    from cugo_b200.ppo import GraphedPpoStep, NativePpoStep
+    nets = []
+    for _ in range(2):
+        actor, _ = _twins(720, 179, seed=5)
+        critic, _ = _twins(770, 1, seed=6, squeeze=True)
+        opt = torch.optim.Adam(list(actor.parameters()) + list(critic.parameters()), lr=3e-4,
+                               capturable=True)
+        nets.append((actor, critic, NativePpoStep(actor, critic, opt)))
+    batches = [_minibatch(4096, 10 + i) for i in range(3)]
+    graphed = GraphedPpoStep(nets[1][2], batches[0])
+    for mb in batches:
+        nets[0][2].step(mb)
+        graphed(mb)
+    torch.cuda.synchronize()
+    for a, b2 in zip(list(nets[0][0].parameters()) + list(nets[0][1].parameters()),
+                     list(nets[1][0].parameters()) + list(nets[1][1].parameters())):
+        assert torch.allclose(a, b2, rtol=1e-5, atol=1e-6)
+    assert torch.allclose(nets[0][2].sums, nets[1][2].sums, rtol=1e-4, atol=1e-6)
+    assert int(nets[0][2].sums[5]) == 3
