@@ -187,166 +187,182 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
 }
 
 // branch_indexed with identical children made once.  A child depends only on
-// (parent row, action), so a block takes kBranchEntries consecutive entries, finds
-// the distinct (parent, action) pairs among them (a shared-memory hash keyed by the
-// pair; each pair's representative is its lowest entry), steps only the distinct
-// pairs -- packed into the block's warps, 32 per warp and kBranchBlock per pass --
-// and after each pass writes the child rows and outputs of every entry whose pair
-// the pass made, from the stepped tiles in shared memory.  An entry with an invalid
-// parent id gets a zero child (status -1, done 1, as step_indexed reports it).
-constexpr int kBranchWarps = 4;
-constexpr int kBranchBlock = 32 * kBranchWarps;
-constexpr int kBranchPer = 2;  // entries per thread
-constexpr int kBranchEntries = kBranchBlock * kBranchPer;
+// (parent row, action), so each warp takes kBranchEntries consecutive entries on its
+// own (no block-wide barrier: while one warp runs the rule code, the others on the
+// SM write children), finds the distinct (parent, action) pairs among them in a
+// shared-memory hash keyed by the pair (numbered in order of first occurrence),
+// steps the distinct pairs 32 per pass, and writes the child row and outputs of
+// every entry from the stepped tile.  Entries with an invalid parent id share one
+// zero child (status -1, done 1, as step_indexed reports it).
+constexpr int kBranchWarps = 2;      // independent warps per block
+#ifndef CB_BRANCH_MIN_BLOCKS
+#define CB_BRANCH_MIN_BLOCKS 6
+#endif
+constexpr int kBranchEntries = 256;  // entries per warp
+constexpr int kBranchPerLane = kBranchEntries / 32;
 constexpr int kBranchHash = 2 * kBranchEntries;  // open addressing, load factor <= 1/2
+constexpr unsigned long long kBranchEmpty = ~0ull;
+constexpr unsigned long long kBranchInvalid = ~0ull - 1;  // every entry with a bad parent id
 
-struct BranchShared {
-  WarpTile tiles[kBranchWarps];
+struct BranchWarpShared {
+  u64 rows[32][kRowWords];          // stepped children of the current pass
   unsigned long long keys[kBranchHash];
-  int rep[kBranchHash];              // lowest entry index holding the key
-  int16_t uniq_of[kBranchEntries];   // entry -> its pair's index among the distinct ones
-  int16_t head[kBranchEntries];      // distinct pair u -> its representative entry
-  int counts[kBranchPer * kBranchWarps];
-  float reward[kBranchBlock];        // outputs of the current pass's pairs
-  int16_t status[kBranchBlock];
-  uint8_t flags[kBranchBlock];       // done | nagari << 1 | committed << 2
+  int16_t slot_u[kBranchHash];      // key -> its pair's index among the distinct ones
+  int16_t uniq_of[kBranchEntries];  // entry -> pair index (-1 past m)
+  int16_t head[kBranchEntries];     // pair -> its first entry
+  float reward[32];                 // outputs of the current pass's pairs
+  int16_t status[32];
+  uint8_t flags[32];                // done | nagari << 1 | committed << 2
 };
 
-__global__ void __launch_bounds__(kBranchBlock, 4) branch_dedup_kernel(
+__global__ void __launch_bounds__(32 * kBranchWarps, CB_BRANCH_MIN_BLOCKS) branch_warp_kernel(
     const u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids,
     const i64* __restrict__ actions, i64 m, u64* __restrict__ children,
     float* __restrict__ reward, bool* __restrict__ done, bool* __restrict__ nagari,
     int16_t* __restrict__ status, bool* __restrict__ committed) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  BranchShared& sh = *reinterpret_cast<BranchShared*>(smem_raw);
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const i64 base = (i64)blockIdx.x * kBranchEntries;
-  constexpr unsigned long long kEmpty = ~0ull;
-  for (int k = t; k < kBranchHash; k += kBranchBlock) {
-    sh.keys[k] = kEmpty;
-    sh.rep[k] = kBranchEntries;
-  }
-  __syncthreads();
-  // Entry e = t + kBranchBlock * j.  Pair key: parent id and action; an invalid
-  // entry (or one past m) is a pair of its own.
-  const auto insert = [&](int e) -> int {
-    const i64 src = lane_source(ids, base + e, m, n_states);
-    const u32 act = base + e < m ? torch_action(__ldg(actions + base + e)) : kNoAction;
-    const unsigned long long key =
-        src >= 0 ? (static_cast<unsigned long long>(src) << 16) | act
-                 : (0xffffull << 48) | static_cast<unsigned long long>(e);
-    u32 h = static_cast<u32>((key * 0x9E3779B97F4A7C15ull) >> 40) & (kBranchHash - 1);
-    for (;;) {
-      const unsigned long long prev = atomicCAS(&sh.keys[h], kEmpty, key);
-      if (prev == kEmpty || prev == key) break;
-      h = (h + 1) & (kBranchHash - 1);
-    }
-    atomicMin(&sh.rep[h], e);
-    return static_cast<int>(h);
-  };
-  static_assert(kBranchPer == 2, "two entries per thread");
-  const int e_a = t, e_b = t + kBranchBlock;
-  const int slot_a = insert(e_a), slot_b = insert(e_b);
-  __syncthreads();
-  // Distinct pairs numbered in entry order (a block scan over the representatives).
-  const bool head_a = sh.rep[slot_a] == e_a, head_b = sh.rep[slot_b] == e_b;
-  const unsigned ballot_a = __ballot_sync(kFull, head_a), ballot_b = __ballot_sync(kFull, head_b);
-  if (lane == 0) {
-    sh.counts[warp] = __popc(ballot_a);
-    sh.counts[kBranchWarps + warp] = __popc(ballot_b);
-  }
-  __syncthreads();
-  int before_a = 0, before_b = 0, distinct = 0;
-#pragma unroll
-  for (int c = 0; c < kBranchPer * kBranchWarps; ++c) {
-    if (c < warp) before_a += sh.counts[c];
-    if (c < kBranchWarps + warp) before_b += sh.counts[c];
-    distinct += sh.counts[c];
-  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  BranchWarpShared& sh = reinterpret_cast<BranchWarpShared*>(smem_raw)[warp];
+  const i64 base = ((i64)blockIdx.x * kBranchWarps + warp) * kBranchEntries;
+  if (base >= m) return;
+  for (int k = lane; k < kBranchHash; k += 32) sh.keys[k] = kBranchEmpty;
+  __syncwarp();
   const unsigned below = (1u << lane) - 1u;
-  if (head_a) {
-    const int u = before_a + __popc(ballot_a & below);
-    sh.head[u] = static_cast<int16_t>(e_a);
-    sh.uniq_of[e_a] = static_cast<int16_t>(u);
+  // Keys of the warp's entries, all loads in flight at once.
+  unsigned long long key[kBranchPerLane];
+#pragma unroll
+  for (int j = 0; j < kBranchPerLane; ++j) {
+    const i64 e = base + 32 * j + lane;
+    const i64 src = lane_source(ids, e, m, n_states);
+    const u32 act = e < m ? torch_action(__ldg(actions + e)) : kNoAction;
+    key[j] = e >= m ? kBranchEmpty
+                    : (src >= 0 ? (static_cast<unsigned long long>(src) << 16) | act : kBranchInvalid);
   }
-  if (head_b) {
-    const int u = before_b + __popc(ballot_b & below);
-    sh.head[u] = static_cast<int16_t>(e_b);
-    sh.uniq_of[e_b] = static_cast<int16_t>(u);
-  }
-  __syncthreads();
-  if (!head_a) sh.uniq_of[e_a] = sh.uniq_of[sh.rep[slot_a]];
-  if (!head_b) sh.uniq_of[e_b] = sh.uniq_of[sh.rep[slot_b]];
-  __syncthreads();
-  WarpTile& tile = sh.tiles[warp];
-  for (int pass = 0; pass * kBranchBlock < distinct; ++pass) {
-    const int first = pass * kBranchBlock;
-    // Step pairs first .. first + kBranchBlock - 1, 32 per warp.
-    if (first + warp * 32 < distinct) {
-      const int u = first + warp * 32 + lane;
-      const int e = u < distinct ? sh.head[u] : -1;
-      const i64 my_src = e >= 0 ? lane_source(ids, base + e, m, n_states) : -1;
-      gather_rows(tile, states, my_src);
-      Game g;
-      load_game(tile, g);
-      __syncwarp();
-      StepOut out{static_cast<u32>(-1), 0, 1, 0, 0};
-      if (my_src >= 0) {
-        out = step_game(g, torch_action(__ldg(actions + base + e)));
-      } else {
-        for (int k = 0; k < kRowWords; ++k) g.w[k] = 0;
-      }
-      store_game(tile, g);
-      const int q = warp * 32 + lane;
-      sh.reward[q] = static_cast<float>(out.reward0);
-      sh.status[q] = static_cast<int16_t>(static_cast<i32>(out.status));
-      sh.flags[q] = static_cast<uint8_t>((out.done != 0) | ((out.nagari != 0) << 1) |
-                                         ((out.committed != 0) << 2));
-    }
-    __syncthreads();
-    // Every entry whose pair this pass made: its child row and its outputs.  A
-    // whole group of 32 entries made in this pass leaves as 496 16-byte stores of
-    // its 7,936 contiguous bytes (each vector two row words, possibly of two rows);
-    // otherwise row by row, the row's words across the lanes.
-    for (int j = 0; j < kBranchPer; ++j) {
-      const int e0 = kBranchBlock * j + warp * 32;
-      const int q_lane = sh.uniq_of[e0 + lane] - first;
-      const bool mine = q_lane >= 0 && q_lane < kBranchBlock;
-      const i64 row0 = base + e0;
-      u64* dst = children + row0 * kRowWords;
-      if (__all_sync(kFull, mine) && row0 + 32 <= m && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-        for (int v = lane; v < 16 * kRowWords; v += 32) {  // 496 vectors of 16 bytes
-          const int w0 = 2 * v, w1 = w0 + 1;
-          const int r0 = w0 / kRowWords, r1 = w1 / kRowWords;
-          const int q0 = sh.uniq_of[e0 + r0] - first;
-          const int q1 = sh.uniq_of[e0 + r1] - first;
-          const u64 a = sh.tiles[q0 >> 5].rows[q0 & 31][w0 - r0 * kRowWords];
-          const u64 b = sh.tiles[q1 >> 5].rows[q1 & 31][w1 - r1 * kRowWords];
-          __stcs(reinterpret_cast<ulonglong2*>(dst) + v, make_ulonglong2(a, b));
+  // Number the distinct keys in order of first occurrence.  Within one round of 32
+  // entries equal keys elect one leader (match), so a key is inserted by one lane
+  // only; keys of earlier rounds are found by a plain read.
+  int distinct = 0;
+#pragma unroll
+  for (int j = 0; j < kBranchPerLane; ++j) {
+    const unsigned long long k = key[j];
+    const unsigned grp = __match_any_sync(kFull, k);
+    const int leader = __ffs(grp) - 1;
+    const bool live = k != kBranchEmpty;
+    bool fresh = false;
+    int h = -1;
+    if (live && lane == leader) {
+      h = static_cast<int>((k * 0x9E3779B97F4A7C15ull) >> 40) & (kBranchHash - 1);
+      for (;;) {
+        unsigned long long cur = sh.keys[h];
+        if (cur == kBranchEmpty) {
+          cur = atomicCAS(&sh.keys[h], kBranchEmpty, k);
+          if (cur == kBranchEmpty) { fresh = true; break; }
         }
+        if (cur == k) break;
+        h = (h + 1) & (kBranchHash - 1);
+      }
+    }
+    const unsigned fresh_ballot = __ballot_sync(kFull, fresh);
+    int u = -1;
+    if (fresh) {
+      u = distinct + __popc(fresh_ballot & below);
+      sh.slot_u[h] = static_cast<int16_t>(u);
+      sh.head[u] = static_cast<int16_t>(32 * j + lane);
+    } else if (live && lane == leader) {
+      u = sh.slot_u[h];  // inserted in an earlier round
+    }
+    distinct += __popc(fresh_ballot);
+    u = __shfl_sync(kFull, u, leader);
+    sh.uniq_of[32 * j + lane] = static_cast<int16_t>(live ? u : -1);
+    __syncwarp();  // this round's numbers are visible to the next round's reads
+  }
+  __syncwarp();
+  const i64 rows_here = m - base < kBranchEntries ? m - base : kBranchEntries;
+  // Full 256-entry groups made in one pass leave as row pairs: 496 contiguous bytes,
+  // 31 vectors of 16 bytes, vector l of a pair holding words 2l and 2l + 1 -- the
+  // same two word positions (and row of the pair) for lane l in every pair.
+  const bool pairs = distinct <= 32 && rows_here == kBranchEntries &&
+                     (reinterpret_cast<uintptr_t>(children) & 15u) == 0;
+  const int w_a = 2 * lane, w_b = 2 * lane + 1;
+  const int r_a = w_a >= kRowWords, r_b = w_b >= kRowWords;
+  const int o_a = w_a - r_a * kRowWords, o_b = w_b - r_b * kRowWords;
+#pragma unroll 1
+  for (int first = 0; first < distinct; first += 32) {
+    const int u = first + lane;
+    const int e = u < distinct ? sh.head[u] : -1;
+    const i64 src = e >= 0 ? lane_source(ids, base + e, m, n_states) : -1;
+    // Rows of the pass: every valid lane of a branch group usually names one parent,
+    // fetched once and replicated.
+    {
+      i64 id0 = -1;
+      const unsigned have = __ballot_sync(kFull, src >= 0);
+      if (have) id0 = __shfl_sync(kFull, src, __ffs(have) - 1);
+      const bool one_parent = __all_sync(kFull, src < 0 || src == id0);
+      if (one_parent && id0 >= 0) {
+        const u64 w = lane < kRowWords ? __ldg(states + id0 * kRowWords + lane) : 0ull;
+#pragma unroll 8
+        for (int r = 0; r < 32; ++r)
+          if (lane < kRowWords) sh.rows[r][lane] = w;
       } else {
-#pragma unroll 4
+#pragma unroll 8
         for (int r = 0; r < 32; ++r) {
-          const i64 row = row0 + r;
-          if (row >= m) break;
-          const int q = sh.uniq_of[e0 + r] - first;
-          if (q < 0 || q >= kBranchBlock) continue;
-          if (lane < kRowWords)
-            __stcs(children + row * kRowWords + lane, sh.tiles[q >> 5].rows[q & 31][lane]);
+          const i64 id = __shfl_sync(kFull, src, r);
+          if (lane < kRowWords) sh.rows[r][lane] = id >= 0 ? __ldg(states + id * kRowWords + lane) : 0ull;
         }
       }
-      const int e = e0 + lane;
-      const int q = sh.uniq_of[e] - first;
-      if (base + e < m && q >= 0 && q < kBranchBlock) {
-        const uint8_t f = sh.flags[q];
-        reward[base + e] = sh.reward[q];
-        status[base + e] = sh.status[q];
-        done[base + e] = f & 1u;
-        nagari[base + e] = (f >> 1) & 1u;
-        committed[base + e] = (f >> 2) & 1u;
+      __syncwarp();
+    }
+    Game g;
+#pragma unroll
+    for (int w = 0; w < kRowWords; ++w) g.w[w] = sh.rows[lane][w];
+    __syncwarp();
+    StepOut out{static_cast<u32>(-1), 0, 1, 0, 0};
+    if (src >= 0) {
+      out = step_game(g, torch_action(__ldg(actions + base + e)));
+    } else {
+      for (int w = 0; w < kRowWords; ++w) g.w[w] = 0;
+    }
+    zero_padding(g);
+#pragma unroll
+    for (int w = 0; w < kRowWords; ++w) sh.rows[lane][w] = g.w[w];
+    sh.reward[lane] = static_cast<float>(out.reward0);
+    sh.status[lane] = static_cast<int16_t>(static_cast<i32>(out.status));
+    sh.flags[lane] = static_cast<uint8_t>((out.done != 0) | ((out.nagari != 0) << 1) |
+                                          ((out.committed != 0) << 2));
+    __syncwarp();
+    if (pairs) {
+      ulonglong2* dst = reinterpret_cast<ulonglong2*>(children + base * kRowWords);
+#pragma unroll 4
+      for (int p = 0; p < kBranchEntries / 2; ++p) {
+        const int q0 = sh.uniq_of[2 * p], q1 = sh.uniq_of[2 * p + 1];
+        if (lane < kRowWords) {
+          const u64 a = sh.rows[r_a ? q1 : q0][o_a];
+          const u64 b = sh.rows[r_b ? q1 : q0][o_b];
+          __stcs(dst + p * kRowWords + lane, make_ulonglong2(a, b));
+        }
+      }
+    } else {
+#pragma unroll 4
+      for (int r = 0; r < rows_here; ++r) {
+        const int q = sh.uniq_of[r] - first;
+        if (q >= 0 && q < 32 && lane < kRowWords)
+          __stcs(children + (base + r) * kRowWords + lane, sh.rows[q][lane]);
       }
     }
-    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kBranchPerLane; ++j) {
+      const int en = 32 * j + lane;
+      const int q = sh.uniq_of[en] - first;
+      if (en < rows_here && q >= 0 && q < 32) {
+        const uint8_t f = sh.flags[q];
+        reward[base + en] = sh.reward[q];
+        status[base + en] = sh.status[q];
+        done[base + en] = f & 1u;
+        nagari[base + en] = (f >> 1) & 1u;
+        committed[base + en] = (f >> 2) & 1u;
+      }
+    }
+    __syncwarp();
   }
 }
 
@@ -675,15 +691,16 @@ int cugo_b200_branch_indexed(const uint8_t* states, int64_t n_states, const int6
   if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
   if (!aligned(states, 8) || !aligned(children, 8)) return CUGO_B200_ERR_ALIGN;
   if (m == 0) return CUGO_B200_OK;
+  constexpr size_t smem = kBranchWarps * sizeof(BranchWarpShared);
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(branch_dedup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             sizeof(BranchShared)) != cudaSuccess)
+    if (cudaFuncSetAttribute(branch_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess)
       return CUGO_B200_ERR_LAUNCH;
     configured = true;
   }
-  branch_dedup_kernel<<<blocks_for(m, kBranchEntries), kBranchBlock, sizeof(BranchShared),
-                        stream>>>(
+  branch_warp_kernel<<<blocks_for(m, kBranchWarps * kBranchEntries), 32 * kBranchWarps, smem,
+                       stream>>>(
       reinterpret_cast<const u64*>(states), n_states, env_ids, actions, m,
       reinterpret_cast<u64*>(children), reward, done, nagari, status, committed);
   return launch_status();
