@@ -8,6 +8,9 @@ JSON line with the per-launch time and the achieved rate against the algorithmic
 bytes or FLOPs of one launch:
 
   mlp       M H B      the policy forward (B blocks of width H), flops_per_row * M
+  gemm      M N K MODE one tcgen05 GEMM layer (MODE plain | silu | residual | pre: the
+                       training forward's SiLU layer keeping its pre-activation), 2MNK
+  wgrad     R O I      the weight gradient dW = dY^T X over R rows (split-K), 2ROI
   mlpsample M H B      the self-play policy step: forward and masked Gumbel-max sampling
                        (one fused launch at H = 512), flops_per_row * M
   observe   ROWS       observe_indexed, 3,319 B per row
@@ -86,8 +89,10 @@ def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
                    opp_hand=torch.randint(0, 1 << 50, (b,), generator=g).to(dev),
                    adv=torch.randn(b, generator=g).to(dev), ret=torch.randn(b, generator=g).to(dev))
     actor, critic = fused_actor().to(dev), fused_critic().to(dev)
+    # The reference trainer's optimizer settings (python/train_ppo50.py:153-156) in
+    # every arm.
     opt = torch.optim.Adam(list(actor.parameters()) + list(critic.parameters()), lr=3e-4,
-                           capturable=True)
+                           eps=1e-5, fused=True, capturable=True)
     step = NativePpoStep(actor, critic, opt)
     sec_eager = _time(lambda: step.step(mb), warmup, iters)
     graphed = GraphedPpoStep(step, mb)
@@ -95,7 +100,8 @@ def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
     # The same networks on the autograd step (fused GEMMs, torch elementwise and
     # reductions), graphed.
     a2, c2 = fused_actor().to(dev), fused_critic().to(dev)
-    opt2 = torch.optim.Adam(list(a2.parameters()) + list(c2.parameters()), lr=3e-4, capturable=True)
+    opt2 = torch.optim.Adam(list(a2.parameters()) + list(c2.parameters()), lr=3e-4, eps=1e-5,
+                            fused=True, capturable=True)
     graphed2 = GraphedPpoStep(PpoStep(a2, c2, opt2), mb)
     sec_autograd = _time(lambda: graphed2(mb), warmup, iters)
 
@@ -111,8 +117,8 @@ def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
         return net[-1](torch.nn.functional.silu(h))
 
     ta, tc = torch_mlp(720, 179), torch_mlp(770, 1)
-    topt = torch.optim.Adam(list(ta.parameters()) + list(tc.parameters()), lr=3e-4,
-                            capturable=True)
+    topt = torch.optim.Adam(list(ta.parameters()) + list(tc.parameters()), lr=3e-4, eps=1e-5,
+                            fused=True, capturable=True)
     cin = critic_input(mb.features, mb.opp_hand)
 
     def torch_step():
@@ -372,6 +378,7 @@ def main() -> None:
     ap.add_argument("dims", nargs="*", type=int)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--mode", default="plain", help="gemm: plain | silu | residual | pre")
     args = ap.parse_args()
     ext = load_extension()
     dev = torch.device("cuda")
@@ -383,6 +390,28 @@ def main() -> None:
         x = torch.randn((m, 720), device=dev).to(torch.bfloat16)
         sec = _time(lambda: pol(x), args.warmup, args.iters)
         out.update(seconds=sec, tflops=pol.flops_per_row() * m / sec / 1e12)
+    elif args.case == "gemm":
+        m, n, k = d[:3]
+        mode = args.mode
+        a = torch.randn((m, k), device=dev).to(torch.bfloat16)
+        w = (torch.randn((n, k), device=dev) * k ** -0.5).to(torch.bfloat16)
+        bias = torch.randn(n, device=dev)
+        res = torch.randn((m, n), device=dev).to(torch.bfloat16)
+        pre = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        out_t = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        run = {"plain": lambda: ext.linear(a, w, bias, out=out_t),
+               "silu": lambda: ext.linear(a, w, bias, out=out_t, act=2),
+               "residual": lambda: ext.linear(a, w, bias, residual=res, out=out_t),
+               "pre": lambda: ext.linear_pre(a, w, bias, 2, pre, out=out_t)}[mode]
+        sec = _time(run, args.warmup, args.iters)
+        out.update(mode=mode, seconds=sec, tflops=2 * m * n * k / sec / 1e12)
+    elif args.case == "wgrad":
+        r, o, i = d
+        dy = torch.randn((r, o), device=dev).to(torch.bfloat16)
+        x = torch.randn((r, i), device=dev).to(torch.bfloat16)
+        dw = torch.empty((o, i), dtype=torch.float32, device=dev)
+        sec = _time(lambda: ext.wgrad_bf16(dy, x, dw), args.warmup, args.iters)
+        out.update(seconds=sec, tflops=2 * r * o * i / sec / 1e12)
     elif args.case == "mlpsample":  # the self-play policy step: MLP + sampling head
         m, h, blocks = d
         pol = ResidualMlpPolicy(h, blocks, "relu", device=dev)

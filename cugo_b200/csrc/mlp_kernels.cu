@@ -74,6 +74,9 @@ struct Epilogue {
   // cover (read by the kernel, so a CUDA graph can change it between replays);
   // null: all M rows.
   const int32_t* window;
+  // Nonzero: the residual's tensor map is instead a second bf16 output receiving
+  // acc + bias before the activation (the pre-activation a training backward reads).
+  int pre;
 };
 
 // The window's first row and row count, clamped to [0, M].
@@ -447,6 +450,13 @@ __device__ __forceinline__ void epilogue_cols(const Epilogue& ep, EpiWarp& io, u
     if (live) {
 #pragma unroll
       for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(r[j]) + bias_s[c0 + j];
+      if constexpr (sizeof(T) == 2) {
+        if (ep.pre) {  // the pre-activation through the other staging buffer
+          if (lane == 0) tma_store_wait_read<0>();
+          __syncwarp();
+          store_chunk<T>(stage + ((c & 1) ^ 1) * EPI_BUF, v, io.map_res, row0, n0 + c0);
+        }
+      }
       activate_chunk<CW>(v, ep.act);
       if (ep.residual) add_residual_row<T>(cur, v);  // ends with __syncwarp
       activate_chunk<CW>(v, ep.act_after);
@@ -974,13 +984,16 @@ bool pair_kernel_enabled() {
 int gemm_launch(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
                 int32_t bias_fp32, const void* residual, int64_t ldr, void* out, int64_t ldo,
                 int32_t out_fp32, int32_t act, int32_t act_after, int64_t m, int64_t n, int64_t k,
-                const int32_t* window, int32_t* error, cudaStream_t stream) {
+                const int32_t* window, int32_t* error, cudaStream_t stream,
+                void* pre = nullptr, int64_t ldp = 0) {
   if (m < 0 || n <= 0 || k <= 0 || act < 0 || act > 3 || act_after < 0 || act_after > 3)
     return CUGO_B200_ERR_ARG;
   if (m == 0) return CUGO_B200_OK;
   if (!a || !w || !out || lda < k || ldw < k || ldo < n || (residual && ldr < n))
     return CUGO_B200_ERR_ARG;
   if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return CUGO_B200_ERR_ARG;
+  if (pre && (residual || out_fp32 || ldp < n)) return CUGO_B200_ERR_ARG;
+  if (pre && (reinterpret_cast<uintptr_t>(pre) % 16 || (ldp * 2) % 16)) return CUGO_B200_ERR_ALIGN;
   const int esz = out_fp32 ? 4 : 2;
   const auto al = [](const void* p, uintptr_t q) { return (reinterpret_cast<uintptr_t>(p) % q) == 0; };
   if (!al(a, 16) || !al(w, 16) || (lda * 2) % 16 || (ldw * 2) % 16 || !al(out, 16) ||
@@ -1000,12 +1013,15 @@ int gemm_launch(const void* a, int64_t lda, const void* w, int64_t ldw, const vo
     attr_set[dev] = true;
   }
   Epilogue ep{bias, residual, ldr, out, ldo, out_fp32 ? 1 : 0, bias_fp32 ? 1 : 0, act, act_after,
-              static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), error, window};
+              static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), error, window,
+              pre ? 1 : 0};
   CUtensorMap ma, mw, mo, mr;
   if (!make_out_map(&mo, out, m, n, ldo, out_fp32 != 0)) return CUGO_B200_ERR_LAUNCH;
   if (residual) {
     if (!make_out_map(&mr, const_cast<void*>(residual), m, n, ldr, out_fp32 != 0))
       return CUGO_B200_ERR_LAUNCH;
+  } else if (pre) {
+    if (!make_out_map(&mr, pre, m, n, ldp, false)) return CUGO_B200_ERR_LAUNCH;
   } else {
     mr = mo;  // unused
   }
@@ -1042,6 +1058,15 @@ int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void* w, int64_t ld
                      act_after, m, n, k, nullptr, error, stream);
 }
 
+int cugo_b200_gemm_bf16_pre(const void* a, int64_t lda, const void* w, int64_t ldw,
+                            const void* bias, int32_t bias_fp32, void* out, int64_t ldo, void* pre,
+                            int64_t ldp, int32_t act, int64_t m, int64_t n, int64_t k,
+                            int32_t* error, cudaStream_t stream) {
+  if (!pre) return CUGO_B200_ERR_ARG;
+  return gemm_launch(a, lda, w, ldw, bias, bias_fp32, nullptr, 0, out, ldo, 0, act, 0, m, n, k,
+                     nullptr, error, stream, pre, ldp);
+}
+
 int cugo_b200_gemm_bf16_window(const void* a, int64_t lda, const void* w, int64_t ldw,
                                const void* bias, int32_t bias_fp32, const void* residual,
                                int64_t ldr, void* out, int64_t ldo, int32_t out_fp32,
@@ -1050,6 +1075,315 @@ int cugo_b200_gemm_bf16_window(const void* a, int64_t lda, const void* w, int64_
   if (!window || (reinterpret_cast<uintptr_t>(window) & 3u)) return CUGO_B200_ERR_ARG;
   return gemm_launch(a, lda, w, ldw, bias, bias_fp32, residual, ldr, out, ldo, out_fp32, act,
                      act_after, m, n, k, window, error, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+// ---- weight gradients: dW = dY^T X over the rows (split-K) --------------------------
+//
+// dW[o][i] = sum_r dY[r][o] X[r][i]: both operands are row-major over the reduction
+// dimension (the minibatch rows), so they enter the MMA MN-major: TMA boxes of 64
+// rows x 64 consecutive outputs (or inputs), 128-byte swizzled, stacked 8 KB apart
+// along M (N); the shared-memory descriptors step 1 KB per 8-row group (stride
+// byte offset) and 8 KB per 64-wide block (leading byte offset), and the
+// instruction descriptor marks A and B transposed.  A 128 x 256 tile of dW has far
+// too little work for the SM count over one K loop, so the rows are split: a work
+// item is (tile, split), each writing its fp32 partial tile into a workspace
+// [splits][Mpad][Npad]; wgrad_reduce_kernel adds the splits in order
+// (deterministic).  Warp roles, barriers and bounded waits as in gemm_kernel.
+struct WgradArgs {
+  float* ws;
+  int64_t mpad, npad;
+  int tiles_m, tiles_n, splits, kt_per_split, k_tiles;
+  int* error;
+};
+
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t addr) {
+  uint64_t d = static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(8192 >> 4) << 16;   // leading byte offset: next 64-wide block
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;   // stride byte offset: next 8-row group
+  d |= static_cast<uint64_t>(1) << 46;           // descriptor version
+  d |= static_cast<uint64_t>(2) << 61;           // 128-byte swizzle
+  return d;
+}
+
+constexpr uint32_t kWgradIdesc = instr_desc(BM, BN) | (1u << 15) | (1u << 16);  // A, B MN-major
+
+__global__ void __launch_bounds__(THREADS, 1)
+    wgrad_kernel(const __grid_constant__ CUtensorMap map_dy, const __grid_constant__ CUtensorMap map_x,
+                 const WgradArgs wa) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* drained = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int items = wa.tiles_m * wa.tiles_n * wa.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], EPI_WARPS);
+    }
+    mbar_init(drained, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_holder)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  bool failed = false;
+  // Item -> (tile m, tile n, split) and its k-tile range [kt0, kt1).
+  const auto decode = [&](int item, int& tm, int& tn, int& split, int& kt0, int& kt1) {
+    const int tile = item / wa.splits;
+    split = item - tile * wa.splits;
+    tm = tile / wa.tiles_n;
+    tn = tile - tm * wa.tiles_n;
+    kt0 = split * wa.kt_per_split;
+    kt1 = kt0 + wa.kt_per_split < wa.k_tiles ? kt0 + wa.kt_per_split : wa.k_tiles;
+  };
+
+  if (warp == 0) {
+    // ---- TMA producer: per stage two 64-wide blocks of dY and four of X ----
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int it = blockIdx.x; it < items && !failed; it += gridDim.x) {
+        int tm, tn, split, kt0, kt1;
+        decode(it, tm, tn, split, kt0, kt1);
+        for (int kt = kt0; kt < kt1; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u)) {
+            failed = true;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          mbar_expect_tx(&full[stage], STAGE_BYTES);
+#pragma unroll
+          for (int h = 0; h < BM / 64; ++h)
+            tma_load_2d(&map_dy, &full[stage], sa + h * 8192, tm * BM + 64 * h, kt * BK);
+#pragma unroll
+          for (int q = 0; q < BN / 64; ++q)
+            tma_load_2d(&map_x, &full[stage], sa + A_BYTES + q * 8192, tn * BN + 64 * q, kt * BK);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (failed) {
+        for (int s = 0; s < STAGES; ++s) mbar_wait(&full[s], 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int iter = 0;
+      for (int it = blockIdx.x; it < items && !failed; it += gridDim.x, ++iter) {
+        int tm, tn, split, kt0, kt1;
+        decode(it, tm, tn, split, kt0, kt1);
+        const int buf = iter & 1;
+        const uint32_t use = static_cast<uint32_t>(iter >> 1);
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u)) {
+          failed = true;
+          break;
+        }
+        fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+        for (int kt = kt0; kt < kt1; ++kt) {
+          if (!mbar_wait(&full[stage], phase)) {
+            failed = true;
+            break;
+          }
+          fence_after();
+          const uint32_t a_addr = smem_addr(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {  // 16 rows = two 8-row groups
+            mma_bf16(d_tmem, sw128_mn_desc(a_addr + kk * 2048), sw128_mn_desc(b_addr + kk * 2048),
+                     kWgradIdesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (failed) break;
+        mma_commit(&acc_full[buf]);
+      }
+      mma_commit(drained);
+      mbar_wait(drained, 0);
+    }
+  } else {
+    // ---- epilogue: warps 2..9, two per TMEM lane quadrant, 128 columns each ----
+    const int quad = epi_quad(warp);
+    const int cbase = epi_col0(warp);
+    int iter = 0;
+    for (int it = blockIdx.x; it < items; it += gridDim.x, ++iter) {
+      int tm, tn, split, kt0, kt1;
+      decode(it, tm, tn, split, kt0, kt1);
+      const int buf = iter & 1;
+      const uint32_t use = static_cast<uint32_t>(iter >> 1);
+      if (!epilogue_wait(&acc_full[buf], use & 1u)) {
+        failed = true;
+        break;
+      }
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(buf * BN + cbase);
+      float* row = wa.ws + ((int64_t)split * wa.mpad + (int64_t)tm * BM + quad * 32 + lane) * wa.npad +
+                   (int64_t)tn * BN + cbase;
+#pragma unroll 1
+      for (int c = 0; c < BN / 2; c += 32) {
+        uint32_t r[32];
+        CB_TMEM_LD32(taddr + c, r);
+        tmem_wait_ld();
+        float4* dst = reinterpret_cast<float4*>(row + c);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                               __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  if (failed) {
+    if (wa.error) atomicExch(wa.error, 1);
+    const uint64_t t0 = now_ns();
+    while (now_ns() - t0 < 100'000ull) {
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// out[o][i] = sum over the splits, in order, of ws[split][o][i] (four columns per
+// thread).
+__global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restrict__ ws, int64_t mpad,
+                                                           int64_t npad, int splits, int64_t m,
+                                                           int64_t n, float* __restrict__ out,
+                                                           int64_t ldo) {
+  const int64_t quads = npad / 4;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= m * quads) return;
+  const int64_t o = idx / quads, i0 = (idx - o * quads) * 4;
+  if (i0 >= n) return;
+  float4 acc = __ldg(reinterpret_cast<const float4*>(ws + o * npad + i0));
+  for (int s = 1; s < splits; ++s) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(ws + ((int64_t)s * mpad + o) * npad + i0));
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  float* dst = out + o * ldo + i0;
+  const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (i0 + e < n) dst[e] = a[e];
+}
+
+// Split count and k-tiles per split for a weight-gradient launch.
+struct WgradPlan {
+  int tiles_m, tiles_n, k_tiles, splits, kt_per_split;
+  int64_t mpad, npad;
+};
+
+WgradPlan wgrad_plan(int64_t rows, int64_t n_out, int64_t n_in) {
+  WgradPlan p{};
+  p.tiles_m = static_cast<int>((n_out + BM - 1) / BM);
+  p.tiles_n = static_cast<int>((n_in + BN - 1) / BN);
+  p.k_tiles = static_cast<int>((rows + BK - 1) / BK);
+  const int tiles = p.tiles_m * p.tiles_n;
+  int want = sm_count() / tiles;  // at most one item per SM: no second wave
+  if (want < 1) want = 1;
+  p.kt_per_split = (p.k_tiles + want - 1) / want;
+  if (p.kt_per_split < 4) p.kt_per_split = 4;  // at least 256 rows per item
+  p.splits = (p.k_tiles + p.kt_per_split - 1) / p.kt_per_split;
+  if (p.splits < 1) p.splits = 1;
+  p.mpad = static_cast<int64_t>(p.tiles_m) * BM;
+  p.npad = static_cast<int64_t>(p.tiles_n) * BN;
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t cugo_b200_wgrad_scratch_floats(int64_t rows, int64_t n_out, int64_t n_in) {
+  if (rows <= 0 || n_out <= 0 || n_in <= 0) return 0;
+  const WgradPlan p = wgrad_plan(rows, n_out, n_in);
+  return static_cast<int64_t>(p.splits) * p.mpad * p.npad;
+}
+
+int cugo_b200_wgrad_bf16(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t rows,
+                         int64_t n_out, int64_t n_in, float* dw, int64_t lddw, float* scratch,
+                         int64_t scratch_floats, int32_t* error, cudaStream_t stream) {
+  if (rows < 0 || n_out <= 0 || n_in <= 0 || lddy < n_out || ldx < n_in || lddw < n_in || !dw)
+    return CUGO_B200_ERR_ARG;
+  if (rows > INT32_MAX || n_out > INT32_MAX || n_in > INT32_MAX) return CUGO_B200_ERR_ARG;
+  if (rows == 0) {
+    for (int64_t o = 0; o < n_out; ++o)
+      if (cudaMemsetAsync(dw + o * lddw, 0, n_in * sizeof(float), stream) != cudaSuccess)
+        return CUGO_B200_ERR_LAUNCH;
+    return CUGO_B200_OK;
+  }
+  if (!dy || !x) return CUGO_B200_ERR_ARG;
+  const auto al = [](const void* p, uintptr_t q) { return (reinterpret_cast<uintptr_t>(p) % q) == 0; };
+  if (!al(dy, 16) || !al(x, 16) || (lddy * 2) % 16 || (ldx * 2) % 16 || !al(dw, 4))
+    return CUGO_B200_ERR_ALIGN;
+  const WgradPlan p = wgrad_plan(rows, n_out, n_in);
+  const int64_t need = static_cast<int64_t>(p.splits) * p.mpad * p.npad;
+  if (!scratch || scratch_floats < need) return CUGO_B200_ERR_CAPACITY;
+  if (!al(scratch, 16)) return CUGO_B200_ERR_ALIGN;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr_set[64] = {};
+  if (dev < 0 || dev >= 64) return CUGO_B200_ERR_LAUNCH;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+        cudaSuccess)
+      return CUGO_B200_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  // Boxes of 64 rows (K) x 64 consecutive columns (M or N), 128-byte swizzle.
+  CUtensorMap mdy, mx;
+  if (!make_map(&mdy, dy, rows, n_out, lddy, BK) || !make_map(&mx, x, rows, n_in, ldx, BK))
+    return CUGO_B200_ERR_LAUNCH;
+  WgradArgs wa{scratch, p.mpad, p.npad, p.tiles_m, p.tiles_n, p.splits, p.kt_per_split, p.k_tiles, error};
+  const int items = p.tiles_m * p.tiles_n * p.splits;
+  const int grid = items < sm_count() ? items : sm_count();
+  wgrad_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(mdy, mx, wa);
+  const int64_t threads = n_out * (p.npad / 4);
+  wgrad_reduce_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+      scratch, p.mpad, p.npad, p.splits, n_out, n_in, dw, lddw);
+  return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }
 
 }  // extern "C"

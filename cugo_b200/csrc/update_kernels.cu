@@ -74,14 +74,16 @@ __device__ __forceinline__ float warp_max(float v) {
 // derivative s (1 + z (1 - s))).
 __device__ __forceinline__ float act_value(float z, int act) {
   if (act == kActRelu) return z > 0.0f ? z : 0.0f;
-  if (act == kActSilu) return z / (1.0f + __expf(-z));
+  if (act == kActSilu) return __fdividef(z, 1.0f + __expf(-z));
   return z;
 }
 
 __device__ __forceinline__ float act_slope(float z, int act) {
   if (act == kActRelu) return z > 0.0f ? 1.0f : 0.0f;
   if (act == kActSilu) {
-    const float s = 1.0f / (1.0f + __expf(-z));
+    // Fast exponential and divide (a few ulp, far below the bf16 rounding of the
+    // stored gradient); IEEE division made this kernel compute-bound.
+    const float s = __fdividef(1.0f, 1.0f + __expf(-z));
     return s * (1.0f + z * (1.0f - s));
   }
   return 1.0f;
@@ -203,6 +205,9 @@ constexpr int kColThreads = 256;
 // Rows [r0, r1) of x (bf16 [rows, n], ld elements apart), thread t of the block
 // owning columns 8 (t % (n / 8)) .. + 7 of rows r0 + t / (n / 8), stepping by the
 // block's row groups; with z, the sums are of dz = du act'(z) and dz is stored.
+// Rows are taken kColBatch at a time with all their loads issued before use.
+constexpr int kColBatch = 8;
+
 __global__ void __launch_bounds__(kColThreads) colsum_kernel(
     const __nv_bfloat16* __restrict__ du, i64 ldu, const __nv_bfloat16* __restrict__ z, i64 ldz,
     int act, __nv_bfloat16* __restrict__ dz, i64 ldd, i64 rows, int n, i64 rows_per_block,
@@ -216,20 +221,34 @@ __global__ void __launch_bounds__(kColThreads) colsum_kernel(
   const i64 r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
   float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (grp < groups) {
-    for (i64 r = r0 + grp; r < r1; r += groups) {
-      float g[8];
-      bf16x8(__ldg(reinterpret_cast<const uint4*>(du + r * ldu) + v), g);
-      if (z) {
-        float zz[8];
-        bf16x8(__ldg(reinterpret_cast<const uint4*>(z + r * ldz) + v), zz);
+    for (i64 rb = r0 + grp; rb < r1; rb += (i64)kColBatch * groups) {
+      uint4 gx[kColBatch], gz[kColBatch];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] *= act_slope(zz[e], act);
-        const uint4 packed = pack8(g);
-        reinterpret_cast<uint4*>(dz + r * ldd)[v] = packed;
-        bf16x8(packed, g);  // the sums are of the stored (bf16) gradient
+      for (int k = 0; k < kColBatch; ++k) {
+        const i64 r = rb + (i64)k * groups;
+        if (r < r1) {
+          gx[k] = __ldg(reinterpret_cast<const uint4*>(du + r * ldu) + v);
+          if (z) gz[k] = __ldg(reinterpret_cast<const uint4*>(z + r * ldz) + v);
+        }
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s[e] += g[e];
+      for (int k = 0; k < kColBatch; ++k) {
+        const i64 r = rb + (i64)k * groups;
+        if (r >= r1) break;
+        float g[8];
+        bf16x8(gx[k], g);
+        if (z) {
+          float zz[8];
+          bf16x8(gz[k], zz);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[e] *= act_slope(zz[e], act);
+          const uint4 packed = pack8(g);
+          reinterpret_cast<uint4*>(dz + r * ldd)[v] = packed;
+          bf16x8(packed, g);  // the sums are of the stored (bf16) gradient
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s[e] += g[e];
+      }
     }
 #pragma unroll
     for (int e = 0; e < 8; ++e) shared_sums[grp * n + 8 * v + e] = s[e];
@@ -242,15 +261,37 @@ __global__ void __launch_bounds__(kColThreads) colsum_kernel(
   }
 }
 
-// out[c] = sum over the blocks of partial[block][c], in block order (deterministic).
-__global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restrict__ partial,
+// Column c of the block partials [blocks][width] summed in a fixed order: thread
+// (c, y) of a 32 x 32 block adds the partials of blocks y, y + 32, ... in turn, then
+// the 32 sums are added in order of y (deterministic, and every column's loads
+// coalesced across the 32 columns of a block row).
+constexpr int kSumRows = 32;
+
+__device__ __forceinline__ bool sum_column(const float* __restrict__ partial, int blocks, int width,
+                                           float& out) {
+  __shared__ float ys[kSumRows][33];
+  const int cx = threadIdx.x & 31, y = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + cx;
+  float tot = 0.0f;
+  if (c < width) {
+#pragma unroll 8
+    for (int b = y; b < blocks; b += kSumRows) tot += __ldg(partial + (i64)b * width + c);
+  }
+  ys[y][cx] = tot;
+  __syncthreads();
+  if (y != 0 || c >= width) return false;
+  out = 0.0f;
+#pragma unroll
+  for (int q = 0; q < kSumRows; ++q) out += ys[q][cx];
+  return true;
+}
+
+// out[c] = sum over the blocks of partial[block][c].
+__global__ void __launch_bounds__(32 * kSumRows) sum_partials_kernel(const float* __restrict__ partial,
                                                            int blocks, int n,
                                                            float* __restrict__ out) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= n) return;
-  float tot = 0.0f;
-  for (int b = 0; b < blocks; ++b) tot += partial[(i64)b * n + c];
-  out[c] = tot;
+  float tot;
+  if (sum_column(partial, blocks, n, tot)) out[blockIdx.x * 32 + (threadIdx.x & 31)] = tot;
 }
 
 // The critic's one-output head backward (v = w . act(h) + b, h [rows, n]):
@@ -270,26 +311,41 @@ __global__ void __launch_bounds__(kColThreads) scalar_head_backward_kernel(
   float wf[8], s[8] = {0, 0, 0, 0, 0, 0, 0, 0}, sw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, sb = 0.0f;
   bf16x8(__ldg(reinterpret_cast<const uint4*>(w) + v), wf);
   if (grp < groups) {
-    for (i64 r = r0 + grp; r < r1; r += groups) {
-      const float d = __ldg(dv + r);
-      float hh[8], g[8];
-      bf16x8(__ldg(reinterpret_cast<const uint4*>(h + r * ldh) + v), hh);
-      // The head's input act(h) in bf16, as the forward's head GEMM read it.
-      float gin[8];
+    for (i64 rb = r0 + grp; rb < r1; rb += (i64)kColBatch * groups) {
+      uint4 hx[kColBatch];
+      float dd[kColBatch];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) gin[e] = act_value(hh[e], act);
-      bf16x8(pack8(gin), gin);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        g[e] = d * wf[e] * act_slope(hh[e], act);
-        sw[e] += d * gin[e];
+      for (int k = 0; k < kColBatch; ++k) {
+        const i64 r = rb + (i64)k * groups;
+        if (r < r1) {
+          hx[k] = __ldg(reinterpret_cast<const uint4*>(h + r * ldh) + v);
+          dd[k] = __ldg(dv + r);
+        }
       }
-      const uint4 packed = pack8(g);
-      reinterpret_cast<uint4*>(dh + r * ldd)[v] = packed;
-      bf16x8(packed, g);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s[e] += g[e];
-      if (v == 0) sb += d;
+      for (int k = 0; k < kColBatch; ++k) {
+        const i64 r = rb + (i64)k * groups;
+        if (r >= r1) break;
+        const float d = dd[k];
+        float hh[8], g[8];
+        bf16x8(hx[k], hh);
+        // The head's input act(h) in bf16, as the forward's head GEMM read it.
+        float gin[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) gin[e] = act_value(hh[e], act);
+        bf16x8(pack8(gin), gin);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          g[e] = d * wf[e] * act_slope(hh[e], act);
+          sw[e] += d * gin[e];
+        }
+        const uint4 packed = pack8(g);
+        reinterpret_cast<uint4*>(dh + r * ldd)[v] = packed;
+        bf16x8(packed, g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s[e] += g[e];
+        if (v == 0) sb += d;
+      }
     }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -306,18 +362,16 @@ __global__ void __launch_bounds__(kColThreads) scalar_head_backward_kernel(
   }
 }
 
-// The scalar head's block partials [blocks][2n + 1] summed in block order into
-// dh_sums [n], dw [n] and db [1].
-__global__ void __launch_bounds__(256) sum_head_partials_kernel(const float* __restrict__ partial,
+// The scalar head's block partials [blocks][2n + 1] summed into dh_sums [n], dw [n]
+// and db [1] (the order of sum_column).
+__global__ void __launch_bounds__(32 * kSumRows) sum_head_partials_kernel(const float* __restrict__ partial,
                                                                 int blocks, int n,
                                                                 float* __restrict__ dh_sums,
                                                                 float* __restrict__ dw,
                                                                 float* __restrict__ db) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  const int width = 2 * n + 1;
-  if (c >= width) return;
-  float tot = 0.0f;
-  for (int b = 0; b < blocks; ++b) tot += partial[(i64)b * width + c];
+  float tot;
+  if (!sum_column(partial, blocks, 2 * n + 1, tot)) return;
+  const int c = blockIdx.x * 32 + (threadIdx.x & 31);
   if (c < n) dh_sums[c] = tot;
   else if (c < 2 * n) dw[c - n] = tot;
   else *db = tot;
@@ -331,9 +385,11 @@ inline int launch_status() {
 
 // Blocks and rows per block of a column-sum launch over `rows` rows.
 inline void colsum_grid(i64 rows, unsigned& blocks, i64& per_block) {
-  const i64 target = 2 * 148;
+  // Enough blocks that every SM holds several (the loads of a batch are all that a
+  // thread keeps in flight), at least 32 rows each.
+  const i64 target = 16 * 148;
   per_block = (rows + target - 1) / target;
-  if (per_block < 16) per_block = 16;
+  if (per_block < 32) per_block = 32;
   blocks = static_cast<unsigned>((rows + per_block - 1) / per_block);
 }
 
@@ -384,7 +440,7 @@ int cugo_b200_colsum_bf16(const void* x, int64_t ldx, const void* z, int64_t ldz
   colsum_kernel<<<blocks, kColThreads, groups * n * sizeof(float), stream>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(z), ldz, act,
       static_cast<__nv_bfloat16*>(dz), ldd, rows, n, per_block, scratch);
-  sum_partials_kernel<<<(n + 255) / 256, 256, 0, stream>>>(scratch, static_cast<int>(blocks), n, sums);
+  sum_partials_kernel<<<(n + 31) / 32, 32 * kSumRows, 0, stream>>>(scratch, static_cast<int>(blocks), n, sums);
   return launch_status();
 }
 
@@ -415,7 +471,7 @@ int cugo_b200_scalar_head_backward(const float* dv, const void* w, const void* h
                                           static_cast<const __nv_bfloat16*>(h), ldh, act,
                                           static_cast<__nv_bfloat16*>(dh), ldd, rows, n, per_block,
                                           scratch);
-  sum_head_partials_kernel<<<(2 * n + 1 + 255) / 256, 256, 0, stream>>>(
+  sum_head_partials_kernel<<<(2 * n + 1 + 31) / 32, 32 * kSumRows, 0, stream>>>(
       scratch, static_cast<int>(blocks), n, dh_sums, dw, db);
   return launch_status();
 }

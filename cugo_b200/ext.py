@@ -46,6 +46,8 @@ _SIGNATURES: dict[str, list] = {
                                _I32, _I64, _I64, _I64, _VP, _VP],
     "cugo_b200_gemm_bf16_window": [_VP, _I64, _VP, _I64, _VP, _I32, _VP, _I64, _VP, _I64, _I32,
                                    _I32, _I32, _I64, _I64, _I64, _VP, _VP, _VP],
+    "cugo_b200_gemm_bf16_pre": [_VP, _I64, _VP, _I64, _VP, _I32, _VP, _I64, _VP, _I64, _I32, _I64,
+                                _I64, _I64, _VP, _VP],
     "cugo_b200_observe_query_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_observe_critic_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP],
     "cugo_b200_redeal": [_VP, _I64, _VP, _I64, _I32, _VP],
@@ -79,6 +81,8 @@ _SIGNATURES: dict[str, list] = {
                               _VP],
     "cugo_b200_scalar_head_backward": [_VP, _VP, _VP, _I64, _I32, _VP, _I64, _I64, _I32, _VP, _VP,
                                        _VP, _VP, _I64, _VP],
+    "cugo_b200_wgrad_bf16": [_VP, _I64, _VP, _I64, _I64, _I64, _I64, _VP, _I64, _VP, _I64, _VP,
+                             _VP],
     "cugo_b200_stock_planes_bf16": [_VP, _I64, _VP, _I64, _VP, _I64, _I32, _VP],
     "cugo_b200_wave_tail": [_I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
                             _VP, _VP, _VP, _VP, _VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP,
@@ -95,7 +99,8 @@ _CONSTANTS = {
     "STATUS_OK": "cugo_b200_status_ok",
 }
 _EXTRA_CONSTANTS = {"EVENT_IN": "cugo_b200_event_inputs", "START_IN": "cugo_b200_start_inputs"}
-_INT64_FUNCTIONS = {"cugo_b200_colsum_scratch_floats": [_I64, _I32]}
+_INT64_FUNCTIONS = {"cugo_b200_colsum_scratch_floats": [_I64, _I32],
+                    "cugo_b200_wgrad_scratch_floats": [_I64, _I64, _I64]}
 _ERRORS = {-1: "invalid argument", -2: "misaligned pointer", -3: "kernel launch failed"}
 
 _LIB: ctypes.CDLL | None = None
@@ -496,12 +501,18 @@ class CugoB200Extension:
     def _colsum_scratch(self, rows: int, n: int, device: torch.device) -> torch.Tensor:
         """The per-block partial sums' buffer, one per device, grown as needed (keep
         the sizes a CUDA graph replays within what it saw at capture)."""
-        need = int(self._lib.cugo_b200_colsum_scratch_floats(rows, n))
+        return self._scratch_floats(int(self._lib.cugo_b200_colsum_scratch_floats(rows, n)), device,
+                                    "colsum")
+
+    def _scratch_floats(self, need: int, device: torch.device, kind: str) -> torch.Tensor:
+        """An fp32 scratch buffer per device and kind of op (launches of one kind are
+        ordered on the stream), grown as needed."""
         cache = self.__dict__.setdefault("_scratch", {})
-        buf = cache.get(device)
+        key = (device, kind)
+        buf = cache.get(key)
         if buf is None or buf.numel() < need:
             buf = torch.empty(max(need, 1), dtype=torch.float32, device=device)
-            cache[device] = buf
+            cache[key] = buf
         return buf
 
     def colsum_bf16(self, x: torch.Tensor, out: torch.Tensor, z: torch.Tensor | None = None,
@@ -515,6 +526,27 @@ class CugoB200Extension:
                 _ptr(x), x.stride(0), _ptr(z), z.stride(0) if z is not None else 0, act, _ptr(dz),
                 dz.stride(0) if dz is not None else 0, rows, n, _ptr(out), _ptr(scratch),
                 scratch.numel(), self._stream(x.device)), "colsum_bf16")
+
+    def wgrad_bf16(self, dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor,
+                   n_out: int | None = None, n_in: int | None = None) -> torch.Tensor:
+        """out (fp32 [n_out, n_in]) = dy[:, :n_out]^T x[:, :n_in] over the rows on the
+        tcgen05 tensor cores (bf16 operands, row-major; split over the rows, splits
+        added in a fixed order)."""
+        rows = dy.shape[0]
+        n_out = dy.shape[1] if n_out is None else n_out
+        n_in = x.shape[1] if n_in is None else n_in
+        if dy.dtype != torch.bfloat16 or x.dtype != torch.bfloat16 or x.shape[0] != rows:
+            raise RuntimeError("wgrad_bf16 expects bf16 dy [rows, n_out] and x [rows, n_in]")
+        if dy.stride(1) != 1 or x.stride(1) != 1 or out.stride(1) != 1 or out.dtype != torch.float32:
+            raise RuntimeError("wgrad_bf16 operands must be row-major, out fp32")
+        with torch.cuda.device(dy.device):
+            scratch = self._scratch_floats(
+                int(self._lib.cugo_b200_wgrad_scratch_floats(rows, n_out, n_in)), dy.device, "wgrad")
+            _check(self._lib.cugo_b200_wgrad_bf16(
+                _ptr(dy), dy.stride(0), _ptr(x), x.stride(0), rows, n_out, n_in, _ptr(out),
+                out.stride(0), _ptr(scratch), scratch.numel(), None, self._stream(dy.device)),
+                "wgrad_bf16")
+        return out
 
     def scalar_head_backward(self, dv: torch.Tensor, w: torch.Tensor, h: torch.Tensor, act: int,
                              dh: torch.Tensor, dh_sums: torch.Tensor, dw: torch.Tensor,
@@ -671,6 +703,27 @@ class CugoB200Extension:
                     raise RuntimeError("linear window must be a CUDA int32 tensor {first row, rows}")
                 _check(self._lib.cugo_b200_gemm_bf16_window(*args, _ptr(window), _ptr(error),
                                                             self._stream(a.device)), "gemm_bf16_window")
+        return out
+
+    def linear_pre(self, a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, act: int,
+                   pre: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """out = act(a @ w.T + bias) and pre = a @ w.T + bias (both bf16) in one GEMM
+        launch: a training forward's layer that keeps its pre-activation."""
+        m, k = a.shape
+        n = w.shape[0]
+        if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or w.shape[1] != k:
+            raise RuntimeError("linear_pre expects bf16 a [m, k] and w [n, k]")
+        if pre.dtype != torch.bfloat16 or pre.shape != (m, n) or pre.stride(1) != 1:
+            raise RuntimeError("linear_pre needs a row-major bf16 pre [m, n]")
+        if out is None:
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+        if bias is not None and bias.dtype not in (torch.bfloat16, torch.float32):
+            raise RuntimeError("linear bias must be bf16 or fp32")
+        with torch.cuda.device(a.device):
+            _check(self._lib.cugo_b200_gemm_bf16_pre(
+                _ptr(a), a.stride(0), _ptr(w), w.stride(0), _ptr(bias),
+                int(bias is not None and bias.dtype == torch.float32), _ptr(out), out.stride(0),
+                _ptr(pre), pre.stride(0), act, m, n, k, None, self._stream(a.device)), "gemm_bf16_pre")
         return out
 
     def redeal_worlds(self, states, env_ids, seats, worlds: int, seed: int = 0, tries: int = 8,

@@ -246,7 +246,7 @@ class FusedResidualMlp(nn.Module):
 # NativePpoStep runs both networks' forward with the activations kept, the fused
 # loss kernel (cugo_b200_ppo_loss) and the backward written out layer by layer,
 # every gradient landing in the parameter's .grad buffer directly:
-#   head (actor)   dW = dy^T g (cuBLAS, fp32 out), db = colsum(dy), dg = dy W on the
+#   head (actor)   dW = dy^T g, db = colsum(dy), dg = dy W on the
 #                  tcgen05 GEMM (dy bf16 with rows padded to 184 columns)
 #   head (critic)  one kernel: dh, its column sums, dW and db of the scalar head
 #   act'(h)        fused with the column sums that are the producing layer's bias
@@ -255,6 +255,7 @@ class FusedResidualMlp(nn.Module):
 #                  dh += dz W1 on the GEMM (residual epilogue), db2 of the block
 #                  below = colsum(dh)
 #   input layer    dW = dh^T x
+# Every dW = dY^T X runs on the split-K tcgen05 kernel (cugo_b200_wgrad_bf16).
 
 _ACT_GRAD = {"relu": 1, "silu": 2}
 
@@ -294,8 +295,8 @@ def train_forward(net: "FusedResidualMlp", x: torch.Tensor):
     h = ext.linear(xb, ws[0][:, :k_in], bs[0])
     saved = {"x": xb, "h": [], "z": [], "u": []}
     for i in range(net.n_blocks):
-        z = ext.linear(h, ws[1 + 2 * i], bs[1 + 2 * i])
-        u = _act(z, kind)
+        z = torch.empty_like(h)
+        u = ext.linear_pre(h, ws[1 + 2 * i], bs[1 + 2 * i], _ACT[kind], z)  # u = act(z), z kept
         saved["h"].append(h)
         saved["z"].append(z)
         saved["u"].append(u)
@@ -341,7 +342,7 @@ def train_backward(net: "FusedResidualMlp", saved: dict, dy: torch.Tensor | None
                                  _grad(lin[-1].weight).view(-1), _grad(lin[-1].bias))
     else:
         n_out = lin[-1].out_features
-        torch.mm(dy[:, :n_out].t(), saved["g"], out_dtype=torch.float32, out=_grad(lin[-1].weight))
+        ext.wgrad_bf16(dy, saved["g"], _grad(lin[-1].weight), n_out=n_out)
         sums = torch.empty(dy.shape[1], dtype=torch.float32, device=dy.device)
         ext.colsum_bf16(dy, sums)
         _grad(lin[-1].bias).copy_(sums[:n_out])
@@ -350,14 +351,14 @@ def train_backward(net: "FusedResidualMlp", saved: dict, dy: torch.Tensor | None
     for i in reversed(range(net.n_blocks)):
         h, z, u = saved["h"][i], saved["z"][i], saved["u"][i]
         fc1, fc2 = lin[1 + 2 * i], lin[2 + 2 * i]
-        torch.mm(dh.t(), u, out_dtype=torch.float32, out=_grad(fc2.weight))
+        ext.wgrad_bf16(dh, u, _grad(fc2.weight))
         du = ext.linear(dh, wt[2 * i + 1])                      # dh W2
         dz = torch.empty_like(du)
         ext.colsum_bf16(du, _grad(fc1.bias), z=z, act=act, dz=dz)
-        torch.mm(dz.t(), h, out_dtype=torch.float32, out=_grad(fc1.weight))
+        ext.wgrad_bf16(dz, h, _grad(fc1.weight))
         dh = ext.linear(dz, wt[2 * i], residual=dh)              # dh + dz W1
         ext.colsum_bf16(dh, _grad(lin[2 * i].bias))              # the layer below's bias
-    torch.mm(dh.t(), saved["x"], out_dtype=torch.float32, out=_grad(lin[0].weight))
+    ext.wgrad_bf16(dh, saved["x"], _grad(lin[0].weight))
 
 
 def fused_actor(hidden: int = 512, blocks: int = 3) -> FusedResidualMlp:
@@ -384,14 +385,20 @@ def critic_input(features: torch.Tensor, opp_hand: torch.Tensor,
                  stock: torch.Tensor | None = None) -> torch.Tensor:
     """[features, one-hot plane of the opponent's hand, (one-hot planes of the next
     8 stock draws, stock_indexed's packing, 0xFF = none)] as bf16 (the reference's
-    _critic_input, python/cugo_ppo50.py:478-482)."""
+    _critic_input, python/cugo_ppo50.py:478-482).  The rows are written into a buffer padded to a multiple of 8 columns (zeros
+    past the last input) and returned as a view of the input width, so the first
+    GEMM reads them in place (its TMA rows must be 16-byte multiples)."""
     dev = opp_hand.device
     bits = torch.arange(ORACLE_FEATURES, device=dev)
-    parts = [features.to(torch.bfloat16), ((opp_hand.view(-1, 1) >> bits) & 1).to(torch.bfloat16)]
+    width = FEATURES + ORACLE_FEATURES + (STOCK_FEATURES if stock is not None else 0)
+    out = torch.empty((features.shape[0], _pad8(width)), dtype=torch.bfloat16, device=dev)
+    out[:, :FEATURES] = features
+    out[:, FEATURES:FEATURES + ORACLE_FEATURES] = (opp_hand.view(-1, 1) >> bits) & 1
     if stock is not None:
         cards = (stock.view(-1, 1) >> torch.arange(0, 64, 8, device=dev)) & 0xFF
-        parts.append((cards.unsqueeze(-1) == bits).flatten(1).to(torch.bfloat16))
-    return torch.cat(parts, 1)
+        out[:, FEATURES + ORACLE_FEATURES:width] = (cards.unsqueeze(-1) == bits).flatten(1)
+    out[:, width:] = 0
+    return out[:, :width]
 
 
 def allreduce_gradients(params: list[torch.Tensor], world: int) -> None:

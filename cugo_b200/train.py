@@ -286,7 +286,8 @@ class PpoTrainer:
                  grad_clip: float = 1.0, use_graph: bool = True, world: int = 1) -> None:
         self.actor, self.critic, self.minibatch = actor, critic, minibatch
         params = list(actor.parameters()) + list(critic.parameters())
-        self.optimizer = torch.optim.Adam(params, lr=lr, capturable=use_graph)
+        # The reference trainer's optimizer (python/train_ppo50.py:153-156).
+        self.optimizer = torch.optim.Adam(params, lr=lr, eps=1e-5, fused=True, capturable=use_graph)
         self.step = make_ppo_step(actor, critic, self.optimizer, clip, value_coef, grad_clip, world)
         self.use_graph = use_graph
         self.world = world

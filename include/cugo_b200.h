@@ -226,6 +226,18 @@ CUGO_B200_API int cugo_b200_gemm_bf16_ex(const void* a, int64_t lda, const void*
                                          int32_t act_after, int64_t m, int64_t n, int64_t k,
                                          int32_t* error, cudaStream_t stream);
 
+/* out = act(a w^T + bias) (bf16) and pre = a w^T + bias (bf16, row stride ldp):
+ * a layer of a training forward that keeps its pre-activation for act' in the
+ * backward, in one launch (no residual, bf16 output only).  Arguments otherwise as
+ * for cugo_b200_gemm_bf16_ex.  Replaces an nn.Linear followed by the activation
+ * under bf16 autocast (python/cugo_ppo_nets50.py:26-64, ResidualMlp's fc1 and
+ * activation, as autograd saves both). */
+CUGO_B200_API int cugo_b200_gemm_bf16_pre(const void* a, int64_t lda, const void* w, int64_t ldw,
+                                          const void* bias, int32_t bias_fp32, void* out,
+                                          int64_t ldo, void* pre, int64_t ldp, int32_t act,
+                                          int64_t m, int64_t n, int64_t k, int32_t* error,
+                                          cudaStream_t stream);
+
 /* cugo_b200_gemm_bf16_ex over a row window read from device memory when the
  * kernel starts: window = int32 {first row, rows} (clamped to [0, m]); only those
  * rows of a and out (and residual) are touched, the others keep their values
@@ -355,6 +367,26 @@ CUGO_B200_API int cugo_b200_scalar_head_backward(const float* dv, const void* w,
                                                  int64_t rows, int32_t n, float* dh_sums,
                                                  float* dw, float* db, float* scratch,
                                                  int64_t scratch_floats, cudaStream_t stream);
+
+/* Weight gradient of a linear layer: dw[o][i] = sum over the rows r of
+ * dy[r][o] x[r][i] (fp32 out, row stride lddw), with dy bf16 [rows, n_out] (row
+ * stride lddy) and x bf16 [rows, n_in] (ldx): both operands enter the tcgen05 MMA
+ * transposed (MN-major), the rows split across the SMs, each split's partial tile
+ * written to scratch and the splits added in a fixed order (the same result on
+ * every run).  scratch: the caller's fp32 buffer (16-byte aligned) of at least
+ * cugo_b200_wgrad_scratch_floats(rows, n_out, n_in) floats; a smaller one returns
+ * CUGO_B200_ERR_CAPACITY.  dy, x 16-byte aligned, strides multiples of 8.  error
+ * as for cugo_b200_gemm_bf16.  Replaces the weight gradients autograd computes
+ * for the reference's nn.Linear layers under bf16 autocast (python/cugo_ppo50.py:
+ * 558-623, PpoUpdater._step's backward). */
+CUGO_B200_API int cugo_b200_wgrad_bf16(const void* dy, int64_t lddy, const void* x, int64_t ldx,
+                                       int64_t rows, int64_t n_out, int64_t n_in, float* dw,
+                                       int64_t lddw, float* scratch, int64_t scratch_floats,
+                                       int32_t* error, cudaStream_t stream);
+
+/* Scratch floats cugo_b200_wgrad_bf16 needs for `rows` rows of an n_out x n_in
+ * weight. */
+CUGO_B200_API int64_t cugo_b200_wgrad_scratch_floats(int64_t rows, int64_t n_out, int64_t n_in);
 
 /* Policy forward that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory — for example a Go/Java/Rust

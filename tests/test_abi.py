@@ -87,3 +87,28 @@ def test_noalloc_forward_capacity_check_does_not_wrap():
     err_capacity = -4
     for m, hidden in ((1 << 33, 1 << 31), (1 << 62, 4), (1, (4 << 20) + 1), ((4 << 20) // 512 + 1, 512)):
         assert fn(None, 720, m, 720, hidden, 3, 180, w, None, 1, None, 180, None, None) == err_capacity
+
+
+def test_wgrad_arguments_checked_before_launch():
+    """The weight-gradient entry refuses bad sizes, misaligned operands and a scratch
+    buffer smaller than its own size query before touching the device; the query
+    covers every split's padded partial tile."""
+    lib = load_library()
+    fn = lib.cugo_b200_wgrad_bf16
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+    fn.argtypes = [vp, i64, vp, i64, i64, i64, i64, vp, i64, vp, i64, vp, vp]
+    fn.restype = ctypes.c_int
+    q = lib.cugo_b200_wgrad_scratch_floats
+    q.argtypes, q.restype = [i64, i64, i64], i64
+    need = q(32768, 512, 512)
+    assert need > 0 and need % (512 * 512) == 0  # whole 128 x 256 tiles per split
+    assert q(32768, 179, 512) % (256 * 512) == 0  # 179 outputs padded to two 128-row tiles
+    assert q(0, 512, 512) == 0
+    a = 0x10000
+    assert fn(a, 512, a, 512, 64, 0, 512, a, 512, a, need, None, None) == -1   # no outputs
+    assert fn(a, 100, a, 512, 64, 512, 512, a, 512, a, need, None, None) == -1  # lddy < n_out
+    assert fn(a + 8, 512, a, 512, 64, 512, 512, a, 512, a, need, None, None) == -2
+    assert fn(a, 516, a, 512, 64, 512, 512, a, 512, a, need, None, None) == -2  # stride not 16 B
+    small = q(64, 512, 512) - 1
+    assert fn(a, 512, a, 512, 64, 512, 512, a, 512, a, small, None, None) == -4
+    assert fn(a, 512, a, 512, 64, 512, 512, a, 512, None, need, None, None) == -4

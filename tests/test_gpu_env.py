@@ -145,6 +145,22 @@ def test_branch_children_match_oracle(ext, oracle):
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("ragged", [0, 100, 300])
+def test_branch_config2_windows_match_oracle(ext, oracle, ragged):
+    """Config 2's layout (256 branches per root, one root per warp's group of
+    entries): every child and output equals the oracle's clone + step, including a
+    ragged end inside a group and inside a block's last warp."""
+    roots = ext.branch_roots(301, seed_base=4242)
+    ids, actions = ext.branch_actions(roots, 256, seed_base=4242)
+    m = ids.numel() - ragged
+    ids, actions = ids[:m].contiguous(), actions[:m].contiguous()
+    out = [n(x) for x in ext.branch_indexed(roots, ids, actions)]
+    o = oracle.step(n(roots)[n(ids)], n(actions))
+    assert np.array_equal(out[0], o[0])
+    for a, b in zip(out[1:], o[1:]):
+        assert np.array_equal(a, b)
+
+
 @pytest.mark.parametrize("layout", ["all_actions", "shuffled", "repeats"])
 def test_branch_entries_of_every_layout_match_oracle(ext, oracle, layout):
     """branch_indexed makes each distinct (parent, action) child once per 256 entries

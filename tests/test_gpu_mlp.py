@@ -163,3 +163,16 @@ def test_policy_logit_bar_at_the_reference_init(ext, capsys):
               f"(autocast {agree_auto:.5f}); vs autocast {agree_pair:.5f}")
     assert err <= 2e-2
     assert agree >= agree_auto - 1e-3
+
+
+@pytest.mark.parametrize("m,n,k,act", [(32768, 512, 512, 2), (1000, 512, 720, 1), (300, 2048, 2048, 2)])
+def test_linear_pre_keeps_the_pre_activation(ext, m, n, k, act):
+    """linear_pre writes act(a w^T + b) and a w^T + b from one GEMM launch: each
+    equals the plain layer's output (no activation / with it) bit for bit."""
+    a = _rand((m, k), seed=1).to(DEV, torch.bfloat16)
+    w = _rand((n, k), scale=k ** -0.5, seed=2).to(DEV, torch.bfloat16)
+    b = _rand((n,), seed=3).to(DEV)
+    pre = torch.empty((m, n), dtype=torch.bfloat16, device=DEV)
+    out = ext.linear_pre(a, w, b, act, pre)
+    assert torch.equal(pre, ext.linear(a, w, b))
+    assert torch.equal(out, ext.linear(a, w, b, act=act))
