@@ -505,6 +505,64 @@ def reference_arm(args, world, rank):
     }))
 
 
+# ---- the data-parallel PPO update (N > 1) ------------------------------------------------
+
+def ppo_dp_bench(world: int, rank: int, rows: int = 32768, warmup: int = 3, iters: int = 10) -> dict:
+    """One PPO minibatch step per rank (3x512 SiLU actor + critic, `rows` rows each,
+    NativePpoStep with the gradient all-reduce over NCCL: the critic's bucket in
+    flight during the actor's backward), and the all-reduce of both buckets alone.
+    Device time (CUDA events), max over ranks; every rank takes the same steps."""
+    from cugo_b200.ppo import Minibatch, NativePpoStep, fused_actor, fused_critic
+    dev = torch.device("cuda")
+    torch.manual_seed(0)  # identical networks on every rank
+    actor, critic = fused_actor().to(dev), fused_critic().to(dev)
+    with torch.no_grad():  # non-zero residual branches and heads
+        for p in list(actor.parameters()) + list(critic.parameters()):
+            if not p.any():
+                p.normal_(0.0, 0.02)
+    g = torch.Generator(device="cpu").manual_seed(1 + rank)  # each rank its own shard
+    legal = torch.rand((rows, 179), generator=g) < 0.1
+    legal[:, 0] = True
+    mb = Minibatch(features=torch.rand((rows, 720), generator=g).to(dev, torch.bfloat16),
+                   legal=legal.to(dev), actions=torch.zeros(rows, dtype=torch.int64, device=dev),
+                   logp_old=torch.full((rows,), -2.0, device=dev),
+                   opp_hand=torch.randint(0, 1 << 50, (rows,), generator=g).to(dev),
+                   adv=torch.randn(rows, generator=g).to(dev), ret=torch.randn(rows, generator=g).to(dev))
+    params = list(actor.parameters()) + list(critic.parameters())
+    opt = torch.optim.Adam(params, lr=3e-4, eps=1e-5, fused=True, capturable=True)
+    step = NativePpoStep(actor, critic, opt, world=world)
+
+    def timed(fn, n):
+        barrier(world)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return all_reduce([a.elapsed_time(b) / 1e3 / n], world, op="max")[0]
+
+    for _ in range(warmup):
+        step.step(mb)
+    sec_step = timed(lambda: step.step(mb), iters)
+    from cugo_b200.ppo import finish_allreduce, start_allreduce
+    buckets = [(list(critic.parameters()), step.flat["critic"]),
+               (list(actor.parameters()), step.flat["actor"])]
+    sec_ar = timed(lambda: [finish_allreduce(start_allreduce(ps, world, f)) for ps, f in buckets], iters)
+    # The networks stay identical on every rank (the averaged gradients are).
+    total = sum(float(p.detach().double().sum()) for p in params)
+    spread = all_reduce([total], world, op="max")[0] - (-all_reduce([-total], world, op="max")[0])
+    nbytes = 4 * sum(p.numel() for p in params)
+    return {"rows_per_rank": rows, "networks": "3x512 actor + critic (SiLU)", "world": world,
+            "step_seconds": sec_step, "rows_per_s": rows * world / sec_step,
+            "allreduce_seconds": sec_ar, "bucket_bytes": nbytes,
+            "allreduce_busbw_gbs": 2 * (world - 1) / world * nbytes / sec_ar / 1e9,
+            "param_sum_spread_over_ranks": spread,
+            "note": "eager steps (the graphed step is single-GPU); allreduce_seconds is both "
+                    "buckets alone, step_seconds includes them overlapped with the backward"}
+
+
 # ---- main -------------------------------------------------------------------------------
 
 def main():
@@ -546,6 +604,9 @@ def main():
         else:
             extras["reference_gpu"] = {"unavailable": "baseline/_ref not staged "
                                                       "(python -m baseline.build_ref)"}
+    elif not args.no_extras:
+        # The data-parallel update is the one extra with a collective: every rank runs it.
+        extras["ppo_update_dp"] = ppo_dp_bench(world, rank)
     peaks = measured_peaks()
     if "engine_only" in extras:
         e = extras["engine_only"]

@@ -404,15 +404,58 @@ def critic_input(features: torch.Tensor, opp_hand: torch.Tensor,
 def allreduce_gradients(params: list[torch.Tensor], world: int) -> None:
     """Averages the gradients of `params` over the ranks with one all-reduce of a
     flat bucket (the data-parallel step of the update; a no-op for one rank)."""
-    if world <= 1:
-        return
-    grads = [p.grad for p in params if p.grad is not None]
-    flat = torch.cat([g.reshape(-1) for g in grads])
-    dist.all_reduce(flat)
-    flat.div_(world)
+    finish_allreduce(start_allreduce(params, world))
+
+
+def flat_gradients(params: list[torch.Tensor]) -> torch.Tensor:
+    """Makes every parameter's .grad a view into one flat fp32 buffer (returned), so a
+    data-parallel step all-reduces the gradients in place, with no gather into a
+    bucket and no copy back.  The gradients must then be written, not replaced
+    (zero_grad with set_to_none=False)."""
+    total = sum(p.numel() for p in params)
+    flat = torch.zeros(total, dtype=torch.float32, device=params[0].device)
     off = 0
-    for g in grads:
-        g.copy_(flat[off:off + g.numel()].view_as(g))
+    for p in params:
+        p.grad = flat[off:off + p.numel()].view_as(p)
+        off += p.numel()
+    return flat
+
+
+class _Bucket:
+    """A flat gradient bucket whose all-reduce is in flight; `grads` are the
+    tensors to copy the result back into (None when the bucket is their storage)."""
+
+    def __init__(self, grads: list[torch.Tensor] | None, flat: torch.Tensor, work, world: int) -> None:
+        self.grads, self.flat, self.work, self.world = grads, flat, work, world
+
+
+def start_allreduce(params: list[torch.Tensor], world: int,
+                    flat: torch.Tensor | None = None) -> "_Bucket | None":
+    """Starts the all-reduce of the gradients of `params` without waiting: on NCCL
+    the collective runs on the communicator's stream after the work queued so far,
+    so the caller's next kernels (the other network's backward) overlap it.  `flat`:
+    the buffer of flat_gradients(params), reduced in place; otherwise the gradients
+    are gathered into a new bucket.  None for one rank."""
+    if world <= 1:
+        return None
+    if flat is not None:
+        return _Bucket(None, flat, dist.all_reduce(flat, async_op=True), world)
+    grads = [p.grad for p in params if p.grad is not None]
+    bucket = torch.cat([g.reshape(-1) for g in grads])
+    return _Bucket(grads, bucket, dist.all_reduce(bucket, async_op=True), world)
+
+
+def finish_allreduce(bucket: "_Bucket | None") -> None:
+    """Waits for a bucket's all-reduce and leaves the averaged gradients in place."""
+    if bucket is None:
+        return
+    bucket.work.wait()
+    bucket.flat.div_(bucket.world)
+    if bucket.grads is None:
+        return
+    off = 0
+    for g in bucket.grads:
+        g.copy_(bucket.flat[off:off + g.numel()].view_as(g))
         off += g.numel()
 
 
@@ -494,6 +537,9 @@ class NativePpoStep(PpoStep):
         super().__init__(actor, critic, optimizer, clip, value_coef, grad_clip, world)
         self.stats = torch.zeros(5, device=self.sums.device)
         self.ones = torch.ones(1, device=self.sums.device)
+        # Each network's gradients live in one flat buffer, the bucket of its all-reduce.
+        self.flat = {"actor": flat_gradients(list(actor.parameters())),
+                     "critic": flat_gradients(list(critic.parameters()))} if world > 1 else {}
 
     @staticmethod
     def supports(actor: nn.Module, critic: nn.Module) -> bool:
@@ -511,9 +557,16 @@ class NativePpoStep(PpoStep):
         dv = torch.empty(b, dtype=torch.float32, device=logits.device)
         ext.ppo_loss(logits, mb.legal, mb.actions, mb.logp_old, mb.adv, value, mb.ret, self.clip,
                      self.entropy_coef, self.value_coef, dy, dv, self.stats)
-        train_backward(self.actor, a_saved, dy=dy)
+        # Data parallel: the critic's gradients are all-reduced while the actor's
+        # backward runs (two buckets, the same collective order on every rank).
         train_backward(self.critic, c_saved, dv=dv)
-        allreduce_gradients([p for g in self.groups for p in g], self.world)
+        critic_bucket = start_allreduce(list(self.critic.parameters()), self.world,
+                                        self.flat.get("critic"))
+        train_backward(self.actor, a_saved, dy=dy)
+        actor_bucket = start_allreduce(list(self.actor.parameters()), self.world,
+                                       self.flat.get("actor"))
+        finish_allreduce(critic_bucket)
+        finish_allreduce(actor_bucket)
         for group in self.groups:
             nn.utils.clip_grad_norm_(group, self.grad_clip, foreach=True)
         self.optimizer.step()
