@@ -66,6 +66,9 @@ class ResidualMlpPolicy:
                         device: torch.device | str = "cuda") -> "ResidualMlpPolicy":
         """Loads a reference ResidualMlp/PpoActor/OracleCritic state dict
         (inp, blocks.i.fc1/fc2, out), e.g. from a train_ppo50.py checkpoint."""
+        if any(k.endswith("norm.weight") for k in state):
+            raise ValueError("ResidualMlpPolicy runs norm='none' networks; load a LayerNorm "
+                             "network as cugo_b200.ppo.FusedResidualMlp(..., norm='layer')")
         hidden, inputs = state["inp.weight"].shape
         outputs = state["out.weight"].shape[0]
         self = cls(hidden, blocks, activation, outputs, device, seed=None, inputs=inputs)

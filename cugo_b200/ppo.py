@@ -49,10 +49,81 @@ def _act_backward(grad: torch.Tensor, z: torch.Tensor, kind: str) -> torch.Tenso
     return torch.ops.aten.silu_backward(grad, z)
 
 
+def _pad4(n: int) -> int:
+    return (n + 3) // 4 * 4
+
+
+def _rows16(t: torch.Tensor) -> torch.Tensor:
+    """t as bf16 rows whose stride is a multiple of 8 elements (16 bytes, the TMA
+    rule): t itself when it already is, else a zero-padded copy viewed at t's width."""
+    if t.dtype == torch.bfloat16 and t.stride(1) == 1 and t.stride(0) % 8 == 0:
+        return t
+    m, k = t.shape
+    z = torch.zeros((m, _pad8(k)), dtype=torch.bfloat16, device=t.device)
+    z[:, :k] = t
+    return z[:, :k]
+
+
+class _LinearFn(torch.autograd.Function):
+    """One nn.Linear on the tcgen05 kernels, for networks run layer by layer under
+    autograd (LayerNorm trunks, the belief head): forward y = x W^T + b (bf16, or fp32
+    for a head); backward dX = dY W on the GEMM with the transposed weight, dW = dY^T X
+    on the split-K weight-gradient kernel, db = the column sums of dY (fixed order)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, ext, out_fp32):
+        m, k = x.shape
+        n = weight.shape[0]
+        xb = _rows16(x)
+        wb = _rows16(weight.detach())
+        if out_fp32:
+            y = torch.empty((m, _pad4(n)), dtype=torch.float32, device=x.device)[:, :n]
+            ext.linear(xb, wb, bias.detach(), out=y)
+        else:
+            y = torch.empty((m, _pad8(n)), dtype=torch.bfloat16, device=x.device)[:, :n]
+            ext.linear(xb, wb, bias.detach(), out=y)
+        ctx.save_for_backward(xb, wb)
+        ctx.ext = ext
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        xb, wb = ctx.saved_tensors
+        ext = ctx.ext
+        m, k = xb.shape
+        n = wb.shape[0]
+        dyb = torch.zeros((m, _pad8(n)), dtype=torch.bfloat16, device=dy.device)
+        dyb[:, :n] = dy
+        dx = None
+        if ctx.needs_input_grad[0]:
+            wt = torch.zeros((k, _pad8(n)), dtype=torch.bfloat16, device=dy.device)
+            wt[:, :n] = wb.t()
+            dx = torch.empty((m, _pad8(k)), dtype=torch.bfloat16, device=dy.device)[:, :k]
+            ext.linear(dyb[:, :n], wt[:, :n], out=dx)
+        dw = torch.empty((n, k), dtype=torch.float32, device=dy.device)
+        ext.wgrad_bf16(dyb, xb, dw, n_out=n, n_in=k)
+        sums = torch.empty(_pad8(n), dtype=torch.float32, device=dy.device)
+        ext.colsum_bf16(dyb, sums)
+        return dx, dw, sums[:n], None, None
+
+
+def _lin(layer: nn.Linear, x: torch.Tensor, ext, out_fp32: bool = False) -> torch.Tensor:
+    return _LinearFn.apply(x, layer.weight, layer.bias, ext, out_fp32)
+
+
+def _layer_norm_bf16(norm: nn.Module, h: torch.Tensor) -> torch.Tensor:
+    """nn.LayerNorm as the reference runs it under bf16 autocast: fp32 statistics
+    and affine, the result rounded to bf16 for the next Linear."""
+    if isinstance(norm, nn.Identity):
+        return h
+    return F.layer_norm(h.float(), norm.normalized_shape, norm.weight, norm.bias,
+                        norm.eps).to(torch.bfloat16)
+
+
 class _Block(nn.Module):
-    def __init__(self, hidden: int) -> None:
+    def __init__(self, hidden: int, norm: str = "none") -> None:
         super().__init__()
-        self.norm = nn.Identity()
+        self.norm = nn.LayerNorm(hidden) if norm == "layer" else nn.Identity()
         self.fc1 = nn.Linear(hidden, hidden)
         self.fc2 = nn.Linear(hidden, hidden)
 
@@ -137,23 +208,34 @@ class _FusedMlpFunction(torch.autograd.Function):
 
 
 class FusedResidualMlp(nn.Module):
-    """ResidualMlp (norm "none") whose forward and data gradients run on the fused
-    tcgen05 GEMM.  squeeze: return [M] for a single output (OracleCritic)."""
+    """ResidualMlp whose forward and gradients run on the tcgen05 kernels.
+    squeeze: return [M] for a single output (OracleCritic).
+
+    norm "none" (the reference trainer's default): the whole network is one autograd
+    function (or one fused kernel for inference).  norm "layer"
+    (python/cugo_ppo_nets50.py:20-37: nn.LayerNorm before each block's fc1 and before
+    the head): layer by layer under autograd, every Linear on the tcgen05 kernels
+    (`_LinearFn`), the LayerNorms and activations in torch; inference keeps an fp32
+    residual stream updated in place by the fc2 GEMMs and normalises it with the
+    native row LayerNorm."""
 
     def __init__(self, inputs: int, outputs: int, hidden: int = 512, blocks: int = 3,
                  activation: str = "silu", squeeze: bool = False, zero_out: bool = False,
-                 value_bins: int = 0, value_top: float = 640.0) -> None:
+                 value_bins: int = 0, value_top: float = 640.0, norm: str = "none") -> None:
         super().__init__()
         if activation not in _ACT:
             raise ValueError("activation must be relu or silu")
+        if norm not in ("none", "layer"):
+            raise ValueError("norm must be none or layer")
         self.activation, self.n_blocks, self.squeeze = activation, blocks, squeeze
+        self.norm_kind = norm
         self.inp = nn.Linear(inputs, hidden)
-        self.blocks = nn.Sequential(*(_Block(hidden) for _ in range(blocks)))
-        self.norm = nn.Identity()
+        self.blocks = nn.Sequential(*(_Block(hidden, norm) for _ in range(blocks)))
+        self.norm = nn.LayerNorm(hidden) if norm == "layer" else nn.Identity()
         self.out = nn.Linear(hidden, outputs)
         # The reference's norm="none" initialisation: zero residual branches; the
-        # actor also zeroes its output layer (python/cugo_ppo_nets50.py:34-36,61-62).
-        for b in self.blocks:
+        # actor also zeroes its output layer (python/cugo_ppo_nets50.py:26-31,61-62).
+        for b in self.blocks if norm == "none" else ():
             nn.init.zeros_(b.fc2.weight)
             nn.init.zeros_(b.fc2.bias)
         if zero_out:
@@ -186,11 +268,58 @@ class FusedResidualMlp(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         params = [t for l in self.linears() for t in (l.weight, l.bias)]
         x = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
-        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in params)):
+        grad = torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in params))
+        if self.norm_kind == "layer":
+            out = self._forward_layers(x)[0] if grad else self._infer_layer(x, params)
+        elif grad:
             out = _FusedMlpFunction.apply(x, self, *params)
         else:
             out = self._infer(x, params)
         return out.squeeze(-1) if self.squeeze and out.shape[-1] == 1 else out
+
+    def forward_hidden(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """(output, the trunk's final hidden state before the head's norm), as the
+        reference's ResidualMlp.forward_hidden (for the belief head); layer by layer."""
+        x = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+        return self._forward_layers(x)
+
+    def _forward_layers(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Layer by layer under autograd: the reference's module structure under bf16
+        autocast (bf16 residual stream, fp32 LayerNorm rounded to bf16)."""
+        ext = self.ext
+        act = F.silu if self.activation == "silu" else F.relu
+        h = _lin(self.inp, _rows16(x[:, :self.inp.in_features]), ext)
+        for b in self.blocks:
+            u = act(_lin(b.fc1, _layer_norm_bf16(b.norm, h), ext))
+            h = h + _lin(b.fc2, u, ext)
+        out = _lin(self.out, act(_layer_norm_bf16(self.norm, h)), ext, out_fp32=True)
+        return out, h
+
+    def _infer_layer(self, x: torch.Tensor, params: list[torch.Tensor]) -> torch.Tensor:
+        """Inference with LayerNorms: an fp32 residual stream updated in place by the
+        fc2 GEMMs' epilogues, normalised into bf16 by the native row LayerNorm."""
+        ext = self.ext
+        act = _ACT[self.activation]
+        ws, bs = self._weights(params)
+        m, k_pad = x.shape[0], ws[0].shape[1]
+        if x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.shape[1] >= k_pad:
+            xb = x[:, :k_pad]
+        else:
+            xb = torch.zeros((m, k_pad), dtype=torch.bfloat16, device=x.device)
+            xb[:, :self.inp.in_features] = x[:, :self.inp.in_features]
+        hidden = ws[0].shape[0]
+        h = torch.empty((m, hidden), dtype=torch.float32, device=x.device)
+        ext.linear(xb, ws[0], bs[0], out=h)
+        for i, b in enumerate(self.blocks):
+            n = ext.layernorm(h, b.norm.weight.detach(), b.norm.bias.detach(), b.norm.eps)
+            u = ext.linear(n, ws[1 + 2 * i], bs[1 + 2 * i], act=act)
+            ext.linear(u, ws[2 + 2 * i], bs[2 + 2 * i], residual=h, out=h)
+        g = ext.layernorm(h, self.norm.weight.detach(), self.norm.bias.detach(), self.norm.eps)
+        g = F.silu(g) if self.activation == "silu" else F.relu(g)
+        n_out = ws[-1].shape[0]
+        out = torch.empty((m, _pad4(n_out)), dtype=torch.float32, device=x.device)
+        ext.linear(g, ws[-1], bs[-1], out=out[:, :n_out])
+        return out[:, :n_out]
 
     def _weights(self, params: list[torch.Tensor]):
         """bf16 weights (the input layer's zero-padded to 16-byte rows, contiguous)
@@ -361,22 +490,65 @@ def train_backward(net: "FusedResidualMlp", saved: dict, dy: torch.Tensor | None
     ext.wgrad_bf16(dh, saved["x"], _grad(lin[0].weight))
 
 
-def fused_actor(hidden: int = 512, blocks: int = 3) -> FusedResidualMlp:
+def fused_actor(hidden: int = 512, blocks: int = 3, norm: str = "none") -> FusedResidualMlp:
     """PpoActor's shape: 720 features -> 179 logits, zero-initialised output layer."""
-    return FusedResidualMlp(FEATURES, ACTIONS, hidden, blocks, "silu", zero_out=True)
+    return FusedResidualMlp(FEATURES, ACTIONS, hidden, blocks, "silu", zero_out=True, norm=norm)
+
+
+class FusedBeliefHead(nn.Module):
+    """The reference's BeliefHead (python/cugo_ppo_nets50.py:94-105, the same parameter
+    names: net.0 LayerNorm, net.1 and net.3 Linear): logits of which of the 50 cards
+    the opponent holds, from the actor trunk's final hidden state; the Linears on
+    the tcgen05 kernels (`_LinearFn`), LayerNorm and GELU in torch, as the reference
+    runs them under bf16 autocast."""
+
+    def __init__(self, inputs: int, width: int | None = None) -> None:
+        super().__init__()
+        width = width or inputs
+        self.net = nn.Sequential(nn.LayerNorm(inputs), nn.Linear(inputs, width), nn.GELU(),
+                                 nn.Linear(width, ORACLE_FEATURES))
+        self._ext = None
+
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        if self._ext is None:
+            self._ext = load_extension()
+        t = F.gelu(_lin(self.net[1], _layer_norm_bf16(self.net[0], h), self._ext))
+        return _lin(self.net[3], t, self._ext, out_fp32=True)
+
+
+def card_plane(masks: torch.Tensor) -> torch.Tensor:
+    """int64 card masks [N] as an fp32 [N, 50] 0/1 plane (the belief targets)."""
+    bits = torch.arange(ORACLE_FEATURES, device=masks.device)
+    return ((masks.view(-1, 1) >> bits) & 1).float()
+
+
+def two_hot(y: torch.Tensor, support: torch.Tensor) -> torch.Tensor:
+    """[N, bins] target whose mean over `support` (increasing) is y clamped to its
+    range: weight split between the two bins around y in proportion to distance
+    (the value-distribution target of the reference's OracleCritic with bins)."""
+    y = torch.minimum(torch.maximum(y, support[0]), support[-1])
+    upper = torch.searchsorted(support, y.contiguous()).clamp(1, support.numel() - 1)
+    lower = upper - 1
+    lo_v, hi_v = support[lower], support[upper]
+    w_upper = ((y - lo_v) / (hi_v - lo_v)).clamp(0.0, 1.0)
+    out = torch.zeros((y.numel(), support.numel()), dtype=torch.float32, device=y.device)
+    out.scatter_(1, lower.view(-1, 1), (1.0 - w_upper).view(-1, 1))
+    out.scatter_add_(1, upper.view(-1, 1), w_upper.view(-1, 1))
+    return out
 
 
 STOCK_FEATURES = 8 * 50  # one-hot planes of the next 8 stock draws
 
 
 def fused_critic(hidden: int = 512, blocks: int = 3, value_bins: int = 0,
-                 value_top: float = 640.0, stock: bool = False) -> FusedResidualMlp:
+                 value_top: float = 640.0, stock: bool = False, norm: str = "none") -> FusedResidualMlp:
     """OracleCritic's shape (python/cugo_ppo_nets50.py:67-91): 770 inputs, or 1,170
     with the stock planes -> one value (or value_bins logits of the return
     distribution)."""
     inputs = FEATURES + ORACLE_FEATURES + (STOCK_FEATURES if stock else 0)
     net = FusedResidualMlp(inputs, value_bins or 1, hidden, blocks, "silu",
-                           squeeze=not value_bins, value_bins=value_bins, value_top=value_top)
+                           squeeze=not value_bins, value_bins=value_bins, value_top=value_top,
+                           norm=norm)
     net.stock = stock
     return net
 
@@ -477,23 +649,35 @@ class Minibatch:
 
 class PpoStep:
     """One PPO minibatch update (python/cugo_ppo50.py:558-623, the plain policy
-    target): clipped surrogate, entropy bonus, smooth-L1 value loss, gradient
-    clipping per network, the optimizer step and the running statistics
-    (policy, value, entropy, KL, clip fraction, count)."""
+    target): clipped surrogate, entropy bonus, value loss (smooth L1, or the
+    cross-entropy against the two-hot return for a critic with value bins),
+    optionally the belief head's binary cross-entropy on the opponent's hand,
+    gradient clipping per network, the optimizer step and the running statistics
+    (policy, value, entropy, KL, clip fraction, count, belief loss)."""
 
     def __init__(self, actor: nn.Module, critic: nn.Module, optimizer: torch.optim.Optimizer,
                  clip: float = 0.2, value_coef: float = 0.5, grad_clip: float = 1.0,
-                 world: int = 1) -> None:
+                 world: int = 1, belief: nn.Module | None = None, belief_coef: float = 0.0) -> None:
         self.actor, self.critic, self.optimizer = actor, critic, optimizer
         self.clip, self.value_coef, self.grad_clip, self.world = clip, value_coef, grad_clip, world
+        self.belief, self.belief_coef = belief, belief_coef
         self.groups = [list(actor.parameters()), list(critic.parameters())]
+        if belief is not None:
+            self.groups.append(list(belief.parameters()))
         dev = next(actor.parameters()).device
         self.entropy_coef = torch.zeros((), device=dev)
-        self.sums = torch.zeros(6, device=dev)
+        self.sums = torch.zeros(7, device=dev)
         self.last_kl = torch.zeros((), device=dev)  # the latest minibatch's KL estimate
 
     def losses(self, mb: Minibatch):
-        logits = self.actor(mb.features).float()
+        belief_loss = None
+        if self.belief is not None:
+            out, hidden = self.actor.forward_hidden(mb.features)
+            logits = out.float()
+            belief_loss = F.binary_cross_entropy_with_logits(self.belief(hidden).float(),
+                                                             card_plane(mb.opp_hand))
+        else:
+            logits = self.actor(mb.features).float()
         stock = mb.stock if getattr(self.critic, "stock", False) else None
         value = self.critic(critic_input(mb.features, mb.opp_hand, stock)).float()
         log_probs = torch.log_softmax(logits.masked_fill(~mb.legal, -1.0e30), dim=1)
@@ -503,14 +687,20 @@ class PpoStep:
         surrogate = torch.minimum(ratio * mb.adv, ratio.clamp(1 - self.clip, 1 + self.clip) * mb.adv)
         policy_loss = -surrogate.mean()
         entropy = -(log_probs.exp() * log_probs).sum(1).mean()
-        value_loss = F.smooth_l1_loss(value, mb.ret)
-        return policy_loss, value_loss, entropy, ratio, log_ratio
+        if getattr(self.critic, "value_bins", 0):
+            target = two_hot(mb.ret, self.critic.support)
+            value_loss = -(target * torch.log_softmax(value, -1)).sum(-1).mean()
+        else:
+            value_loss = F.smooth_l1_loss(value, mb.ret)
+        return policy_loss, value_loss, entropy, ratio, log_ratio, belief_loss
 
     def step(self, mb: Minibatch) -> None:
         """One update, eager (every kernel launched from Python)."""
         self.optimizer.zero_grad(set_to_none=False)
-        policy_loss, value_loss, entropy, ratio, log_ratio = self.losses(mb)
+        policy_loss, value_loss, entropy, ratio, log_ratio, belief_loss = self.losses(mb)
         loss = policy_loss - self.entropy_coef * entropy + self.value_coef * value_loss
+        if belief_loss is not None:
+            loss = loss + self.belief_coef * belief_loss
         loss.backward()
         allreduce_gradients([p for g in self.groups for p in g], self.world)
         for group in self.groups:
@@ -519,9 +709,10 @@ class PpoStep:
         with torch.no_grad():
             kl = ((ratio - 1) - log_ratio).mean()
             self.last_kl.copy_(kl)
+            bl = belief_loss.detach() if belief_loss is not None else torch.zeros_like(kl)
             self.sums += torch.stack((policy_loss.detach(), value_loss.detach(), entropy.detach(), kl,
                                       ((ratio - 1).abs() > self.clip).float().mean(),
-                                      torch.ones_like(kl)))
+                                      torch.ones_like(kl), bl))
 
 
 class NativePpoStep(PpoStep):
@@ -544,6 +735,7 @@ class NativePpoStep(PpoStep):
     @staticmethod
     def supports(actor: nn.Module, critic: nn.Module) -> bool:
         return (isinstance(actor, FusedResidualMlp) and isinstance(critic, FusedResidualMlp)
+                and actor.norm_kind == "none" and critic.norm_kind == "none"
                 and not critic.value_bins and critic.out.out_features == 1
                 and actor.out.out_features == ACTIONS and actor.inp.in_features == FEATURES)
 
@@ -572,16 +764,18 @@ class NativePpoStep(PpoStep):
         self.optimizer.step()
         self.last_kl.copy_(self.stats[3])
         self.sums[:5] += self.stats
-        self.sums[5:] += self.ones
+        self.sums[5:6] += self.ones
 
 
 def make_ppo_step(actor: nn.Module, critic: nn.Module, optimizer: torch.optim.Optimizer,
                   clip: float = 0.2, value_coef: float = 0.5, grad_clip: float = 1.0,
-                  world: int = 1) -> PpoStep:
-    """The native step where both networks are FusedResidualMlp (scalar critic),
-    else the autograd one."""
-    cls = NativePpoStep if NativePpoStep.supports(actor, critic) else PpoStep
-    return cls(actor, critic, optimizer, clip, value_coef, grad_clip, world)
+                  world: int = 1, belief: nn.Module | None = None,
+                  belief_coef: float = 0.0) -> PpoStep:
+    """The native step where both networks are FusedResidualMlp (norm "none", scalar
+    critic, no belief head), else the autograd one."""
+    if belief is None and NativePpoStep.supports(actor, critic):
+        return NativePpoStep(actor, critic, optimizer, clip, value_coef, grad_clip, world)
+    return PpoStep(actor, critic, optimizer, clip, value_coef, grad_clip, world, belief, belief_coef)
 
 
 class GraphedPpoStep:

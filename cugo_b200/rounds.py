@@ -130,7 +130,7 @@ def fused_sampler_params(model: nn.Module, features_width: int):
             return model.weights, model._fp32_biases(), _ACT[model.activation]
         return None
     weights = getattr(model, "_weights", None)
-    if weights is None:
+    if weights is None or getattr(model, "norm_kind", "none") != "none":
         return None
     ws, bs = weights([t for l in model.linears() for t in (l.weight, l.bias)])
     if (fused_mlp_supported(ws[0].shape[0], model.n_blocks, ws[0].shape[1], ws[-1].shape[0])

@@ -269,6 +269,7 @@ class TrainStats:
     explained_var: float
     updates: int
     epochs: float
+    belief_loss: float = float("nan")
 
 
 class PpoTrainer:
@@ -283,12 +284,16 @@ class PpoTrainer:
 
     def __init__(self, actor: nn.Module, critic: nn.Module, lr: float = 3e-4,
                  minibatch: int = 32768, clip: float = 0.2, value_coef: float = 0.5,
-                 grad_clip: float = 1.0, use_graph: bool = True, world: int = 1) -> None:
+                 grad_clip: float = 1.0, use_graph: bool = True, world: int = 1,
+                 belief: nn.Module | None = None, belief_coef: float = 0.0) -> None:
         self.actor, self.critic, self.minibatch = actor, critic, minibatch
+        self.belief = belief
         params = list(actor.parameters()) + list(critic.parameters())
+        params += list(belief.parameters()) if belief is not None else []
         # The reference trainer's optimizer (python/train_ppo50.py:153-156).
         self.optimizer = torch.optim.Adam(params, lr=lr, eps=1e-5, fused=True, capturable=use_graph)
-        self.step = make_ppo_step(actor, critic, self.optimizer, clip, value_coef, grad_clip, world)
+        self.step = make_ppo_step(actor, critic, self.optimizer, clip, value_coef, grad_clip, world,
+                                  belief, belief_coef)
         self.use_graph = use_graph
         self.world = world
         self.graphed: GraphedPpoStep | None = None
@@ -316,6 +321,8 @@ class PpoTrainer:
         parts = [self.critic(critic_input(data.features[i:i + chunk], data.opp_hand[i:i + chunk],
                                           None if stock is None else stock[i:i + chunk]))
                  for i in range(0, n, chunk)]
+        if getattr(self.critic, "value_bins", 0):  # the mean of the return distribution
+            return torch.cat([self.critic.value(p) for p in parts])
         return torch.cat([p.float().reshape(-1) for p in parts])
 
     def _explained_variance(self, returns: torch.Tensor, values: torch.Tensor) -> float:
@@ -370,7 +377,8 @@ class PpoTrainer:
         count = max(1.0, s[5])
         return TrainStats(policy_loss=s[0] / count, value_loss=s[1] / count, entropy=s[2] / count,
                           kl=s[3] / count, clipfrac=s[4] / count, explained_var=explained_var,
-                          updates=updates, epochs=updates / max(1, steps))
+                          updates=updates, epochs=updates / max(1, steps),
+                          belief_loss=s[6] / count if self.belief is not None else float("nan"))
 
 
 def iteration(ext: Any, trainer: PpoTrainer, storage: RolloutStorage, games: int,
