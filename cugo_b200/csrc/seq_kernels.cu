@@ -656,23 +656,25 @@ constexpr int games_smem_bytes(int length) { return 2 * (1 + length) * kKvPitch 
 // ---- decode attention, staged through shared memory by bulk copies ----------------
 //
 // For caches of up to kStagedSlots slots and up to kStagedHeads heads (the sequence
-// policy's 50 slots and 8 heads).  A persistent block takes one query at a time
-// (all its heads): one thread reads the query's cache row and position and issues
-// one bulk copy (cp.async.bulk, completing on an mbarrier) of the attended key
-// slots of each head and one of the value slots -- (pos + 1) x 64 contiguous bytes
-// each -- into one of two shared-memory stages, so the next query's rows are in
-// flight while this one is computed.  Warp h then works on head h from shared
-// memory: four lanes per slot take the 32-dimension dot product of 8 slots per
-// pass, the warp forms the softmax over the slots (fp32), and lane d sums the
-// weighted values of dimension d.  With an append, the slot pos row is not copied:
-// the new key and value go to the stage from the token's own k_new / v_new and to
-// the cache in global memory.  Every wait is bounded (about 2 s on the global
-// timer); a wait that gives up sets *error and the block stops.
+// policy's 50 slots and 8 heads).  A persistent block takes its queries in order (all
+// heads of one query at a time).  One thread reads every query's cache row and
+// position first, then keeps a ring of shared memory filled: each query takes
+// 2 x heads x (pos + 1) x 64 contiguous bytes of the ring (its attended key slots of
+// every head, then its value slots), loaded by one bulk copy (cp.async.bulk) per head
+// and tensor completing on the query's mbarrier -- as many queries in flight as the
+// ring holds (a query's bytes grow with its position, so the ring is filled by
+// bytes, not by a fixed number of stages).  Warp h then works on head h from shared
+// memory: four lanes per slot take the 32-dimension dot product of 8 slots per pass,
+// the warp forms the softmax over the slots (fp32), and lane d sums the weighted
+// values of dimension d.  With an append, the slot pos row is not copied: the new key
+// and value go to the ring from the token's own k_new / v_new and to the cache in
+// global memory.  Every wait is bounded (about 2 s on the global timer); a wait that
+// gives up sets *error and the block stops after its copies in flight have landed.
 constexpr int kStagedSlots = 64;
 constexpr int kStagedHeads = 8;
 constexpr int kStagedThreads = 32 * kStagedHeads;
-constexpr int kStages = 2;
-constexpr int kMaxItemsPerBlock = 256;  // queries a block takes (their rows and positions are prefetched)
+constexpr int kRingItems = 16;          // queries in flight at most (one mbarrier each)
+constexpr int kMaxItemsPerBlock = 64;  // queries a block takes (their rows and positions are prefetched)
 constexpr uint64_t kStagedWaitNs = 2'000'000'000ull;
 
 struct StageInfo {
@@ -708,23 +710,20 @@ __device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Persistent: block b takes queries b, b + grid, ... (at most kMaxItemsPerBlock).
-// All their cache rows and positions are read first, by the whole block, so a
-// copy is issued without a dependent load; two stages keep one query in flight
-// while one is computed, and two blocks run on each SM.
-__global__ void __launch_bounds__(kStagedThreads, 2) decode_attention_staged_kernel(
+__global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_kernel(
     const __nv_bfloat16* __restrict__ q, i64 ldq, const __nv_bfloat16* __restrict__ k_new,
     const __nv_bfloat16* __restrict__ v_new, i64 ldn, __nv_bfloat16* keys, __nv_bfloat16* values,
     i64 n_rows, int heads, int slots, const i64* __restrict__ pos, i64 pos_clamp,
     const i64* __restrict__ rows, i64 n, float scale, __nv_bfloat16* __restrict__ out, i64 ldo,
-    int32_t* error) {
+    int32_t* error, int ring_bytes) {
   extern __shared__ __align__(128) unsigned char smem[];
-  // Layout: kStages stages x {keys, values} x heads x slots x 64 B, the per-warp
-  // slot weights, the items' rows and positions, the mbarriers.
-  const int stage_half = heads * slots * kDh;  // bf16 elements of one stage's keys
-  __nv_bfloat16* stage_kv = reinterpret_cast<__nv_bfloat16*>(smem);
-  float* weights = reinterpret_cast<float*>(smem + kStages * 2 * stage_half * 2);
+  // Layout: the ring, the per-warp slot weights, the items' rows and positions, the
+  // ring offsets of the items in flight, their mbarriers.
+  unsigned char* ring = smem;
+  float* weights = reinterpret_cast<float*>(smem + ring_bytes);
   StageInfo* info = reinterpret_cast<StageInfo*>(weights + kStagedHeads * kStagedSlots);
-  uint64_t* full = reinterpret_cast<uint64_t*>(info + kMaxItemsPerBlock);
+  int* ring_off = reinterpret_cast<int*>(info + kMaxItemsPerBlock);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring_off + kRingItems);
   const int t = threadIdx.x, lane = t & 31, h = t >> 5;
   const i64 grid = gridDim.x;
   const int items = n > blockIdx.x ? static_cast<int>((n - blockIdx.x + grid - 1) / grid) : 0;
@@ -745,48 +744,75 @@ __global__ void __launch_bounds__(kStagedThreads, 2) decode_attention_staged_ker
     info[k].pos = ok ? static_cast<int>(p) : -1;
   }
   if (t == 0) {
-    for (int s = 0; s < kStages; ++s)
+    for (int s = 0; s < kRingItems; ++s)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  // Thread 0: start item k's copies (the attended slots of every head) into stage s.
-  const auto issue = [&](int k, int s) {
+  // Ring bookkeeping, thread 0 only: items [consumed, issued) are in flight, taking
+  // live_bytes bytes; the next one goes at `head` (or wraps to 0).
+  int issued = 0, head = 0, live_bytes = 0;
+  const auto item_bytes = [&](int k) {
+    return info[k].row >= 0 ? 2 * heads * (info[k].pos + 1) * kDh * 2 : 0;
+  };
+  const auto issue = [&](int k, int at) {
     const i64 r = info[k].row;
-    const int copied = r >= 0 ? (k_new ? info[k].pos : info[k].pos + 1) : 0;
+    uint64_t* bar = &full[k % kRingItems];
+    const int p1 = info[k].pos + 1;
+    const int copied = r >= 0 ? (k_new ? p1 - 1 : p1) : 0;
     const uint32_t bytes = static_cast<uint32_t>(copied) * kDh * 2;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full[s])),
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                  "r"(bytes * 2u * static_cast<uint32_t>(heads))
                  : "memory");
     if (bytes == 0) return;
     for (int hh = 0; hh < heads; ++hh) {
       const i64 src = (r * heads + hh) * static_cast<i64>(slots) * kDh;
-      __nv_bfloat16* kd = stage_kv + (2 * s) * stage_half + hh * slots * kDh;
-      __nv_bfloat16* vd = stage_kv + (2 * s + 1) * stage_half + hh * slots * kDh;
+      unsigned char* kd = ring + at + hh * p1 * kDh * 2;
+      unsigned char* vd = ring + at + (heads + hh) * p1 * kDh * 2;
       asm volatile(
           "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-          ::"r"(smem_u32(kd)), "l"(keys + src), "r"(bytes), "r"(smem_u32(&full[s]))
+          ::"r"(smem_u32(kd)), "l"(keys + src), "r"(bytes), "r"(smem_u32(bar))
           : "memory");
       asm volatile(
           "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-          ::"r"(smem_u32(vd)), "l"(values + src), "r"(bytes), "r"(smem_u32(&full[s]))
+          ::"r"(smem_u32(vd)), "l"(values + src), "r"(bytes), "r"(smem_u32(bar))
           : "memory");
     }
   };
+  // Issues items while the ring has room (thread 0; `consumed`: the oldest live item).
+  const auto fill = [&](int consumed) {
+    while (issued < items && issued - consumed < kRingItems) {
+      const int need = item_bytes(issued);
+      int at;
+      if (live_bytes == 0) {
+        at = 0;
+      } else {
+        const int tail = ring_off[consumed % kRingItems];
+        if (head > tail) {  // live bytes in [tail, head)
+          if (head + need <= ring_bytes) at = head;
+          else if (need <= tail) at = 0;
+          else break;
+        } else if (head < tail) {  // wrapped: live in [tail, end) and [0, head)
+          if (head + need <= tail) at = head;
+          else break;
+        } else {
+          break;  // head == tail with live bytes: the ring is full
+        }
+      }
+      ring_off[issued % kRingItems] = at;
+      head = at + need;
+      live_bytes += need;
+      issue(issued, at);
+      ++issued;
+    }
+  };
 
-  if (t == 0)
-    for (int k = 0; k < kStages - 1 && k < items; ++k) issue(k, k);
+  if (t == 0) fill(0);
   float* wrow = weights + h * kStagedSlots;
   bool failed = false;
   for (int k = 0; k < items; ++k) {
-    const int s = k % kStages;
-    const uint32_t parity = static_cast<uint32_t>((k / kStages) & 1);
-    // Item k + kStages - 1 goes to the stage item k - 1 freed (at k = 0: the one
-    // stage the prologue left unused).
-    const int next = k + kStages - 1;
-    if (t == 0 && next < items) issue(next, next % kStages);
-    if (!stage_wait(&full[s], parity)) {
+    if (!stage_wait(&full[k % kRingItems], static_cast<uint32_t>((k / kRingItems) & 1))) {
       failed = true;
       if (t == 0 && error) atomicExch(error, 1);
       break;
@@ -800,9 +826,10 @@ __global__ void __launch_bounds__(kStagedThreads, 2) decode_attention_staged_ker
         o[lane] = __float2bfloat16_rn(0.0f);
         if (lane == 0 && error) atomicExch(error, 1);
       } else {
-        __nv_bfloat16* ks = stage_kv + (2 * s) * stage_half + h * slots * kDh;
-        __nv_bfloat16* vs = stage_kv + (2 * s + 1) * stage_half + h * slots * kDh;
-        if (k_new) {  // the token's own key and value: slot p of the stage and the cache
+        const int at = ring_off[k % kRingItems];
+        __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(ring + at) + h * (p + 1) * kDh;
+        __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(ring + at) + (heads + h) * (p + 1) * kDh;
+        if (k_new) {  // the token's own key and value: slot p of the ring and the cache
           const __nv_bfloat16 kn = k_new[i * ldn + h * kDh + lane];
           const __nv_bfloat16 vn = v_new[i * ldn + h * kDh + lane];
           ks[p * kDh + lane] = kn;
@@ -812,24 +839,33 @@ __global__ void __launch_bounds__(kStagedThreads, 2) decode_attention_staged_ker
           values[dst] = vn;
           __syncwarp();
         }
-        // Scores: lane 4j + c holds dimensions 8c .. 8c + 7 of slot 8 * pass + j.
-        float qf[8];
-        bf16x8(__ldg(reinterpret_cast<const uint4*>(q + i * ldq + h * kDh) + (lane & 3)), qf);
+        // Scores: lane 2j + c holds dimensions 16c .. 16c + 15 of slot 16 * pass + j.
+        float qf[16];
+        {
+          const uint4* qp = reinterpret_cast<const uint4*>(q + i * ldq + h * kDh) + 2 * (lane & 1);
+          bf16x8(__ldg(qp), qf);
+          bf16x8(__ldg(qp + 1), qf + 8);
+        }
         float mx = -INFINITY;
-        for (int t0 = 0; t0 <= p; t0 += 8) {
-          const int slot = t0 + (lane >> 2);
-          float d = 0.0f;
+        for (int t0 = 0; t0 <= p; t0 += 16) {
+          const int slot = t0 + (lane >> 1);
+          float d0 = 0.0f, d1 = 0.0f;
           if (slot <= p) {
-            float kf[8];
-            bf16x8(reinterpret_cast<const uint4*>(ks + slot * kDh)[lane & 3], kf);
+            const uint4* kp = reinterpret_cast<const uint4*>(ks + slot * kDh) + 2 * (lane & 1);
+            float kf[16];
+            bf16x8(kp[0], kf);
+            bf16x8(kp[1], kf + 8);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) d = fmaf(kf[e], qf[e], d);
+            for (int e = 0; e < 8; ++e) {
+              d0 = fmaf(kf[e], qf[e], d0);
+              d1 = fmaf(kf[8 + e], qf[8 + e], d1);
+            }
           }
+          float d = d0 + d1;
           d += __shfl_xor_sync(kFull, d, 1);
-          d += __shfl_xor_sync(kFull, d, 2);
           if (slot <= p) {
             d *= scale;
-            if ((lane & 3) == 0) wrow[slot] = d;
+            if ((lane & 1) == 0) wrow[slot] = d;
             mx = fmaxf(mx, d);
           }
         }
@@ -843,27 +879,60 @@ __global__ void __launch_bounds__(kStagedThreads, 2) decode_attention_staged_ker
         }
         sum = warp_sum(sum);
         __syncwarp();
-        // Output: lane d sums the weighted values of dimension d.
-        float acc = 0.0f;
-        for (int j = 0; j <= p; ++j) acc = fmaf(wrow[j], __bfloat162float(vs[j * kDh + lane]), acc);
-        o[lane] = __float2bfloat16_rn(acc / sum);
+        // Output: lane c + 16 g sums dimensions 2c, 2c + 1 over slots g, g + 2, ...
+        // (two partial sums per dimension in flight), then the two slot halves meet
+        // by one shuffle; all additions in a fixed order.
+        const __nv_bfloat162* vp = reinterpret_cast<const __nv_bfloat162*>(vs) + (lane & 15);
+        float ax0 = 0.0f, ay0 = 0.0f, ax1 = 0.0f, ay1 = 0.0f;
+        int j = lane >> 4;
+        for (; j + 2 <= p; j += 4) {
+          const float2 v0 = __bfloat1622float2(vp[j * (kDh / 2)]);
+          const float2 v1 = __bfloat1622float2(vp[(j + 2) * (kDh / 2)]);
+          const float w0 = wrow[j], w1 = wrow[j + 2];
+          ax0 = fmaf(w0, v0.x, ax0);
+          ay0 = fmaf(w0, v0.y, ay0);
+          ax1 = fmaf(w1, v1.x, ax1);
+          ay1 = fmaf(w1, v1.y, ay1);
+        }
+        if (j <= p) {
+          const float2 v0 = __bfloat1622float2(vp[j * (kDh / 2)]);
+          ax0 = fmaf(wrow[j], v0.x, ax0);
+          ay0 = fmaf(wrow[j], v0.y, ay0);
+        }
+        float ax = ax0 + ax1, ay = ay0 + ay1;
+        const float bx = __shfl_xor_sync(kFull, ax, 16), by = __shfl_xor_sync(kFull, ay, 16);
+        if (lane < 16) {
+          const float inv = 1.0f / sum;
+          reinterpret_cast<__nv_bfloat162*>(o)[lane] =
+              __floats2bfloat162_rn((ax + bx) * inv, (ay + by) * inv);
+        }
       }
     }
-    __syncthreads();  // stage s and the weights are free again
+    __syncthreads();  // item k's ring bytes and the weights are free again
+    if (t == 0) {
+      live_bytes -= item_bytes(k);
+      fill(k + 1);
+    }
   }
   if (failed) {
     // Let copies already issued land before the block's shared memory goes away.
     __syncthreads();
     if (t == 0)
-      for (int s = 0; s < kStages; ++s) stage_wait(&full[s], 0), stage_wait(&full[s], 1);
+      for (int k = 0; k < issued; ++k)
+        stage_wait(&full[k % kRingItems], static_cast<uint32_t>((k / kRingItems) & 1));
   }
   __syncthreads();
 }
 
+// The ring holds the largest query of this cache (2 x heads x slots x 64 bytes, so a
+// query always fits an empty ring), rounded up to 1 KB: at the sequence policy's 8
+// heads and 50 slots four blocks (32 warps) fit an SM.
+int ring_bytes_for(int heads, int slots) { return (2 * heads * slots * kDh * 2 + 1023) / 1024 * 1024; }
+
 size_t staged_smem_bytes(int heads, int slots) {
-  return static_cast<size_t>(kStages) * 2 * heads * slots * kDh * 2 +
-         kStagedHeads * kStagedSlots * 4 + kMaxItemsPerBlock * sizeof(StageInfo) +
-         kStages * sizeof(uint64_t);
+  return static_cast<size_t>(ring_bytes_for(heads, slots)) + kStagedHeads * kStagedSlots * 4 +
+         kMaxItemsPerBlock * sizeof(StageInfo) + kRingItems * sizeof(int) +
+         kRingItems * sizeof(uint64_t);
 }
 
 }  // namespace
@@ -884,7 +953,8 @@ int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new, co
   if (!aligned(q, 16) || ldq % 8 || !aligned(keys, 16) || !aligned(values, 16) || !aligned(out, 2) ||
       (k_new && (!aligned(k_new, 16) || !aligned(v_new, 16) || ldn % 8)))
     return CUGO_B200_ERR_ALIGN;
-  if (heads <= kStagedHeads && slots <= kStagedSlots &&
+  // The staged kernel stores the output as bf16 pairs (4-byte aligned rows).
+  if (heads <= kStagedHeads && slots <= kStagedSlots && aligned(out, 4) && ldo % 2 == 0 &&
       staged_smem_bytes(heads, slots) <= static_cast<size_t>(227 * 1024)) {
     const size_t smem = staged_smem_bytes(heads, slots);
     static size_t configured = 0;
@@ -899,13 +969,20 @@ int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new, co
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess)
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    i64 grid = n < 2 * sms ? n : 2 * sms;  // two blocks per SM
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_attention_staged_kernel,
+                                                      kStagedThreads, smem) != cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    i64 grid = n < per_sm * sms ? n : static_cast<i64>(per_sm) * sms;
     if ((n + grid - 1) / grid > kMaxItemsPerBlock) grid = (n + kMaxItemsPerBlock - 1) / kMaxItemsPerBlock;
     decode_attention_staged_kernel<<<static_cast<unsigned>(grid), kStagedThreads, smem, stream>>>(
         static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k_new),
         static_cast<const __nv_bfloat16*>(v_new), ldn, static_cast<__nv_bfloat16*>(keys),
         static_cast<__nv_bfloat16*>(values), n_rows, heads, slots, pos, pos_clamp, rows, n, scale,
-        static_cast<__nv_bfloat16*>(out), ldo, error);
+        static_cast<__nv_bfloat16*>(out), ldo, error, ring_bytes_for(heads, slots));
     return launch_status();
   }
   decode_attention_kernel<<<blocks_for_warps(n * heads), 256, 0, stream>>>(
