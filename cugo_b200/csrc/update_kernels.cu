@@ -329,14 +329,24 @@ __global__ void __launch_bounds__(kColThreads) scalar_head_backward_kernel(
         const float d = dd[k];
         float hh[8], g[8];
         bf16x8(hx[k], hh);
-        // The head's input act(h) in bf16, as the forward's head GEMM read it.
-        float gin[8];
+        // The head's input act(h) in bf16, as the forward's head GEMM read it, and
+        // act'(h), from one sigmoid per element for SiLU.
+        float gin[8], slope[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) gin[e] = act_value(hh[e], act);
+        for (int e = 0; e < 8; ++e) {
+          if (act == kActSilu) {
+            const float sg = __fdividef(1.0f, 1.0f + __expf(-hh[e]));
+            gin[e] = hh[e] * sg;
+            slope[e] = sg * (1.0f + hh[e] * (1.0f - sg));
+          } else {
+            gin[e] = act_value(hh[e], act);
+            slope[e] = act_slope(hh[e], act);
+          }
+        }
         bf16x8(pack8(gin), gin);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          g[e] = d * wf[e] * act_slope(hh[e], act);
+          g[e] = d * wf[e] * slope[e];
           sw[e] += d * gin[e];
         }
         const uint4 packed = pack8(g);

@@ -505,10 +505,11 @@ class CugoB200Extension:
                                     "colsum")
 
     def _scratch_floats(self, need: int, device: torch.device, kind: str) -> torch.Tensor:
-        """An fp32 scratch buffer per device and kind of op (launches of one kind are
-        ordered on the stream), grown as needed."""
+        """An fp32 scratch buffer per device, stream and kind of op (launches of one
+        kind on one stream are ordered; two streams never share one), grown as
+        needed."""
         cache = self.__dict__.setdefault("_scratch", {})
-        key = (device, kind)
+        key = (device, kind, torch.cuda.current_stream(device).cuda_stream)
         buf = cache.get(key)
         if buf is None or buf.numel() < need:
             buf = torch.empty(max(need, 1), dtype=torch.float32, device=device)

@@ -731,6 +731,10 @@ class NativePpoStep(PpoStep):
         # Each network's gradients live in one flat buffer, the bucket of its all-reduce.
         self.flat = {"actor": flat_gradients(list(actor.parameters())),
                      "critic": flat_gradients(list(critic.parameters()))} if world > 1 else {}
+        # On one GPU the critic's forward and backward run on a second stream beside
+        # the actor's: the two networks are independent up to the loss, and the
+        # kernels of one fill the SMs the other's tail waves and small launches leave.
+        self.side = torch.cuda.Stream(self.sums.device) if world == 1 and self.sums.is_cuda else None
 
     @staticmethod
     def supports(actor: nn.Module, critic: nn.Module) -> bool:
@@ -741,24 +745,42 @@ class NativePpoStep(PpoStep):
 
     def step(self, mb: Minibatch) -> None:
         ext = self.actor.ext
-        logits, a_saved = train_forward(self.actor, mb.features)
         stock = mb.stock if getattr(self.critic, "stock", False) else None
-        value, c_saved = train_forward(self.critic, critic_input(mb.features, mb.opp_hand, stock))
+        main, side = torch.cuda.current_stream(), self.side
+        if side is not None:  # the critic's forward beside the actor's
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                value, c_saved = train_forward(self.critic,
+                                               critic_input(mb.features, mb.opp_hand, stock))
+            logits, a_saved = train_forward(self.actor, mb.features)
+            main.wait_stream(side)
+            value.record_stream(main)
+        else:
+            logits, a_saved = train_forward(self.actor, mb.features)
+            value, c_saved = train_forward(self.critic, critic_input(mb.features, mb.opp_hand, stock))
         b = logits.shape[0]
         dy = torch.empty((b, _pad8(ACTIONS)), dtype=torch.bfloat16, device=logits.device)
         dv = torch.empty(b, dtype=torch.float32, device=logits.device)
         ext.ppo_loss(logits, mb.legal, mb.actions, mb.logp_old, mb.adv, value, mb.ret, self.clip,
                      self.entropy_coef, self.value_coef, dy, dv, self.stats)
-        # Data parallel: the critic's gradients are all-reduced while the actor's
-        # backward runs (two buckets, the same collective order on every rank).
-        train_backward(self.critic, c_saved, dv=dv)
-        critic_bucket = start_allreduce(list(self.critic.parameters()), self.world,
-                                        self.flat.get("critic"))
-        train_backward(self.actor, a_saved, dy=dy)
-        actor_bucket = start_allreduce(list(self.actor.parameters()), self.world,
-                                       self.flat.get("actor"))
-        finish_allreduce(critic_bucket)
-        finish_allreduce(actor_bucket)
+        if side is not None:  # the two backwards side by side
+            side.wait_stream(main)
+            dv.record_stream(side)
+            with torch.cuda.stream(side):
+                train_backward(self.critic, c_saved, dv=dv)
+            train_backward(self.actor, a_saved, dy=dy)
+            main.wait_stream(side)
+        else:
+            # Data parallel: the critic's gradients are all-reduced while the actor's
+            # backward runs (two buckets, the same collective order on every rank).
+            train_backward(self.critic, c_saved, dv=dv)
+            critic_bucket = start_allreduce(list(self.critic.parameters()), self.world,
+                                            self.flat.get("critic"))
+            train_backward(self.actor, a_saved, dy=dy)
+            actor_bucket = start_allreduce(list(self.actor.parameters()), self.world,
+                                           self.flat.get("actor"))
+            finish_allreduce(critic_bucket)
+            finish_allreduce(actor_bucket)
         for group in self.groups:
             nn.utils.clip_grad_norm_(group, self.grad_clip, foreach=True)
         self.optimizer.step()
