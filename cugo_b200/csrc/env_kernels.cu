@@ -117,9 +117,19 @@ struct RoundTail {
   float* reward0;
   bool* nagari;
   i64* bad;
-  uint32_t* keep;        // [ceil(m / 32)]
+  uint32_t* keep;        // [groups][stride]: per group and warp, the ballot of its rows
   const int32_t* m_dev;  // optional device-resident row count (at most m)
+  int groups;            // 1: the running rows in order; 3: grouped by their next decision
+  i64 stride;            // ceil(m / 32)
 };
+
+// Group of a running game's next decision for grouped compaction: 0 a primary play,
+// 1 a pending floor choice, 2 a prompt (Go/Stop, Gukjin, Chongtong).  A warp of one
+// group runs one branch of the rule code in the next round.
+__device__ __forceinline__ int next_decision_group(const Game& g) {
+  if (g.pend_active()) return 1;
+  return decision_kind(g) == kDecPrimary ? 0 : 2;
+}
 
 __device__ __forceinline__ i64 device_rows(const int32_t* m_dev, i64 m) {
   if (!m_dev) return m;
@@ -169,9 +179,19 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
       const u32 st = static_cast<u32>(out.status);
       if (st != kOk && st != kFinished) atomicAdd(reinterpret_cast<unsigned long long*>(tail.bad), 1ull);
     }
-    const unsigned mask = __ballot_sync(kFull, src >= 0 && !fin);
+    const bool running = src >= 0 && !fin;
     const i64 w = ((i64)blockIdx.x * kBlock + (threadIdx.x & ~31)) >> 5;
-    if ((threadIdx.x & 31) == 0 && w * 32 < m) tail.keep[w] = mask;
+    if (tail.groups == 1) {
+      const unsigned mask = __ballot_sync(kFull, running);
+      if ((threadIdx.x & 31) == 0 && w * 32 < m) tail.keep[w] = mask;
+    } else {
+      const int grp = running ? next_decision_group(g) : -1;
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const unsigned mask = __ballot_sync(kFull, grp == q);
+        if ((threadIdx.x & 31) == 0 && w * 32 < m) tail.keep[q * tail.stride + w] = mask;
+      }
+    }
   }
   if (row < m && reward) {  // internal callers may skip the per-row outputs
     reward[row] = static_cast<float>(out.reward0);
@@ -366,57 +386,71 @@ __global__ void __launch_bounds__(32 * kBranchWarps, CB_BRANCH_MIN_BLOCKS) branc
   }
 }
 
-// Exclusive prefix over the warps' running counts (one block): offsets[w], and
-// the total in *count.
+// Exclusive prefix over the warps' running counts (one block): offsets[q][w] for
+// each group q in turn (group q's rows follow every row of groups < q), and the
+// total in *count.
 __global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __restrict__ keep,
                                                             i64 m, const int32_t* __restrict__ m_dev,
                                                             int32_t* __restrict__ offsets,
-                                                            int32_t* __restrict__ count) {
+                                                            int32_t* __restrict__ count, int groups,
+                                                            i64 stride) {
   __shared__ int32_t sums[32];
   const i64 warps = (device_rows(m_dev, m) + 31) / 32;
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const i64 per = (warps + blockDim.x - 1) / blockDim.x;  // consecutive warps per thread
   const i64 w0 = t * per;
-  int32_t mine = 0;
-  for (i64 w = w0; w < w0 + per && w < warps; ++w) mine += __popc(__ldg(keep + w));
-  int32_t incl = mine;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int32_t v = __shfl_up_sync(kFull, incl, o);
-    if (lane >= o) incl += v;
-  }
-  if (lane == 31) sums[wid] = incl;
-  __syncthreads();
-  if (wid == 0) {
-    int32_t v = lane < (int)(blockDim.x >> 5) ? sums[lane] : 0;
+  int32_t base = 0;
+  for (int q = 0; q < groups; ++q) {
+    const uint32_t* kq = keep + q * stride;
+    int32_t mine = 0;
+    for (i64 w = w0; w < w0 + per && w < warps; ++w) mine += __popc(__ldg(kq + w));
+    int32_t incl = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int32_t u = __shfl_up_sync(kFull, v, o);
-      if (lane >= o) v += u;
+      const int32_t v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
     }
-    sums[lane] = v;  // inclusive over warps 0..lane
+    __syncthreads();  // the previous group's readers of sums are done
+    if (lane == 31) sums[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      int32_t v = lane < (int)(blockDim.x >> 5) ? sums[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t u = __shfl_up_sync(kFull, v, o);
+        if (lane >= o) v += u;
+      }
+      sums[lane] = v;  // inclusive over warps 0..lane
+    }
+    __syncthreads();
+    int32_t run = base + incl - mine + (wid > 0 ? sums[wid - 1] : 0);
+    for (i64 w = w0; w < w0 + per && w < warps; ++w) {
+      offsets[q * stride + w] = run;
+      run += __popc(__ldg(kq + w));
+    }
+    base += sums[31];
   }
-  __syncthreads();
-  int32_t run = incl - mine + (wid > 0 ? sums[wid - 1] : 0);
-  for (i64 w = w0; w < w0 + per && w < warps; ++w) {
-    offsets[w] = run;
-    run += __popc(__ldg(keep + w));
-  }
-  if (t == blockDim.x - 1) *count = run;
+  if (t == 0) *count = base;
 }
 
-// next_ids[offsets[w] + rank of the row among its warp's running rows] = ids[row].
+// next_ids[offsets[q][w] + rank of the row among its warp's rows of group q] = ids[row].
 __global__ void __launch_bounds__(256) compact_scatter_kernel(const uint32_t* __restrict__ keep,
                                                               const int32_t* __restrict__ offsets,
                                                               const i64* __restrict__ ids, i64 m,
                                                               const int32_t* __restrict__ m_dev,
-                                                              i64* __restrict__ next_ids) {
+                                                              i64* __restrict__ next_ids, int groups,
+                                                              i64 stride) {
   const i64 row = (i64)blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= device_rows(m_dev, m)) return;
-  const uint32_t mask = __ldg(keep + (row >> 5));
   const int lane = static_cast<int>(row & 31);
-  if ((mask >> lane) & 1u)
-    next_ids[__ldg(offsets + (row >> 5)) + __popc(mask & ((1u << lane) - 1u))] = __ldg(ids + row);
+  for (int q = 0; q < groups; ++q) {
+    const uint32_t mask = __ldg(keep + q * stride + (row >> 5));
+    if ((mask >> lane) & 1u) {
+      next_ids[__ldg(offsets + q * stride + (row >> 5)) + __popc(mask & ((1u << lane) - 1u))] =
+          __ldg(ids + row);
+      return;
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kBlock) clone_kernel(const u64* __restrict__ states, i64 n_states,
@@ -643,10 +677,11 @@ int cugo_b200_step_indexed(uint8_t* states, int64_t n_states, const int64_t* env
                      committed, nullptr, stream);
 }
 
-int cugo_b200_step_compact(uint8_t* states, int64_t n_states, const int64_t* env_ids,
-                           const int64_t* actions, int64_t m, int32_t* decision, float* reward0,
-                           bool* nagari, int64_t* bad, int64_t* next_ids, int32_t* next_count,
-                           int32_t* scratch, const int32_t* m_dev, cudaStream_t stream) {
+static int step_compact_common(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                               const int64_t* actions, int64_t m, int32_t* decision,
+                               float* reward0, bool* nagari, int64_t* bad, int64_t* next_ids,
+                               int32_t* next_count, int32_t* scratch, const int32_t* m_dev,
+                               int groups, cudaStream_t stream) {
   if (n_states < 0 || m < 0) return CUGO_B200_ERR_ARG;
   if (m > 0 && (!env_ids || !actions || !decision || !reward0 || !nagari || !bad || !next_ids ||
                 !next_count || !scratch))
@@ -659,16 +694,33 @@ int cugo_b200_step_compact(uint8_t* states, int64_t n_states, const int64_t* env
   }
   const i64 warps = (m + 31) / 32;  // capacity; the kernels use the device count
   uint32_t* keep = reinterpret_cast<uint32_t*>(scratch);
-  int32_t* offsets = scratch + warps;
+  int32_t* offsets = scratch + groups * warps;
   if (m_dev == next_count) return CUGO_B200_ERR_ARG;  // the count is rewritten mid-call
-  RoundTail tail{decision, reward0, nagari, bad, keep, m_dev};
+  RoundTail tail{decision, reward0, nagari, bad, keep, m_dev, groups, warps};
   step_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<u64*>(states), n_states, env_ids, actions, m, nullptr, nullptr, nullptr,
       nullptr, nullptr, nullptr, nullptr, tail);
-  compact_scan_kernel<<<1, 1024, 0, stream>>>(keep, m, m_dev, offsets, next_count);
+  compact_scan_kernel<<<1, 1024, 0, stream>>>(keep, m, m_dev, offsets, next_count, groups, warps);
   compact_scatter_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, stream>>>(
-      keep, offsets, env_ids, m, m_dev, next_ids);
+      keep, offsets, env_ids, m, m_dev, next_ids, groups, warps);
   return launch_status();
+}
+
+int cugo_b200_step_compact(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                           const int64_t* actions, int64_t m, int32_t* decision, float* reward0,
+                           bool* nagari, int64_t* bad, int64_t* next_ids, int32_t* next_count,
+                           int32_t* scratch, const int32_t* m_dev, cudaStream_t stream) {
+  return step_compact_common(states, n_states, env_ids, actions, m, decision, reward0, nagari, bad,
+                             next_ids, next_count, scratch, m_dev, 1, stream);
+}
+
+int cugo_b200_step_compact_grouped(uint8_t* states, int64_t n_states, const int64_t* env_ids,
+                                   const int64_t* actions, int64_t m, int32_t* decision,
+                                   float* reward0, bool* nagari, int64_t* bad, int64_t* next_ids,
+                                   int32_t* next_count, int32_t* scratch, const int32_t* m_dev,
+                                   cudaStream_t stream) {
+  return step_compact_common(states, n_states, env_ids, actions, m, decision, reward0, nagari, bad,
+                             next_ids, next_count, scratch, m_dev, 3, stream);
 }
 
 int cugo_b200_step_events_indexed(uint8_t* states, int64_t n_states, const int64_t* env_ids,

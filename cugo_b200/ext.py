@@ -65,6 +65,8 @@ _SIGNATURES: dict[str, list] = {
                                             _VP],
     "cugo_b200_step_compact": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
                                _VP, _VP],
+    "cugo_b200_step_compact_grouped": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP,
+                                       _VP, _VP, _VP],
     "cugo_b200_rowdot_bf16": [_VP, _I64, _VP, _VP, _I64, _I64, _VP, _I64, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
@@ -432,22 +434,25 @@ class CugoB200Extension:
 
     def step_compact(self, states, env_ids, actions, decision, reward0, nagari, bad, next_ids,
                      next_count, scratch: torch.Tensor | None = None,
-                     m_dev: torch.Tensor | None = None) -> None:
+                     m_dev: torch.Tensor | None = None, grouped: bool = False) -> None:
         """step_indexed plus a self-play round's bookkeeping (see the C declaration):
         decision int32, reward0 fp32, nagari bool indexed by game id; bad int64 [1];
         next_ids int64 [>= m] and next_count int32 [1] receive the games still running,
-        in order; scratch int32 [>= 2 * ceil(m / 32)] (allocated when not given)."""
+        in order, or with `grouped` grouped by their next decision (primary plays,
+        floor choices, prompts); scratch int32 [>= 2 (grouped: 6) * ceil(m / 32)]
+        (allocated when not given)."""
         self._indexed_args(states, env_ids, actions)
         m = env_ids.numel()
         if next_ids.numel() < m or next_ids.dtype != torch.int64 or next_count.dtype != torch.int32:
             raise RuntimeError("step_compact: next_ids int64 [>= m], next_count int32 [1]")
-        need = 2 * ((m + 31) // 32)
+        need = (6 if grouped else 2) * ((m + 31) // 32)
         if scratch is None:
             scratch = torch.empty(max(need, 1), dtype=torch.int32, device=states.device)
         if scratch.dtype != torch.int32 or scratch.numel() < need:
-            raise RuntimeError("step_compact: scratch int32 [>= 2 * ceil(m / 32)]")
+            raise RuntimeError(f"step_compact: scratch int32 [>= {need}]")
+        fn = self._lib.cugo_b200_step_compact_grouped if grouped else self._lib.cugo_b200_step_compact
         with torch.cuda.device(states.device):
-            _check(self._lib.cugo_b200_step_compact(
+            _check(fn(
                 _ptr(states), states.size(0), _ptr(env_ids), _ptr(actions), m, _ptr(decision),
                 _ptr(reward0), _ptr(nagari), _ptr(bad), _ptr(next_ids), _ptr(next_count),
                 _ptr(scratch), _ptr(m_dev), self._stream(states.device)), "step_compact")

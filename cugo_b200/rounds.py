@@ -31,7 +31,7 @@ class RunningSet:
     stable sort puts the running rows first and their number is the count."""
 
     def __init__(self, ext, states: torch.Tensor, running: torch.Tensor | None = None,
-                 check_every: int = 4, lookahead: int = 2) -> None:
+                 check_every: int = 4, lookahead: int = 2, grouped: bool = False) -> None:
         dev = states.device
         g = states.shape[0]
         self.ext, self.states, self.g = ext, states, g
@@ -48,7 +48,12 @@ class RunningSet:
         self.reward0 = torch.zeros(g, dtype=torch.float32, device=dev)
         self.nagari = torch.zeros(g, dtype=torch.bool, device=dev)
         self.bad = torch.zeros(1, **i64)
-        self.scratch = torch.empty(max(1, 2 * ((g + 31) // 32)), dtype=torch.int32, device=dev)
+        # grouped: each round's list is grouped by the games' next decision (primary
+        # plays, floor choices, prompts) instead of kept in row order, so a warp of
+        # the next round runs one branch of the rule code (1.3-1.7x faster steps).
+        self.grouped = grouped
+        self.scratch = torch.empty(max(1, (6 if grouped else 2) * ((g + 31) // 32)),
+                                   dtype=torch.int32, device=dev)
         self.rounds = 0
         self.bound = g  # the host's upper bound of the running count
         self.check_every, self.lookahead = check_every, lookahead
@@ -81,7 +86,8 @@ class RunningSet:
         active = self.ids[k] if device_count else self.ids[k][:self.bound]
         self.ext.step_compact(self.states, active, actions, self.decision, self.reward0,
                               self.nagari, self.bad, self.ids[1 - k], self.counts[1 - k:2 - k],
-                              self.scratch, m_dev=self.counts[k:k + 1] if device_count else None)
+                              self.scratch, m_dev=self.counts[k:k + 1] if device_count else None,
+                              grouped=self.grouped)
         self.rounds += 1
 
     def read_count(self) -> int:

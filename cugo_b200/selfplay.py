@@ -90,7 +90,7 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     writes of positions past the running count)."""
     g = game_index.numel()
     states = ext.create(game_index + seed_base, game_index & 1)
-    run = RunningSet(ext, states, check_every=CHECK_EVERY)
+    run = RunningSet(ext, states, check_every=CHECK_EVERY, grouped=True)
     fused = getattr(policy, "samples_in_kernel", lambda: False)()
     # The policy timer needs each round's row count: it reads the count every round.
     device_count = fused and timer is None

@@ -104,6 +104,19 @@ CUGO_B200_API int cugo_b200_step_compact(uint8_t* states, int64_t n_states,
                                          int32_t* next_count, int32_t* scratch,
                                          const int32_t* m_dev, cudaStream_t stream);
 
+/* cugo_b200_step_compact with next_ids grouped by each running game's next
+ * decision: the games about to make a primary play first, then those with a
+ * pending floor choice, then those answering a prompt (Go/Stop, Gukjin,
+ * Chongtong), each group in env_ids order.  A round that steps the groups in this
+ * order runs one branch of the rule code per warp almost everywhere.  scratch:
+ * int32 [6 * ceil(m / 32)].  No reference counterpart (as cugo_b200_step_compact). */
+CUGO_B200_API int cugo_b200_step_compact_grouped(uint8_t* states, int64_t n_states,
+                                                 const int64_t* env_ids, const int64_t* actions,
+                                                 int64_t m, int32_t* decision, float* reward0,
+                                                 bool* nagari, int64_t* bad, int64_t* next_ids,
+                                                 int32_t* next_count, int32_t* scratch,
+                                                 const int32_t* m_dev, cudaStream_t stream);
+
 /* step_events_indexed (torch50_ext.cu:626-660): step_indexed plus the committed
  * action's event record, int64 [m, 9] (zero when nothing was committed). */
 CUGO_B200_API int cugo_b200_step_events_indexed(uint8_t* states, int64_t n_states, const int64_t* env_ids,

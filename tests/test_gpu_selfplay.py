@@ -52,6 +52,49 @@ def test_step_compact_matches_step_indexed(ext):
     assert bool(done.any()) and bool((status == 9).any())
 
 
+def test_step_compact_grouped_orders_by_next_decision(ext):
+    """The grouped round tail writes the same running games as the in-order one,
+    grouped by their next decision -- primary plays, then pending floor choices,
+    then prompts (Go/Stop, Gukjin, Chongtong) -- each group in env_ids order, with the
+    same rows, decision counters, rewards, nagari flags and bad count."""
+    n = 20000
+    idx = torch.arange(n, device=DEV, dtype=torch.int64)
+    states = ext.create(idx + 777, idx & 1)
+    g = torch.Generator().manual_seed(21)
+    for _ in range(10):
+        _, legal, _, _, _ = ext.observe_indexed(states, idx)
+        logits = torch.randn((n, 180), generator=g).to(DEV)
+        acts, _ = ext.sample_actions(logits, legal, idx, torch.zeros(n, dtype=torch.int32, device=DEV))
+        ext.step_indexed(states, idx, acts.clamp_min(0))
+    ids = torch.randperm(n, generator=g)[:15000].to(DEV)
+    _, legal, _, _, _ = ext.observe_indexed(states, ids)
+    logits = torch.randn((ids.numel(), 180), generator=g).to(DEV)
+    acts, _ = ext.sample_actions(logits, legal, ids, torch.zeros(ids.numel(), dtype=torch.int32, device=DEV))
+    outs = []
+    for grouped in (False, True):
+        st = states.clone()
+        decision = torch.zeros(n, dtype=torch.int32, device=DEV)
+        reward0, nag = torch.zeros(n, device=DEV), torch.zeros(n, dtype=torch.bool, device=DEV)
+        bad = torch.zeros(1, dtype=torch.int64, device=DEV)
+        nxt = torch.full((n,), -7, dtype=torch.int64, device=DEV)
+        count = torch.zeros(1, dtype=torch.int32, device=DEV)
+        ext.step_compact(st, ids, acts, decision, reward0, nag, bad, nxt, count, grouped=grouped)
+        outs.append((st, decision, reward0, nag, bad, nxt[:int(count)].clone()))
+    (s0, d0, r0, n0, b0, order), (s1, d1, r1, n1, b1, grouped_ids) = outs
+    for a, b in ((s0, s1), (d0, d1), (r0, r1), (n0, n1), (b0, b1)):
+        assert torch.equal(a, b)
+    # The next decision of each running game, from its legal actions: a floor choice
+    # offers actions 127..176 only, a prompt 123..126 (Go/Stop, Chongtong) or 177..178
+    # (Gukjin) only, a primary play actions below 123 (or none).
+    _, legal, _, _, _ = ext.observe_indexed(s1, order)
+    choice = legal[:, 127:177].any(1)
+    prompt = legal[:, 123:127].any(1) | legal[:, 177:179].any(1)
+    group = torch.where(choice, 1, torch.where(prompt, 2, 0))
+    expect = torch.cat([order[group == q] for q in range(3)])
+    assert int(count) > 0 and bool((group == 1).any()) and bool((group == 2).any())
+    assert torch.equal(grouped_ids, expect)
+
+
 def _reference_loop(ext, policy, game_index, seed_base=12345, max_rounds=128):
     """The collection loop with separate ops and torch bookkeeping; games that the
     deal ended take no decision (reward 0)."""
