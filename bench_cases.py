@@ -11,6 +11,8 @@ bytes or FLOPs of one launch:
   gemm      M N K MODE one tcgen05 GEMM layer (MODE plain | silu | residual | pre: the
                        training forward's SiLU layer keeping its pre-activation), 2MNK
   wgrad     R O I      the weight gradient dW = dY^T X over R rows (split-K), 2ROI
+  seqwave   [WAVE]     config 4: one wave of sequence-policy self-play (graphed decision
+                       steps) under torch.profiler; kernel time per step by kernel
   mlpsample M H B      the self-play policy step: forward and masked Gumbel-max sampling
                        (one fused launch at H = 512), flops_per_row * M
   observe   ROWS       observe_indexed, 3,319 B per row
@@ -70,6 +72,42 @@ def _mid_game(ext, rows: int, decisions: int = 6):
     for _ in range(decisions):
         ext.selfplay_random_step(states, game, dec, done, steps, feats, legal)
     return states, feats, legal
+
+
+def seqwave_case(wave: int) -> dict:
+    """One wave of config 4 (SeqWaveSelfPlay, one CUDA graph per decision step) after a
+    capture wave, its kernels listed by torch.profiler: device time per decision step
+    by kernel, largest first, with each kernel's share."""
+    from torch.profiler import ProfilerActivity, profile
+
+    from cugo_b200.seq import SeqDecoder
+    from cugo_b200.seq_selfplay import SeqWaveSelfPlay
+    sp = SeqWaveSelfPlay(SeqDecoder.from_state_dict(SeqDecoder.random_state(0)), wave=wave)
+    sp.play_wave(0)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    steps = sp.play_wave(wave)
+    b.record()
+    torch.cuda.synchronize()
+    wave_s = a.elapsed_time(b) / 1e3
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        steps_p = sp.play_wave(2 * wave)
+        torch.cuda.synchronize()
+    sp.release()
+    per = {}
+    for ev in prof.key_averages():
+        t = getattr(ev, "self_device_time_total", None)
+        t = ev.self_cuda_time_total if t is None else t
+        if t > 0:
+            per[ev.key] = per.get(ev.key, 0.0) + t
+    total = sum(per.values())
+    top = sorted(per.items(), key=lambda kv: -kv[1])
+    return {"wave": wave, "steps": steps, "wave_seconds": wave_s, "ms_per_step": wave_s * 1e3 / steps,
+            "games_per_s": wave / wave_s, "profiled_steps": steps_p,
+            "kernel_us_per_step": round(total / steps_p, 1),
+            "kernels": [{"name": k[:90], "us_per_step": round(v / steps_p, 2),
+                         "share": round(v / total, 4)} for k, v in top[:25]]}
 
 
 def ppo_case(b: int, warmup: int = 3, iters: int = 10) -> dict:
@@ -412,6 +450,8 @@ def main() -> None:
         dw = torch.empty((o, i), dtype=torch.float32, device=dev)
         sec = _time(lambda: ext.wgrad_bf16(dy, x, dw), args.warmup, args.iters)
         out.update(seconds=sec, tflops=2 * r * o * i / sec / 1e12)
+    elif args.case == "seqwave":
+        out.update(seqwave_case(d[0] if d else 4096))
     elif args.case == "mlpsample":  # the self-play policy step: MLP + sampling head
         m, h, blocks = d
         pol = ResidualMlpPolicy(h, blocks, "relu", device=dev)
