@@ -1,7 +1,9 @@
 """Incremental inference of the event-sequence policy on the native kernels.
 
 `SeqDecoder` runs the decode half of the reference's ``SeqNet``
-(python/cugo_seq50.py:131-339) in "hybrid" mode: opening, event and query tokens
+(python/cugo_seq50.py:131-339), query mode "hybrid" or "events" (the events query reads
+the context columns only: its first layer's weight is zero on the other features), with
+opening, event and query tokens
 and ``cached_step`` — one new token per cache row through the pre-LN transformer
 layers with the token's key/value appended to the row's KV cache — and the
 ``readout`` head.  Per layer:
@@ -33,6 +35,13 @@ MAX_EVENTS = 48  # python/cugo_seq50.py:34
 FEATURES = 720
 ACTIONS = 179
 QUERY_IN = FEATURES + ACTIONS  # hybrid query input (python/cugo_seq50.py:152-153)
+# Feature columns the "events" query reads (python/cugo_contract50.py:34-36, contract
+# v4): the decision context of contract v3, then the own hand, the table counts and
+# the round multiplier.  The column list is the feature contract checkpoints are
+# trained on, so it is the reference's.
+EVENTS_CONTEXT = [*range(200, 250), *range(396, 453), *range(471, 476), 552,
+                  *range(0, 50), *range(491, 496), 557, 710, 711]
+EVENTS_QUERY_IN = len(EVENTS_CONTEXT) + ACTIONS
 QUERY_LD = 904                 # query rows padded to a multiple of 16 bytes
 ACT_GELU = 3
 
@@ -118,11 +127,23 @@ class SeqDecoder:
         self.event_b = fp32(p["event_in.bias"])
         self.start_wt = bf16(p["start_in.weight"].t())   # [274, d]
         self.start_b = fp32(p["start_in.bias"])
-        q0 = p["query_in.0.weight"]
-        if q0.shape[1] != QUERY_IN:
-            raise ValueError("only the hybrid query (720 features + 179 legal) is supported")
+        q0 = p["query_in.0.weight"].detach().float().cpu()
         w = torch.zeros((q0.shape[0], QUERY_LD), dtype=torch.float32)
-        w[:, :QUERY_IN] = q0.detach().float().cpu()
+        if q0.shape[1] == QUERY_IN:  # "hybrid": every feature and the legal actions
+            self.mode = "hybrid"
+            w[:, :QUERY_IN] = q0
+        elif q0.shape[1] == EVENTS_QUERY_IN:
+            # "events": the context columns and the legal actions.  The query input
+            # keeps the hybrid layout (observe_query_bf16 writes all 720 features);
+            # the other feature columns get zero weights, so the layer is the
+            # reference's product over the selected columns.
+            self.mode = "events"
+            ctx = len(EVENTS_CONTEXT)
+            w[:, EVENTS_CONTEXT] = q0[:, :ctx]
+            w[:, FEATURES:QUERY_IN] = q0[:, ctx:]
+        else:
+            raise ValueError("query_in.0 must read the hybrid (720 + 179) or events "
+                             f"({len(EVENTS_CONTEXT)} + 179) query")
         self.q_w0 = bf16(w)
         self.q_b0 = fp32(p["query_in.0.bias"])
         self.q_w1 = bf16(p["query_in.2.weight"])
@@ -149,13 +170,14 @@ class SeqDecoder:
     @classmethod
     def from_state_dict(cls, state: dict[str, torch.Tensor], heads: int = 8,
                         device: torch.device | str = "cuda") -> "SeqDecoder":
-        """Loads a reference SeqNet(mode="hybrid") state dict (weights rounded to bf16)."""
+        """Loads a reference SeqNet state dict, mode "hybrid" or "events" (weights
+        rounded to bf16)."""
         layers = len({k.split(".")[2] for k in state if k.startswith("encoder.layers.")})
         return cls(state, layers, heads, device)
 
     @staticmethod
     def random_state(seed: int = 0, d_model: int = 256, layers: int = 4, ffn: int = 1024,
-                     outputs: int = ACTIONS) -> dict[str, torch.Tensor]:
+                     outputs: int = ACTIONS, mode: str = "hybrid") -> dict[str, torch.Tensor]:
         """A SeqNet-shaped state dict drawn from torch.manual_seed(seed): nn.Linear's
         default U(-1/sqrt(in), 1/sqrt(in)) weights and biases, N(0, 0.02) position and
         token-type tables, LayerNorm weight 1 and bias 0 (python/cugo_seq50.py:154-166)."""
@@ -170,7 +192,7 @@ class SeqDecoder:
         st: dict[str, torch.Tensor] = {}
         st.update(lin("event_in", d, 8 * 50 + 12 + 2))
         st.update(lin("start_in", d, 5 * 50 + 12 + 8 + 4))
-        st.update(lin("query_in.0", 2 * d, QUERY_IN))
+        st.update(lin("query_in.0", 2 * d, QUERY_IN if mode == "hybrid" else EVENTS_QUERY_IN))
         st.update(lin("query_in.2", d, 2 * d))
         st["position"] = torch.randn((MAX_EVENTS + 1, d), generator=g) * 0.02
         st["token_type"] = torch.randn((3, d), generator=g) * 0.02

@@ -18,6 +18,9 @@ and the reference's outputs with weights SeqDecoder.random_state(seed=11):
   start_tok, event_tok0   start_token and the first event_token, fp32
   att_out          decode_attention(use_triton=False) in fp32 on
                    tests/seq_reference.attention_case(seed=3, n=48, n_rows=64)
+  logits_events_full, logits_events_autocast
+                   SeqNet("events").forward in fp32 and under bf16 autocast (CPU) with
+                   the weights SeqDecoder.random_state(seed=11, mode="events")
 """
 from __future__ import annotations
 
@@ -110,12 +113,19 @@ def main() -> None:
         logits_inc = model.readout(h)
         aq, ak, av, apos, arows = attention_case(seed=3, n=48, n_rows=64)
         att_out = decode_attention(aq, ak, av, apos, use_triton=False, rows=arows)
+        events_model = SeqNet("events", 179).eval()
+        events_model.load_state_dict(SeqDecoder.random_state(seed=WEIGHT_SEED, mode="events"),
+                                     strict=True)
+        logits_events_full = events_model(feats, t["legal"], hist)
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            logits_events_autocast = events_model(feats, t["legal"], hist).float()
     out = HERE / "seq_decode.npz"
     np.savez_compressed(out, games=games, start=start, events=events, count=count, seat=seat,
                         features=feats.numpy(), legal=legal, logits_full=logits_full.numpy(),
                         logits_autocast=logits_autocast.numpy(), logits_inc=logits_inc.numpy(),
                         start_tok=start_tok.numpy(), event_tok0=event_tok0.numpy(),
-                        att_out=att_out.numpy())
+                        att_out=att_out.numpy(), logits_events_full=logits_events_full.numpy(),
+                        logits_events_autocast=logits_events_autocast.numpy())
     d = (logits_inc - logits_full).abs().max().item()
     print(out.name, out.stat().st_size, "events max", int(count.max()), "inc-vs-full", d)
 

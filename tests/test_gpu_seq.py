@@ -237,6 +237,24 @@ def test_decoder_matches_reference_seqnet(golden):
     assert torch.equal(logits.argmax(1)[clear], full.argmax(1)[clear])
 
 
+def test_events_query_decoder_matches_reference_seqnet(golden):
+    """SeqNet in "events" mode (the query reads the context columns and the legal
+    actions only): the same bar as the hybrid decoder against the reference's own
+    fp32 forward (golden made by importing the reference's SeqNet)."""
+    from cugo_b200.seq import SeqDecoder
+    g = golden("seq_decode")
+    dec = SeqDecoder.from_state_dict(SeqDecoder.random_state(seed=11, mode="events"), device=DEV)
+    assert dec.mode == "events"
+    logits = _run_decoder(dec, _inputs(g))
+    torch.cuda.synchronize()
+    full = torch.from_numpy(g["logits_events_full"]).to(DEV)
+    auto = torch.from_numpy(g["logits_events_autocast"]).to(DEV)
+    err = (logits - full).abs().max().item()
+    err_ref = (auto - full).abs().max().item()
+    assert err <= 1.5 * err_ref + 1e-4, (err, err_ref)
+    assert err <= 2e-2 * full.abs().max().item()
+
+
 def test_decoder_cuda_graph_replay_matches_eager(golden):
     t = _inputs(golden("seq_decode"))
     dec = _decoder()
