@@ -1497,10 +1497,13 @@ namespace {
 //                  columns), rewritten in place layer after layer; during the input
 //                  layer its chunks hold the x tiles streamed in by TMA, after the
 //                  head it stages the fp32 output for TMA stores;
-//                  a 6-stage ring of weight tiles: each stage is this CTA's half
+//                  a 5-stage ring of weight tiles: each stage is this CTA's half
 //                  (128 rows x 64) of a 256-row tile (16 KB), so each SM streams
 //                  half of every weight tile and the bytes in flight cover twice the
 //                  MMA work a single CTA's would;
+//                  the fp32 biases of the input and hidden layers (up to 8 vectors of
+//                  512), copied in once per launch: the epilogue reads 16 columns'
+//                  biases as four 16-byte broadcasts instead of a load and 16 shuffles;
 //   tensor memory  the fp32 accumulator of a whole layer, 128 lanes x 512 columns;
 //                  the head's (at most 256 columns) in the upper half, so the next
 //                  tile's input-layer MMAs into the lower half overlap the head
@@ -1520,13 +1523,16 @@ constexpr int F_H = 512;
 constexpr int F_CHUNKS = F_H / BK;            // 8
 constexpr int F_CHUNK_BYTES = BM * BK * 2;    // 16 KB
 constexpr int F_ACT_BYTES = F_CHUNKS * F_CHUNK_BYTES;
-constexpr int F_WSTAGES = 6;
+constexpr int F_WSTAGES = 5;
+constexpr int F_BIAS_SLOTS = 8;                        // bias vectors kept in shared memory
+constexpr int F_BIAS_BYTES = F_BIAS_SLOTS * F_H * 4;  // 16 KB
 constexpr int F_W_ROWS = BN / 2;              // weight rows per CTA per stage
 constexpr int F_W_BYTES = F_W_ROWS * BK * 2;  // 16 KB
 constexpr int F_MAX_BLOCKS = 4;
 constexpr int F_MAX_LAYERS = 2 + 2 * F_MAX_BLOCKS;
 constexpr int F_MAX_KIN = 1024;
-constexpr int F_SMEM_BYTES = F_ACT_BYTES + F_WSTAGES * F_W_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+constexpr int F_SMEM_BYTES =
+    F_ACT_BYTES + F_WSTAGES * F_W_BYTES + F_BIAS_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 // Epilogue warps per CTA: F_EPI_WARPS / 4 per TMEM lane quadrant, each draining
 // 512 / (F_EPI_WARPS / 4) columns in 16-column chunks.
 #ifndef CB_FUSED_EPI_WARPS
@@ -1638,6 +1644,22 @@ __device__ __forceinline__ void act_store16(uint8_t* act, int r, int col0, const
   }
 }
 
+// act_store16 of max(v, 0): the ReLU folded into the bf16 conversion (the same bits as
+// rounding max(v, 0)).
+__device__ __forceinline__ void act_store16_relu(uint8_t* act, int r, int col0, const float* v) {
+  const int kc = col0 >> 6, p0 = (col0 & 63) >> 3;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;"
+          : "=r"(w[e])
+          : "f"(v[8 * j + 2 * e + 1]), "f"(v[8 * j + 2 * e]));
+    *reinterpret_cast<uint4*>(act_piece(act, kc, r, p0 + j)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 __device__ __forceinline__ void act_load16(uint8_t* act, int r, int col0, float* v) {
   const int kc = col0 >> 6, p0 = (col0 & 63) >> 3;
 #pragma unroll
@@ -1660,6 +1682,26 @@ __device__ __forceinline__ void fused_bias16(const float* b, int col0, int limit
   const float mine = (b && lane < 16 && col0 + lane < limit) ? __ldg(b + col0 + lane) : 0.0f;
 #pragma unroll
   for (int j = 0; j < 16; ++j) out[j] = __shfl_sync(0xffffffffu, mine, j);
+}
+
+// The 16 biases col0 .. col0 + 15 of layer `layer` (input or hidden, all columns below
+// 512): from the shared-memory copy (every lane reads the same 16 bytes four times),
+// or for a layer past the staged ones from global memory.
+__device__ __forceinline__ void fused_layer_bias16(const float* bias_s, const float* b, int layer,
+                                                   int col0, float* out) {
+  if (layer >= F_BIAS_SLOTS) {
+    fused_bias16(b, col0, F_H, out);
+    return;
+  }
+  const float4* p = reinterpret_cast<const float4*>(bias_s + layer * F_H + col0);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 t = p[q];
+    out[4 * q] = t.x;
+    out[4 * q + 1] = t.y;
+    out[4 * q + 2] = t.z;
+    out[4 * q + 3] = t.w;
+  }
 }
 
 #define CB_TMEM_ST16(taddr, r)                                                                  \
@@ -1688,7 +1730,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* act = smem;
   uint8_t* wring = smem + F_ACT_BYTES;
-  uint64_t* wfull = reinterpret_cast<uint64_t*>(wring + F_WSTAGES * F_W_BYTES);
+  float* bias_s = reinterpret_cast<float*>(wring + F_WSTAGES * F_W_BYTES);  // [F_BIAS_SLOTS][512]
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(wring + F_WSTAGES * F_W_BYTES + F_BIAS_BYTES);
   uint64_t* wempty = wfull + F_WSTAGES;
   uint64_t* xfull = wempty + F_WSTAGES;  // [8]
   uint64_t* xempty = xfull + F_CHUNKS;   // [8]
@@ -1736,6 +1779,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
                      smem_addr(tmem_holder)),
                  "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  // The biases of layers 0 .. min(hidden_layers, F_BIAS_SLOTS - 1) (zeros for none).
+  const int staged = (hidden_layers + 1 < F_BIAS_SLOTS ? hidden_layers + 1 : F_BIAS_SLOTS) * F_H;
+  for (int i = threadIdx.x; i < staged; i += blockDim.x) {
+    const float* b = args.bias[i / F_H];
+    bias_s[i] = b ? __ldg(b + i % F_H) : 0.0f;
   }
   fence_before();
   __syncthreads();
@@ -1945,12 +1994,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
         uint32_t raw[F_CW];
         float v[F_CW];
         CB_TMEM_LD16(tq + static_cast<uint32_t>(col0), raw);
-        fused_bias16(args.bias[0], col0, F_H, v);
+        fused_layer_bias16(bias_s, args.bias[0], 0, col0, v);
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < F_CW; ++j) v[j] += __uint_as_float(raw[j]);
-        if (args.blocks == 0) activate_chunk<F_CW>(v, act_code);
-        act_store16(act, r, col0, v);
+        if (args.blocks == 0 && act_code == kActRelu) {
+          act_store16_relu(act, r, col0, v);
+        } else {
+          if (args.blocks == 0) activate_chunk<F_CW>(v, act_code);
+          act_store16(act, r, col0, v);
+        }
       }
       fused_phase_done(ready0);
       for (int l = 1; l <= hidden_layers && !failed; ++l) {
@@ -1960,6 +2013,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
         }
         const bool fc1 = (l & 1) == 1;
         const bool last = l == hidden_layers;
+        const bool relu_out = act_code == kActRelu && (fc1 || last);  // ReLU in the bf16 pack
         for (int c = 0; c < F_GROUP_COLS / F_CW; ++c) {
           const int col0 = group * F_GROUP_COLS + c * F_CW;
           uint32_t raw[F_CW];
@@ -1968,13 +2022,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
           if (fc1) {
             // u = act(h W1^T + b1) over h in ACT; h + b2 into the accumulator for fc2.
             float b2[F_CW], h[F_CW];
-            fused_bias16(args.bias[l + 1], col0, F_H, b2);
+            fused_layer_bias16(bias_s, args.bias[l + 1], l + 1, col0, b2);
             act_load16(act, r, col0, h);
-            fused_bias16(args.bias[l], col0, F_H, v);
+            fused_layer_bias16(bias_s, args.bias[l], l, col0, v);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < F_CW; ++j) v[j] += __uint_as_float(raw[j]);
-            activate_chunk<F_CW>(v, act_code);
+            if (!relu_out) activate_chunk<F_CW>(v, act_code);
 #pragma unroll
             for (int j = 0; j < F_CW; ++j) raw[j] = __float_as_uint(h[j] + b2[j]);
             CB_TMEM_ST16(tq + static_cast<uint32_t>(col0), raw);
@@ -1982,9 +2036,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < F_CW; ++j) v[j] = __uint_as_float(raw[j]);
-            if (last) activate_chunk<F_CW>(v, act_code);
+            if (last && !relu_out) activate_chunk<F_CW>(v, act_code);
           }
-          act_store16(act, r, col0, v);
+          if (relu_out) act_store16_relu(act, r, col0, v);
+          else act_store16(act, r, col0, v);
         }
         fused_phase_done(ready0);
       }

@@ -29,7 +29,7 @@ def _net(k_in, blocks, n_out, seed):
 @pytest.mark.parametrize("m,k_in,blocks,n_out,act", [
     (1000, 720, 3, 180, "relu"), (129, 720, 3, 179, "silu"), (70000, 720, 3, 180, "relu"),
     (300, 512, 0, 64, "relu"), (1000, 1024, 4, 256, "silu"), (1, 720, 1, 1, "relu"),
-    (4099, 776, 3, 1, "silu"), (257, 8, 2, 16, "relu")])
+    (4099, 776, 3, 1, "silu"), (257, 8, 2, 16, "relu"), (2000, 720, 4, 180, "relu")])
 def test_fused_mlp_matches_fp32(ext, m, k_in, blocks, n_out, act):
     ws, bs = _net(k_in, blocks, n_out, seed=m + k_in)
     g = torch.Generator().manual_seed(1)
@@ -50,6 +50,22 @@ def test_fused_mlp_matches_fp32(ext, m, k_in, blocks, n_out, act):
         top2 = exact.topk(2, dim=1).values
         clear = (top2[:, 0] - top2[:, 1]) > 4 * err
         assert torch.equal(out.argmax(1)[clear], exact.argmax(1)[clear])
+
+
+def test_fused_mlp_without_some_biases(ext):
+    # Layers without a bias read zeros, from the shared-memory copy (layers 0..7) and
+    # from the global path (layer 8 of a four-block network) alike.
+    ws, bs = _net(720, 4, 180, seed=11)
+    keep = [b if i % 3 else None for i, b in enumerate(bs)]
+    zeros = [b if b is not None else torch.zeros(w.shape[0], device=DEV) for b, w in zip(keep, ws)]
+    g = torch.Generator().manual_seed(5)
+    x = torch.rand((3000, 720), generator=g).to(DEV, torch.bfloat16)
+    out = ext.mlp_fused(x, ws, keep, ACT["relu"])
+    ref = ext.mlp_fused(x, ws, zeros, ACT["relu"])
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    exact = mlp_forward_fp32(ws, zeros, x, 4, "relu")
+    assert float((out - exact).abs().max()) <= 1e-2 * max(1.0, float(exact.abs().max()))
 
 
 def test_fused_mlp_is_deterministic_and_respects_strides(ext):
