@@ -35,14 +35,26 @@ using namespace cb::tile;
 
 // ---- kernels -------------------------------------------------------------------
 
+// seeds == nullptr: game i is deal seed_base + index[i] with first player index[i] & 1
+// (the drivers' seeding, without materialising the two arrays).
 __global__ void __launch_bounds__(kBlock) create_kernel(const i64* __restrict__ seeds,
                                                         const i64* __restrict__ first, i64 n,
-                                                        u64* __restrict__ rows) {
+                                                        u64* __restrict__ rows,
+                                                        const i64* __restrict__ index = nullptr,
+                                                        i64 seed_base = 0) {
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   Game g;
-  if (row < n) create_game(g, static_cast<u64>(__ldg(seeds + row)), static_cast<u32>(__ldg(first + row) & 1));
-  else for (int k = 0; k < kRowWords; ++k) g.w[k] = 0;
+  if (row < n) {
+    if (seeds) {
+      create_game(g, static_cast<u64>(__ldg(seeds + row)), static_cast<u32>(__ldg(first + row) & 1));
+    } else {
+      const i64 gi = __ldg(index + row);
+      create_game(g, static_cast<u64>(seed_base + gi), static_cast<u32>(gi & 1));
+    }
+  } else {
+    for (int k = 0; k < kRowWords; ++k) g.w[k] = 0;
+  }
   store_game(t, g);
   scatter_rows(t, rows, row < n ? row : -1);
 }
@@ -59,6 +71,9 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) observe_kernel(
     const i64 md = __ldg(m_dev);
     m = md < 0 ? 0 : (md < m ? md : m);
   }
+  // A grid sized for the batch's capacity: blocks past a device count have nothing
+  // to write (no block-wide barrier below, so they may leave at once).
+  if ((i64)blockIdx.x * kBlock >= m) return;
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
@@ -144,6 +159,7 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
     int16_t* __restrict__ status, bool* __restrict__ committed, i64* __restrict__ events,
     RoundTail tail = RoundTail{}) {
   m = device_rows(tail.m_dev, m);
+  if ((i64)blockIdx.x * kBlock >= m) return;  // past a device count: nothing to write
   WarpTile& t = my_tile();
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
@@ -433,7 +449,8 @@ __global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __re
   if (t == 0) *count = base;
 }
 
-// next_ids[offsets[q][w] + rank of the row among its warp's rows of group q] = ids[row].
+// next_ids[offsets[q][w] + rank of the row among its warp's rows of group q] = ids[row]
+// (the row itself without ids).
 __global__ void __launch_bounds__(256) compact_scatter_kernel(const uint32_t* __restrict__ keep,
                                                               const int32_t* __restrict__ offsets,
                                                               const i64* __restrict__ ids, i64 m,
@@ -447,10 +464,36 @@ __global__ void __launch_bounds__(256) compact_scatter_kernel(const uint32_t* __
     const uint32_t mask = __ldg(keep + q * stride + (row >> 5));
     if ((mask >> lane) & 1u) {
       next_ids[__ldg(offsets + q * stride + (row >> 5)) + __popc(mask & ((1u << lane) - 1u))] =
-          __ldg(ids + row);
+          ids ? __ldg(ids + row) : row;
       return;
     }
   }
+}
+
+// A batch's running set at the deal: per row, zero decision count, reward and nagari,
+// and ids[row] = spare[row] = row (so every entry of both id lists is a valid row);
+// per warp, the ballot of its rows whose game the deal did not end (done byte 0);
+// *bad = 0.  compact_scan_kernel and compact_scatter_kernel then list those rows.
+__global__ void __launch_bounds__(256) running_flags_kernel(const uint8_t* __restrict__ states, i64 n,
+                                                            i64* __restrict__ ids,
+                                                            i64* __restrict__ spare,
+                                                            uint32_t* __restrict__ keep,
+                                                            int32_t* __restrict__ decision,
+                                                            float* __restrict__ reward0,
+                                                            bool* __restrict__ nagari,
+                                                            i64* __restrict__ bad) {
+  const i64 row = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool running = row < n && __ldg(states + row * (kRowWords * 8) + kDoneByte) == 0;
+  const unsigned mask = __ballot_sync(kFull, running);
+  if (row < n) {
+    ids[row] = row;
+    if (spare) spare[row] = row;
+    decision[row] = 0;
+    reward0[row] = 0.0f;
+    nagari[row] = false;
+    if ((threadIdx.x & 31) == 0) keep[row >> 5] = mask;
+  }
+  if (row == 0) *bad = 0;
 }
 
 __global__ void __launch_bounds__(kBlock) clone_kernel(const u64* __restrict__ states, i64 n_states,
@@ -528,6 +571,38 @@ int64_t cugo_b200_choice_action_begin(void) { return kChoiceBegin; }
 int64_t cugo_b200_event_words(void) { return kEventWords; }
 int64_t cugo_b200_start_words(void) { return kStartWords; }
 int64_t cugo_b200_status_ok(void) { return kOk; }
+
+int cugo_b200_create_indexed(const int64_t* index, int64_t seed_base, int64_t n, uint8_t* states,
+                             cudaStream_t stream) {
+  if (n < 0 || (n > 0 && (!index || !states))) return CUGO_B200_ERR_ARG;
+  if (!aligned(states, 8)) return CUGO_B200_ERR_ALIGN;
+  if (n == 0) return CUGO_B200_OK;
+  create_kernel<<<blocks_for(n, kBlock), kBlock, 0, stream>>>(
+      nullptr, nullptr, n, reinterpret_cast<u64*>(states), index, seed_base);
+  return launch_status();
+}
+
+int64_t cugo_b200_running_init_scratch(int64_t n) { return n < 0 ? -1 : 2 * ((n + 31) / 32); }
+
+int cugo_b200_running_init(const uint8_t* states, int64_t n, int64_t* ids, int64_t* spare_ids,
+                           int32_t* count,
+                           int32_t* decision, float* reward0, bool* nagari, int64_t* bad,
+                           int32_t* scratch, int64_t scratch_len, cudaStream_t stream) {
+  if (n < 0 || n > INT32_MAX) return CUGO_B200_ERR_ARG;
+  if (!count || !bad || !scratch) return CUGO_B200_ERR_ARG;
+  if (n > 0 && (!states || !ids || !decision || !reward0 || !nagari)) return CUGO_B200_ERR_ARG;
+  const i64 words = (n + 31) / 32;
+  if (scratch_len < 2 * words) return CUGO_B200_ERR_CAPACITY;
+  uint32_t* keep = reinterpret_cast<uint32_t*>(scratch);
+  int32_t* offsets = scratch + words;
+  running_flags_kernel<<<static_cast<unsigned>(n > 0 ? (n + 255) / 256 : 1), 256, 0, stream>>>(
+      states, n, ids, spare_ids, keep, decision, reward0, nagari, bad);
+  compact_scan_kernel<<<1, 1024, 0, stream>>>(keep, n, nullptr, offsets, count, 1, words);
+  if (n > 0)
+    compact_scatter_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+        keep, offsets, nullptr, n, nullptr, ids, 1, words);
+  return launch_status();
+}
 
 int cugo_b200_create(const int64_t* seeds, const int64_t* first_players, int64_t n,
                      uint8_t* states, cudaStream_t stream) {

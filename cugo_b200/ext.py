@@ -24,6 +24,8 @@ _VP, _I64, _I32, _U32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.
 # name -> argument types after the leading pointers (all return int status)
 _SIGNATURES: dict[str, list] = {
     "cugo_b200_create": [_VP, _VP, _I64, _VP, _VP],
+    "cugo_b200_create_indexed": [_VP, _I64, _I64, _VP, _VP],
+    "cugo_b200_running_init": [_VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _VP],
     "cugo_b200_observe": [_VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_observe_indexed": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP],
     "cugo_b200_step": [_VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
@@ -102,7 +104,8 @@ _CONSTANTS = {
 }
 _EXTRA_CONSTANTS = {"EVENT_IN": "cugo_b200_event_inputs", "START_IN": "cugo_b200_start_inputs"}
 _INT64_FUNCTIONS = {"cugo_b200_colsum_scratch_floats": [_I64, _I32],
-                    "cugo_b200_wgrad_scratch_floats": [_I64, _I64, _I64]}
+                    "cugo_b200_wgrad_scratch_floats": [_I64, _I64, _I64],
+                    "cugo_b200_running_init_scratch": [_I64]}
 _ERRORS = {-1: "invalid argument", -2: "misaligned pointer", -3: "kernel launch failed"}
 
 _LIB: ctypes.CDLL | None = None
@@ -224,6 +227,44 @@ class CugoB200Extension:
             _check(self._lib.cugo_b200_create(_ptr(seeds), _ptr(first_players), n, _ptr(states),
                                               self._stream(seeds.device)), "create")
         return states
+
+    def create_indexed(self, index: torch.Tensor, seed_base: int) -> torch.Tensor:
+        """create(index + seed_base, index & 1) in one kernel (see the C declaration)."""
+        _check_cuda_1d(index, torch.int64, "index")
+        n = index.numel()
+        with torch.cuda.device(index.device):
+            states = torch.empty((n, self.STATE_BYTES), dtype=torch.uint8, device=index.device)
+            _check(self._lib.cugo_b200_create_indexed(_ptr(index), int(seed_base), n, _ptr(states),
+                                                      self._stream(index.device)), "create_indexed")
+        return states
+
+    def running_init(self, states, ids, count, decision, reward0, nagari, bad,
+                     scratch: torch.Tensor, spare_ids: torch.Tensor | None = None) -> None:
+        """A fresh batch's running set (see the C declaration): ids int64 [>= n] gets the
+        rows whose game the deal did not end (then i at position i), count int32 [1]
+        their number, spare_ids (optional, int64 [>= n]) i at position i; decision int32,
+        reward0 fp32, nagari bool [n] zeroed; bad int64 [1] zeroed; scratch int32
+        [>= 2 * ceil(n / 32)]."""
+        self._states(states)
+        n = states.size(0)
+        for t, dt, name in ((ids, torch.int64, "ids"), (count, torch.int32, "count"),
+                            (decision, torch.int32, "decision"), (reward0, torch.float32, "reward0"),
+                            (nagari, torch.bool, "nagari"), (bad, torch.int64, "bad"),
+                            (scratch, torch.int32, "scratch")):
+            if t.dtype != dt or not t.is_contiguous() or t.device != states.device:
+                raise RuntimeError(f"running_init: {name} must be a contiguous {dt} tensor on the states' device")
+        if ids.numel() < n or decision.numel() < n or reward0.numel() < n or nagari.numel() < n:
+            raise RuntimeError("running_init: ids, decision, reward0 and nagari need n entries")
+        if spare_ids is not None and (spare_ids.dtype != torch.int64 or spare_ids.numel() < n
+                                      or not spare_ids.is_contiguous()
+                                      or spare_ids.device != states.device):
+            raise RuntimeError("running_init: spare_ids must be a contiguous int64 tensor of n entries")
+        with torch.cuda.device(states.device):
+            _check(self._lib.cugo_b200_running_init(
+                _ptr(states), n, _ptr(ids), _ptr(spare_ids), _ptr(count), _ptr(decision),
+                _ptr(reward0),
+                _ptr(nagari), _ptr(bad), _ptr(scratch), scratch.numel(),
+                self._stream(states.device)), "running_init")
 
     def observe(self, states: torch.Tensor) -> list[torch.Tensor]:
         self._states(states)

@@ -36,24 +36,37 @@ class RunningSet:
         g = states.shape[0]
         self.ext, self.states, self.g = ext, states, g
         i64 = dict(dtype=torch.int64, device=dev)
-        if running is None:
-            running = states[:, DONE_BYTE] == 0
-        # Running rows first, in order; the rest stay valid rows (read, not used).
-        head = torch.sort((~running).to(torch.uint8), stable=True).indices
-        self.ids = (head, torch.zeros(g, **i64))
-        self.counts = torch.zeros(2, dtype=torch.int32, device=dev)
-        self.counts[0:1].copy_(running.sum().view(1))
-        self.positions = torch.arange(g, **i64)
-        self.decision = torch.zeros(g, dtype=torch.int32, device=dev)
-        self.reward0 = torch.zeros(g, dtype=torch.float32, device=dev)
-        self.nagari = torch.zeros(g, dtype=torch.bool, device=dev)
-        self.bad = torch.zeros(1, **i64)
         # grouped: each round's list is grouped by the games' next decision (primary
         # plays, floor choices, prompts) instead of kept in row order, so a warp of
         # the next round runs one branch of the rule code (1.3-1.7x faster steps).
         self.grouped = grouped
         self.scratch = torch.empty(max(1, (6 if grouped else 2) * ((g + 31) // 32)),
                                    dtype=torch.int32, device=dev)
+        self.counts = torch.empty(2, dtype=torch.int32, device=dev)
+        self.bad = torch.empty(1, **i64)
+        if running is None and dev.type == "cuda":
+            # The games the deal did not end, in row order, and the zeroed per-game
+            # arrays: three kernels (ext.running_init) instead of a sort and fills.  Every
+            # entry of both id lists is a valid row (entries past the count are read).
+            self.ids = (torch.empty(g, **i64), torch.empty(g, **i64))
+            self.decision = torch.empty(g, dtype=torch.int32, device=dev)
+            self.reward0 = torch.empty(g, dtype=torch.float32, device=dev)
+            self.nagari = torch.empty(g, dtype=torch.bool, device=dev)
+            ext.running_init(states, self.ids[0], self.counts[0:1], self.decision, self.reward0,
+                             self.nagari, self.bad, self.scratch, spare_ids=self.ids[1])
+        else:
+            if running is None:
+                running = states[:, DONE_BYTE] == 0
+            # Running rows first, in order; the rest stay valid rows (read, not used).
+            head = torch.sort((~running).to(torch.uint8), stable=True).indices
+            self.ids = (head, torch.zeros(g, **i64))
+            self.counts.zero_()
+            self.counts[0:1].copy_(running.sum().view(1))
+            self.decision = torch.zeros(g, dtype=torch.int32, device=dev)
+            self.reward0 = torch.zeros(g, dtype=torch.float32, device=dev)
+            self.nagari = torch.zeros(g, dtype=torch.bool, device=dev)
+            self.bad.zero_()
+        self._positions: torch.Tensor | None = None
         self.rounds = 0
         self.bound = g  # the host's upper bound of the running count
         self.check_every, self.lookahead = check_every, lookahead
@@ -65,6 +78,13 @@ class RunningSet:
         self._pending: list[tuple[torch.cuda.Event, int, int]] = []
         self._copies = 0
         self.done = g == 0
+
+    @property
+    def positions(self) -> torch.Tensor:
+        """0 .. g - 1 (int64, made on first use)."""
+        if self._positions is None:
+            self._positions = torch.arange(self.g, dtype=torch.int64, device=self.states.device)
+        return self._positions
 
     # -- the current round ---------------------------------------------------------
     @property

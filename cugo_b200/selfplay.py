@@ -89,7 +89,7 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
     receives the action game i chose at its decision d (the extra last row takes the
     writes of positions past the running count)."""
     g = game_index.numel()
-    states = ext.create(game_index + seed_base, game_index & 1)
+    states = ext.create_indexed(game_index, seed_base)  # seed_base + i, first player i & 1
     run = RunningSet(ext, states, check_every=CHECK_EVERY, grouped=True)
     fused = getattr(policy, "samples_in_kernel", lambda: False)()
     # The policy timer needs each round's row count: it reads the count every round.
@@ -131,6 +131,10 @@ def play_batch(ext, policy, game_index: torch.Tensor, seed_base: int = 12345,
         raise RuntimeError(f"games did not finish within {max_rounds} rounds")
     if launches is not None:
         launches.append(n_launch)
-    decisions = int(run.decision.sum())
-    played = int(run.decision.max()) if g else 0  # every live game decides once per round
-    return BatchResult(g, decisions, played, int(run.bad.item()), run.reward0, run.nagari)
+    if g == 0:
+        return BatchResult(0, 0, 0, int(run.bad.item()), run.reward0, run.nagari)
+    # One host read for the totals; every live game decides once per round, so the
+    # most decisions of a game is the number of rounds played.
+    decisions, played, bad = torch.stack([run.decision.sum(), run.decision.max().long(),
+                                          run.bad[0]]).tolist()
+    return BatchResult(g, decisions, played, bad, run.reward0, run.nagari)

@@ -64,6 +64,13 @@ CUGO_B200_API int64_t cugo_b200_status_ok(void);            /* STATUS_OK = 0 */
 CUGO_B200_API int cugo_b200_create(const int64_t* seeds, const int64_t* first_players, int64_t n,
                      uint8_t* states, cudaStream_t stream);
 
+/* create from game indices (the drivers build the seed and first-player arrays from
+ * an index with torch ops first, python/cugo_ppo_nets50.py:15-17): game i gets seed
+ * seed_base + index[i] and first player index[i] & 1, the rows cugo_b200_create makes
+ * from those two arrays.  No reference counterpart. */
+CUGO_B200_API int cugo_b200_create_indexed(const int64_t* index, int64_t seed_base, int64_t n,
+                                           uint8_t* states, cudaStream_t stream);
+
 /* observe (torch50_ext.cu:501-518): features, legal mask, deciding player,
  * done flag and packet status of every row; read only. */
 CUGO_B200_API int cugo_b200_observe(const uint8_t* states, int64_t n, float* features, bool* legal,
@@ -116,6 +123,21 @@ CUGO_B200_API int cugo_b200_step_compact_grouped(uint8_t* states, int64_t n_stat
                                                  bool* nagari, int64_t* bad, int64_t* next_ids,
                                                  int32_t* next_count, int32_t* scratch,
                                                  const int32_t* m_dev, cudaStream_t stream);
+
+/* The running set of a freshly created batch for the self-play round loop (the
+ * reference's drivers keep a live index list and compact it with torch ops,
+ * python/cugo_ppo50.py:359,375): ids[0 .. *count) = the rows whose game the deal did
+ * not end, in row order, ids[i] = i past them, and spare_ids[i] = i (optional: the
+ * other list of a double-buffered loop), so every entry is a valid row; decision,
+ * reward0 and nagari zeroed for all n rows; *bad = 0.  scratch: int32
+ * [cugo_b200_running_init_scratch(n)] (= 2 * ceil(n / 32)); a shorter one returns
+ * CUGO_B200_ERR_CAPACITY.  No reference counterpart. */
+CUGO_B200_API int64_t cugo_b200_running_init_scratch(int64_t n);
+CUGO_B200_API int cugo_b200_running_init(const uint8_t* states, int64_t n, int64_t* ids,
+                                         int64_t* spare_ids, int32_t* count, int32_t* decision,
+                                         float* reward0, bool* nagari, int64_t* bad,
+                                         int32_t* scratch, int64_t scratch_len,
+                                         cudaStream_t stream);
 
 /* step_events_indexed (torch50_ext.cu:626-660): step_indexed plus the committed
  * action's event record, int64 [m, 9] (zero when nothing was committed). */

@@ -112,3 +112,21 @@ def test_wgrad_arguments_checked_before_launch():
     small = q(64, 512, 512) - 1
     assert fn(a, 512, a, 512, 64, 512, 512, a, 512, a, small, None, None) == -4
     assert fn(a, 512, a, 512, 64, 512, 512, a, 512, None, need, None, None) == -4
+
+
+def test_running_init_arguments_checked_before_launch():
+    """The running-set entry refuses a negative size, missing outputs and a scratch
+    buffer shorter than its own size query before touching the device."""
+    lib = load_library()
+    fn = lib.cugo_b200_running_init
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    fn.argtypes = [vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, i64, vp]
+    fn.restype = ctypes.c_int
+    q = lib.cugo_b200_running_init_scratch
+    q.argtypes, q.restype = [i64], i64
+    assert q(0) == 0 and q(1) == 2 and q(64) == 4 and q(65) == 6 and q(-1) == -1
+    a = 0x10000
+    assert fn(a, -1, a, a, a, a, a, a, a, a, 4, None) == -1        # negative size
+    assert fn(a, 64, None, a, a, a, a, a, a, a, 4, None) == -1     # no ids
+    assert fn(a, 64, a, a, a, a, a, a, None, a, 4, None) == -1     # no bad counter
+    assert fn(a, 65, a, None, a, a, a, a, a, a, q(65) - 1, None) == -4  # scratch too short

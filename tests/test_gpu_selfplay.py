@@ -176,3 +176,39 @@ def test_play_batch_replays_on_the_oracle(ext, oracle, games_from):
     assert int(dec.sum()) == res.decisions
     assert np.array_equal(r0, res.reward0.cpu().numpy())
     assert np.array_equal(nag, res.nagari.cpu().numpy())
+
+
+def test_create_indexed_matches_create(ext):
+    idx = torch.randint(0, 1 << 40, (5000,), device=DEV, dtype=torch.int64)
+    a = ext.create_indexed(idx, 777)
+    b = ext.create(idx + 777, idx & 1)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert ext.create_indexed(idx[:0], 777).shape == (0, ext.STATE_BYTES)
+
+
+@pytest.mark.parametrize("n", [0, 1, 31, 4097])
+def test_running_init_lists_the_games_the_deal_left_running(ext, n):
+    idx = torch.arange(n, device=DEV, dtype=torch.int64)
+    states = ext.create_indexed(idx, 12345)
+    if n:  # end some games at the deal by hand: their done byte is set
+        ended = torch.rand(n, device=DEV) < 0.3
+        states[ended, 239] = 1
+    running = states[:, 239] == 0
+    ids = torch.full((n + 5,), -7, dtype=torch.int64, device=DEV)
+    count = torch.full((1,), -1, dtype=torch.int32, device=DEV)
+    decision = torch.full((n,), 9, dtype=torch.int32, device=DEV)
+    reward0 = torch.full((n,), 3.0, device=DEV)
+    nagari = torch.ones(n, dtype=torch.bool, device=DEV)
+    bad = torch.full((1,), 5, dtype=torch.int64, device=DEV)
+    scratch = torch.empty(max(1, 2 * ((n + 31) // 32)), dtype=torch.int32, device=DEV)
+    spare = torch.full((n,), -7, dtype=torch.int64, device=DEV)
+    ext.running_init(states, ids, count, decision, reward0, nagari, bad, scratch, spare_ids=spare)
+    torch.cuda.synchronize()
+    k = int(count)
+    assert k == int(running.sum())
+    assert torch.equal(ids[:k], torch.nonzero(running).squeeze(1))
+    pos = torch.arange(n, device=DEV)
+    assert torch.equal(ids[k:n], pos[k:]) and torch.equal(spare, pos)  # valid rows everywhere
+    assert bool((ids[n:] == -7).all())  # nothing past n written
+    assert not decision.any() and not reward0.any() and not nagari.any() and int(bad) == 0
