@@ -59,6 +59,18 @@ __device__ __forceinline__ void bf16x8(const uint4 raw, float* f) {
   }
 }
 
+// d += A B for one m16n8k16 tile (bf16 operands, fp32 accumulators) in the register
+// fragments of mma.sync: a0..a3 rows (g, g + 8) x K columns (2c, 2c + 1, 2c + 8, 2c + 9),
+// b0, b1 K rows (2c, 2c + 1), (2c + 8, 2c + 9) of column g; d rows g, g + 8 x columns
+// 2c, 2c + 1 (g = lane / 4, c = lane % 4; the lower K index in the lower 16 bits).
+__device__ __forceinline__ void mma_m16n8k16_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                                  uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
@@ -839,49 +851,57 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
           values[dst] = vn;
           __syncwarp();
         }
-        // Scores: lane 2j + c holds dimensions 16c .. 16c + 15 of slot 16 * pass + j.
-        float qf[16];
-        {
-          const uint4* qp = reinterpret_cast<const uint4*>(q + i * ldq + h * kDh) + 2 * (lane & 1);
-          bf16x8(__ldg(qp), qf);
-          bf16x8(__ldg(qp + 1), qf + 8);
-        }
+        // Scores on the tensor cores: mma.sync m16n8k16 (bf16 in, fp32 out) with the
+        // block's 16 slots as the A rows and the query in every B column.  The 32
+        // dimensions go in as two K steps in a permuted order (the same for A and B,
+        // so the dot products are unchanged): lane (g, c) = (lane / 4, lane % 4) loads
+        // dimensions 8c .. 8c + 7 of slots g and g + 8 as one 16-byte read each (a
+        // warp reads 512 contiguous bytes: no bank conflicts) and the same 8 query
+        // dimensions; its bf16 pairs are K columns (2c, 2c + 1) and (2c + 8, 2c + 9)
+        // of the two steps.  Lane (g, c) gets the scores of slots g and g + 8 of the
+        // block.  Rows past p read slot p and are masked.
+        const int g = lane >> 2, c = lane & 3;
+        const uint4 qb = __ldg(reinterpret_cast<const uint4*>(q + i * ldq + h * kDh) + c);
+        const int nblk = (p >> 4) + 1;  // p < kStagedSlots = 64: at most 4 blocks
+        float sc[kStagedSlots / 16][2];
         float mx = -INFINITY;
-        for (int t0 = 0; t0 <= p; t0 += 16) {
-          const int slot = t0 + (lane >> 1);
-          float d0 = 0.0f, d1 = 0.0f;
-          if (slot <= p) {
-            const uint4* kp = reinterpret_cast<const uint4*>(ks + slot * kDh) + 2 * (lane & 1);
-            float kf[16];
-            bf16x8(kp[0], kf);
-            bf16x8(kp[1], kf + 8);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              d0 = fmaf(kf[e], qf[e], d0);
-              d1 = fmaf(kf[8 + e], qf[8 + e], d1);
+        for (int b = 0; b < kStagedSlots / 16; ++b) {
+          if (b < nblk) {
+            const int s0 = 16 * b + g, s1 = s0 + 8;
+            const uint4 k0 = *reinterpret_cast<const uint4*>(ks + (s0 <= p ? s0 : p) * kDh + 8 * c);
+            const uint4 k1 = *reinterpret_cast<const uint4*>(ks + (s1 <= p ? s1 : p) * kDh + 8 * c);
+            float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            mma_m16n8k16_bf16(d, k0.x, k1.x, k0.y, k1.y, qb.x, qb.y);
+            mma_m16n8k16_bf16(d, k0.z, k1.z, k0.w, k1.w, qb.z, qb.w);
+            sc[b][0] = s0 <= p ? d[0] * scale : -INFINITY;
+            sc[b][1] = s1 <= p ? d[2] * scale : -INFINITY;
+            mx = fmaxf(mx, fmaxf(sc[b][0], sc[b][1]));
+          }
+        }
+        // The four lanes of a row group hold the same scores: reduce over g only.
+        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 16));
+        float sum = 0.0f;
+#pragma unroll
+        for (int b = 0; b < kStagedSlots / 16; ++b) {
+          if (b < nblk) {
+            const float w0 = expf(sc[b][0] - mx), w1 = expf(sc[b][1] - mx);  // 0 past p
+            sum += w0 + w1;
+            if (c == 0) {
+              wrow[16 * b + g] = w0;
+              wrow[16 * b + g + 8] = w1;
             }
           }
-          float d = d0 + d1;
-          d += __shfl_xor_sync(kFull, d, 1);
-          if (slot <= p) {
-            d *= scale;
-            if ((lane & 1) == 0) wrow[slot] = d;
-            mx = fmaxf(mx, d);
-          }
         }
-        mx = warp_max(mx);
+        sum += __shfl_xor_sync(kFull, sum, 4);
+        sum += __shfl_xor_sync(kFull, sum, 8);
+        sum += __shfl_xor_sync(kFull, sum, 16);
         __syncwarp();
-        float sum = 0.0f;
-        for (int j = lane; j <= p; j += 32) {
-          const float w = expf(wrow[j] - mx);
-          wrow[j] = w;
-          sum += w;
-        }
-        sum = warp_sum(sum);
-        __syncwarp();
-        // Output: lane c + 16 g sums dimensions 2c, 2c + 1 over slots g, g + 2, ...
-        // (two partial sums per dimension in flight), then the two slot halves meet
-        // by one shuffle; all additions in a fixed order.
+        // Output: lane l sums dimensions 2 (l % 16), 2 (l % 16) + 1 over slots l / 16,
+        // l / 16 + 2, ... (two partial sums per dimension in flight), then the two slot
+        // halves meet by one shuffle; all additions in a fixed order.
         const __nv_bfloat162* vp = reinterpret_cast<const __nv_bfloat162*>(vs) + (lane & 15);
         float ax0 = 0.0f, ay0 = 0.0f, ax1 = 0.0f, ay1 = 0.0f;
         int j = lane >> 4;
