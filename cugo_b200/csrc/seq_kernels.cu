@@ -762,37 +762,38 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
   }
   __syncthreads();
 
-  // Ring bookkeeping, thread 0 only: items [consumed, issued) are in flight, taking
-  // live_bytes bytes; the next one goes at `head` (or wraps to 0).
+  // Ring bookkeeping, warp 0 (every lane keeps the same copy): items [consumed,
+  // issued) are in flight, taking live_bytes bytes; the next one goes at `head` (or
+  // wraps to 0).
   int issued = 0, head = 0, live_bytes = 0;
   const auto item_bytes = [&](int k) {
     return info[k].row >= 0 ? 2 * heads * (info[k].pos + 1) * kDh * 2 : 0;
   };
+  // Item k's copies (warp 0): lane 0 posts the expected bytes on the item's mbarrier,
+  // then lane j < 2 x heads copies the key (j < heads) or value slots of head j % heads.
   const auto issue = [&](int k, int at) {
     const i64 r = info[k].row;
     uint64_t* bar = &full[k % kRingItems];
     const int p1 = info[k].pos + 1;
     const int copied = r >= 0 ? (k_new ? p1 - 1 : p1) : 0;
     const uint32_t bytes = static_cast<uint32_t>(copied) * kDh * 2;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes * 2u * static_cast<uint32_t>(heads))
-                 : "memory");
-    if (bytes == 0) return;
-    for (int hh = 0; hh < heads; ++hh) {
-      const i64 src = (r * heads + hh) * static_cast<i64>(slots) * kDh;
-      unsigned char* kd = ring + at + hh * p1 * kDh * 2;
-      unsigned char* vd = ring + at + (heads + hh) * p1 * kDh * 2;
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-          ::"r"(smem_u32(kd)), "l"(keys + src), "r"(bytes), "r"(smem_u32(bar))
-          : "memory");
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-          ::"r"(smem_u32(vd)), "l"(values + src), "r"(bytes), "r"(smem_u32(bar))
-          : "memory");
-    }
+    if (lane == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                   "r"(bytes * 2u * static_cast<uint32_t>(heads))
+                   : "memory");
+    __syncwarp();
+    if (bytes == 0 || lane >= 2 * heads) return;
+    const int hh = lane < heads ? lane : lane - heads;
+    const i64 src = (r * heads + hh) * static_cast<i64>(slots) * kDh;
+    unsigned char* dst = ring + at + (lane < heads ? hh : heads + hh) * p1 * kDh * 2;
+    const __nv_bfloat16* from = (lane < heads ? keys : values) + src;
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(from), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
   };
-  // Issues items while the ring has room (thread 0; `consumed`: the oldest live item).
+  // Issues items while the ring has room (warp 0, every lane the same decisions;
+  // `consumed`: the oldest live item).
   const auto fill = [&](int consumed) {
     while (issued < items && issued - consumed < kRingItems) {
       const int need = item_bytes(issued);
@@ -812,7 +813,7 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
           break;  // head == tail with live bytes: the ring is full
         }
       }
-      ring_off[issued % kRingItems] = at;
+      if (lane == 0) ring_off[issued % kRingItems] = at;
       head = at + need;
       live_bytes += need;
       issue(issued, at);
@@ -820,7 +821,7 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
     }
   };
 
-  if (t == 0) fill(0);
+  if (h == 0) fill(0);
   float* wrow = weights + h * kStagedSlots;
   bool failed = false;
   for (int k = 0; k < items; ++k) {
@@ -929,18 +930,16 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
       }
     }
     __syncthreads();  // item k's ring bytes and the weights are free again
-    if (t == 0) {
+    if (h == 0) {
       live_bytes -= item_bytes(k);
       fill(k + 1);
     }
   }
-  if (failed) {
-    // Let copies already issued land before the block's shared memory goes away.
-    __syncthreads();
-    if (t == 0)
-      for (int k = 0; k < issued; ++k)
-        stage_wait(&full[k % kRingItems], static_cast<uint32_t>((k / kRingItems) & 1));
-  }
+  // After a failed wait (decided over the whole block, so every thread takes the same
+  // barriers) let copies already issued land before the shared memory goes away.
+  if (__syncthreads_or(failed) && t == 0)
+    for (int k = 0; k < issued; ++k)
+      stage_wait(&full[k % kRingItems], static_cast<uint32_t>((k / kRingItems) & 1));
   __syncthreads();
 }
 
