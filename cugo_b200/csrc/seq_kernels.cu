@@ -33,6 +33,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
+#include <atomic>
 #include <stdint.h>
 
 #include "../../include/cugo_b200.h"
@@ -669,13 +670,16 @@ constexpr int games_smem_bytes(int length) { return 2 * (1 + length) * kKvPitch 
 //
 // For caches of up to kStagedSlots slots and up to kStagedHeads heads (the sequence
 // policy's 50 slots and 8 heads).  A persistent block takes its queries in order (all
-// heads of one query at a time).  One thread reads every query's cache row and
-// position first, then keeps a ring of shared memory filled: each query takes
+// heads of one query at a time).  The block reads every query's cache row and
+// position first, then warp 0 keeps a ring of shared memory filled: each query takes
 // 2 x heads x (pos + 1) x 64 contiguous bytes of the ring (its attended key slots of
-// every head, then its value slots), loaded by one bulk copy (cp.async.bulk) per head
-// and tensor completing on the query's mbarrier -- as many queries in flight as the
-// ring holds (a query's bytes grow with its position, so the ring is filled by
-// bytes, not by a fixed number of stages).  Warp h then works on head h from shared
+// every head, then its value slots) followed by its query row and, with an append,
+// its new key and value rows (heads x 64 bytes each), loaded by one bulk copy
+// (cp.async.bulk) per head and tensor and one per row, all completing on the query's
+// mbarrier -- as many queries in flight as the ring holds (a query's bytes grow with
+// its position, so the ring is filled by bytes, not by a fixed number of stages).
+// Nothing a query needs is read from global memory after its wait: under a saturated
+// memory system a load issued there would cost a full round trip per query.  Warp h then works on head h from shared
 // memory: four lanes per slot take the 32-dimension dot product of 8 slots per pass,
 // the warp forms the softmax over the slots (fp32), and lane d sums the weighted
 // values of dimension d.  With an append, the slot pos row is not copied: the new key
@@ -766,30 +770,50 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
   // issued) are in flight, taking live_bytes bytes; the next one goes at `head` (or
   // wraps to 0).
   int issued = 0, head = 0, live_bytes = 0;
+  const int row_bytes = heads * kDh * 2;  // one token's query (or key, or value) row
+  const int token_rows = k_new ? 3 : 1;
   const auto item_bytes = [&](int k) {
-    return info[k].row >= 0 ? 2 * heads * (info[k].pos + 1) * kDh * 2 : 0;
+    return info[k].row >= 0 ? (2 * (info[k].pos + 1) + token_rows) * row_bytes : 0;
   };
   // Item k's copies (warp 0): lane 0 posts the expected bytes on the item's mbarrier,
-  // then lane j < 2 x heads copies the key (j < heads) or value slots of head j % heads.
+  // then lane j < 2 x heads copies the key (j < heads) or value slots of head j % heads,
+  // lane 2 x heads the query row, lanes 2 x heads + 1 and + 2 the new key and value.
   const auto issue = [&](int k, int at) {
     const i64 r = info[k].row;
     uint64_t* bar = &full[k % kRingItems];
     const int p1 = info[k].pos + 1;
     const int copied = r >= 0 ? (k_new ? p1 - 1 : p1) : 0;
     const uint32_t bytes = static_cast<uint32_t>(copied) * kDh * 2;
+    const uint32_t total =
+        r >= 0 ? bytes * 2u * static_cast<uint32_t>(heads) + static_cast<uint32_t>(token_rows * row_bytes)
+               : 0u;
     if (lane == 0)
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                   "r"(bytes * 2u * static_cast<uint32_t>(heads))
+                   "r"(total)
                    : "memory");
     __syncwarp();
-    if (bytes == 0 || lane >= 2 * heads) return;
-    const int hh = lane < heads ? lane : lane - heads;
-    const i64 src = (r * heads + hh) * static_cast<i64>(slots) * kDh;
-    unsigned char* dst = ring + at + (lane < heads ? hh : heads + hh) * p1 * kDh * 2;
-    const __nv_bfloat16* from = (lane < heads ? keys : values) + src;
+    if (r < 0) return;
+    const void* from;
+    unsigned char* dst;
+    uint32_t size;
+    if (lane < 2 * heads) {
+      if (bytes == 0) return;
+      const int hh = lane < heads ? lane : lane - heads;
+      from = (lane < heads ? keys : values) + (r * heads + hh) * static_cast<i64>(slots) * kDh;
+      dst = ring + at + (lane < heads ? hh : heads + hh) * p1 * kDh * 2;
+      size = bytes;
+    } else if (lane < 2 * heads + token_rows) {
+      const int j = lane - 2 * heads;  // 0 query, 1 new key, 2 new value
+      const i64 i = blockIdx.x + static_cast<i64>(k) * grid;
+      from = j == 0 ? q + i * ldq : (j == 1 ? k_new : v_new) + i * ldn;
+      dst = ring + at + (2 * heads * p1 * kDh * 2) + j * row_bytes;
+      size = static_cast<uint32_t>(row_bytes);
+    } else {
+      return;
+    }
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-        ::"r"(smem_u32(dst)), "l"(from), "r"(bytes), "r"(smem_u32(bar))
+        ::"r"(smem_u32(dst)), "l"(from), "r"(size), "r"(smem_u32(bar))
         : "memory");
   };
   // Issues items while the ring has room (warp 0, every lane the same decisions;
@@ -842,9 +866,12 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
         const int at = ring_off[k % kRingItems];
         __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(ring + at) + h * (p + 1) * kDh;
         __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(ring + at) + (heads + h) * (p + 1) * kDh;
+        // The token rows behind the slots: query, then (append) new key and new value.
+        const __nv_bfloat16* tok =
+            reinterpret_cast<const __nv_bfloat16*>(ring + at) + 2 * heads * (p + 1) * kDh + h * kDh;
         if (k_new) {  // the token's own key and value: slot p of the ring and the cache
-          const __nv_bfloat16 kn = k_new[i * ldn + h * kDh + lane];
-          const __nv_bfloat16 vn = v_new[i * ldn + h * kDh + lane];
+          const __nv_bfloat16 kn = tok[heads * kDh + lane];
+          const __nv_bfloat16 vn = tok[2 * heads * kDh + lane];
           ks[p * kDh + lane] = kn;
           vs[p * kDh + lane] = vn;
           const i64 dst = ((r * heads + h) * static_cast<i64>(slots) + p) * kDh + lane;
@@ -862,7 +889,7 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
         // of the two steps.  Lane (g, c) gets the scores of slots g and g + 8 of the
         // block.  Rows past p read slot p and are masked.
         const int g = lane >> 2, c = lane & 3;
-        const uint4 qb = __ldg(reinterpret_cast<const uint4*>(q + i * ldq + h * kDh) + c);
+        const uint4 qb = reinterpret_cast<const uint4*>(tok)[c];
         const int nblk = (p >> 4) + 1;  // p < kStagedSlots = 64: at most 4 blocks
         float sc[kStagedSlots / 16][2];
         float mx = -INFINITY;
@@ -943,10 +970,13 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
   __syncthreads();
 }
 
-// The ring holds the largest query of this cache (2 x heads x slots x 64 bytes, so a
-// query always fits an empty ring), rounded up to 1 KB: at the sequence policy's 8
-// heads and 50 slots four blocks (32 warps) fit an SM.
-int ring_bytes_for(int heads, int slots) { return (2 * heads * slots * kDh * 2 + 1023) / 1024 * 1024; }
+// The ring holds the largest query of this cache (2 x heads x slots x 64 bytes of slots
+// and three token rows of heads x 64 bytes, so a query always fits an empty ring),
+// rounded up to 1 KB: at the sequence policy's 8 heads and 50 slots four blocks (32
+// warps) fit an SM.
+int ring_bytes_for(int heads, int slots) {
+  return ((2 * slots + 3) * heads * kDh * 2 + 1023) / 1024 * 1024;
+}
 
 size_t staged_smem_bytes(int heads, int slots) {
   return static_cast<size_t>(ring_bytes_for(heads, slots)) + kStagedHeads * kStagedSlots * 4 +
@@ -976,18 +1006,19 @@ int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new, co
   if (heads <= kStagedHeads && slots <= kStagedSlots && aligned(out, 4) && ldo % 2 == 0 &&
       staged_smem_bytes(heads, slots) <= static_cast<size_t>(227 * 1024)) {
     const size_t smem = staged_smem_bytes(heads, slots);
-    static size_t configured = 0;
-    if (smem > configured) {
+    // The shared-memory opt-in is a per-device function attribute.
+    static std::atomic<size_t> configured[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUGO_B200_ERR_LAUNCH;
+    if (smem > configured[dev].load(std::memory_order_acquire)) {
       if (cudaFuncSetAttribute(decode_attention_staged_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(smem)) != cudaSuccess)
         return CUGO_B200_ERR_LAUNCH;
-      configured = smem;
+      configured[dev].store(smem, std::memory_order_release);
     }
     int sms = 148;
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_attention_staged_kernel,
                                                       kStagedThreads, smem) != cudaSuccess ||
