@@ -16,7 +16,8 @@ bytes or FLOPs of one launch:
   mlpsample M H B      the self-play policy step: forward and masked Gumbel-max sampling
                        (one fused launch at H = 512), flops_per_row * M
   observe   ROWS       observe_indexed, 3,319 B per row
-  step      ROWS       step_indexed on live mid-game rows, 521 B per row
+  step      ROWS       step_indexed on live mid-game rows with random legal actions,
+                       521 B per row
   branch    ROOTS PER  branch_indexed, 274 B per branch
   selfplay  SLOTS      the fused config-1 decision kernel, 4,027 B per decision
   attention N R        decode attention with KV append over a [R, 8, 50, 32] bf16 cache,
@@ -72,6 +73,15 @@ def _mid_game(ext, rows: int, decisions: int = 6):
     for _ in range(decisions):
         ext.selfplay_random_step(states, game, dec, done, steps, feats, legal)
     return states, feats, legal
+
+
+def _random_legal(ext, states, ids):
+    """A uniformly drawn legal action for each row ids[j] as the row is now (its
+    current legal mask, observed here), in the order of ids."""
+    legal = ext.observe_indexed(states, ids)[1]
+    u = torch.rand(legal.shape, device=legal.device,
+                   generator=torch.Generator(device=legal.device).manual_seed(1))
+    return torch.where(legal, u, torch.full_like(u, -1.0)).argmax(1)
 
 
 def seqwave_case(wave: int) -> dict:
@@ -354,9 +364,9 @@ def reference_gpu_case(games: int = 262144, warmup: int = 1, iters: int = 2) -> 
     out["loop_speedup_native"] = out["play_batch_games_per_s"] / out["loop_reference_ext_games_per_s"]
 
     # -- engine ops --------------------------------------------------------------------
-    states, _, legal = _mid_game(ext, games)
+    states, _, _ = _mid_game(ext, games)
     ids = torch.randperm(games, device=dev)
-    acts = legal.to(torch.int64).argmax(1).index_select(0, ids)
+    acts = _random_legal(ext, states, ids)
     snapshot = states.clone()
     for name, e in (("reference", ref_ext), ("cugo", ext)):
         sec = _events_time(lambda: e.observe_indexed(states, ids), warmup + 2, iters + 3)
@@ -469,10 +479,12 @@ def main() -> None:
         sec = _time(lambda: ext.observe_indexed(states, ids), args.warmup, args.iters)
         out.update(seconds=sec, gbs=rows * 3319 / sec / 1e9)
     elif args.case == "step":
+        # Live mid-game rows in random order, each given a uniformly drawn legal action
+        # of its current decision (the mask observed on the rows as they are now).
         (rows,) = d
-        states, _, legal = _mid_game(ext, rows)
+        states, _, _ = _mid_game(ext, rows)
         ids = torch.randperm(rows, device=dev)
-        acts = legal.to(torch.int64).argmax(1).index_select(0, ids)
+        acts = _random_legal(ext, states, ids)
         snapshot = states.clone()
 
         def run():

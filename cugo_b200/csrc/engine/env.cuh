@@ -182,8 +182,17 @@ CB_HD Mask floor_after(Mask floor_std, u32 card, u32 pick, bool& need, bool& bad
   return floor_std & ~card_bit(pick);
 }
 
-CB_HD Peek peek_regular(const Game& g, u32 card, u32 played_pick, u32 drawn_pick) {
+// A card play or shake (`card` lands on the floor, then the flipped card), or a bomb,
+// grenade or bomb credit (card = kNoCard: the bomb's month leaves the floor, then only
+// the flipped card lands).  Both kinds share one body so that a warp whose rows mix
+// them runs it once: they differ only in the floor before the flip and in the
+// played card's resolution.
+CB_HD Peek peek_turn(const Game& g, u32 kind, u32 card, u32 month, u32 played_pick,
+                     u32 drawn_pick) {
   Peek p;
+  const bool regular = card != kNoCard;
+  Mask floor = g.floor_std();
+  if (!regular && kind != kActCredit) floor &= ~month_cards(month);
   Mask stock = g.stock();
   u64 rng = g.rng();
   const Flip f = flip_stock(stock, rng);
@@ -192,22 +201,25 @@ CB_HD Peek peek_regular(const Game& g, u32 card, u32 played_pick, u32 drawn_pick
     return p;
   }
   p.revealed = f.card;
-  const Mask floor = g.floor_std();
-  const Mask pm = floor & month_cards(card_month(card));
-  const u32 pmc = popc(pm);
-  const bool same = card_month(card) == card_month(f.card);
-  if (same && ((pmc == 1 && !g.last_turn()) || pmc == 0 || pmc == 2)) return p;
+  Mask after_played = floor;
+  if (regular) {
+    const Mask pm = floor & month_cards(card_month(card));
+    const u32 pmc = popc(pm);
+    const bool same = card_month(card) == card_month(f.card);
+    if (same && ((pmc == 1 && !g.last_turn()) || pmc == 0 || pmc == 2)) return p;
+    bool need, bad;
+    after_played = floor_after(floor, card, played_pick, need, bad);
+    if (need) {
+      p.decision = kDecFloorPlayed;
+      p.choices = pm;
+      return p;
+    }
+    if (bad) {
+      p.status = kInvalidChoice;
+      return p;
+    }
+  }
   bool need, bad;
-  const Mask after_played = floor_after(floor, card, played_pick, need, bad);
-  if (need) {
-    p.decision = kDecFloorPlayed;
-    p.choices = pm;
-    return p;
-  }
-  if (bad) {
-    p.status = kInvalidChoice;
-    return p;
-  }
   const Mask dm = after_played & month_cards(card_month(f.card));
   floor_after(after_played, f.card, drawn_pick, need, bad);
   if (need) {
@@ -219,43 +231,13 @@ CB_HD Peek peek_regular(const Game& g, u32 card, u32 played_pick, u32 drawn_pick
   return p;
 }
 
-// Bombs, grenades and bomb credits flip one card and resolve only that card.
-CB_HD Peek peek_special(const Game& g, u32 kind, u32 month, u32 drawn_pick) {
-  Peek p;
-  Mask floor = g.floor_std();
-  if (kind != kActCredit) floor &= ~month_cards(month);
-  Mask stock = g.stock();
-  u64 rng = g.rng();
-  const Flip f = flip_stock(stock, rng);
-  if (f.card == kNoCard) {
-    p.status = kStockEmpty;
-    return p;
-  }
-  p.revealed = f.card;
-  bool need, bad;
-  const Mask dm = floor & month_cards(card_month(f.card));
-  floor_after(floor, f.card, drawn_pick, need, bad);
-  if (need) {
-    p.decision = kDecFloorDrawn;
-    p.choices = dm;
-  } else if (bad) {
-    p.status = kInvalidChoice;
-  }
-  return p;
-}
-
 CB_HD Peek peek_pending(const Game& g) {
-  switch (g.pa_kind()) {
-    case kActPlay:
-    case kActShake:
-      return peek_regular(g, g.pa_card(), g.pa_played_pick(), g.pa_drawn_pick());
-    case kActBomb:
-    case kActGrenade:
-    case kActCredit:
-      return peek_special(g, g.pa_kind(), g.pa_month(), g.pa_drawn_pick());
-    default:
-      return Peek{};  // bonus plays and prompts never open a floor choice
-  }
+  const u32 kind = g.pa_kind();
+  if (kind == kActPlay || kind == kActShake)
+    return peek_turn(g, kind, g.pa_card(), 0xffu, g.pa_played_pick(), g.pa_drawn_pick());
+  if (kind == kActBomb || kind == kActGrenade || kind == kActCredit)
+    return peek_turn(g, kind, kNoCard, g.pa_month(), kNoCard, g.pa_drawn_pick());
+  return Peek{};  // bonus plays and prompts never open a floor choice
 }
 
 // Turns `v` into the table the chooser sees at the pending choice: the card
@@ -594,18 +576,39 @@ CB_HD void observe_game(const Game& g, PacketRef pk, ObsMeta& meta) {
 
 // ---- committing actions (cugo/game/rollout50.h:231-399 and the layers below) --
 
-// A card play or shake: play, flip, resolve, steal, then the end-of-turn checks.
-CB_HD void commit_regular(Game& g, u32 card, bool shake) {
+// A card play or shake (play, flip, resolve both cards), or a bomb, grenade or bomb
+// credit (the month's cards captured, then only the flipped card resolved), followed
+// by the steal and the end-of-turn checks.  One body for both kinds, so a warp whose
+// rows mix them runs the flip, the resolution and the end of the turn once; the
+// order of every state change is the reference's for each kind.
+CB_HD void commit_turn(Game& g, u32 kind, u32 card, u32 month) {
   const u32 a = g.actor();
-  if (shake) {
-    const Mask month = month_cards(card_month(card));
-    g.set_shown(a, g.shown(a) | (g.hand(a) & month));
-    const u32 mb = month_bit(card);
-    if (popc(g.hand(a) & month) == 4) g.set_shaken4(a, g.shaken4(a) | mb);
-    else g.set_shaken(a, g.shaken(a) | mb);
+  const Mask before = g.pile(a);
+  const bool regular = kind == kActPlay || kind == kActShake;
+  u32 base_steal = 0;
+  if (regular) {
+    if (kind == kActShake) {
+      const Mask mc = month_cards(card_month(card));
+      g.set_shown(a, g.shown(a) | (g.hand(a) & mc));
+      const u32 mb = month_bit(card);
+      if (popc(g.hand(a) & mc) == 4) g.set_shaken4(a, g.shaken4(a) | mb);
+      else g.set_shaken(a, g.shaken(a) | mb);
+    }
+    g.set_hand(a, g.hand(a) & ~card_bit(card));
+  } else if (kind == kActCredit) {
+    g.set_credits(a, g.credits(a) - 1u);
+  } else {
+    const Mask hc = g.hand(a) & month_cards(month);
+    const Mask fc = g.floor_std() & month_cards(month);
+    g.set_hand(a, g.hand(a) & ~hc);
+    g.set_floor(g.floor() & ~fc);
+    g.set_pile(a, g.pile(a) | hc | fc);
+    const bool grenade = kind == kActGrenade;
+    g.set_credits(a, (g.credits(a) + (grenade ? 1u : 2u)) & 0xffu);
+    if (!grenade) g.set_bombs(a, (g.bombs(a) + 1u) & 0xffu);
+    base_steal = g.last_turn() ? 0u : 1u;
   }
-  g.set_hand(a, g.hand(a) & ~card_bit(card));
-  g.set_played(card);
+  g.set_played(regular ? card : kNoCard);
   Mask stock = g.stock();
   u64 rng = g.rng();
   const Flip f = flip_stock(stock, rng);
@@ -614,10 +617,9 @@ CB_HD void commit_regular(Game& g, u32 card, bool shake) {
   g.set_drawn(f.card);
   g.set_flip_bonus(f.bonuses);
   g.set_phase(kPhaseResolve);
-  const Mask before = g.pile(a);
   Tally t;
   resolve_turn(g, g.pa_played_pick(), g.pa_drawn_pick(), t);
-  steal_pi(g, a, steal_count(t));
+  steal_pi(g, a, (base_steal + steal_count(t)) & 0xffu);
   after_turn(g, a);
   if ((t.events & kEvTtadak) && g.turn() == 1u) side_payment(g, a, 7);
   missions_update(g, a, g.pile(a) & ~before);
@@ -646,56 +648,19 @@ CB_HD void commit_bonus(Game& g, u32 card) {
   }
 }
 
-// Bomb, grenade or bomb credit: (the month's cards captured,) one card flipped
-// and resolved, then the turn ends.
-CB_HD void commit_special(Game& g, u32 kind, u32 month) {
-  const u32 a = g.actor();
-  const Mask before = g.pile(a);
-  u32 base_steal = 0;
-  if (kind == kActCredit) {
-    g.set_credits(a, g.credits(a) - 1u);
-  } else {
-    const Mask hc = g.hand(a) & month_cards(month);
-    const Mask fc = g.floor_std() & month_cards(month);
-    g.set_hand(a, g.hand(a) & ~hc);
-    g.set_floor(g.floor() & ~fc);
-    g.set_pile(a, g.pile(a) | hc | fc);
-    const bool grenade = kind == kActGrenade;
-    g.set_credits(a, (g.credits(a) + (grenade ? 1u : 2u)) & 0xffu);
-    if (!grenade) g.set_bombs(a, (g.bombs(a) + 1u) & 0xffu);
-    base_steal = g.last_turn() ? 0u : 1u;
-  }
-  Mask stock = g.stock();
-  u64 rng = g.rng();
-  const Flip f = flip_stock(stock, rng);
-  g.set_stock(stock);
-  g.set_rng(rng);
-  Tally t;
-  t.last = g.last_turn();
-  resolve_card(g, f.card, g.pa_drawn_pick(), t);
-  if (f.bonuses) capture(g, f.bonuses, t);
-  if (g.floor() == 0 && t.captured != 0) t.events |= kEvSweep;
-  const u32 steal = (base_steal + steal_count(t)) & 0xffu;
-  close_turn(g);
-  steal_pi(g, a, steal);
-  after_turn(g, a);
-  missions_update(g, a, g.pile(a) & ~before);
-  sync_stop(g);
-}
-
 CB_HD void commit_pending(Game& g) {
   g.set_held(0, g.held(0) | g.hand(0));
   g.set_held(1, g.held(1) | g.hand(1));
   const u32 kind = g.pa_kind();
   switch (kind) {
     case kActPlay:
-    case kActShake:  // one call site: plays and shakes of a warp share one inlined copy
-      commit_regular(g, g.pa_card(), kind == kActShake);
-      break;
-    case kActBonus: commit_bonus(g, g.pa_card()); break;
+    case kActShake:
     case kActBomb:
     case kActGrenade:
-    case kActCredit: commit_special(g, kind, g.pa_month()); break;
+    case kActCredit:  // one call site: these rows of a warp share one inlined turn
+      commit_turn(g, kind, g.pa_card(), g.pa_month());
+      break;
+    case kActBonus: commit_bonus(g, g.pa_card()); break;
     case kActGo:
     case kActStop: {
       const u32 d = g.gostop_actor();

@@ -282,14 +282,17 @@ CB_HD void close_turn(Game& g) {
 }
 
 // resolve_turn50: the played and the drawn card against the floor, with ppuk,
-// ttadak, jjok and sweep.  Phase must be kPhaseResolve.
+// ttadak, jjok and sweep.  Phase must be kPhaseResolve.  Without a played card
+// (a bomb, grenade or bomb credit) only the drawn card and its bonus cards resolve
+// (the draw-only resolution of a special play, cugo/game/special50.h:140-158).
 CB_HD void resolve_turn(Game& g, u32 played_pick, u32 drawn_pick, Tally& t) {
   const u32 played = g.played(), drawn = g.drawn();
-  const Mask pm = g.floor_std() & month_cards(card_month(played));
+  const bool has_played = played != kNoCard;
+  const Mask pm = has_played ? g.floor_std() & month_cards(card_month(played)) : Mask{0};
   const u32 pmc = popc(pm);
-  const bool same = card_month(played) == card_month(drawn);
+  const bool same = has_played && card_month(played) == card_month(drawn);
   t.last = g.last_turn();
-  const Mask pair = card_bit(played) | card_bit(drawn);
+  const Mask pair = (has_played ? card_bit(played) : Mask{0}) | card_bit(drawn);
   const Mask bonus = g.flip_bonus();
   if (same && pmc == 1 && !t.last) {
     // Ppuk: the three cards of the month stay on the floor as a stack.
@@ -308,7 +311,7 @@ CB_HD void resolve_turn(Game& g, u32 played_pick, u32 drawn_pick, Tally& t) {
     capture(g, pair | bonus, t);
     if (!t.last) t.events |= kEvJjok;
   } else {
-    resolve_card(g, played, played_pick, t);
+    if (has_played) resolve_card(g, played, played_pick, t);
     resolve_card(g, drawn, drawn_pick, t);
     if (bonus) capture(g, bonus, t);
   }
