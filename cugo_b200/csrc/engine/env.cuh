@@ -159,6 +159,11 @@ struct Peek {
   u32 decision = kDecNone;  // kDecFloorPlayed, kDecFloorDrawn or kDecNone
   Mask choices = 0;         // floor cards the choice may take
   u32 revealed = kNoCard;   // the standard card the stock flip showed
+  // The flip itself, for the commit that follows a complete probe: the bonus cards
+  // flipped before `revealed`, and the stock and its random stream after it.
+  Mask flip_bonus = 0;
+  Mask stock_after = 0;
+  u64 rng_after = 0;
 };
 
 // The floor after `card` lands on it, given the pick for a two-card match.
@@ -201,6 +206,9 @@ CB_HD Peek peek_turn(const Game& g, u32 kind, u32 card, u32 month, u32 played_pi
     return p;
   }
   p.revealed = f.card;
+  p.flip_bonus = f.bonuses;
+  p.stock_after = stock;
+  p.rng_after = rng;
   Mask after_played = floor;
   if (regular) {
     const Mask pm = floor & month_cards(card_month(card));
@@ -579,9 +587,10 @@ CB_HD void observe_game(const Game& g, PacketRef pk, ObsMeta& meta) {
 // A card play or shake (play, flip, resolve both cards), or a bomb, grenade or bomb
 // credit (the month's cards captured, then only the flipped card resolved), followed
 // by the steal and the end-of-turn checks.  One body for both kinds, so a warp whose
-// rows mix them runs the flip, the resolution and the end of the turn once; the
-// order of every state change is the reference's for each kind.
-CB_HD void commit_turn(Game& g, u32 kind, u32 card, u32 month) {
+// rows mix them runs the resolution and the end of the turn once; the order of every
+// state change is the reference's for each kind.  `flip` is the complete probe of this
+// action (peek_pending on the same row): its stock flip is the one the commit makes.
+CB_HD void commit_turn(Game& g, u32 kind, u32 card, u32 month, const Peek& flip) {
   const u32 a = g.actor();
   const Mask before = g.pile(a);
   const bool regular = kind == kActPlay || kind == kActShake;
@@ -609,13 +618,10 @@ CB_HD void commit_turn(Game& g, u32 kind, u32 card, u32 month) {
     base_steal = g.last_turn() ? 0u : 1u;
   }
   g.set_played(regular ? card : kNoCard);
-  Mask stock = g.stock();
-  u64 rng = g.rng();
-  const Flip f = flip_stock(stock, rng);
-  g.set_stock(stock);
-  g.set_rng(rng);
-  g.set_drawn(f.card);
-  g.set_flip_bonus(f.bonuses);
+  g.set_stock(flip.stock_after);
+  g.set_rng(flip.rng_after);
+  g.set_drawn(flip.revealed);
+  g.set_flip_bonus(flip.flip_bonus);
   g.set_phase(kPhaseResolve);
   Tally t;
   resolve_turn(g, g.pa_played_pick(), g.pa_drawn_pick(), t);
@@ -648,7 +654,8 @@ CB_HD void commit_bonus(Game& g, u32 card) {
   }
 }
 
-CB_HD void commit_pending(Game& g) {
+// Commits the pending action; `probe` is its complete probe (peek_pending).
+CB_HD void commit_pending(Game& g, const Peek& probe) {
   g.set_held(0, g.held(0) | g.hand(0));
   g.set_held(1, g.held(1) | g.hand(1));
   const u32 kind = g.pa_kind();
@@ -658,7 +665,7 @@ CB_HD void commit_pending(Game& g) {
     case kActBomb:
     case kActGrenade:
     case kActCredit:  // one call site: these rows of a warp share one inlined turn
-      commit_turn(g, kind, g.pa_card(), g.pa_month());
+      commit_turn(g, kind, g.pa_card(), g.pa_month(), probe);
       break;
     case kActBonus: commit_bonus(g, g.pa_card()); break;
     case kActGo:
@@ -759,7 +766,10 @@ struct StepOut {
   u32 done, nagari, committed;
 };
 
-// torch_step50: one unified action (0..178; anything else is kNoAction).
+// torch_step50: one unified action (0..178; anything else is kNoAction).  A row at a
+// floor choice probes its pending action twice (to validate the choice, then with the
+// choice made); every other row once, after its pending record is written.  Both go
+// through one probe call site, so the probe's code is in the kernel once.
 CB_HD StepOut step_game(Game& g, u32 action) {
   StepOut out{kOk, 0, 0, 0, 0};
   if (g.done()) {
@@ -767,33 +777,40 @@ CB_HD StepOut step_game(Game& g, u32 action) {
     return StepOut{kFinished, reward0(g), g.done(), g.nagari(), 0};
   }
   const bool choosing = g.pend_active() != 0;
-  const LegalInfo li = torch_legal(g);
-  if (li.status != kOk) {
-    g.set_status(li.status);
-    return StepOut{li.status, 0, g.done(), g.nagari(), 0};
+  if (!choosing) {  // torch_legal without a pending probe
+    const u32 kind = decision_kind(g);
+    Legal legal;
+    if (kind == kDecGukjin) legal.w2 = (u64{1} << (177 - 128)) | (u64{1} << (178 - 128));
+    else legal = primary_legal(g);
+    if (!legal.has(action)) {
+      g.set_status(kNotLegal);
+      return StepOut{kNotLegal, 0, g.done(), g.nagari(), 0};
+    }
+    begin_pending(g, action);
   }
-  if (!li.legal.has(action)) {
-    g.set_status(kNotLegal);
-    return StepOut{kNotLegal, 0, g.done(), g.nagari(), 0};
-  }
-  const Peek& p = li.peek;
-  if (choosing) {
-    if (p.decision == kDecPiCard) g.set_n_pi(g.n_pi() + 1u);
+  Peek next;
+CB_NO_UNROLL
+  for (u32 pass = choosing ? 0u : 1u; pass < 2u; ++pass) {
+    next = peek_pending(g);
+    if (pass == 1u || next.status != kOk) break;
+    // A choosing row's first probe: the choice must be one of its floor cards.
+    if (!choice_legal(next.choices).has(action)) {
+      g.set_status(kNotLegal);
+      return StepOut{kNotLegal, 0, g.done(), g.nagari(), 0};
+    }
+    if (next.decision == kDecPiCard) g.set_n_pi(g.n_pi() + 1u);
     else g.set_n_resolve(g.n_resolve() + 1u);
     g.set_n_choice(g.n_choice() + 1u);
     const u32 card = action - kChoiceBegin;
-    if (p.decision == kDecFloorPlayed) g.set_pa_played_pick(card);
-    else if (p.decision == kDecFloorDrawn) g.set_pa_drawn_pick(card);
-  } else {
-    begin_pending(g, action);
+    if (next.decision == kDecFloorPlayed) g.set_pa_played_pick(card);
+    else if (next.decision == kDecFloorDrawn) g.set_pa_drawn_pick(card);
   }
-  const Peek next = peek_pending(g);
   if (next.status != kOk) {
     g.set_status(next.status);
     return StepOut{next.status, 0, g.done(), g.nagari(), 0};
   }
   if (next.decision == kDecNone) {
-    commit_pending(g);
+    commit_pending(g, next);
     if (g.pend_selected_pi() != 0) g.set_pa_pi_pick(g.pend_selected_pi());
     g.set_pend_active(0);
     const u32 k = g.pa_kind();
