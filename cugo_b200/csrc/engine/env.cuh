@@ -249,14 +249,12 @@ CB_HD Peek peek_pending(const Game& g) {
 }
 
 // Turns `v` into the table the chooser sees at the pending choice: the card
-// played and the stock flipped; for a drawn-card choice also the played card
-// already resolved (postchance50.h:188-198, 288-292, 391-399).
+// played and the stock flipped (the flip of `p`, the row's probe); for a drawn-card
+// choice also the played card already resolved (postchance50.h:188-198, 288-292,
+// 391-399).
 CB_HD void stage_pending_view(Game& v, const Peek& p) {
   const u32 a = v.actor();
   const u32 kind = v.pa_kind();
-  Mask stock = v.stock();
-  u64 rng = v.rng();
-  const Flip f = flip_stock(stock, rng);
   if (kind == kActPlay || kind == kActShake) {
     const u32 card = v.pa_card();
     if (kind == kActShake) {
@@ -266,10 +264,10 @@ CB_HD void stage_pending_view(Game& v, const Peek& p) {
     }
     v.set_hand(a, v.hand(a) & ~card_bit(card));
     v.set_played(card);
-    v.set_stock(stock);
-    v.set_rng(rng);
-    v.set_drawn(f.card);
-    v.set_flip_bonus(f.bonuses);
+    v.set_stock(p.stock_after);
+    v.set_rng(p.rng_after);
+    v.set_drawn(p.revealed);
+    v.set_flip_bonus(p.flip_bonus);
     v.set_phase(kPhaseResolve);
     if (p.decision == kDecFloorDrawn) {
       Tally t;
@@ -292,10 +290,10 @@ CB_HD void stage_pending_view(Game& v, const Peek& p) {
     v.set_credits(a, (v.credits(a) + (grenade ? 1u : 2u)) & 0xffu);
     if (!grenade) v.set_bombs(a, (v.bombs(a) + 1u) & 0xffu);
   }
-  v.set_stock(stock);
-  v.set_rng(rng);
-  v.set_drawn(f.card);
-  v.set_flip_bonus(f.bonuses);
+  v.set_stock(p.stock_after);
+  v.set_rng(p.rng_after);
+  v.set_drawn(p.revealed);
+  v.set_flip_bonus(p.flip_bonus);
 }
 
 // ---- observation packet ------------------------------------------------------
