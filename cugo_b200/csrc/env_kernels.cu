@@ -403,48 +403,75 @@ __global__ void __launch_bounds__(32 * kBranchWarps, CB_BRANCH_MIN_BLOCKS) branc
 }
 
 // Exclusive prefix over the warps' running counts (one block): offsets[q][w] for
-// each group q in turn (group q's rows follow every row of groups < q), and the
-// total in *count.
+// each group q (group q's rows follow every row of groups < q), and the total in
+// *count.  The groups (at most kMaxGroups) are scanned together: every thread loads
+// its consecutive warps' words of all groups at once, and one round of block
+// barriers serves them all.
+constexpr int kMaxGroups = 3;
+
 __global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __restrict__ keep,
                                                             i64 m, const int32_t* __restrict__ m_dev,
                                                             int32_t* __restrict__ offsets,
                                                             int32_t* __restrict__ count, int groups,
                                                             i64 stride) {
-  __shared__ int32_t sums[32];
+  __shared__ int32_t sums[kMaxGroups][32];
   const i64 warps = (device_rows(m_dev, m) + 31) / 32;
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int nwarps = static_cast<int>(blockDim.x >> 5);
   const i64 per = (warps + blockDim.x - 1) / blockDim.x;  // consecutive warps per thread
   const i64 w0 = t * per;
-  int32_t base = 0;
-  for (int q = 0; q < groups; ++q) {
-    const uint32_t* kq = keep + q * stride;
-    int32_t mine = 0;
-    for (i64 w = w0; w < w0 + per && w < warps; ++w) mine += __popc(__ldg(kq + w));
-    int32_t incl = mine;
+  const i64 w1 = w0 + per < warps ? w0 + per : warps;
+  int32_t mine[kMaxGroups] = {0, 0, 0};
+  for (i64 w = w0; w < w1; ++w) {
+#pragma unroll
+    for (int q = 0; q < kMaxGroups; ++q)
+      if (q < groups) mine[q] += __popc(__ldg(keep + q * stride + w));
+  }
+  int32_t incl[kMaxGroups];
+#pragma unroll
+  for (int q = 0; q < kMaxGroups; ++q) incl[q] = mine[q];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int q = 0; q < kMaxGroups; ++q) {
+      const int32_t v = __shfl_up_sync(kFull, incl[q], o);
+      if (lane >= o) incl[q] += v;
+    }
+  }
+  if (lane == 31) {
+#pragma unroll
+    for (int q = 0; q < kMaxGroups; ++q) sums[q][wid] = incl[q];
+  }
+  __syncthreads();
+  if (wid < groups) {  // warp q scans group q's warp totals
+    int32_t v = lane < nwarps ? sums[wid][lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int32_t v = __shfl_up_sync(kFull, incl, o);
-      if (lane >= o) incl += v;
+      const int32_t u = __shfl_up_sync(kFull, v, o);
+      if (lane >= o) v += u;
     }
-    __syncthreads();  // the previous group's readers of sums are done
-    if (lane == 31) sums[wid] = incl;
-    __syncthreads();
-    if (wid == 0) {
-      int32_t v = lane < (int)(blockDim.x >> 5) ? sums[lane] : 0;
+    sums[wid][lane] = v;  // inclusive over warps 0..lane
+  }
+  __syncthreads();
+  int32_t run[kMaxGroups];
+  int32_t base = 0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int32_t u = __shfl_up_sync(kFull, v, o);
-        if (lane >= o) v += u;
+  for (int q = 0; q < kMaxGroups; ++q) {
+    if (q < groups) {
+      run[q] = base + incl[q] - mine[q] + (wid > 0 ? sums[q][wid - 1] : 0);
+      base += sums[q][31];
+    } else {
+      run[q] = 0;
+    }
+  }
+  for (i64 w = w0; w < w1; ++w) {
+#pragma unroll
+    for (int q = 0; q < kMaxGroups; ++q) {
+      if (q < groups) {
+        offsets[q * stride + w] = run[q];
+        run[q] += __popc(__ldg(keep + q * stride + w));
       }
-      sums[lane] = v;  // inclusive over warps 0..lane
     }
-    __syncthreads();
-    int32_t run = base + incl - mine + (wid > 0 ? sums[wid - 1] : 0);
-    for (i64 w = w0; w < w0 + per && w < warps; ++w) {
-      offsets[q * stride + w] = run;
-      run += __popc(__ldg(kq + w));
-    }
-    base += sums[31];
   }
   if (t == 0) *count = base;
 }

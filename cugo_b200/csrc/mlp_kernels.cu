@@ -56,6 +56,15 @@ constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + BAR_BYTES +
                            BN * 4 /*bias*/ + EPI_STAGE_BYTES;
 constexpr uint64_t kWaitNs = 2'000'000'000ull;
 
+// Shared memory and tensor memory of gemm_kernel at output tile width tbn (256, 128 or
+// 64 columns; 256 everywhere else).
+__host__ __device__ constexpr int g_stage_bytes(int tbn) { return A_BYTES + tbn * BK * 2; }
+__host__ __device__ constexpr int g_smem_bytes(int tbn) {
+  return STAGES * g_stage_bytes(tbn) + 1024 /*align*/ + BAR_BYTES + tbn * 4 /*bias*/ +
+         EPI_STAGE_BYTES;
+}
+static_assert(g_smem_bytes(BN) == SMEM_BYTES, "the 256-wide tile is the default shape");
+
 enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActGelu = 3 };
 
 struct Epilogue {
@@ -379,10 +388,12 @@ struct EpiWarp {
 // Epilogue warp w owns TMEM lanes 32 (w % 4) .. +31 (the hardware's lane quadrant
 // for warp w) and columns 128 ((w - 2) / 4) .. +127 of the tile.
 __device__ __forceinline__ int epi_quad(int warp) { return warp & 3; }
-__device__ __forceinline__ int epi_col0(int warp) { return ((warp - 2) >> 2) * (BN / 2); }
+template <int TBN = BN>
+__device__ __forceinline__ int epi_col0(int warp) { return ((warp - 2) >> 2) * (TBN / 2); }
 
 // Starts the warp's first residual chunk and stages the tile's bias (fp32) in
 // shared memory.
+template <int TBN = BN>
 __device__ __forceinline__ void epilogue_begin(const Epilogue& ep, EpiWarp& io, uint8_t* stage,
                                                float* bias_s, int epi_tid, int row0, int n0,
                                                int cbase) {
@@ -393,7 +404,7 @@ __device__ __forceinline__ void epilogue_begin(const Epilogue& ep, EpiWarp& io, 
   if (ep.residual) residual_load(io.map_res, &io.res_bar[0], stage, n0 + cbase, row0);
   // The previous tile's readers of bias_s are past this barrier.
   asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory");
-  for (int c = epi_tid; c < BN; c += EPI_THREADS) {
+  for (int c = epi_tid; c < TBN; c += EPI_THREADS) {
     const int n = n0 + c;
     float b = 0.0f;
     if (ep.bias && n < ep.n)
@@ -423,12 +434,13 @@ __device__ __forceinline__ bool epilogue_wait(uint64_t* acc_full, uint32_t parit
 // TMEM -> bias -> activation -> residual -> activation -> global for this warp's
 // 32 rows x 128 columns (tile columns cbase .. cbase + 127; taddr: the warp's lane
 // quadrant and accumulator buffer), in 64-byte-row chunks of CW columns.
-template <typename T>
+template <typename T, int TBN = BN>
 __device__ __forceinline__ void epilogue_cols(const Epilogue& ep, EpiWarp& io, uint32_t taddr,
                                               uint8_t* stage, const float* bias_s, int row0, int n0,
                                               int cbase) {
   constexpr int CW = 64 / static_cast<int>(sizeof(T));
-  constexpr int CHUNKS = (BN / 2) / CW;
+  constexpr int CHUNKS = (TBN / 2) / CW;
+  static_assert((TBN / 2) % CW == 0, "a warp's columns are whole chunks");
   const int lane = threadIdx.x & 31;
 #pragma unroll 1
   for (int c = 0; c < CHUNKS; ++c) {
@@ -472,15 +484,18 @@ __device__ __forceinline__ void epilogue_cols(const Epilogue& ep, EpiWarp& io, u
   }
 }
 
+template <int TBN = BN>
 __device__ __forceinline__ void epilogue_tile(const Epilogue& ep, EpiWarp& io, uint32_t taddr,
                                               uint8_t* stage, const float* bias_s, int row0, int n0,
                                               int cbase) {
-  if (ep.out_fp32) epilogue_cols<float>(ep, io, taddr, stage, bias_s, row0, n0, cbase);
-  else epilogue_cols<__nv_bfloat16>(ep, io, taddr, stage, bias_s, row0, n0, cbase);
+  if (ep.out_fp32) epilogue_cols<float, TBN>(ep, io, taddr, stage, bias_s, row0, n0, cbase);
+  else epilogue_cols<__nv_bfloat16, TBN>(ep, io, taddr, stage, bias_s, row0, n0, cbase);
 }
 
 // ---- the kernel ------------------------------------------------------------------
 
+// TBN: output tile width (256, or 128 / 64 when wider tiles would leave SMs idle).
+template <int TBN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_out,
@@ -490,7 +505,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                                              ~static_cast<uintptr_t>(1023));
   // Layout: operand stages | epilogue staging (1 KB aligned, as the 64-byte TMA
   // swizzle of the stores requires) | barriers | bias.
-  uint8_t* epi_stage = smem + STAGES * STAGE_BYTES;
+  constexpr int kStage = g_stage_bytes(TBN);
+  constexpr uint32_t kTmemCols = 2 * TBN;  // two accumulators
+  uint8_t* epi_stage = smem + STAGES * kStage;
   uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
@@ -505,7 +522,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   int r0, m_rows;
   row_window(ep, r0, m_rows);
   const int tiles_m = (m_rows + BM - 1) / BM;
-  const int tiles_n = (ep.n + BN - 1) / BN;
+  const int tiles_n = (ep.n + TBN - 1) / TBN;
   const int tiles = tiles_m * tiles_n;
   const int k_tiles = (ep.k + BK - 1) / BK;
 
@@ -525,7 +542,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_holder)),
-                 "r"(TMEM_COLS));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   fence_before();
@@ -546,10 +563,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             failed = true;
             break;
           }
-          uint8_t* sa = smem + stage * STAGE_BYTES;
-          mbar_expect_tx(&full[stage], STAGE_BYTES);
+          uint8_t* sa = smem + stage * kStage;
+          mbar_expect_tx(&full[stage], kStage);
           tma_load_2d(&map_a, &full[stage], sa, kt * BK, r0 + tm * BM);
-          tma_load_2d(&map_w, &full[stage], sa + A_BYTES, kt * BK, tn * BN);
+          tma_load_2d(&map_w, &full[stage], sa + A_BYTES, kt * BK, tn * TBN);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -564,7 +581,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---- MMA issuer ----
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(BM, BN);
+      constexpr uint32_t idesc = instr_desc(BM, TBN);
       int stage = 0;
       uint32_t phase = 0;
       int iter = 0;
@@ -576,14 +593,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * TBN);
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&full[stage], phase)) {
             failed = true;
             break;
           }
           fence_after();
-          const uint32_t a_addr = smem_addr(smem + stage * STAGE_BYTES);
+          const uint32_t a_addr = smem_addr(smem + stage * kStage);
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
@@ -606,25 +623,25 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ---- epilogue: warps 2..9 (two per TMEM lane quadrant) ----
     const int quad = epi_quad(warp);
-    const int cbase = epi_col0(warp);
+    const int cbase = epi_col0<TBN>(warp);
     const int epi_tid = threadIdx.x - 64;  // 0..255
     uint8_t* stage = epi_stage + (warp - 2) * 2 * EPI_BUF;
     EpiWarp io{&map_out, &map_res, res_bars + 2 * (warp - 2), 0u, true};
     int iter = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
       const int tm = t / tiles_n, tn = t - tm * tiles_n;
-      const int n0 = tn * BN;
+      const int n0 = tn * TBN;
       const int buf = iter & 1;
       const uint32_t use = static_cast<uint32_t>(iter >> 1);
       const int row0 = r0 + tm * BM + quad * 32;
-      epilogue_begin(ep, io, stage, bias_s, epi_tid, row0, n0, cbase);
+      epilogue_begin<TBN>(ep, io, stage, bias_s, epi_tid, row0, n0, cbase);
       if (!epilogue_wait(&acc_full[buf], use & 1u)) {
         failed = true;
         break;
       }
-      epilogue_tile(ep, io,
-                    tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                        static_cast<uint32_t>(buf * BN),
+      epilogue_tile<TBN>(ep, io,
+                         tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(buf * TBN),
                     stage, bias_s, row0, n0, cbase);
       if (!io.ok) failed = true;
       fence_before();
@@ -646,7 +663,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     __syncwarp();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(TMEM_COLS));
+                 "r"(kTmemCols));
   }
 }
 
@@ -1005,8 +1022,12 @@ int gemm_launch(const void* a, int64_t lda, const void* w, int64_t ldw, const vo
   static bool attr_set[64] = {};
   if (dev < 0 || dev >= 64) return CUGO_B200_ERR_LAUNCH;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess ||
+    if (cudaFuncSetAttribute(gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             g_smem_bytes(256)) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             g_smem_bytes(128)) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             g_smem_bytes(64)) != cudaSuccess ||
         cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              P_SMEM_BYTES) != cudaSuccess)
       return CUGO_B200_ERR_LAUNCH;
@@ -1025,22 +1046,45 @@ int gemm_launch(const void* a, int64_t lda, const void* w, int64_t ldw, const vo
   } else {
     mr = mo;  // unused
   }
-  // The pair kernel halves the weight bytes each SM streams per FLOP, which pays
-  // when the K loop is long (measured: 262144x2048x2048 1,425 vs 1,317 TFLOP/s);
-  // with K <= 720 the epilogue bounds both kernels and the single one is faster.
-  const bool pair = !window && m > BM && k >= 1024 && pair_kernel_enabled();
-  if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, pair ? P_BN_HALF : BN))
+  // Tile shape.  Wide tiles read each A tile fewer times per FLOP, so the single-CTA
+  // kernel takes the widest output tile (256, then 128 columns, else 64) whose tiles
+  // reach 60% of the SMs: narrower tiles pay only when wide ones would leave most SMs
+  // idle (measured in CUDA graphs on B200: a 4,096 x 256 x 256 layer, 32 wide tiles,
+  // 9.7 us at 256 columns and 5.7 us at 64; 4,096 x 768 x 256, 96 wide tiles, 7.1 us
+  // at 256 and 7.6-8.0 us narrower; 32,768 x 512 x 512 21 us at 256, 25 us at 128).
+  // The pair kernel halves the weight bytes each SM streams per FLOP, which pays when
+  // the K loop is long and its 256 x 256 tiles fill every pair at least once
+  // (262144x2048x2048 1,425 vs 1,317 TFLOP/s; but 4,096 x 256 x 1,024, 16 pair tiles,
+  // 14.1 us against 9.2 us for 64-column single tiles).
+  const int sms = sm_count();
+  const int64_t tiles_m = (m + BM - 1) / BM;
+  const int64_t enough = (3 * static_cast<int64_t>(sms)) / 5;
+  int tbn = 64;
+  for (int cand : {256, 128}) {
+    if (tiles_m * ((n + cand - 1) / cand) >= enough) {
+      tbn = cand;
+      break;
+    }
+  }
+  const int64_t pair_tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
+  const bool pair = !window && m > BM && k >= 1024 && pair_kernel_enabled() &&
+                    pair_tiles >= max_pairs(dev);
+  if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, pair ? P_BN_HALF : tbn))
     return CUGO_B200_ERR_LAUNCH;
   if (pair) {
     // 256 x 256 tiles, one CTA pair per tile, persistent over the co-resident pairs.
-    const int64_t tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
-    const int64_t pairs = tiles < max_pairs(dev) ? tiles : max_pairs(dev);
+    const int64_t pairs = pair_tiles < max_pairs(dev) ? pair_tiles : max_pairs(dev);
     gemm_pair_kernel<<<static_cast<unsigned>(2 * pairs), THREADS, P_SMEM_BYTES, stream>>>(
         ma, mw, mo, mr, ep);
   } else {
-    const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
-    const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mw, mo, mr, ep);
+    const int64_t tiles = tiles_m * ((n + tbn - 1) / tbn);
+    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    if (tbn == 256)
+      gemm_kernel<256><<<grid, THREADS, g_smem_bytes(256), stream>>>(ma, mw, mo, mr, ep);
+    else if (tbn == 128)
+      gemm_kernel<128><<<grid, THREADS, g_smem_bytes(128), stream>>>(ma, mw, mo, mr, ep);
+    else
+      gemm_kernel<64><<<grid, THREADS, g_smem_bytes(64), stream>>>(ma, mw, mo, mr, ep);
   }
   return cudaGetLastError() == cudaSuccess ? CUGO_B200_OK : CUGO_B200_ERR_LAUNCH;
 }

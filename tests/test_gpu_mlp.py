@@ -37,12 +37,18 @@ def _rand(shape, scale=1.0, seed=0):
     (777, 180, 512, 0, 0, False, True),       # head, fp32 out, ragged N
     (128, 64, 720, 2, 0, False, False),       # narrow layer
     (300_000, 512, 512, 1, 0, False, False),  # many persistent tiles per SM
+    (4096, 256, 256, 0, 0, False, False),     # 64-column tiles (32 wide ones for 148 SMs)
+    (8192, 256, 256, 2, 0, False, False),     # 128-column tiles
+    (4096, 256, 1024, 0, 0, True, True),      # long K, fp32 residual: 64-column tiles, not pairs
+    (1000, 200, 256, 1, 0, True, False),      # narrow tiles with ragged N and a residual
 ])
 def test_linear_matches_fp32(ext, m, n, k, act, act_after, res, fp32):
     a = _rand((m, k), 1.0, 1)
     w = _rand((n, k), (2.0 / k) ** 0.5, 2)
     b = _rand((n,), 0.1, 3)
     r = _rand((m, n), 1.0, 4) if res else None
+    if res and fp32:  # the residual has the output's dtype
+        r = r.float()
     err = torch.zeros(1, dtype=torch.int32, device=DEV)
     out = ext.linear(a, w, b, residual=r.clone() if res else None, act=act, act_after=act_after,
                      out_dtype=torch.float32 if fp32 else torch.bfloat16, error=err)
