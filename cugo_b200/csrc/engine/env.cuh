@@ -147,6 +147,43 @@ CB_UNROLL
   return m;
 }
 
+// primary_legal(g).has(action) without building the mask: the step needs only the
+// one action's bit, and the mask's month sets (bombs, grenades, shakes over all twelve
+// months) cost more than the rest of a plain play's legality.  The same rules for the
+// action's own month.
+CB_HD bool primary_action_legal(const Game& g, u32 action) {
+  const u32 kind = decision_kind(g);
+  if (kind == kDecChongtong) return action == 125u || action == 126u;
+  if (kind == kDecGoStop) return action == 123u || action == 124u;
+  if (kind != kDecPrimary || g.stock() == 0) return false;
+  const u32 a = g.actor();
+  const Mask hand = g.hand(a);
+  if (action >= 48u && action < 50u) return (hand & card_bit(action)) != 0;  // bonus play
+  if (action == 122u) return g.credits(a) != 0;
+  if (action >= 123u) return false;
+  // A card play (0..47), shake (50..97), bomb (98..109) or grenade (110..121): the
+  // counts of the month's cards in hand and on the floor decide.
+  u32 month, card = kNoCard;
+  if (action < 48u) card = action;
+  else if (action < 98u) card = action - 50u;
+  if (card != kNoCard) {
+    if (!(hand & card_bit(card))) return false;
+    month = card_month(card);
+  } else {
+    month = action < 110u ? action - 98u : action - 110u;
+  }
+  const Mask mc = month_cards(month);
+  const u32 in_hand = popc(hand & mc), on_floor = popc(g.floor_std() & mc);
+  const bool bomb = in_hand == 3u && on_floor == 1u;
+  const bool grenade = in_hand == 2u && on_floor == 2u;
+  const u32 mb = 1u << month;
+  if (action < 48u) return !(bomb || grenade);  // forced months take no single play
+  if (action < 98u)
+    return on_floor == 0u && ((in_hand == 3u && !(g.shaken(a) & mb)) ||
+                              (in_hand == 4u && !(g.shaken4(a) & mb)));
+  return action < 110u ? bomb : grenade;
+}
+
 // ---- pending floor choices (cugo/game/postchance50.h:150-456) ----------------
 //
 // A primary action whose flipped card leaves a two-card floor choice stays
@@ -775,12 +812,10 @@ CB_HD StepOut step_game(Game& g, u32 action) {
     return StepOut{kFinished, reward0(g), g.done(), g.nagari(), 0};
   }
   const bool choosing = g.pend_active() != 0;
-  if (!choosing) {  // torch_legal without a pending probe
-    const u32 kind = decision_kind(g);
-    Legal legal;
-    if (kind == kDecGukjin) legal.w2 = (u64{1} << (177 - 128)) | (u64{1} << (178 - 128));
-    else legal = primary_legal(g);
-    if (!legal.has(action)) {
+  if (!choosing) {  // torch_legal without a pending probe, for this action only
+    const bool ok = decision_kind(g) == kDecGukjin ? (action == 177u || action == 178u)
+                                                     : primary_action_legal(g, action);
+    if (!ok) {
       g.set_status(kNotLegal);
       return StepOut{kNotLegal, 0, g.done(), g.nagari(), 0};
     }

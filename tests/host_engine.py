@@ -77,6 +77,15 @@ def step(rows, actions, events: bool = False):
     return out + (ev,) if events else out
 
 
+def legal_check(rows):
+    """Per row, the first action (0..255) on which the step's single-action legality
+    check disagrees with the primary legal mask, or -1."""
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    out = np.zeros(rows.shape[0], dtype=np.int32)
+    lib().cugo_host_legal_check(_p(rows), ctypes.c_int64(rows.shape[0]), _p(out))
+    return out
+
+
 def start(rows):
     rows = np.ascontiguousarray(rows, dtype=np.uint8)
     out = np.zeros((rows.shape[0], START_WORDS), dtype=np.int64)

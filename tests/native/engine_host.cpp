@@ -88,4 +88,20 @@ void cugo_host_philox(const uint32_t* ctr, const uint32_t* key, uint32_t* out) {
   for (int i = 0; i < 4; ++i) out[i] = p.v[i];
 }
 
+// Rows at which primary_action_legal disagrees with the primary legal mask (every
+// action 0..255 of every row); mismatches[i] = the first such action or -1.
+void cugo_host_legal_check(const uint8_t* rows, int64_t n, int32_t* mismatches) {
+  for (int64_t i = 0; i < n; ++i) {
+    const Game g = load(rows + i * kRowBytes);
+    const Legal m = primary_legal(g);
+    mismatches[i] = -1;
+    for (uint32_t a = 0; a < 256; ++a) {
+      if (m.has(a) != primary_action_legal(g, a)) {
+        mismatches[i] = static_cast<int32_t>(a);
+        break;
+      }
+    }
+  }
+}
+
 }  // extern "C"

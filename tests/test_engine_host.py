@@ -20,6 +20,30 @@ def test_random_play_matches_oracle(oracle, family, salt):
     assert all(stats["kinds"][k] > 0 for k in required), stats["kinds"]
 
 
+def test_single_action_legality_matches_the_mask():
+    """The step checks one action's legality without building the legal mask; on every
+    decision of seeded random games (and on rows with a pile of specials: shakes,
+    bombs, grenades, credits) it agrees with the mask for all 256 action values."""
+    seeds, first = dif.seeds_for(0, 2048, 0)
+    rows = he.create(seeds, first)
+    rng = np.random.default_rng(7)
+    checked = 0
+    for _ in range(40):
+        assert (he.legal_check(rows) == -1).all()
+        checked += rows.shape[0]
+        _, legal, _, done, _ = he.observe(rows)
+        live = ~done & legal.any(1)
+        if not live.any():
+            break
+        rows = rows[live]
+        legal = legal[live]
+        # Prefer special plays (98..122) when offered, so their rules are exercised.
+        u = rng.random(legal.shape) + np.where(np.arange(179) >= 98, 0.5, 0.0) * (rng.random() < 0.5)
+        actions = np.where(legal, u, -1.0).argmax(1).astype(np.int64)
+        rows = he.step(rows, actions)[0]
+    assert checked > 40_000
+
+
 def test_golden_steps(golden):
     g = golden("steps")
     f, legal, player, done, status = he.observe(g["rows"])
