@@ -152,6 +152,31 @@ __device__ __forceinline__ i64 device_rows(const int32_t* m_dev, i64 m) {
   return md < 0 ? 0 : (md < m ? md : m);
 }
 
+// Rule path a row's step takes, for the block's partition of its rows: 0 a card play,
+// 1 a bonus play, 2 a shake, bomb, grenade or bomb credit, 3 a floor choice, 4 a
+// prompt answer, a finished row or an action outside the primary range, 5 no row.
+__device__ __forceinline__ int step_path(const u64* row, u32 action, bool live) {
+  if (!live) return 5;
+  Game g;  // only the two words read below
+  g.w[27] = row[27];
+  g.w[29] = row[29];
+  if (g.done()) return 4;
+  if (g.pend_active()) return 3;
+  if (action < 48u) return 0;
+  if (action < 50u) return 1;
+  if (action <= 122u) return 2;
+  return 4;
+}
+constexpr int kStepPaths = 6;
+
+// kPartition: a block's 128 rows are stepped in the order of their rule path (a
+// stable counting sort through shared memory), so a warp runs mostly one path of the
+// rules instead of every path its rows take (rows in random order with random legal
+// actions: a warp of 32 almost always mixes card plays with a choice or a special
+// play); each warp then writes the rows it stepped straight to their destinations.
+// Without it (the self-play round tail, whose running list is already grouped by next
+// decision) every warp steps its own 32 rows and the round's bookkeeping follows.
+template <bool kPartition>
 __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
     u64* __restrict__ states, i64 n_states, const i64* __restrict__ ids,
     const i64* __restrict__ actions, i64 m, u64* __restrict__ children,
@@ -161,36 +186,85 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
   m = device_rows(tail.m_dev, m);
   if ((i64)blockIdx.x * kBlock >= m) return;  // past a device count: nothing to write
   WarpTile& t = my_tile();
+  const int lane = threadIdx.x & 31;
   const i64 row = (i64)blockIdx.x * kBlock + threadIdx.x;
   const i64 src = lane_source(ids, row, m, n_states);
   gather_rows(t, states, src);
+  const u32 action = src >= 0 ? torch_action(__ldg(actions + row)) : kNoAction;
+  // The row this thread steps: its own, or with kPartition its place in path order.
+  int mine = threadIdx.x;
+  i64 msrc = src;
+  u32 maction = action;
+  if constexpr (kPartition) {
+    __shared__ i64 src_s[kBlock];
+    __shared__ u32 action_s[kBlock];
+    __shared__ int16_t perm[kBlock];
+    __shared__ int path_count[kWarpsPerBlock][kStepPaths];
+    const int warp = threadIdx.x >> 5;
+    src_s[threadIdx.x] = src;
+    action_s[threadIdx.x] = action;
+    const int path = step_path(t.rows[lane], action, src >= 0);
+    int rank = 0;
+#pragma unroll
+    for (int c = 0; c < kStepPaths; ++c) {
+      const unsigned b = __ballot_sync(kFull, path == c);
+      if (lane == 0) path_count[warp][c] = __popc(b);
+      if (path == c) rank = __popc(b & ((1u << lane) - 1u));
+    }
+    __syncthreads();  // every tile gathered, every warp's counts written
+    int at = rank;
+    for (int c = 0; c < path; ++c)
+#pragma unroll
+      for (int w = 0; w < kWarpsPerBlock; ++w) at += path_count[w][c];
+    for (int w = 0; w < warp; ++w) at += path_count[w][path];
+    perm[at] = static_cast<int16_t>(threadIdx.x);
+    __syncthreads();
+    mine = perm[threadIdx.x];
+    msrc = src_s[mine];
+    maction = action_s[mine];
+  }
+  WarpTile& mt = tile_of_block_row(mine);
+  const int mr = mine & 31;
+  const i64 mrow = (i64)blockIdx.x * kBlock + mine;
   Game g;
-  load_game(t, g);
-  __syncwarp();
+  load_game_row(mt, mr, g);
   StepOut out{static_cast<u32>(-1), 0, 1, 0, 0};
   i64 ev[kEventWords];
 #pragma unroll
   for (int k = 0; k < (int)kEventWords; ++k) ev[k] = 0;
-  if (src >= 0) {
+  if (msrc >= 0) {
     const EventBase before = event_base(g);
-    out = step_game(g, torch_action(__ldg(actions + row)));
+    out = step_game(g, maction);
     if (events && out.committed) event_words(before, g, ev);
   } else if (children) {
     for (int k = 0; k < kRowWords; ++k) g.w[k] = 0;
   }
-  store_game(t, g);
-  const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
-  if (children) store_tile(t, children, tile_base, m, row < m ? row : -1);
-  else if (!ids) store_tile(t, states, tile_base, m, src);  // in place, rows in order
-  else scatter_rows(t, states, src);
-  if (tail.keep) {  // ids are distinct (one row per game)
-    const i64 id = src;
+  store_game_row(mt, mr, g);
+  if constexpr (kPartition) {
+    // This warp's 32 stepped rows, one 248-byte row per pass, to their destinations.
+    __syncwarp();
+    const i64 dst = children ? (mrow < m ? mrow : -1) : msrc;
+    u64* base = children ? children : states;
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r) {
+      const int br = __shfl_sync(kFull, mine, r);
+      const i64 d = __shfl_sync(kFull, dst, r);
+      if (d >= 0 && lane < kRowWords)
+        base[d * kRowWords + lane] = tile_of_block_row(br).rows[br & 31][lane];
+    }
+  } else {
+    const i64 tile_base = (i64)blockIdx.x * kBlock + (threadIdx.x & ~31);
+    if (children) store_tile(t, children, tile_base, m, row < m ? row : -1);
+    else if (!ids) store_tile(t, states, tile_base, m, src);  // in place, rows in order
+    else scatter_rows(t, states, src);
+  }
+  if (!kPartition && tail.keep) {  // ids are distinct (one row per game)
     const bool fin = src >= 0 && out.done != 0;
     if (src >= 0) {
-      tail.decision[id] += 1;
+      tail.decision[src] += 1;
       if (fin) {
-        tail.reward0[id] = static_cast<float>(out.reward0);
-        tail.nagari[id] = out.nagari != 0;
+        tail.reward0[src] = static_cast<float>(out.reward0);
+        tail.nagari[src] = out.nagari != 0;
       }
       const u32 st = static_cast<u32>(out.status);
       if (st != kOk && st != kFinished) atomicAdd(reinterpret_cast<unsigned long long*>(tail.bad), 1ull);
@@ -199,25 +273,25 @@ __global__ void __launch_bounds__(kBlock, CB_ENGINE_MIN_BLOCKS) step_kernel(
     const i64 w = ((i64)blockIdx.x * kBlock + (threadIdx.x & ~31)) >> 5;
     if (tail.groups == 1) {
       const unsigned mask = __ballot_sync(kFull, running);
-      if ((threadIdx.x & 31) == 0 && w * 32 < m) tail.keep[w] = mask;
+      if (lane == 0 && w * 32 < m) tail.keep[w] = mask;
     } else {
       const int grp = running ? next_decision_group(g) : -1;
 #pragma unroll
       for (int q = 0; q < 3; ++q) {
         const unsigned mask = __ballot_sync(kFull, grp == q);
-        if ((threadIdx.x & 31) == 0 && w * 32 < m) tail.keep[q * tail.stride + w] = mask;
+        if (lane == 0 && w * 32 < m) tail.keep[q * tail.stride + w] = mask;
       }
     }
   }
-  if (row < m && reward) {  // internal callers may skip the per-row outputs
-    reward[row] = static_cast<float>(out.reward0);
-    done[row] = out.done != 0;
-    nagari[row] = out.nagari != 0;
-    status[row] = static_cast<int16_t>(static_cast<i32>(out.status));
-    committed[row] = out.committed != 0;
+  if (mrow < m && reward) {  // internal callers may skip the per-row outputs
+    reward[mrow] = static_cast<float>(out.reward0);
+    done[mrow] = out.done != 0;
+    nagari[mrow] = out.nagari != 0;
+    status[mrow] = static_cast<int16_t>(static_cast<i32>(out.status));
+    committed[mrow] = out.committed != 0;
     if (events) {
 #pragma unroll
-      for (int k = 0; k < (int)kEventWords; ++k) events[row * kEventWords + k] = ev[k];
+      for (int k = 0; k < (int)kEventWords; ++k) events[mrow * kEventWords + k] = ev[k];
     }
   }
 }
@@ -741,7 +815,7 @@ int cugo_b200_observe_indexed(const uint8_t* states, int64_t n_states, const int
 // drivers in other translation units (not part of the C ABI).
 int cb_step_in_place(uint8_t* states, int64_t n, const int64_t* actions, cudaStream_t stream) {
   if (n <= 0) return CUGO_B200_OK;
-  step_kernel<<<blocks_for(n, kBlock), kBlock, 0, stream>>>(
+  step_kernel<true><<<blocks_for(n, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<u64*>(states), n, nullptr, actions, n, nullptr, nullptr, nullptr, nullptr,
       nullptr, nullptr, nullptr);
   return launch_status();
@@ -759,7 +833,7 @@ static int step_common(uint8_t* states, int64_t n_states, const int64_t* env_ids
   if (m > 0 && n_states > 0 && !states) return CUGO_B200_ERR_ARG;
   if (!aligned(states, 8) || !aligned(children, 8) || !aligned(events, 8)) return CUGO_B200_ERR_ALIGN;
   if (m == 0) return CUGO_B200_OK;
-  step_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+  step_kernel<true><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<u64*>(states), n_states, env_ids, actions, m,
       reinterpret_cast<u64*>(children), reward, done, nagari, status, committed, events);
   return launch_status();
@@ -799,7 +873,7 @@ static int step_compact_common(uint8_t* states, int64_t n_states, const int64_t*
   int32_t* offsets = scratch + groups * warps;
   if (m_dev == next_count) return CUGO_B200_ERR_ARG;  // the count is rewritten mid-call
   RoundTail tail{decision, reward0, nagari, bad, keep, m_dev, groups, warps};
-  step_kernel<<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
+  step_kernel<false><<<blocks_for(m, kBlock), kBlock, 0, stream>>>(
       reinterpret_cast<u64*>(states), n_states, env_ids, actions, m, nullptr, nullptr, nullptr,
       nullptr, nullptr, nullptr, nullptr, tail);
   compact_scan_kernel<<<1, 1024, 0, stream>>>(keep, m, m_dev, offsets, next_count, groups, warps);

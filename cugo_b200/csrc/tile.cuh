@@ -36,10 +36,15 @@ struct alignas(16) WarpTile {
 };
 static_assert(sizeof(WarpTile) <= 9 * 1024, "tile fits the shared budget");
 
-__device__ __forceinline__ WarpTile& my_tile() {
+__device__ __forceinline__ WarpTile* block_tiles() {
   __shared__ WarpTile tiles[kWarpsPerBlock];
-  return tiles[threadIdx.x >> 5];
+  return tiles;
 }
+
+__device__ __forceinline__ WarpTile& my_tile() { return block_tiles()[threadIdx.x >> 5]; }
+
+// The tile holding row r (0..127) of the block.
+__device__ __forceinline__ WarpTile& tile_of_block_row(int r) { return block_tiles()[r >> 5]; }
 
 // Row id this lane's game reads: ids[row] for indexed ops, row itself otherwise;
 // -1 past the end of the batch or for an id outside [0, n_states).
@@ -135,6 +140,18 @@ __device__ __forceinline__ void store_game(WarpTile& t, Game g) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int k = 0; k < kRowWords; ++k) t.rows[lane][k] = g.w[k];
+}
+
+// Row r of a tile (another lane's, or another warp's tile).
+__device__ __forceinline__ void load_game_row(const WarpTile& t, int r, Game& g) {
+#pragma unroll
+  for (int k = 0; k < kRowWords; ++k) g.w[k] = t.rows[r][k];
+}
+
+__device__ __forceinline__ void store_game_row(WarpTile& t, int r, Game g) {
+  zero_padding(g);
+#pragma unroll
+  for (int k = 0; k < kRowWords; ++k) t.rows[r][k] = g.w[k];
 }
 
 // This lane's packet slice of the tile (valid once every lane has loaded its row).
