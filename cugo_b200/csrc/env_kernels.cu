@@ -495,11 +495,31 @@ __global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __re
   const i64 per = (warps + blockDim.x - 1) / blockDim.x;  // consecutive warps per thread
   const i64 w0 = t * per;
   const i64 w1 = w0 + per < warps ? w0 + per : warps;
+  // A thread's words move as 16-byte vectors when its whole span [w0, w0 + per) lies
+  // in the arrays and starts 16-byte aligned (words past the row count read as zero;
+  // their offsets are written but never read): a warp's loads and stores then touch a
+  // quarter of the sectors the word-by-word loop does.
+  const bool vec = per % 4 == 0 && stride % 4 == 0 && w0 < warps && w0 + per <= stride &&
+                   (reinterpret_cast<uintptr_t>(keep) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(offsets) & 15u) == 0;
   int32_t mine[kMaxGroups] = {0, 0, 0};
-  for (i64 w = w0; w < w1; ++w) {
+  if (vec) {
+    for (i64 w = w0; w < w0 + per; w += 4) {
 #pragma unroll
-    for (int q = 0; q < kMaxGroups; ++q)
-      if (q < groups) mine[q] += __popc(__ldg(keep + q * stride + w));
+      for (int q = 0; q < kMaxGroups; ++q) {
+        if (q < groups) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(keep + q * stride + w));
+          mine[q] += (w < warps ? __popc(v.x) : 0) + (w + 1 < warps ? __popc(v.y) : 0) +
+                     (w + 2 < warps ? __popc(v.z) : 0) + (w + 3 < warps ? __popc(v.w) : 0);
+        }
+      }
+    }
+  } else {
+    for (i64 w = w0; w < w1; ++w) {
+#pragma unroll
+      for (int q = 0; q < kMaxGroups; ++q)
+        if (q < groups) mine[q] += __popc(__ldg(keep + q * stride + w));
+    }
   }
   int32_t incl[kMaxGroups];
 #pragma unroll
@@ -538,12 +558,30 @@ __global__ void __launch_bounds__(1024) compact_scan_kernel(const uint32_t* __re
       run[q] = 0;
     }
   }
-  for (i64 w = w0; w < w1; ++w) {
+  if (vec) {
+    for (i64 w = w0; w < w0 + per; w += 4) {
 #pragma unroll
-    for (int q = 0; q < kMaxGroups; ++q) {
-      if (q < groups) {
-        offsets[q * stride + w] = run[q];
-        run[q] += __popc(__ldg(keep + q * stride + w));
+      for (int q = 0; q < kMaxGroups; ++q) {
+        if (q < groups) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(keep + q * stride + w));
+          int4 o;
+          o.x = run[q];
+          o.y = o.x + (w < warps ? __popc(v.x) : 0);
+          o.z = o.y + (w + 1 < warps ? __popc(v.y) : 0);
+          o.w = o.z + (w + 2 < warps ? __popc(v.z) : 0);
+          run[q] = o.w + (w + 3 < warps ? __popc(v.w) : 0);
+          *reinterpret_cast<int4*>(offsets + q * stride + w) = o;
+        }
+      }
+    }
+  } else {
+    for (i64 w = w0; w < w1; ++w) {
+#pragma unroll
+      for (int q = 0; q < kMaxGroups; ++q) {
+        if (q < groups) {
+          offsets[q * stride + w] = run[q];
+          run[q] += __popc(__ldg(keep + q * stride + w));
+        }
       }
     }
   }
