@@ -260,6 +260,43 @@ class SeqDecoder:
             ext.linear(f, L.w2, L.b2, residual=x, out=x)
         return x
 
+    def cached_step_segments(self, cache: SeqKVCache, x: torch.Tensor,
+                             segments: list[tuple[int, torch.Tensor | None, torch.Tensor]]
+                             ) -> torch.Tensor:
+        """cached_step over consecutive row segments of x fp32 [n, d] (updated in place
+        and returned) that share every layer's LayerNorm and GEMM launches.  segments =
+        [(count, rows, positions)]: the segment's tokens go to cache rows `rows`
+        (default 0..count-1) at slot min(positions[row], slots - 1).  At every layer the
+        segments' attention launches (each with its KV append) run in order, so a later
+        segment sees the slots an earlier one appended exactly as if it had run as its
+        own pass after it; every other layer computes each row on its own, so each
+        row's result is cached_step's."""
+        ext = self.ext
+        n, d = x.shape
+        heads, dh = self.heads, d // self.heads
+        if sum(c for c, _, _ in segments) != n:
+            raise ValueError("the segments must cover the rows of x")
+        clamp = cache.slots - 1
+        att = torch.empty((n, d), dtype=torch.bfloat16, device=x.device)
+        for i, L in enumerate(self.blocks):
+            a = ext.layernorm(x, L.norm1_w, L.norm1_b, self.eps)
+            qkv = ext.linear(a, L.w_in, L.b_in)
+            q = qkv[:, :d].view(n, heads, dh)
+            k = qkv[:, d:2 * d].view(n, heads, dh)
+            v = qkv[:, 2 * d:].view(n, heads, dh)
+            s0 = 0
+            for count, rows, positions in segments:
+                s1 = s0 + count
+                ext.decode_attention(q[s0:s1], cache.k[i], cache.v[i], positions, rows=rows,
+                                     k_new=k[s0:s1], v_new=v[s0:s1], pos_clamp=clamp,
+                                     out=att[s0:s1].view(count, heads, dh))
+                s0 = s1
+            ext.linear(att, L.w_out, L.b_out, residual=x, out=x)
+            a = ext.layernorm(x, L.norm2_w, L.norm2_b, self.eps)
+            f = ext.linear(a, L.w1, L.b1, act=ACT_GELU)
+            ext.linear(f, L.w2, L.b2, residual=x, out=x)
+        return x
+
     # -- training forward over whole games ---------------------------------------
     def forward_games(self, hist, features: torch.Tensor, legal: torch.Tensor,
                       seen: torch.Tensor, length: int | None = None) -> torch.Tensor:

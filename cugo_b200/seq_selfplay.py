@@ -7,14 +7,23 @@ in the batch and are skipped by the kernels' bookkeeping).  Two CUDA graphs:
 
   reset  deal the wave's games, their opening records and opening tokens (both
          seats' caches; the pool opponent's cache for pool games), zero the logs
-  step   observe every game into the query rows; the query token through the
-         cached transformer on the mover's cache row and the readout (and, in pool
-         games where the opponent moves, the opponent network on its own cache);
+  step   observe every game into the query rows; one pass of the cached
+         transformer over the tokens the previous step left (its event's tokens for
+         both seats' caches; at a wave's first step the opening tokens) and the query
+         tokens on the mover's cache row, and the readout (and, in pool games where
+         the opponent moves, the same for the opponent network on its own cache);
          Gumbel-max sampling; the engine step with its event words; the event's
-         tokens into both seats' caches (and the opponent's); then one wave-tail
-         kernel does the rest of the step's bookkeeping on the device: bad-status
-         counts, final rewards, the event log, the per-decision records, the cache
-         lengths, event counts and decision counters, and the wave's running count
+         tokens embedded for the next step's pass; then one wave-tail kernel does the
+         rest of the step's bookkeeping on the device: bad-status counts, final
+         rewards, the event log, the per-decision records, the cache lengths, event
+         counts and decision counters, and the wave's running count
+
+One pass per step: the event tokens of step s and the query tokens of step s + 1
+share every layer's LayerNorm and GEMM launches (rows 0 .. 2w - 1 and 2w .. 3w - 1
+of one residual stream), with the events' attention (and cache append) before the
+queries' at every layer -- the same arithmetic per row as an event pass followed by
+a query pass, at half the launches.  The events of a wave's last step are never
+embedded into the cache: no query follows them.
 
 The host replays the step graph and, every 4 steps, copies the running count into
 pinned memory behind an event and reads it; the wave ends at the first copy that
@@ -59,6 +68,10 @@ class SeqWaveSelfPlay:
         self.start = torch.zeros((w, self.ext.START_WORDS), **i64)
         self.cache = decoder.new_cache(2 * w)  # row = seat * w + game
         self.query = torch.zeros((w, QUERY_LD), dtype=torch.bfloat16, device=dev)
+        # The step's residual stream: the previous step's tokens for both seats' cache
+        # rows, then the query rows; and the slots those tokens go to.
+        self.x = torch.zeros((3 * w, decoder.d_model), dtype=torch.float32, device=dev)
+        self.prev_pos = torch.zeros(2 * w, **i64)
         self.started = torch.zeros(w, dtype=torch.bool, device=dev)
         # Device state the wave-tail kernel updates.
         self.state = {
@@ -84,6 +97,8 @@ class SeqWaveSelfPlay:
         if self.pool:
             p = self.pool
             self.opp_cache = opponent.new_cache(p)  # row = pool game (the opponent's seat)
+            self.opp_x = torch.zeros((2 * p, opponent.d_model), dtype=torch.float32, device=dev)
+            self.opp_prev_pos = torch.zeros(p, **i64)
             self.learner_seat = (self.ids[:p] >> 1) & 1
             self.opp_seat = 1 - self.learner_seat
             self.learner = torch.ones(w, dtype=torch.bool, device=dev)
@@ -133,27 +148,30 @@ class SeqWaveSelfPlay:
         st["running"].copy_(self.started.sum())
         if self.records is not None:
             self.records["valid"].zero_()
-        self.cache.length.zero_()
-        dec.cached_step(self.cache, dec.start_token(self.start, self.seats2), slots=1)
+        # The opening tokens go to slot 0 in the first step's pass.
+        dec.start_token(self.start, self.seats2, out=self.x[:2 * self.w])
+        self.prev_pos.zero_()
         self.cache.length.fill_(1)
         if self.pool:
             p = self.pool
-            self.opp_cache.length.zero_()
             opp = self.opponent
-            opp.cached_step(self.opp_cache, opp.start_token(self.start[:p], self.opp_seat), slots=1)
+            opp.start_token(self.start[:p], self.opp_seat, out=self.opp_x[:p])
+            self.opp_prev_pos.zero_()
             self.opp_cache.length.fill_(1)
 
     def _step(self) -> None:
         ext, dec, w, ids, st = self.ext, self.dec, self.w, self.ids, self.state
         query, legal, players, done, status = ext.observe_query_bf16(self.states, ids, query=self.query)
         seat = players.long() & 1
-        x = dec.query_token(query)
-        dec.cached_step(self.cache, x, rows=seat * w + ids)
+        x = dec.query_token(query, out=self.x[2 * w:])
+        dec.cached_step_segments(self.cache, self.x, [(2 * w, None, self.prev_pos),
+                                                      (w, seat * w + ids, self.cache.length)])
         logits = dec.readout(x)
         if self.pool:
             p, opp = self.pool, self.opponent
-            xo = opp.query_token(query[:p])
-            opp.cached_step(self.opp_cache, xo)
+            xo = opp.query_token(query[:p], out=self.opp_x[p:])
+            opp.cached_step_segments(self.opp_cache, self.opp_x,
+                                     [(p, None, self.opp_prev_pos), (p, None, self.opp_cache.length)])
             theirs = seat[:p] != self.learner_seat
             logits[:p] = torch.where(theirs.unsqueeze(1), opp.readout(xo)[:, :logits.shape[1]],
                                      logits[:p])
@@ -166,11 +184,14 @@ class SeqWaveSelfPlay:
         step_out = ext.step_events_indexed(self.states, ids, actions)
         events = step_out[5]
         # The event's tokens for both seats (row i of 2w reads event i % w), at the
-        # games' event counts before this step.
-        dec.cached_step(self.cache, dec.event_token(events, self.seats2, st["count"]))
+        # games' event counts before this step, for the next step's pass at the slots
+        # the cache lengths give now (the wave tail advances them).
+        self.prev_pos.copy_(self.cache.length)
+        dec.event_token(events, self.seats2, st["count"], out=self.x[:2 * w])
         if self.pool:
             p, opp = self.pool, self.opponent
-            opp.cached_step(self.opp_cache, opp.event_token(events[:p], self.opp_seat, st["count"][:p]))
+            self.opp_prev_pos.copy_(self.opp_cache.length)
+            opp.event_token(events[:p], self.opp_seat, st["count"][:p], out=self.opp_x[:p])
             self.opp_cache.length += (step_out[4][:p] & ~done[:p]).long()
         ext.wave_tail(done, status, players, actions, logp, step_out, st, self.records,
                       learner=self.learner if self.pool else None)

@@ -349,3 +349,78 @@ def test_wave_selfplay_records_replay_on_the_engine(ext, pool):
     if pool:
         assert int(sp.records["valid"][:, :pool].sum()) < int(decisions[:pool].sum())
     sp.release()
+
+
+def _two_pass_driver(decoder, opponent, pool):
+    """The wave step as two passes of the cached transformer per step -- the query
+    tokens before the engine step, the event's tokens after it, the opening tokens in
+    the reset -- the order the reference's WaveCollector runs them in."""
+    from cugo_b200.seq_selfplay import SeqWaveSelfPlay
+
+    class TwoPass(SeqWaveSelfPlay):
+        def _reset(self):
+            super()._reset()
+            dec = self.dec
+            self.cache.length.zero_()
+            dec.cached_step(self.cache, self.x[:2 * self.w].clone(), slots=1)
+            self.cache.length.fill_(1)
+            if self.pool:
+                self.opp_cache.length.zero_()
+                self.opponent.cached_step(self.opp_cache, self.opp_x[:self.pool].clone(), slots=1)
+                self.opp_cache.length.fill_(1)
+
+        def _step(self):
+            ext, dec, w, ids, st = self.ext, self.dec, self.w, self.ids, self.state
+            query, legal, players, done, status = ext.observe_query_bf16(self.states, ids,
+                                                                          query=self.query)
+            seat = players.long() & 1
+            x = dec.query_token(query)
+            dec.cached_step(self.cache, x, rows=seat * w + ids)
+            logits = dec.readout(x)
+            if self.pool:
+                p, opp = self.pool, self.opponent
+                xo = opp.query_token(query[:p])
+                opp.cached_step(self.opp_cache, xo)
+                theirs = seat[:p] != self.learner_seat
+                logits[:p] = torch.where(theirs.unsqueeze(1), opp.readout(xo)[:, :logits.shape[1]],
+                                         logits[:p])
+                self.learner[:p] = ~theirs
+            actions, logp = ext.sample_actions(logits, legal, self.game0 + ids, st["decision"],
+                                               seed_base=self.seed_base)
+            self.rec_query.index_copy_(0, st["step_index"].clamp_max(self.max_steps - 1),
+                                       query.unsqueeze(0))
+            step_out = ext.step_events_indexed(self.states, ids, actions)
+            events = step_out[5]
+            dec.cached_step(self.cache, dec.event_token(events, self.seats2, st["count"]))
+            if self.pool:
+                p, opp = self.pool, self.opponent
+                opp.cached_step(self.opp_cache,
+                                opp.event_token(events[:p], self.opp_seat, st["count"][:p]))
+                self.opp_cache.length += (step_out[4][:p] & ~done[:p]).long()
+            ext.wave_tail(done, status, players, actions, logp, step_out, st, self.records,
+                          learner=self.learner if self.pool else None)
+
+    return TwoPass(decoder, wave=512, graphs=False, opponent=opponent, pool_games=pool)
+
+
+@pytest.mark.parametrize("pool", [0, 128])
+def test_wave_one_pass_equals_two_passes(ext, pool):
+    """The driver runs the previous step's event tokens and this step's query tokens
+    as one pass (shared LayerNorm and GEMM launches, the events' attention first at
+    every layer); the same wave played with two passes per step records the same
+    actions, log p and event logs."""
+    from cugo_b200.seq_selfplay import SeqWaveSelfPlay
+    runs = []
+    for two in (False, True):
+        opponent = _decoder(seed=5) if pool else None
+        dec = _decoder(seed=0)
+        sp = (_two_pass_driver(dec, opponent, pool) if two else
+              SeqWaveSelfPlay(dec, wave=512, graphs=False, opponent=opponent, pool_games=pool))
+        steps = sp.play_wave(game0=321)
+        torch.cuda.synchronize()
+        runs.append((steps, sp.records["actions"].clone(), sp.records["logp"].clone(),
+                     sp.events.clone(), sp.final_reward0.clone()))
+    (s0, *a), (s1, *b) = runs
+    assert s0 == s1
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
