@@ -95,6 +95,48 @@ def test_step_compact_grouped_orders_by_next_decision(ext):
     assert torch.equal(grouped_ids, expect)
 
 
+@pytest.mark.parametrize("device_rows", [None, 100_003])
+def test_step_compact_grouped_at_scale(ext, device_rows):
+    """Round tails of 131,072 entries (the scan moves each thread's words as 16-byte
+    vectors from about 100k entries on), with all of them stepped or only the first
+    `device_rows` (a device-resident count, so the last vector reaches past the rows):
+    the running games, grouped by next decision, as stepping those entries with
+    step_indexed and grouping them from their legal actions gives."""
+    n, m = 140_000, 131_072
+    idx = torch.arange(n, device=DEV, dtype=torch.int64)
+    states = ext.create(idx + 99, idx & 1)
+    g = torch.Generator().manual_seed(5)
+    for _ in range(8):
+        _, legal, _, _, _ = ext.observe_indexed(states, idx)
+        logits = torch.randn((n, 180), generator=g).to(DEV)
+        acts, _ = ext.sample_actions(logits, legal, idx, torch.zeros(n, dtype=torch.int32, device=DEV))
+        ext.step_indexed(states, idx, acts.clamp_min(0))
+    ids = torch.randperm(n, generator=g)[:m].to(DEV)
+    _, legal, _, _, _ = ext.observe_indexed(states, ids)
+    logits = torch.randn((m, 180), generator=g).to(DEV)
+    acts, _ = ext.sample_actions(logits, legal, ids, torch.zeros(m, dtype=torch.int32, device=DEV))
+    k = m if device_rows is None else device_rows
+    ref = states.clone()
+    _, done, _, _, _ = ext.step_indexed(ref, ids[:k], acts[:k])
+    order = ids[:k][~done]
+    _, legal, _, _, _ = ext.observe_indexed(ref, order)
+    choice = legal[:, 127:177].any(1)
+    prompt = legal[:, 123:127].any(1) | legal[:, 177:179].any(1)
+    group = torch.where(choice, 1, torch.where(prompt, 2, 0))
+    expect = torch.cat([order[group == q] for q in range(3)])
+    decision = torch.zeros(n, dtype=torch.int32, device=DEV)
+    reward0, nag = torch.zeros(n, device=DEV), torch.zeros(n, dtype=torch.bool, device=DEV)
+    bad = torch.zeros(1, dtype=torch.int64, device=DEV)
+    nxt = torch.full((n,), -7, dtype=torch.int64, device=DEV)
+    count = torch.zeros(1, dtype=torch.int32, device=DEV)
+    m_dev = None if device_rows is None else torch.tensor([k], dtype=torch.int32, device=DEV)
+    ext.step_compact(states, ids, acts, decision, reward0, nag, bad, nxt, count, m_dev=m_dev,
+                     grouped=True)
+    assert torch.equal(states, ref)
+    assert int(count) == expect.numel() > 0
+    assert torch.equal(nxt[:int(count)], expect)
+
+
 def _reference_loop(ext, policy, game_index, seed_base=12345, max_rounds=128):
     """The collection loop with separate ops and torch bookkeeping; games that the
     deal ended take no decision (reward 0)."""
