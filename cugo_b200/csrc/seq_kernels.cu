@@ -102,12 +102,16 @@ __global__ void __launch_bounds__(256, 3) decode_attention_kernel(
     const __nv_bfloat16* __restrict__ v_new, i64 ldn, __nv_bfloat16* keys, __nv_bfloat16* values,
     i64 n_rows, int heads, int slots, const i64* __restrict__ pos, i64 pos_clamp,
     const i64* __restrict__ rows, i64 n, float scale, __nv_bfloat16* __restrict__ out, i64 ldo,
-    int32_t* error) {
+    int32_t* error, const bool* __restrict__ active) {
   const i64 gw = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (gw >= n * heads) return;
   const int lane = threadIdx.x & 31, half = lane & 1, sl = lane >> 1;
   const i64 i = gw / heads;
   const int h = static_cast<int>(gw - i * heads);
+  if (active && !active[i]) {  // an inactive query: zero output, no cache access
+    out[i * ldo + h * kDh + lane] = __float2bfloat16_rn(0.0f);
+    return;
+  }
   const i64 r = rows ? __ldg(rows + i) : i;
   i64 p = -1;
   if (pos_clamp < 0) {
@@ -731,7 +735,7 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
     const __nv_bfloat16* __restrict__ v_new, i64 ldn, __nv_bfloat16* keys, __nv_bfloat16* values,
     i64 n_rows, int heads, int slots, const i64* __restrict__ pos, i64 pos_clamp,
     const i64* __restrict__ rows, i64 n, float scale, __nv_bfloat16* __restrict__ out, i64 ldo,
-    int32_t* error, int ring_bytes) {
+    int32_t* error, int ring_bytes, const bool* __restrict__ active) {
   extern __shared__ __align__(128) unsigned char smem[];
   // Layout: the ring, the per-warp slot weights, the items' rows and positions, the
   // ring offsets of the items in flight, their mbarriers.
@@ -756,8 +760,9 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
       }
     }
     const bool ok = p >= 0 && p < slots && r >= 0 && r < n_rows;
-    info[k].row = ok ? r : -1;
-    info[k].pos = ok ? static_cast<int>(p) : -1;
+    const bool skip = active && !active[i];  // inactive: no copies, zero output, no error
+    info[k].row = skip ? -2 : (ok ? r : -1);
+    info[k].pos = ok && !skip ? static_cast<int>(p) : -1;
   }
   if (t == 0) {
     for (int s = 0; s < kRingItems; ++s)
@@ -825,7 +830,13 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
       if (live_bytes == 0) {
         at = 0;
       } else {
-        const int tail = ring_off[consumed % kRingItems];
+        // The live bytes start at the oldest item in flight that holds any (an item
+        // without bytes -- an invalid or inactive query -- may sit at an offset that
+        // bounds nothing: a later item can have gone to offset 0 when the ring was
+        // empty).  live_bytes > 0, so one exists before `issued`.
+        int oldest = consumed;
+        while (item_bytes(oldest) == 0) ++oldest;
+        const int tail = ring_off[oldest % kRingItems];
         if (head > tail) {  // live bytes in [tail, head)
           if (head + need <= ring_bytes) at = head;
           else if (need <= tail) at = 0;
@@ -861,7 +872,7 @@ __global__ void __launch_bounds__(kStagedThreads, 4) decode_attention_staged_ker
       __nv_bfloat16* o = out + i * ldo + h * kDh;
       if (r < 0) {
         o[lane] = __float2bfloat16_rn(0.0f);
-        if (lane == 0 && error) atomicExch(error, 1);
+        if (r == -1 && lane == 0 && error) atomicExch(error, 1);
       } else {
         const int at = ring_off[k % kRingItems];
         __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(ring + at) + h * (p + 1) * kDh;
@@ -988,12 +999,13 @@ size_t staged_smem_bytes(int heads, int slots) {
 
 extern "C" {
 
-int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new, const void* v_new,
-                               int64_t ldn, void* keys, void* values, int64_t n_rows,
-                               int32_t heads, int32_t slots, int32_t head_dim,
-                               const int64_t* pos, int64_t pos_clamp, const int64_t* rows,
-                               int64_t n, float scale, void* out, int64_t ldo, int32_t* error,
-                               cudaStream_t stream) {
+int cugo_b200_decode_attention_active(const void* q, int64_t ldq, const void* k_new,
+                                      const void* v_new, int64_t ldn, void* keys, void* values,
+                                      int64_t n_rows, int32_t heads, int32_t slots,
+                                      int32_t head_dim, const int64_t* pos, int64_t pos_clamp,
+                                      const int64_t* rows, int64_t n, float scale, void* out,
+                                      int64_t ldo, const bool* active, int32_t* error,
+                                      cudaStream_t stream) {
   if (n < 0 || heads <= 0 || slots <= 0 || slots > kMaxSlots || head_dim != kDh || n_rows <= 0)
     return CUGO_B200_ERR_ARG;
   if (n == 0) return CUGO_B200_OK;
@@ -1032,15 +1044,26 @@ int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new, co
         static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k_new),
         static_cast<const __nv_bfloat16*>(v_new), ldn, static_cast<__nv_bfloat16*>(keys),
         static_cast<__nv_bfloat16*>(values), n_rows, heads, slots, pos, pos_clamp, rows, n, scale,
-        static_cast<__nv_bfloat16*>(out), ldo, error, ring_bytes_for(heads, slots));
+        static_cast<__nv_bfloat16*>(out), ldo, error, ring_bytes_for(heads, slots), active);
     return launch_status();
   }
   decode_attention_kernel<<<blocks_for_warps(n * heads), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k_new),
       static_cast<const __nv_bfloat16*>(v_new), ldn, static_cast<__nv_bfloat16*>(keys),
       static_cast<__nv_bfloat16*>(values), n_rows, heads, slots, pos, pos_clamp, rows, n, scale,
-      static_cast<__nv_bfloat16*>(out), ldo, error);
+      static_cast<__nv_bfloat16*>(out), ldo, error, active);
   return launch_status();
+}
+
+int cugo_b200_decode_attention(const void* q, int64_t ldq, const void* k_new, const void* v_new,
+                               int64_t ldn, void* keys, void* values, int64_t n_rows,
+                               int32_t heads, int32_t slots, int32_t head_dim,
+                               const int64_t* pos, int64_t pos_clamp, const int64_t* rows,
+                               int64_t n, float scale, void* out, int64_t ldo, int32_t* error,
+                               cudaStream_t stream) {
+  return cugo_b200_decode_attention_active(q, ldq, k_new, v_new, ldn, keys, values, n_rows, heads,
+                                           slots, head_dim, pos, pos_clamp, rows, n, scale, out,
+                                           ldo, nullptr, error, stream);
 }
 
 int cugo_b200_layernorm(const float* x, int64_t ldx, const float* gamma, const float* beta,

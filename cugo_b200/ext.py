@@ -72,6 +72,9 @@ _SIGNATURES: dict[str, list] = {
     "cugo_b200_rowdot_bf16": [_VP, _I64, _VP, _VP, _I64, _I64, _VP, _I64, _VP],
     "cugo_b200_decode_attention": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32, _I32,
                                    _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64, _VP, _VP],
+    "cugo_b200_decode_attention_active": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _I32, _I32,
+                                          _I32, _VP, _I64, _VP, _I64, ctypes.c_float, _VP, _I64,
+                                          _VP, _VP, _VP],
     "cugo_b200_layernorm": [_VP, _I64, _VP, _VP, _I64, ctypes.c_float, _VP, _I64, _I64, _VP],
     "cugo_b200_event_embed": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _VP, _I64, _VP],
     "cugo_b200_start_embed": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _VP, _I64, _VP],
@@ -924,13 +927,15 @@ class CugoB200Extension:
                          pos: torch.Tensor, rows: torch.Tensor | None = None,
                          k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
                          pos_clamp: int = -1, out: torch.Tensor | None = None,
-                         error: torch.Tensor | None = None) -> torch.Tensor:
+                         error: torch.Tensor | None = None,
+                         active: torch.Tensor | None = None) -> torch.Tensor:
         """decode_attention (python/cugo_seq_attention50.py:43-57) on the native kernel.
 
         q [n, heads, dh] bf16 (dh = 32, rows of q may be strided), keys/values
         [rows, heads, slots, dh] bf16 contiguous, pos/rows int64 -> out [n, heads, dh].
         k_new/v_new ([n, heads, dh]) are first written to slot pos of each row.
-        pos_clamp >= 0: pos is the per-row length array, position = min(pos[row], clamp)."""
+        pos_clamp >= 0: pos is the per-row length array, position = min(pos[row], clamp).
+        active (bool [n]): only those queries attend and append; the others get zeros."""
         n, heads, dh = q.shape
         if q.dtype != torch.bfloat16 or keys.dtype != torch.bfloat16 or values.dtype != torch.bfloat16:
             raise RuntimeError("decode_attention expects bf16 q, keys and values")
@@ -948,11 +953,21 @@ class CugoB200Extension:
         if out is None:
             out = torch.empty((n, heads, dh), dtype=torch.bfloat16, device=q.device)
         with torch.cuda.device(q.device):
-            _check(self._lib.cugo_b200_decode_attention(
-                _ptr(q), q.stride(0), _ptr(k_new), _ptr(v_new), ldn, _ptr(keys), _ptr(values),
-                keys.shape[0], heads, keys.shape[2], dh, _ptr(pos), pos_clamp, _ptr(rows), n,
-                float(dh ** -0.5), _ptr(out), out.stride(0), _ptr(error),
-                self._stream(q.device)), "decode_attention")
+            if active is None:
+                _check(self._lib.cugo_b200_decode_attention(
+                    _ptr(q), q.stride(0), _ptr(k_new), _ptr(v_new), ldn, _ptr(keys), _ptr(values),
+                    keys.shape[0], heads, keys.shape[2], dh, _ptr(pos), pos_clamp, _ptr(rows), n,
+                    float(dh ** -0.5), _ptr(out), out.stride(0), _ptr(error),
+                    self._stream(q.device)), "decode_attention")
+            else:
+                _check_cuda_1d(active, torch.bool, "active")
+                if active.numel() != n:
+                    raise RuntimeError("decode_attention: active must have one entry per query")
+                _check(self._lib.cugo_b200_decode_attention_active(
+                    _ptr(q), q.stride(0), _ptr(k_new), _ptr(v_new), ldn, _ptr(keys), _ptr(values),
+                    keys.shape[0], heads, keys.shape[2], dh, _ptr(pos), pos_clamp, _ptr(rows), n,
+                    float(dh ** -0.5), _ptr(out), out.stride(0), _ptr(active), _ptr(error),
+                    self._stream(q.device)), "decode_attention")
         return out
 
     def layernorm(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,

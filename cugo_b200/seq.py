@@ -261,12 +261,14 @@ class SeqDecoder:
         return x
 
     def cached_step_segments(self, cache: SeqKVCache, x: torch.Tensor,
-                             segments: list[tuple[int, torch.Tensor | None, torch.Tensor]]
+                             segments: list[tuple], active: torch.Tensor | None = None
                              ) -> torch.Tensor:
         """cached_step over consecutive row segments of x fp32 [n, d] (updated in place
         and returned) that share every layer's LayerNorm and GEMM launches.  segments =
         [(count, rows, positions)]: the segment's tokens go to cache rows `rows`
-        (default 0..count-1) at slot min(positions[row], slots - 1).  At every layer the
+        (default 0..count-1) at slot min(positions[row], slots - 1).  With `active`
+        (bool [n]) only those tokens attend and append (the others' outputs are
+        meaningless and must not be used).  At every layer the
         segments' attention launches (each with its KV append) run in order, so a later
         segment sees the slots an earlier one appended exactly as if it had run as its
         own pass after it; every other layer computes each row on its own, so each
@@ -289,7 +291,8 @@ class SeqDecoder:
                 s1 = s0 + count
                 ext.decode_attention(q[s0:s1], cache.k[i], cache.v[i], positions, rows=rows,
                                      k_new=k[s0:s1], v_new=v[s0:s1], pos_clamp=clamp,
-                                     out=att[s0:s1].view(count, heads, dh))
+                                     out=att[s0:s1].view(count, heads, dh),
+                                     active=None if active is None else active[s0:s1])
                 s0 = s1
             ext.linear(att, L.w_out, L.b_out, residual=x, out=x)
             a = ext.layernorm(x, L.norm2_w, L.norm2_b, self.eps)

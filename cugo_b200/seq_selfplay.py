@@ -72,6 +72,7 @@ class SeqWaveSelfPlay:
         # rows, then the query rows; and the slots those tokens go to.
         self.x = torch.zeros((3 * w, decoder.d_model), dtype=torch.float32, device=dev)
         self.prev_pos = torch.zeros(2 * w, **i64)
+        self.live = torch.ones(3 * w, dtype=torch.bool, device=dev)  # rows that attend
         self.started = torch.zeros(w, dtype=torch.bool, device=dev)
         # Device state the wave-tail kernel updates.
         self.state = {
@@ -164,14 +165,20 @@ class SeqWaveSelfPlay:
         query, legal, players, done, status = ext.observe_query_bf16(self.states, ids, query=self.query)
         seat = players.long() & 1
         x = dec.query_token(query, out=self.x[2 * w:])
+        # Games that finished before this step feed no later decision: their tokens
+        # neither attend nor append (the wave tail leaves their records alone).
+        live = ~done
+        self.live.copy_(torch.cat((live, live, live)))
         dec.cached_step_segments(self.cache, self.x, [(2 * w, None, self.prev_pos),
-                                                      (w, seat * w + ids, self.cache.length)])
+                                                      (w, seat * w + ids, self.cache.length)],
+                                 active=self.live)
         logits = dec.readout(x)
         if self.pool:
             p, opp = self.pool, self.opponent
             xo = opp.query_token(query[:p], out=self.opp_x[p:])
             opp.cached_step_segments(self.opp_cache, self.opp_x,
-                                     [(p, None, self.opp_prev_pos), (p, None, self.opp_cache.length)])
+                                     [(p, None, self.opp_prev_pos), (p, None, self.opp_cache.length)],
+                                     active=torch.cat((live[:p], live[:p])))
             theirs = seat[:p] != self.learner_seat
             logits[:p] = torch.where(theirs.unsqueeze(1), opp.readout(xo)[:, :logits.shape[1]],
                                      logits[:p])

@@ -540,6 +540,17 @@ CUGO_B200_API int cugo_b200_decode_attention(const void* q, int64_t ldq, const v
                                              void* out, int64_t ldo, int32_t* error,
                                              cudaStream_t stream);
 
+/* cugo_b200_decode_attention restricted to the queries with active[i] set (bool [n],
+ * device; NULL: all): an inactive query reads and writes no cache slot, appends
+ * nothing, sets no error and gets zeros.  The sequence self-play wave passes its
+ * unfinished games, whose rows alone feed a later decision (no counterpart in the
+ * reference, whose wave runs every row). */
+CUGO_B200_API int cugo_b200_decode_attention_active(
+    const void* q, int64_t ldq, const void* k_new, const void* v_new, int64_t ldn, void* keys,
+    void* values, int64_t n_rows, int32_t heads, int32_t slots, int32_t head_dim,
+    const int64_t* pos, int64_t pos_clamp, const int64_t* rows, int64_t n, float scale, void* out,
+    int64_t ldo, const bool* active, int32_t* error, cudaStream_t stream);
+
 /* nn.LayerNorm(d) of fp32 rows (eps as given, biased variance) into bf16 rows,
  * the operand of the next GEMM (norm1/norm2/norm of the sequence transformer,
  * python/cugo_seq50.py:311,321; python/cugo_seq50.py:226).  d in {128, 256, 512,

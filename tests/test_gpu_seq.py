@@ -424,3 +424,58 @@ def test_wave_one_pass_equals_two_passes(ext, pool):
     assert s0 == s1
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("slots", [50, 100])  # the staged kernel, then the warp-per-head one
+def test_decode_attention_active_mask(ext, slots):
+    """decode_attention restricted to active queries: those attend and append exactly as
+    without the mask; the others get zeros, leave their cache rows untouched and set
+    no error."""
+    g = torch.Generator(device="cpu").manual_seed(3)
+    n, rows_n, heads, dh = 2048, 4096, 8, 32
+    kc = torch.randn((rows_n, heads, slots, dh), generator=g).to(DEV, torch.bfloat16)
+    vc = torch.randn((rows_n, heads, slots, dh), generator=g).to(DEV, torch.bfloat16)
+    qkv = torch.randn((n, 3 * heads * dh), generator=g).to(DEV, torch.bfloat16)
+    q, kn, vn = (qkv[:, i * 256:(i + 1) * 256].view(n, heads, dh) for i in range(3))
+    length = torch.randint(0, slots, (rows_n,), generator=g).to(DEV)
+    rows = torch.randperm(rows_n, generator=g)[:n].to(DEV)
+    active = (torch.rand(n, generator=g) < 0.7).to(DEV)
+    k0, v0 = kc.clone(), vc.clone()
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ref = ext.decode_attention(q, k0, v0, length, rows=rows, k_new=kn, v_new=vn,
+                               pos_clamp=slots - 1, error=err)
+    for _ in range(2):  # the same result twice
+        k1, v1 = kc.clone(), vc.clone()
+        out = ext.decode_attention(q, k1, v1, length, rows=rows, k_new=kn, v_new=vn,
+                                   pos_clamp=slots - 1, error=err, active=active)
+        torch.cuda.synchronize()
+        assert int(err) == 0
+        assert torch.equal(out[active], ref[active])
+        assert not bool(out[~active].float().abs().any())
+        on, off = rows[active], rows[~active]
+        assert torch.equal(k1[on], k0[on]) and torch.equal(v1[on], v0[on])
+        assert torch.equal(k1[off], kc[off]) and torch.equal(v1[off], vc[off])
+
+
+def test_decode_attention_invalid_rows_leave_the_others_alone(ext):
+    """Queries with an out-of-range cache row take no ring space; the valid queries of
+    the same launch get exactly what they get without them (an item without bytes must
+    not misplace the ring's live data), and the error flag is set."""
+    g = torch.Generator(device="cpu").manual_seed(8)
+    n, rows_n, heads, slots, dh = 4096, 8192, 8, 50, 32
+    kc = torch.randn((rows_n, heads, slots, dh), generator=g).to(DEV, torch.bfloat16)
+    vc = torch.randn((rows_n, heads, slots, dh), generator=g).to(DEV, torch.bfloat16)
+    q = torch.randn((n, heads, dh), generator=g).to(DEV, torch.bfloat16)
+    length = torch.randint(0, slots, (rows_n,), generator=g).to(DEV)
+    rows = torch.randperm(rows_n, generator=g)[:n].to(DEV)
+    bad = torch.rand(n, generator=g).to(DEV) < 0.3
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ref = ext.decode_attention(q, kc, vc, length, rows=rows, pos_clamp=slots - 1, error=err)
+    torch.cuda.synchronize()
+    assert int(err) == 0
+    out = ext.decode_attention(q, kc, vc, length, rows=torch.where(bad, -1, rows),
+                               pos_clamp=slots - 1, error=err)
+    torch.cuda.synchronize()
+    assert int(err) == 1
+    assert torch.equal(out[~bad], ref[~bad])
+    assert not bool(out[~bad].isnan().any()) and not bool(out[bad].float().abs().any())
